@@ -1,0 +1,421 @@
+"""Benchmark of the B200 TTT dual-form scan (one JSON line from rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
+
+Workloads (synthetic seeded data of those shapes, see
+ttt-triton_b200/synthetic.py):
+
+* ``mlp_fwd_c1`` (default, the headline): TTT-MLP forward, B16 NH12 L2048 F64 FF256,
+  bf16 activations / fp32 state, checkpoint group 16 (config 1).
+* ``linear_fwd_c0``: TTT-Linear forward, fp32, B2 NH4 L256 F64 (config 0).
+* ``linear_fwdbwd_c2``: TTT-Linear forward+backward, bf16, B32 NH8 L4096 F64 (config 2).
+* ``mlp_fwdbwd_c3``: TTT-MLP forward+backward, bf16, B64 NH16 L8192 F64 FF256, memo 16 (config 3).
+
+A step is one pass of the hot path over one batch. Multi-GPU runs are weak scaling:
+every rank processes its own full batch (the (b, h) streams are independent, so there
+is no data-path collective); timing is the max over ranks of the device-timed region.
+The reference arm (``--impl reference``) times the CPU port of the reference's ops/
+path (oracle/ttt_oracle.py) on the host cores over a bounded sample of the workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "ttt-triton_b200"))
+
+import torch  # noqa: E402
+
+WORKLOADS = {
+    "linear_fwd_c0": dict(kind="linear", B=2, NH=4, L=256, F=64, FF=None, dtype="f32", bwd=False, ckpt=16, memo=None),
+    "mlp_fwd_c1": dict(kind="mlp", B=16, NH=12, L=2048, F=64, FF=256, dtype="bf16", bwd=False, ckpt=16, memo=None),
+    "linear_fwdbwd_c2": dict(kind="linear", B=32, NH=8, L=4096, F=64, FF=None, dtype="bf16", bwd=True, ckpt=16, memo=None),
+    "mlp_fwdbwd_c3": dict(kind="mlp", B=64, NH=16, L=8192, F=64, FF=256, dtype="bf16", bwd=True, ckpt=16, memo=16),
+}
+CS = 16
+DT = {"f32": torch.float32, "bf16": torch.bfloat16}
+METRIC = "TTT tokens/s (B*H*L) fwd & fwd+bwd at 1/2/4/8 B200; % of HBM roofline"
+
+
+def peaks():
+    path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def algorithmic(w):
+    """Compulsory bytes and useful FLOPs per token (one (b, h, t))."""
+    F, FF = w["F"], w["FF"]
+    eb = 4 if w["dtype"] == "f32" else 2
+    fwd_elems = 3 * F + CS + F  # read XQ, XK, XV, eta row; write XQW
+    bwd_elems = (3 * F + CS) + F + (3 * F + CS)  # re-read inputs, read dXQW, write dXQ/dXK/dXV/deta
+    nbytes = eb * (fwd_elems + (bwd_elems if w["bwd"] else 0))
+    if w["kind"] == "linear":
+        fwd_flops = 6 * F * F + 4 * CS * F
+        bwd_flops = 2 * fwd_flops + 16 * F * F + 8 * CS * F  # group re-forward + reverse step products
+    else:
+        fwd_flops = 14 * F * FF + 4 * CS * F + 4 * CS * FF
+        bwd_flops = 2 * fwd_flops + 22 * F * FF + 8 * CS * FF + 8 * CS * F
+    flops = fwd_flops + (bwd_flops if w["bwd"] else 0)
+    return nbytes, flops
+
+
+# --------------------------------------------------------------------------- inputs / steps
+def make_inputs(w, device, seed):
+    import synthetic as S
+
+    NC = w["L"] // CS
+    dt = DT[w["dtype"]]
+    if w["kind"] == "linear":
+        d = S.make_linear_inputs(w["B"], w["NH"], NC, CS, w["F"], dtype=dt, device=device, seed=seed)
+    else:
+        d = S.make_mlp_inputs(w["B"], w["NH"], NC, CS, w["F"], w["FF"], dtype=dt, device=device, seed=seed)
+    dO = S.make_upstream((w["B"], w["NH"], NC, CS, w["F"]), device=device, seed=seed + 1, dtype=dt) if w["bwd"] else None
+    return d, dO
+
+
+LIN = ("ln_w", "ln_b", "W1", "b1", "XQ", "XV", "XK", "eta")
+MLP = ("ln_w", "ln_b", "W1", "b1", "W2", "b2", "XQ", "XV", "XK", "eta")
+
+
+def kernel_step(w, d, dO):
+    """One pass of the hot path through the functional core (inputs resident in HBM).
+    Returns the number of kernel launches it made."""
+    import _core
+
+    if w["kind"] == "linear":
+        XQW, _, _, Wc, bc = _core.linear_forward(*(d[k] for k in LIN), w["ckpt"])
+        if w["bwd"]:
+            _core.linear_backward(d["ln_w"], d["ln_b"], Wc, bc, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"])
+            return 2
+        return 1
+    XQW, _, ck, _ = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"])
+    if w["bwd"]:
+        _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"])
+        return 2
+    return 1
+
+
+def api_step(w, host, dev_bufs, out_host):
+    """End-to-end step through the public API with host buffers: H2D copies of every
+    input, the reference-facing call (TritonLinear / TritonMLP .apply, plus backward),
+    D2H of the result. Returns (h2d_bytes, d2h_bytes)."""
+    from linear_triton import TritonLinear
+    from mlp_triton import TritonMLP
+
+    h2d = 0
+    for k, t in host.items():
+        dev_bufs[k].copy_(t, non_blocking=True)
+        h2d += t.numel() * t.element_size()
+    d = dev_bufs
+    if w["kind"] == "linear":
+        leaves = [d[k] for k in LIN]
+        if w["bwd"]:
+            leaves = [t.requires_grad_(True) for t in leaves]
+        out = TritonLinear.apply(*leaves, w["ckpt"])
+    else:
+        leaves = [d[k] for k in MLP]
+        if w["bwd"]:
+            leaves = [t.requires_grad_(True) for t in leaves]
+        out = TritonMLP.apply(*leaves, w["ckpt"], w["memo"] or w["ckpt"])[0]
+    if w["bwd"]:
+        out.backward(d["dO"])
+        res = d["XQ"].grad
+        for t in leaves:
+            t.grad = None
+            t.requires_grad_(False)
+    else:
+        res = out
+    out_host.copy_(res.detach(), non_blocking=True)
+    return h2d, out_host.numel() * out_host.element_size()
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        with open(self.file.name) as f:
+            rows = [r.split(",") for r in f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- arms
+def cpu_reference(w, budget_s=12.0):
+    """The reference's ops/ path restated on the host cores (oracle/ttt_oracle.py), fp32,
+    on a bounded sample of the workload: the full sequence for a batch slice."""
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import synthetic as S
+    import ttt_oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    NC = w["L"] // CS
+    B, NH = 1, min(w["NH"], 4)
+    if w["kind"] == "linear":
+        d = S.make_linear_inputs(B, NH, NC, CS, w["F"], seed=0)
+    else:
+        d = S.make_mlp_inputs(B, NH, NC, CS, w["F"], w["FF"], seed=0)
+    dO = S.make_upstream((B, NH, NC, CS, w["F"]), seed=1)
+    tokens = B * NH * NC * CS
+    best = None
+    t_end = time.perf_counter() + budget_s
+    reps = 0
+    while reps < 1 or (time.perf_counter() < t_end and reps < 20):
+        t0 = time.perf_counter()
+        if w["bwd"]:
+            (O.linear_grads if w["kind"] == "linear" else O.mlp_grads)(d, dO)
+        else:
+            with torch.no_grad():
+                if w["kind"] == "linear":
+                    O.linear_scan(*(d[k] for k in LIN))
+                else:
+                    O.mlp_scan(*(d[k] for k in MLP))
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+        reps += 1
+    sample = f"B={B} NH={NH} L={w['L']} (full sequence, batch/head slice), fp32, best of {reps}"
+    return tokens / best, threads, sample
+
+
+def run_reference(args, w, rank, world):
+    if rank != 0:
+        return
+    value, cores, sample = cpu_reference(w)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, **{k: v for k, v in w.items() if k in ("B", "NH", "L", "F", "FF")}},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, w, rank, world, local_rank):
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    d, dO = make_inputs(w, dev, seed=rank)
+    NC = w["L"] // CS
+    tokens_rank = w["B"] * w["NH"] * w["L"]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        kernel_step(w, d, dO)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local_rank)
+    sampler.start()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    launches = 0
+    for _ in range(args.steps):
+        launches += kernel_step(w, d, dO)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    # per-kernel durations of the dominant kernel (backward for fwd+bwd workloads)
+    kern_ms = kernel_durations(w, d, dO, args.steps)
+    # end-to-end through the public API with host buffers
+    e2e_ms, h2d, d2h = e2e_time(w, d, dO, dev, args)
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+    if rank != 0:
+        return
+    ms_step = ms / args.steps
+    value = world * tokens_rank / (ms_step / 1e3)
+    hbm, bf16, bf16_sus, src = peaks()
+    nbytes_tok, flops_tok = algorithmic(w)
+    dom_ms = kern_ms
+    if w["kind"] == "mlp":
+        achieved = flops_tok * tokens_rank / (dom_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
+                "traffic": None, "peak_source": src}
+    else:
+        achieved = nbytes_tok * tokens_rank / (dom_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": None, "peak_source": src}
+    roof["kernel"] = ("linear" if w["kind"] == "linear" else "mlp") + ("_bwd_kernel" if w["bwd"] else "_fwd_kernel")
+    roof["kernel_ms"] = dom_ms
+    roof["hbm_roofline_tokens_per_s"] = hbm * 1e9 / nbytes_tok
+    roof["hbm_frac"] = (tokens_rank / (ms_step / 1e3)) / roof["hbm_roofline_tokens_per_s"]
+    roof["tensor_roofline_tokens_per_s"] = bf16 * 1e12 / flops_tok
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
+        "config": {"workload": args.workload, "B_per_rank": w["B"], "NH": w["NH"], "L": w["L"], "F": w["F"],
+                   "FF": w["FF"], "CS": CS, "checkpoint_group_size": w["ckpt"], "memo_segment_size": w["memo"],
+                   "global_batch": w["B"] * world, "parallelism": f"streams sharded over {world} GPU(s), no collective",
+                   "l2": "inputs larger than L2 (no flush)"},
+        "roofline": roof,
+        "e2e": {"value": world * tokens_rank / (e2e_ms / args.steps / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_reference(w)
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    print(json.dumps(line), flush=True)
+
+
+def kernel_durations(w, d, dO, steps):
+    """Average device time of the dominant kernel's launch (CUDA events on its stream)."""
+    import _core
+
+    stream = torch.cuda.current_stream()
+    tot = 0.0
+    n = max(1, min(steps, 5))
+    for _ in range(n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if w["kind"] == "linear":
+            _, _, _, Wc, bc = (None, None, None, None, None)
+            if w["bwd"]:
+                _, _, _, Wc, bc = _core.linear_forward(*(d[k] for k in LIN), w["ckpt"])
+                e0.record(stream)
+                _core.linear_backward(d["ln_w"], d["ln_b"], Wc, bc, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"])
+            else:
+                e0.record(stream)
+                _core.linear_forward(*(d[k] for k in LIN), w["ckpt"])
+        else:
+            if w["bwd"]:
+                _, _, ck, _ = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"])
+                e0.record(stream)
+                _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"])
+            else:
+                e0.record(stream)
+                _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+    return tot / n
+
+
+def e2e_time(w, d, dO, dev, args):
+    host = {k: v.detach().cpu().pin_memory() for k, v in d.items()}
+    if dO is not None:
+        host["dO"] = dO.cpu().pin_memory()
+    dev_bufs = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
+    out_host = torch.empty(d["XQ"].shape, dtype=d["XQ"].dtype).pin_memory()
+    for _ in range(max(1, min(args.warmup, 2))):
+        api_step(w, host, dev_bufs, out_host)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    h2d = d2h = 0
+    for _ in range(args.steps):
+        h2d, d2h = api_step(w, host, dev_bufs, out_host)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1), h2d, d2h
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mlp_fwd_c1")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    w = WORKLOADS[args.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, w, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, w, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,159 @@
+/*
+ * ttt_b200.h -- C ABI of the B200 (sm_100a) TTT-Linear / TTT-MLP dual-form scan.
+ *
+ * Drop-in boundary for the Triton launches of Ali-Najar/ttt-triton. Each entry point
+ * replaces one `kernel[grid](...)` launch inside the reference's autograd wrappers and
+ * takes plain device pointers, sizes, dtype codes and a cudaStream_t (as void*). Nothing
+ * here allocates: the caller owns every output and scratch buffer, exactly as the
+ * reference wrappers own theirs (torch.empty on the input's device). Work is enqueued
+ * asynchronously on `stream`; the functions never synchronise the device.
+ *
+ * Layout (all contiguous, element strides implied by the shapes):
+ *   activations XQ, XK, XV, XQW, dXQW, dXQ, dXK, dXV : [B, NH, NC, CS, F]
+ *   eta, d_eta                                       : [B, NH, NC, CS, CS]
+ *   ttt_norm_weight / ttt_norm_bias                  : [NH, F]
+ *   Linear state W / b                               : [B, NH, F, F] / [B, NH, 1, F]    (fp32)
+ *   MLP state W1 / b1 / W2 / b2                      : [B, NH, F, FF] / [B, NH, 1, FF] /
+ *                                                      [B, NH, FF, F] / [B, NH, 1, F]   (fp32)
+ *   checkpoints (K = ceil(NC / checkpoint_group_size)) : [B, NH, K, ...state...]          (fp32)
+ *   memo states (NS = ceil(NC / memo_segment_size))    : [B, NH, NS, ...state...]         (fp32)
+ * Per-tensor dtype codes select fp32 / bf16 / fp16 storage; arithmetic is fp32 with fp32
+ * inner state (tensor-core operands are rounded to the activation type).
+ *
+ * Every function returns TTT_OK (0) or a negative TTT_ERR_* code; ttt_last_error()
+ * gives the message for the calling thread.
+ */
+#ifndef TTT_B200_H_
+#define TTT_B200_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TTT_OK 0
+#define TTT_ERR_NULL (-1)        /* a required pointer is NULL */
+#define TTT_ERR_SHAPE (-2)       /* a size is out of range or inconsistent */
+#define TTT_ERR_DTYPE (-3)       /* unknown dtype code */
+#define TTT_ERR_UNSUPPORTED (-4) /* valid request this build cannot run (e.g. shared memory) */
+#define TTT_ERR_SCRATCH (-5)     /* scratch buffer smaller than the *_scratch_bytes query */
+#define TTT_ERR_CUDA (-6)        /* a CUDA runtime call failed; message has the CUDA error */
+#define TTT_ERR_ALIGN (-7)       /* a pointer is not aligned to its element size */
+
+#define TTT_DTYPE_F32 0
+#define TTT_DTYPE_BF16 1
+#define TTT_DTYPE_F16 2
+
+/* Version of this ABI (major * 10000 + minor * 100 + patch). */
+int ttt_abi_version(void);
+
+/* Message of the last failing call on this host thread ("" after a success). */
+const char* ttt_last_error(void);
+
+/*
+ * TTT-Linear forward scan. Replaces the launch of `ttt_linear_scan_forward` in
+ * linear_triton.py:96-127 (TritonLinear._forward_core). Computes, per mini-batch, the
+ * dual form of ops/ttt_linear.py:8-54 (LayerNorm eps 1e-8, full eta matrix):
+ *   XQW = XQ + LN(XQ W + b - (eta * (XQ XK^T + 1)) G),  G = ln_fused_l2_bwd(XK W + b, XV - XK)
+ *   W <- W - XK^T diag(eta[CS-1, :]) G,  b <- b - eta[CS-1, :] G
+ * Writes XQW (dtype dt_out), the final state W_last/b_last and the state at the start
+ * of every checkpoint group (W_ckpt/b_ckpt, as kernels/linear_forward.py:55-73).
+ */
+int ttt_linear_fwd(int B, int NH, int NC, int CS, int F, int checkpoint_group_size,
+                   const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
+                   const float* W1_init, const float* b1_init,
+                   const void* XQ, int dt_xq, const void* XV, int dt_xv, const void* XK, int dt_xk,
+                   const void* eta, int dt_eta,
+                   void* XQW, int dt_out,
+                   float* W1_last, float* b1_last, float* W1_ckpt, float* b1_ckpt,
+                   void* stream);
+
+/* Bytes of scratch ttt_linear_bwd needs for these sizes. */
+size_t ttt_linear_bwd_scratch_bytes(int B, int NH, int NC, int CS, int F, int checkpoint_group_size);
+
+/*
+ * TTT-Linear backward. Replaces the launch of `ttt_linear_scan_backward` in
+ * linear_triton.py:201-246 (TritonLinear._backward_core), with the full dual-form
+ * gradients of ops/ttt_linear.py (d_eta is the whole CS x CS block per mini-batch).
+ * Inputs are the forward's inputs plus its checkpoints and dXQW. Outputs:
+ *   d_ln_w, d_ln_b : [B, NH, F] fp32 per-(b,h) partial sums (the caller sums over B,
+ *                    as linear_triton.py:251-252 does)
+ *   dW1, db1       : [B, NH, F, F], [B, NH, 1, F] fp32
+ *   dXQ, dXV, dXK  : [B, NH, NC, CS, F], d_eta : [B, NH, NC, CS, CS], all dtype dt_grad
+ * `scratch` must hold ttt_linear_bwd_scratch_bytes(...) bytes (its contents are
+ * overwritten; no initialisation needed).
+ */
+int ttt_linear_bwd(int B, int NH, int NC, int CS, int F, int checkpoint_group_size,
+                   const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
+                   const float* W1_ckpt, const float* b1_ckpt,
+                   const void* XQ, int dt_xq, const void* XV, int dt_xv, const void* XK, int dt_xk,
+                   const void* eta, int dt_eta,
+                   const void* dXQW, int dt_dout,
+                   float* d_ln_w, float* d_ln_b, float* dW1, float* db1,
+                   void* dXQ, void* dXV, void* dXK, void* d_eta, int dt_grad,
+                   void* scratch, size_t scratch_bytes, void* stream);
+
+/*
+ * TTT-MLP forward scan (F -> FF -> F, tanh-GELU). Replaces the launch of
+ * `ttt_mlp_scan_forward` in mlp_triton.py:130-178 (TritonMLP._forward_core) and, with
+ * FF == F, the F x F launch of mlp_triton_back.py:109-146. Dual form of
+ * ops/ttt_mlp.py:9-67. Besides XQW, the final state and the group-start checkpoints, it
+ * writes the memo states: the state AFTER mini-batch i for every i with
+ * i % memo_segment_size == 0 (kernels/mlp_forward.py:193-226). Memo pointers may all be
+ * NULL to skip them.
+ */
+int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_group_size, int memo_segment_size,
+                const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
+                const float* W1_init, const float* b1_init, const float* W2_init, const float* b2_init,
+                const void* XQ, int dt_xq, const void* XV, int dt_xv, const void* XK, int dt_xk,
+                const void* eta, int dt_eta,
+                void* XQW, int dt_out,
+                float* W1_last, float* b1_last, float* W2_last, float* b2_last,
+                float* W1_ckpt, float* b1_ckpt, float* W2_ckpt, float* b2_ckpt,
+                float* W1_memo, float* b1_memo, float* W2_memo, float* b2_memo,
+                void* stream);
+
+/* Bytes of scratch ttt_mlp_bwd needs for these sizes. */
+size_t ttt_mlp_bwd_scratch_bytes(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_group_size);
+
+/*
+ * TTT-MLP backward. Replaces the launch of `ttt_mlp_scan_backward` in
+ * mlp_triton.py:274-333 (and the F x F one of mlp_triton_back.py:238-293), with the full
+ * dual-form gradients of ops/ttt_mlp.py. Outputs as ttt_linear_bwd plus dW2/db2
+ * ([B, NH, FF, F], [B, NH, 1, F] fp32); dW1/db1 are [B, NH, F, FF], [B, NH, 1, FF].
+ */
+int ttt_mlp_bwd(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_group_size,
+                const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
+                const float* W1_ckpt, const float* b1_ckpt, const float* W2_ckpt, const float* b2_ckpt,
+                const void* XQ, int dt_xq, const void* XV, int dt_xv, const void* XK, int dt_xk,
+                const void* eta, int dt_eta,
+                const void* dXQW, int dt_dout,
+                float* d_ln_w, float* d_ln_b, float* dW1, float* db1, float* dW2, float* db2,
+                void* dXQ, void* dXV, void* dXK, void* d_eta, int dt_grad,
+                void* scratch, size_t scratch_bytes, void* stream);
+
+/*
+ * Read-out of a frozen (memo) MLP state. Replaces `mlp_cached_readout_triton`
+ * (kernels/mlp_cached_readout.py:112-143):
+ *   out = XQ + LN(gelu(XQ W1 + b1) W2 + b2)   (LayerNorm eps 1e-6, fp32 output)
+ * XQ is [B, NH, NCseg, CS, F] contiguous. The state tensors may be strided in their
+ * two leading dimensions (the reference passes non-contiguous memo slices
+ * W1_memo[:, :, j]); *_sb / *_sh are their batch / head strides in elements, and the
+ * trailing matrix of each (b, h) must be contiguous. Unlike the shipped Triton kernel,
+ * every (b, h) is read and written at its own offset.
+ */
+int ttt_mlp_cached_readout(int B, int NH, int NCseg, int CS, int F, int FF,
+                           const void* XQ, int dt_xq,
+                           const float* W1, long long W1_sb, long long W1_sh,
+                           const float* b1, long long b1_sb, long long b1_sh,
+                           const float* W2, long long W2_sb, long long W2_sh,
+                           const float* b2, long long b2_sb, long long b2_sh,
+                           const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
+                           float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TTT_B200_H_ */

@@ -1,0 +1,258 @@
+"""CPU oracle for the TTT-Linear / TTT-MLP mini-batch dual-form scan.
+
+TEST INFRASTRUCTURE ONLY. This module is the checker the CUDA path is compared
+against; it is never the thing measured or shipped. Only ``tests/``,
+``__graft_entry__.smoke()`` and the ``cpu_baseline`` / ``--impl reference`` legs of
+``bench.py`` may import it. The product path (``ttt-triton_b200/``) never imports it
+and fails loudly when its CUDA library is missing.
+
+What it restates (reference paths are relative to the Ali-Najar/ttt-triton root):
+
+* ``ln_fwd``             -> ops/ttt_utils.py:4-18   (biased variance, eps 1e-8)
+* ``ln_fused_l2_bwd``    -> ops/ttt_utils.py:21-48  (closed-form d/dx of 1/2||LN(x)-t||^2)
+* ``gelu_bwd``           -> ops/ttt_utils.py:51-54  (tanh-GELU derivative, truncated constants)
+* ``linear_step``        -> ops/ttt_linear.py:8-54  (compute_mini_batch, dual form)
+* ``mlp_step``           -> ops/ttt_mlp.py:9-67     (compute_mini_batch, dual form)
+* ``ttt_linear``/``ttt_mlp`` -> ops/ttt_linear.py:57-84, ops/ttt_mlp.py:70-99 and the
+  scan driver utils.py:126-161. Activation checkpointing there changes memory only,
+  not values, so the oracle runs the plain loop.
+* checkpoint / memo / final-state side outputs -> kernels/linear_forward.py:54-73,147-148
+  and kernels/mlp_forward.py:83-117,193-237 (state at the START of every checkpoint
+  group; memo = state AFTER mini-batch i for i % memo_segment_size == 0).
+* ``mlp_cached_readout`` -> kernels/mlp_cached_readout.py:7-109,112-143 with the
+  (b, h) offsets the kernel intends (its shipped offsets drop b and h, so only the
+  (0, 0) slice of the shipped kernel is meaningful; the goldens use B = NH = 1).
+
+Parity is pinned by ``tests/golden/*.npz``, generated from the reference's own
+``ops/`` package and Triton kernel (``tests/golden/make_golden.py``) and checked by
+``tests/test_oracle.py``. Gradients come from torch autograd through this
+restatement, exactly as the reference's ``ops/`` path gets them; ``dual_bwd.py``
+holds the hand-derived backward the CUDA kernels implement and is checked against
+these autograd gradients.
+
+Everything runs in the dtype of the inputs (the tests use float64).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as Fn
+
+LN_EPS = 1e-8  # ops/ttt_utils.py:4,21
+READOUT_EPS = 1e-6  # kernels/mlp_cached_readout.py:99
+
+
+# --------------------------------------------------------------------------- helpers
+def ln_fwd(x, gamma, beta, eps=LN_EPS):
+    """LayerNorm forward, biased variance (ops/ttt_utils.py:4-18)."""
+    mu = x.mean(dim=-1, keepdim=True)
+    var = x.var(dim=-1, keepdim=True, unbiased=False)
+    std = torch.sqrt(var + eps)
+    return gamma * ((x - mu) / std) + beta
+
+
+def ln_fused_l2_bwd(x, l2_target, gamma, beta, eps=LN_EPS):
+    """Gradient of 1/2 ||LN(x) - target||^2 w.r.t. x (ops/ttt_utils.py:21-48)."""
+    D = x.shape[-1]
+    mu = x.mean(dim=-1, keepdim=True)
+    var = x.var(dim=-1, keepdim=True, unbiased=False)
+    std = torch.sqrt(var + eps)
+    x_hat = (x - mu) / std
+    y = gamma * x_hat + beta
+    grad_output = y - l2_target
+    grad_x_hat = grad_output * gamma
+    return (
+        (1.0 / D)
+        * (
+            D * grad_x_hat
+            - grad_x_hat.sum(dim=-1, keepdim=True)
+            - x_hat * (grad_x_hat * x_hat).sum(dim=-1, keepdim=True)
+        )
+        / std
+    )
+
+
+def gelu_bwd(x):
+    """tanh-GELU derivative with the reference's truncated constants (ops/ttt_utils.py:51-54)."""
+    tanh_out = torch.tanh(0.79788456 * x * (1 + 0.044715 * x * x))
+    return 0.5 * x * ((1 - tanh_out * tanh_out) * (0.79788456 + 0.1070322243 * x * x)) + 0.5 * (1 + tanh_out)
+
+
+def gelu_tanh(x):
+    """F.gelu(approximate="tanh") as used by ops/ttt_mlp.py:16,28."""
+    return Fn.gelu(x, approximate="tanh")
+
+
+# --------------------------------------------------------------------------- one step
+def linear_step(W, b, ln_w, ln_b, XQ, XK, XV, eta):
+    """One mini-batch of TTT-Linear in dual form (ops/ttt_linear.py:8-54).
+
+    Shapes (leading dims broadcast): XQ/XK/XV [B,NH,CS,F], eta [B,NH,CS,CS],
+    W [B,NH,F,F], b [B,NH,1,F], ln_w/ln_b [NH,1,F]. Returns (W', b', XQW).
+    """
+    Z1 = XK @ W + b
+    target = XV - XK
+    G = ln_fused_l2_bwd(Z1, target, ln_w, ln_b)
+    Attn = XQ @ XK.transpose(-2, -1)
+    b_bar = b - eta @ G
+    Z1_bar = XQ @ W - (eta * Attn) @ G + b_bar
+    last_eta = eta[:, :, -1, :, None]
+    W_new = W - (last_eta * XK).transpose(-1, -2) @ G
+    b_new = b - torch.sum(last_eta * G, dim=-2, keepdim=True)
+    return W_new, b_new, XQ + ln_fwd(Z1_bar, ln_w, ln_b)
+
+
+def mlp_step(W1, b1, W2, b2, ln_w, ln_b, XQ, XK, XV, eta):
+    """One mini-batch of TTT-MLP in dual form (ops/ttt_mlp.py:9-67)."""
+    Z1 = XK @ W1 + b1
+    X2 = gelu_tanh(Z1)
+    Z2 = X2 @ W2 + b2
+    target = XV - XK
+    G2 = ln_fused_l2_bwd(Z2, target, ln_w, ln_b)
+    G1 = G2 @ W2.transpose(-2, -1) * gelu_bwd(Z1)
+    Attn1 = XQ @ XK.transpose(-2, -1)
+    b1_bar = b1 - eta @ G1
+    Z1_bar = XQ @ W1 - (eta * Attn1) @ G1 + b1_bar
+    X2_bar = gelu_tanh(Z1_bar)
+    Attn2 = X2_bar @ X2.transpose(-2, -1)
+    b2_bar = b2 - eta @ G2
+    Z2_bar = X2_bar @ W2 - (eta * Attn2) @ G2 + b2_bar
+    last_eta = eta[:, :, -1, :, None]
+    W1_new = W1 - (last_eta * XK).transpose(-1, -2) @ G1
+    b1_new = b1 - torch.sum(last_eta * G1, dim=-2, keepdim=True)
+    W2_new = W2 - (last_eta * X2).transpose(-1, -2) @ G2
+    b2_new = b2 - torch.sum(last_eta * G2, dim=-2, keepdim=True)
+    return W1_new, b1_new, W2_new, b2_new, XQ + ln_fwd(Z2_bar, ln_w, ln_b)
+
+
+# --------------------------------------------------------------------------- scans
+def linear_scan(ln_w, ln_b, W1, b1, XQ, XV, XK, eta, checkpoint_group_size=1):
+    """TTT-Linear over the whole sequence, kernel layout in and out.
+
+    Inputs follow ``TritonLinear.apply`` (linear_triton.py:15-53): XQ/XV/XK
+    [B,NH,NC,CS,F], eta [B,NH,NC,CS,CS], W1 [B,NH,F,F], b1 [B,NH,1,F], ln [NH,F].
+    Returns a dict with XQW [B,NH,NC,CS,F], W_last, b_last and the checkpoints
+    [B,NH,K,F,F] / [B,NH,K,1,F] (state at the start of each group,
+    kernels/linear_forward.py:55-73).
+    """
+    B, NH, NC, CS, F = XQ.shape
+    ckpt = max(int(checkpoint_group_size), 1)
+    lw = ln_w.reshape(NH, 1, F)
+    lb = ln_b.reshape(NH, 1, F)
+    W, b = W1, b1
+    outs, W_ck, b_ck = [], [], []
+    for n in range(NC):
+        if n % ckpt == 0:
+            W_ck.append(W)
+            b_ck.append(b)
+        W, b, o = linear_step(W, b, lw, lb, XQ[:, :, n], XK[:, :, n], XV[:, :, n], eta[:, :, n])
+        outs.append(o)
+    return {
+        "XQW": torch.stack(outs, dim=2),
+        "W_last": W,
+        "b_last": b,
+        "W_ckpt": torch.stack(W_ck, dim=2),
+        "b_ckpt": torch.stack(b_ck, dim=2),
+    }
+
+
+def mlp_scan(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, checkpoint_group_size=1, memo_segment_size=1):
+    """TTT-MLP over the whole sequence, kernel layout (mlp_triton.py:15-62).
+
+    Returns XQW, final states, checkpoints (start of each group) and memo states
+    (state after mini-batch i for i % memo_segment_size == 0,
+    kernels/mlp_forward.py:193-226), each [B,NH,K|NS,...].
+    """
+    B, NH, NC, CS, F = XQ.shape
+    ckpt = max(int(checkpoint_group_size), 1)
+    memo = max(int(memo_segment_size), 1)
+    lw = ln_w.reshape(NH, 1, F)
+    lb = ln_b.reshape(NH, 1, F)
+    st = (W1, b1, W2, b2)
+    outs = []
+    ck = [[], [], [], []]
+    mm = [[], [], [], []]
+    for n in range(NC):
+        if n % ckpt == 0:
+            for i in range(4):
+                ck[i].append(st[i])
+        *st, o = mlp_step(*st, lw, lb, XQ[:, :, n], XK[:, :, n], XV[:, :, n], eta[:, :, n])
+        outs.append(o)
+        if n % memo == 0:
+            for i in range(4):
+                mm[i].append(st[i])
+    res = {"XQW": torch.stack(outs, dim=2)}
+    for i, name in enumerate(("W1", "b1", "W2", "b2")):
+        res[name + "_last"] = st[i]
+        res[name + "_ckpt"] = torch.stack(ck[i], dim=2)
+        res[name + "_memo"] = torch.stack(mm[i], dim=2)
+    return res
+
+
+def ttt_linear(XK, XQ, XV, eta, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, checkpoint_group_size):
+    """``ops.ttt_linear`` signature and output layout [B,NC,CS,NH,F] (ops/ttt_linear.py:57-84)."""
+    out = linear_scan(ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, XQ, XV, XK, eta, checkpoint_group_size)
+    return out["XQW"].permute(0, 2, 3, 1, 4)
+
+
+def ttt_mlp(XK, XQ, XV, eta, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, checkpoint_group_size):
+    """``ops.ttt_mlp`` signature and output layout [B,NC,CS,NH,F] (ops/ttt_mlp.py:70-99)."""
+    out = mlp_scan(ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ, XV, XK, eta, checkpoint_group_size)
+    return out["XQW"].permute(0, 2, 3, 1, 4)
+
+
+def mlp_cached_readout(XQ_seg, W1, b1, W2, b2, ln_w, ln_b, eps=READOUT_EPS):
+    """XQ + LN(gelu(XQ W1 + b1) W2 + b2) for a frozen state (kernels/mlp_cached_readout.py:88-101,143).
+
+    XQ_seg [B,NH,NCseg,CS,F]; W1 [B,NH,F,FF]; b1 [B,NH,1,FF]; W2 [B,NH,FF,F];
+    b2 [B,NH,1,F]; ln [NH,F]. The GELU is the kernel's tanh form
+    (kernels/utils.py:9-14), i.e. the same function as F.gelu(approximate="tanh").
+    """
+    B, NH, NCs, CS, F = XQ_seg.shape
+    Z1 = XQ_seg @ W1[:, :, None] + b1[:, :, None]
+    X2 = gelu_tanh(Z1)
+    Z2 = X2 @ W2[:, :, None] + b2[:, :, None]
+    lw = ln_w.reshape(1, NH, 1, 1, F)
+    lb = ln_b.reshape(1, NH, 1, 1, F)
+    return XQ_seg + ln_fwd(Z2, lw, lb, eps=eps)
+
+
+# --------------------------------------------------------------------------- gradients
+LINEAR_GRAD_NAMES = ("ln_w", "ln_b", "W1", "b1", "XQ", "XV", "XK", "eta")
+MLP_GRAD_NAMES = ("ln_w", "ln_b", "W1", "b1", "W2", "b2", "XQ", "XV", "XK", "eta")
+
+
+def linear_grads(inp, dO):
+    """Autograd gradients of <XQW, dO> w.r.t. every TritonLinear input (order of linear_triton.py:254-265)."""
+    leaves = {k: inp[k].detach().clone().requires_grad_(True) for k in LINEAR_GRAD_NAMES}
+    out = linear_scan(leaves["ln_w"], leaves["ln_b"], leaves["W1"], leaves["b1"], leaves["XQ"], leaves["XV"], leaves["XK"], leaves["eta"])
+    out["XQW"].backward(dO)
+    return {k: leaves[k].grad.detach() for k in LINEAR_GRAD_NAMES}, {k: v.detach() for k, v in out.items()}
+
+
+def mlp_grads(inp, dO):
+    """Autograd gradients of <XQW, dO> w.r.t. every TritonMLP input (order of mlp_triton.py:338-351)."""
+    leaves = {k: inp[k].detach().clone().requires_grad_(True) for k in MLP_GRAD_NAMES}
+    out = mlp_scan(
+        leaves["ln_w"], leaves["ln_b"], leaves["W1"], leaves["b1"], leaves["W2"], leaves["b2"],
+        leaves["XQ"], leaves["XV"], leaves["XK"], leaves["eta"],
+    )
+    out["XQW"].backward(dO)
+    return {k: leaves[k].grad.detach() for k in MLP_GRAD_NAMES}, {k: v.detach() for k, v in out.items()}
+
+
+def rel_l2(a, b):
+    """Relative L2 error ||a - b|| / ||b|| in float64 (the parity metric of the build)."""
+    a = torch.as_tensor(a).double()
+    b = torch.as_tensor(b).double()
+    den = torch.linalg.vector_norm(b)
+    num = torch.linalg.vector_norm(a - b)
+    if den == 0:
+        return float(num)
+    return float(num / den)
+
+
+def num_checkpoints(NC, ckpt):
+    return math.ceil(NC / max(int(ckpt), 1))

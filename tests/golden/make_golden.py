@@ -1,0 +1,145 @@
+"""Generate the golden vectors that pin the CPU oracle to the reference.
+
+Run in a container that has the reference checkout (read-only is fine):
+
+    python tests/golden/make_golden.py /path/to/ttt-triton
+
+It imports the reference's own ``ops`` package (the PyTorch dual-form path,
+ops/ttt_linear.py:57-84, ops/ttt_mlp.py:70-99) with TorchDynamo disabled (CPU Inductor
+cannot build here) and ``forecast`` imported first (ttt_layer <-> forecast import
+cycle), runs it in float64 on seeded float32-representable inputs, and takes gradients
+with torch autograd exactly as the reference's training path does. The cached-readout
+golden runs the reference's Triton kernel (kernels/mlp_cached_readout.py:7-109) under
+the Triton CPU interpreter at B = NH = 1, the only slice its offsets address correctly.
+
+Outputs ``tests/golden/*.npz`` (float32 storage). The GPU box never runs this script.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+
+os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
+os.environ.setdefault("TRITON_INTERPRET", "1")
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(REPO, "ttt-triton_b200"))
+import synthetic  # noqa: E402  (seeded generators shared with the tests and bench)
+
+sys.path.remove(os.path.join(REPO, "ttt-triton_b200"))
+for name in [m for m in sys.modules if m == "ops" or m.startswith("ops.") or m == "kernels" or m.startswith("kernels.")]:
+    del sys.modules[name]
+
+
+def _np(t):
+    return t.detach().to(torch.float32).cpu().numpy()
+
+
+def _grads(fn, leaves, dO):
+    leaves = {k: v.detach().clone().requires_grad_(True) for k, v in leaves.items()}
+    out = fn(**leaves)
+    out.backward(dO)
+    return out.detach(), {k: v.grad.detach() for k, v in leaves.items()}
+
+
+def linear_case(ref_ops, B, NH, NC, F, ckpt, eta_mode, seed, with_grads=True, perturb=True):
+    d = synthetic.make_linear_inputs(B, NH, NC, 16, F, seed=seed, eta_mode=eta_mode)
+    if perturb:
+        d = synthetic.perturb_params(d, seed=seed + 7)
+    d = {k: v.float() for k, v in d.items()}  # float32-representable inputs
+    d64 = {k: v.double() for k, v in d.items()}
+
+    def fn(XQ, XK, XV, eta, ln_w, ln_b, W1, b1):
+        return ref_ops.ttt_linear(XK, XQ, XV, eta, ln_w, ln_b, W1, b1, ckpt)  # [B,NC,CS,NH,F]
+
+    leaves = {k: d64[k] for k in ("XQ", "XK", "XV", "eta", "ln_w", "ln_b", "W1", "b1")}
+    res = {("in_" + k): _np(v) for k, v in d.items()}
+    res["ckpt"] = np.array(ckpt)
+    if with_grads:
+        dO = synthetic.make_upstream((B, NC, 16, NH, F), seed=seed + 1).double()
+        out, grads = _grads(fn, leaves, dO)
+        res["dO"] = _np(dO)
+        res.update({("grad_" + k): _np(v) for k, v in grads.items()})
+    else:
+        with torch.no_grad():
+            out = fn(**leaves)
+    res["out"] = _np(out)
+    return res
+
+
+def mlp_case(ref_ops, B, NH, NC, F, FF, ckpt, eta_mode, seed, with_grads=True, perturb=True):
+    d = synthetic.make_mlp_inputs(B, NH, NC, 16, F, FF, seed=seed, eta_mode=eta_mode)
+    if perturb:
+        d = synthetic.perturb_params(d, seed=seed + 7)
+    d = {k: v.float() for k, v in d.items()}
+    d64 = {k: v.double() for k, v in d.items()}
+
+    def fn(XQ, XK, XV, eta, ln_w, ln_b, W1, b1, W2, b2):
+        return ref_ops.ttt_mlp(XK, XQ, XV, eta, ln_w, ln_b, W1, b1, W2, b2, ckpt)
+
+    leaves = {k: d64[k] for k in ("XQ", "XK", "XV", "eta", "ln_w", "ln_b", "W1", "b1", "W2", "b2")}
+    res = {("in_" + k): _np(v) for k, v in d.items()}
+    res["ckpt"] = np.array(ckpt)
+    if with_grads:
+        dO = synthetic.make_upstream((B, NC, 16, NH, F), seed=seed + 1).double()
+        out, grads = _grads(fn, leaves, dO)
+        res["dO"] = _np(dO)
+        res.update({("grad_" + k): _np(v) for k, v in grads.items()})
+    else:
+        with torch.no_grad():
+            out = fn(**leaves)
+    res["out"] = _np(out)
+    return res
+
+
+def cached_readout_case(ref_root, NCs, F, FF, seed):
+    sys.path.insert(0, ref_root)
+    from kernels.mlp_cached_readout import mlp_cached_readout_kernel
+
+    g = torch.Generator().manual_seed(seed)
+    XQ = torch.randn(1, 1, NCs, 16, F, generator=g) / 8
+    W1 = torch.randn(1, 1, F, FF, generator=g) * 0.05
+    b1 = torch.randn(1, 1, 1, FF, generator=g) * 0.02
+    W2 = torch.randn(1, 1, FF, F, generator=g) * 0.05
+    b2 = torch.randn(1, 1, 1, F, generator=g) * 0.02
+    ln_w = 1 + 0.1 * torch.randn(1, F, generator=g)
+    ln_b = 0.1 * torch.randn(1, F, generator=g)
+    out = torch.empty(1, 1, NCs, 16, F)
+    # the wrapper asserts CUDA tensors (kernels/mlp_cached_readout.py:122); the kernel
+    # itself runs under the interpreter, launched as the wrapper does (:128-141)
+    mlp_cached_readout_kernel[(1, 1, NCs)](
+        XQ, W1, b1, W2, b2, ln_w, ln_b, out,
+        CS_F_stride=16 * F, F_FF_stride=F * FF, FF_F_stride=FF * F, F_stride=F, FF_stride=FF,
+        NH=1, CS=16, F=F, FF=FF, num_warps=4,
+    )
+    res = {"in_XQ": XQ, "in_W1": W1, "in_b1": b1, "in_W2": W2, "in_b2": b2, "in_ln_w": ln_w, "in_ln_b": ln_b, "out": XQ + out}
+    return {k: _np(v) for k, v in res.items()}
+
+
+def main():
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    sys.path.insert(0, ref_root)
+    import forecast  # noqa: F401  (must precede ttt_layer / ops imports in the reference)
+    import ops as ref_ops
+
+    cases = {
+        "linear_small": linear_case(ref_ops, B=2, NH=2, NC=4, F=32, ckpt=2, eta_mode="causal", seed=10),
+        "linear_equal_eta": linear_case(ref_ops, B=1, NH=2, NC=3, F=64, ckpt=16, eta_mode="equal", seed=11),
+        "linear_config0_fwd": linear_case(ref_ops, B=2, NH=4, NC=16, F=64, ckpt=16, eta_mode="causal", seed=0, with_grads=False, perturb=False),
+        "mlp_small": mlp_case(ref_ops, B=2, NH=2, NC=3, F=16, FF=64, ckpt=2, eta_mode="causal", seed=20),
+        "mlp_fxf_equal_eta": mlp_case(ref_ops, B=1, NH=2, NC=3, F=32, FF=32, ckpt=16, eta_mode="equal", seed=21),
+        "cached_readout": cached_readout_case(ref_root, NCs=3, F=32, FF=128, seed=30),
+    }
+    for name, res in cases.items():
+        path = os.path.join(HERE, name + ".npz")
+        np.savez_compressed(path, **res)
+        print(f"wrote {path} ({os.path.getsize(path) / 1024:.0f} KiB)")
+
+
+if __name__ == "__main__":
+    main()

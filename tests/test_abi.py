@@ -1,0 +1,79 @@
+"""CPU: the C-ABI library loads, exports every declared entry point, and rejects bad
+arguments on the host (before any CUDA call), plus host-side checks of the Python layer."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+import _lib
+
+HDR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "ttt_b200.h")
+
+
+def header_functions():
+    text = open(HDR).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(ttt_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_abi():
+    names = header_functions()
+    for want in ("ttt_linear_fwd", "ttt_linear_bwd", "ttt_mlp_fwd", "ttt_mlp_bwd", "ttt_mlp_cached_readout"):
+        assert want in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for name in header_functions():
+        assert hasattr(lib, name), name
+    assert sorted(_lib.exported_symbols()) == header_functions()
+    assert _lib.lib.ttt_abi_version() == 10000
+
+
+FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: every call below fails its host checks first
+
+
+def _linear_fwd(B=1, NH=1, NC=2, CS=16, F=16, ckpt=1, dt=0, null_out=False):
+    return _lib.lib.ttt_linear_fwd(
+        B, NH, NC, CS, F, ckpt, FAKE, FAKE, 0, FAKE, FAKE, FAKE, dt, FAKE, 0, FAKE, 0, FAKE, 0,
+        None if null_out else FAKE, 0, FAKE, FAKE, FAKE, FAKE, None)
+
+
+def test_host_checks_reject_bad_arguments():
+    assert _linear_fwd(B=0) == -2
+    assert "positive" in _lib.lib.ttt_last_error().decode()
+    assert _linear_fwd(CS=15) == -2
+    assert _linear_fwd(F=3) == -2
+    assert _linear_fwd(ckpt=0) == -2
+    assert _linear_fwd(dt=7) == -3
+    assert _linear_fwd(null_out=True) == -1
+    rc = _lib.lib.ttt_linear_bwd(1, 1, 4, 16, 16, 2, FAKE, FAKE, 0, FAKE, FAKE, FAKE, 0, FAKE, 0, FAKE, 0, FAKE, 0,
+                                 FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 0, FAKE, 16, None)
+    assert rc == -5 and "scratch" in _lib.lib.ttt_last_error().decode()
+
+
+def test_scratch_sizes():
+    assert _lib.lib.ttt_linear_bwd_scratch_bytes(2, 3, 10, 16, 64, 4) == 4 * 2 * 3 * 4 * 16 * 64
+    assert _lib.lib.ttt_linear_bwd_scratch_bytes(2, 3, 3, 16, 64, 16) == 4 * 2 * 3 * 3 * 16 * 64  # group clamps to NC
+    assert _lib.lib.ttt_mlp_bwd_scratch_bytes(1, 1, 8, 16, 64, 256, 4) == 4 * (2 * 64 * 256 + 4 * 16 * 320)
+    assert _lib.lib.ttt_linear_bwd_scratch_bytes(0, 1, 1, 1, 1, 1) == 0
+
+
+def test_python_layer_refuses_cpu_tensors():
+    import ops
+
+    x = torch.zeros(1, 1, 2, 16, 16)
+    eta = torch.zeros(1, 1, 2, 16, 16)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        ops.ttt_linear(x, x, x, eta, torch.ones(1, 16), torch.zeros(1, 16), torch.zeros(1, 1, 16, 16),
+                       torch.zeros(1, 1, 1, 16), 1)
+
+
+def test_dtype_codes():
+    assert _lib.dtype_code(torch.zeros(1)) == 0
+    assert _lib.dtype_code(torch.zeros(1, dtype=torch.bfloat16)) == 1
+    assert _lib.dtype_code(torch.zeros(1, dtype=torch.float16)) == 2
+    with pytest.raises(TypeError):
+        _lib.dtype_code(torch.zeros(1, dtype=torch.float64))

@@ -1,0 +1,135 @@
+"""CPU: the oracle is pinned to the reference and the hand-derived backward to autograd.
+
+* golden vectors (tests/golden/*.npz, made by tests/golden/make_golden.py from the
+  reference's own ops/ package and Triton read-out kernel) vs the oracle restatement;
+* the hand-derived dual-form backward (oracle/dual_bwd.py, the algorithm of the CUDA
+  backward) vs autograd through the oracle, for several checkpoint group sizes;
+* finite differences pin the oracle's autograd gradients;
+* known answers: eta = 0 leaves the state unchanged; with all eta rows equal the dual
+  form equals the primal (update-then-read-out) form.
+"""
+
+import pytest
+import torch
+
+import dual_bwd as D
+import synthetic as S
+import ttt_oracle as O
+from helpers import load_golden
+
+GOLD_TOL = 1e-6  # goldens are stored as float32
+
+
+def _ops_out_to_kernel(out):
+    return out.permute(0, 3, 1, 2, 4)  # [B,NC,CS,NH,F] -> [B,NH,NC,CS,F]
+
+
+@pytest.mark.parametrize("name", ["linear_small", "linear_equal_eta", "linear_config0_fwd"])
+def test_linear_oracle_matches_reference_golden(name):
+    inp, g = load_golden(name)
+    d = {k: v.double() for k, v in inp.items()}
+    out = O.ttt_linear(d["XK"], d["XQ"], d["XV"], d["eta"], d["ln_w"], d["ln_b"], d["W1"], d["b1"], int(g["ckpt"]))
+    assert O.rel_l2(out, g["out"]) < GOLD_TOL
+    if "dO" in g:
+        grads, _ = O.linear_grads(d, _ops_out_to_kernel(g["dO"].double()))
+        for k, v in grads.items():
+            assert O.rel_l2(v, g["grad_" + k]) < GOLD_TOL, k
+
+
+@pytest.mark.parametrize("name", ["mlp_small", "mlp_fxf_equal_eta"])
+def test_mlp_oracle_matches_reference_golden(name):
+    inp, g = load_golden(name)
+    d = {k: v.double() for k, v in inp.items()}
+    out = O.ttt_mlp(d["XK"], d["XQ"], d["XV"], d["eta"], d["ln_w"], d["ln_b"], d["W1"], d["b1"], d["W2"], d["b2"],
+                    int(g["ckpt"]))
+    assert O.rel_l2(out, g["out"]) < GOLD_TOL
+    grads, _ = O.mlp_grads(d, _ops_out_to_kernel(g["dO"].double()))
+    for k, v in grads.items():
+        assert O.rel_l2(v, g["grad_" + k]) < GOLD_TOL, k
+
+
+def test_cached_readout_oracle_matches_reference_kernel():
+    inp, g = load_golden("cached_readout")
+    d = {k: v.double() for k, v in inp.items()}
+    out = O.mlp_cached_readout(d["XQ"], d["W1"], d["b1"], d["W2"], d["b2"], d["ln_w"], d["ln_b"])
+    assert O.rel_l2(out, g["out"]) < 1e-6
+
+
+@pytest.mark.parametrize("eta_mode", ["causal", "equal"])
+@pytest.mark.parametrize("ckpt", [1, 3, 16])
+def test_linear_hand_backward_matches_autograd(eta_mode, ckpt):
+    d = S.perturb_params(S.make_linear_inputs(2, 2, 7, 16, 32, eta_mode=eta_mode), seed=5)
+    d = {k: v.double() for k, v in d.items()}
+    dO = S.make_upstream((2, 2, 7, 16, 32)).double()
+    ref, _ = O.linear_grads(d, dO)
+    got = D.linear_backward(d, dO, ckpt)
+    for k in ref:
+        assert O.rel_l2(got[k], ref[k]) < 1e-12, k
+
+
+@pytest.mark.parametrize("eta_mode", ["causal", "equal"])
+@pytest.mark.parametrize("ckpt", [1, 2, 16])
+def test_mlp_hand_backward_matches_autograd(eta_mode, ckpt):
+    d = S.perturb_params(S.make_mlp_inputs(2, 2, 5, 16, 16, 64, eta_mode=eta_mode), seed=5)
+    d = {k: v.double() for k, v in d.items()}
+    dO = S.make_upstream((2, 2, 5, 16, 16)).double()
+    ref, _ = O.mlp_grads(d, dO)
+    got = D.mlp_backward(d, dO, ckpt)
+    for k in ref:
+        assert O.rel_l2(got[k], ref[k]) < 1e-12, k
+
+
+def test_oracle_gradients_match_finite_differences():
+    torch.manual_seed(0)
+    d = S.perturb_params(S.make_linear_inputs(1, 1, 3, 4, 8), seed=3)
+    d = {k: v.double() for k, v in d.items()}
+    dO = S.make_upstream((1, 1, 3, 4, 8)).double()
+    grads, _ = O.linear_grads(d, dO)
+
+    def loss(dd):
+        return (O.linear_scan(dd["ln_w"], dd["ln_b"], dd["W1"], dd["b1"], dd["XQ"], dd["XV"], dd["XK"], dd["eta"])["XQW"] * dO).sum()
+
+    h = 1e-6
+    for k in ("XQ", "XK", "XV", "eta", "W1", "ln_w"):
+        flat = d[k].reshape(-1)
+        for idx in (0, flat.numel() // 2, flat.numel() - 1):
+            dp = {kk: vv.clone() for kk, vv in d.items()}
+            dm = {kk: vv.clone() for kk, vv in d.items()}
+            dp[k].reshape(-1)[idx] += h
+            dm[k].reshape(-1)[idx] -= h
+            fd = (loss(dp) - loss(dm)) / (2 * h)
+            an = grads[k].reshape(-1)[idx]
+            assert abs(float(fd - an)) <= 1e-6 * max(1.0, abs(float(an))), (k, idx, float(fd), float(an))
+
+
+def test_zero_eta_leaves_state_unchanged():
+    d = S.perturb_params(S.make_mlp_inputs(1, 2, 4, 16, 16, 32), seed=1)
+    d = {k: v.double() for k, v in d.items()}
+    d["eta"] = torch.zeros_like(d["eta"])
+    res = O.mlp_scan(d["ln_w"], d["ln_b"], d["W1"], d["b1"], d["W2"], d["b2"], d["XQ"], d["XV"], d["XK"], d["eta"])
+    for k in ("W1", "b1", "W2", "b2"):
+        assert torch.equal(res[k + "_last"], d[k])
+    lw = d["ln_w"].reshape(2, 1, 1, 16)
+    lb = d["ln_b"].reshape(2, 1, 1, 16)
+    Z1 = d["XQ"] @ d["W1"][:, :, None] + d["b1"][:, :, None]
+    ref = d["XQ"] + O.ln_fwd(O.gelu_tanh(Z1) @ d["W2"][:, :, None] + d["b2"][:, :, None], lw, lb)
+    assert O.rel_l2(res["XQW"], ref) < 1e-13
+
+
+def test_equal_eta_dual_equals_primal():
+    """All eta rows equal (what the forecaster feeds): the dual-form read-out equals the
+    primal form that updates W first and then reads out (kernels/linear_forward.py:128-145)."""
+    d = S.perturb_params(S.make_linear_inputs(2, 2, 5, 16, 32, eta_mode="equal"), seed=2)
+    d = {k: v.double() for k, v in d.items()}
+    res = O.linear_scan(d["ln_w"], d["ln_b"], d["W1"], d["b1"], d["XQ"], d["XV"], d["XK"], d["eta"])
+    lw, lb = d["ln_w"].reshape(2, 1, 32), d["ln_b"].reshape(2, 1, 32)
+    W, b = d["W1"], d["b1"]
+    outs = []
+    for n in range(5):
+        XQ, XK, XV, eta = (d[k][:, :, n] for k in ("XQ", "XK", "XV", "eta"))
+        G = O.ln_fused_l2_bwd(XK @ W + b, XV - XK, lw, lb)
+        e = eta[:, :, -1, :, None]
+        W = W - (e * XK).transpose(-1, -2) @ G
+        b = b - (e * G).sum(-2, keepdim=True)
+        outs.append(XQ + O.ln_fwd(XQ @ W + b, lw, lb))
+    assert O.rel_l2(res["XQW"], torch.stack(outs, 2)) < 1e-12

@@ -1,0 +1,249 @@
+"""Functional host side of the B200 TTT scan: shape checks, allocation, C-ABI launches.
+
+Every function here allocates its outputs with ``torch.empty`` on the inputs' device
+(as the reference wrappers do, linear_triton.py:81-88, mlp_triton.py:102-119), makes the
+inputs contiguous, and enqueues one kernel on the current CUDA stream. None of them
+synchronises the device.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from _lib import check, dtype_code, lib, ptr, require_cuda, stream_of
+
+
+def _c(t):
+    return t.contiguous()
+
+
+def _check_acts(XQ, XV, XK, eta):
+    if XQ.dim() != 5:
+        raise ValueError(f"XQ must be [B, NH, NC, CS, F], got shape {tuple(XQ.shape)}")
+    B, NH, NC, CS, F = XQ.shape
+    for name, t in (("XV", XV), ("XK", XK)):
+        if tuple(t.shape) != (B, NH, NC, CS, F):
+            raise ValueError(f"{name} must have XQ's shape {tuple(XQ.shape)}, got {tuple(t.shape)}")
+    if tuple(eta.shape) != (B, NH, NC, CS, CS):
+        raise ValueError(f"eta must be [B, NH, NC, CS, CS] = {(B, NH, NC, CS, CS)}, got {tuple(eta.shape)}")
+    return B, NH, NC, CS, F
+
+
+def _check_ln(ln_w, ln_b, NH, F):
+    for name, t in (("ttt_norm_weight", ln_w), ("ttt_norm_bias", ln_b)):
+        if t.numel() != NH * F:
+            raise ValueError(f"{name} must have NH * F = {NH * F} elements, got shape {tuple(t.shape)}")
+    if ln_w.dtype != ln_b.dtype:
+        ln_b = ln_b.to(ln_w.dtype)
+    return _c(ln_w), _c(ln_b)
+
+
+def _state(t, shape, name):
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} must be {tuple(shape)}, got {tuple(t.shape)}")
+    return t.to(torch.float32).contiguous()
+
+
+# --------------------------------------------------------------------------- Linear
+def linear_forward(ln_w, ln_b, W1, b1, XQ, XV, XK, eta, checkpoint_group_size):
+    """TTT-Linear scan forward. Returns (XQW in XQ's dtype, W_last, b_last, W_ckpt, b_ckpt)."""
+    require_cuda(ln_w, ln_b, W1, b1, XQ, XV, XK, eta)
+    B, NH, NC, CS, F = _check_acts(XQ, XV, XK, eta)
+    ckpt = int(checkpoint_group_size)
+    if ckpt <= 0:
+        raise ValueError(f"checkpoint_group_size must be positive, got {ckpt}")
+    K = math.ceil(NC / ckpt)
+    ln_w, ln_b = _check_ln(ln_w, ln_b, NH, F)
+    W1 = _state(W1, (B, NH, F, F), "W1_init")
+    b1 = _state(b1, (B, NH, 1, F), "b1_init")
+    XQ, XV, XK, eta = _c(XQ), _c(XV), _c(XK), _c(eta)
+    dev = XQ.device
+    XQW = torch.empty(B, NH, NC, CS, F, device=dev, dtype=XQ.dtype)
+    W_last = torch.empty(B, NH, F, F, device=dev, dtype=torch.float32)
+    b_last = torch.empty(B, NH, 1, F, device=dev, dtype=torch.float32)
+    W_ckpt = torch.empty(B, NH, K, F, F, device=dev, dtype=torch.float32)
+    b_ckpt = torch.empty(B, NH, K, 1, F, device=dev, dtype=torch.float32)
+    rc = lib.ttt_linear_fwd(
+        B, NH, NC, CS, F, ckpt,
+        ptr(ln_w), ptr(ln_b), dtype_code(ln_w),
+        ptr(W1), ptr(b1),
+        ptr(XQ), dtype_code(XQ), ptr(XV), dtype_code(XV), ptr(XK), dtype_code(XK),
+        ptr(eta), dtype_code(eta),
+        ptr(XQW), dtype_code(XQW),
+        ptr(W_last), ptr(b_last), ptr(W_ckpt), ptr(b_ckpt),
+        stream_of(XQ),
+    )
+    check(rc, "ttt_linear_fwd")
+    return XQW, W_last, b_last, W_ckpt, b_ckpt
+
+
+def linear_backward(ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, dXQW, checkpoint_group_size, grad_dtype=None):
+    """TTT-Linear scan backward. Returns (d_ln_w [B,NH,F] per-(b,h) partials, d_ln_b,
+    dW1, db1 (fp32), dXQ, dXV, dXK, d_eta (grad_dtype, default XQ's dtype))."""
+    require_cuda(ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, dXQW)
+    B, NH, NC, CS, F = _check_acts(XQ, XV, XK, eta)
+    ckpt = int(checkpoint_group_size)
+    ln_w, ln_b = _check_ln(ln_w, ln_b, NH, F)
+    if tuple(dXQW.shape) != tuple(XQ.shape):
+        raise ValueError(f"upstream gradient must have XQ's shape {tuple(XQ.shape)}, got {tuple(dXQW.shape)}")
+    XQ, XV, XK, eta, dXQW = _c(XQ), _c(XV), _c(XK), _c(eta), _c(dXQW)
+    W_ckpt, b_ckpt = _c(W_ckpt), _c(b_ckpt)
+    gdt = grad_dtype or XQ.dtype
+    dev = XQ.device
+    d_ln_w = torch.empty(B, NH, F, device=dev, dtype=torch.float32)
+    d_ln_b = torch.empty(B, NH, F, device=dev, dtype=torch.float32)
+    dW1 = torch.empty(B, NH, F, F, device=dev, dtype=torch.float32)
+    db1 = torch.empty(B, NH, 1, F, device=dev, dtype=torch.float32)
+    dXQ = torch.empty(B, NH, NC, CS, F, device=dev, dtype=gdt)
+    dXV = torch.empty_like(dXQ)
+    dXK = torch.empty_like(dXQ)
+    deta = torch.empty(B, NH, NC, CS, CS, device=dev, dtype=gdt)
+    nbytes = lib.ttt_linear_bwd_scratch_bytes(B, NH, NC, CS, F, ckpt)
+    scratch = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+    rc = lib.ttt_linear_bwd(
+        B, NH, NC, CS, F, ckpt,
+        ptr(ln_w), ptr(ln_b), dtype_code(ln_w),
+        ptr(W_ckpt), ptr(b_ckpt),
+        ptr(XQ), dtype_code(XQ), ptr(XV), dtype_code(XV), ptr(XK), dtype_code(XK),
+        ptr(eta), dtype_code(eta),
+        ptr(dXQW), dtype_code(dXQW),
+        ptr(d_ln_w), ptr(d_ln_b), ptr(dW1), ptr(db1),
+        ptr(dXQ), ptr(dXV), ptr(dXK), ptr(deta), dtype_code(dXQ),
+        ptr(scratch), nbytes, stream_of(XQ),
+    )
+    check(rc, "ttt_linear_bwd")
+    return d_ln_w, d_ln_b, dW1, db1, dXQ, dXV, dXK, deta
+
+
+# --------------------------------------------------------------------------- MLP
+def mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, checkpoint_group_size, memo_segment_size=None):
+    """TTT-MLP scan forward. Returns (XQW, (W1,b1,W2,b2)_last, (…)_ckpt, (…)_memo or None)."""
+    require_cuda(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta)
+    B, NH, NC, CS, F = _check_acts(XQ, XV, XK, eta)
+    FF = W1.shape[-1]
+    ckpt = int(checkpoint_group_size)
+    if ckpt <= 0:
+        raise ValueError(f"checkpoint_group_size must be positive, got {ckpt}")
+    K = math.ceil(NC / ckpt)
+    ln_w, ln_b = _check_ln(ln_w, ln_b, NH, F)
+    W1 = _state(W1, (B, NH, F, FF), "W1_init")
+    b1 = _state(b1, (B, NH, 1, FF), "b1_init")
+    W2 = _state(W2, (B, NH, FF, F), "W2_init")
+    b2 = _state(b2, (B, NH, 1, F), "b2_init")
+    XQ, XV, XK, eta = _c(XQ), _c(XV), _c(XK), _c(eta)
+    dev = XQ.device
+    f32 = dict(device=dev, dtype=torch.float32)
+    XQW = torch.empty(B, NH, NC, CS, F, device=dev, dtype=XQ.dtype)
+    last = (torch.empty(B, NH, F, FF, **f32), torch.empty(B, NH, 1, FF, **f32),
+            torch.empty(B, NH, FF, F, **f32), torch.empty(B, NH, 1, F, **f32))
+    ck = (torch.empty(B, NH, K, F, FF, **f32), torch.empty(B, NH, K, 1, FF, **f32),
+          torch.empty(B, NH, K, FF, F, **f32), torch.empty(B, NH, K, 1, F, **f32))
+    memo = None
+    memo_seg = 1
+    if memo_segment_size is not None:
+        memo_seg = int(memo_segment_size)
+        if memo_seg <= 0:
+            raise ValueError(f"memo_segment_size must be positive, got {memo_seg}")
+        NS = math.ceil(NC / memo_seg)
+        memo = (torch.empty(B, NH, NS, F, FF, **f32), torch.empty(B, NH, NS, 1, FF, **f32),
+                torch.empty(B, NH, NS, FF, F, **f32), torch.empty(B, NH, NS, 1, F, **f32))
+    mp = memo if memo is not None else (None, None, None, None)
+    rc = lib.ttt_mlp_fwd(
+        B, NH, NC, CS, F, FF, ckpt, memo_seg,
+        ptr(ln_w), ptr(ln_b), dtype_code(ln_w),
+        ptr(W1), ptr(b1), ptr(W2), ptr(b2),
+        ptr(XQ), dtype_code(XQ), ptr(XV), dtype_code(XV), ptr(XK), dtype_code(XK),
+        ptr(eta), dtype_code(eta),
+        ptr(XQW), dtype_code(XQW),
+        *[ptr(t) for t in last], *[ptr(t) for t in ck], *[ptr(t) for t in mp],
+        stream_of(XQ),
+    )
+    check(rc, "ttt_mlp_fwd")
+    return XQW, last, ck, memo
+
+
+def mlp_backward(ln_w, ln_b, ckpts, XQ, XV, XK, eta, dXQW, checkpoint_group_size, grad_dtype=None):
+    """TTT-MLP scan backward. ckpts = (W1, b1, W2, b2) checkpoints from mlp_forward.
+    Returns (d_ln_w, d_ln_b [B,NH,F] partials, dW1, db1, dW2, db2, dXQ, dXV, dXK, d_eta)."""
+    W1c, b1c, W2c, b2c = (_c(t) for t in ckpts)
+    require_cuda(ln_w, ln_b, W1c, b1c, W2c, b2c, XQ, XV, XK, eta, dXQW)
+    B, NH, NC, CS, F = _check_acts(XQ, XV, XK, eta)
+    FF = W1c.shape[-1]
+    ckpt = int(checkpoint_group_size)
+    ln_w, ln_b = _check_ln(ln_w, ln_b, NH, F)
+    if tuple(dXQW.shape) != tuple(XQ.shape):
+        raise ValueError(f"upstream gradient must have XQ's shape {tuple(XQ.shape)}, got {tuple(dXQW.shape)}")
+    XQ, XV, XK, eta, dXQW = _c(XQ), _c(XV), _c(XK), _c(eta), _c(dXQW)
+    gdt = grad_dtype or XQ.dtype
+    dev = XQ.device
+    f32 = dict(device=dev, dtype=torch.float32)
+    d_ln_w = torch.empty(B, NH, F, **f32)
+    d_ln_b = torch.empty(B, NH, F, **f32)
+    dW1 = torch.empty(B, NH, F, FF, **f32)
+    db1 = torch.empty(B, NH, 1, FF, **f32)
+    dW2 = torch.empty(B, NH, FF, F, **f32)
+    db2 = torch.empty(B, NH, 1, F, **f32)
+    dXQ = torch.empty(B, NH, NC, CS, F, device=dev, dtype=gdt)
+    dXV = torch.empty_like(dXQ)
+    dXK = torch.empty_like(dXQ)
+    deta = torch.empty(B, NH, NC, CS, CS, device=dev, dtype=gdt)
+    nbytes = lib.ttt_mlp_bwd_scratch_bytes(B, NH, NC, CS, F, FF, ckpt)
+    scratch = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
+    rc = lib.ttt_mlp_bwd(
+        B, NH, NC, CS, F, FF, ckpt,
+        ptr(ln_w), ptr(ln_b), dtype_code(ln_w),
+        ptr(W1c), ptr(b1c), ptr(W2c), ptr(b2c),
+        ptr(XQ), dtype_code(XQ), ptr(XV), dtype_code(XV), ptr(XK), dtype_code(XK),
+        ptr(eta), dtype_code(eta),
+        ptr(dXQW), dtype_code(dXQW),
+        ptr(d_ln_w), ptr(d_ln_b), ptr(dW1), ptr(db1), ptr(dW2), ptr(db2),
+        ptr(dXQ), ptr(dXV), ptr(dXK), ptr(deta), dtype_code(dXQ),
+        ptr(scratch), nbytes, stream_of(XQ),
+    )
+    check(rc, "ttt_mlp_bwd")
+    return d_ln_w, d_ln_b, dW1, db1, dW2, db2, dXQ, dXV, dXK, deta
+
+
+def _lead_strides(t, inner_numel, name):
+    """Batch / head element strides of a [B, NH, ...] fp32 state whose trailing block is contiguous."""
+    if t.dtype != torch.float32:
+        t = t.to(torch.float32)
+    inner = t.shape[2:]
+    expect = 1
+    for d in range(t.dim() - 1, 1, -1):
+        if t.stride(d) != expect:
+            t = t.contiguous()
+            break
+        expect *= t.shape[d]
+    if math.prod(inner) != inner_numel:
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, trailing block must hold {inner_numel} elements")
+    return t, t.stride(0), t.stride(1)
+
+
+def mlp_cached_readout(XQ_seg, W1, b1, W2, b2, ln_w, ln_b):
+    """XQ_seg + LN(gelu(XQ_seg W1 + b1) W2 + b2) in fp32 (LN eps 1e-6)."""
+    require_cuda(XQ_seg, W1, b1, W2, b2, ln_w, ln_b)
+    if XQ_seg.dim() != 5:
+        raise ValueError(f"XQ_seg must be [B, NH, NCseg, CS, F], got {tuple(XQ_seg.shape)}")
+    B, NH, NCs, CS, F = XQ_seg.shape
+    FF = W1.shape[-1]
+    for name, t, lead in (("W1", W1, (B, NH)), ("b1", b1, (B, NH)), ("W2", W2, (B, NH)), ("b2", b2, (B, NH))):
+        if tuple(t.shape[:2]) != lead:
+            raise ValueError(f"{name} must start with [B, NH] = {lead}, got {tuple(t.shape)}")
+    W1, W1_sb, W1_sh = _lead_strides(W1, F * FF, "W1")
+    b1, b1_sb, b1_sh = _lead_strides(b1, FF, "b1")
+    W2, W2_sb, W2_sh = _lead_strides(W2, FF * F, "W2")
+    b2, b2_sb, b2_sh = _lead_strides(b2, F, "b2")
+    ln_w, ln_b = _check_ln(ln_w, ln_b, NH, F)
+    XQ_seg = _c(XQ_seg)
+    out = torch.empty(B, NH, NCs, CS, F, device=XQ_seg.device, dtype=torch.float32)
+    rc = lib.ttt_mlp_cached_readout(
+        B, NH, NCs, CS, F, FF, ptr(XQ_seg), dtype_code(XQ_seg),
+        ptr(W1), W1_sb, W1_sh, ptr(b1), b1_sb, b1_sh,
+        ptr(W2), W2_sb, W2_sh, ptr(b2), b2_sb, b2_sh,
+        ptr(ln_w), ptr(ln_b), dtype_code(ln_w), ptr(out), stream_of(XQ_seg),
+    )
+    check(rc, "ttt_mlp_cached_readout")
+    return out

@@ -1,0 +1,114 @@
+"""ctypes binding of libttt_b200.so (the C ABI declared in include/ttt_b200.h).
+
+The library must exist: there is no fallback path. Import fails with a clear message
+when it has not been built (``python ttt-triton_b200/build.py``), and every call checks
+that its tensors live on a CUDA device.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libttt_b200.so")
+
+DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_Z = ctypes.c_size_t
+_L = ctypes.c_longlong
+
+_SIGNATURES = {
+    "ttt_abi_version": ([], _I),
+    "ttt_last_error": ([], ctypes.c_char_p),
+    "ttt_linear_fwd": ([_I] * 6 + [_P, _P, _I, _P, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P], _I),
+    "ttt_linear_bwd_scratch_bytes": ([_I] * 6, _Z),
+    "ttt_linear_bwd": (
+        [_I] * 6
+        + [_P, _P, _I, _P, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I]
+        + [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _Z, _P],
+        _I,
+    ),
+    "ttt_mlp_fwd": (
+        [_I] * 8
+        + [_P, _P, _I, _P, _P, _P, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I]
+        + [_P] * 12
+        + [_P],
+        _I,
+    ),
+    "ttt_mlp_bwd_scratch_bytes": ([_I] * 7, _Z),
+    "ttt_mlp_bwd": (
+        [_I] * 7
+        + [_P, _P, _I, _P, _P, _P, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I]
+        + [_P] * 10
+        + [_I, _P, _Z, _P],
+        _I,
+    ),
+    "ttt_mlp_cached_readout": (
+        [_I] * 6 + [_P, _I] + [_P, _L, _L] * 4 + [_P, _P, _I, _P, _P],
+        _I,
+    ),
+}
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build the CUDA library first (python ttt-triton_b200/build.py); "
+            "this package has no CPU or Triton fallback"
+        )
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (args, res) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    return lib
+
+
+lib = _load()
+
+
+def exported_symbols():
+    """Names of the C-ABI entry points this binding expects (all must resolve)."""
+    return list(_SIGNATURES)
+
+
+def check(rc, name):
+    if rc != 0:
+        msg = lib.ttt_last_error().decode(errors="replace")
+        raise RuntimeError(f"{name} failed (status {rc}): {msg}")
+
+
+def dtype_code(t):
+    try:
+        return DTYPE_CODES[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}; expected float32, bfloat16 or float16") from None
+
+
+def ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def stream_of(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def require_cuda(*tensors):
+    dev = None
+    for t in tensors:
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"expected a torch.Tensor, got {type(t).__name__}")
+        if not t.is_cuda:
+            raise RuntimeError(
+                "ttt-b200 kernels need CUDA tensors (there is no CPU fallback); got a tensor on " + str(t.device)
+            )
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"all tensors must be on one device, got {dev} and {t.device}")
+    return dev

@@ -1,0 +1,324 @@
+// Shared device helpers for the TTT dual-form scan kernels (sm_100a).
+//
+// Layout conventions (all kernels): one (batch, head) pair is a "stream"; stream
+// s = b * NH + h. Activations are [B, NH, NC, CS, F] contiguous, eta is
+// [B, NH, NC, CS, CS], inner states are fp32 [B, NH, rows, cols].
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ttt {
+
+enum DType : int { DT_F32 = 0, DT_BF16 = 1, DT_F16 = 2 };
+
+constexpr float kLnEps = 1e-8f;       // ops/ttt_utils.py:4,21
+constexpr float kReadoutEps = 1e-6f;  // kernels/mlp_cached_readout.py:99
+
+// ----------------------------------------------------------------- typed element access
+__device__ __forceinline__ float ld_elem(const void* p, long long i, int dt) {
+  if (dt == DT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  if (dt == DT_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void st_elem(void* p, long long i, int dt, float v) {
+  if (dt == DT_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  } else if (dt == DT_F16) {
+    reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  } else {
+    reinterpret_cast<float*>(p)[i] = v;
+  }
+}
+
+// Copy n elements of a typed global array (offset base) into fp32 shared memory.
+__device__ __forceinline__ void load_tile(float* dst, const void* src, long long base, int n, int dt) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = ld_elem(src, base + i, dt);
+}
+
+__device__ __forceinline__ void store_tile(void* dst, long long base, const float* src, int n, int dt) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) st_elem(dst, base + i, dt, src[i]);
+}
+
+__device__ __forceinline__ void copy_f32(float* dst, const float* src, int n) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+}
+
+// ----------------------------------------------------------------- block matmul (fp32 FMA)
+// C[m][n] = alpha * sum_k A(m,k) B(k,n) + beta * C[m][n]   (beta == 0 never reads C)
+// A(m,k) = TA ? A[k*lda + m] : A[m*lda + k];  B(k,n) = TB ? B[n*ldb + k] : B[k*ldb + n]
+// Pointers are generic (shared or global). M and N must be even. The whole block
+// participates; callers synchronise before (inputs ready) and after (outputs ready).
+// Every output element is owned by one thread, and the owner depends only on (M, N),
+// so two calls with the same (M, N) may update the same C without a barrier between.
+template <bool TA, bool TB>
+__device__ __forceinline__ void block_mm(float* C, int ldc, const float* A, int lda, const float* B, int ldb,
+                                         int M, int N, int K, float alpha, float beta) {
+  const int tn = N >> 1;
+  const int tiles = (M >> 1) * tn;
+  for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
+    const int m = (t / tn) << 1;
+    const int n = (t % tn) << 1;
+    float c00 = 0.f, c01 = 0.f, c10 = 0.f, c11 = 0.f;
+#pragma unroll 4
+    for (int k = 0; k < K; ++k) {
+      const float a0 = TA ? A[(long long)k * lda + m] : A[(long long)m * lda + k];
+      const float a1 = TA ? A[(long long)k * lda + m + 1] : A[(long long)(m + 1) * lda + k];
+      const float b0 = TB ? B[(long long)n * ldb + k] : B[(long long)k * ldb + n];
+      const float b1 = TB ? B[(long long)(n + 1) * ldb + k] : B[(long long)k * ldb + n + 1];
+      c00 = fmaf(a0, b0, c00);
+      c01 = fmaf(a0, b1, c01);
+      c10 = fmaf(a1, b0, c10);
+      c11 = fmaf(a1, b1, c11);
+    }
+    float* c0 = C + (long long)m * ldc + n;
+    float* c1 = c0 + ldc;
+    if (beta == 0.f) {
+      c0[0] = alpha * c00;
+      c0[1] = alpha * c01;
+      c1[0] = alpha * c10;
+      c1[1] = alpha * c11;
+    } else {
+      c0[0] = fmaf(alpha, c00, beta * c0[0]);
+      c0[1] = fmaf(alpha, c01, beta * c0[1]);
+      c1[0] = fmaf(alpha, c10, beta * c1[0]);
+      c1[1] = fmaf(alpha, c11, beta * c1[1]);
+    }
+  }
+}
+
+// ----------------------------------------------------------------- warp reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ----------------------------------------------------------------- GELU (tanh form)
+// Forward and its exact derivative, as F.gelu(approximate="tanh") and its autograd
+// (ops/ttt_mlp.py:16,28). tanhf is CUDA's own.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+__device__ __forceinline__ float gelu_tanh_grad(float x) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  const float t = tanhf(k0 * (x + k1 * x * x * x));
+  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k0 * (1.f + 3.f * k1 * x * x);
+}
+
+// The reference's gelu_bwd with its truncated constants (ops/ttt_utils.py:51-54) and the
+// exact derivative of that expression (what autograd applies to it).
+__device__ __forceinline__ float gelu_bwd_ref(float x) {
+  const float t = tanhf(0.79788456f * x * (1.f + 0.044715f * x * x));
+  return 0.5f * x * ((1.f - t * t) * (0.79788456f + 0.1070322243f * x * x)) + 0.5f * (1.f + t);
+}
+
+__device__ __forceinline__ float gelu_bwd_ref_grad(float x) {
+  const float a = 0.79788456f, c = 0.1070322243f, k = 0.044715f;
+  const float t = tanhf(a * x * (1.f + k * x * x));
+  const float dt = (1.f - t * t) * (a + 3.f * a * k * x * x);
+  const float poly = a + c * x * x;
+  return 0.5f * (1.f - t * t) * poly + 0.5f * x * (-2.f * t * dt * poly + (1.f - t * t) * 2.f * c * x) + 0.5f * dt;
+}
+
+// ----------------------------------------------------------------- row-wise LayerNorm pieces
+// All row functions: one warp per row (rows strided by warp count), row width F.
+
+// Row statistics: writes mean and 1/std (std = sqrt(var + eps), biased variance).
+__device__ __forceinline__ void row_stats(const float* x, int F, float eps, float& mu, float& rstd, float& stdv) {
+  const int lane = threadIdx.x & 31;
+  float s = 0.f;
+  for (int j = lane; j < F; j += 32) s += x[j];
+  mu = warp_sum(s) / F;
+  float v = 0.f;
+  for (int j = lane; j < F; j += 32) {
+    const float d = x[j] - mu;
+    v += d * d;
+  }
+  stdv = sqrtf(warp_sum(v) / F + eps);
+  rstd = 1.f / stdv;
+}
+
+// G = ln_fused_l2_bwd(Z + b, XV - XK) row by row (ops/ttt_utils.py:21-48). Z holds X W
+// on entry and Z + b on exit (bias skipped when bvec is null); G receives the gradient.
+// Optionally records each row's mean and std.
+__device__ __forceinline__ void ln_fused_rows(float* Z, float* G, const float* bvec, const float* XV, const float* XK,
+                                              const float* gam, const float* bet, int C, int F, float* mu_out,
+                                              float* std_out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int r = warp; r < C; r += nw) {
+    float* z = Z + r * F;
+    if (bvec) {
+      for (int j = lane; j < F; j += 32) z[j] += bvec[j];
+      __syncwarp();
+    }
+    float mu, rstd, sd;
+    row_stats(z, F, kLnEps, mu, rstd, sd);
+    float s1 = 0.f, s2 = 0.f;
+    for (int j = lane; j < F; j += 32) {
+      const float xh = (z[j] - mu) * rstd;
+      const float gh = (gam[j] * xh + bet[j] - (XV[r * F + j] - XK[r * F + j])) * gam[j];
+      s1 += gh;
+      s2 += gh * xh;
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    const float inv = rstd / F;
+    for (int j = lane; j < F; j += 32) {
+      const float xh = (z[j] - mu) * rstd;
+      const float gh = (gam[j] * xh + bet[j] - (XV[r * F + j] - XK[r * F + j])) * gam[j];
+      G[r * F + j] = (F * gh - s1 - xh * s2) * inv;
+    }
+    if (lane == 0 && mu_out) {
+      mu_out[r] = mu;
+      std_out[r] = sd;
+    }
+  }
+}
+
+// Backward of G = ln_fused_l2_bwd(Z, T) for every row, given dG (hand derivation of
+// autograd through ops/ttt_utils.py:21-48). Z includes its bias; mu/sd are its row
+// statistics. Writes dZ, dT (= -d_g_hat * gamma) and keeps d_g_hat in DGH for the
+// gamma/beta column sums (ln_fused_bwd_cols); DXH is scratch.
+__device__ __forceinline__ void ln_fused_bwd_rows(const float* Z, const float* mu1, const float* sd1, const float* G,
+                                                  const float* dG, const float* XV, const float* XK, const float* gam,
+                                                  const float* bet, int C, int F, float* DXH, float* DGH, float* dT,
+                                                  float* dZ) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int r = warp; r < C; r += nw) {
+    const float mu = mu1[r], sd = sd1[r], rstd = 1.f / sd;
+    float sdG = 0.f, sdGx = 0.f, sgx = 0.f, sdGG = 0.f;
+    for (int j = lane; j < F; j += 32) {
+      const float xh = (Z[r * F + j] - mu) * rstd;
+      const float gh = (gam[j] * xh + bet[j] - (XV[r * F + j] - XK[r * F + j])) * gam[j];
+      const float d = dG[r * F + j];
+      sdG += d;
+      sdGx += d * xh;
+      sgx += gh * xh;
+      sdGG += d * G[r * F + j];
+    }
+    sdG = warp_sum(sdG);
+    sdGx = warp_sum(sdGx);
+    sgx = warp_sum(sgx);
+    sdGG = warp_sum(sdGG);
+    const float inv = rstd / F;
+    const float dstd = -sdGG * rstd;
+    float sx = 0.f, sxx = 0.f;
+    for (int j = lane; j < F; j += 32) {
+      const float xh = (Z[r * F + j] - mu) * rstd;
+      const float gh = (gam[j] * xh + bet[j] - (XV[r * F + j] - XK[r * F + j])) * gam[j];
+      const float d = dG[r * F + j];
+      const float dgh = (F * d - sdG - xh * sdGx) * inv;
+      const float dxh = -(d * sgx + gh * sdGx) * inv + dgh * gam[j] * gam[j];
+      DXH[r * F + j] = dxh;
+      DGH[r * F + j] = dgh;
+      dT[r * F + j] = -dgh * gam[j];
+      sx += dxh;
+      sxx += dxh * xh;
+    }
+    sx = warp_sum(sx);
+    sxx = warp_sum(sxx);
+    for (int j = lane; j < F; j += 32) {
+      const float xh = (Z[r * F + j] - mu) * rstd;
+      dZ[r * F + j] = (F * DXH[r * F + j] - sx - xh * sxx) * inv + dstd * xh / F;
+    }
+  }
+}
+
+// gamma / beta gradient contributions of the fused-LN backward, summed over rows.
+__device__ __forceinline__ void ln_fused_bwd_cols(const float* Z, const float* mu1, const float* sd1, const float* DGH,
+                                                  const float* XV, const float* XK, const float* gam, const float* bet,
+                                                  int C, int F, float* dgam, float* dbet) {
+  for (int j = threadIdx.x; j < F; j += blockDim.x) {
+    float a = 0.f, b = 0.f;
+    for (int r = 0; r < C; ++r) {
+      const float xh = (Z[r * F + j] - mu1[r]) / sd1[r];
+      const float go = gam[j] * xh + bet[j] - (XV[r * F + j] - XK[r * F + j]);
+      const float dgh = DGH[r * F + j];
+      a += dgh * (go + gam[j] * xh);
+      b += dgh * gam[j];
+    }
+    dgam[j] += a;
+    dbet[j] += b;
+  }
+}
+
+// Readout LayerNorm backward: Zb (bias added in place when bvec is set) becomes x_bar,
+// dZb = d LN / d Zb given dO (rows), gamma applied.
+__device__ __forceinline__ void readout_ln_bwd_rows(float* Zb, const float* bvec, const float* dO, const float* gam,
+                                                    int C, int F, float* dZb) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int r = warp; r < C; r += nw) {
+    float* z = Zb + r * F;
+    if (bvec) {
+      for (int j = lane; j < F; j += 32) z[j] += bvec[j];
+      __syncwarp();
+    }
+    float mu, rstd, sd;
+    row_stats(z, F, kLnEps, mu, rstd, sd);
+    float s1 = 0.f, s2 = 0.f;
+    for (int j = lane; j < F; j += 32) {
+      const float xh = (z[j] - mu) * rstd;
+      const float g = dO[r * F + j] * gam[j];
+      s1 += g;
+      s2 += g * xh;
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    __syncwarp();
+    for (int j = lane; j < F; j += 32) {
+      const float xh = (z[j] - mu) * rstd;
+      const float g = dO[r * F + j] * gam[j];
+      dZb[r * F + j] = (F * g - s1 - xh * s2) * (rstd / F);
+      z[j] = xh;
+    }
+  }
+}
+
+// gamma / beta gradient of the readout LayerNorm: sums over rows of dO * x_bar and dO.
+__device__ __forceinline__ void readout_ln_bwd_cols(const float* dO, const float* xbar, int C, int F, float* dgam,
+                                                    float* dbet) {
+  for (int j = threadIdx.x; j < F; j += blockDim.x) {
+    float a = 0.f, b = 0.f;
+    for (int r = 0; r < C; ++r) {
+      a += dO[r * F + j] * xbar[r * F + j];
+      b += dO[r * F + j];
+    }
+    dgam[j] += a;
+    dbet[j] += b;
+  }
+}
+
+// Readout forward: out = XQ + LN(Zb + b) written to global (typed), one warp per row.
+__device__ __forceinline__ void readout_ln_store_rows(float* Zb, const float* bvec, const float* XQ, const float* gam,
+                                                      const float* bet, int C, int F, float eps, void* out,
+                                                      long long base, int dt_out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int r = warp; r < C; r += nw) {
+    float* z = Zb + r * F;
+    if (bvec) {
+      for (int j = lane; j < F; j += 32) z[j] += bvec[j];
+      __syncwarp();
+    }
+    float mu, rstd, sd;
+    row_stats(z, F, eps, mu, rstd, sd);
+    for (int j = lane; j < F; j += 32)
+      st_elem(out, base + r * F + j, dt_out, XQ[r * F + j] + gam[j] * (z[j] - mu) * rstd + bet[j]);
+  }
+}
+
+// acc[j] = sum_c w[c] * X[c][j] for j < N (one thread per column).
+__device__ __forceinline__ void weighted_colsum(float* acc, const float* w, const float* X, int C, int N) {
+  for (int j = threadIdx.x; j < N; j += blockDim.x) {
+    float a = 0.f;
+    for (int c = 0; c < C; ++c) a += w[c] * X[c * N + j];
+    acc[j] = a;
+  }
+}
+
+}  // namespace ttt

@@ -1,0 +1,76 @@
+"""Drop-in for the reference's ``mlp_triton.TritonMLP`` (mlp_triton.py:12-468).
+
+    XQW, W1_memo, b1_memo, W2_memo, b2_memo = TritonMLP.apply(
+        ttt_norm_weight [NH,F], ttt_norm_bias [NH,F],
+        W1_init [B,NH,F,FF], b1_init [B,NH,1,FF], W2_init [B,NH,FF,F], b2_init [B,NH,1,F],
+        XQ, XV, XK [B,NH,NC,CS,F], eta [B,NH,NC,CS,CS],
+        checkpoint_group_size, memo_segment_size)
+
+XQW is [B,NH,NC,CS,F] in XQ's dtype. The memo states are fp32 [B,NH,NS,...] with
+NS = ceil(NC / memo_segment_size), holding the inner state AFTER mini-batch i for each
+i % memo_segment_size == 0 (kernels/mlp_forward.py:193-226); they are
+non-differentiable (mlp_triton.py:196). Backward returns the twelve gradients of
+mlp_triton.py:338-351 in XQ's dtype (LN gradients summed over the batch, full d_eta).
+"""
+
+from __future__ import annotations
+
+import torch
+
+import _core
+from _sharding import HEAD, LN, local_map
+
+
+def _forward_core(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ, XV, XK, eta,
+                  checkpoint_group_size, memo_segment_size):
+    ckpt = int(checkpoint_group_size)
+    XQW, _, ck, memo = _core.mlp_forward(
+        ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ, XV, XK, eta, ckpt, memo_segment_size
+    )
+    ctx.ckpt = ckpt
+    ctx.save_for_backward(XQ, XV, XK, eta, ttt_norm_weight, ttt_norm_bias, *ck)
+    ctx.mark_non_differentiable(*memo)
+    return (XQW, *memo)
+
+
+def _backward_core(ctx, grad_XQW):
+    XQ, XV, XK, eta, ln_w, ln_b, W1c, b1c, W2c, b2c = ctx.saved_tensors
+    mp = XQ.dtype
+    d_ln_w, d_ln_b, dW1, db1, dW2, db2, dXQ, dXV, dXK, deta = _core.mlp_backward(
+        ln_w, ln_b, (W1c, b1c, W2c, b2c), XQ, XV, XK, eta, grad_XQW, ctx.ckpt
+    )
+    return (
+        d_ln_w.sum(0).reshape(ln_w.shape).to(mp),
+        d_ln_b.sum(0).reshape(ln_b.shape).to(mp),
+        dW1.to(mp), db1.to(mp), dW2.to(mp), db2.to(mp),
+        dXQ, dXV, dXK, deta,
+        None, None,
+    )
+
+
+_forward_sharded = local_map(
+    _forward_core,
+    in_placements=(None, LN, LN, HEAD, HEAD, HEAD, HEAD, HEAD, HEAD, HEAD, HEAD, None, None),
+    out_placements=(HEAD, HEAD, HEAD, HEAD, HEAD),
+)
+_backward_sharded = local_map(
+    _backward_core,
+    in_placements=(None, HEAD),
+    out_placements=(LN, LN, HEAD, HEAD, HEAD, HEAD, HEAD, HEAD, HEAD, HEAD, None, None),
+)
+
+
+class TritonMLP(torch.autograd.Function):
+    sharded_mode = False
+
+    @staticmethod
+    def forward(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ_batch, XV_batch,
+                XK_batch, eta_batch, checkpoint_group_size, memo_segment_size):
+        core = _forward_sharded if TritonMLP.sharded_mode else _forward_core
+        return core(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ_batch, XV_batch,
+                    XK_batch, eta_batch, checkpoint_group_size, memo_segment_size)
+
+    @staticmethod
+    def backward(ctx, grad_L_XQW_batch, *unused):
+        core = _backward_sharded if TritonMLP.sharded_mode else _backward_core
+        return core(ctx, grad_L_XQW_batch)

@@ -1,0 +1,41 @@
+"""``ttt_mlp`` with the signature and output layout of ops/ttt_mlp.py:70-99.
+
+    XQW = ttt_mlp(XK, XQ, XV, eta, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init,
+                  W2_init, b2_init, checkpoint_group_size)   # -> [B, NC, CS, NH, F]
+"""
+
+from __future__ import annotations
+
+import torch
+
+import _core
+
+
+class _MLPScan(torch.autograd.Function):
+    """TTT-MLP scan without memo outputs (the ops path never reads them)."""
+
+    @staticmethod
+    def forward(ctx, ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, ckpt):
+        XQW, _, ck, _ = _core.mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, ckpt, None)
+        ctx.ckpt = ckpt
+        ctx.save_for_backward(XQ, XV, XK, eta, ln_w, ln_b, *ck)
+        return XQW
+
+    @staticmethod
+    def backward(ctx, grad):
+        XQ, XV, XK, eta, ln_w, ln_b, W1c, b1c, W2c, b2c = ctx.saved_tensors
+        mp = XQ.dtype
+        d_ln_w, d_ln_b, dW1, db1, dW2, db2, dXQ, dXV, dXK, deta = _core.mlp_backward(
+            ln_w, ln_b, (W1c, b1c, W2c, b2c), XQ, XV, XK, eta, grad, ctx.ckpt
+        )
+        return (d_ln_w.sum(0).reshape(ln_w.shape).to(mp), d_ln_b.sum(0).reshape(ln_b.shape).to(mp),
+                dW1.to(mp), db1.to(mp), dW2.to(mp), db2.to(mp), dXQ, dXV, dXK, deta, None)
+
+
+def ttt_mlp(XK, XQ, XV, eta, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init,
+            checkpoint_group_size):
+    NC = XQ.shape[2]
+    ckpt = int(checkpoint_group_size)
+    ckpt = NC if ckpt <= 0 else min(ckpt, NC)
+    out = _MLPScan.apply(ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ, XV, XK, eta, ckpt)
+    return out.permute(0, 2, 3, 1, 4)

@@ -1,0 +1,94 @@
+"""Seeded synthetic inputs with the shapes and value distributions of the benchmark configs.
+
+The reference benchmarks nothing itself; its configs (batch, heads, sequence, head dim,
+mini-batch 16, inner width) are reproduced here with seeded data:
+
+* XQ, XK, XV ~ N(0, 1) / 8 in kernel layout [B, NH, NC, CS, F];
+* W ~ N(0, 0.02^2), biases 0, LayerNorm gamma = 1, beta = 0 (ttt_layer.py:81-89, 363-364);
+* eta in the full [B, NH, NC, CS, CS] layout the kernels take:
+  - ``"causal"``: eta[b,h,n,i,j] = s[b,h,n,j] / (i + 1) for j <= i, else 0, with
+    s = sigmoid(N(0, 1)) / 64 (a per-token learning rate with a 1/(i+1) factor; the
+    [j <= i] mask makes the reference's unmasked eta * Attn equal the causal dual form);
+  - ``"equal"``: eta[b,h,n,i,j] = s[b,h,n,j] / CS for every row i, which is what the
+    forecaster's layer feeds (ttt_layer.py:151-163, 309).
+* upstream gradient dZ ~ N(0, 1) for backward.
+
+Generation runs on ``device`` with a generator seeded there, so the large configs are
+created directly in HBM.
+"""
+
+from __future__ import annotations
+
+import torch
+
+
+def _randn(shape, gen, device, dtype=torch.float32):
+    return torch.randn(shape, generator=gen, device=device, dtype=dtype)
+
+
+def make_eta(s, mode="causal"):
+    """Build the [.., CS, CS] eta matrix from per-token rates s [.., CS]."""
+    CS = s.shape[-1]
+    idx = torch.arange(CS, device=s.device)
+    if mode == "causal":
+        scale = 1.0 / (idx.to(s.dtype) + 1.0)  # row i -> 1/(i+1)
+        mask = (idx[None, :] <= idx[:, None]).to(s.dtype)  # [i, j] = j <= i
+        return s[..., None, :] * (scale[:, None] * mask)
+    if mode == "equal":
+        return (s[..., None, :] / CS).expand(*s.shape[:-1], CS, CS).contiguous()
+    raise ValueError(f"unknown eta mode {mode!r}")
+
+
+def make_linear_inputs(B, NH, NC, CS=16, F=64, dtype=torch.float32, device="cpu", seed=0, eta_mode="causal"):
+    """Inputs of ``TritonLinear.apply`` (linear_triton.py:15-53) as a dict."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    d = {}
+    d["XQ"] = (_randn((B, NH, NC, CS, F), g, device) / 8).to(dtype)
+    d["XK"] = (_randn((B, NH, NC, CS, F), g, device) / 8).to(dtype)
+    d["XV"] = (_randn((B, NH, NC, CS, F), g, device) / 8).to(dtype)
+    s = torch.sigmoid(_randn((B, NH, NC, CS), g, device)) / 64
+    d["eta"] = make_eta(s, eta_mode).to(dtype)
+    W = _randn((NH, F, F), g, device) * 0.02
+    d["W1"] = W[None].expand(B, NH, F, F).contiguous()
+    d["b1"] = torch.zeros(B, NH, 1, F, device=device)
+    d["ln_w"] = torch.ones(NH, F, device=device)
+    d["ln_b"] = torch.zeros(NH, F, device=device)
+    return d
+
+
+def make_mlp_inputs(B, NH, NC, CS=16, F=64, FF=256, dtype=torch.float32, device="cpu", seed=0, eta_mode="causal"):
+    """Inputs of ``TritonMLP.apply`` (mlp_triton.py:15-62) as a dict."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    d = {}
+    d["XQ"] = (_randn((B, NH, NC, CS, F), g, device) / 8).to(dtype)
+    d["XK"] = (_randn((B, NH, NC, CS, F), g, device) / 8).to(dtype)
+    d["XV"] = (_randn((B, NH, NC, CS, F), g, device) / 8).to(dtype)
+    s = torch.sigmoid(_randn((B, NH, NC, CS), g, device)) / 64
+    d["eta"] = make_eta(s, eta_mode).to(dtype)
+    W1 = _randn((NH, F, FF), g, device) * 0.02
+    W2 = _randn((NH, FF, F), g, device) * 0.02
+    d["W1"] = W1[None].expand(B, NH, F, FF).contiguous()
+    d["b1"] = torch.zeros(B, NH, 1, FF, device=device)
+    d["W2"] = W2[None].expand(B, NH, FF, F).contiguous()
+    d["b2"] = torch.zeros(B, NH, 1, F, device=device)
+    d["ln_w"] = torch.ones(NH, F, device=device)
+    d["ln_b"] = torch.zeros(NH, F, device=device)
+    return d
+
+
+def make_upstream(shape, device="cpu", seed=1, dtype=torch.float32):
+    """dZ ~ N(0, 1) with the output's shape."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    return _randn(shape, g, device).to(dtype)
+
+
+def perturb_params(d, device="cpu", seed=2, scale=0.1):
+    """Non-trivial LN params and biases so their gradients are exercised (tests only)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = dict(d)
+    out["ln_w"] = d["ln_w"] + scale * _randn(d["ln_w"].shape, g, device)
+    out["ln_b"] = d["ln_b"] + scale * _randn(d["ln_b"].shape, g, device)
+    for k in ("b1", "b2"):
+        if k in d:
+            out[k] = d[k] + 0.02 * _randn(d[k].shape, g, device)
+    return out
