@@ -9,6 +9,7 @@ ttt-triton_b200/synthetic.py):
 * ``mlp_fwd_c1`` (default, the headline): TTT-MLP forward, B16 NH12 L2048 F64 FF256,
   bf16 activations / fp32 state, checkpoint group 16 (config 1).
 * ``linear_fwd_c0``: TTT-Linear forward, fp32, B2 NH4 L256 F64 (config 0).
+* ``linear_fwd_c2``: TTT-Linear forward only at the config-2 shape (diagnostic).
 * ``linear_fwdbwd_c2``: TTT-Linear forward+backward, bf16, B32 NH8 L4096 F64 (config 2).
 * ``mlp_fwdbwd_c3``: TTT-MLP forward+backward, bf16, B64 NH16 L8192 F64 FF256, memo 16 (config 3).
 
@@ -38,6 +39,7 @@ import torch  # noqa: E402
 WORKLOADS = {
     "linear_fwd_c0": dict(kind="linear", B=2, NH=4, L=256, F=64, FF=None, dtype="f32", bwd=False, ckpt=16, memo=None),
     "mlp_fwd_c1": dict(kind="mlp", B=16, NH=12, L=2048, F=64, FF=256, dtype="bf16", bwd=False, ckpt=16, memo=None),
+    "linear_fwd_c2": dict(kind="linear", B=32, NH=8, L=4096, F=64, FF=None, dtype="bf16", bwd=False, ckpt=16, memo=None),
     "linear_fwdbwd_c2": dict(kind="linear", B=32, NH=8, L=4096, F=64, FF=None, dtype="bf16", bwd=True, ckpt=16, memo=None),
     "mlp_fwdbwd_c3": dict(kind="mlp", B=64, NH=16, L=8192, F=64, FF=256, dtype="bf16", bwd=True, ckpt=16, memo=16),
 }

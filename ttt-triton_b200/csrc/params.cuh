@@ -1,0 +1,130 @@
+// Launch parameter blocks shared by the general and the tensor-core kernels.
+#pragma once
+
+namespace ttt {
+
+struct LinFwdParams {
+  int B, NH, NC, CS, F, ckpt, K;
+  const void* ln_w;
+  const void* ln_b;
+  int dt_ln;
+  const float* W_init;
+  const float* b_init;
+  const void* XQ;
+  const void* XV;
+  const void* XK;
+  const void* eta;
+  int dt_xq, dt_xv, dt_xk, dt_eta;
+  void* out;
+  int dt_out;
+  float* W_last;
+  float* b_last;
+  float* W_ckpt;
+  float* b_ckpt;
+};
+
+struct LinBwdParams {
+  int B, NH, NC, CS, F, ckpt, K;
+  const void* ln_w;
+  const void* ln_b;
+  int dt_ln;
+  const float* W_ckpt;
+  const float* b_ckpt;
+  const void* XQ;
+  const void* XV;
+  const void* XK;
+  const void* eta;
+  int dt_xq, dt_xv, dt_xk, dt_eta;
+  const void* dout;
+  int dt_dout;
+  float* d_ln_w;
+  float* d_ln_b;
+  float* dW;
+  float* db;
+  void* dXQ;
+  void* dXV;
+  void* dXK;
+  void* deta;
+  int dt_grad;
+  float* scratch;  // [B*NH][ckpt][CS][F] pre-activations Z of one group
+};
+
+struct MlpFwdParams {
+  int B, NH, NC, CS, F, FF, ckpt, K, memo, NS;
+  const void* ln_w;
+  const void* ln_b;
+  int dt_ln;
+  const float* W1_init;
+  const float* b1_init;
+  const float* W2_init;
+  const float* b2_init;
+  const void* XQ;
+  const void* XV;
+  const void* XK;
+  const void* eta;
+  int dt_xq, dt_xv, dt_xk, dt_eta;
+  void* out;
+  int dt_out;
+  float* W1_last;
+  float* b1_last;
+  float* W2_last;
+  float* b2_last;
+  float* W1_ckpt;
+  float* b1_ckpt;
+  float* W2_ckpt;
+  float* b2_ckpt;
+  float* W1_memo;
+  float* b1_memo;
+  float* W2_memo;
+  float* b2_memo;
+};
+
+struct MlpBwdParams {
+  int B, NH, NC, CS, F, FF, ckpt, K;
+  const void* ln_w;
+  const void* ln_b;
+  int dt_ln;
+  const float* W1_ckpt;
+  const float* b1_ckpt;
+  const float* W2_ckpt;
+  const float* b2_ckpt;
+  const void* XQ;
+  const void* XV;
+  const void* XK;
+  const void* eta;
+  int dt_xq, dt_xv, dt_xk, dt_eta;
+  const void* dout;
+  int dt_dout;
+  float* d_ln_w;
+  float* d_ln_b;
+  float* dW1;
+  float* db1;
+  float* dW2;
+  float* db2;
+  void* dXQ;
+  void* dXV;
+  void* dXK;
+  void* deta;
+  int dt_grad;
+  float* scratch;  // per stream: W1 [F*FF], W2 [FF*F], Z1/Z2 of one group [ckpt][CS*(FF+F)]
+};
+
+struct ReadoutParams {
+  int B, NH, NCs, CS, F, FF;
+  const void* XQ;
+  int dt_xq;
+  const float* W1;
+  long long W1_sb, W1_sh;
+  const float* b1;
+  long long b1_sb, b1_sh;
+  const float* W2;
+  long long W2_sb, W2_sh;
+  const float* b2;
+  long long b2_sb, b2_sh;
+  const void* ln_w;
+  const void* ln_b;
+  int dt_ln;
+  float* out;
+};
+
+}  // namespace ttt

@@ -13,54 +13,10 @@
 // whole sequence.
 #include "capi_common.cuh"
 #include "common.cuh"
+#include "fast_paths.cuh"
+#include "params.cuh"
 
 namespace ttt {
-
-struct LinFwdParams {
-  int B, NH, NC, CS, F, ckpt, K;
-  const void* ln_w;
-  const void* ln_b;
-  int dt_ln;
-  const float* W_init;
-  const float* b_init;
-  const void* XQ;
-  const void* XV;
-  const void* XK;
-  const void* eta;
-  int dt_xq, dt_xv, dt_xk, dt_eta;
-  void* out;
-  int dt_out;
-  float* W_last;
-  float* b_last;
-  float* W_ckpt;
-  float* b_ckpt;
-};
-
-struct LinBwdParams {
-  int B, NH, NC, CS, F, ckpt, K;
-  const void* ln_w;
-  const void* ln_b;
-  int dt_ln;
-  const float* W_ckpt;
-  const float* b_ckpt;
-  const void* XQ;
-  const void* XV;
-  const void* XK;
-  const void* eta;
-  int dt_xq, dt_xv, dt_xk, dt_eta;
-  const void* dout;
-  int dt_dout;
-  float* d_ln_w;
-  float* d_ln_b;
-  float* dW;
-  float* db;
-  void* dXQ;
-  void* dXV;
-  void* dXK;
-  void* deta;
-  int dt_grad;
-  float* scratch;  // [B*NH][ckpt][CS][F] pre-activations Z of one group
-};
 
 __global__ void __launch_bounds__(256) linear_fwd_kernel(LinFwdParams p) {
   extern __shared__ float sm[];
@@ -339,6 +295,8 @@ extern "C" int ttt_linear_fwd(int B, int NH, int NC, int CS, int F, int checkpoi
   p.dt_xq = dt_xq; p.dt_xv = dt_xv; p.dt_xk = dt_xk; p.dt_eta = dt_eta;
   p.out = XQW; p.dt_out = dt_out;
   p.W_last = W1_last; p.b_last = b1_last; p.W_ckpt = W1_ckpt; p.b_ckpt = b1_ckpt;
+  rc = linear_fwd_fast(p, (cudaStream_t)stream);
+  if (rc != TTT_NOT_APPLICABLE) return rc;
   const size_t smem = linear_fwd_smem(CS, F);
   rc = prepare_smem(linear_fwd_kernel, smem, "ttt_linear_fwd");
   if (rc) return rc;
