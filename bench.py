@@ -99,12 +99,13 @@ def kernel_step(w, d, dO):
     import _core
 
     if w["kind"] == "linear":
-        XQW, _, _, Wc, bc = _core.linear_forward(*(d[k] for k in LIN), w["ckpt"])
+        XQW, Wl, bl, Wc, bc, Z = _core.linear_forward(*(d[k] for k in LIN), w["ckpt"], for_backward=w["bwd"])
         if w["bwd"]:
-            _core.linear_backward(d["ln_w"], d["ln_b"], Wc, bc, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"])
+            _core.linear_backward(d["ln_w"], d["ln_b"], Wc, bc, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
+                                  Z=Z, W_last=Wl, b_last=bl)
             return 2
         return 1
-    XQW, _, ck, _ = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"])
+    XQW, _, ck, _ = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"], for_backward=w["bwd"])
     if w["bwd"]:
         _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"])
         return 2
@@ -342,14 +343,14 @@ def kernel_durations(w, d, dO, steps):
     for _ in range(n):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if w["kind"] == "linear":
-            _, _, _, Wc, bc = (None, None, None, None, None)
             if w["bwd"]:
-                _, _, _, Wc, bc = _core.linear_forward(*(d[k] for k in LIN), w["ckpt"])
+                _, Wl, bl, Wc, bc, Z = _core.linear_forward(*(d[k] for k in LIN), w["ckpt"])
                 e0.record(stream)
-                _core.linear_backward(d["ln_w"], d["ln_b"], Wc, bc, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"])
+                _core.linear_backward(d["ln_w"], d["ln_b"], Wc, bc, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
+                                      Z=Z, W_last=Wl, b_last=bl)
             else:
                 e0.record(stream)
-                _core.linear_forward(*(d[k] for k in LIN), w["ckpt"])
+                _core.linear_forward(*(d[k] for k in LIN), w["ckpt"], for_backward=False)
         else:
             if w["bwd"]:
                 _, _, ck, _ = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"])
@@ -357,7 +358,7 @@ def kernel_durations(w, d, dO, steps):
                 _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"])
             else:
                 e0.record(stream)
-                _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"])
+                _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"], for_backward=False)
         e1.record(stream)
         torch.cuda.synchronize()
         tot += e0.elapsed_time(e1)

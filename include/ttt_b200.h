@@ -59,6 +59,9 @@ const char* ttt_last_error(void);
  *   W <- W - XK^T diag(eta[CS-1, :]) G,  b <- b - eta[CS-1, :] G
  * Writes XQW (dtype dt_out), the final state W_last/b_last and the state at the start
  * of every checkpoint group (W_ckpt/b_ckpt, as kernels/linear_forward.py:55-73).
+ * W1_ckpt/b1_ckpt may both be NULL when no backward follows (inference).
+ * Z_out (optional, NULL to skip) receives the fp32 pre-activation Z = XK W_n + b_n of
+ * every mini-batch, [B, NH, NC, CS, F]; ttt_linear_bwd uses it to skip recomputation.
  */
 int ttt_linear_fwd(int B, int NH, int NC, int CS, int F, int checkpoint_group_size,
                    const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
@@ -67,22 +70,28 @@ int ttt_linear_fwd(int B, int NH, int NC, int CS, int F, int checkpoint_group_si
                    const void* eta, int dt_eta,
                    void* XQW, int dt_out,
                    float* W1_last, float* b1_last, float* W1_ckpt, float* b1_ckpt,
-                   void* stream);
+                   float* Z_out, void* stream);
 
-/* Bytes of scratch ttt_linear_bwd needs for these sizes. */
+/* Bytes of scratch ttt_linear_bwd needs for these sizes (checkpoint-recompute path). */
 size_t ttt_linear_bwd_scratch_bytes(int B, int NH, int NC, int CS, int F, int checkpoint_group_size);
 
 /*
  * TTT-Linear backward. Replaces the launch of `ttt_linear_scan_backward` in
  * linear_triton.py:201-246 (TritonLinear._backward_core), with the full dual-form
  * gradients of ops/ttt_linear.py (d_eta is the whole CS x CS block per mini-batch).
- * Inputs are the forward's inputs plus its checkpoints and dXQW. Outputs:
+ * Inputs are the forward's inputs plus its checkpoints and dXQW. With Z_saved (the
+ * forward's Z_out) and the final state W1_last/b1_last, the backward walks the sequence
+ * once from the end, recovering each mini-batch's state by undoing its rank-CS update;
+ * otherwise (Z_saved NULL) it re-runs each checkpoint group forward from W1_ckpt/b1_ckpt.
+ * Outputs:
  *   d_ln_w, d_ln_b : [B, NH, F] fp32 per-(b,h) partial sums (the caller sums over B,
  *                    as linear_triton.py:251-252 does)
  *   dW1, db1       : [B, NH, F, F], [B, NH, 1, F] fp32
  *   dXQ, dXV, dXK  : [B, NH, NC, CS, F], d_eta : [B, NH, NC, CS, CS], all dtype dt_grad
  * `scratch` must hold ttt_linear_bwd_scratch_bytes(...) bytes (its contents are
- * overwritten; no initialisation needed).
+ * overwritten; no initialisation needed); it may be NULL when Z_saved is given and the
+ * request is inside the tensor-core envelope (CS = 16, F = 64, one 16-bit dtype); the
+ * call fails with TTT_ERR_SCRATCH if it is needed and missing.
  */
 int ttt_linear_bwd(int B, int NH, int NC, int CS, int F, int checkpoint_group_size,
                    const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
@@ -90,6 +99,7 @@ int ttt_linear_bwd(int B, int NH, int NC, int CS, int F, int checkpoint_group_si
                    const void* XQ, int dt_xq, const void* XV, int dt_xv, const void* XK, int dt_xk,
                    const void* eta, int dt_eta,
                    const void* dXQW, int dt_dout,
+                   const float* Z_saved, const float* W1_last, const float* b1_last,
                    float* d_ln_w, float* d_ln_b, float* dW1, float* db1,
                    void* dXQ, void* dXV, void* dXK, void* d_eta, int dt_grad,
                    void* scratch, size_t scratch_bytes, void* stream);
@@ -101,7 +111,7 @@ int ttt_linear_bwd(int B, int NH, int NC, int CS, int F, int checkpoint_group_si
  * ops/ttt_mlp.py:9-67. Besides XQW, the final state and the group-start checkpoints, it
  * writes the memo states: the state AFTER mini-batch i for every i with
  * i % memo_segment_size == 0 (kernels/mlp_forward.py:193-226). Memo pointers may all be
- * NULL to skip them.
+ * NULL to skip them, and so may the four checkpoint pointers when no backward follows.
  */
 int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_group_size, int memo_segment_size,
                 const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,

@@ -38,7 +38,7 @@ FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: every call below fails its
 def _linear_fwd(B=1, NH=1, NC=2, CS=16, F=16, ckpt=1, dt=0, null_out=False):
     return _lib.lib.ttt_linear_fwd(
         B, NH, NC, CS, F, ckpt, FAKE, FAKE, 0, FAKE, FAKE, FAKE, dt, FAKE, 0, FAKE, 0, FAKE, 0,
-        None if null_out else FAKE, 0, FAKE, FAKE, FAKE, FAKE, None)
+        None if null_out else FAKE, 0, FAKE, FAKE, FAKE, FAKE, None, None)
 
 
 def test_host_checks_reject_bad_arguments():
@@ -50,7 +50,8 @@ def test_host_checks_reject_bad_arguments():
     assert _linear_fwd(dt=7) == -3
     assert _linear_fwd(null_out=True) == -1
     rc = _lib.lib.ttt_linear_bwd(1, 1, 4, 16, 16, 2, FAKE, FAKE, 0, FAKE, FAKE, FAKE, 0, FAKE, 0, FAKE, 0, FAKE, 0,
-                                 FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 0, FAKE, 16, None)
+                                 FAKE, 0, None, None, None, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 0, FAKE,
+                                 16, None)
     assert rc == -5 and "scratch" in _lib.lib.ttt_last_error().decode()
 
 

@@ -45,7 +45,7 @@ def test_linear_fwd_bwd_matches_oracle(dtype, shape):
     for k in NAMES:
         assert grads[k].dtype == d[k].dtype
         assert_close("d" + k, grads[k], ref_grads[k], tol)
-    XQW, W_last, b_last, W_ck, b_ck = _core.linear_forward(*(d[k] for k in NAMES), ckpt)
+    XQW, W_last, b_last, W_ck, b_ck, Zs = _core.linear_forward(*(d[k] for k in NAMES), ckpt)
     full = O.linear_scan(*(oracle_inputs(d)[k] for k in NAMES), ckpt)
     W0 = d["W1"].double().cpu()
     assert_close("W_last - W0", W_last.double().cpu() - W0, full["W_last"] - W0, tol)
@@ -85,7 +85,7 @@ def test_ops_signature_and_layout():
 def test_zero_eta_identity():
     d, _ = make(2, 2, 3, 16, 64, torch.float32, seed=9)
     d["eta"] = torch.zeros_like(d["eta"])
-    XQW, W_last, b_last, _, _ = _core.linear_forward(*(d[k] for k in NAMES), 2)
+    XQW, W_last, b_last, _, _, _ = _core.linear_forward(*(d[k] for k in NAMES), 2, for_backward=False)
     assert torch.equal(W_last, d["W1"]) and torch.equal(b_last, d["b1"])
     lw, lb = d["ln_w"].reshape(1, 2, 1, 1, 64), d["ln_b"].reshape(1, 2, 1, 1, 64)
     ref = d["XQ"] + O.ln_fwd(d["XQ"] @ d["W1"][:, :, None] + d["b1"][:, :, None], lw, lb)
@@ -128,3 +128,31 @@ def test_full_size_config2_sampled_streams():
         assert_close(f"XQW[{b},{h}]", out[b:b + 1, h:h + 1], r["XQW"], 2e-2)
         for k in ("XQ", "XK", "XV", "eta", "W1", "b1"):
             assert_close(f"d{k}[{b},{h}]", grads[k][b:b + 1, h:h + 1], rg[k], 2e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_backward_paths_agree(dtype):
+    """The single reverse walk over stored Z (tensor-core path) and the checkpoint-group
+    recompute (general path) both match the oracle on the same inputs."""
+    B, NH, NC, CS, F, ckpt = 2, 2, 7, 16, 64, 3
+    d, dO = make(B, NH, NC, CS, F, dtype, seed=21)
+    ref_grads, _ = O.linear_grads(oracle_inputs(d), dO.double().cpu())
+    _, Wl, bl, Wc, bc, Z = _core.linear_forward(*(d[k] for k in NAMES), ckpt)
+    args = (d["ln_w"], d["ln_b"], Wc, bc, d["XQ"], d["XV"], d["XK"], d["eta"], dO, ckpt)
+    walk = _core.linear_backward(*args, Z=Z, W_last=Wl, b_last=bl)
+    regroup = _core.linear_backward(*args)
+    names = ("ln_w", "ln_b", "W1", "b1", "XQ", "XV", "XK", "eta")
+    for res in (walk, regroup):
+        got = dict(zip(names, res))
+        got["ln_w"], got["ln_b"] = got["ln_w"].sum(0), got["ln_b"].sum(0)
+        for k in names:
+            assert_close("d" + k, got[k], ref_grads[k].reshape(got[k].shape), 2e-2)
+
+
+def test_inference_forward_skips_saved_state():
+    d, _ = make(1, 2, 3, 16, 64, torch.bfloat16, seed=23)
+    with torch.no_grad():
+        out = TritonLinear.apply(*(d[k] for k in NAMES), 2)
+    XQW, W_last, b_last, W_ck, b_ck, Z = _core.linear_forward(*(d[k] for k in NAMES), 2, for_backward=False)
+    assert W_ck is None and b_ck is None and Z is None
+    assert torch.equal(out, XQW)

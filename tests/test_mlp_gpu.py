@@ -92,7 +92,7 @@ def test_full_size_config1_sampled_streams():
     re-run through the oracle at full length."""
     B, NH, NC, CS, F, FF = 16, 12, 128, 16, 64, 256
     d = S.make_mlp_inputs(B, NH, NC, CS, F, FF, dtype=torch.bfloat16, device=DEV, seed=0)
-    out, last, _, _ = _core.mlp_forward(*(d[k] for k in NAMES), 16, None)
+    out, last, _, _ = _core.mlp_forward(*(d[k] for k in NAMES), 16, None, for_backward=False)
     torch.cuda.synchronize()
     for b, h in ((0, 0), (7, 5), (15, 11)):
         sub = {k: (v[b:b + 1, h:h + 1] if k not in ("ln_w", "ln_b") else v[h:h + 1]) for k, v in d.items()}

@@ -47,8 +47,12 @@ def _state(t, shape, name):
 
 
 # --------------------------------------------------------------------------- Linear
-def linear_forward(ln_w, ln_b, W1, b1, XQ, XV, XK, eta, checkpoint_group_size):
-    """TTT-Linear scan forward. Returns (XQW in XQ's dtype, W_last, b_last, W_ckpt, b_ckpt)."""
+def linear_forward(ln_w, ln_b, W1, b1, XQ, XV, XK, eta, checkpoint_group_size, for_backward=True):
+    """TTT-Linear scan forward. Returns (XQW in XQ's dtype, W_last, b_last, W_ckpt, b_ckpt, Z).
+
+    With ``for_backward`` the group-start checkpoints and the fp32 pre-activations Z of
+    every mini-batch are kept for ``linear_backward``; without it (inference) neither is
+    written and both come back as None."""
     require_cuda(ln_w, ln_b, W1, b1, XQ, XV, XK, eta)
     B, NH, NC, CS, F = _check_acts(XQ, XV, XK, eta)
     ckpt = int(checkpoint_group_size)
@@ -63,8 +67,11 @@ def linear_forward(ln_w, ln_b, W1, b1, XQ, XV, XK, eta, checkpoint_group_size):
     XQW = torch.empty(B, NH, NC, CS, F, device=dev, dtype=XQ.dtype)
     W_last = torch.empty(B, NH, F, F, device=dev, dtype=torch.float32)
     b_last = torch.empty(B, NH, 1, F, device=dev, dtype=torch.float32)
-    W_ckpt = torch.empty(B, NH, K, F, F, device=dev, dtype=torch.float32)
-    b_ckpt = torch.empty(B, NH, K, 1, F, device=dev, dtype=torch.float32)
+    W_ckpt = b_ckpt = Z = None
+    if for_backward:
+        W_ckpt = torch.empty(B, NH, K, F, F, device=dev, dtype=torch.float32)
+        b_ckpt = torch.empty(B, NH, K, 1, F, device=dev, dtype=torch.float32)
+        Z = torch.empty(B, NH, NC, CS, F, device=dev, dtype=torch.float32)
     rc = lib.ttt_linear_fwd(
         B, NH, NC, CS, F, ckpt,
         ptr(ln_w), ptr(ln_b), dtype_code(ln_w),
@@ -72,17 +79,24 @@ def linear_forward(ln_w, ln_b, W1, b1, XQ, XV, XK, eta, checkpoint_group_size):
         ptr(XQ), dtype_code(XQ), ptr(XV), dtype_code(XV), ptr(XK), dtype_code(XK),
         ptr(eta), dtype_code(eta),
         ptr(XQW), dtype_code(XQW),
-        ptr(W_last), ptr(b_last), ptr(W_ckpt), ptr(b_ckpt),
+        ptr(W_last), ptr(b_last), ptr(W_ckpt), ptr(b_ckpt), ptr(Z),
         stream_of(XQ),
     )
     check(rc, "ttt_linear_fwd")
-    return XQW, W_last, b_last, W_ckpt, b_ckpt
+    return XQW, W_last, b_last, W_ckpt, b_ckpt, Z
 
 
-def linear_backward(ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, dXQW, checkpoint_group_size, grad_dtype=None):
+def linear_backward(ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, dXQW, checkpoint_group_size, grad_dtype=None,
+                    Z=None, W_last=None, b_last=None):
     """TTT-Linear scan backward. Returns (d_ln_w [B,NH,F] per-(b,h) partials, d_ln_b,
-    dW1, db1 (fp32), dXQ, dXV, dXK, d_eta (grad_dtype, default XQ's dtype))."""
+    dW1, db1 (fp32), dXQ, dXV, dXK, d_eta (grad_dtype, default XQ's dtype)).
+
+    ``Z``, ``W_last``, ``b_last`` (from ``linear_forward``) enable the single reverse walk;
+    without them each checkpoint group is re-run forward."""
     require_cuda(ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, dXQW)
+    if Z is not None:
+        require_cuda(Z, W_last, b_last)
+        Z, W_last, b_last = _c(Z), _c(W_last), _c(b_last)
     B, NH, NC, CS, F = _check_acts(XQ, XV, XK, eta)
     ckpt = int(checkpoint_group_size)
     ln_w, ln_b = _check_ln(ln_w, ln_b, NH, F)
@@ -109,6 +123,7 @@ def linear_backward(ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, dXQW, checkpoin
         ptr(XQ), dtype_code(XQ), ptr(XV), dtype_code(XV), ptr(XK), dtype_code(XK),
         ptr(eta), dtype_code(eta),
         ptr(dXQW), dtype_code(dXQW),
+        ptr(Z), ptr(W_last), ptr(b_last),
         ptr(d_ln_w), ptr(d_ln_b), ptr(dW1), ptr(db1),
         ptr(dXQ), ptr(dXV), ptr(dXK), ptr(deta), dtype_code(dXQ),
         ptr(scratch), nbytes, stream_of(XQ),
@@ -118,8 +133,11 @@ def linear_backward(ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, dXQW, checkpoin
 
 
 # --------------------------------------------------------------------------- MLP
-def mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, checkpoint_group_size, memo_segment_size=None):
-    """TTT-MLP scan forward. Returns (XQW, (W1,b1,W2,b2)_last, (…)_ckpt, (…)_memo or None)."""
+def mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, checkpoint_group_size, memo_segment_size=None,
+                for_backward=True):
+    """TTT-MLP scan forward. Returns (XQW, (W1,b1,W2,b2)_last, (…)_ckpt or None, (…)_memo or None).
+
+    Without ``for_backward`` (inference) the checkpoints are not written."""
     require_cuda(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta)
     B, NH, NC, CS, F = _check_acts(XQ, XV, XK, eta)
     FF = W1.shape[-1]
@@ -138,8 +156,11 @@ def mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, checkpoint_group_si
     XQW = torch.empty(B, NH, NC, CS, F, device=dev, dtype=XQ.dtype)
     last = (torch.empty(B, NH, F, FF, **f32), torch.empty(B, NH, 1, FF, **f32),
             torch.empty(B, NH, FF, F, **f32), torch.empty(B, NH, 1, F, **f32))
-    ck = (torch.empty(B, NH, K, F, FF, **f32), torch.empty(B, NH, K, 1, FF, **f32),
-          torch.empty(B, NH, K, FF, F, **f32), torch.empty(B, NH, K, 1, F, **f32))
+    ck = None
+    if for_backward:
+        ck = (torch.empty(B, NH, K, F, FF, **f32), torch.empty(B, NH, K, 1, FF, **f32),
+              torch.empty(B, NH, K, FF, F, **f32), torch.empty(B, NH, K, 1, F, **f32))
+    cp = ck if ck is not None else (None, None, None, None)
     memo = None
     memo_seg = 1
     if memo_segment_size is not None:
@@ -157,7 +178,7 @@ def mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, checkpoint_group_si
         ptr(XQ), dtype_code(XQ), ptr(XV), dtype_code(XV), ptr(XK), dtype_code(XK),
         ptr(eta), dtype_code(eta),
         ptr(XQW), dtype_code(XQW),
-        *[ptr(t) for t in last], *[ptr(t) for t in ck], *[ptr(t) for t in mp],
+        *[ptr(t) for t in last], *[ptr(t) for t in cp], *[ptr(t) for t in mp],
         stream_of(XQ),
     )
     check(rc, "ttt_mlp_fwd")

@@ -25,11 +25,12 @@ _L = ctypes.c_longlong
 _SIGNATURES = {
     "ttt_abi_version": ([], _I),
     "ttt_last_error": ([], ctypes.c_char_p),
-    "ttt_linear_fwd": ([_I] * 6 + [_P, _P, _I, _P, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P], _I),
+    "ttt_linear_fwd": ([_I] * 6 + [_P, _P, _I, _P, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P], _I),
     "ttt_linear_bwd_scratch_bytes": ([_I] * 6, _Z),
     "ttt_linear_bwd": (
         [_I] * 6
         + [_P, _P, _I, _P, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I]
+        + [_P, _P, _P]
         + [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _Z, _P],
         _I,
     ),

@@ -77,6 +77,15 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t* r, uint32_t addr) {
                : "r"(addr));
 }
 
+// Two 8x8 b16 matrices; lanes 0-15 supply the row addresses (matrix l/8, row l%8).
+__device__ __forceinline__ void ldsm_x2(uint32_t* r, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x2_t(uint32_t* r, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];\n" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
+}
+
 // Transposed store of four 8x8 b16 matrices (inverse of ldsm_x4_t's distribution).
 __device__ __forceinline__ void stsm_x4_t(uint32_t addr, const uint32_t* r) {
   asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(r[0]),

@@ -21,6 +21,7 @@ struct LinFwdParams {
   float* b_last;
   float* W_ckpt;
   float* b_ckpt;
+  float* Z_out;  // optional [B,NH,NC,CS,F] fp32: Z = XK W_n + b_n of every mini-batch
 };
 
 struct LinBwdParams {
@@ -46,7 +47,10 @@ struct LinBwdParams {
   void* dXK;
   void* deta;
   int dt_grad;
-  float* scratch;  // [B*NH][ckpt][CS][F] pre-activations Z of one group
+  float* scratch;        // [B*NH][ckpt][CS][F] pre-activations Z of one group (checkpoint path)
+  const float* Z_saved;  // optional: Z of every mini-batch stored by the forward
+  const float* W_last;   // final state (with Z_saved: start of the reverse walk)
+  const float* b_last;
 };
 
 struct MlpFwdParams {

@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(256) linear_fwd_kernel(LinFwdParams p) {
   __syncthreads();
 
   for (int n = 0; n < p.NC; ++n) {
-    if (n % p.ckpt == 0) {
+    if (p.W_ckpt && n % p.ckpt == 0) {
       const long long k = s * p.K + n / p.ckpt;
       for (int i = threadIdx.x; i < F * F; i += blockDim.x) p.W_ckpt[k * F * F + i] = W[i];
       for (int i = threadIdx.x; i < F; i += blockDim.x) p.b_ckpt[k * F + i] = bvec[i];
@@ -67,6 +67,10 @@ __global__ void __launch_bounds__(256) linear_fwd_kernel(LinFwdParams p) {
 
     ln_fused_rows(Z, G, bvec, XV, XK, gam, bet, C, F, nullptr, nullptr);
     for (int i = threadIdx.x; i < CC; i += blockDim.x) P[i] = E[i] * (P[i] + 1.f);
+    if (p.Z_out) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < CF; i += blockDim.x) p.Z_out[xb + i] = Z[i];
+    }
     for (int i = threadIdx.x; i < CF; i += blockDim.x) XKe[i] = E[(C - 1) * C + i / F] * XK[i];
     __syncthreads();
 
@@ -277,12 +281,15 @@ extern "C" int ttt_linear_fwd(int B, int NH, int NC, int CS, int F, int checkpoi
                               const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
                               const float* W1_init, const float* b1_init, const void* XQ, int dt_xq, const void* XV,
                               int dt_xv, const void* XK, int dt_xk, const void* eta, int dt_eta, void* XQW, int dt_out,
-                              float* W1_last, float* b1_last, float* W1_ckpt, float* b1_ckpt, void* stream) {
+                              float* W1_last, float* b1_last, float* W1_ckpt, float* b1_ckpt, float* Z_out,
+                              void* stream) {
   int rc = check_common(B, NH, NC, CS, F, checkpoint_group_size);
   if (rc) return rc;
   TTT_REQUIRE(ttt_norm_weight && ttt_norm_bias && W1_init && b1_init && XQ && XV && XK && eta && XQW && W1_last &&
-                  b1_last && W1_ckpt && b1_ckpt,
+                  b1_last,
               TTT_ERR_NULL, "ttt_linear_fwd: NULL pointer argument");
+  TTT_REQUIRE((W1_ckpt == nullptr) == (b1_ckpt == nullptr), TTT_ERR_NULL,
+              "ttt_linear_fwd: checkpoint pointers must be both set or both NULL");
   TTT_REQUIRE(valid_dtype(dt_ln) && valid_dtype(dt_xq) && valid_dtype(dt_xv) && valid_dtype(dt_xk) &&
                   valid_dtype(dt_eta) && valid_dtype(dt_out),
               TTT_ERR_DTYPE, "ttt_linear_fwd: unknown dtype code");
@@ -294,7 +301,7 @@ extern "C" int ttt_linear_fwd(int B, int NH, int NC, int CS, int F, int checkpoi
   p.XQ = XQ; p.XV = XV; p.XK = XK; p.eta = eta;
   p.dt_xq = dt_xq; p.dt_xv = dt_xv; p.dt_xk = dt_xk; p.dt_eta = dt_eta;
   p.out = XQW; p.dt_out = dt_out;
-  p.W_last = W1_last; p.b_last = b1_last; p.W_ckpt = W1_ckpt; p.b_ckpt = b1_ckpt;
+  p.W_last = W1_last; p.b_last = b1_last; p.W_ckpt = W1_ckpt; p.b_ckpt = b1_ckpt; p.Z_out = Z_out;
   rc = linear_fwd_fast(p, (cudaStream_t)stream);
   if (rc != TTT_NOT_APPLICABLE) return rc;
   const size_t smem = linear_fwd_smem(CS, F);
@@ -314,19 +321,17 @@ extern "C" int ttt_linear_bwd(int B, int NH, int NC, int CS, int F, int checkpoi
                               const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
                               const float* W1_ckpt, const float* b1_ckpt, const void* XQ, int dt_xq, const void* XV,
                               int dt_xv, const void* XK, int dt_xk, const void* eta, int dt_eta, const void* dXQW,
-                              int dt_dout, float* d_ln_w, float* d_ln_b, float* dW1, float* db1, void* dXQ, void* dXV,
-                              void* dXK, void* d_eta, int dt_grad, void* scratch, size_t scratch_bytes, void* stream) {
+                              int dt_dout, const float* Z_saved, const float* W1_last, const float* b1_last,
+                              float* d_ln_w, float* d_ln_b, float* dW1, float* db1, void* dXQ, void* dXV, void* dXK,
+                              void* d_eta, int dt_grad, void* scratch, size_t scratch_bytes, void* stream) {
   int rc = check_common(B, NH, NC, CS, F, checkpoint_group_size);
   if (rc) return rc;
   TTT_REQUIRE(ttt_norm_weight && ttt_norm_bias && W1_ckpt && b1_ckpt && XQ && XV && XK && eta && dXQW && d_ln_w &&
-                  d_ln_b && dW1 && db1 && dXQ && dXV && dXK && d_eta && scratch,
+                  d_ln_b && dW1 && db1 && dXQ && dXV && dXK && d_eta,
               TTT_ERR_NULL, "ttt_linear_bwd: NULL pointer argument");
   TTT_REQUIRE(valid_dtype(dt_ln) && valid_dtype(dt_xq) && valid_dtype(dt_xv) && valid_dtype(dt_xk) &&
                   valid_dtype(dt_eta) && valid_dtype(dt_dout) && valid_dtype(dt_grad),
               TTT_ERR_DTYPE, "ttt_linear_bwd: unknown dtype code");
-  const size_t need = ttt_linear_bwd_scratch_bytes(B, NH, NC, CS, F, checkpoint_group_size);
-  TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "ttt_linear_bwd: scratch has %zu bytes, needs %zu",
-              scratch_bytes, need);
   LinBwdParams p;
   p.B = B; p.NH = NH; p.NC = NC; p.CS = CS; p.F = F;
   p.ckpt = checkpoint_group_size < NC ? checkpoint_group_size : NC;
@@ -340,6 +345,12 @@ extern "C" int ttt_linear_bwd(int B, int NH, int NC, int CS, int F, int checkpoi
   p.d_ln_w = d_ln_w; p.d_ln_b = d_ln_b; p.dW = dW1; p.db = db1;
   p.dXQ = dXQ; p.dXV = dXV; p.dXK = dXK; p.deta = d_eta; p.dt_grad = dt_grad;
   p.scratch = (float*)scratch;
+  p.Z_saved = Z_saved; p.W_last = W1_last; p.b_last = b1_last;
+  rc = linear_bwd_fast(p, (cudaStream_t)stream);
+  if (rc != TTT_NOT_APPLICABLE) return rc;
+  const size_t need = ttt_linear_bwd_scratch_bytes(B, NH, NC, CS, F, checkpoint_group_size);
+  TTT_REQUIRE(scratch && scratch_bytes >= need, TTT_ERR_SCRATCH, "ttt_linear_bwd: scratch has %zu bytes, needs %zu",
+              scratch ? scratch_bytes : (size_t)0, need);
   const size_t smem = linear_bwd_smem(CS, F);
   rc = prepare_smem(linear_bwd_kernel, smem, "ttt_linear_bwd");
   if (rc) return rc;

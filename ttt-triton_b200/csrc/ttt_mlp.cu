@@ -14,6 +14,7 @@
 // in the backward) where they stay L2-resident, per-row activations in shared memory.
 #include "capi_common.cuh"
 #include "common.cuh"
+#include "fast_paths.cuh"
 #include "params.cuh"
 
 namespace ttt {
@@ -62,7 +63,7 @@ __global__ void __launch_bounds__(256) mlp_fwd_kernel(MlpFwdParams p) {
   __syncthreads();
 
   for (int n = 0; n < p.NC; ++n) {
-    if (n % p.ckpt == 0) {
+    if (p.W1_ckpt && n % p.ckpt == 0) {
       const long long k = s * p.K + n / p.ckpt;
       copy_state(p.W1_ckpt + k * F * FF, W1, (long long)F * FF);
       copy_state(p.W2_ckpt + k * FF * F, W2, (long long)FF * F);
@@ -494,8 +495,11 @@ extern "C" int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int che
   if (rc) return rc;
   TTT_REQUIRE(memo_segment_size > 0, TTT_ERR_SHAPE, "memo_segment_size must be positive (got %d)", memo_segment_size);
   TTT_REQUIRE(ttt_norm_weight && ttt_norm_bias && W1_init && b1_init && W2_init && b2_init && XQ && XV && XK && eta &&
-                  XQW && W1_last && b1_last && W2_last && b2_last && W1_ckpt && b1_ckpt && W2_ckpt && b2_ckpt,
+                  XQW && W1_last && b1_last && W2_last && b2_last,
               TTT_ERR_NULL, "ttt_mlp_fwd: NULL pointer argument");
+  const bool any_ck = W1_ckpt || b1_ckpt || W2_ckpt || b2_ckpt;
+  const bool all_ck = W1_ckpt && b1_ckpt && W2_ckpt && b2_ckpt;
+  TTT_REQUIRE(!any_ck || all_ck, TTT_ERR_NULL, "ttt_mlp_fwd: checkpoint pointers must be all set or all NULL");
   const bool any_memo = W1_memo || b1_memo || W2_memo || b2_memo;
   const bool all_memo = W1_memo && b1_memo && W2_memo && b2_memo;
   TTT_REQUIRE(!any_memo || all_memo, TTT_ERR_NULL, "ttt_mlp_fwd: memo pointers must be all set or all NULL");
@@ -514,6 +518,8 @@ extern "C" int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int che
   p.W1_last = W1_last; p.b1_last = b1_last; p.W2_last = W2_last; p.b2_last = b2_last;
   p.W1_ckpt = W1_ckpt; p.b1_ckpt = b1_ckpt; p.W2_ckpt = W2_ckpt; p.b2_ckpt = b2_ckpt;
   p.W1_memo = all_memo ? W1_memo : nullptr; p.b1_memo = b1_memo; p.W2_memo = W2_memo; p.b2_memo = b2_memo;
+  rc = mlp_fwd_fast(p, (cudaStream_t)stream);
+  if (rc != TTT_NOT_APPLICABLE) return rc;
   const size_t smem = mlp_fwd_smem(CS, F, FF);
   rc = prepare_smem(mlp_fwd_kernel, smem, "ttt_mlp_fwd");
   if (rc) return rc;

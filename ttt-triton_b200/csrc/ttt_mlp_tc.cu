@@ -1,0 +1,533 @@
+// TTT-MLP forward on the tensor cores (mma.sync bf16/fp16, fp32 accumulate) for the
+// benchmark shape: F = 64, FF = 256, CS = 16, 16-bit activations.
+//
+// One CTA of 8 warps per (batch, head) stream; warp w owns hidden units
+// [32w, 32w + 32). Its slices of the fp32 state, W1^T (32 x 64) and W2^T (64 x 32), stay in
+// mma accumulator fragments for the whole sequence (the accumulator layout of W1^T is the
+// B-operand layout of W1, and of W2^T the B layout of W2); the biases live in shared
+// memory. Per mini-batch (ops/ttt_mlp.py:9-67):
+//   A (MMA)  Z1 = XK W1 + b1, Z1q = XQ W1 + b1, X2 = gelu(Z1), partial Z2_w = X2_w W2_w;
+//            warps 0-1 form -P1 = -eta * (XQ XK^T + 1)
+//   C (rows) Z2 = sum_w Z2_w + b2, G2 = ln_fused_l2_bwd(Z2, XV - XK) (16 lanes per token)
+//   D (MMA)  H = G2 W2^T, G1 = H * gelu_bwd(Z1); W1 += XK^T (-e G1), b1 += 1^T (-e G1);
+//            Z1bar = Z1q - P1 G1, X2bar = gelu(Z1bar), A2_w = X2bar_w X2_w^T,
+//            partial Z2bar_w = X2bar_w W2_w - (eta * A2_w) G2  (- eta G2 once);
+//            W2 += X2^T (-e G2), b2 += 1^T (-e G2)
+//   E (rows) XQW = XQ + LN(sum_w Z2bar_w + b2_old)
+// The dual-form product P2 G2 = (eta * (sum_w A2_w + 1)) G2 is split by linearity over the
+// warps' partial A2_w, so no cross-warp reduction of A2 is needed. GELU and its derivative
+// use the hardware tanh approximation (tanh.approx.f32, relative error ~2^-11), below the
+// 16-bit operand rounding of this path.
+#include "capi_common.cuh"
+#include "common.cuh"
+#include "fast_paths.cuh"
+#include "mma.cuh"
+#include "params.cuh"
+
+namespace ttt {
+namespace mlp_tc {
+
+constexpr int F = 64, FF = 256, C = 16, NW = 8, NTHREADS = 32 * NW, NSTAGE = 3;
+constexpr int TILE = C * F * 2;
+constexpr int ETA = C * C * 2;
+constexpr int STAGE = 3 * TILE + ETA;
+constexpr int OFF_XQ = 0, OFF_XK = TILE, OFF_XV = 2 * TILE, OFF_ETA = 3 * TILE;
+constexpr int PLD = F + 8;                              // fp32 row stride of the partial tiles
+constexpr int OFF_PART = NSTAGE * STAGE;                // fp32 [NW][C][PLD] per-warp partial sums
+constexpr int OFF_G = OFF_PART + NW * C * PLD * 4;      // 16-bit [C][F] swizzled: G2
+constexpr int OFF_EG = OFF_G + TILE;                    // 16-bit [C][F] swizzled: -e * G2
+constexpr int OFF_P = OFF_EG + TILE;                    // 16-bit [C][C]: -P1
+constexpr int OFF_B1 = OFF_P + ETA;                     // fp32 [FF]
+constexpr int OFF_B2 = OFF_B1 + FF * 4;                 // fp32 [2][F] (ping-pong)
+constexpr int SMEM = OFF_B2 + 2 * F * 4;
+
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float gelu_fast(float x) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  return 0.5f * x * (1.f + tanh_fast(k0 * (x + k1 * x * x * x)));
+}
+// the reference's gelu_bwd (ops/ttt_utils.py:51-54) with the hardware tanh
+__device__ __forceinline__ float gelu_bwd_fast(float x) {
+  const float t = tanh_fast(0.79788456f * x * (1.f + 0.044715f * x * x));
+  return 0.5f * x * ((1.f - t * t) * (0.79788456f + 0.1070322243f * x * x)) + 0.5f * (1.f + t);
+}
+
+__device__ __forceinline__ void load_stage(uint8_t* st, const MlpFwdParams& p, long long s, int n) {
+  const int tid = threadIdx.x;
+  const long long tb = (s * p.NC + n) * (long long)(C * F) * 2;
+  if (tid < 128) {
+    const int row = tid >> 3, ch = tid & 7;
+    const uint32_t dst = smem_u32(st) + swz128(row, ch);
+    cp_async16(dst + OFF_XQ, (const uint8_t*)p.XQ + tb + row * 128 + ch * 16);
+    cp_async16(dst + OFF_XK, (const uint8_t*)p.XK + tb + row * 128 + ch * 16);
+  } else {
+    const int i = tid - 128, row = i >> 3, ch = i & 7;
+    cp_async16(smem_u32(st) + OFF_XV + swz128(row, ch), (const uint8_t*)p.XV + tb + row * 128 + ch * 16);
+    if (i < 32) {
+      const long long eb = (s * p.NC + n) * (long long)(C * C) * 2;
+      cp_async16(smem_u32(st) + OFF_ETA + i * 16, (const uint8_t*)p.eta + eb + i * 16);
+    }
+  }
+}
+
+__device__ __forceinline__ float red16(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 8);
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack4(const uint8_t* src, float* v) {
+  const uint2 u = *reinterpret_cast<const uint2*>(src);
+  const float2 a = Half2<T>::unpack(u.x), b = Half2<T>::unpack(u.y);
+  v[0] = a.x;
+  v[1] = a.y;
+  v[2] = b.x;
+  v[3] = b.y;
+}
+
+// Sum of the 8 warps' partial tiles for token tk, features 4q..4q+3.
+__device__ __forceinline__ void sum_partials(const float* part, int tk, int q, float* z) {
+  float4 acc = *reinterpret_cast<const float4*>(part + tk * PLD + 4 * q);
+#pragma unroll
+  for (int w = 1; w < NW; ++w) {
+    const float4 v = *reinterpret_cast<const float4*>(part + (w * C + tk) * PLD + 4 * q);
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  z[0] = acc.x;
+  z[1] = acc.y;
+  z[2] = acc.z;
+  z[3] = acc.w;
+}
+
+// State slices <-> global [F][FF] (W1) and [FF][F] (W2) layouts.
+__device__ __forceinline__ void state_io(float (*S1)[8][4], float (*S2)[4][4], float* W1, float* W2, int fb, int g,
+                                         int t, bool store) {
+#pragma unroll
+  for (int m = 0; m < 2; ++m)
+#pragma unroll
+    for (int nf = 0; nf < 8; ++nf) {
+      const int f = 8 * nf + 2 * t, ff = fb + 16 * m + g;
+      float* p0 = W1 + f * FF + ff;
+      if (store) {
+        p0[0] = S1[m][nf][0];
+        p0[FF] = S1[m][nf][1];
+        p0[8] = S1[m][nf][2];
+        p0[FF + 8] = S1[m][nf][3];
+      } else {
+        S1[m][nf][0] = p0[0];
+        S1[m][nf][1] = p0[FF];
+        S1[m][nf][2] = p0[8];
+        S1[m][nf][3] = p0[FF + 8];
+      }
+    }
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int f = 16 * m + g, ff = fb + 8 * j + 2 * t;
+      float* p0 = W2 + ff * F + f;
+      if (store) {
+        p0[0] = S2[m][j][0];
+        p0[F] = S2[m][j][1];
+        p0[8] = S2[m][j][2];
+        p0[F + 8] = S2[m][j][3];
+      } else {
+        S2[m][j][0] = p0[0];
+        S2[m][j][1] = p0[F];
+        S2[m][j][2] = p0[8];
+        S2[m][j][3] = p0[F + 8];
+      }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p) {
+  using H = Half2<T>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int mi = lane >> 3, r8 = lane & 7;
+  const long long s = blockIdx.x;
+  const int h = (int)(s % p.NH);
+  const int tk = tid >> 4, q = tid & 15;
+  const int fb = 32 * warp;
+  float* part = reinterpret_cast<float*>(smem + OFF_PART);
+  float* pw = part + warp * C * PLD;
+  float* b1s = reinterpret_cast<float*>(smem + OFF_B1);
+  float* b2s = reinterpret_cast<float*>(smem + OFF_B2);
+
+  float S1[2][8][4], S2[4][4][4];
+  state_io(S1, S2, const_cast<float*>(p.W1_init + s * F * FF), const_cast<float*>(p.W2_init + s * FF * F), fb, g, t,
+           false);
+  for (int i = tid; i < FF; i += NTHREADS) b1s[i] = p.b1_init[s * FF + i];
+  for (int i = tid; i < F; i += NTHREADS) b2s[i] = p.b2_init[s * F + i];
+  float gm[4], bt[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    gm[j] = ld_elem(p.ln_w, (long long)h * F + 4 * q + j, p.dt_ln);
+    bt[j] = ld_elem(p.ln_b, (long long)h * F + 4 * q + j, p.dt_ln);
+  }
+  const uint32_t ones = H::pack(1.f, 1.f);
+  const uint32_t a_ones[4] = {ones, ones, ones, ones};
+
+#pragma unroll
+  for (int i = 0; i < NSTAGE - 1; ++i) {
+    if (i < p.NC) load_stage(smem + i * STAGE, p, s, i);
+    cp_async_commit();
+  }
+
+  int ck_left = 0, memo_left = 0;  // mini-batches until the next checkpoint / memo state
+  for (int n = 0; n < p.NC; ++n) {
+    cp_async_wait<NSTAGE - 2>();
+    __syncthreads();
+    {
+      const int nn = n + NSTAGE - 1;
+      if (nn < p.NC) load_stage(smem + (nn % NSTAGE) * STAGE, p, s, nn);
+      cp_async_commit();
+    }
+    const uint8_t* st = smem + (n % NSTAGE) * STAGE;
+    const uint32_t sb = smem_u32(st);
+    const float* b2_old = b2s + (n & 1) * F;
+    float* b2_new = b2s + ((n + 1) & 1) * F;
+
+    if (p.W1_ckpt && ck_left == 0) {  // state at the start of the checkpoint group
+      const long long k = s * p.K + n / p.ckpt;
+      state_io(S1, S2, p.W1_ckpt + k * F * FF, p.W2_ckpt + k * FF * F, fb, g, t, true);
+      for (int i = tid; i < FF; i += NTHREADS) p.b1_ckpt[k * FF + i] = b1s[i];
+      for (int i = tid; i < F; i += NTHREADS) p.b2_ckpt[k * F + i] = b2_old[i];
+      ck_left = p.ckpt;
+    }
+    --ck_left;
+
+    // ---------------- A: Z1 = XK W1 + b1, Z1q = XQ W1 + b1 (warp's 32 hidden units)
+    float Z1[4][4], Zq[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) Z1[j][c] = Zq[j][c] = 0.f;
+    float A1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t ak[4], aq[4];
+      const uint32_t aoff = swz128((mi & 1) * 8 + r8, 2 * kk + (mi >> 1));
+      ldsm_x4(ak, sb + OFF_XK + aoff);
+      ldsm_x4(aq, sb + OFF_XQ + aoff);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int m = j >> 1, hh = 2 * (j & 1);
+        const uint32_t b[2] = {H::pack(S1[m][2 * kk][hh], S1[m][2 * kk][hh + 1]),
+                               H::pack(S1[m][2 * kk + 1][hh], S1[m][2 * kk + 1][hh + 1])};
+        mma16816<T>(Z1[j], ak, b);
+        mma16816<T>(Zq[j], aq, b);
+      }
+      if (warp < 2) {
+        uint32_t bk[2];
+        ldsm_x2(bk, sb + OFF_XK + swz128(8 * warp + r8, 2 * kk + (mi & 1)));
+        mma16816<T>(A1, aq, bk);
+      }
+    }
+    if (warp < 2) {
+      const int j0 = 8 * warp + 2 * t;
+      const T* E = reinterpret_cast<const T*>(st + OFF_ETA);
+      const float2 e_lo = H::unpack(*reinterpret_cast<const uint32_t*>(E + g * C + j0));
+      const float2 e_hi = H::unpack(*reinterpret_cast<const uint32_t*>(E + (g + 8) * C + j0));
+      *reinterpret_cast<uint32_t*>(smem + OFF_P + (g * C + j0) * 2) =
+          H::pack(-e_lo.x * (A1[0] + 1.f), -e_lo.y * (A1[1] + 1.f));
+      *reinterpret_cast<uint32_t*>(smem + OFF_P + ((g + 8) * C + j0) * 2) =
+          H::pack(-e_hi.x * (A1[2] + 1.f), -e_hi.y * (A1[3] + 1.f));
+    }
+    uint32_t X2p[4][2], GPp[4][2];  // gelu(Z1) and gelu_bwd(Z1), 16-bit pairs in C layout
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 bb = *reinterpret_cast<const float2*>(b1s + fb + 8 * j + 2 * t);
+      const float z0 = Z1[j][0] + bb.x, z1 = Z1[j][1] + bb.y, z2 = Z1[j][2] + bb.x, z3 = Z1[j][3] + bb.y;
+      Zq[j][0] += bb.x;
+      Zq[j][1] += bb.y;
+      Zq[j][2] += bb.x;
+      Zq[j][3] += bb.y;
+      X2p[j][0] = H::pack(gelu_fast(z0), gelu_fast(z1));
+      X2p[j][1] = H::pack(gelu_fast(z2), gelu_fast(z3));
+      GPp[j][0] = H::pack(gelu_bwd_fast(z0), gelu_bwd_fast(z1));
+      GPp[j][1] = H::pack(gelu_bwd_fast(z2), gelu_bwd_fast(z3));
+    }
+    // partial Z2_w = X2_w W2_w  (B operand of W2 = accumulator layout of W2^T)
+#pragma unroll
+    for (int nf = 0; nf < 8; ++nf) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int m = nf >> 1, hh = 2 * (nf & 1);
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        const uint32_t a[4] = {X2p[2 * ks][0], X2p[2 * ks][1], X2p[2 * ks + 1][0], X2p[2 * ks + 1][1]};
+        const uint32_t b[2] = {H::pack(S2[m][2 * ks][hh], S2[m][2 * ks][hh + 1]),
+                               H::pack(S2[m][2 * ks + 1][hh], S2[m][2 * ks + 1][hh + 1])};
+        mma16816<T>(acc, a, b);
+      }
+      *reinterpret_cast<float2*>(pw + g * PLD + 8 * nf + 2 * t) = make_float2(acc[0], acc[1]);
+      *reinterpret_cast<float2*>(pw + (g + 8) * PLD + 8 * nf + 2 * t) = make_float2(acc[2], acc[3]);
+    }
+    __syncthreads();
+
+    // ---------------- C: Z2 = sum + b2, G2 = ln_fused_l2_bwd(Z2, XV - XK)
+    {
+      float z[4], xv[4], xk[4];
+      sum_partials(part, tk, q, z);
+      const float4 bb = *reinterpret_cast<const float4*>(b2_old + 4 * q);
+      z[0] += bb.x;
+      z[1] += bb.y;
+      z[2] += bb.z;
+      z[3] += bb.w;
+      const uint32_t xo = swz128(tk, q >> 1) + (q & 1) * 8;
+      unpack4<T>(st + OFF_XV + xo, xv);
+      unpack4<T>(st + OFF_XK + xo, xk);
+      const float mu = red16(z[0] + z[1] + z[2] + z[3]) * (1.f / F);
+      float d[4], m2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        d[j] = z[j] - mu;
+        m2 += d[j] * d[j];
+      }
+      const float rstd = 1.f / sqrtf(red16(m2) * (1.f / F) + kLnEps);
+      float xh[4], gh[4], s1 = 0.f, s2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xh[j] = d[j] * rstd;
+        gh[j] = (gm[j] * xh[j] + bt[j] - (xv[j] - xk[j])) * gm[j];
+        s1 += gh[j];
+        s2 += gh[j] * xh[j];
+      }
+      s1 = red16(s1);
+      s2 = red16(s2);
+      const float inv = rstd * (1.f / F);
+      float G[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) G[j] = (F * gh[j] - s1 - xh[j] * s2) * inv;
+      const float e = (float)reinterpret_cast<const T*>(st + OFF_ETA)[(C - 1) * C + tk];
+      *reinterpret_cast<uint2*>(smem + OFF_G + xo) = make_uint2(H::pack(G[0], G[1]), H::pack(G[2], G[3]));
+      *reinterpret_cast<uint2*>(smem + OFF_EG + xo) =
+          make_uint2(H::pack(-e * G[0], -e * G[1]), H::pack(-e * G[2], -e * G[3]));
+    }
+    __syncthreads();
+
+    // ---------------- D
+    const uint32_t gb = smem_u32(smem + OFF_G), egb = smem_u32(smem + OFF_EG);
+    uint32_t ub[2][4], eb[2][4];  // G1 and -e*G1 transposed: [token half][hidden tile]
+    {
+      // H = G2 W2^T (B operand of W2^T via movmatrix of the W2^T accumulators)
+      float Hh[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) Hh[j][0] = Hh[j][1] = Hh[j][2] = Hh[j][3] = 0.f;
+#pragma unroll
+      for (int kf = 0; kf < 4; ++kf) {
+        uint32_t ag[4];
+        ldsm_x4(ag, gb + swz128((mi & 1) * 8 + r8, 2 * kf + (mi >> 1)));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t b[2] = {movm_t(H::pack(S2[kf][j][0], S2[kf][j][1])),
+                                 movm_t(H::pack(S2[kf][j][2], S2[kf][j][3]))};
+          mma16816<T>(Hh[j], ag, b);
+        }
+      }
+      const T* E = reinterpret_cast<const T*>(st + OFF_ETA);
+      const float eg0 = -(float)E[(C - 1) * C + g], eg1 = -(float)E[(C - 1) * C + g + 8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 gp0 = H::unpack(GPp[j][0]), gp1 = H::unpack(GPp[j][1]);
+        const float g0 = Hh[j][0] * gp0.x, g1 = Hh[j][1] * gp0.y, g2 = Hh[j][2] * gp1.x, g3 = Hh[j][3] * gp1.y;
+        ub[0][j] = movm_t(H::pack(g0, g1));
+        ub[1][j] = movm_t(H::pack(g2, g3));
+        eb[0][j] = movm_t(H::pack(eg0 * g0, eg0 * g1));
+        eb[1][j] = movm_t(H::pack(eg1 * g2, eg1 * g3));
+      }
+    }
+    // W1^T += (-e G1)^T XK ; b1 += 1^T (-e G1)
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t bx[4];
+      ldsm_x4_t(bx, sb + OFF_XK + swz128((mi & 1) * 8 + r8, 2 * np + (mi >> 1)));
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        const uint32_t a[4] = {eb[0][2 * m], eb[0][2 * m + 1], eb[1][2 * m], eb[1][2 * m + 1]};
+        mma16816<T>(S1[m][2 * np], a, bx);
+        mma16816<T>(S1[m][2 * np + 1], a, bx + 2);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float db[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t b[2] = {eb[0][j], eb[1][j]};
+      mma16816<T>(db, a_ones, b);
+      if (g == 0) {
+        float2* bp = reinterpret_cast<float2*>(b1s + fb + 8 * j + 2 * t);
+        const float2 o = *bp;
+        *bp = make_float2(o.x + db[0], o.y + db[1]);
+      }
+    }
+    // Z1bar = Z1q - P1 G1, X2bar = gelu(Z1bar)
+    uint32_t XBp[4][2];
+    {
+      uint32_t ap[4];
+      ldsm_x4(ap, smem_u32(smem + OFF_P) + ((mi & 1) * 8 + r8) * 32 + (mi >> 1) * 16);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t b[2] = {ub[0][j], ub[1][j]};
+        mma16816<T>(Zq[j], ap, b);
+        XBp[j][0] = H::pack(gelu_fast(Zq[j][0]), gelu_fast(Zq[j][1]));
+        XBp[j][1] = H::pack(gelu_fast(Zq[j][2]), gelu_fast(Zq[j][3]));
+      }
+    }
+    // A2_w = X2bar_w X2_w^T ; a = -(eta * (A2_w [+1 on warp 0]))
+    uint32_t aA2[4];
+    {
+      float A2[2][4];
+#pragma unroll
+      for (int jt = 0; jt < 2; ++jt) {
+        A2[jt][0] = A2[jt][1] = A2[jt][2] = A2[jt][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          const uint32_t a[4] = {XBp[2 * ks][0], XBp[2 * ks][1], XBp[2 * ks + 1][0], XBp[2 * ks + 1][1]};
+          const uint32_t b[2] = {X2p[2 * ks][jt], X2p[2 * ks + 1][jt]};
+          mma16816<T>(A2[jt], a, b);
+        }
+      }
+      const T* E = reinterpret_cast<const T*>(st + OFF_ETA);
+      const float one = warp == 0 ? 1.f : 0.f;
+      float v[2][4];
+#pragma unroll
+      for (int jt = 0; jt < 2; ++jt) {
+        const float2 e0 = H::unpack(*reinterpret_cast<const uint32_t*>(E + g * C + 8 * jt + 2 * t));
+        const float2 e1 = H::unpack(*reinterpret_cast<const uint32_t*>(E + (g + 8) * C + 8 * jt + 2 * t));
+        v[jt][0] = -e0.x * (A2[jt][0] + one);
+        v[jt][1] = -e0.y * (A2[jt][1] + one);
+        v[jt][2] = -e1.x * (A2[jt][2] + one);
+        v[jt][3] = -e1.y * (A2[jt][3] + one);
+      }
+      aA2[0] = H::pack(v[0][0], v[0][1]);
+      aA2[1] = H::pack(v[0][2], v[0][3]);
+      aA2[2] = H::pack(v[1][0], v[1][1]);
+      aA2[3] = H::pack(v[1][2], v[1][3]);
+    }
+    // partial Z2bar_w = X2bar_w W2_w + aA2 G2  -> shared memory
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t bg[4];
+      ldsm_x4_t(bg, gb + swz128((mi & 1) * 8 + r8, 2 * np + (mi >> 1)));
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int nf = 2 * np + hf, m = nf >> 1, hh = 2 * (nf & 1);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816<T>(acc, aA2, bg + 2 * hf);
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          const uint32_t a[4] = {XBp[2 * ks][0], XBp[2 * ks][1], XBp[2 * ks + 1][0], XBp[2 * ks + 1][1]};
+          const uint32_t b[2] = {H::pack(S2[m][2 * ks][hh], S2[m][2 * ks][hh + 1]),
+                                 H::pack(S2[m][2 * ks + 1][hh], S2[m][2 * ks + 1][hh + 1])};
+          mma16816<T>(acc, a, b);
+        }
+        *reinterpret_cast<float2*>(pw + g * PLD + 8 * nf + 2 * t) = make_float2(acc[0], acc[1]);
+        *reinterpret_cast<float2*>(pw + (g + 8) * PLD + 8 * nf + 2 * t) = make_float2(acc[2], acc[3]);
+      }
+    }
+    // W2^T += (-e G2)^T X2 ; b2_new = b2_old + 1^T (-e G2) (warp w: features 8w..8w+7)
+    {
+      uint32_t bx2[4][2];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        bx2[j][0] = movm_t(X2p[j][0]);
+        bx2[j][1] = movm_t(X2p[j][1]);
+      }
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        uint32_t a[4];
+        ldsm_x4_t(a, egb + swz128((mi >> 1) * 8 + r8, 2 * m + (mi & 1)));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) mma16816<T>(S2[m][j], a, bx2[j]);
+      }
+      uint32_t bg2[2];
+      ldsm_x2_t(bg2, egb + swz128((lane & 8) + r8, warp));
+      float db[4] = {0.f, 0.f, 0.f, 0.f};
+      mma16816<T>(db, a_ones, bg2);
+      if (g == 0) {
+        const int f = 8 * warp + 2 * t;
+        b2_new[f] = b2_old[f] + db[0];
+        b2_new[f + 1] = b2_old[f + 1] + db[1];
+      }
+    }
+    __syncthreads();
+
+    // ---------------- E: XQW = XQ + LN(sum_w Z2bar_w + b2_old)
+    {
+      float z[4], xq[4];
+      sum_partials(part, tk, q, z);
+      const float4 bb = *reinterpret_cast<const float4*>(b2_old + 4 * q);
+      z[0] += bb.x;
+      z[1] += bb.y;
+      z[2] += bb.z;
+      z[3] += bb.w;
+      unpack4<T>(st + OFF_XQ + swz128(tk, q >> 1) + (q & 1) * 8, xq);
+      const float mu = red16(z[0] + z[1] + z[2] + z[3]) * (1.f / F);
+      float d[4], m2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        d[j] = z[j] - mu;
+        m2 += d[j] * d[j];
+      }
+      const float rstd = 1.f / sqrtf(red16(m2) * (1.f / F) + kLnEps);
+      float y[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) y[j] = xq[j] + gm[j] * d[j] * rstd + bt[j];
+      uint8_t* dst = (uint8_t*)p.out + ((s * p.NC + n) * (long long)(C * F) + tk * F + 4 * q) * 2;
+      *reinterpret_cast<uint2*>(dst) = make_uint2(H::pack(y[0], y[1]), H::pack(y[2], y[3]));
+    }
+
+    if (p.W1_memo && memo_left == 0) {  // state after this mini-batch
+      const long long m = s * p.NS + n / p.memo;
+      state_io(S1, S2, p.W1_memo + m * F * FF, p.W2_memo + m * FF * F, fb, g, t, true);
+      for (int i = tid; i < FF; i += NTHREADS) p.b1_memo[m * FF + i] = b1s[i];
+      for (int i = tid; i < F; i += NTHREADS) p.b2_memo[m * F + i] = b2_new[i];
+      memo_left = p.memo;
+    }
+    --memo_left;
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  state_io(S1, S2, p.W1_last + s * F * FF, p.W2_last + s * FF * F, fb, g, t, true);
+  const float* b2_fin = b2s + (p.NC & 1) * F;
+  for (int i = tid; i < FF; i += NTHREADS) p.b1_last[s * FF + i] = b1s[i];
+  for (int i = tid; i < F; i += NTHREADS) p.b2_last[s * F + i] = b2_fin[i];
+}
+
+}  // namespace mlp_tc
+
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+int mlp_fwd_fast(const MlpFwdParams& p, cudaStream_t stream) {
+  using namespace mlp_tc;
+  if (p.CS != C || p.F != F || p.FF != FF) return TTT_NOT_APPLICABLE;
+  const int dt = p.dt_xq;
+  if (dt != DT_BF16 && dt != DT_F16) return TTT_NOT_APPLICABLE;
+  if (p.dt_xk != dt || p.dt_xv != dt || p.dt_eta != dt || p.dt_out != dt) return TTT_NOT_APPLICABLE;
+  if (!aligned16(p.XQ) || !aligned16(p.XK) || !aligned16(p.XV) || !aligned16(p.eta) || !aligned16(p.out))
+    return TTT_NOT_APPLICABLE;
+  int rc;
+  if (dt == DT_BF16) {
+    rc = prepare_smem(mlp_fwd_tc_kernel<__nv_bfloat16>, SMEM, "ttt_mlp_fwd");
+    if (rc) return rc;
+    mlp_fwd_tc_kernel<__nv_bfloat16><<<p.B * p.NH, NTHREADS, SMEM, stream>>>(p);
+  } else {
+    rc = prepare_smem(mlp_fwd_tc_kernel<__half>, SMEM, "ttt_mlp_fwd");
+    if (rc) return rc;
+    mlp_fwd_tc_kernel<__half><<<p.B * p.NH, NTHREADS, SMEM, stream>>>(p);
+  }
+  return check_launch("ttt_mlp_fwd");
+}
+
+}  // namespace ttt

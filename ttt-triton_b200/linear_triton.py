@@ -24,19 +24,21 @@ from _sharding import HEAD, LN, local_map
 
 def _forward_core(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, XQ, XV, XK, eta, checkpoint_group_size):
     ckpt = int(checkpoint_group_size)
-    XQW, _, _, W_ckpt, b_ckpt = _core.linear_forward(
-        ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, XQ, XV, XK, eta, ckpt
+    train = any(ctx.needs_input_grad)
+    XQW, W_last, b_last, W_ckpt, b_ckpt, Z = _core.linear_forward(
+        ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, XQ, XV, XK, eta, ckpt, for_backward=train
     )
     ctx.ckpt = ckpt
-    ctx.save_for_backward(XQ, XV, XK, eta, ttt_norm_weight, ttt_norm_bias, W_ckpt, b_ckpt)
+    if train:
+        ctx.save_for_backward(XQ, XV, XK, eta, ttt_norm_weight, ttt_norm_bias, W_ckpt, b_ckpt, Z, W_last, b_last)
     return XQW
 
 
 def _backward_core(ctx, grad_XQW):
-    XQ, XV, XK, eta, ln_w, ln_b, W_ckpt, b_ckpt = ctx.saved_tensors
+    XQ, XV, XK, eta, ln_w, ln_b, W_ckpt, b_ckpt, Z, W_last, b_last = ctx.saved_tensors
     mp = XQ.dtype
     d_ln_w, d_ln_b, dW1, db1, dXQ, dXV, dXK, deta = _core.linear_backward(
-        ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, grad_XQW, ctx.ckpt
+        ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, grad_XQW, ctx.ckpt, Z=Z, W_last=W_last, b_last=b_last
     )
     return (
         d_ln_w.sum(0).reshape(ln_w.shape).to(mp),

@@ -25,8 +25,10 @@ def _forward_core(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init
                   checkpoint_group_size, memo_segment_size):
     ckpt = int(checkpoint_group_size)
     XQW, _, ck, memo = _core.mlp_forward(
-        ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ, XV, XK, eta, ckpt, memo_segment_size
+        ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ, XV, XK, eta, ckpt, memo_segment_size,
+        for_backward=any(ctx.needs_input_grad),
     )
+    ck = ck if ck is not None else ()
     ctx.ckpt = ckpt
     ctx.save_for_backward(XQ, XV, XK, eta, ttt_norm_weight, ttt_norm_bias, *ck)
     ctx.mark_non_differentiable(*memo)

@@ -26,8 +26,10 @@ def _forward_core(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init
                          f"W2 {tuple(W2_init.shape)} for F = {F}")
     ckpt = int(checkpoint_group_size)
     XQW, _, ck, _ = _core.mlp_forward(
-        ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ, XV, XK, eta, ckpt, None
+        ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ, XV, XK, eta, ckpt, None,
+        for_backward=any(ctx.needs_input_grad),
     )
+    ck = ck if ck is not None else ()
     ctx.ckpt = ckpt
     ctx.save_for_backward(XQ, XV, XK, eta, ttt_norm_weight, ttt_norm_bias, *ck)
     return XQW

@@ -16,7 +16,9 @@ class _MLPScan(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, ckpt):
-        XQW, _, ck, _ = _core.mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, ckpt, None)
+        XQW, _, ck, _ = _core.mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, ckpt, None,
+                                          for_backward=any(ctx.needs_input_grad))
+        ck = ck if ck is not None else ()
         ctx.ckpt = ckpt
         ctx.save_for_backward(XQ, XV, XK, eta, ln_w, ln_b, *ck)
         return XQW
