@@ -105,6 +105,32 @@ int ttt_linear_bwd(int B, int NH, int NC, int CS, int F, int checkpoint_group_si
                    void* scratch, size_t scratch_bytes, void* stream);
 
 /*
+ * Allocation-free TTT-Linear backward (no counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory where they enqueue work, for example an
+ * inference-engine plugin whose enqueue callback is only handed pre-sized buffers, or a
+ * service that fixes its device-memory budget at start-up. Same arguments, algorithm and
+ * results as ttt_linear_bwd on its checkpoint-recompute path (no Z_saved), but the
+ * scratch comes from a 16 MiB array compiled into the library, which every GPU that
+ * loads the library holds until the process exits. Requests needing more than 16 MiB
+ * (ttt_linear_bwd_scratch_bytes) fail with TTT_ERR_SCRATCH. The call allocates nothing.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress,
+ * once per device, on the current device); make that first call before any stream
+ * capture. All calls on a device share the one array: calls whose work overlaps on the
+ * GPU (different streams, no ordering between them) race on it. Each call overwrites
+ * the part it uses before reading it, so no clearing is needed between calls.
+ */
+int ttt_linear_bwd_noalloc(int B, int NH, int NC, int CS, int F, int checkpoint_group_size,
+                           const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
+                           const float* W1_ckpt, const float* b1_ckpt,
+                           const void* XQ, int dt_xq, const void* XV, int dt_xv, const void* XK, int dt_xk,
+                           const void* eta, int dt_eta,
+                           const void* dXQW, int dt_dout,
+                           float* d_ln_w, float* d_ln_b, float* dW1, float* db1,
+                           void* dXQ, void* dXV, void* dXK, void* d_eta, int dt_grad,
+                           void* stream);
+
+/*
  * TTT-MLP forward scan (F -> FF -> F, tanh-GELU). Replaces the launch of
  * `ttt_mlp_scan_forward` in mlp_triton.py:130-178 (TritonMLP._forward_core) and, with
  * FF == F, the F x F launch of mlp_triton_back.py:109-146. Dual form of

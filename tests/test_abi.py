@@ -78,3 +78,10 @@ def test_dtype_codes():
     assert _lib.dtype_code(torch.zeros(1, dtype=torch.float16)) == 2
     with pytest.raises(TypeError):
         _lib.dtype_code(torch.zeros(1, dtype=torch.float64))
+
+
+def test_noalloc_backward_rejects_requests_beyond_its_scratch():
+    # 4096 streams x 16 x 16 x 64 fp32 = 64 MiB of scratch > the library's 16 MiB
+    rc = _lib.lib.ttt_linear_bwd_noalloc(64, 64, 16, 16, 64, 16, FAKE, FAKE, 0, FAKE, FAKE, FAKE, 0, FAKE, 0, FAKE,
+                                         0, FAKE, 0, FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 0, None)
+    assert rc == -5 and "16777216" in _lib.lib.ttt_last_error().decode()

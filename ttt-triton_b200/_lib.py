@@ -34,6 +34,12 @@ _SIGNATURES = {
         + [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _Z, _P],
         _I,
     ),
+    "ttt_linear_bwd_noalloc": (
+        [_I] * 6
+        + [_P, _P, _I, _P, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I]
+        + [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P],
+        _I,
+    ),
     "ttt_mlp_fwd": (
         [_I] * 8
         + [_P, _P, _I, _P, _P, _P, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I]

@@ -11,6 +11,8 @@
 // This is the general path (any CS, F with the shared-memory budget): fp32 FMA math on
 // shared-memory tiles. The inner state W (F x F fp32) stays in shared memory for the
 // whole sequence.
+#include <mutex>
+
 #include "capi_common.cuh"
 #include "common.cuh"
 #include "fast_paths.cuh"
@@ -356,4 +358,80 @@ extern "C" int ttt_linear_bwd(int B, int NH, int NC, int CS, int F, int checkpoi
   if (rc) return rc;
   linear_bwd_kernel<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
   return check_launch("ttt_linear_bwd");
+}
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free backward. Some callers cannot allocate device memory where they enqueue
+// work: an inference-engine plugin's enqueue callback that is only handed pre-sized
+// buffers, or a service that fixes its whole device-memory budget at start-up. For them,
+// the checkpoint-recompute backward can take its scratch from a fixed array compiled into
+// this library instead of a caller buffer. Every GPU that loads the library holds this
+// array until the process exits.
+namespace ttt {
+constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;  // 16 MiB per device
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device.
+static int noalloc_scratch(float** out) {
+  constexpr int kMaxDevices = 64;
+  static float* addr[kMaxDevices] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(TTT_ERR_CUDA, "ttt_linear_bwd_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(TTT_ERR_UNSUPPORTED, "ttt_linear_bwd_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return fail(TTT_ERR_CUDA, "ttt_linear_bwd_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return TTT_OK;
+}
+}  // namespace ttt
+
+extern "C" int ttt_linear_bwd_noalloc(int B, int NH, int NC, int CS, int F, int checkpoint_group_size,
+                                      const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
+                                      const float* W1_ckpt, const float* b1_ckpt, const void* XQ, int dt_xq,
+                                      const void* XV, int dt_xv, const void* XK, int dt_xk, const void* eta,
+                                      int dt_eta, const void* dXQW, int dt_dout, float* d_ln_w, float* d_ln_b,
+                                      float* dW1, float* db1, void* dXQ, void* dXV, void* dXK, void* d_eta,
+                                      int dt_grad, void* stream) {
+  int rc = check_common(B, NH, NC, CS, F, checkpoint_group_size);
+  if (rc) return rc;
+  TTT_REQUIRE(ttt_norm_weight && ttt_norm_bias && W1_ckpt && b1_ckpt && XQ && XV && XK && eta && dXQW && d_ln_w &&
+                  d_ln_b && dW1 && db1 && dXQ && dXV && dXK && d_eta,
+              TTT_ERR_NULL, "ttt_linear_bwd_noalloc: NULL pointer argument");
+  TTT_REQUIRE(valid_dtype(dt_ln) && valid_dtype(dt_xq) && valid_dtype(dt_xv) && valid_dtype(dt_xk) &&
+                  valid_dtype(dt_eta) && valid_dtype(dt_dout) && valid_dtype(dt_grad),
+              TTT_ERR_DTYPE, "ttt_linear_bwd_noalloc: unknown dtype code");
+  const size_t need = ttt_linear_bwd_scratch_bytes(B, NH, NC, CS, F, checkpoint_group_size);
+  TTT_REQUIRE(need <= kNoAllocScratchBytes, TTT_ERR_SCRATCH,
+              "ttt_linear_bwd_noalloc: these sizes need %zu bytes of scratch, the library's fixed scratch holds %zu "
+              "(use ttt_linear_bwd with a caller buffer)",
+              need, kNoAllocScratchBytes);
+  float* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  LinBwdParams p;
+  p.B = B; p.NH = NH; p.NC = NC; p.CS = CS; p.F = F;
+  p.ckpt = checkpoint_group_size < NC ? checkpoint_group_size : NC;
+  p.K = (NC + p.ckpt - 1) / p.ckpt;
+  p.ln_w = ttt_norm_weight; p.ln_b = ttt_norm_bias; p.dt_ln = dt_ln;
+  p.W_ckpt = W1_ckpt; p.b_ckpt = b1_ckpt;
+  p.XQ = XQ; p.XV = XV; p.XK = XK; p.eta = eta;
+  p.dt_xq = dt_xq; p.dt_xv = dt_xv; p.dt_xk = dt_xk; p.dt_eta = dt_eta;
+  p.dout = dXQW; p.dt_dout = dt_dout;
+  p.d_ln_w = d_ln_w; p.d_ln_b = d_ln_b; p.dW = dW1; p.db = db1;
+  p.dXQ = dXQ; p.dXV = dXV; p.dXK = dXK; p.deta = d_eta; p.dt_grad = dt_grad;
+  p.scratch = scratch;
+  p.Z_saved = nullptr; p.W_last = nullptr; p.b_last = nullptr;
+  const size_t smem = linear_bwd_smem(CS, F);
+  rc = prepare_smem(linear_bwd_kernel, smem, "ttt_linear_bwd_noalloc");
+  if (rc) return rc;
+  linear_bwd_kernel<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
+  return check_launch("ttt_linear_bwd_noalloc");
 }
