@@ -45,6 +45,14 @@ WORKLOADS = {
 }
 CS = 16
 DT = {"f32": torch.float32, "bf16": torch.bfloat16}
+# DRAM bytes (read + write) of one launch of the dominant kernel from an ncu capture of
+# the same workload: (bytes, tokens in that launch, summary file). Scaled to the
+# launch measured here by tokens processed.
+NCU_TRAFFIC = {
+    ("mlp_fwd_c1", "mlp_fwd"): (235.5e6, 16 * 12 * 2048, "profiles/mlp_fwd_tc_config1.md"),
+    ("linear_fwd_c2", "linear_fwd"): (557.6e6, 32 * 8 * 4096, "profiles/linear_fwd_tc_config2.md"),
+    ("linear_fwdbwd_c2", "linear_bwd"): (1252.9e6, 32 * 8 * 4096, "profiles/linear_bwd_tc_config2.md"),
+}
 METRIC = "TTT tokens/s (B*H*L) fwd & fwd+bwd at 1/2/4/8 B200; % of HBM roofline"
 
 
@@ -59,20 +67,25 @@ def peaks():
 
 
 def algorithmic(w):
-    """Compulsory bytes and useful FLOPs per token (one (b, h, t))."""
+    """Compulsory bytes and useful FLOPs per token (one (b, h, t)) for each pass.
+
+    Bytes: the forward reads XQ, XK, XV and one eta row and writes XQW; the backward
+    re-reads those inputs, reads dXQW and writes dXQ, dXK, dXV and one eta row of d_eta.
+    Inner state, checkpoints, memo states and the stored pre-activations are excluded.
+    FLOPs: 2 * (multiply-adds) of the dual-form products of ops/ttt_linear.py:8-54 /
+    ops/ttt_mlp.py:9-67 and of their hand-derived backward (reverse walk over stored Z).
+    """
     F, FF = w["F"], w["FF"]
     eb = 4 if w["dtype"] == "f32" else 2
-    fwd_elems = 3 * F + CS + F  # read XQ, XK, XV, eta row; write XQW
-    bwd_elems = (3 * F + CS) + F + (3 * F + CS)  # re-read inputs, read dXQW, write dXQ/dXK/dXV/deta
-    nbytes = eb * (fwd_elems + (bwd_elems if w["bwd"] else 0))
+    fwd_bytes = eb * (3 * F + CS + F)
+    bwd_bytes = eb * ((3 * F + CS) + F + (3 * F + CS))
     if w["kind"] == "linear":
         fwd_flops = 6 * F * F + 4 * CS * F
-        bwd_flops = 2 * fwd_flops + 16 * F * F + 8 * CS * F  # group re-forward + reverse step products
+        bwd_flops = 16 * F * F + 12 * CS * F
     else:
         fwd_flops = 14 * F * FF + 4 * CS * F + 4 * CS * FF
-        bwd_flops = 2 * fwd_flops + 22 * F * FF + 8 * CS * FF + 8 * CS * F
-    flops = fwd_flops + (bwd_flops if w["bwd"] else 0)
-    return nbytes, flops
+        bwd_flops = 38 * F * FF + 12 * CS * FF + 12 * CS * F
+    return {"fwd": (fwd_bytes, fwd_flops), "bwd": (bwd_bytes, bwd_flops)}
 
 
 # --------------------------------------------------------------------------- inputs / steps
@@ -298,21 +311,33 @@ def run_ours(args, w, rank, world, local_rank):
     ms_step = ms / args.steps
     value = world * tokens_rank / (ms_step / 1e3)
     hbm, bf16, bf16_sus, src = peaks()
-    nbytes_tok, flops_tok = algorithmic(w)
+    alg = algorithmic(w)
+    dom = "bwd" if w["bwd"] else "fwd"  # dominant kernel: the backward when there is one
+    dom_bytes, dom_flops = alg[dom]
     dom_ms = kern_ms
     if w["kind"] == "mlp":
-        achieved = flops_tok * tokens_rank / (dom_ms / 1e3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
-                "traffic": None, "peak_source": src}
+        achieved = dom_flops * tokens_rank / (dom_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16}
     else:
-        achieved = nbytes_tok * tokens_rank / (dom_ms / 1e3) / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": None, "peak_source": src}
-    roof["kernel"] = ("linear" if w["kind"] == "linear" else "mlp") + ("_bwd_kernel" if w["bwd"] else "_fwd_kernel")
-    roof["kernel_ms"] = dom_ms
-    roof["hbm_roofline_tokens_per_s"] = hbm * 1e9 / nbytes_tok
-    roof["hbm_frac"] = (tokens_rank / (ms_step / 1e3)) / roof["hbm_roofline_tokens_per_s"]
-    roof["tensor_roofline_tokens_per_s"] = bf16 * 1e12 / flops_tok
+        achieved = dom_bytes * tokens_rank / (dom_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm}
+    kname = ("linear" if w["kind"] == "linear" else "mlp") + "_" + dom
+    traffic = NCU_TRAFFIC.get((args.workload, kname))
+    roof.update({
+        "traffic": traffic[0] * (tokens_rank / traffic[1]) if traffic else None,
+        "traffic_source": traffic[2] if traffic else None,
+        "peak_source": src,
+        "kernel": kname,
+        "kernel_ms": dom_ms,
+        "algorithmic_bytes_per_token": dom_bytes,
+        "algorithmic_flops_per_token": dom_flops,
+    })
+    step_bytes = alg["fwd"][0] + (alg["bwd"][0] if w["bwd"] else 0)
+    step_flops = alg["fwd"][1] + (alg["bwd"][1] if w["bwd"] else 0)
+    roof["hbm_roofline_tokens_per_s"] = hbm * 1e9 / step_bytes
+    roof["hbm_frac_of_step"] = (tokens_rank / (ms_step / 1e3)) / roof["hbm_roofline_tokens_per_s"]
+    roof["tensor_roofline_tokens_per_s"] = bf16 * 1e12 / step_flops
+    roof["tensor_frac_of_step"] = (tokens_rank / (ms_step / 1e3)) / roof["tensor_roofline_tokens_per_s"]
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",

@@ -46,14 +46,32 @@ __device__ __forceinline__ float tanh_fast(float x) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-__device__ __forceinline__ float gelu_fast(float x) {
-  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  return 0.5f * x * (1.f + tanh_fast(k0 * (x + k1 * x * x * x)));
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+
+// gelu (F.gelu approximate="tanh") of a pair, on Blackwell's paired fp32 pipe.
+__device__ __forceinline__ float2 gelu2(float2 x) {
+  const float2 u = __fmul2_rn(x, x);
+  const float2 a = __ffma2_rn(f2(0.044715f), u, f2(1.f));
+  const float2 arg = __fmul2_rn(f2(0.7978845608f), __fmul2_rn(x, a));
+  const float2 t = make_float2(tanh_fast(arg.x), tanh_fast(arg.y));
+  const float2 hx = __fmul2_rn(f2(0.5f), x);
+  return __ffma2_rn(hx, t, hx);
 }
-// the reference's gelu_bwd (ops/ttt_utils.py:51-54) with the hardware tanh
-__device__ __forceinline__ float gelu_bwd_fast(float x) {
-  const float t = tanh_fast(0.79788456f * x * (1.f + 0.044715f * x * x));
-  return 0.5f * x * ((1.f - t * t) * (0.79788456f + 0.1070322243f * x * x)) + 0.5f * (1.f + t);
+
+// gelu and the reference's gelu_bwd (ops/ttt_utils.py:51-54) of a pair, sharing one tanh:
+// their tanh arguments differ only in the 10th digit of sqrt(2/pi), far below the
+// hardware tanh's error.
+__device__ __forceinline__ void gelu2_and_bwd(float2 x, float2& g, float2& gp) {
+  const float2 u = __fmul2_rn(x, x);
+  const float2 a = __ffma2_rn(f2(0.044715f), u, f2(1.f));
+  const float2 arg = __fmul2_rn(f2(0.7978845608f), __fmul2_rn(x, a));
+  const float2 t = make_float2(tanh_fast(arg.x), tanh_fast(arg.y));
+  const float2 hx = __fmul2_rn(f2(0.5f), x);
+  g = __ffma2_rn(hx, t, hx);
+  const float2 poly = __ffma2_rn(f2(0.1070322243f), u, f2(0.79788456f));
+  const float2 omt2 = __ffma2_rn(make_float2(-t.x, -t.y), t, f2(1.f));
+  const float2 base = __ffma2_rn(f2(0.5f), t, f2(0.5f));
+  gp = __ffma2_rn(__fmul2_rn(hx, omt2), poly, base);
 }
 
 __device__ __forceinline__ void load_stage(uint8_t* st, const MlpFwdParams& p, long long s, int n) {
@@ -249,15 +267,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 bb = *reinterpret_cast<const float2*>(b1s + fb + 8 * j + 2 * t);
-      const float z0 = Z1[j][0] + bb.x, z1 = Z1[j][1] + bb.y, z2 = Z1[j][2] + bb.x, z3 = Z1[j][3] + bb.y;
+      const float2 z01 = __fadd2_rn(make_float2(Z1[j][0], Z1[j][1]), bb);
+      const float2 z23 = __fadd2_rn(make_float2(Z1[j][2], Z1[j][3]), bb);
       Zq[j][0] += bb.x;
       Zq[j][1] += bb.y;
       Zq[j][2] += bb.x;
       Zq[j][3] += bb.y;
-      X2p[j][0] = H::pack(gelu_fast(z0), gelu_fast(z1));
-      X2p[j][1] = H::pack(gelu_fast(z2), gelu_fast(z3));
-      GPp[j][0] = H::pack(gelu_bwd_fast(z0), gelu_bwd_fast(z1));
-      GPp[j][1] = H::pack(gelu_bwd_fast(z2), gelu_bwd_fast(z3));
+      float2 g01, g23, d01, d23;
+      gelu2_and_bwd(z01, g01, d01);
+      gelu2_and_bwd(z23, g23, d23);
+      X2p[j][0] = H::pack(g01.x, g01.y);
+      X2p[j][1] = H::pack(g23.x, g23.y);
+      GPp[j][0] = H::pack(d01.x, d01.y);
+      GPp[j][1] = H::pack(d23.x, d23.y);
     }
     // partial Z2_w = X2_w W2_w  (B operand of W2 = accumulator layout of W2^T)
 #pragma unroll
@@ -380,8 +402,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p)
       for (int j = 0; j < 4; ++j) {
         const uint32_t b[2] = {ub[0][j], ub[1][j]};
         mma16816<T>(Zq[j], ap, b);
-        XBp[j][0] = H::pack(gelu_fast(Zq[j][0]), gelu_fast(Zq[j][1]));
-        XBp[j][1] = H::pack(gelu_fast(Zq[j][2]), gelu_fast(Zq[j][3]));
+        const float2 g01 = gelu2(make_float2(Zq[j][0], Zq[j][1])), g23 = gelu2(make_float2(Zq[j][2], Zq[j][3]));
+        XBp[j][0] = H::pack(g01.x, g01.y);
+        XBp[j][1] = H::pack(g23.x, g23.y);
       }
     }
     // A2_w = X2bar_w X2_w^T ; a = -(eta * (A2_w [+1 on warp 0]))
