@@ -23,6 +23,7 @@
 #include "fast_paths.cuh"
 #include "mma.cuh"
 #include "params.cuh"
+#include "tmem.cuh"
 
 namespace ttt {
 namespace mlp_tc {
@@ -40,6 +41,7 @@ constexpr int OFF_P = OFF_EG + TILE;                    // 16-bit [C][C]: -P1
 constexpr int OFF_B1 = OFF_P + ETA;                     // fp32 [FF]
 constexpr int OFF_B2 = OFF_B1 + FF * 4;                 // fp32 [2][F] (ping-pong)
 constexpr int SMEM = OFF_B2 + 2 * F * 4;
+constexpr uint32_t TMEM_COLS = 256;  // W1^T and W2^T slices of 8 warps: 2 x 128 columns
 
 __device__ __forceinline__ float tanh_fast(float x) {
   float y;
@@ -128,8 +130,7 @@ __device__ __forceinline__ void sum_partials(const float* part, int tk, int q, f
 }
 
 // State slices <-> global [F][FF] (W1) and [FF][F] (W2) layouts.
-__device__ __forceinline__ void state_io(float (*S1)[8][4], float (*S2)[4][4], float* W1, float* W2, int fb, int g,
-                                         int t, bool store) {
+__device__ __forceinline__ void w1_io(float (*S1)[8][4], float* W1, int fb, int g, int t, bool store) {
 #pragma unroll
   for (int m = 0; m < 2; ++m)
 #pragma unroll
@@ -148,6 +149,8 @@ __device__ __forceinline__ void state_io(float (*S1)[8][4], float (*S2)[4][4], f
         S1[m][nf][3] = p0[FF + 8];
       }
     }
+}
+__device__ __forceinline__ void w2_io(float (*S2)[4][4], float* W2, int fb, int g, int t, bool store) {
 #pragma unroll
   for (int m = 0; m < 4; ++m)
 #pragma unroll
@@ -168,10 +171,23 @@ __device__ __forceinline__ void state_io(float (*S1)[8][4], float (*S2)[4][4], f
     }
 }
 
+// A warp's 64-value state slice <-> its 64 TMEM columns (two 32-column loads / stores).
+__device__ __forceinline__ void slice_ld(uint32_t a, float* v) {
+  tmem_ld32(a, v);
+  tmem_ld32(a + 32, v + 32);
+  tmem_wait_ld();
+}
+__device__ __forceinline__ void slice_st(uint32_t a, const float* v) {
+  tmem_st32(a, v);
+  tmem_st32(a + 32, v + 32);
+  tmem_wait_st();
+}
+
 template <typename T>
-__global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p) {
+__global__ void __launch_bounds__(NTHREADS, 2) mlp_fwd_tc_kernel(MlpFwdParams p) {
   using H = Half2<T>;
   extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint32_t tmem_base_sh;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int mi = lane >> 3, r8 = lane & 7;
   const long long s = blockIdx.x;
@@ -183,9 +199,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p)
   float* b1s = reinterpret_cast<float*>(smem + OFF_B1);
   float* b2s = reinterpret_cast<float*>(smem + OFF_B2);
 
-  float S1[2][8][4], S2[4][4][4];
-  state_io(S1, S2, const_cast<float*>(p.W1_init + s * F * FF), const_cast<float*>(p.W2_init + s * FF * F), fb, g, t,
-           false);
+  // fp32 state slices live in TMEM: warp w uses lanes 32*(w%4).. and columns
+  // [128*(w/4), +64) for W1^T, [+64, +128) for W2^T.
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_sh, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tS1 = tmem_lane_addr(tmem_base_sh, warp, 128 * (warp >> 2));
+  const uint32_t tS2 = tS1 + 64;
+  {
+    float S1[2][8][4], S2[4][4][4];
+    w1_io(S1, const_cast<float*>(p.W1_init + s * F * FF), fb, g, t, false);
+    w2_io(S2, const_cast<float*>(p.W2_init + s * FF * F), fb, g, t, false);
+    slice_st(tS1, &S1[0][0][0]);
+    slice_st(tS2, &S2[0][0][0]);
+  }
   for (int i = tid; i < FF; i += NTHREADS) b1s[i] = p.b1_init[s * FF + i];
   for (int i = tid; i < F; i += NTHREADS) b2s[i] = p.b2_init[s * F + i];
   float gm[4], bt[4];
@@ -219,7 +250,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p)
 
     if (p.W1_ckpt && ck_left == 0) {  // state at the start of the checkpoint group
       const long long k = s * p.K + n / p.ckpt;
-      state_io(S1, S2, p.W1_ckpt + k * F * FF, p.W2_ckpt + k * FF * F, fb, g, t, true);
+      float S1[2][8][4], S2[4][4][4];
+      slice_ld(tS1, &S1[0][0][0]);
+      w1_io(S1, p.W1_ckpt + k * F * FF, fb, g, t, true);
+      slice_ld(tS2, &S2[0][0][0]);
+      w2_io(S2, p.W2_ckpt + k * FF * F, fb, g, t, true);
       for (int i = tid; i < FF; i += NTHREADS) p.b1_ckpt[k * FF + i] = b1s[i];
       for (int i = tid; i < F; i += NTHREADS) p.b2_ckpt[k * F + i] = b2_old[i];
       ck_left = p.ckpt;
@@ -227,74 +262,83 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p)
     --ck_left;
 
     // ---------------- A: Z1 = XK W1 + b1, Z1q = XQ W1 + b1 (warp's 32 hidden units)
-    float Z1[4][4], Zq[4][4];
+    float Zq[4][4];
+    uint32_t X2p[4][2], GPp[4][2];  // gelu(Z1) and gelu_bwd(Z1), 16-bit pairs in C layout
+    {
+      float S1[2][8][4];
+      slice_ld(tS1, &S1[0][0][0]);
+      float Z1[4][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) Z1[j][c] = Zq[j][c] = 0.f;
-    float A1[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c = 0; c < 4; ++c) Z1[j][c] = Zq[j][c] = 0.f;
+      float A1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t ak[4], aq[4];
-      const uint32_t aoff = swz128((mi & 1) * 8 + r8, 2 * kk + (mi >> 1));
-      ldsm_x4(ak, sb + OFF_XK + aoff);
-      ldsm_x4(aq, sb + OFF_XQ + aoff);
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t ak[4], aq[4];
+        const uint32_t aoff = swz128((mi & 1) * 8 + r8, 2 * kk + (mi >> 1));
+        ldsm_x4(ak, sb + OFF_XK + aoff);
+        ldsm_x4(aq, sb + OFF_XQ + aoff);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int m = j >> 1, hh = 2 * (j & 1);
-        const uint32_t b[2] = {H::pack(S1[m][2 * kk][hh], S1[m][2 * kk][hh + 1]),
-                               H::pack(S1[m][2 * kk + 1][hh], S1[m][2 * kk + 1][hh + 1])};
-        mma16816<T>(Z1[j], ak, b);
-        mma16816<T>(Zq[j], aq, b);
+        for (int j = 0; j < 4; ++j) {
+          const int m = j >> 1, hh = 2 * (j & 1);
+          const uint32_t b[2] = {H::pack(S1[m][2 * kk][hh], S1[m][2 * kk][hh + 1]),
+                                 H::pack(S1[m][2 * kk + 1][hh], S1[m][2 * kk + 1][hh + 1])};
+          mma16816<T>(Z1[j], ak, b);
+          mma16816<T>(Zq[j], aq, b);
+        }
+        if (warp < 2) {
+          uint32_t bk[2];
+          ldsm_x2(bk, sb + OFF_XK + swz128(8 * warp + r8, 2 * kk + (mi & 1)));
+          mma16816<T>(A1, aq, bk);
+        }
       }
       if (warp < 2) {
-        uint32_t bk[2];
-        ldsm_x2(bk, sb + OFF_XK + swz128(8 * warp + r8, 2 * kk + (mi & 1)));
-        mma16816<T>(A1, aq, bk);
+        const int j0 = 8 * warp + 2 * t;
+        const T* E = reinterpret_cast<const T*>(st + OFF_ETA);
+        const float2 e_lo = H::unpack(*reinterpret_cast<const uint32_t*>(E + g * C + j0));
+        const float2 e_hi = H::unpack(*reinterpret_cast<const uint32_t*>(E + (g + 8) * C + j0));
+        *reinterpret_cast<uint32_t*>(smem + OFF_P + (g * C + j0) * 2) =
+            H::pack(-e_lo.x * (A1[0] + 1.f), -e_lo.y * (A1[1] + 1.f));
+        *reinterpret_cast<uint32_t*>(smem + OFF_P + ((g + 8) * C + j0) * 2) =
+            H::pack(-e_hi.x * (A1[2] + 1.f), -e_hi.y * (A1[3] + 1.f));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 bb = *reinterpret_cast<const float2*>(b1s + fb + 8 * j + 2 * t);
+        const float2 z01 = __fadd2_rn(make_float2(Z1[j][0], Z1[j][1]), bb);
+        const float2 z23 = __fadd2_rn(make_float2(Z1[j][2], Z1[j][3]), bb);
+        Zq[j][0] += bb.x;
+        Zq[j][1] += bb.y;
+        Zq[j][2] += bb.x;
+        Zq[j][3] += bb.y;
+        float2 g01, g23, d01, d23;
+        gelu2_and_bwd(z01, g01, d01);
+        gelu2_and_bwd(z23, g23, d23);
+        X2p[j][0] = H::pack(g01.x, g01.y);
+        X2p[j][1] = H::pack(g23.x, g23.y);
+        GPp[j][0] = H::pack(d01.x, d01.y);
+        GPp[j][1] = H::pack(d23.x, d23.y);
       }
     }
-    if (warp < 2) {
-      const int j0 = 8 * warp + 2 * t;
-      const T* E = reinterpret_cast<const T*>(st + OFF_ETA);
-      const float2 e_lo = H::unpack(*reinterpret_cast<const uint32_t*>(E + g * C + j0));
-      const float2 e_hi = H::unpack(*reinterpret_cast<const uint32_t*>(E + (g + 8) * C + j0));
-      *reinterpret_cast<uint32_t*>(smem + OFF_P + (g * C + j0) * 2) =
-          H::pack(-e_lo.x * (A1[0] + 1.f), -e_lo.y * (A1[1] + 1.f));
-      *reinterpret_cast<uint32_t*>(smem + OFF_P + ((g + 8) * C + j0) * 2) =
-          H::pack(-e_hi.x * (A1[2] + 1.f), -e_hi.y * (A1[3] + 1.f));
-    }
-    uint32_t X2p[4][2], GPp[4][2];  // gelu(Z1) and gelu_bwd(Z1), 16-bit pairs in C layout
+    {
+      // partial Z2_w = X2_w W2_w  (B operand of W2 = accumulator layout of W2^T)
+      float S2[4][4][4];
+      slice_ld(tS2, &S2[0][0][0]);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 bb = *reinterpret_cast<const float2*>(b1s + fb + 8 * j + 2 * t);
-      const float2 z01 = __fadd2_rn(make_float2(Z1[j][0], Z1[j][1]), bb);
-      const float2 z23 = __fadd2_rn(make_float2(Z1[j][2], Z1[j][3]), bb);
-      Zq[j][0] += bb.x;
-      Zq[j][1] += bb.y;
-      Zq[j][2] += bb.x;
-      Zq[j][3] += bb.y;
-      float2 g01, g23, d01, d23;
-      gelu2_and_bwd(z01, g01, d01);
-      gelu2_and_bwd(z23, g23, d23);
-      X2p[j][0] = H::pack(g01.x, g01.y);
-      X2p[j][1] = H::pack(g23.x, g23.y);
-      GPp[j][0] = H::pack(d01.x, d01.y);
-      GPp[j][1] = H::pack(d23.x, d23.y);
-    }
-    // partial Z2_w = X2_w W2_w  (B operand of W2 = accumulator layout of W2^T)
+      for (int nf = 0; nf < 8; ++nf) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const int m = nf >> 1, hh = 2 * (nf & 1);
 #pragma unroll
-    for (int nf = 0; nf < 8; ++nf) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      const int m = nf >> 1, hh = 2 * (nf & 1);
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        const uint32_t a[4] = {X2p[2 * ks][0], X2p[2 * ks][1], X2p[2 * ks + 1][0], X2p[2 * ks + 1][1]};
-        const uint32_t b[2] = {H::pack(S2[m][2 * ks][hh], S2[m][2 * ks][hh + 1]),
-                               H::pack(S2[m][2 * ks + 1][hh], S2[m][2 * ks + 1][hh + 1])};
-        mma16816<T>(acc, a, b);
+        for (int ks = 0; ks < 2; ++ks) {
+          const uint32_t a[4] = {X2p[2 * ks][0], X2p[2 * ks][1], X2p[2 * ks + 1][0], X2p[2 * ks + 1][1]};
+          const uint32_t b[2] = {H::pack(S2[m][2 * ks][hh], S2[m][2 * ks][hh + 1]),
+                                 H::pack(S2[m][2 * ks + 1][hh], S2[m][2 * ks + 1][hh + 1])};
+          mma16816<T>(acc, a, b);
+        }
+        *reinterpret_cast<float2*>(pw + g * PLD + 8 * nf + 2 * t) = make_float2(acc[0], acc[1]);
+        *reinterpret_cast<float2*>(pw + (g + 8) * PLD + 8 * nf + 2 * t) = make_float2(acc[2], acc[3]);
       }
-      *reinterpret_cast<float2*>(pw + g * PLD + 8 * nf + 2 * t) = make_float2(acc[0], acc[1]);
-      *reinterpret_cast<float2*>(pw + (g + 8) * PLD + 8 * nf + 2 * t) = make_float2(acc[2], acc[3]);
     }
     __syncthreads();
 
@@ -347,15 +391,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p)
       float Hh[4][4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) Hh[j][0] = Hh[j][1] = Hh[j][2] = Hh[j][3] = 0.f;
+      {
+        float S2[4][4][4];
+        slice_ld(tS2, &S2[0][0][0]);
 #pragma unroll
-      for (int kf = 0; kf < 4; ++kf) {
-        uint32_t ag[4];
-        ldsm_x4(ag, gb + swz128((mi & 1) * 8 + r8, 2 * kf + (mi >> 1)));
+        for (int kf = 0; kf < 4; ++kf) {
+          uint32_t ag[4];
+          ldsm_x4(ag, gb + swz128((mi & 1) * 8 + r8, 2 * kf + (mi >> 1)));
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t b[2] = {movm_t(H::pack(S2[kf][j][0], S2[kf][j][1])),
-                                 movm_t(H::pack(S2[kf][j][2], S2[kf][j][3]))};
-          mma16816<T>(Hh[j], ag, b);
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t b[2] = {movm_t(H::pack(S2[kf][j][0], S2[kf][j][1])),
+                                   movm_t(H::pack(S2[kf][j][2], S2[kf][j][3]))};
+            mma16816<T>(Hh[j], ag, b);
+          }
         }
       }
       const T* E = reinterpret_cast<const T*>(st + OFF_ETA);
@@ -371,16 +419,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p)
       }
     }
     // W1^T += (-e G1)^T XK ; b1 += 1^T (-e G1)
+    {
+      float S1[2][8][4];
+      slice_ld(tS1, &S1[0][0][0]);
 #pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      uint32_t bx[4];
-      ldsm_x4_t(bx, sb + OFF_XK + swz128((mi & 1) * 8 + r8, 2 * np + (mi >> 1)));
+      for (int np = 0; np < 4; ++np) {
+        uint32_t bx[4];
+        ldsm_x4_t(bx, sb + OFF_XK + swz128((mi & 1) * 8 + r8, 2 * np + (mi >> 1)));
 #pragma unroll
-      for (int m = 0; m < 2; ++m) {
-        const uint32_t a[4] = {eb[0][2 * m], eb[0][2 * m + 1], eb[1][2 * m], eb[1][2 * m + 1]};
-        mma16816<T>(S1[m][2 * np], a, bx);
-        mma16816<T>(S1[m][2 * np + 1], a, bx + 2);
+        for (int m = 0; m < 2; ++m) {
+          const uint32_t a[4] = {eb[0][2 * m], eb[0][2 * m + 1], eb[1][2 * m], eb[1][2 * m + 1]};
+          mma16816<T>(S1[m][2 * np], a, bx);
+          mma16816<T>(S1[m][2 * np + 1], a, bx + 2);
+        }
       }
+      slice_st(tS1, &S1[0][0][0]);
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -438,29 +491,31 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p)
       aA2[2] = H::pack(v[1][0], v[1][1]);
       aA2[3] = H::pack(v[1][2], v[1][3]);
     }
-    // partial Z2bar_w = X2bar_w W2_w + aA2 G2  -> shared memory
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      uint32_t bg[4];
-      ldsm_x4_t(bg, gb + swz128((mi & 1) * 8 + r8, 2 * np + (mi >> 1)));
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int nf = 2 * np + hf, m = nf >> 1, hh = 2 * (nf & 1);
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        mma16816<T>(acc, aA2, bg + 2 * hf);
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          const uint32_t a[4] = {XBp[2 * ks][0], XBp[2 * ks][1], XBp[2 * ks + 1][0], XBp[2 * ks + 1][1]};
-          const uint32_t b[2] = {H::pack(S2[m][2 * ks][hh], S2[m][2 * ks][hh + 1]),
-                                 H::pack(S2[m][2 * ks + 1][hh], S2[m][2 * ks + 1][hh + 1])};
-          mma16816<T>(acc, a, b);
-        }
-        *reinterpret_cast<float2*>(pw + g * PLD + 8 * nf + 2 * t) = make_float2(acc[0], acc[1]);
-        *reinterpret_cast<float2*>(pw + (g + 8) * PLD + 8 * nf + 2 * t) = make_float2(acc[2], acc[3]);
-      }
-    }
-    // W2^T += (-e G2)^T X2 ; b2_new = b2_old + 1^T (-e G2) (warp w: features 8w..8w+7)
     {
+      float S2[4][4][4];
+      slice_ld(tS2, &S2[0][0][0]);
+      // partial Z2bar_w = X2bar_w W2_w + aA2 G2  -> shared memory (old W2)
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t bg[4];
+        ldsm_x4_t(bg, gb + swz128((mi & 1) * 8 + r8, 2 * np + (mi >> 1)));
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int nf = 2 * np + hf, m = nf >> 1, hh = 2 * (nf & 1);
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+          mma16816<T>(acc, aA2, bg + 2 * hf);
+#pragma unroll
+          for (int ks = 0; ks < 2; ++ks) {
+            const uint32_t a[4] = {XBp[2 * ks][0], XBp[2 * ks][1], XBp[2 * ks + 1][0], XBp[2 * ks + 1][1]};
+            const uint32_t b[2] = {H::pack(S2[m][2 * ks][hh], S2[m][2 * ks][hh + 1]),
+                                   H::pack(S2[m][2 * ks + 1][hh], S2[m][2 * ks + 1][hh + 1])};
+            mma16816<T>(acc, a, b);
+          }
+          *reinterpret_cast<float2*>(pw + g * PLD + 8 * nf + 2 * t) = make_float2(acc[0], acc[1]);
+          *reinterpret_cast<float2*>(pw + (g + 8) * PLD + 8 * nf + 2 * t) = make_float2(acc[2], acc[3]);
+        }
+      }
+      // W2^T += (-e G2)^T X2
       uint32_t bx2[4][2];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -474,6 +529,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p)
 #pragma unroll
         for (int j = 0; j < 4; ++j) mma16816<T>(S2[m][j], a, bx2[j]);
       }
+      slice_st(tS2, &S2[0][0][0]);
+    }
+    {  // b2_new = b2_old + 1^T (-e G2) (warp w: features 8w..8w+7)
       uint32_t bg2[2];
       ldsm_x2_t(bg2, egb + swz128((lane & 8) + r8, warp));
       float db[4] = {0.f, 0.f, 0.f, 0.f};
@@ -513,7 +571,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p)
 
     if (p.W1_memo && memo_left == 0) {  // state after this mini-batch
       const long long m = s * p.NS + n / p.memo;
-      state_io(S1, S2, p.W1_memo + m * F * FF, p.W2_memo + m * FF * F, fb, g, t, true);
+      float S1[2][8][4], S2[4][4][4];
+      slice_ld(tS1, &S1[0][0][0]);
+      w1_io(S1, p.W1_memo + m * F * FF, fb, g, t, true);
+      slice_ld(tS2, &S2[0][0][0]);
+      w2_io(S2, p.W2_memo + m * FF * F, fb, g, t, true);
       for (int i = tid; i < FF; i += NTHREADS) p.b1_memo[m * FF + i] = b1s[i];
       for (int i = tid; i < F; i += NTHREADS) p.b2_memo[m * F + i] = b2_new[i];
       memo_left = p.memo;
@@ -522,10 +584,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_fwd_tc_kernel(MlpFwdParams p)
   }
   cp_async_wait<0>();
   __syncthreads();
-  state_io(S1, S2, p.W1_last + s * F * FF, p.W2_last + s * FF * F, fb, g, t, true);
+  {
+    float S1[2][8][4], S2[4][4][4];
+    slice_ld(tS1, &S1[0][0][0]);
+    w1_io(S1, p.W1_last + s * F * FF, fb, g, t, true);
+    slice_ld(tS2, &S2[0][0][0]);
+    w2_io(S2, p.W2_last + s * FF * F, fb, g, t, true);
+  }
   const float* b2_fin = b2s + (p.NC & 1) * F;
   for (int i = tid; i < FF; i += NTHREADS) p.b1_last[s * FF + i] = b1s[i];
   for (int i = tid; i < F; i += NTHREADS) p.b2_last[s * F + i] = b2_fin[i];
+  // every warp's TMEM accesses are complete (slice_ld / slice_st wait); free the columns
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  if (warp == 0) tmem_dealloc(tmem_base_sh, TMEM_COLS);
 }
 
 }  // namespace mlp_tc
