@@ -302,14 +302,11 @@ def run_ours(args, w, rank, world, local_rank):
     kern_ms = kernel_durations(w, d, dO, args.steps)
     # end-to-end through the public API with host buffers
     e2e_ms, h2d, d2h = e2e_time(w, d, dO, dev, args)
-    if world > 1:
-        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0]), float(t[1])
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], world, dev)
     if rank != 0:
         return
     ms_step = ms / args.steps
-    value = world * tokens_rank / (ms_step / 1e3)
+    value = weak_scaling_value(world, tokens_rank, ms_step)
     hbm, bf16, bf16_sus, src = peaks()
     alg = algorithmic(w)
     dom = "bwd" if w["bwd"] else "fwd"  # dominant kernel: the backward when there is one
@@ -356,6 +353,22 @@ def run_ours(args, w, rank, world, local_rank):
         v, cores, sample = cpu_reference(w)
         line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
     print(json.dumps(line), flush=True)
+
+
+def max_over_ranks(times, world, device):
+    """Each timing is the max over ranks (the slowest rank bounds the job)."""
+    if world == 1:
+        return list(times)
+    import torch.distributed as dist
+
+    t = torch.tensor(list(times), device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t]
+
+
+def weak_scaling_value(world, tokens_per_rank, ms_per_step):
+    """Whole-job tokens/s: every rank processes its own batch of tokens_per_rank."""
+    return world * tokens_per_rank / (ms_per_step / 1e3)
 
 
 def kernel_durations(w, d, dO, steps):

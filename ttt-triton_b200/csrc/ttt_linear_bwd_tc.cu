@@ -120,7 +120,7 @@ __device__ __forceinline__ void direct_afrag(uint32_t* a, const float (*X)[4], f
 }
 
 template <typename T>
-__global__ void __launch_bounds__(NTHREADS) linear_bwd_tc_kernel(LinBwdParams p) {
+__global__ void __launch_bounds__(NTHREADS, 2) linear_bwd_tc_kernel(LinBwdParams p) {
   using H = Half2<T>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
