@@ -118,9 +118,10 @@ def kernel_step(w, d, dO):
                                   Z=Z, W_last=Wl, b_last=bl)
             return 2
         return 1
-    XQW, _, ck, _ = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"], for_backward=w["bwd"])
+    XQW, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"], for_backward=w["bwd"])
     if w["bwd"]:
-        _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"])
+        _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
+                           saved=zs, W1_last=last[0], W2_last=last[2])
         return 2
     return 1
 
@@ -391,9 +392,10 @@ def kernel_durations(w, d, dO, steps):
                 _core.linear_forward(*(d[k] for k in LIN), w["ckpt"], for_backward=False)
         else:
             if w["bwd"]:
-                _, _, ck, _ = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"])
+                _, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"])
                 e0.record(stream)
-                _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"])
+                _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
+                                   saved=zs, W1_last=last[0], W2_last=last[2])
             else:
                 e0.record(stream)
                 _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"], for_backward=False)

@@ -138,6 +138,10 @@ int ttt_linear_bwd_noalloc(int B, int NH, int NC, int CS, int F, int checkpoint_
  * writes the memo states: the state AFTER mini-batch i for every i with
  * i % memo_segment_size == 0 (kernels/mlp_forward.py:193-226). Memo pointers may all be
  * NULL to skip them, and so may the four checkpoint pointers when no backward follows.
+ * Z1_out / Z1b_out ([B, NH, NC, CS, FF]) and Z2_out / Z2b_out ([B, NH, NC, CS, F]),
+ * optional (all or none), receive the fp32 pre-activations of every mini-batch:
+ * Z1 = XK W1 + b1, Z1bar = XQ W1 + b1 - P1 G1 (before its GELU), Z2 = X2 W2 + b2 and
+ * Z2bar = X2bar W2 + b2 - P2 G2; ttt_mlp_bwd uses them to walk the sequence once.
  */
 int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_group_size, int memo_segment_size,
                 const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
@@ -148,6 +152,7 @@ int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_gro
                 float* W1_last, float* b1_last, float* W2_last, float* b2_last,
                 float* W1_ckpt, float* b1_ckpt, float* W2_ckpt, float* b2_ckpt,
                 float* W1_memo, float* b1_memo, float* W2_memo, float* b2_memo,
+                float* Z1_out, float* Z2_out, float* Z1b_out, float* Z2b_out,
                 void* stream);
 
 /* Bytes of scratch ttt_mlp_bwd needs for these sizes. */
@@ -158,6 +163,11 @@ size_t ttt_mlp_bwd_scratch_bytes(int B, int NH, int NC, int CS, int F, int FF, i
  * mlp_triton.py:274-333 (and the F x F one of mlp_triton_back.py:238-293), with the full
  * dual-form gradients of ops/ttt_mlp.py. Outputs as ttt_linear_bwd plus dW2/db2
  * ([B, NH, FF, F], [B, NH, 1, F] fp32); dW1/db1 are [B, NH, F, FF], [B, NH, 1, FF].
+ * Z1_saved .. Z2b_saved (the four ttt_mlp_fwd pre-activation outputs) with W1_last and
+ * W2_last, all set or all NULL, let the tensor-core path (F = 64, FF = 256, CS = 16,
+ * 16-bit activations) walk the sequence once from the end without re-running the
+ * forward; scratch may then be NULL. Otherwise the checkpoints are re-run and scratch
+ * must hold ttt_mlp_bwd_scratch_bytes().
  */
 int ttt_mlp_bwd(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_group_size,
                 const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
@@ -165,6 +175,8 @@ int ttt_mlp_bwd(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_gro
                 const void* XQ, int dt_xq, const void* XV, int dt_xv, const void* XK, int dt_xk,
                 const void* eta, int dt_eta,
                 const void* dXQW, int dt_dout,
+                const float* Z1_saved, const float* Z2_saved, const float* Z1b_saved, const float* Z2b_saved,
+                const float* W1_last, const float* W2_last,
                 float* d_ln_w, float* d_ln_b, float* dW1, float* db1, float* dW2, float* db2,
                 void* dXQ, void* dXV, void* dXK, void* d_eta, int dt_grad,
                 void* scratch, size_t scratch_bytes, void* stream);

@@ -85,3 +85,19 @@ def test_noalloc_backward_rejects_requests_beyond_its_scratch():
     rc = _lib.lib.ttt_linear_bwd_noalloc(64, 64, 16, 16, 64, 16, FAKE, FAKE, 0, FAKE, FAKE, FAKE, 0, FAKE, 0, FAKE,
                                          0, FAKE, 0, FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 0, None)
     assert rc == -5 and "16777216" in _lib.lib.ttt_last_error().decode()
+
+
+def test_mlp_saved_preactivations_all_or_none():
+    P = [FAKE] * 4
+    rc = _lib.lib.ttt_mlp_fwd(1, 1, 2, 16, 64, 256, 1, 1, FAKE, FAKE, 0, *P, FAKE, 1, FAKE, 1, FAKE, 1, FAKE, 1,
+                              FAKE, 1, *P, *P, None, None, None, None, FAKE, None, None, None, None)
+    assert rc == -1 and "pre-activation" in _lib.lib.ttt_last_error().decode()
+
+    def bwd(saved, scratch):
+        return _lib.lib.ttt_mlp_bwd(1, 1, 2, 16, 64, 256, 1, FAKE, FAKE, 0, *P, FAKE, 1, FAKE, 1, FAKE, 1, FAKE, 1,
+                                    FAKE, 1, *saved, *([FAKE] * 10), 1, scratch, 0, None)
+
+    assert bwd([FAKE, None, None, None, None, None], None) == -1
+    assert "all set or all NULL" in _lib.lib.ttt_last_error().decode()
+    # without the saved pre-activations the recompute path needs its scratch buffer
+    assert bwd([None] * 6, None) == -5

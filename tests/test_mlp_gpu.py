@@ -48,7 +48,7 @@ def test_mlp_fwd_bwd_matches_oracle(dtype, shape):
     for i, name in enumerate(("W1", "b1", "W2", "b2")):
         assert memos[i].shape[2] == NS
         assert_close(name + "_memo", memos[i], full[name + "_memo"], tol)
-    XQW, last, ck, _ = _core.mlp_forward(*(d[k] for k in NAMES), ckpt, None)
+    XQW, last, ck, _, _ = _core.mlp_forward(*(d[k] for k in NAMES), ckpt, None)
     for i, name in enumerate(("W1", "b1", "W2", "b2")):
         init = od[name]
         assert_close(name + "_last - init", last[i].double().cpu() - init, full[name + "_last"] - init, tol)
@@ -92,7 +92,7 @@ def test_full_size_config1_sampled_streams():
     re-run through the oracle at full length."""
     B, NH, NC, CS, F, FF = 16, 12, 128, 16, 64, 256
     d = S.make_mlp_inputs(B, NH, NC, CS, F, FF, dtype=torch.bfloat16, device=DEV, seed=0)
-    out, last, _, _ = _core.mlp_forward(*(d[k] for k in NAMES), 16, None, for_backward=False)
+    out, last, _, _, _ = _core.mlp_forward(*(d[k] for k in NAMES), 16, None, for_backward=False)
     torch.cuda.synchronize()
     for b, h in ((0, 0), (7, 5), (15, 11)):
         sub = {k: (v[b:b + 1, h:h + 1] if k not in ("ln_w", "ln_b") else v[h:h + 1]) for k, v in d.items()}
@@ -111,3 +111,53 @@ def test_long_sequence_config3_streams_fwd_bwd():
     assert_close("XQW", out, ref["XQW"], 2e-2)
     for k in NAMES:
         assert_close("d" + k, grads[k], ref_grads[k], 2e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("eta_mode", ["causal", "equal"])
+def test_backward_paths_agree(dtype, eta_mode):
+    """The single reverse walk over the stored pre-activations (tensor-core path) and the
+    checkpoint-group recompute (general path) both match the oracle on the same inputs."""
+    B, NH, NC, CS, F, FF, ckpt = 2, 2, 7, 16, 64, 256, 3
+    d, dO = make(B, NH, NC, CS, F, FF, dtype, seed=31, eta_mode=eta_mode)
+    ref_grads, _ = O.mlp_grads(oracle_inputs(d), dO.double().cpu())
+    _, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in NAMES), ckpt, None)
+    args = (d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, ckpt)
+    walk = _core.mlp_backward(*args, saved=zs, W1_last=last[0], W2_last=last[2])
+    regroup = _core.mlp_backward(*args)
+    names = ("ln_w", "ln_b", "W1", "b1", "W2", "b2", "XQ", "XV", "XK", "eta")
+    for res in (walk, regroup):
+        got = dict(zip(names, res))
+        got["ln_w"], got["ln_b"] = got["ln_w"].sum(0), got["ln_b"].sum(0)
+        for k in names:
+            assert_close("d" + k, got[k], ref_grads[k].reshape(got[k].shape), 2e-2)
+
+
+def test_saved_preactivations_match_oracle():
+    """The forward's stored Z1, Z2, Z1bar, Z2bar equal the oracle's per-mini-batch values."""
+    B, NH, NC, CS, F, FF = 1, 2, 5, 16, 64, 256
+    d, _ = make(B, NH, NC, CS, F, FF, torch.bfloat16, seed=41)
+    _, _, _, _, zs = _core.mlp_forward(*(d[k] for k in NAMES), 2, None)
+    od = oracle_inputs(d)
+    st = [od["W1"], od["b1"], od["W2"], od["b2"]]
+    gamma, beta = od["ln_w"].reshape(NH, 1, F), od["ln_b"].reshape(NH, 1, F)
+    ref = [[], [], [], []]
+    for n in range(NC):
+        XQ, XK, XV, eta = (od[k][:, :, n] for k in ("XQ", "XK", "XV", "eta"))
+        Z1 = XK @ st[0] + st[1]
+        X2 = O.gelu_tanh(Z1)
+        Z2 = X2 @ st[2] + st[3]
+        G2 = O.ln_fused_l2_bwd(Z2, XV - XK, gamma, beta)
+        G1 = (G2 @ st[2].transpose(-1, -2)) * O.gelu_bwd(Z1)
+        P1 = eta * (XQ @ XK.transpose(-1, -2) + 1)
+        Z1b = XQ @ st[0] + st[1] - P1 @ G1
+        X2b = O.gelu_tanh(Z1b)
+        P2 = eta * (X2b @ X2.transpose(-1, -2) + 1)
+        Z2b = X2b @ st[2] + st[3] - P2 @ G2
+        for i, z in enumerate((Z1, Z2, Z1b, Z2b)):
+            ref[i].append(z)
+        e = eta[:, :, -1, :, None]
+        st = [st[0] - (e * XK).transpose(-1, -2) @ G1, st[1] - (e * G1).sum(-2, keepdim=True),
+              st[2] - (e * X2).transpose(-1, -2) @ G2, st[3] - (e * G2).sum(-2, keepdim=True)]
+    for i, name in enumerate(("Z1", "Z2", "Z1bar", "Z2bar")):
+        assert_close(name, zs[i], torch.stack(ref[i], 2), 2e-2)

@@ -135,9 +135,11 @@ def linear_backward(ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, dXQW, checkpoin
 # --------------------------------------------------------------------------- MLP
 def mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, checkpoint_group_size, memo_segment_size=None,
                 for_backward=True):
-    """TTT-MLP scan forward. Returns (XQW, (W1,b1,W2,b2)_last, (…)_ckpt or None, (…)_memo or None).
+    """TTT-MLP scan forward. Returns (XQW, (W1,b1,W2,b2)_last, (…)_ckpt or None, (…)_memo or None,
+    (Z1, Z2, Z1bar, Z2bar) or None).
 
-    Without ``for_backward`` (inference) the checkpoints are not written."""
+    With ``for_backward`` the checkpoints and the fp32 pre-activations of every mini-batch
+    are kept for ``mlp_backward``; without it (inference) neither is written."""
     require_cuda(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta)
     B, NH, NC, CS, F = _check_acts(XQ, XV, XK, eta)
     FF = W1.shape[-1]
@@ -171,6 +173,11 @@ def mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, checkpoint_group_si
         memo = (torch.empty(B, NH, NS, F, FF, **f32), torch.empty(B, NH, NS, 1, FF, **f32),
                 torch.empty(B, NH, NS, FF, F, **f32), torch.empty(B, NH, NS, 1, F, **f32))
     mp = memo if memo is not None else (None, None, None, None)
+    zs = None
+    if for_backward:
+        zs = (torch.empty(B, NH, NC, CS, FF, **f32), torch.empty(B, NH, NC, CS, F, **f32),
+              torch.empty(B, NH, NC, CS, FF, **f32), torch.empty(B, NH, NC, CS, F, **f32))
+    zp = zs if zs is not None else (None, None, None, None)
     rc = lib.ttt_mlp_fwd(
         B, NH, NC, CS, F, FF, ckpt, memo_seg,
         ptr(ln_w), ptr(ln_b), dtype_code(ln_w),
@@ -178,18 +185,28 @@ def mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, checkpoint_group_si
         ptr(XQ), dtype_code(XQ), ptr(XV), dtype_code(XV), ptr(XK), dtype_code(XK),
         ptr(eta), dtype_code(eta),
         ptr(XQW), dtype_code(XQW),
-        *[ptr(t) for t in last], *[ptr(t) for t in cp], *[ptr(t) for t in mp],
+        *[ptr(t) for t in last], *[ptr(t) for t in cp], *[ptr(t) for t in mp], *[ptr(t) for t in zp],
         stream_of(XQ),
     )
     check(rc, "ttt_mlp_fwd")
-    return XQW, last, ck, memo
+    return XQW, last, ck, memo, zs
 
 
-def mlp_backward(ln_w, ln_b, ckpts, XQ, XV, XK, eta, dXQW, checkpoint_group_size, grad_dtype=None):
+def mlp_backward(ln_w, ln_b, ckpts, XQ, XV, XK, eta, dXQW, checkpoint_group_size, grad_dtype=None,
+                 saved=None, W1_last=None, W2_last=None):
     """TTT-MLP scan backward. ckpts = (W1, b1, W2, b2) checkpoints from mlp_forward.
-    Returns (d_ln_w, d_ln_b [B,NH,F] partials, dW1, db1, dW2, db2, dXQ, dXV, dXK, d_eta)."""
+    Returns (d_ln_w, d_ln_b [B,NH,F] partials, dW1, db1, dW2, db2, dXQ, dXV, dXK, d_eta).
+
+    ``saved`` = (Z1, Z2, Z1bar, Z2bar) from ``mlp_forward`` with the final W1 and W2
+    enable the single reverse walk; without them each checkpoint group is re-run forward."""
     W1c, b1c, W2c, b2c = (_c(t) for t in ckpts)
     require_cuda(ln_w, ln_b, W1c, b1c, W2c, b2c, XQ, XV, XK, eta, dXQW)
+    sp = (None,) * 6
+    if saved is not None:
+        if W1_last is None or W2_last is None:
+            raise ValueError("saved pre-activations need W1_last and W2_last")
+        sp = tuple(_c(t) for t in (*saved, W1_last, W2_last))
+        require_cuda(*sp)
     B, NH, NC, CS, F = _check_acts(XQ, XV, XK, eta)
     FF = W1c.shape[-1]
     ckpt = int(checkpoint_group_size)
@@ -219,6 +236,7 @@ def mlp_backward(ln_w, ln_b, ckpts, XQ, XV, XK, eta, dXQW, checkpoint_group_size
         ptr(XQ), dtype_code(XQ), ptr(XV), dtype_code(XV), ptr(XK), dtype_code(XK),
         ptr(eta), dtype_code(eta),
         ptr(dXQW), dtype_code(dXQW),
+        *[ptr(t) for t in sp],
         ptr(d_ln_w), ptr(d_ln_b), ptr(dW1), ptr(db1), ptr(dW2), ptr(db2),
         ptr(dXQ), ptr(dXV), ptr(dXK), ptr(deta), dtype_code(dXQ),
         ptr(scratch), nbytes, stream_of(XQ),

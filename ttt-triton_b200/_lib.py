@@ -44,6 +44,7 @@ _SIGNATURES = {
         [_I] * 8
         + [_P, _P, _I, _P, _P, _P, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I]
         + [_P] * 12
+        + [_P] * 4
         + [_P],
         _I,
     ),
@@ -51,6 +52,7 @@ _SIGNATURES = {
     "ttt_mlp_bwd": (
         [_I] * 7
         + [_P, _P, _I, _P, _P, _P, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I]
+        + [_P] * 6
         + [_P] * 10
         + [_I, _P, _Z, _P],
         _I,

@@ -14,5 +14,6 @@ namespace ttt {
 int linear_fwd_fast(const LinFwdParams& p, cudaStream_t stream);
 int mlp_fwd_fast(const MlpFwdParams& p, cudaStream_t stream);
 int linear_bwd_fast(const LinBwdParams& p, cudaStream_t stream);
+int mlp_bwd_fast(const MlpBwdParams& p, cudaStream_t stream);
 
 }  // namespace ttt

@@ -1,0 +1,73 @@
+// Pieces shared by the tensor-core TTT-MLP kernels (F = 64, FF = 256, CS = 16): the
+// accumulator-fragment layout of a warp's state slices and their TMEM / global copies.
+//
+// Warp w owns hidden units [32w, 32w + 32). Its slice of W1 is held as W1^T (32 x 64,
+// fragments [2][8][4]: hidden rows 16m + g (+8), feature columns 8nf + 2t (+1)), its
+// slice of W2 as W2^T (64 x 32, fragments [4][4][4]: feature rows 16m + g (+8), hidden
+// columns 8j + 2t (+1)). These accumulator layouts are directly the mma B-operand layouts
+// of W1 and W2 (k = feature resp. hidden); movmatrix turns them into those of W1^T, W2^T.
+#pragma once
+
+#include "tmem.cuh"
+
+namespace ttt {
+namespace mlp_tc {
+
+constexpr int F = 64, FF = 256, C = 16;
+
+// State slices <-> global [F][FF] (W1) and [FF][F] (W2) layouts.
+__device__ __forceinline__ void w1_io(float (*S1)[8][4], float* W1, int fb, int g, int t, bool store) {
+#pragma unroll
+  for (int m = 0; m < 2; ++m)
+#pragma unroll
+    for (int nf = 0; nf < 8; ++nf) {
+      const int f = 8 * nf + 2 * t, ff = fb + 16 * m + g;
+      float* p0 = W1 + f * FF + ff;
+      if (store) {
+        p0[0] = S1[m][nf][0];
+        p0[FF] = S1[m][nf][1];
+        p0[8] = S1[m][nf][2];
+        p0[FF + 8] = S1[m][nf][3];
+      } else {
+        S1[m][nf][0] = p0[0];
+        S1[m][nf][1] = p0[FF];
+        S1[m][nf][2] = p0[8];
+        S1[m][nf][3] = p0[FF + 8];
+      }
+    }
+}
+__device__ __forceinline__ void w2_io(float (*S2)[4][4], float* W2, int fb, int g, int t, bool store) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int f = 16 * m + g, ff = fb + 8 * j + 2 * t;
+      float* p0 = W2 + ff * F + f;
+      if (store) {
+        p0[0] = S2[m][j][0];
+        p0[F] = S2[m][j][1];
+        p0[8] = S2[m][j][2];
+        p0[F + 8] = S2[m][j][3];
+      } else {
+        S2[m][j][0] = p0[0];
+        S2[m][j][1] = p0[F];
+        S2[m][j][2] = p0[8];
+        S2[m][j][3] = p0[F + 8];
+      }
+    }
+}
+
+// A warp's 64-value state slice <-> its 64 TMEM columns (two 32-column loads / stores).
+__device__ __forceinline__ void slice_ld(uint32_t a, float* v) {
+  tmem_ld32(a, v);
+  tmem_ld32(a + 32, v + 32);
+  tmem_wait_ld();
+}
+__device__ __forceinline__ void slice_st(uint32_t a, const float* v) {
+  tmem_st32(a, v);
+  tmem_st32(a + 32, v + 32);
+  tmem_wait_st();
+}
+
+}  // namespace mlp_tc
+}  // namespace ttt

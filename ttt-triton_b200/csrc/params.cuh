@@ -81,6 +81,12 @@ struct MlpFwdParams {
   float* b1_memo;
   float* W2_memo;
   float* b2_memo;
+  // optional fp32 pre-activations of every mini-batch, kept for the reverse-walk backward:
+  // Z1 = XK W1 + b1, Z1bar (before its GELU) [B,NH,NC,CS,FF]; Z2 = X2 W2 + b2, Z2bar [B,NH,NC,CS,F]
+  float* Z1_out;
+  float* Z2_out;
+  float* Z1b_out;
+  float* Z2b_out;
 };
 
 struct MlpBwdParams {
@@ -111,6 +117,14 @@ struct MlpBwdParams {
   void* deta;
   int dt_grad;
   float* scratch;  // per stream: W1 [F*FF], W2 [FF*F], Z1/Z2 of one group [ckpt][CS*(FF+F)]
+  // optional: the forward's fp32 pre-activations (ttt_mlp_fwd Z1_out..Z2b_out) and final
+  // weights; with them the tensor-core backward walks the sequence once from the end
+  const float* Z1_saved;
+  const float* Z2_saved;
+  const float* Z1b_saved;
+  const float* Z2b_saved;
+  const float* W1_last;
+  const float* W2_last;
 };
 
 struct ReadoutParams {

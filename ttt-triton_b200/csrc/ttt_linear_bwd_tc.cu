@@ -23,6 +23,7 @@
 #include "fast_paths.cuh"
 #include "mma.cuh"
 #include "params.cuh"
+#include "tc_util.cuh"
 
 namespace ttt {
 namespace lin_bwd_tc {
@@ -71,24 +72,6 @@ __device__ __forceinline__ void load_stage(uint8_t* st, const LinBwdParams& p, l
   cp_async16(smem_u32(st) + OFF_ZS + tid * 16, zsrc);
 }
 
-__device__ __forceinline__ float red16(float v) {
-  v += __shfl_xor_sync(0xffffffffu, v, 1);
-  v += __shfl_xor_sync(0xffffffffu, v, 2);
-  v += __shfl_xor_sync(0xffffffffu, v, 4);
-  v += __shfl_xor_sync(0xffffffffu, v, 8);
-  return v;
-}
-
-template <typename T>
-__device__ __forceinline__ void unpack4(const uint8_t* src, float* v) {
-  const uint2 u = *reinterpret_cast<const uint2*>(src);
-  const float2 a = Half2<T>::unpack(u.x), b = Half2<T>::unpack(u.y);
-  v[0] = a.x;
-  v[1] = a.y;
-  v[2] = b.x;
-  v[3] = b.y;
-}
-
 // 16-bit copy of a warp's accumulator slice (rows f_in, columns 8w..8w+7) into a
 // swizzled [64][64] tile.
 template <typename T>
@@ -98,25 +81,6 @@ __device__ __forceinline__ void store_slice(uint8_t* tile, const float (*X)[4], 
     *reinterpret_cast<uint32_t*>(tile + swz128(16 * mt + g, warp) + 4 * t) = Half2<T>::pack(X[mt][0], X[mt][1]);
     *reinterpret_cast<uint32_t*>(tile + swz128(16 * mt + g + 8, warp) + 4 * t) = Half2<T>::pack(X[mt][2], X[mt][3]);
   }
-}
-
-// -P^T / dA^T style A fragment: transpose of a 16x16 tile held as two C tiles.
-template <typename T>
-__device__ __forceinline__ void transpose_afrag(uint32_t* a, const float (*X)[4], float scale) {
-  using H = Half2<T>;
-  a[0] = movm_t(H::pack(scale * X[0][0], scale * X[0][1]));
-  a[1] = movm_t(H::pack(scale * X[1][0], scale * X[1][1]));
-  a[2] = movm_t(H::pack(scale * X[0][2], scale * X[0][3]));
-  a[3] = movm_t(H::pack(scale * X[1][2], scale * X[1][3]));
-}
-
-template <typename T>
-__device__ __forceinline__ void direct_afrag(uint32_t* a, const float (*X)[4], float scale) {
-  using H = Half2<T>;
-  a[0] = H::pack(scale * X[0][0], scale * X[0][1]);
-  a[1] = H::pack(scale * X[0][2], scale * X[0][3]);
-  a[2] = H::pack(scale * X[1][0], scale * X[1][1]);
-  a[3] = H::pack(scale * X[1][2], scale * X[1][3]);
 }
 
 template <typename T>

@@ -19,6 +19,7 @@
 #include "fast_paths.cuh"
 #include "mma.cuh"
 #include "params.cuh"
+#include "tc_util.cuh"
 
 namespace ttt {
 namespace lin_tc {
@@ -53,25 +54,6 @@ __device__ __forceinline__ void load_stage(uint8_t* st, const LinFwdParams& p, l
       cp_async16(smem_u32(st) + OFF_ETA + i * 16, (const uint8_t*)p.eta + eb + i * 16);
     }
   }
-}
-
-// Sum over the 16 lanes of a half-warp (one token's 64 features, 4 per lane).
-__device__ __forceinline__ float red16(float v) {
-  v += __shfl_xor_sync(0xffffffffu, v, 1);
-  v += __shfl_xor_sync(0xffffffffu, v, 2);
-  v += __shfl_xor_sync(0xffffffffu, v, 4);
-  v += __shfl_xor_sync(0xffffffffu, v, 8);
-  return v;
-}
-
-template <typename T>
-__device__ __forceinline__ void unpack4(const uint8_t* src, float* v) {
-  const uint2 u = *reinterpret_cast<const uint2*>(src);
-  const float2 a = Half2<T>::unpack(u.x), b = Half2<T>::unpack(u.y);
-  v[0] = a.x;
-  v[1] = a.y;
-  v[2] = b.x;
-  v[3] = b.y;
 }
 
 template <typename T>

@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(256) mlp_fwd_kernel(MlpFwdParams p) {
     for (int i = threadIdx.x; i < CFF; i += blockDim.x) {
       const float z = Z1[i] + b1[i % FF];
       Z1[i] = z;
+      if (p.Z1_out) p.Z1_out[(s * p.NC + n) * CFF + i] = z;
       const float x2 = gelu_tanh(z);
       X2[i] = x2;
       X2e[i] = e[i / FF] * x2;
@@ -98,13 +99,18 @@ __global__ void __launch_bounds__(256) mlp_fwd_kernel(MlpFwdParams p) {
     __syncthreads();
     ln_fused_rows(Z2, G2, b2, XV, XK, gam, bet, C, F, nullptr, nullptr);
     __syncthreads();
+    if (p.Z2_out)
+      for (int i = threadIdx.x; i < CF; i += blockDim.x) p.Z2_out[xb + i] = Z2[i];
     block_mm<false, true>(G1, FF, G2, F, W2, F, C, FF, F, 1.f, 0.f);  // H = G2 W2^T
     __syncthreads();
     for (int i = threadIdx.x; i < CFF; i += blockDim.x) G1[i] *= gelu_bwd_ref(Z1[i]);
     __syncthreads();
     block_mm<false, false>(Z1b, FF, P1, C, G1, FF, C, FF, C, -1.f, 1.f);  // Z1b -= P1 G1
     __syncthreads();
-    for (int i = threadIdx.x; i < CFF; i += blockDim.x) Z1b[i] = gelu_tanh(Z1b[i]);  // X2_bar
+    for (int i = threadIdx.x; i < CFF; i += blockDim.x) {
+      if (p.Z1b_out) p.Z1b_out[(s * p.NC + n) * CFF + i] = Z1b[i];
+      Z1b[i] = gelu_tanh(Z1b[i]);  // X2_bar
+    }
     __syncthreads();
     block_mm<false, true>(P2, C, Z1b, FF, X2, FF, C, C, FF, 1.f, 0.f);  // A2 = X2b X2^T
     block_mm<false, false>(Z2b, F, Z1b, FF, W2, F, C, F, FF, 1.f, 0.f);  // Z2b = X2b W2
@@ -114,6 +120,10 @@ __global__ void __launch_bounds__(256) mlp_fwd_kernel(MlpFwdParams p) {
     block_mm<false, false>(Z2b, F, P2, C, G2, F, C, F, C, -1.f, 1.f);  // Z2b -= P2 G2
     __syncthreads();
     readout_ln_store_rows(Z2b, b2, XQ, gam, bet, C, F, kLnEps, p.out, xb, p.dt_out);
+    if (p.Z2b_out) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < CF; i += blockDim.x) p.Z2b_out[xb + i] = Z2b[i];
+    }
     block_mm<true, false>(W1, FF, XKe, F, G1, FF, F, FF, C, -1.f, 1.f);  // W1 -= (e*XK)^T G1
     block_mm<true, false>(W2, F, X2e, FF, G2, F, FF, F, C, -1.f, 1.f);  // W2 -= (e*X2)^T G2
     weighted_colsum(tmp1, e, G1, C, FF);
@@ -490,7 +500,7 @@ extern "C" int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int che
                            const void* eta, int dt_eta, void* XQW, int dt_out, float* W1_last, float* b1_last,
                            float* W2_last, float* b2_last, float* W1_ckpt, float* b1_ckpt, float* W2_ckpt,
                            float* b2_ckpt, float* W1_memo, float* b1_memo, float* W2_memo, float* b2_memo,
-                           void* stream) {
+                           float* Z1_out, float* Z2_out, float* Z1b_out, float* Z2b_out, void* stream) {
   int rc = check_mlp(B, NH, NC, CS, F, FF, checkpoint_group_size);
   if (rc) return rc;
   TTT_REQUIRE(memo_segment_size > 0, TTT_ERR_SHAPE, "memo_segment_size must be positive (got %d)", memo_segment_size);
@@ -518,6 +528,10 @@ extern "C" int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int che
   p.W1_last = W1_last; p.b1_last = b1_last; p.W2_last = W2_last; p.b2_last = b2_last;
   p.W1_ckpt = W1_ckpt; p.b1_ckpt = b1_ckpt; p.W2_ckpt = W2_ckpt; p.b2_ckpt = b2_ckpt;
   p.W1_memo = all_memo ? W1_memo : nullptr; p.b1_memo = b1_memo; p.W2_memo = W2_memo; p.b2_memo = b2_memo;
+  const bool any_z = Z1_out || Z2_out || Z1b_out || Z2b_out;
+  TTT_REQUIRE(!any_z || (Z1_out && Z2_out && Z1b_out && Z2b_out), TTT_ERR_NULL,
+              "ttt_mlp_fwd: the four pre-activation outputs must be all set or all NULL");
+  p.Z1_out = Z1_out; p.Z2_out = Z2_out; p.Z1b_out = Z1b_out; p.Z2b_out = Z2b_out;
   rc = mlp_fwd_fast(p, (cudaStream_t)stream);
   if (rc != TTT_NOT_APPLICABLE) return rc;
   const size_t smem = mlp_fwd_smem(CS, F, FF);
@@ -538,20 +552,22 @@ extern "C" int ttt_mlp_bwd(int B, int NH, int NC, int CS, int F, int FF, int che
                            const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln, const float* W1_ckpt,
                            const float* b1_ckpt, const float* W2_ckpt, const float* b2_ckpt, const void* XQ, int dt_xq,
                            const void* XV, int dt_xv, const void* XK, int dt_xk, const void* eta, int dt_eta,
-                           const void* dXQW, int dt_dout, float* d_ln_w, float* d_ln_b, float* dW1, float* db1,
+                           const void* dXQW, int dt_dout, const float* Z1_saved, const float* Z2_saved,
+                           const float* Z1b_saved, const float* Z2b_saved, const float* W1_last,
+                           const float* W2_last, float* d_ln_w, float* d_ln_b, float* dW1, float* db1,
                            float* dW2, float* db2, void* dXQ, void* dXV, void* dXK, void* d_eta, int dt_grad,
                            void* scratch, size_t scratch_bytes, void* stream) {
   int rc = check_mlp(B, NH, NC, CS, F, FF, checkpoint_group_size);
   if (rc) return rc;
   TTT_REQUIRE(ttt_norm_weight && ttt_norm_bias && W1_ckpt && b1_ckpt && W2_ckpt && b2_ckpt && XQ && XV && XK && eta &&
-                  dXQW && d_ln_w && d_ln_b && dW1 && db1 && dW2 && db2 && dXQ && dXV && dXK && d_eta && scratch,
+                  dXQW && d_ln_w && d_ln_b && dW1 && db1 && dW2 && db2 && dXQ && dXV && dXK && d_eta,
               TTT_ERR_NULL, "ttt_mlp_bwd: NULL pointer argument");
   TTT_REQUIRE(valid_dtype(dt_ln) && valid_dtype(dt_xq) && valid_dtype(dt_xv) && valid_dtype(dt_xk) &&
                   valid_dtype(dt_eta) && valid_dtype(dt_dout) && valid_dtype(dt_grad),
               TTT_ERR_DTYPE, "ttt_mlp_bwd: unknown dtype code");
-  const size_t need = ttt_mlp_bwd_scratch_bytes(B, NH, NC, CS, F, FF, checkpoint_group_size);
-  TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "ttt_mlp_bwd: scratch has %zu bytes, needs %zu", scratch_bytes,
-              need);
+  const bool any_saved = Z1_saved || Z2_saved || Z1b_saved || Z2b_saved || W1_last || W2_last;
+  TTT_REQUIRE(!any_saved || (Z1_saved && Z2_saved && Z1b_saved && Z2b_saved && W1_last && W2_last), TTT_ERR_NULL,
+              "ttt_mlp_bwd: the saved pre-activations and final weights must be all set or all NULL");
   MlpBwdParams p;
   p.B = B; p.NH = NH; p.NC = NC; p.CS = CS; p.F = F; p.FF = FF;
   p.ckpt = checkpoint_group_size < NC ? checkpoint_group_size : NC;
@@ -564,6 +580,13 @@ extern "C" int ttt_mlp_bwd(int B, int NH, int NC, int CS, int F, int FF, int che
   p.d_ln_w = d_ln_w; p.d_ln_b = d_ln_b; p.dW1 = dW1; p.db1 = db1; p.dW2 = dW2; p.db2 = db2;
   p.dXQ = dXQ; p.dXV = dXV; p.dXK = dXK; p.deta = d_eta; p.dt_grad = dt_grad;
   p.scratch = (float*)scratch;
+  p.Z1_saved = Z1_saved; p.Z2_saved = Z2_saved; p.Z1b_saved = Z1b_saved; p.Z2b_saved = Z2b_saved;
+  p.W1_last = W1_last; p.W2_last = W2_last;
+  rc = mlp_bwd_fast(p, (cudaStream_t)stream);
+  if (rc != TTT_NOT_APPLICABLE) return rc;
+  const size_t need = ttt_mlp_bwd_scratch_bytes(B, NH, NC, CS, F, FF, checkpoint_group_size);
+  TTT_REQUIRE(scratch && scratch_bytes >= need, TTT_ERR_SCRATCH, "ttt_mlp_bwd: scratch has %zu bytes, needs %zu",
+              scratch ? scratch_bytes : (size_t)0, need);
   const size_t smem = mlp_bwd_smem(CS, F, FF);
   rc = prepare_smem(mlp_bwd_kernel, smem, "ttt_mlp_bwd");
   if (rc) return rc;

@@ -23,12 +23,14 @@
 #include "fast_paths.cuh"
 #include "mma.cuh"
 #include "params.cuh"
+#include "mlp_tc_common.cuh"
+#include "tc_util.cuh"
 #include "tmem.cuh"
 
 namespace ttt {
 namespace mlp_tc {
 
-constexpr int F = 64, FF = 256, C = 16, NW = 8, NTHREADS = 32 * NW, NSTAGE = 3;
+constexpr int NW = 8, NTHREADS = 32 * NW, NSTAGE = 3;
 constexpr int TILE = C * F * 2;
 constexpr int ETA = C * C * 2;
 constexpr int STAGE = 3 * TILE + ETA;
@@ -42,39 +44,6 @@ constexpr int OFF_B1 = OFF_P + ETA;                     // fp32 [FF]
 constexpr int OFF_B2 = OFF_B1 + FF * 4;                 // fp32 [2][F] (ping-pong)
 constexpr int SMEM = OFF_B2 + 2 * F * 4;
 constexpr uint32_t TMEM_COLS = 256;  // W1^T and W2^T slices of 8 warps: 2 x 128 columns
-
-__device__ __forceinline__ float tanh_fast(float x) {
-  float y;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
-
-// gelu (F.gelu approximate="tanh") of a pair, on Blackwell's paired fp32 pipe.
-__device__ __forceinline__ float2 gelu2(float2 x) {
-  const float2 u = __fmul2_rn(x, x);
-  const float2 a = __ffma2_rn(f2(0.044715f), u, f2(1.f));
-  const float2 arg = __fmul2_rn(f2(0.7978845608f), __fmul2_rn(x, a));
-  const float2 t = make_float2(tanh_fast(arg.x), tanh_fast(arg.y));
-  const float2 hx = __fmul2_rn(f2(0.5f), x);
-  return __ffma2_rn(hx, t, hx);
-}
-
-// gelu and the reference's gelu_bwd (ops/ttt_utils.py:51-54) of a pair, sharing one tanh:
-// their tanh arguments differ only in the 10th digit of sqrt(2/pi), far below the
-// hardware tanh's error.
-__device__ __forceinline__ void gelu2_and_bwd(float2 x, float2& g, float2& gp) {
-  const float2 u = __fmul2_rn(x, x);
-  const float2 a = __ffma2_rn(f2(0.044715f), u, f2(1.f));
-  const float2 arg = __fmul2_rn(f2(0.7978845608f), __fmul2_rn(x, a));
-  const float2 t = make_float2(tanh_fast(arg.x), tanh_fast(arg.y));
-  const float2 hx = __fmul2_rn(f2(0.5f), x);
-  g = __ffma2_rn(hx, t, hx);
-  const float2 poly = __ffma2_rn(f2(0.1070322243f), u, f2(0.79788456f));
-  const float2 omt2 = __ffma2_rn(make_float2(-t.x, -t.y), t, f2(1.f));
-  const float2 base = __ffma2_rn(f2(0.5f), t, f2(0.5f));
-  gp = __ffma2_rn(__fmul2_rn(hx, omt2), poly, base);
-}
 
 __device__ __forceinline__ void load_stage(uint8_t* st, const MlpFwdParams& p, long long s, int n) {
   const int tid = threadIdx.x;
@@ -94,24 +63,6 @@ __device__ __forceinline__ void load_stage(uint8_t* st, const MlpFwdParams& p, l
   }
 }
 
-__device__ __forceinline__ float red16(float v) {
-  v += __shfl_xor_sync(0xffffffffu, v, 1);
-  v += __shfl_xor_sync(0xffffffffu, v, 2);
-  v += __shfl_xor_sync(0xffffffffu, v, 4);
-  v += __shfl_xor_sync(0xffffffffu, v, 8);
-  return v;
-}
-
-template <typename T>
-__device__ __forceinline__ void unpack4(const uint8_t* src, float* v) {
-  const uint2 u = *reinterpret_cast<const uint2*>(src);
-  const float2 a = Half2<T>::unpack(u.x), b = Half2<T>::unpack(u.y);
-  v[0] = a.x;
-  v[1] = a.y;
-  v[2] = b.x;
-  v[3] = b.y;
-}
-
 // Sum of the 8 warps' partial tiles for token tk, features 4q..4q+3.
 __device__ __forceinline__ void sum_partials(const float* part, int tk, int q, float* z) {
   float4 acc = *reinterpret_cast<const float4*>(part + tk * PLD + 4 * q);
@@ -127,60 +78,6 @@ __device__ __forceinline__ void sum_partials(const float* part, int tk, int q, f
   z[1] = acc.y;
   z[2] = acc.z;
   z[3] = acc.w;
-}
-
-// State slices <-> global [F][FF] (W1) and [FF][F] (W2) layouts.
-__device__ __forceinline__ void w1_io(float (*S1)[8][4], float* W1, int fb, int g, int t, bool store) {
-#pragma unroll
-  for (int m = 0; m < 2; ++m)
-#pragma unroll
-    for (int nf = 0; nf < 8; ++nf) {
-      const int f = 8 * nf + 2 * t, ff = fb + 16 * m + g;
-      float* p0 = W1 + f * FF + ff;
-      if (store) {
-        p0[0] = S1[m][nf][0];
-        p0[FF] = S1[m][nf][1];
-        p0[8] = S1[m][nf][2];
-        p0[FF + 8] = S1[m][nf][3];
-      } else {
-        S1[m][nf][0] = p0[0];
-        S1[m][nf][1] = p0[FF];
-        S1[m][nf][2] = p0[8];
-        S1[m][nf][3] = p0[FF + 8];
-      }
-    }
-}
-__device__ __forceinline__ void w2_io(float (*S2)[4][4], float* W2, int fb, int g, int t, bool store) {
-#pragma unroll
-  for (int m = 0; m < 4; ++m)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int f = 16 * m + g, ff = fb + 8 * j + 2 * t;
-      float* p0 = W2 + ff * F + f;
-      if (store) {
-        p0[0] = S2[m][j][0];
-        p0[F] = S2[m][j][1];
-        p0[8] = S2[m][j][2];
-        p0[F + 8] = S2[m][j][3];
-      } else {
-        S2[m][j][0] = p0[0];
-        S2[m][j][1] = p0[F];
-        S2[m][j][2] = p0[8];
-        S2[m][j][3] = p0[F + 8];
-      }
-    }
-}
-
-// A warp's 64-value state slice <-> its 64 TMEM columns (two 32-column loads / stores).
-__device__ __forceinline__ void slice_ld(uint32_t a, float* v) {
-  tmem_ld32(a, v);
-  tmem_ld32(a + 32, v + 32);
-  tmem_wait_ld();
-}
-__device__ __forceinline__ void slice_st(uint32_t a, const float* v) {
-  tmem_st32(a, v);
-  tmem_st32(a + 32, v + 32);
-  tmem_wait_st();
 }
 
 template <typename T>
@@ -312,6 +209,11 @@ __global__ void __launch_bounds__(NTHREADS, 2) mlp_fwd_tc_kernel(MlpFwdParams p)
         Zq[j][1] += bb.y;
         Zq[j][2] += bb.x;
         Zq[j][3] += bb.y;
+        if (p.Z1_out) {
+          float* zo = p.Z1_out + (s * p.NC + n) * (long long)(C * FF) + fb + 8 * j + 2 * t;
+          *reinterpret_cast<float2*>(zo + g * FF) = z01;
+          *reinterpret_cast<float2*>(zo + (g + 8) * FF) = z23;
+        }
         float2 g01, g23, d01, d23;
         gelu2_and_bwd(z01, g01, d01);
         gelu2_and_bwd(z23, g23, d23);
@@ -351,6 +253,9 @@ __global__ void __launch_bounds__(NTHREADS, 2) mlp_fwd_tc_kernel(MlpFwdParams p)
       z[1] += bb.y;
       z[2] += bb.z;
       z[3] += bb.w;
+      if (p.Z2_out)
+        *reinterpret_cast<float4*>(p.Z2_out + (s * p.NC + n) * (long long)(C * F) + tk * F + 4 * q) =
+            make_float4(z[0], z[1], z[2], z[3]);
       const uint32_t xo = swz128(tk, q >> 1) + (q & 1) * 8;
       unpack4<T>(st + OFF_XV + xo, xv);
       unpack4<T>(st + OFF_XK + xo, xk);
@@ -455,6 +360,11 @@ __global__ void __launch_bounds__(NTHREADS, 2) mlp_fwd_tc_kernel(MlpFwdParams p)
       for (int j = 0; j < 4; ++j) {
         const uint32_t b[2] = {ub[0][j], ub[1][j]};
         mma16816<T>(Zq[j], ap, b);
+        if (p.Z1b_out) {
+          float* zo = p.Z1b_out + (s * p.NC + n) * (long long)(C * FF) + fb + 8 * j + 2 * t;
+          *reinterpret_cast<float2*>(zo + g * FF) = make_float2(Zq[j][0], Zq[j][1]);
+          *reinterpret_cast<float2*>(zo + (g + 8) * FF) = make_float2(Zq[j][2], Zq[j][3]);
+        }
         const float2 g01 = gelu2(make_float2(Zq[j][0], Zq[j][1])), g23 = gelu2(make_float2(Zq[j][2], Zq[j][3]));
         XBp[j][0] = H::pack(g01.x, g01.y);
         XBp[j][1] = H::pack(g23.x, g23.y);
@@ -553,6 +463,9 @@ __global__ void __launch_bounds__(NTHREADS, 2) mlp_fwd_tc_kernel(MlpFwdParams p)
       z[1] += bb.y;
       z[2] += bb.z;
       z[3] += bb.w;
+      if (p.Z2b_out)
+        *reinterpret_cast<float4*>(p.Z2b_out + (s * p.NC + n) * (long long)(C * F) + tk * F + 4 * q) =
+            make_float4(z[0], z[1], z[2], z[3]);
       unpack4<T>(st + OFF_XQ + swz128(tk, q >> 1) + (q & 1) * 8, xq);
       const float mu = red16(z[0] + z[1] + z[2] + z[3]) * (1.f / F);
       float d[4], m2 = 0.f;

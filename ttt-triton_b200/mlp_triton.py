@@ -24,22 +24,23 @@ from _sharding import HEAD, LN, local_map
 def _forward_core(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ, XV, XK, eta,
                   checkpoint_group_size, memo_segment_size):
     ckpt = int(checkpoint_group_size)
-    XQW, _, ck, memo = _core.mlp_forward(
+    XQW, last, ck, memo, zs = _core.mlp_forward(
         ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init, b2_init, XQ, XV, XK, eta, ckpt, memo_segment_size,
         for_backward=any(ctx.needs_input_grad),
     )
-    ck = ck if ck is not None else ()
     ctx.ckpt = ckpt
-    ctx.save_for_backward(XQ, XV, XK, eta, ttt_norm_weight, ttt_norm_bias, *ck)
+    if ck is not None:
+        ctx.save_for_backward(XQ, XV, XK, eta, ttt_norm_weight, ttt_norm_bias, *ck, *zs, last[0], last[2])
     ctx.mark_non_differentiable(*memo)
     return (XQW, *memo)
 
 
 def _backward_core(ctx, grad_XQW):
-    XQ, XV, XK, eta, ln_w, ln_b, W1c, b1c, W2c, b2c = ctx.saved_tensors
+    XQ, XV, XK, eta, ln_w, ln_b, W1c, b1c, W2c, b2c, Z1, Z2, Z1b, Z2b, W1l, W2l = ctx.saved_tensors
     mp = XQ.dtype
     d_ln_w, d_ln_b, dW1, db1, dW2, db2, dXQ, dXV, dXK, deta = _core.mlp_backward(
-        ln_w, ln_b, (W1c, b1c, W2c, b2c), XQ, XV, XK, eta, grad_XQW, ctx.ckpt
+        ln_w, ln_b, (W1c, b1c, W2c, b2c), XQ, XV, XK, eta, grad_XQW, ctx.ckpt,
+        saved=(Z1, Z2, Z1b, Z2b), W1_last=W1l, W2_last=W2l,
     )
     return (
         d_ln_w.sum(0).reshape(ln_w.shape).to(mp),

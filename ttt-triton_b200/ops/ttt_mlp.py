@@ -16,19 +16,20 @@ class _MLPScan(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, ckpt):
-        XQW, _, ck, _ = _core.mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, ckpt, None,
+        XQW, last, ck, _, zs = _core.mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, ckpt, None,
                                           for_backward=any(ctx.needs_input_grad))
-        ck = ck if ck is not None else ()
         ctx.ckpt = ckpt
-        ctx.save_for_backward(XQ, XV, XK, eta, ln_w, ln_b, *ck)
+        if ck is not None:
+            ctx.save_for_backward(XQ, XV, XK, eta, ln_w, ln_b, *ck, *zs, last[0], last[2])
         return XQW
 
     @staticmethod
     def backward(ctx, grad):
-        XQ, XV, XK, eta, ln_w, ln_b, W1c, b1c, W2c, b2c = ctx.saved_tensors
+        XQ, XV, XK, eta, ln_w, ln_b, W1c, b1c, W2c, b2c, Z1, Z2, Z1b, Z2b, W1l, W2l = ctx.saved_tensors
         mp = XQ.dtype
         d_ln_w, d_ln_b, dW1, db1, dW2, db2, dXQ, dXV, dXK, deta = _core.mlp_backward(
-            ln_w, ln_b, (W1c, b1c, W2c, b2c), XQ, XV, XK, eta, grad, ctx.ckpt
+            ln_w, ln_b, (W1c, b1c, W2c, b2c), XQ, XV, XK, eta, grad, ctx.ckpt,
+            saved=(Z1, Z2, Z1b, Z2b), W1_last=W1l, W2_last=W2l,
         )
         return (d_ln_w.sum(0).reshape(ln_w.shape).to(mp), d_ln_b.sum(0).reshape(ln_b.shape).to(mp),
                 dW1.to(mp), db1.to(mp), dW2.to(mp), db2.to(mp), dXQ, dXV, dXK, deta, None)
