@@ -52,6 +52,8 @@ NCU_TRAFFIC = {
     ("mlp_fwd_c1", "mlp_fwd"): (235.5e6, 16 * 12 * 2048, "profiles/mlp_fwd_tc_config1.md"),
     ("linear_fwd_c2", "linear_fwd"): (557.6e6, 32 * 8 * 4096, "profiles/linear_fwd_tc_config2.md"),
     ("linear_fwdbwd_c2", "linear_bwd"): (1252.9e6, 32 * 8 * 4096, "profiles/linear_bwd_tc_config2.md"),
+    # captured at batch 4 (64 streams); traffic per stream is size-independent, scaled by tokens
+    ("mlp_fwdbwd_c3", "mlp_bwd"): (1849.8e6, 4 * 16 * 8192, "profiles/mlp_bwd_tc_config3.md"),
 }
 METRIC = "TTT tokens/s (B*H*L) fwd & fwd+bwd at 1/2/4/8 B200; % of HBM roofline"
 
@@ -433,10 +435,16 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mlp_fwd_c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's per-rank batch (smaller cases for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.batch is not None:
+        if args.batch <= 0:
+            raise SystemExit("--batch must be positive")
+        w["B"] = args.batch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
