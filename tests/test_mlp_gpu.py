@@ -161,3 +161,23 @@ def test_saved_preactivations_match_oracle():
               st[2] - (e * X2).transpose(-1, -2) @ G2, st[3] - (e * G2).sum(-2, keepdim=True)]
     for i, name in enumerate(("Z1", "Z2", "Z1bar", "Z2bar")):
         assert_close(name, zs[i], torch.stack(ref[i], 2), 2e-2)
+
+
+@pytest.mark.parametrize("B,NH", [(1, 2), (2, 150), (4, 64)])
+def test_forward_sampled_streams_few_and_many(B, NH):
+    """Grids below and above the number of SMs (one and several waves): final states,
+    checkpoints, memo states and outputs of sampled streams match the oracle."""
+    NC, CS, F, FF = 3, 16, 64, 256
+    d, _ = make(B, NH, NC, CS, F, FF, torch.bfloat16, seed=B + NH)
+    out, last, ck, memo, zs = _core.mlp_forward(*(d[k] for k in NAMES), 2, 1)
+    od = oracle_inputs(d)
+    for b, hh in ((0, 0), (B - 1, NH - 1), (B // 2, NH // 2)):
+        sub = {k: (v[b:b + 1, hh:hh + 1] if k not in ("ln_w", "ln_b") else v[hh:hh + 1]) for k, v in od.items()}
+        r = O.mlp_scan(*(sub[k] for k in NAMES), 2, 1)
+        assert_close(f"XQW[{b},{hh}]", out[b:b + 1, hh:hh + 1], r["XQW"], 2e-2)
+        for i, name in enumerate(("W1", "b1", "W2", "b2")):
+            init = sub[name]
+            assert_close(f"{name}_last[{b},{hh}]", last[i][b:b + 1, hh:hh + 1].double().cpu() - init,
+                         r[name + "_last"] - init, 2e-2)
+            assert_close(f"{name}_ckpt[{b},{hh}]", ck[i][b:b + 1, hh:hh + 1], r[name + "_ckpt"], 2e-2)
+            assert_close(f"{name}_memo[{b},{hh}]", memo[i][b:b + 1, hh:hh + 1], r[name + "_memo"], 2e-2)

@@ -1,11 +1,12 @@
 // Pieces shared by the tensor-core TTT-MLP kernels (F = 64, FF = 256, CS = 16): the
 // accumulator-fragment layout of a warp's state slices and their TMEM / global copies.
 //
-// Warp w owns hidden units [32w, 32w + 32). Its slice of W1 is held as W1^T (32 x 64,
-// fragments [2][8][4]: hidden rows 16m + g (+8), feature columns 8nf + 2t (+1)), its
-// slice of W2 as W2^T (64 x 32, fragments [4][4][4]: feature rows 16m + g (+8), hidden
-// columns 8j + 2t (+1)). These accumulator layouts are directly the mma B-operand layouts
-// of W1 and W2 (k = feature resp. hidden); movmatrix turns them into those of W1^T, W2^T.
+// A warp owns 16 M consecutive hidden units (M = 2: 32 units, M = 1: 16). Its slice of W1
+// is held as W1^T (16M x 64, fragments [M][8][4]: hidden rows 16m + g (+8), feature columns
+// 8nf + 2t (+1)), its slice of W2 as W2^T (64 x 16M, fragments [4][2M][4]: feature rows
+// 16m + g (+8), hidden columns 8j + 2t (+1)). These accumulator layouts are directly the
+// mma B-operand layouts of W1 and W2 (k = feature resp. hidden); movmatrix turns them into
+// those of W1^T, W2^T.
 #pragma once
 
 #include "tmem.cuh"
@@ -15,10 +16,12 @@ namespace mlp_tc {
 
 constexpr int F = 64, FF = 256, C = 16;
 
-// State slices <-> global [F][FF] (W1) and [FF][F] (W2) layouts.
+// State slices <-> global [F][FF] (W1) and [FF][F] (W2) layouts. A warp owning 16 * M
+// hidden units from fb holds W1^T as M x 8 accumulator tiles and W2^T as 4 x 2M tiles.
+template <int M = 2>
 __device__ __forceinline__ void w1_io(float (*S1)[8][4], float* W1, int fb, int g, int t, bool store) {
 #pragma unroll
-  for (int m = 0; m < 2; ++m)
+  for (int m = 0; m < M; ++m)
 #pragma unroll
     for (int nf = 0; nf < 8; ++nf) {
       const int f = 8 * nf + 2 * t, ff = fb + 16 * m + g;
@@ -36,11 +39,12 @@ __device__ __forceinline__ void w1_io(float (*S1)[8][4], float* W1, int fb, int 
       }
     }
 }
-__device__ __forceinline__ void w2_io(float (*S2)[4][4], float* W2, int fb, int g, int t, bool store) {
+template <int M = 2>
+__device__ __forceinline__ void w2_io(float (*S2)[2 * M][4], float* W2, int fb, int g, int t, bool store) {
 #pragma unroll
   for (int m = 0; m < 4; ++m)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 2 * M; ++j) {
       const int f = 16 * m + g, ff = fb + 8 * j + 2 * t;
       float* p0 = W2 + ff * F + f;
       if (store) {
@@ -57,15 +61,17 @@ __device__ __forceinline__ void w2_io(float (*S2)[4][4], float* W2, int fb, int 
     }
 }
 
-// A warp's 64-value state slice <-> its 64 TMEM columns (two 32-column loads / stores).
+// A warp's state slice of NV values (32 or 64) <-> its NV TMEM columns.
+template <int NV = 64>
 __device__ __forceinline__ void slice_ld(uint32_t a, float* v) {
   tmem_ld32(a, v);
-  tmem_ld32(a + 32, v + 32);
+  if (NV == 64) tmem_ld32(a + 32, v + 32);
   tmem_wait_ld();
 }
+template <int NV = 64>
 __device__ __forceinline__ void slice_st(uint32_t a, const float* v) {
   tmem_st32(a, v);
-  tmem_st32(a + 32, v + 32);
+  if (NV == 64) tmem_st32(a + 32, v + 32);
   tmem_wait_st();
 }
 
