@@ -155,6 +155,14 @@ int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_gro
                 float* Z1_out, float* Z2_out, float* Z1b_out, float* Z2b_out,
                 void* stream);
 
+/*
+ * Reads and clears this library's device error word for the current device, synchronising
+ * with it. Non-zero bits mean a kernel gave up waiting for its own asynchronous copies
+ * (bit 0: a TMA stage did not land within 2 s) and voided the affected streams' results.
+ * No counterpart in the reference (its Triton kernels have no bounded waits).
+ */
+int ttt_device_status(unsigned int* status);
+
 /* Bytes of scratch ttt_mlp_bwd needs for these sizes. */
 size_t ttt_mlp_bwd_scratch_bytes(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_group_size);
 

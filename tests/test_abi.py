@@ -101,3 +101,7 @@ def test_mlp_saved_preactivations_all_or_none():
     assert "all set or all NULL" in _lib.lib.ttt_last_error().decode()
     # without the saved pre-activations the recompute path needs its scratch buffer
     assert bwd([None] * 6, None) == -5
+
+
+def test_device_status_rejects_null():
+    assert _lib.lib.ttt_device_status(None) == -1

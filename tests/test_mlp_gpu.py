@@ -181,3 +181,14 @@ def test_forward_sampled_streams_few_and_many(B, NH):
                          r[name + "_last"] - init, 2e-2)
             assert_close(f"{name}_ckpt[{b},{hh}]", ck[i][b:b + 1, hh:hh + 1], r[name + "_ckpt"], 2e-2)
             assert_close(f"{name}_memo[{b},{hh}]", memo[i][b:b + 1, hh:hh + 1], r[name + "_memo"], 2e-2)
+
+
+def test_no_bounded_wait_gave_up():
+    """The TMA-staged kernels report a stage that never landed in the device error word;
+    after a run it must be clear."""
+    import _lib
+
+    _lib.device_status()
+    d, _ = make(2, 3, 5, 16, 64, 256, torch.bfloat16, seed=51)
+    _core.mlp_forward(*(d[k] for k in NAMES), 2, None, for_backward=False)
+    assert _lib.device_status() == 0

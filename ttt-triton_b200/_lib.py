@@ -57,6 +57,7 @@ _SIGNATURES = {
         + [_I, _P, _Z, _P],
         _I,
     ),
+    "ttt_device_status": ([_P], _I),
     "ttt_mlp_cached_readout": (
         [_I] * 6 + [_P, _I] + [_P, _L, _L] * 4 + [_P, _P, _I, _P, _P],
         _I,
@@ -90,6 +91,13 @@ def check(rc, name):
     if rc != 0:
         msg = lib.ttt_last_error().decode(errors="replace")
         raise RuntimeError(f"{name} failed (status {rc}): {msg}")
+
+
+def device_status():
+    """Read and clear the device error word (synchronises with the current device)."""
+    v = ctypes.c_uint(0)
+    check(lib.ttt_device_status(ctypes.byref(v)), "ttt_device_status")
+    return v.value
 
 
 def dtype_code(t):

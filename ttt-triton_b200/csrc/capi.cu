@@ -1,6 +1,90 @@
-// ABI-wide entry points: version and the per-thread last-error message.
+// ABI-wide entry points: version, the per-thread last-error message and the device error
+// word; host helpers shared by the kernels' entry points (TMA tensor maps).
+#include <mutex>
+
 #include "capi_common.cuh"
+#include "common.cuh"
+#include "tma.cuh"
 
 extern "C" int ttt_abi_version(void) { return 10000; }
 
 extern "C" const char* ttt_last_error(void) { return ttt::last_error_buffer(); }
+
+namespace ttt {
+
+// Bits set by kernels that gave up waiting (see tma.cuh); one word per device.
+static __device__ unsigned int g_device_error;
+
+int device_error_word(unsigned int** out, const char* who) {
+  constexpr int kMaxDevices = 64;
+  static unsigned int* addr[kMaxDevices] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(TTT_ERR_CUDA, "%s: cudaGetDevice: %s", who, cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(TTT_ERR_UNSUPPORTED, "%s: device %d out of range", who, dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_device_error);
+    if (e != cudaSuccess) return fail(TTT_ERR_CUDA, "%s: cudaGetSymbolAddress: %s", who, cudaGetErrorString(e));
+    addr[dev] = static_cast<unsigned int*>(p);
+  }
+  *out = addr[dev];
+  return TTT_OK;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver the runtime already loaded (no link-time dependency).
+static EncodeTiledFn encode_tiled(const char* who) {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!fn) fail(TTT_ERR_CUDA, "%s: cuTensorMapEncodeTiled is not available from the driver", who);
+  return fn;
+}
+
+int make_tile_map(CUtensorMap* map, const void* base, int dtype_code, unsigned long long rows, const char* who) {
+  EncodeTiledFn fn = encode_tiled(who);
+  if (!fn) return TTT_ERR_CUDA;
+  const cuuint64_t dims[2] = {64, rows};
+  const cuuint64_t strides[1] = {128};  // bytes between rows
+  const cuuint32_t box[2] = {64, 16};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      dtype_code == DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TTT_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", who, (int)r);
+  return TTT_OK;
+}
+
+}  // namespace ttt
+
+// Reads and clears the device error word of the current device (synchronises with it).
+extern "C" int ttt_device_status(unsigned int* status) {
+  TTT_REQUIRE(status, TTT_ERR_NULL, "ttt_device_status: NULL pointer argument");
+  unsigned int* w = nullptr;
+  int rc = ttt::device_error_word(&w, "ttt_device_status");
+  if (rc) return rc;
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return ttt::fail(TTT_ERR_CUDA, "ttt_device_status: %s", cudaGetErrorString(e));
+  if (v) {
+    const unsigned int zero = 0;
+    e = cudaMemcpy(w, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return ttt::fail(TTT_ERR_CUDA, "ttt_device_status: %s", cudaGetErrorString(e));
+  }
+  *status = v;
+  return TTT_OK;
+}

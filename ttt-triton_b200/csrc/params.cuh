@@ -87,6 +87,7 @@ struct MlpFwdParams {
   float* Z2_out;
   float* Z1b_out;
   float* Z2b_out;
+  unsigned int* err;  // device error word (set by the entry point for kernels with bounded waits)
 };
 
 struct MlpBwdParams {

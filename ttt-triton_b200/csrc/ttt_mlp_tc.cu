@@ -25,6 +25,7 @@
 #include "params.cuh"
 #include "mlp_tc_common.cuh"
 #include "tc_util.cuh"
+#include "tma.cuh"
 #include "tmem.cuh"
 
 namespace ttt {
@@ -33,8 +34,12 @@ namespace mlp_tc {
 constexpr int NW = 8, NTHREADS = 32 * NW, NSTAGE = 3;
 constexpr int TILE = C * F * 2;
 constexpr int ETA = C * C * 2;
-constexpr int STAGE = 3 * TILE + ETA;
-constexpr int OFF_XQ = 0, OFF_XK = TILE, OFF_XV = 2 * TILE, OFF_ETA = 3 * TILE;
+// Stage of one mini-batch, filled by TMA: XQ, XK, XV tiles (1024-byte aligned for the
+// 128-byte swizzle) and the eta tile.
+constexpr int OFF_XQ = 0, OFF_XK = 1024 * ((TILE + 1023) / 1024), OFF_XV = 2 * OFF_XK, OFF_ETA = 3 * OFF_XK;
+constexpr int STAGE = 1024 * ((OFF_ETA + ETA + 1023) / 1024);
+constexpr uint32_t STAGE_BYTES = 3 * TILE + ETA;  // bytes the copies of one stage deliver
+constexpr int kCopyThread = NTHREADS - 32;          // lane 0 of the last warp issues and awaits the copies
 constexpr int PLD = F + 8;                              // fp32 row stride of the partial tiles
 constexpr int OFF_PART = NSTAGE * STAGE;                // fp32 [NW][C][PLD] per-warp partial sums
 constexpr int OFF_G = OFF_PART + NW * C * PLD * 4;      // 16-bit [C][F] swizzled: G2
@@ -42,25 +47,19 @@ constexpr int OFF_EG = OFF_G + TILE;                    // 16-bit [C][F] swizzle
 constexpr int OFF_P = OFF_EG + TILE;                    // 16-bit [C][C]: -P1
 constexpr int OFF_B1 = OFF_P + ETA;                     // fp32 [FF]
 constexpr int OFF_B2 = OFF_B1 + FF * 4;                 // fp32 [2][F] (ping-pong)
-constexpr int SMEM = OFF_B2 + 2 * F * 4;
+constexpr int SMEM = OFF_B2 + 2 * F * 4 + 1024;  // + slack to align the base to 1024 bytes
 constexpr uint32_t TMEM_COLS = 256;  // W1^T and W2^T slices of 8 warps: 2 x 128 columns
 
-__device__ __forceinline__ void load_stage(uint8_t* st, const MlpFwdParams& p, long long s, int n) {
-  const int tid = threadIdx.x;
-  const long long tb = (s * p.NC + n) * (long long)(C * F) * 2;
-  if (tid < 128) {
-    const int row = tid >> 3, ch = tid & 7;
-    const uint32_t dst = smem_u32(st) + swz128(row, ch);
-    cp_async16(dst + OFF_XQ, (const uint8_t*)p.XQ + tb + row * 128 + ch * 16);
-    cp_async16(dst + OFF_XK, (const uint8_t*)p.XK + tb + row * 128 + ch * 16);
-  } else {
-    const int i = tid - 128, row = i >> 3, ch = i & 7;
-    cp_async16(smem_u32(st) + OFF_XV + swz128(row, ch), (const uint8_t*)p.XV + tb + row * 128 + ch * 16);
-    if (i < 32) {
-      const long long eb = (s * p.NC + n) * (long long)(C * C) * 2;
-      cp_async16(smem_u32(st) + OFF_ETA + i * 16, (const uint8_t*)p.eta + eb + i * 16);
-    }
-  }
+// One thread: TMA copies of mini-batch n's XQ, XK, XV tiles and eta tile into stage `st`,
+// completing on mbarrier `bar`.
+__device__ __forceinline__ void issue_stage(uint32_t st, uint32_t bar, const MlpFwdParams& p, const CUtensorMap* tq,
+                                            const CUtensorMap* tk, const CUtensorMap* tv, long long s, int n) {
+  const int row = (int)((s * p.NC + n) * C);
+  mbar_expect_tx(bar, STAGE_BYTES);
+  tma_load_2d(st + OFF_XQ, tq, 0, row, bar);
+  tma_load_2d(st + OFF_XK, tk, 0, row, bar);
+  tma_load_2d(st + OFF_XV, tv, 0, row, bar);
+  bulk_load(st + OFF_ETA, (const uint8_t*)p.eta + (s * p.NC + n) * (long long)ETA, ETA, bar);
 }
 
 // Sum of the 8 warps' partial tiles for token tk, features 4q..4q+3.
@@ -81,10 +80,15 @@ __device__ __forceinline__ void sum_partials(const float* part, int tk, int q, f
 }
 
 template <typename T>
-__global__ void __launch_bounds__(NTHREADS, 2) mlp_fwd_tc_kernel(MlpFwdParams p) {
+__global__ void __launch_bounds__(NTHREADS, 2)
+    mlp_fwd_tc_kernel(MlpFwdParams p, const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v) {
   using H = Half2<T>;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   __shared__ uint32_t tmem_base_sh;
+  __shared__ __align__(8) uint64_t full_bar[NSTAGE];  // stage n % NSTAGE landed
+  __shared__ int abort_sh;                            // a stage never landed: stop waiting
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int mi = lane >> 3, r8 = lane & 7;
   const long long s = blockIdx.x;
@@ -102,9 +106,20 @@ __global__ void __launch_bounds__(NTHREADS, 2) mlp_fwd_tc_kernel(MlpFwdParams p)
     tmem_alloc(&tmem_base_sh, TMEM_COLS);
     tmem_relinquish();
   }
+  if (tid == 32) {
+    for (int i = 0; i < NSTAGE; ++i) mbar_init(smem_u32(&full_bar[i]), 1);
+    abort_sh = 0;
+    fence_mbar_init();
+  }
   tmem_fence_before();
   __syncthreads();
   tmem_fence_after();
+  int last_issued = -1;  // (copy thread) last mini-batch whose stage copies were issued
+  if (tid == kCopyThread)
+    for (int i = 0; i < NSTAGE - 1 && i < p.NC; ++i) {
+      issue_stage(smem_u32(smem + i * STAGE), smem_u32(&full_bar[i]), p, &tm_q, &tm_k, &tm_v, s, i);
+      last_issued = i;
+    }
   const uint32_t tS1 = tmem_lane_addr(tmem_base_sh, warp, 128 * (warp >> 2));
   const uint32_t tS2 = tS1 + 64;
   {
@@ -125,20 +140,21 @@ __global__ void __launch_bounds__(NTHREADS, 2) mlp_fwd_tc_kernel(MlpFwdParams p)
   const uint32_t ones = H::pack(1.f, 1.f);
   const uint32_t a_ones[4] = {ones, ones, ones, ones};
 
-#pragma unroll
-  for (int i = 0; i < NSTAGE - 1; ++i) {
-    if (i < p.NC) load_stage(smem + i * STAGE, p, s, i);
-    cp_async_commit();
-  }
-
   int ck_left = 0, memo_left = 0;  // mini-batches until the next checkpoint / memo state
   for (int n = 0; n < p.NC; ++n) {
-    cp_async_wait<NSTAGE - 2>();
+    // The copy thread waits for stage n; the CTA barrier then publishes it to every warp and
+    // tells the copy thread that mini-batch n-1 is done, so its stage may be refilled.
+    if (tid == kCopyThread && !abort_sh &&
+        !mbar_wait(smem_u32(&full_bar[n % NSTAGE]), (uint32_t)((n / NSTAGE) & 1), p.err))
+      abort_sh = 1;  // results of this stream are void; the error word reports it
     __syncthreads();
     {
       const int nn = n + NSTAGE - 1;
-      if (nn < p.NC) load_stage(smem + (nn % NSTAGE) * STAGE, p, s, nn);
-      cp_async_commit();
+      if (tid == kCopyThread && nn < p.NC && !abort_sh) {
+        issue_stage(smem_u32(smem + (nn % NSTAGE) * STAGE), smem_u32(&full_bar[nn % NSTAGE]), p, &tm_q, &tm_k, &tm_v, s,
+                    nn);
+        last_issued = nn;
+      }
     }
     const uint8_t* st = smem + (n % NSTAGE) * STAGE;
     const uint32_t sb = smem_u32(st);
@@ -495,7 +511,6 @@ __global__ void __launch_bounds__(NTHREADS, 2) mlp_fwd_tc_kernel(MlpFwdParams p)
     }
     --memo_left;
   }
-  cp_async_wait<0>();
   __syncthreads();
   {
     float S1[2][8][4], S2[4][4][4];
@@ -504,6 +519,11 @@ __global__ void __launch_bounds__(NTHREADS, 2) mlp_fwd_tc_kernel(MlpFwdParams p)
     slice_ld(tS2, &S2[0][0][0]);
     w2_io(S2, p.W2_last + s * FF * F, fb, g, t, true);
   }
+  // after a timeout, copies issued but never awaited may still be in flight: drain them
+  // (bounded) before the CTA's shared memory goes away
+  if (tid == kCopyThread && abort_sh)
+    for (int m = last_issued - NSTAGE + 1; m <= last_issued; ++m)
+      if (m >= 0) mbar_wait(smem_u32(&full_bar[m % NSTAGE]), (uint32_t)((m / NSTAGE) & 1), nullptr);
   const float* b2_fin = b2s + (p.NC & 1) * F;
   for (int i = tid; i < FF; i += NTHREADS) p.b1_last[s * FF + i] = b1s[i];
   for (int i = tid; i < F; i += NTHREADS) p.b2_last[s * F + i] = b2_fin[i];
@@ -526,15 +546,23 @@ int mlp_fwd_fast(const MlpFwdParams& p, cudaStream_t stream) {
   if (p.dt_xk != dt || p.dt_xv != dt || p.dt_eta != dt || p.dt_out != dt) return TTT_NOT_APPLICABLE;
   if (!aligned16(p.XQ) || !aligned16(p.XK) || !aligned16(p.XV) || !aligned16(p.eta) || !aligned16(p.out))
     return TTT_NOT_APPLICABLE;
-  int rc;
+  const unsigned long long rows = (unsigned long long)p.B * p.NH * p.NC * C;
+  CUtensorMap tq, tk, tv;
+  int rc = make_tile_map(&tq, p.XQ, dt, rows, "ttt_mlp_fwd");
+  if (!rc) rc = make_tile_map(&tk, p.XK, dt, rows, "ttt_mlp_fwd");
+  if (!rc) rc = make_tile_map(&tv, p.XV, dt, rows, "ttt_mlp_fwd");
+  if (rc) return rc;
+  MlpFwdParams q = p;
+  rc = device_error_word(&q.err, "ttt_mlp_fwd");
+  if (rc) return rc;
   if (dt == DT_BF16) {
     rc = prepare_smem(mlp_fwd_tc_kernel<__nv_bfloat16>, SMEM, "ttt_mlp_fwd");
     if (rc) return rc;
-    mlp_fwd_tc_kernel<__nv_bfloat16><<<p.B * p.NH, NTHREADS, SMEM, stream>>>(p);
+    mlp_fwd_tc_kernel<__nv_bfloat16><<<p.B * p.NH, NTHREADS, SMEM, stream>>>(q, tq, tk, tv);
   } else {
     rc = prepare_smem(mlp_fwd_tc_kernel<__half>, SMEM, "ttt_mlp_fwd");
     if (rc) return rc;
-    mlp_fwd_tc_kernel<__half><<<p.B * p.NH, NTHREADS, SMEM, stream>>>(p);
+    mlp_fwd_tc_kernel<__half><<<p.B * p.NH, NTHREADS, SMEM, stream>>>(q, tq, tk, tv);
   }
   return check_launch("ttt_mlp_fwd");
 }
