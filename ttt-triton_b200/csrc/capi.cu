@@ -53,12 +53,13 @@ static EncodeTiledFn encode_tiled(const char* who) {
   return fn;
 }
 
-int make_tile_map(CUtensorMap* map, const void* base, int dtype_code, unsigned long long rows, const char* who) {
+int make_tile_map(CUtensorMap* map, const void* base, int dtype_code, unsigned long long rows, const char* who,
+                  unsigned box_rows) {
   EncodeTiledFn fn = encode_tiled(who);
   if (!fn) return TTT_ERR_CUDA;
   const cuuint64_t dims[2] = {64, rows};
   const cuuint64_t strides[1] = {128};  // bytes between rows
-  const cuuint32_t box[2] = {64, 16};
+  const cuuint32_t box[2] = {64, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUtensorMapDataType dt =
       dtype_code == DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;

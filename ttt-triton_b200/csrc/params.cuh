@@ -22,6 +22,7 @@ struct LinFwdParams {
   float* W_ckpt;
   float* b_ckpt;
   float* Z_out;  // optional [B,NH,NC,CS,F] fp32: Z = XK W_n + b_n of every mini-batch
+  unsigned int* err;  // device error word (set by the entry point for kernels with bounded waits)
 };
 
 struct LinBwdParams {

@@ -77,9 +77,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
 }
 
 // ---------------------------------------------------------------------------------- host
-// Tensor map of a [rows][64] 16-bit matrix (row stride 128 bytes) read in 16 x 64 boxes with
-// the 128-byte swizzle. dtype_code: 1 bf16, 2 f16. Returns 0 or a TTT_ERR_* code.
-int make_tile_map(CUtensorMap* map, const void* base, int dtype_code, unsigned long long rows, const char* who);
+// Tensor map of a [rows][64] 16-bit matrix (row stride 128 bytes) read in box_rows x 64 boxes
+// (box_rows <= 256) with the 128-byte swizzle. dtype_code: 1 bf16, 2 f16. Returns 0 or a
+// TTT_ERR_* code.
+int make_tile_map(CUtensorMap* map, const void* base, int dtype_code, unsigned long long rows, const char* who,
+                  unsigned box_rows = 16);
 
 // Device address of the library's device error word on the current device.
 int device_error_word(unsigned int** out, const char* who);
