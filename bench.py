@@ -49,8 +49,8 @@ DT = {"f32": torch.float32, "bf16": torch.bfloat16}
 # the same workload: (bytes, tokens in that launch, summary file). Scaled to the
 # launch measured here by tokens processed.
 NCU_TRAFFIC = {
-    ("mlp_fwd_c1", "mlp_fwd"): (235.5e6, 16 * 12 * 2048, "profiles/mlp_fwd_tc_config1.md"),
-    ("linear_fwd_c2", "linear_fwd"): (557.6e6, 32 * 8 * 4096, "profiles/linear_fwd_tc_config2.md"),
+    ("mlp_fwd_c1", "mlp_fwd"): (232.0e6, 16 * 12 * 2048, "profiles/mlp_fwd_tc_config1.md"),
+    ("linear_fwd_c2", "linear_fwd"): (557.3e6, 32 * 8 * 4096, "profiles/linear_fwd_tc_config2.md"),
     ("linear_fwdbwd_c2", "linear_bwd"): (1252.9e6, 32 * 8 * 4096, "profiles/linear_bwd_tc_config2.md"),
     # captured at batch 4 (64 streams); traffic per stream is size-independent, scaled by tokens
     ("mlp_fwdbwd_c3", "mlp_bwd"): (1849.8e6, 4 * 16 * 8192, "profiles/mlp_bwd_tc_config3.md"),
