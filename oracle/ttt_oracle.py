@@ -219,6 +219,60 @@ def mlp_cached_readout(XQ_seg, W1, b1, W2, b2, ln_w, ln_b, eps=READOUT_EPS):
     return XQ_seg + ln_fwd(Z2, lw, lb, eps=eps)
 
 
+def memo_mix(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, memo_segment_size):
+    """Memo-state mixing of the TTT-MLP layer's output (ttt_layer.py:503-559), all segments.
+
+    XQW, XQ, XK, XU [B,NH,NC,CS,F]; memo states [B,NH,NS,...] from mlp_scan(..., memo_segment_size)
+    (memo j = state after mini-batch j * memo_segment_size). Segment i covers mini-batches
+    [i*M, min((i+1)*M, NC)). Its summary is the mean of its XK over mini-batches and tokens
+    (ttt_layer.py:519); the summaries of earlier segments enter detached (:527, :558). For
+    i >= 1 each token mixes, with softmax weights over sims_j = <XU, summary_j> (j = 0..i,
+    :522-533), the online output (weight of j = i, :536) and the cached read-outs of memo
+    states 0..i-1 (:540-554). Segment 0 passes through. Differentiable in XQW, XU and XK
+    (through the current segment's summary); the cached read-outs carry no gradient (:542).
+    """
+    B, NH, NC, CS, F = XQW.shape
+    M = int(memo_segment_size)
+    NS = math.ceil(NC / M)
+    out_segs = []
+    cached = []
+    for i in range(NS):
+        s0, s1 = i * M, min((i + 1) * M, NC)
+        XQ_seg = XQ[:, :, s0:s1]
+        XU_seg = XU[:, :, s0:s1]
+        XQW_seg = XQW[:, :, s0:s1]
+        summary_cur = XK[:, :, s0:s1].mean(dim=(2, 3))
+        if i == 0:
+            cached.append(summary_cur.detach())
+            out_segs.append(XQW_seg)
+            continue
+        sims = [(XU_seg * summ[:, :, None, None, :]).sum(dim=-1) for summ in cached]
+        sims.append((XU_seg * summary_cur[:, :, None, None, :]).sum(dim=-1))
+        gamma = torch.softmax(torch.stack(sims, dim=-1), dim=-1)
+        seg = gamma[..., -1:] * XQW_seg
+        for j in range(i):
+            with torch.no_grad():
+                delta = mlp_cached_readout(XQ_seg, W1_memo[:, :, j], b1_memo[:, :, j], W2_memo[:, :, j],
+                                           b2_memo[:, :, j], ln_w, ln_b)
+            seg = seg + gamma[..., j:j + 1] * delta
+        out_segs.append(seg)
+        cached.append(summary_cur.detach())
+    return torch.cat(out_segs, dim=2)
+
+
+MEMO_MIX_GRAD_NAMES = ("XQW", "XU", "XK")
+
+
+def memo_mix_grads(inp, dO, memo_segment_size):
+    """Autograd gradients of <memo_mix(...), dO> w.r.t. XQW, XU and XK."""
+    leaves = {k: (inp[k].detach().clone().requires_grad_(True) if k in MEMO_MIX_GRAD_NAMES else inp[k])
+              for k in inp}
+    out = memo_mix(leaves["XQW"], leaves["XQ"], leaves["XK"], leaves["XU"], leaves["W1_memo"], leaves["b1_memo"],
+                   leaves["W2_memo"], leaves["b2_memo"], leaves["ln_w"], leaves["ln_b"], memo_segment_size)
+    out.backward(dO)
+    return {k: leaves[k].grad for k in MEMO_MIX_GRAD_NAMES}, out.detach()
+
+
 # --------------------------------------------------------------------------- gradients
 LINEAR_GRAD_NAMES = ("ln_w", "ln_b", "W1", "b1", "XQ", "XV", "XK", "eta")
 MLP_GRAD_NAMES = ("ln_w", "ln_b", "W1", "b1", "W2", "b2", "XQ", "XV", "XK", "eta")

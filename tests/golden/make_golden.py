@@ -10,7 +10,8 @@ cannot build here) and ``forecast`` imported first (ttt_layer <-> forecast impor
 cycle), runs it in float64 on seeded float32-representable inputs, and takes gradients
 with torch autograd exactly as the reference's training path does. The cached-readout
 golden runs the reference's Triton kernel (kernels/mlp_cached_readout.py:7-109) under
-the Triton CPU interpreter at B = NH = 1, the only slice its offsets address correctly.
+the Triton CPU interpreter at B = NH = 1, the only slice its offsets address correctly; the
+memo-mixing golden runs the reference's own mixing loop of TTTMLP.ttt with that kernel.
 
 Outputs ``tests/golden/*.npz`` (float32 storage). The GPU box never runs this script.
 """
@@ -121,6 +122,75 @@ def cached_readout_case(ref_root, NCs, F, FF, seed):
     return {k: _np(v) for k, v in res.items()}
 
 
+def memo_mix_case(ref_root, NC, F, FF, M, seed):
+    """The reference's own memo-mixing loop (TTTMLP.ttt, ttt_layer.py:451-561) at B = NH = 1:
+    TritonMLP.apply is stubbed to return the given scan output and memo states, and the
+    cached read-outs run the reference's Triton kernel under the CPU interpreter (its CUDA
+    wrapper is swapped for a launch of the same kernel). Gradients w.r.t. XQW, XU and XK
+    come from autograd through the reference code."""
+    import types
+
+    sys.path.insert(0, ref_root)
+    import ttt_layer
+    from kernels.mlp_cached_readout import mlp_cached_readout_kernel
+
+    NS = -(-NC // M)
+    g = torch.Generator().manual_seed(seed)
+    t = {
+        "XQW": torch.randn(1, 1, NC, 16, F, generator=g) / 4,
+        "XQ": torch.randn(1, 1, NC, 16, F, generator=g) / 8,
+        "XK": torch.randn(1, 1, NC, 16, F, generator=g) / 8,
+        "XU": torch.randn(1, 1, NC, 16, F, generator=g),
+        "W1_memo": torch.randn(1, 1, NS, F, FF, generator=g) * 0.05,
+        "b1_memo": torch.randn(1, 1, NS, 1, FF, generator=g) * 0.02,
+        "W2_memo": torch.randn(1, 1, NS, FF, F, generator=g) * 0.05,
+        "b2_memo": torch.randn(1, 1, NS, 1, F, generator=g) * 0.02,
+        "ln_w": 1 + 0.1 * torch.randn(1, F, generator=g),
+        "ln_b": 0.1 * torch.randn(1, F, generator=g),
+    }
+    dO = torch.randn(1, NC * 16, F, generator=g)
+    leaves = {k: t[k].clone().requires_grad_(True) for k in ("XQW", "XU", "XK")}
+
+    def readout(XQ_seg, W1, b1, W2, b2, ln_w, ln_b):
+        XQ_seg, W1, b1, W2, b2 = (x.detach().contiguous() for x in (XQ_seg, W1, b1, W2, b2))
+        out = torch.empty_like(XQ_seg)
+        mlp_cached_readout_kernel[(1, 1, XQ_seg.shape[2])](
+            XQ_seg, W1, b1, W2, b2, ln_w.detach(), ln_b.detach(), out,
+            CS_F_stride=16 * F, F_FF_stride=F * FF, FF_F_stride=FF * F, F_stride=F, FF_stride=FF,
+            NH=1, CS=16, F=F, FF=FF, num_warps=4,
+        )
+        return XQ_seg + out
+
+    class StubMLP:
+        # The scan output is handed over in a non-contiguous layout: with B = NH = 1 a
+        # contiguous one would make the loop's `.contiguous()` segment copies (ttt_layer.py:516)
+        # aliases of the tensor it then writes in place (:557), which autograd rejects; with
+        # B * NH > 1, as in training, the slices are strided and copied anyway.
+        @staticmethod
+        def apply(*args):
+            xqw = leaves["XQW"].transpose(-1, -2).contiguous().transpose(-1, -2)
+            return (xqw, t["W1_memo"], t["b1_memo"], t["W2_memo"], t["b2_memo"])
+
+    saved = ttt_layer.mlp_cached_readout_triton, ttt_layer.TritonMLP
+    ttt_layer.mlp_cached_readout_triton, ttt_layer.TritonMLP = readout, StubMLP
+    try:
+        layer = types.SimpleNamespace(
+            W1=torch.zeros(1, F, FF), b1=torch.zeros(1, 1, FF), W2=torch.zeros(1, FF, F), b2=torch.zeros(1, 1, F),
+            ttt_norm_weight=t["ln_w"], ttt_norm_bias=t["ln_b"], use_kernel=True, width=F,
+            config=types.SimpleNamespace(scan_checkpoint_group_size=1, mem_cache_segment_n_mini_batches=M))
+        inputs = {"XQ": t["XQ"], "XK": leaves["XK"], "XV": t["XQ"], "XU": leaves["XU"],
+                  "eta": torch.zeros(1, 1, NC, 16, 16)}
+        out = ttt_layer.TTTMLP.ttt(layer, inputs)  # [B, L, NH * F]
+        out.backward(dO)
+    finally:
+        ttt_layer.mlp_cached_readout_triton, ttt_layer.TritonMLP = saved
+    res = {"in_" + k: v for k, v in t.items()}
+    res.update({"M": torch.tensor(M), "dO": dO.reshape(1, NC, 16, 1, F).permute(0, 3, 1, 2, 4),
+                "out": out.detach().reshape(1, NC, 16, 1, F).permute(0, 3, 1, 2, 4)})
+    res.update({"grad_" + k: v.grad for k, v in leaves.items()})
+    return {k: _np(v) for k, v in res.items()}
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     sys.path.insert(0, ref_root)
@@ -134,6 +204,7 @@ def main():
         "mlp_small": mlp_case(ref_ops, B=2, NH=2, NC=3, F=16, FF=64, ckpt=2, eta_mode="causal", seed=20),
         "mlp_fxf_equal_eta": mlp_case(ref_ops, B=1, NH=2, NC=3, F=32, FF=32, ckpt=16, eta_mode="equal", seed=21),
         "cached_readout": cached_readout_case(ref_root, NCs=3, F=32, FF=128, seed=30),
+        "memo_mix": memo_mix_case(ref_root, NC=7, F=32, FF=128, M=2, seed=40),
     }
     for name, res in cases.items():
         path = os.path.join(HERE, name + ".npz")

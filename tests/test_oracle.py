@@ -57,6 +57,17 @@ def test_cached_readout_oracle_matches_reference_kernel():
 
 @pytest.mark.parametrize("eta_mode", ["causal", "equal"])
 @pytest.mark.parametrize("ckpt", [1, 3, 16])
+def test_memo_mix_oracle_matches_reference_loop():
+    """The memo-state mixing restatement against the reference's own loop (TTTMLP.ttt run
+    with its Triton cached read-out under the interpreter), output and gradients."""
+    inp, g = load_golden("memo_mix")
+    inp = {k: v.double() for k, v in inp.items()}
+    grads, out = O.memo_mix_grads(inp, g["dO"].double(), int(g["M"]))
+    assert O.rel_l2(out, g["out"].double()) < 1e-6
+    for k in O.MEMO_MIX_GRAD_NAMES:
+        assert O.rel_l2(grads[k], g["grad_" + k].double()) < 1e-6, k
+
+
 def test_linear_hand_backward_matches_autograd(eta_mode, ckpt):
     d = S.perturb_params(S.make_linear_inputs(2, 2, 7, 16, 32, eta_mode=eta_mode), seed=5)
     d = {k: v.double() for k, v in d.items()}
