@@ -55,8 +55,6 @@ def test_cached_readout_oracle_matches_reference_kernel():
     assert O.rel_l2(out, g["out"]) < 1e-6
 
 
-@pytest.mark.parametrize("eta_mode", ["causal", "equal"])
-@pytest.mark.parametrize("ckpt", [1, 3, 16])
 def test_memo_mix_oracle_matches_reference_loop():
     """The memo-state mixing restatement against the reference's own loop (TTTMLP.ttt run
     with its Triton cached read-out under the interpreter), output and gradients."""
@@ -68,6 +66,8 @@ def test_memo_mix_oracle_matches_reference_loop():
         assert O.rel_l2(grads[k], g["grad_" + k].double()) < 1e-6, k
 
 
+@pytest.mark.parametrize("eta_mode", ["causal", "equal"])
+@pytest.mark.parametrize("ckpt", [1, 3, 16])
 def test_linear_hand_backward_matches_autograd(eta_mode, ckpt):
     d = S.perturb_params(S.make_linear_inputs(2, 2, 7, 16, 32, eta_mode=eta_mode), seed=5)
     d = {k: v.double() for k, v in d.items()}
