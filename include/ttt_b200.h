@@ -156,6 +156,30 @@ int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_gro
                 void* stream);
 
 /*
+ * Memo-state mixing of the TTT-MLP layer's output: the segment loop of ttt_layer.py:503-559
+ * (per segment i >= 1, softmax over <XU, summary_j> weighting the online output XQW and the
+ * cached read-outs of memo states 0..i-1, each one launch of mlp_cached_readout_triton in the
+ * reference) as one launch sequence. XQW, XQ, XK, XU, out / dOut, dXQW, dXU, dXK are
+ * [B, NH, NC, CS, F] contiguous in one 16-bit type (dt); memo states [B, NH, NS, ...] fp32 as
+ * ttt_mlp_fwd writes them, NS = ceil(NC / memo_segment_size). Tensor-core path: CS = 16,
+ * F = 64, FF = 256, NS <= 64. The backward gives dXQW, dXU and the summary part of dXK (the
+ * cached read-outs and earlier summaries carry no gradient, as in the reference). Scratch:
+ * ttt_memo_mix_scratch_bytes() bytes, 16-byte aligned.
+ */
+size_t ttt_memo_mix_scratch_bytes(int B, int NH, int NC, int memo_segment_size);
+int ttt_memo_mix_fwd(int B, int NH, int NC, int CS, int F, int FF, int memo_segment_size,
+                     const void* XQW, const void* XQ, const void* XK, const void* XU, int dt,
+                     const float* W1_memo, const float* b1_memo, const float* W2_memo, const float* b2_memo,
+                     const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
+                     void* out, void* scratch, size_t scratch_bytes, void* stream);
+int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, int memo_segment_size,
+                     const void* XQW, const void* XQ, const void* XK, const void* XU, int dt,
+                     const float* W1_memo, const float* b1_memo, const float* W2_memo, const float* b2_memo,
+                     const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
+                     const void* dOut, void* dXQW, void* dXU, void* dXK,
+                     void* scratch, size_t scratch_bytes, void* stream);
+
+/*
  * Reads and clears this library's device error word for the current device, synchronising
  * with it. Non-zero bits mean a kernel gave up waiting for its own asynchronous copies
  * (bit 0: a TMA stage did not land within 2 s) and voided the affected streams' results.

@@ -105,3 +105,20 @@ def test_mlp_saved_preactivations_all_or_none():
 
 def test_device_status_rejects_null():
     assert _lib.lib.ttt_device_status(None) == -1
+
+
+def test_memo_mix_host_checks():
+    P = [FAKE] * 4
+
+    def fwd(NC, M, F=64, dt=1, scratch=FAKE, nbytes=1 << 40):
+        return _lib.lib.ttt_memo_mix_fwd(1, 1, NC, 16, F, 256, M, *P, dt, *P, FAKE, FAKE, 1, FAKE, scratch, nbytes,
+                                         None)
+
+    assert fwd(8, 0) == -2
+    assert fwd(8, 2, F=32) == -4 and "F = 64" in _lib.lib.ttt_last_error().decode()
+    assert fwd(130, 2) == -4 and "at most 64" in _lib.lib.ttt_last_error().decode()
+    assert fwd(8, 2, dt=0) == -3
+    assert fwd(8, 2, scratch=None) == -1
+    assert fwd(8, 2, nbytes=16) == -5
+    # W1/W2 16-bit copies (2 * F * FF * 2 bytes) plus summary and its gradient (2 * F * 4) per memo state
+    assert _lib.lib.ttt_memo_mix_scratch_bytes(2, 3, 9, 4) == 2 * 3 * 3 * (2 * 64 * 256 * 2 + 2 * 64 * 4)

@@ -1,0 +1,64 @@
+"""GPU parity of the fused memo-state mixing (ttt_layer.py:503-559) against the oracle."""
+
+import pytest
+import torch
+
+import _core
+import synthetic as S
+import ttt_oracle as O
+from helpers import assert_close, oracle_inputs
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+SCAN = ("ln_w", "ln_b", "W1", "b1", "W2", "b2", "XQ", "XV", "XK", "eta")
+
+
+def make(B, NH, NC, M, dtype, seed):
+    d = S.perturb_params(S.make_mlp_inputs(B, NH, NC, 16, 64, 256, seed=seed), seed=seed + 1)
+    d = {k: (v.to(dtype) if k in ("XQ", "XV", "XK", "eta") else v) for k, v in d.items()}
+    od = oracle_inputs(d)
+    r = O.mlp_scan(*(od[k] for k in SCAN), 1, M)
+    g = torch.Generator().manual_seed(seed + 2)
+    XU = (torch.randn(B, NH, NC, 16, 64, generator=g)).to(dtype)
+    inp = {"XQW": r["XQW"].to(dtype), "XQ": d["XQ"], "XK": d["XK"], "XU": XU,
+           "W1_memo": r["W1_memo"].float(), "b1_memo": r["b1_memo"].float(), "W2_memo": r["W2_memo"].float(),
+           "b2_memo": r["b2_memo"].float(), "ln_w": d["ln_w"], "ln_b": d["ln_b"]}
+    return inp
+
+
+ORDER = ("XQW", "XQ", "XK", "XU", "W1_memo", "b1_memo", "W2_memo", "b2_memo", "ln_w", "ln_b")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(1, 2, 7, 2), (1, 1, 40, 16), (2, 1, 9, 3)])
+def test_memo_mix_matches_oracle(dtype, shape):
+    """Forward and gradients (XQW, XU, XK), including segments of 256 tokens (two 128-token
+    tiles) and a ragged last segment."""
+    B, NH, NC, M = shape
+    inp = make(B, NH, NC, M, dtype, seed=NC + M)
+    dO = S.make_upstream((B, NH, NC, 16, 64), seed=3).to(dtype)
+    from kernels.mlp_memo_mix import mlp_memo_mix
+
+    leaves = {k: (v.to(DEV).requires_grad_(k in ("XQW", "XU", "XK")) if v.is_floating_point() else v.to(DEV))
+              for k, v in inp.items()}
+    out = mlp_memo_mix(*(leaves[k] for k in ORDER), M)
+    out.backward(dO.to(DEV))
+    ref_g, ref = O.memo_mix_grads({k: v.double() for k, v in inp.items()}, dO.double(), M)
+    assert out.dtype == dtype and out.shape == inp["XQW"].shape
+    assert_close("out", out, ref, 2e-2)
+    for k in ("XQW", "XU", "XK"):
+        assert_close("d" + k, leaves[k].grad, ref_g[k], 2e-2)
+    # segment 0 passes through unchanged
+    assert torch.equal(out[:, :, :M].cpu(), inp["XQW"][:, :, :M])
+
+
+def test_memo_mix_rejects_unsupported_shapes_and_no_wait_gave_up():
+    import _lib
+
+    inp = make(1, 1, 4, 2, torch.bfloat16, seed=7)
+    dev = {k: v.to(DEV) for k, v in inp.items()}
+    with pytest.raises(ValueError, match="memo_segment_size"):
+        _core.memo_mix_forward(*(dev[k] for k in ORDER), 0)
+    _lib.device_status()
+    _core.memo_mix_forward(*(dev[k] for k in ORDER), 2)
+    assert _lib.device_status() == 0

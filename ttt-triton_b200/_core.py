@@ -286,3 +286,66 @@ def mlp_cached_readout(XQ_seg, W1, b1, W2, b2, ln_w, ln_b):
     )
     check(rc, "ttt_mlp_cached_readout")
     return out
+
+
+# --------------------------------------------------------------------------- memo mixing
+def _memo_args(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, memo_segment_size):
+    require_cuda(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b)
+    if XQW.dim() != 5:
+        raise ValueError(f"XQW must be [B, NH, NC, CS, F], got {tuple(XQW.shape)}")
+    B, NH, NC, CS, F = XQW.shape
+    for name, t in (("XQ", XQ), ("XK", XK), ("XU", XU)):
+        if tuple(t.shape) != tuple(XQW.shape):
+            raise ValueError(f"{name} must have XQW's shape {tuple(XQW.shape)}, got {tuple(t.shape)}")
+        if t.dtype != XQW.dtype:
+            raise ValueError(f"{name} must have XQW's dtype {XQW.dtype}, got {t.dtype}")
+    M = int(memo_segment_size)
+    if M <= 0:
+        raise ValueError(f"memo_segment_size must be positive, got {M}")
+    NS = math.ceil(NC / M)
+    FF = W1_memo.shape[-1]
+    mem = (_state(W1_memo, (B, NH, NS, F, FF), "W1_memo"), _state(b1_memo, (B, NH, NS, 1, FF), "b1_memo"),
+           _state(W2_memo, (B, NH, NS, FF, F), "W2_memo"), _state(b2_memo, (B, NH, NS, 1, F), "b2_memo"))
+    ln_w, ln_b = _check_ln(ln_w, ln_b, NH, F)
+    return (B, NH, NC, CS, F, FF, M), (_c(XQW), _c(XQ), _c(XK), _c(XU)), mem, ln_w, ln_b
+
+
+def memo_mix_forward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, memo_segment_size):
+    """Memo-state mixing of the TTT-MLP output (ttt_layer.py:503-559) as one launch sequence.
+    Returns the mixed output in XQW's dtype and layout [B, NH, NC, CS, F]."""
+    dims, acts, mem, ln_w, ln_b = _memo_args(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b,
+                                             memo_segment_size)
+    B, NH, NC, CS, F, FF, M = dims
+    XQW, XQ, XK, XU = acts
+    out = torch.empty_like(XQW)
+    nbytes = lib.ttt_memo_mix_scratch_bytes(B, NH, NC, M)
+    scratch = torch.empty(max(nbytes, 1), device=XQW.device, dtype=torch.uint8)
+    rc = lib.ttt_memo_mix_fwd(
+        B, NH, NC, CS, F, FF, M, ptr(XQW), ptr(XQ), ptr(XK), ptr(XU), dtype_code(XQW),
+        *[ptr(t) for t in mem], ptr(ln_w), ptr(ln_b), dtype_code(ln_w),
+        ptr(out), ptr(scratch), nbytes, stream_of(XQW),
+    )
+    check(rc, "ttt_memo_mix_fwd")
+    return out
+
+
+def memo_mix_backward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, memo_segment_size, dOut):
+    """Gradients of the memo mixing: (dXQW, dXU, dXK), dXK being the part through the
+    segment summaries (the cached read-outs carry none, ttt_layer.py:542)."""
+    dims, acts, mem, ln_w, ln_b = _memo_args(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b,
+                                             memo_segment_size)
+    B, NH, NC, CS, F, FF, M = dims
+    XQW, XQ, XK, XU = acts
+    if tuple(dOut.shape) != tuple(XQW.shape):
+        raise ValueError(f"upstream gradient must have XQW's shape {tuple(XQW.shape)}, got {tuple(dOut.shape)}")
+    dOut = _c(dOut.to(XQW.dtype))
+    dXQW, dXU, dXK = torch.empty_like(XQW), torch.empty_like(XQW), torch.empty_like(XQW)
+    nbytes = lib.ttt_memo_mix_scratch_bytes(B, NH, NC, M)
+    scratch = torch.empty(max(nbytes, 1), device=XQW.device, dtype=torch.uint8)
+    rc = lib.ttt_memo_mix_bwd(
+        B, NH, NC, CS, F, FF, M, ptr(XQW), ptr(XQ), ptr(XK), ptr(XU), dtype_code(XQW),
+        *[ptr(t) for t in mem], ptr(ln_w), ptr(ln_b), dtype_code(ln_w),
+        ptr(dOut), ptr(dXQW), ptr(dXU), ptr(dXK), ptr(scratch), nbytes, stream_of(XQW),
+    )
+    check(rc, "ttt_memo_mix_bwd")
+    return dXQW, dXU, dXK

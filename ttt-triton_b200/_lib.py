@@ -58,6 +58,9 @@ _SIGNATURES = {
         _I,
     ),
     "ttt_device_status": ([_P], _I),
+    "ttt_memo_mix_scratch_bytes": ([_I] * 4, _Z),
+    "ttt_memo_mix_fwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P, _P, _Z, _P], _I),
+    "ttt_memo_mix_bwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P] * 4 + [_P, _Z, _P], _I),
     "ttt_mlp_cached_readout": (
         [_I] * 6 + [_P, _I] + [_P, _L, _L] * 4 + [_P, _P, _I, _P, _P],
         _I,

@@ -53,21 +53,27 @@ static EncodeTiledFn encode_tiled(const char* who) {
   return fn;
 }
 
-int make_tile_map(CUtensorMap* map, const void* base, int dtype_code, unsigned long long rows, const char* who,
-                  unsigned box_rows) {
+int make_map_2d(CUtensorMap* map, const void* base, int dtype_code, unsigned long long cols, unsigned long long rows,
+                unsigned long long row_stride_bytes, unsigned box_cols, unsigned box_rows, bool swizzle128,
+                const char* who) {
   EncodeTiledFn fn = encode_tiled(who);
   if (!fn) return TTT_ERR_CUDA;
-  const cuuint64_t dims[2] = {64, rows};
-  const cuuint64_t strides[1] = {128};  // bytes between rows
-  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUtensorMapDataType dt =
       dtype_code == DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TTT_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", who, (int)r);
   return TTT_OK;
+}
+
+int make_tile_map(CUtensorMap* map, const void* base, int dtype_code, unsigned long long rows, const char* who,
+                  unsigned box_rows) {
+  return make_map_2d(map, base, dtype_code, 64, rows, 128, 64, box_rows, true, who);
 }
 
 }  // namespace ttt

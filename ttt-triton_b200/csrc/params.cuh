@@ -129,6 +129,32 @@ struct MlpBwdParams {
   const float* W2_last;
 };
 
+// Memo-state mixing (ttt_layer.py:503-559); activations [B,NH,NC,16,64] in one 16-bit type.
+struct MemoMixParams {
+  int B, NH, NC, M, NS, TILES;  // M = memo_segment_size, NS = ceil(NC / M), TILES = 128-token tiles per segment
+  int dt_ln;
+  const void* XQW;
+  const void* XQ;
+  const void* XK;
+  const void* XU;
+  const float* W1_memo;  // [B,NH,NS,F,FF]
+  const float* b1_memo;  // [B,NH,NS,1,FF]
+  const float* W2_memo;  // [B,NH,NS,FF,F]
+  const float* b2_memo;  // [B,NH,NS,1,F]
+  const void* ln_w;
+  const void* ln_b;
+  void* out;             // forward
+  const void* dOut;      // backward
+  void* dXQW;
+  void* dXU;
+  void* dXK;
+  void* W1T;             // scratch: 16-bit [B,NH,NS,FF,F]
+  void* W2T;             // scratch: 16-bit [B,NH,NS,F,FF]
+  float* summary;        // scratch: [B,NH,NS,F]
+  float* dsum;           // scratch: [B,NH,NS,F] (backward)
+  unsigned int* err;
+};
+
 struct ReadoutParams {
   int B, NH, NCs, CS, F, FF;
   const void* XQ;

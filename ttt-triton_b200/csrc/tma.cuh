@@ -83,6 +83,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
 int make_tile_map(CUtensorMap* map, const void* base, int dtype_code, unsigned long long rows, const char* who,
                   unsigned box_rows = 16);
 
+// General 2-D tensor map over a row-major 16-bit matrix [rows][cols] (row stride in bytes, a
+// multiple of 16) read in box_rows x box_cols boxes; swizzle128 selects the 128-byte swizzle
+// (box_cols * 2 must then be 128).
+int make_map_2d(CUtensorMap* map, const void* base, int dtype_code, unsigned long long cols, unsigned long long rows,
+                unsigned long long row_stride_bytes, unsigned box_cols, unsigned box_rows, bool swizzle128,
+                const char* who);
+
 // Device address of the library's device error word on the current device.
 int device_error_word(unsigned int** out, const char* who);
 

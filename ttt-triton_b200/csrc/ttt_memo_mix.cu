@@ -1,0 +1,581 @@
+// Memo-state mixing of the TTT-MLP layer's output (ttt_layer.py:503-559) in one launch, on
+// the 5th-generation tensor cores.
+//
+// Segment i of a stream covers mini-batches [i M, min((i+1) M, NC)) (M = memo_segment_size).
+// For i >= 1 every token t of the segment mixes
+//   out_t = g_i(t) XQW_t + sum_{j<i} g_j(t) R_j(XQ_t),   g = softmax_j(<XU_t, summary_j>),
+// where summary_j is the mean of segment j's XK and R_j the cached read-out of memo state j:
+// R_j(x) = x + LN(gelu(x W1_j + b1_j) W2_j + b2_j) (LayerNorm eps 1e-6,
+// kernels/mlp_cached_readout.py:88-101). Segment 0 passes through.
+//
+// Kernels:
+//   memo_prep   one CTA per (stream, memo state j): 16-bit K-major copies of W1_j^T [FF][F]
+//               and W2_j^T [F][FF] (the tensor-core B operands) and summary_j.
+//   memo_mix    one CTA (8 warps) per (stream, segment, 128-token tile), heavy segments
+//               first. Per earlier state j:
+//                 Z1 = XQ W1_j      128 x 256 x 64 tcgen05.mma into tensor memory
+//                 X2 = gelu(Z1+b1)  all warps: 32-column TMEM loads, 16-bit K-major
+//                                   swizzled tiles in shared memory
+//                 Z2 = X2 W2_j      128 x 64 x 256 tcgen05.mma
+//                 R_j              warps 0-3, one token per thread: LayerNorm in registers
+//               forward: accumulate g_j R_j; backward: dg_j = <dOut_t, R_j(t)>.
+//               W1_j / W2_j arrive by TMA (128-byte swizzle) as soon as the previous
+//               product that read their buffer completes; the product for j+1 is issued
+//               behind the one for j, so the tensor cores work under the epilogues.
+//   memo_dxk    backward only: dXK of segment i's tokens = d summary_i / (tokens in i).
+// Backward of the mixing (the read-outs carry no gradient, ttt_layer.py:542): dXQW =
+// g_i dOut; ds_j = g_j (dg_j - sum_k g_k dg_k); dXU = sum_j ds_j summary_j; d summary_i =
+// sum_t ds_i(t) XU_t (the earlier summaries enter detached).
+#include <type_traits>
+
+#include "capi_common.cuh"
+#include "common.cuh"
+#include "mma.cuh"
+#include "params.cuh"
+#include "tc_util.cuh"
+#include "tma.cuh"
+#include "tmem.cuh"
+#include "umma.cuh"
+
+namespace ttt {
+namespace memo {
+
+constexpr int F = 64, FF = 256, C = 16, ROWS = 128, NW = 8, NTHREADS = 32 * NW, NS_MAX = 64;
+constexpr float kReadoutEps = 1e-6f;  // kernels/mlp_cached_readout.py:99
+// shared memory (1024-byte aligned base)
+constexpr int OFF_XQ = 0;                          // [128][64] 16-bit, K-major 128-byte swizzle
+constexpr int OFF_W1 = OFF_XQ + ROWS * F * 2;      // [256][64]: W1_j^T
+constexpr int OFF_W2 = OFF_W1 + FF * F * 2;        // 4 x [64][64]: W2_j^T, K chunks of 64
+constexpr int OFF_X2 = OFF_W2 + F * FF * 2;        // 4 x [128][64]: gelu(Z1 + b1), K chunks of 64
+constexpr int OFF_G = OFF_X2 + ROWS * FF * 2;      // fp32 [128][NS_MAX]: mixing weights g_j(t)
+constexpr int OFF_DG = OFF_G + ROWS * NS_MAX * 4;  // fp32 [128][NS_MAX]: dg_j(t) (backward)
+constexpr int OFF_LN = OFF_DG + ROWS * NS_MAX * 4; // fp32 [2][64]: LayerNorm weight, bias
+constexpr int SMEM = OFF_LN + 2 * F * 4 + 1024;    // + slack to align the base
+constexpr uint32_t TMEM_COLS = 512;                // Z1: columns 0-255, Z2: 256-319
+constexpr uint32_t XQ_BYTES = ROWS * F * 2, W1_BYTES = FF * F * 2, W2_BYTES = F * FF * 2;
+static_assert(OFF_W1 % 1024 == 0 && OFF_W2 % 1024 == 0 && OFF_X2 % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+
+struct Maps {
+  CUtensorMap xq;  // XQ rows, 128-row boxes
+  CUtensorMap w1;  // W1^T copies [B*NH*NS*256][64], 256-row boxes
+  CUtensorMap w2;  // W2^T copies [B*NH*NS*64][256], 64 x 64 boxes
+};
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------- prep
+template <typename T>
+__global__ void __launch_bounds__(256) memo_prep_kernel(MemoMixParams p) {
+  using H = Half2<T>;
+  const long long sj = blockIdx.x;  // (stream, memo state)
+  const long long s = sj / p.NS;
+  const int j = (int)(sj % p.NS);
+  const float* W1 = p.W1_memo + sj * F * FF;  // [F][FF]
+  const float* W2 = p.W2_memo + sj * FF * F;  // [FF][F]
+  T* W1T = reinterpret_cast<T*>(p.W1T) + sj * FF * F;  // [FF][F]
+  T* W2T = reinterpret_cast<T*>(p.W2T) + sj * F * FF;  // [F][FF]
+  __shared__ float tile[64][65];
+  // W1^T: four 64 x 64 blocks (ff block), transposed through shared memory
+  for (int blk = 0; blk < FF / 64; ++blk) {
+    for (int i = threadIdx.x; i < 64 * 64; i += 256) tile[i / 64][i % 64] = W1[(i / 64) * FF + blk * 64 + i % 64];
+    __syncthreads();
+    for (int i = threadIdx.x; i < 32 * 64; i += 256) {
+      const int r = i / 32, c = 2 * (i % 32);  // W1T row blk*64 + r, features c, c+1
+      *reinterpret_cast<uint32_t*>(W1T + (blk * 64 + r) * F + c) = H::pack(tile[c][r], tile[c + 1][r]);
+    }
+    __syncthreads();
+  }
+  for (int blk = 0; blk < FF / 64; ++blk) {
+    for (int i = threadIdx.x; i < 64 * 64; i += 256) tile[i / 64][i % 64] = W2[(blk * 64 + i / 64) * F + i % 64];
+    __syncthreads();
+    for (int i = threadIdx.x; i < 32 * 64; i += 256) {
+      const int r = i / 32, c = 2 * (i % 32);  // W2T row r (feature), hidden blk*64 + c, c+1
+      *reinterpret_cast<uint32_t*>(W2T + r * FF + blk * 64 + c) = H::pack(tile[c][r], tile[c + 1][r]);
+    }
+    __syncthreads();
+  }
+  // summary_j = mean of segment j's XK rows
+  const int n0 = j * p.M, n1 = min((j + 1) * p.M, p.NC);
+  const long long r0 = (s * p.NC + n0) * C, nrows = (long long)(n1 - n0) * C;
+  const T* XK = reinterpret_cast<const T*>(p.XK);
+  float* red = &tile[0][0];
+  const int f = threadIdx.x & 63, part = threadIdx.x >> 6;
+  float acc = 0.f;
+  for (long long r = part; r < nrows; r += 4) acc += (float)XK[(r0 + r) * F + f];
+  red[part * 64 + f] = acc;
+  __syncthreads();
+  if (threadIdx.x < 64)
+    p.summary[sj * F + f] = (red[f] + red[64 + f] + red[128 + f] + red[192 + f]) / (float)nrows;
+}
+
+// ---------------------------------------------------------------------------------- mix
+// blockIdx.x -> (stream, segment, tile) with the heaviest segments first.
+__device__ __forceinline__ void decode_block(const MemoMixParams& p, long long& s, int& seg, int& tile) {
+  const long long per_seg = (long long)p.B * p.NH * p.TILES;
+  const long long b = blockIdx.x;
+  seg = p.NS - 1 - (int)(b / per_seg);
+  const long long r = b % per_seg;
+  s = r / p.TILES;
+  tile = (int)(r % p.TILES);
+}
+
+template <typename T, bool BWD>
+__global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, const __grid_constant__ Maps maps) {
+  using H = Half2<T>;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ __align__(8) uint64_t bars[5];  // XQ, W1, W2 landed; product 1, product 2 complete
+  __shared__ int abort_sh;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  long long s;
+  int seg, tile;
+  decode_block(p, s, seg, tile);
+  const int n0 = seg * p.M, n1 = min((seg + 1) * p.M, p.NC);
+  const int seg_rows = (n1 - n0) * C;
+  const int row0 = tile * ROWS;  // first token of the tile within the segment
+  if (row0 >= seg_rows) return;  // empty tail tile (uniform over the CTA)
+  const long long tok0 = (s * p.NC + n0) * C + row0;  // global token index of row 0
+  const int nrows = min(ROWS, seg_rows - row0);
+  const T* XQW = reinterpret_cast<const T*>(p.XQW);
+  const T* XU = reinterpret_cast<const T*>(p.XU);
+
+  if (seg == 0) {  // passes through (forward: out = XQW; backward: dXQW = dOut, dXU = 0)
+    const T* src = reinterpret_cast<const T*>(BWD ? p.dOut : p.XQW);
+    T* dst = reinterpret_cast<T*>(BWD ? p.dXQW : p.out);
+    for (int i = tid; i < nrows * F; i += NTHREADS) dst[tok0 * F + i] = src[tok0 * F + i];
+    if (BWD)
+      for (int i = tid; i < nrows * F; i += NTHREADS) reinterpret_cast<T*>(p.dXU)[tok0 * F + i] = H::from_float(0.f);
+    return;
+  }
+
+  const uint32_t sXQ = smem_u32(smem + OFF_XQ), sW1 = smem_u32(smem + OFF_W1), sW2 = smem_u32(smem + OFF_W2);
+  const uint32_t sX2 = smem_u32(smem + OFF_X2);
+  float* G = reinterpret_cast<float*>(smem + OFF_G);
+  float* DG = reinterpret_cast<float*>(smem + OFF_DG);
+  float* LN = reinterpret_cast<float*>(smem + OFF_LN);
+  const uint32_t b_xq = smem_u32(&bars[0]), b_w1 = smem_u32(&bars[1]), b_w2 = smem_u32(&bars[2]);
+  const uint32_t b_p1 = smem_u32(&bars[3]), b_p2 = smem_u32(&bars[4]);
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  const uint32_t idesc1 = umma_idesc_f32(kBf16, ROWS, FF), idesc2 = umma_idesc_f32(kBf16, ROWS, F);
+  const int h = (int)(s % p.NH);
+  const int nstate = seg;  // memo states 0 .. seg-1 are read out
+
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_sh, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (tid == 32) {
+    for (int i = 0; i < 5; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    abort_sh = 0;
+    fence_mbar_init();
+  }
+  if (tid < 2 * F) LN[tid] = ld_elem(tid < F ? p.ln_w : p.ln_b, (long long)h * F + (tid % F), p.dt_ln);
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tZ1 = tmem_base_sh, tZ2 = tmem_base_sh + 256;
+
+  auto load_w1 = [&](int j) {
+    mbar_expect_tx(b_w1, W1_BYTES);
+    tma_load_2d(sW1, &maps.w1, 0, (int)((s * p.NS + j) * FF), b_w1);
+  };
+  auto load_w2 = [&](int j) {
+    mbar_expect_tx(b_w2, W2_BYTES);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) tma_load_2d(sW2 + a * (F * 64 * 2), &maps.w2, 64 * a, (int)((s * p.NS + j) * F), b_w2);
+  };
+  auto product1 = [&]() {  // Z1 = XQ W1_j  (K = 64)
+    tmem_fence_after();
+    const uint64_t da = umma_desc_k_sw128(sXQ), db = umma_desc_k_sw128(sW1);
+#pragma unroll
+    for (int k = 0; k < F / 16; ++k) umma_ss(tZ1, da + 2 * k, db + 2 * k, idesc1, k > 0);
+    umma_commit(b_p1);
+  };
+  auto product2 = [&]() {  // Z2 = X2 W2_j  (K = 256 in four 64-wide chunks)
+    tmem_fence_after();
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const uint64_t da = umma_desc_k_sw128(sX2 + a * (ROWS * 64 * 2)), db = umma_desc_k_sw128(sW2 + a * (F * 64 * 2));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) umma_ss(tZ2, da + 2 * k, db + 2 * k, idesc2, (a | k) != 0);
+    }
+    umma_commit(b_p2);
+  };
+  auto wait = [&](uint32_t bar, int phase) {
+    if (!abort_sh && !mbar_wait(bar, (uint32_t)(phase & 1), p.err)) abort_sh = 1;
+  };
+
+  // copy thread (0): XQ tile and the first weights
+  if (tid == 0) {
+    mbar_expect_tx(b_xq, XQ_BYTES);
+    tma_load_2d(sXQ, &maps.xq, 0, (int)tok0, b_xq);
+    load_w1(0);
+    load_w2(0);
+  }
+  // mixing weights g_j(t), j = 0..seg (threads 0-127, one token each)
+  const int r = tid;  // row of threads 0-127
+  if (tid < ROWS && r < nrows) {
+    float xu[F];
+#pragma unroll
+    for (int c = 0; c < F; c += 2) {
+      const float2 v = H::unpack(*reinterpret_cast<const uint32_t*>(XU + (tok0 + r) * F + c));
+      xu[c] = v.x;
+      xu[c + 1] = v.y;
+    }
+    float mx = -INFINITY;
+    for (int j = 0; j <= seg; ++j) {
+      const float* sm = p.summary + (s * p.NS + j) * F;
+      float d = 0.f;
+#pragma unroll
+      for (int c = 0; c < F; ++c) d += xu[c] * __ldg(sm + c);
+      G[r * NS_MAX + j] = d;
+      mx = fmaxf(mx, d);
+    }
+    float tot = 0.f;
+    for (int j = 0; j <= seg; ++j) {
+      const float e = __expf(G[r * NS_MAX + j] - mx);
+      G[r * NS_MAX + j] = e;
+      tot += e;
+    }
+    const float inv = 1.f / tot;
+    for (int j = 0; j <= seg; ++j) G[r * NS_MAX + j] *= inv;
+  }
+  if (tid == 0) {
+    wait(b_xq, 0);
+    wait(b_w1, 0);
+    if (!abort_sh) product1();
+  }
+  __syncthreads();  // mixing weights written; the XQ tile is in shared memory
+
+  float acc[F];   // forward: sum_j g_j R_j;  backward: dOut row
+  float xq[F];    // XQ row
+  if (tid < ROWS) {
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      const uint4 u = *reinterpret_cast<const uint4*>(smem + OFF_XQ + swz128(r, ch));
+      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 v = H::unpack(w4[k]);
+        xq[8 * ch + 2 * k] = v.x;
+        xq[8 * ch + 2 * k + 1] = v.y;
+      }
+    }
+    const T* dO = reinterpret_cast<const T*>(p.dOut);
+#pragma unroll
+    for (int c = 0; c < F; c += 2) {
+      if (BWD && r < nrows) {
+        const float2 v = H::unpack(*reinterpret_cast<const uint32_t*>(dO + (tok0 + r) * F + c));
+        acc[c] = v.x;
+        acc[c + 1] = v.y;
+      } else {
+        acc[c] = acc[c + 1] = 0.f;
+      }
+    }
+  }
+
+  for (int j = 0; j < nstate; ++j) {
+    // ---- X2 = gelu(Z1 + b1_j): warp w reads lanes of quadrant w % 4, columns 128 (w / 4) ..
+    if (lane == 0) wait(b_p1, j);
+    __syncwarp();
+    tmem_fence_after();
+    if (tid == 0 && j + 1 < nstate && !abort_sh) load_w1(j + 1);  // product 1 of j no longer reads W1
+    {
+      const int q = warp & 3, hc = warp >> 2, row = 32 * q + lane;
+      const float* b1 = p.b1_memo + (s * p.NS + j) * FF;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        const int col = 128 * hc + 32 * c4;
+        float z[32];
+        tmem_ld32(tmem_lane_addr(tZ1, warp, col), z);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const float2 bb = __ldg(reinterpret_cast<const float2*>(b1 + col + 2 * u));
+          const float2 g = gelu2(make_float2(z[2 * u] + bb.x, z[2 * u + 1] + bb.y));
+          pk[u] = H::pack(g.x, g.y);
+        }
+        const int atom = col / 64, ch0 = (col % 64) / 8;
+        uint8_t* base = smem + OFF_X2 + atom * (ROWS * 64 * 2);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          *reinterpret_cast<uint4*>(base + swz128(row, ch0 + u)) =
+              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+      }
+    }
+    fence_proxy_async();  // X2 stores -> visible to the tensor cores
+    tmem_fence_before();
+    __syncthreads();
+    if (tid == 0 && !abort_sh) {
+      wait(b_w2, j);
+      if (!abort_sh) product2();
+      if (j + 1 < nstate) {
+        wait(b_w1, j + 1);
+        if (!abort_sh) product1();  // Z1 of j has been read by every warp
+      }
+    }
+    // ---- R_j = XQ + LN(Z2 + b2_j) (warps 0-3, one token per thread)
+    if (warp < 4) {
+      if (lane == 0) wait(b_p2, j);
+      __syncwarp();
+      tmem_fence_after();
+      float z[F];
+      tmem_ld32(tmem_lane_addr(tZ2, warp, 0), z);
+      tmem_ld32(tmem_lane_addr(tZ2, warp, 32), z + 32);
+      tmem_wait_ld();
+      if (tid == 0 && j + 1 < nstate && !abort_sh) load_w2(j + 1);  // product 2 of j no longer reads W2
+      const float* b2 = p.b2_memo + (s * p.NS + j) * F;
+      float mu = 0.f;
+#pragma unroll
+      for (int c = 0; c < F; ++c) {
+        z[c] += __ldg(b2 + c);
+        mu += z[c];
+      }
+      mu *= 1.f / F;
+      float var = 0.f;
+#pragma unroll
+      for (int c = 0; c < F; ++c) {
+        z[c] -= mu;
+        var += z[c] * z[c];
+      }
+      const float rstd = 1.f / sqrtf(var * (1.f / F) + kReadoutEps);
+      if (!BWD) {
+        const float gj = r < nrows ? G[r * NS_MAX + j] : 0.f;
+#pragma unroll
+        for (int c = 0; c < F; ++c) acc[c] += gj * (xq[c] + LN[c] * z[c] * rstd + LN[F + c]);
+      } else {
+        float d = 0.f;
+#pragma unroll
+        for (int c = 0; c < F; ++c) d += acc[c] * (xq[c] + LN[c] * z[c] * rstd + LN[F + c]);
+        if (r < nrows) DG[r * NS_MAX + j] = d;
+      }
+    }
+    tmem_fence_before();
+  }
+
+  // ---- tail (threads 0-127, one token each)
+  if (tid < ROWS && r < nrows) {
+    const long long o = (tok0 + r) * F;
+    const float gi = G[r * NS_MAX + seg];
+    if (!BWD) {
+      T* out = reinterpret_cast<T*>(p.out);
+#pragma unroll
+      for (int c = 0; c < F; c += 2) {
+        const float2 w = H::unpack(*reinterpret_cast<const uint32_t*>(XQW + o + c));
+        *reinterpret_cast<uint32_t*>(out + o + c) = H::pack(acc[c] + gi * w.x, acc[c + 1] + gi * w.y);
+      }
+    } else {
+      float dgi = 0.f;
+#pragma unroll
+      for (int c = 0; c < F; c += 2) {
+        const float2 w = H::unpack(*reinterpret_cast<const uint32_t*>(XQW + o + c));
+        dgi += acc[c] * w.x + acc[c + 1] * w.y;
+      }
+      DG[r * NS_MAX + seg] = dgi;
+      float sg = 0.f;
+      for (int k = 0; k <= seg; ++k) sg += G[r * NS_MAX + k] * DG[r * NS_MAX + k];
+      float dxu[F];
+#pragma unroll
+      for (int c = 0; c < F; ++c) dxu[c] = 0.f;
+      for (int k = 0; k <= seg; ++k) {
+        const float ds = G[r * NS_MAX + k] * (DG[r * NS_MAX + k] - sg);
+        DG[r * NS_MAX + k] = ds;
+        const float* sm = p.summary + (s * p.NS + k) * F;
+#pragma unroll
+        for (int c = 0; c < F; ++c) dxu[c] += ds * __ldg(sm + c);
+      }
+      T* dXU = reinterpret_cast<T*>(p.dXU);
+      T* dXQW = reinterpret_cast<T*>(p.dXQW);
+#pragma unroll
+      for (int c = 0; c < F; c += 2) {
+        *reinterpret_cast<uint32_t*>(dXU + o + c) = H::pack(dxu[c], dxu[c + 1]);
+        *reinterpret_cast<uint32_t*>(dXQW + o + c) = H::pack(gi * acc[c], gi * acc[c + 1]);
+      }
+    }
+  }
+  if (BWD) {
+    // d summary_seg += sum over this tile's tokens of ds_seg(t) XU_t  (X2 region as scratch)
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(smem + OFF_X2);  // [128][64]
+    if (tid < ROWS) {
+      const float ds = r < nrows ? DG[r * NS_MAX + seg] : 0.f;
+#pragma unroll
+      for (int c = 0; c < F; c += 2) {
+        float2 v = make_float2(0.f, 0.f);
+        if (r < nrows) v = H::unpack(*reinterpret_cast<const uint32_t*>(XU + (tok0 + r) * F + c));
+        red[r * F + c] = ds * v.x;
+        red[r * F + c + 1] = ds * v.y;
+      }
+    }
+    __syncthreads();
+    if (tid < F) {
+      float a = 0.f;
+      for (int i = 0; i < ROWS; ++i) a += red[i * F + tid];
+      atomicAdd(p.dsum + (s * p.NS + seg) * F + tid, a);
+    }
+  }
+  // a timed-out wait may leave products in flight: drain (bounded) before freeing memory
+  if (tid == 0 && abort_sh) {
+    mbar_wait(b_p1, (uint32_t)((nstate - 1) & 1), nullptr);
+    mbar_wait(b_p2, (uint32_t)((nstate - 1) & 1), nullptr);
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  if (warp == 0) tmem_dealloc(tmem_base_sh, TMEM_COLS);
+}
+
+// dXK of every token: d summary_i / (tokens of segment i) for i >= 1, zero in segment 0.
+template <typename T>
+__global__ void memo_dxk_kernel(MemoMixParams p) {
+  const long long total = (long long)p.B * p.NH * p.NC * C * F;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long tok = i / F;
+    const int f = (int)(i % F);
+    const long long s = tok / ((long long)p.NC * C);
+    const int n = (int)((tok / C) % p.NC);
+    const int seg = n / p.M;
+    float v = 0.f;
+    if (seg > 0) {
+      const int cnt = (min((seg + 1) * p.M, p.NC) - seg * p.M) * C;
+      v = p.dsum[(s * p.NS + seg) * F + f] / (float)cnt;
+    }
+    reinterpret_cast<T*>(p.dXK)[i] = Half2<T>::from_float(v);
+  }
+}
+
+}  // namespace memo
+
+using namespace memo;
+
+static bool aligned16(const void* q) { return ((uintptr_t)q & 15) == 0; }
+
+// Scratch layout: W1^T and W2^T 16-bit copies, then summary (and d summary) fp32.
+static size_t prep_bytes(long long B, long long NH, long long NS) { return (size_t)(B * NH * NS) * 2 * F * FF * 2; }
+
+template <typename T>
+static int run(MemoMixParams p, bool bwd, cudaStream_t stream, const char* who) {
+  const long long streams = (long long)p.B * p.NH;
+  memo_prep_kernel<T><<<(unsigned)(streams * p.NS), 256, 0, stream>>>(p);
+  int rc = check_launch(who);
+  if (rc) return rc;
+  Maps maps;
+  const int dt = std::is_same<T, __nv_bfloat16>::value ? DT_BF16 : DT_F16;
+  rc = make_tile_map(&maps.xq, p.XQ, dt, (unsigned long long)streams * p.NC * C, who, ROWS);
+  if (!rc) rc = make_tile_map(&maps.w1, p.W1T, dt, (unsigned long long)streams * p.NS * FF, who, FF);
+  if (!rc) rc = make_map_2d(&maps.w2, p.W2T, dt, FF, (unsigned long long)streams * p.NS * F, FF * 2, 64, 64, true, who);
+  if (rc) return rc;
+  rc = device_error_word(&p.err, who);
+  if (rc) return rc;
+  if (bwd) {
+    cudaError_t e = cudaMemsetAsync(p.dsum, 0, (size_t)streams * p.NS * F * sizeof(float), stream);
+    if (e != cudaSuccess) return fail(TTT_ERR_CUDA, "%s: %s", who, cudaGetErrorString(e));
+  }
+  const unsigned grid = (unsigned)(streams * p.NS * p.TILES);
+  if (!bwd) {
+    rc = prepare_smem(memo_mix_kernel<T, false>, SMEM, who);
+    if (rc) return rc;
+    memo_mix_kernel<T, false><<<grid, NTHREADS, SMEM, stream>>>(p, maps);
+  } else {
+    rc = prepare_smem(memo_mix_kernel<T, true>, SMEM, who);
+    if (rc) return rc;
+    memo_mix_kernel<T, true><<<grid, NTHREADS, SMEM, stream>>>(p, maps);
+    rc = check_launch(who);
+    if (rc) return rc;
+    memo_dxk_kernel<T><<<148 * 8, 256, 0, stream>>>(p);
+  }
+  return check_launch(who);
+}
+
+static int check_mix(int B, int NH, int NC, int CS, int F_, int FF_, int M, int dt, int dt_ln, const char* who) {
+  TTT_REQUIRE(B > 0 && NH > 0 && NC > 0 && M > 0, TTT_ERR_SHAPE, "%s: B, NH, NC, memo_segment_size must be positive",
+              who);
+  TTT_REQUIRE(CS == C && F_ == F && FF_ == FF, TTT_ERR_UNSUPPORTED,
+              "%s: implemented for CS = 16, F = 64, FF = 256 (got %d, %d, %d)", who, CS, F_, FF_);
+  TTT_REQUIRE((NC + M - 1) / M <= NS_MAX, TTT_ERR_UNSUPPORTED, "%s: at most %d memo segments (got %d)", who, NS_MAX,
+              (NC + M - 1) / M);
+  TTT_REQUIRE(dt == DT_BF16 || dt == DT_F16, TTT_ERR_DTYPE, "%s: activations must be bf16 or f16", who);
+  TTT_REQUIRE(valid_dtype(dt_ln), TTT_ERR_DTYPE, "%s: unknown LayerNorm dtype code", who);
+  return TTT_OK;
+}
+
+static void fill_common(MemoMixParams& p, int B, int NH, int NC, int M) {
+  p.B = B;
+  p.NH = NH;
+  p.NC = NC;
+  p.M = M;
+  p.NS = (NC + M - 1) / M;
+  p.TILES = (M * C + ROWS - 1) / ROWS;
+}
+
+}  // namespace ttt
+
+using namespace ttt;
+
+extern "C" size_t ttt_memo_mix_scratch_bytes(int B, int NH, int NC, int memo_segment_size) {
+  if (B <= 0 || NH <= 0 || NC <= 0 || memo_segment_size <= 0) return 0;
+  const long long NS = (NC + memo_segment_size - 1) / memo_segment_size;
+  return prep_bytes(B, NH, NS) + (size_t)B * NH * NS * memo::F * sizeof(float) * 2;
+}
+
+extern "C" int ttt_memo_mix_fwd(int B, int NH, int NC, int CS, int F, int FF, int memo_segment_size, const void* XQW,
+                                const void* XQ, const void* XK, const void* XU, int dt, const float* W1_memo,
+                                const float* b1_memo, const float* W2_memo, const float* b2_memo,
+                                const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln, void* out,
+                                void* scratch, size_t scratch_bytes, void* stream) {
+  const char* who = "ttt_memo_mix_fwd";
+  int rc = check_mix(B, NH, NC, CS, F, FF, memo_segment_size, dt, dt_ln, who);
+  if (rc) return rc;
+  TTT_REQUIRE(XQW && XQ && XK && XU && W1_memo && b1_memo && W2_memo && b2_memo && ttt_norm_weight && ttt_norm_bias &&
+                  out && scratch,
+              TTT_ERR_NULL, "%s: NULL pointer argument", who);
+  TTT_REQUIRE(aligned16(XQ) && aligned16(scratch), TTT_ERR_ALIGN, "%s: XQ and scratch must be 16-byte aligned", who);
+  const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size);
+  TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "%s: scratch has %zu bytes, needs %zu", who, scratch_bytes, need);
+  MemoMixParams p = {};
+  fill_common(p, B, NH, NC, memo_segment_size);
+  p.XQW = XQW; p.XQ = XQ; p.XK = XK; p.XU = XU;
+  p.W1_memo = W1_memo; p.b1_memo = b1_memo; p.W2_memo = W2_memo; p.b2_memo = b2_memo;
+  p.ln_w = ttt_norm_weight; p.ln_b = ttt_norm_bias; p.dt_ln = dt_ln;
+  p.out = out;
+  uint8_t* sc = static_cast<uint8_t*>(scratch);
+  const size_t half = prep_bytes(B, NH, p.NS) / 2;
+  p.W1T = sc;
+  p.W2T = sc + half;
+  p.summary = reinterpret_cast<float*>(sc + 2 * half);
+  p.dsum = p.summary + (size_t)B * NH * p.NS * memo::F;
+  return dt == DT_BF16 ? run<__nv_bfloat16>(p, false, (cudaStream_t)stream, who)
+                       : run<__half>(p, false, (cudaStream_t)stream, who);
+}
+
+extern "C" int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, int memo_segment_size, const void* XQW,
+                                const void* XQ, const void* XK, const void* XU, int dt, const float* W1_memo,
+                                const float* b1_memo, const float* W2_memo, const float* b2_memo,
+                                const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln, const void* dOut,
+                                void* dXQW, void* dXU, void* dXK, void* scratch, size_t scratch_bytes, void* stream) {
+  const char* who = "ttt_memo_mix_bwd";
+  int rc = check_mix(B, NH, NC, CS, F, FF, memo_segment_size, dt, dt_ln, who);
+  if (rc) return rc;
+  TTT_REQUIRE(XQW && XQ && XK && XU && W1_memo && b1_memo && W2_memo && b2_memo && ttt_norm_weight && ttt_norm_bias &&
+                  dOut && dXQW && dXU && dXK && scratch,
+              TTT_ERR_NULL, "%s: NULL pointer argument", who);
+  TTT_REQUIRE(aligned16(XQ) && aligned16(scratch), TTT_ERR_ALIGN, "%s: XQ and scratch must be 16-byte aligned", who);
+  const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size);
+  TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "%s: scratch has %zu bytes, needs %zu", who, scratch_bytes, need);
+  MemoMixParams p = {};
+  fill_common(p, B, NH, NC, memo_segment_size);
+  p.XQW = XQW; p.XQ = XQ; p.XK = XK; p.XU = XU;
+  p.W1_memo = W1_memo; p.b1_memo = b1_memo; p.W2_memo = W2_memo; p.b2_memo = b2_memo;
+  p.ln_w = ttt_norm_weight; p.ln_b = ttt_norm_bias; p.dt_ln = dt_ln;
+  p.dOut = dOut; p.dXQW = dXQW; p.dXU = dXU; p.dXK = dXK;
+  uint8_t* sc = static_cast<uint8_t*>(scratch);
+  const size_t half = prep_bytes(B, NH, p.NS) / 2;
+  p.W1T = sc;
+  p.W2T = sc + half;
+  p.summary = reinterpret_cast<float*>(sc + 2 * half);
+  p.dsum = p.summary + (size_t)B * NH * p.NS * memo::F;
+  return dt == DT_BF16 ? run<__nv_bfloat16>(p, true, (cudaStream_t)stream, who)
+                       : run<__half>(p, true, (cudaStream_t)stream, who);
+}
