@@ -12,6 +12,8 @@ ttt-triton_b200/synthetic.py):
 * ``linear_fwd_c2``: TTT-Linear forward only at the config-2 shape (diagnostic).
 * ``linear_fwdbwd_c2``: TTT-Linear forward+backward, bf16, B32 NH8 L4096 F64 (config 2).
 * ``mlp_fwdbwd_c3``: TTT-MLP forward+backward, bf16, B64 NH16 L8192 F64 FF256, memo 16 (config 3).
+* ``memo_mix_c3``: the layer's memo-state mixing (cached read-outs of every earlier memo
+  state, ttt_layer.py:503-559), forward+backward, at the config-3 shape (32 memo segments).
 
 A step is one pass of the hot path over one batch. Multi-GPU runs are weak scaling:
 every rank processes its own full batch (the (b, h) streams are independent, so there
@@ -42,7 +44,9 @@ WORKLOADS = {
     "linear_fwd_c2": dict(kind="linear", B=32, NH=8, L=4096, F=64, FF=None, dtype="bf16", bwd=False, ckpt=16, memo=None),
     "linear_fwdbwd_c2": dict(kind="linear", B=32, NH=8, L=4096, F=64, FF=None, dtype="bf16", bwd=True, ckpt=16, memo=None),
     "mlp_fwdbwd_c3": dict(kind="mlp", B=64, NH=16, L=8192, F=64, FF=256, dtype="bf16", bwd=True, ckpt=16, memo=16),
+    "memo_mix_c3": dict(kind="memo", B=64, NH=16, L=8192, F=64, FF=256, dtype="bf16", bwd=True, ckpt=16, memo=16),
 }
+MEMO = ("XQW", "XQ", "XK", "XU", "W1_memo", "b1_memo", "W2_memo", "b2_memo", "ln_w", "ln_b")
 CS = 16
 DT = {"f32": torch.float32, "bf16": torch.bfloat16}
 # DRAM bytes (read + write) of one launch of the dominant kernel from an ncu capture of
@@ -79,6 +83,15 @@ def algorithmic(w):
     """
     F, FF = w["F"], w["FF"]
     eb = 4 if w["dtype"] == "f32" else 2
+    if w["kind"] == "memo":
+        # forward reads XQW, XQ, XK, XU and writes the output; backward re-reads XQW, XQ, XK,
+        # XU, reads dOut and writes dXQW, dXU, dXK. Each token of segment i reads out the i
+        # earlier memo states (2 * 2 * F * FF FLOPs each) in both passes.
+        NC, M = w["L"] // CS, w["memo"]
+        NS = -(-NC // M)
+        mean_i = sum(i * (min((i + 1) * M, NC) - i * M) for i in range(NS)) / NC
+        flops = mean_i * 4 * F * FF
+        return {"fwd": (eb * 5 * F, flops), "bwd": (eb * 8 * F, flops)}
     fwd_bytes = eb * (3 * F + CS + F)
     bwd_bytes = eb * ((3 * F + CS) + F + (3 * F + CS))
     if w["kind"] == "linear":
@@ -96,6 +109,10 @@ def make_inputs(w, device, seed):
 
     NC = w["L"] // CS
     dt = DT[w["dtype"]]
+    if w["kind"] == "memo":
+        return S.make_memo_inputs(w["B"], w["NH"], NC, CS, w["F"], w["FF"], w["memo"], dtype=dt, device=device,
+                                  seed=seed), S.make_upstream((w["B"], w["NH"], NC, CS, w["F"]), device=device,
+                                                              seed=seed + 1, dtype=dt)
     if w["kind"] == "linear":
         d = S.make_linear_inputs(w["B"], w["NH"], NC, CS, w["F"], dtype=dt, device=device, seed=seed)
     else:
@@ -113,6 +130,12 @@ def kernel_step(w, d, dO):
     Returns the number of kernel launches it made."""
     import _core
 
+    if w["kind"] == "memo":
+        _core.memo_mix_forward(*(d[k] for k in MEMO), w["memo"])
+        if w["bwd"]:
+            _core.memo_mix_backward(*(d[k] for k in MEMO), w["memo"], dO)
+            return 5  # prep + mix (forward), prep + mix + dXK (backward)
+        return 2
     if w["kind"] == "linear":
         XQW, Wl, bl, Wc, bc, Z = _core.linear_forward(*(d[k] for k in LIN), w["ckpt"], for_backward=w["bwd"])
         if w["bwd"]:
@@ -140,6 +163,18 @@ def api_step(w, host, dev_bufs, out_host):
         dev_bufs[k].copy_(t, non_blocking=True)
         h2d += t.numel() * t.element_size()
     d = dev_bufs
+    if w["kind"] == "memo":
+        from kernels.mlp_memo_mix import mlp_memo_mix
+
+        leaves = [d[k].requires_grad_(k in ("XQW", "XU", "XK")) for k in MEMO]
+        out = mlp_memo_mix(*leaves, w["memo"])
+        out.backward(d["dO"])
+        res = d["XU"].grad
+        for t in leaves:
+            t.grad = None
+            t.requires_grad_(False)
+        out_host.copy_(res.detach(), non_blocking=True)
+        return h2d, out_host.numel() * out_host.element_size()
     if w["kind"] == "linear":
         leaves = [d[k] for k in LIN]
         if w["bwd"]:
@@ -229,6 +264,15 @@ def cpu_reference(w, budget_s=12.0):
     torch.set_num_threads(threads)
     NC = w["L"] // CS
     B, NH = 1, min(w["NH"], 4)
+    if w["kind"] == "memo":
+        B, NH = 1, 1
+        d = S.make_memo_inputs(B, NH, NC, CS, w["F"], w["FF"], w["memo"], seed=0)
+        dO = S.make_upstream((B, NH, NC, CS, w["F"]), seed=1)
+        tokens = B * NH * NC * CS
+        t0 = time.perf_counter()
+        O.memo_mix_grads(d, dO, w["memo"])
+        dt = time.perf_counter() - t0
+        return tokens / dt, threads, f"B=1 NH=1 L={w['L']} (full sequence, one stream), fp32, forward+backward, 1 run"
     if w["kind"] == "linear":
         d = S.make_linear_inputs(B, NH, NC, CS, w["F"], seed=0)
     else:
@@ -315,13 +359,13 @@ def run_ours(args, w, rank, world, local_rank):
     dom = "bwd" if w["bwd"] else "fwd"  # dominant kernel: the backward when there is one
     dom_bytes, dom_flops = alg[dom]
     dom_ms = kern_ms
-    if w["kind"] == "mlp":
+    if w["kind"] in ("mlp", "memo"):
         achieved = dom_flops * tokens_rank / (dom_ms / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16}
     else:
         achieved = dom_bytes * tokens_rank / (dom_ms / 1e3) / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm}
-    kname = ("linear" if w["kind"] == "linear" else "mlp") + "_" + dom
+    kname = w["kind"] + "_" + dom
     traffic = NCU_TRAFFIC.get((args.workload, kname))
     roof.update({
         "traffic": traffic[0] * (tokens_rank / traffic[1]) if traffic else None,
@@ -383,7 +427,10 @@ def kernel_durations(w, d, dO, steps):
     n = max(1, min(steps, 5))
     for _ in range(n):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        if w["kind"] == "linear":
+        if w["kind"] == "memo":
+            e0.record(stream)
+            _core.memo_mix_backward(*(d[k] for k in MEMO), w["memo"], dO)
+        elif w["kind"] == "linear":
             if w["bwd"]:
                 _, Wl, bl, Wc, bc, Z = _core.linear_forward(*(d[k] for k in LIN), w["ckpt"])
                 e0.record(stream)

@@ -76,6 +76,29 @@ def make_mlp_inputs(B, NH, NC, CS=16, F=64, FF=256, dtype=torch.float32, device=
     return d
 
 
+def make_memo_inputs(B, NH, NC, CS=16, F=64, FF=256, memo_segment_size=16, dtype=torch.float32, device="cpu",
+                     seed=0):
+    """Inputs of the memo-state mixing at a layer's shapes: the scan output XQW, XQ, XK and the
+    mixing query XU ~ N(0,1)/8 (XQW ~ N(0,1)), memo states near the MLP's initialisation
+    (W ~ N(0, 0.02^2), biases ~ N(0, 0.01^2)) as TritonMLP returns them [B,NH,NS,...], LN
+    weight 1 and bias 0."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    NS = -(-NC // memo_segment_size)
+    d = {
+        "XQW": _randn((B, NH, NC, CS, F), g, device).to(dtype),
+        "XQ": (_randn((B, NH, NC, CS, F), g, device) / 8).to(dtype),
+        "XK": (_randn((B, NH, NC, CS, F), g, device) / 8).to(dtype),
+        "XU": (_randn((B, NH, NC, CS, F), g, device) / 8).to(dtype),
+        "W1_memo": _randn((B, NH, NS, F, FF), g, device) * 0.02,
+        "b1_memo": _randn((B, NH, NS, 1, FF), g, device) * 0.01,
+        "W2_memo": _randn((B, NH, NS, FF, F), g, device) * 0.02,
+        "b2_memo": _randn((B, NH, NS, 1, F), g, device) * 0.01,
+        "ln_w": torch.ones(NH, F, device=device),
+        "ln_b": torch.zeros(NH, F, device=device),
+    }
+    return d
+
+
 def make_upstream(shape, device="cpu", seed=1, dtype=torch.float32):
     """dZ ~ N(0, 1) with the output's shape."""
     g = torch.Generator(device=device).manual_seed(seed)
