@@ -47,10 +47,13 @@ constexpr int OFF_XQ = 0;                          // [128][64] 16-bit, K-major 
 constexpr int OFF_W1 = OFF_XQ + ROWS * F * 2;      // [256][64]: W1_j^T
 constexpr int OFF_W2 = OFF_W1 + FF * F * 2;        // 4 x [64][64]: W2_j^T, K chunks of 64
 constexpr int OFF_X2 = OFF_W2 + F * FF * 2;        // 4 x [128][64]: gelu(Z1 + b1), K chunks of 64
-constexpr int OFF_G = OFF_X2 + ROWS * FF * 2;      // fp32 [128][NS_MAX]: mixing weights g_j(t)
-constexpr int OFF_DG = OFF_G + ROWS * NS_MAX * 4;  // fp32 [128][NS_MAX]: dg_j(t) (backward)
-constexpr int OFF_LN = OFF_DG + ROWS * NS_MAX * 4; // fp32 [2][64]: LayerNorm weight, bias
-constexpr int SMEM = OFF_LN + 2 * F * 4 + 1024;    // + slack to align the base
+constexpr int GLD = NS_MAX + 1;                    // row stride of the per-token tables (conflict-free)
+constexpr int OFF_G = OFF_X2 + ROWS * FF * 2;      // fp32 [128][GLD]: mixing weights g_j(t)
+constexpr int OFF_DG = OFF_G + ROWS * GLD * 4;     // fp32 [128][GLD]: dg_j(t) (backward)
+constexpr int OFF_LN = OFF_DG + ROWS * GLD * 4;    // fp32 [2][64]: LayerNorm weight, bias
+constexpr int OFF_B1 = OFF_LN + 2 * F * 4;         // fp32 [3][256]: b1_j ring (state j in slot j % 3)
+constexpr int OFF_B2 = OFF_B1 + 3 * FF * 4;        // fp32 [3][64]: b2_j ring
+constexpr int SMEM = OFF_B2 + 3 * F * 4 + 1024;    // + slack to align the base
 constexpr uint32_t TMEM_COLS = 512;                // Z1: columns 0-255, Z2: 256-319
 constexpr uint32_t XQ_BYTES = ROWS * F * 2, W1_BYTES = FF * F * 2, W2_BYTES = F * FF * 2;
 static_assert(OFF_W1 % 1024 == 0 && OFF_W2 % 1024 == 0 && OFF_X2 % 1024 == 0, "swizzled tiles need 1024-byte alignment");
@@ -154,6 +157,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   float* G = reinterpret_cast<float*>(smem + OFF_G);
   float* DG = reinterpret_cast<float*>(smem + OFF_DG);
   float* LN = reinterpret_cast<float*>(smem + OFF_LN);
+
   const uint32_t b_xq = smem_u32(&bars[0]), b_w1 = smem_u32(&bars[1]), b_w2 = smem_u32(&bars[2]);
   const uint32_t b_p1 = smem_u32(&bars[3]), b_p2 = smem_u32(&bars[4]);
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -184,6 +188,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     mbar_expect_tx(b_w2, W2_BYTES);
 #pragma unroll
     for (int a = 0; a < 4; ++a) tma_load_2d(sW2 + a * (F * 64 * 2), &maps.w2, 64 * a, (int)((s * p.NS + j) * F), b_w2);
+  };
+  // Biases of state j into ring slot j % 3 (plain loads; the next CTA barrier publishes them).
+  // A slot is rewritten two states after its last reader, which is past a barrier by then.
+  auto load_bias = [&](int j) {
+    float* b1s = reinterpret_cast<float*>(smem + OFF_B1) + (j % 3) * FF;
+    float* b2s = reinterpret_cast<float*>(smem + OFF_B2) + (j % 3) * F;
+    b1s[tid] = __ldg(p.b1_memo + (s * p.NS + j) * FF + tid);
+    if (tid < F) b2s[tid] = __ldg(p.b2_memo + (s * p.NS + j) * F + tid);
   };
   auto product1 = [&]() {  // Z1 = XQ W1_j  (K = 64)
     tmem_fence_after();
@@ -229,24 +241,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
       float d = 0.f;
 #pragma unroll
       for (int c = 0; c < F; ++c) d += xu[c] * __ldg(sm + c);
-      G[r * NS_MAX + j] = d;
+      G[r * GLD + j] = d;
       mx = fmaxf(mx, d);
     }
     float tot = 0.f;
     for (int j = 0; j <= seg; ++j) {
-      const float e = __expf(G[r * NS_MAX + j] - mx);
-      G[r * NS_MAX + j] = e;
+      const float e = __expf(G[r * GLD + j] - mx);
+      G[r * GLD + j] = e;
       tot += e;
     }
     const float inv = 1.f / tot;
-    for (int j = 0; j <= seg; ++j) G[r * NS_MAX + j] *= inv;
+    for (int j = 0; j <= seg; ++j) G[r * GLD + j] *= inv;
   }
+  if (nstate > 0) load_bias(0);
   if (tid == 0) {
     wait(b_xq, 0);
     wait(b_w1, 0);
     if (!abort_sh) product1();
   }
-  __syncthreads();  // mixing weights written; the XQ tile is in shared memory
+  __syncthreads();  // mixing weights and state 0's biases written; the XQ tile is in shared memory
 
   float acc[F];   // forward: sum_j g_j R_j;  backward: dOut row
   float xq[F];    // XQ row
@@ -283,7 +296,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     if (tid == 0 && j + 1 < nstate && !abort_sh) load_w1(j + 1);  // product 1 of j no longer reads W1
     {
       const int q = warp & 3, hc = warp >> 2, row = 32 * q + lane;
-      const float* b1 = p.b1_memo + (s * p.NS + j) * FF;
+      const float* b1 = reinterpret_cast<const float*>(smem + OFF_B1) + (j % 3) * FF;
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         const int col = 128 * hc + 32 * c4;
@@ -293,7 +306,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
         uint32_t pk[16];
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-          const float2 bb = __ldg(reinterpret_cast<const float2*>(b1 + col + 2 * u));
+          const float2 bb = *reinterpret_cast<const float2*>(b1 + col + 2 * u);
           const float2 g = gelu2(make_float2(z[2 * u] + bb.x, z[2 * u + 1] + bb.y));
           pk[u] = H::pack(g.x, g.y);
         }
@@ -305,6 +318,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
               make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
       }
     }
+    if (j + 1 < nstate) load_bias(j + 1);
     fence_proxy_async();  // X2 stores -> visible to the tensor cores
     tmem_fence_before();
     __syncthreads();
@@ -326,11 +340,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
       tmem_ld32(tmem_lane_addr(tZ2, warp, 32), z + 32);
       tmem_wait_ld();
       if (tid == 0 && j + 1 < nstate && !abort_sh) load_w2(j + 1);  // product 2 of j no longer reads W2
-      const float* b2 = p.b2_memo + (s * p.NS + j) * F;
+      const float* b2 = reinterpret_cast<const float*>(smem + OFF_B2) + (j % 3) * F;
       float mu = 0.f;
 #pragma unroll
       for (int c = 0; c < F; ++c) {
-        z[c] += __ldg(b2 + c);
+        z[c] += b2[c];
         mu += z[c];
       }
       mu *= 1.f / F;
@@ -342,14 +356,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
       }
       const float rstd = 1.f / sqrtf(var * (1.f / F) + kReadoutEps);
       if (!BWD) {
-        const float gj = r < nrows ? G[r * NS_MAX + j] : 0.f;
+        const float gj = r < nrows ? G[r * GLD + j] : 0.f;
 #pragma unroll
         for (int c = 0; c < F; ++c) acc[c] += gj * (xq[c] + LN[c] * z[c] * rstd + LN[F + c]);
       } else {
         float d = 0.f;
 #pragma unroll
         for (int c = 0; c < F; ++c) d += acc[c] * (xq[c] + LN[c] * z[c] * rstd + LN[F + c]);
-        if (r < nrows) DG[r * NS_MAX + j] = d;
+        if (r < nrows) DG[r * GLD + j] = d;
       }
     }
     tmem_fence_before();
@@ -358,7 +372,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   // ---- tail (threads 0-127, one token each)
   if (tid < ROWS && r < nrows) {
     const long long o = (tok0 + r) * F;
-    const float gi = G[r * NS_MAX + seg];
+    const float gi = G[r * GLD + seg];
     if (!BWD) {
       T* out = reinterpret_cast<T*>(p.out);
 #pragma unroll
@@ -373,15 +387,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
         const float2 w = H::unpack(*reinterpret_cast<const uint32_t*>(XQW + o + c));
         dgi += acc[c] * w.x + acc[c + 1] * w.y;
       }
-      DG[r * NS_MAX + seg] = dgi;
+      DG[r * GLD + seg] = dgi;
       float sg = 0.f;
-      for (int k = 0; k <= seg; ++k) sg += G[r * NS_MAX + k] * DG[r * NS_MAX + k];
+      for (int k = 0; k <= seg; ++k) sg += G[r * GLD + k] * DG[r * GLD + k];
       float dxu[F];
 #pragma unroll
       for (int c = 0; c < F; ++c) dxu[c] = 0.f;
       for (int k = 0; k <= seg; ++k) {
-        const float ds = G[r * NS_MAX + k] * (DG[r * NS_MAX + k] - sg);
-        DG[r * NS_MAX + k] = ds;
+        const float ds = G[r * GLD + k] * (DG[r * GLD + k] - sg);
+        DG[r * GLD + k] = ds;
         const float* sm = p.summary + (s * p.NS + k) * F;
 #pragma unroll
         for (int c = 0; c < F; ++c) dxu[c] += ds * __ldg(sm + c);
@@ -400,7 +414,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     __syncthreads();
     float* red = reinterpret_cast<float*>(smem + OFF_X2);  // [128][64]
     if (tid < ROWS) {
-      const float ds = r < nrows ? DG[r * NS_MAX + seg] : 0.f;
+      const float ds = r < nrows ? DG[r * GLD + seg] : 0.f;
 #pragma unroll
       for (int c = 0; c < F; c += 2) {
         float2 v = make_float2(0.f, 0.f);
