@@ -14,8 +14,8 @@
 //   memo_mix    one CTA (8 warps) per (stream, segment, 128-token tile), heavy segments
 //               first. Per earlier state j:
 //                 Z1 = XQ W1_j      128 x 256 x 64 tcgen05.mma into tensor memory
-//                 X2 = gelu(Z1+b1)  all warps: 32-column TMEM loads, 16-bit K-major
-//                                   swizzled tiles in shared memory
+//                 X2 = gelu(Z1+b1)  all warps (more columns to warps 4-7): 32-column TMEM
+//                                   loads, 16-bit K-major swizzled tiles in shared memory
 //                 Z2 = X2 W2_j      128 x 64 x 256 tcgen05.mma
 //                 R_j              warps 0-3, one token per thread: LayerNorm in registers
 //               forward: accumulate g_j R_j; backward: dg_j = <dOut_t, R_j(t)>.
@@ -295,11 +295,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     tmem_fence_after();
     if (tid == 0 && j + 1 < nstate && !abort_sh) load_w1(j + 1);  // product 1 of j no longer reads W1
     {
-      const int q = warp & 3, hc = warp >> 2, row = 32 * q + lane;
+      // the eight 32-column chunks of a row: 3 for warps 0-3 (they also run the read-out
+      // LayerNorm below), 5 for warps 4-7
+      const int q = warp & 3, row = 32 * q + lane;
+      const int c_begin = warp < 4 ? 0 : 3, c_end = warp < 4 ? 3 : 8;
       const float* b1 = reinterpret_cast<const float*>(smem + OFF_B1) + (j % 3) * FF;
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        const int col = 128 * hc + 32 * c4;
+#pragma unroll 1
+      for (int c4 = c_begin; c4 < c_end; ++c4) {
+        const int col = 32 * c4;
         float z[32];
         tmem_ld32(tmem_lane_addr(tZ1, warp, col), z);
         tmem_wait_ld();
