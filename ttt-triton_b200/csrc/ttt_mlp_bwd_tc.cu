@@ -206,9 +206,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
     const long long xb = (s * p.NC + n) * (long long)(C * F);
     const uint32_t xo = swz128(tk, q >> 1) + (q & 1) * 8;
 
-    // ---------------- R1: G2 from the stored Z2; read-out LayerNorm backward from Z2bar
-    float xh[4], gh[4], Gr[4], rstd;
-    {
+    // G2 = ln_fused_l2_bwd(Z2, XV - XK) for token tk, features 4q.., with its normalised input
+    // xh, the scaled residual gh and 1/std (rows; formed in R1 and again in R2 rather than
+    // kept in registers across M1)
+    auto g2_rows = [&](float* xh, float* gh, float* Gr, float& rstd) {
       const float4 z4 = *reinterpret_cast<const float4*>(st + OFF_Z2 + (tk * F + 4 * q) * 4);
       float z[4] = {z4.x, z4.y, z4.z, z4.w}, xv[4], xk[4];
       unpack4<T>(st + OFF_XV + xo, xv);
@@ -234,6 +235,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
       const float inv = rstd * (1.f / F);
 #pragma unroll
       for (int j = 0; j < 4; ++j) Gr[j] = (F * gh[j] - s1 - xh[j] * s2) * inv;
+    };
+
+    // ---------------- R1: G2 from the stored Z2; read-out LayerNorm backward from Z2bar
+    {
+      float xh[4], gh[4], Gr[4], rstd;
+      g2_rows(xh, gh, Gr, rstd);
       const float e = (float)E[(C - 1) * C + tk];
       *reinterpret_cast<uint2*>(smem + OFF_G + xo) = make_uint2(H::pack(Gr[0], Gr[1]), H::pack(Gr[2], Gr[3]));
       *reinterpret_cast<uint2*>(smem + OFF_EG + xo) =
@@ -451,26 +458,52 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
       }
     }
     // carried dW2: dX2 -= e (G2 dW2^T), d e -= rowsum(X2 * (G2 dW2^T)); partial dG2 = (-e X2) dW2
-    float PG[8][4];
+    // straight to the warp's partial tile. dW2^T is processed in two halves of feature rows
+    // (32 TMEM columns each) to keep registers free.
     float de0 = 0.f, de1 = 0.f;  // d e partials of tokens g, g + 8
     {
-      float D2[4][4][4];
-      slice_ld(tD2, &D2[0][0][0]);
+      uint32_t aX[4][2];  // -e X2 in accumulator-pair layout
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 x01 = H::unpack(X2p[j][0]), x23 = H::unpack(X2p[j][1]);
+        aX[j][0] = H::pack(-eg0 * x01.x, -eg0 * x01.y);
+        aX[j][1] = H::pack(-eg1 * x23.x, -eg1 * x23.y);
+      }
       float GD[4][4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) GD[j][0] = GD[j][1] = GD[j][2] = GD[j][3] = 0.f;
+      float* pw = PA + warp * C * PLD;
 #pragma unroll
-      for (int kf = 0; kf < 4; ++kf) {
-        uint32_t ag[4];
-        ldsm_x4(ag, sG + swz128((mi & 1) * 8 + r8, 2 * kf + (mi >> 1)));
+      for (int half = 0; half < 2; ++half) {
+        float D2h[2][4][4];  // feature tiles m = 2 half, 2 half + 1
+        tmem_ld32(tD2 + 32 * half, &D2h[0][0][0]);
+        tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t b[2] = {movm_t(H::pack(D2[kf][j][0], D2[kf][j][1])),
-                                 movm_t(H::pack(D2[kf][j][2], D2[kf][j][3]))};
-          mma16816<T>(GD[j], ag, b);
+        for (int mm = 0; mm < 2; ++mm) {
+          uint32_t ag[4];
+          ldsm_x4(ag, sG + swz128((mi & 1) * 8 + r8, 2 * (2 * half + mm) + (mi >> 1)));
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t b[2] = {movm_t(H::pack(D2h[mm][j][0], D2h[mm][j][1])),
+                                   movm_t(H::pack(D2h[mm][j][2], D2h[mm][j][3]))};
+            mma16816<T>(GD[j], ag, b);
+          }
+        }
+#pragma unroll
+        for (int nh = 0; nh < 4; ++nh) {  // output feature tiles nf = 4 half + nh
+          const int nf = 4 * half + nh, mm = nh >> 1, hh = 2 * (nh & 1);
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int ks = 0; ks < 2; ++ks) {
+            const uint32_t a[4] = {aX[2 * ks][0], aX[2 * ks][1], aX[2 * ks + 1][0], aX[2 * ks + 1][1]};
+            const uint32_t b[2] = {H::pack(D2h[mm][2 * ks][hh], D2h[mm][2 * ks][hh + 1]),
+                                   H::pack(D2h[mm][2 * ks + 1][hh], D2h[mm][2 * ks + 1][hh + 1])};
+            mma16816<T>(acc, a, b);
+          }
+          *reinterpret_cast<float2*>(pw + g * PLD + 8 * nf + 2 * t) = make_float2(acc[0], acc[1]);
+          *reinterpret_cast<float2*>(pw + (g + 8) * PLD + 8 * nf + 2 * t) = make_float2(acc[2], acc[3]);
         }
       }
-      uint32_t aX[4][2];  // -e X2 in accumulator-pair layout
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 x01 = H::unpack(X2p[j][0]), x23 = H::unpack(X2p[j][1]);
@@ -480,67 +513,54 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
         dX2[j][3] -= eg1 * GD[j][3];
         de0 -= x01.x * GD[j][0] + x01.y * GD[j][1];
         de1 -= x23.x * GD[j][2] + x23.y * GD[j][3];
-        aX[j][0] = H::pack(-eg0 * x01.x, -eg0 * x01.y);
-        aX[j][1] = H::pack(-eg1 * x23.x, -eg1 * x23.y);
-      }
-#pragma unroll
-      for (int nf = 0; nf < 8; ++nf) {
-        PG[nf][0] = PG[nf][1] = PG[nf][2] = PG[nf][3] = 0.f;
-        const int m = nf >> 1, hh = 2 * (nf & 1);
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          const uint32_t a[4] = {aX[2 * ks][0], aX[2 * ks][1], aX[2 * ks + 1][0], aX[2 * ks + 1][1]};
-          const uint32_t b[2] = {H::pack(D2[m][2 * ks][hh], D2[m][2 * ks][hh + 1]),
-                                 H::pack(D2[m][2 * ks + 1][hh], D2[m][2 * ks + 1][hh + 1])};
-          mma16816<T>(PG[nf], a, b);
-        }
       }
     }
     // carried dW1, db1: dG1 = -e (XK dW1 + db1), d e -= rowsum((XK dW1 + db1) * G1);
-    // partial dXK = (-e G1) dW1^T
+    // partial dXK = (-e G1) dW1^T. dW1^T in two halves of hidden rows (m-tiles).
     float dG1[4][4];
     {
-      float D1[2][8][4];
-      slice_ld(tD1, &D1[0][0][0]);
-      float XD[4][4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) XD[j][0] = XD[j][1] = XD[j][2] = XD[j][3] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t ak[4];
-        ldsm_x4(ak, sb + OFF_XK + swz128((mi & 1) * 8 + r8, 2 * kk + (mi >> 1)));
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int m = j >> 1, hh = 2 * (j & 1);
-          const uint32_t b[2] = {H::pack(D1[m][2 * kk][hh], D1[m][2 * kk][hh + 1]),
-                                 H::pack(D1[m][2 * kk + 1][hh], D1[m][2 * kk + 1][hh + 1])};
-          mma16816<T>(XD[j], ak, b);
-        }
-      }
-      uint32_t aG[4][2];  // -e G1
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float u0 = XD[j][0] + DB1[j][0], u1 = XD[j][1] + DB1[j][1];
-        const float u2 = XD[j][2] + DB1[j][0], u3 = XD[j][3] + DB1[j][1];
-        de0 -= u0 * G1[j][0] + u1 * G1[j][1];
-        de1 -= u2 * G1[j][2] + u3 * G1[j][3];
-        dG1[j][0] = -eg0 * u0;
-        dG1[j][1] = -eg0 * u1;
-        dG1[j][2] = -eg1 * u2;
-        dG1[j][3] = -eg1 * u3;
-        aG[j][0] = H::pack(-eg0 * G1[j][0], -eg0 * G1[j][1]);
-        aG[j][1] = H::pack(-eg1 * G1[j][2], -eg1 * G1[j][3]);
-      }
       float KD[8][4];
 #pragma unroll
       for (int nf = 0; nf < 8; ++nf) KD[nf][0] = KD[nf][1] = KD[nf][2] = KD[nf][3] = 0.f;
 #pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        const uint32_t a[4] = {aG[2 * ks][0], aG[2 * ks][1], aG[2 * ks + 1][0], aG[2 * ks + 1][1]};
+      for (int mh = 0; mh < 2; ++mh) {
+        float D1h[8][4];  // hidden rows 16 mh .. of the slice
+        tmem_ld32(tD1 + 32 * mh, &D1h[0][0]);
+        tmem_wait_ld();
+        float XD[2][4];  // hidden tiles j = 2 mh, 2 mh + 1
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) XD[jj][0] = XD[jj][1] = XD[jj][2] = XD[jj][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          uint32_t ak[4];
+          ldsm_x4(ak, sb + OFF_XK + swz128((mi & 1) * 8 + r8, 2 * kk + (mi >> 1)));
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            const int hh = 2 * jj;
+            const uint32_t b[2] = {H::pack(D1h[2 * kk][hh], D1h[2 * kk][hh + 1]),
+                                   H::pack(D1h[2 * kk + 1][hh], D1h[2 * kk + 1][hh + 1])};
+            mma16816<T>(XD[jj], ak, b);
+          }
+        }
+        uint32_t aG[2][2];  // -e G1 for j = 2 mh, 2 mh + 1
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = 2 * mh + jj;
+          const float u0 = XD[jj][0] + DB1[j][0], u1 = XD[jj][1] + DB1[j][1];
+          const float u2 = XD[jj][2] + DB1[j][0], u3 = XD[jj][3] + DB1[j][1];
+          de0 -= u0 * G1[j][0] + u1 * G1[j][1];
+          de1 -= u2 * G1[j][2] + u3 * G1[j][3];
+          dG1[j][0] = -eg0 * u0;
+          dG1[j][1] = -eg0 * u1;
+          dG1[j][2] = -eg1 * u2;
+          dG1[j][3] = -eg1 * u3;
+          aG[jj][0] = H::pack(-eg0 * G1[j][0], -eg0 * G1[j][1]);
+          aG[jj][1] = H::pack(-eg1 * G1[j][2], -eg1 * G1[j][3]);
+        }
+        const uint32_t a[4] = {aG[0][0], aG[0][1], aG[1][0], aG[1][1]};
 #pragma unroll
         for (int nf = 0; nf < 8; ++nf) {
-          const uint32_t b[2] = {movm_t(H::pack(D1[ks][nf][0], D1[ks][nf][1])),
-                                 movm_t(H::pack(D1[ks][nf][2], D1[ks][nf][3]))};
+          const uint32_t b[2] = {movm_t(H::pack(D1h[nf][0], D1h[nf][1])), movm_t(H::pack(D1h[nf][2], D1h[nf][3]))};
           mma16816<T>(KD[nf], a, b);
         }
       }
@@ -570,38 +590,45 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
         dHp[j][1] = H::pack(dG1[j][2] * GP[j][2], dG1[j][3] * GP[j][3]);
       }
     }
-    // partial dG2 += dH W2_n - (eta * (A2_w [+1]))^T dZ2bar -> shared memory
+    // partial dG2 += dH W2_n - (eta * (A2_w [+1]))^T dZ2bar (added to the partial tile)
     {
-      float S2[4][4][4];
-      slice_ld(tS2, &S2[0][0][0]);
-#pragma unroll
-      for (int nf = 0; nf < 8; ++nf) {
-        const int m = nf >> 1, hh = 2 * (nf & 1);
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          const uint32_t a[4] = {dHp[2 * ks][0], dHp[2 * ks][1], dHp[2 * ks + 1][0], dHp[2 * ks + 1][1]};
-          const uint32_t b[2] = {H::pack(S2[m][2 * ks][hh], S2[m][2 * ks][hh + 1]),
-                                 H::pack(S2[m][2 * ks + 1][hh], S2[m][2 * ks + 1][hh + 1])};
-          mma16816<T>(PG[nf], a, b);
-        }
-      }
-    }
-    {
-      float Y[2][4];
-#pragma unroll
-      for (int jt = 0; jt < 2; ++jt)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) Y[jt][c] = ev[jt][c] * (A2[jt][c] + one_w0);
+      float PG[8][4];
       uint32_t aYT[4];
-      transpose_afrag<T>(aYT, Y, -1.f);
+      {
+        float Y[2][4];
+#pragma unroll
+        for (int jt = 0; jt < 2; ++jt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) Y[jt][c] = ev[jt][c] * (A2[jt][c] + one_w0);
+        transpose_afrag<T>(aYT, Y, -1.f);
+      }
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
         uint32_t bz[4];
         ldsm_x4_t(bz, sDZB + swz128((mi & 1) * 8 + r8, 2 * np + (mi >> 1)));
+        PG[2 * np][0] = PG[2 * np][1] = PG[2 * np][2] = PG[2 * np][3] = 0.f;
+        PG[2 * np + 1][0] = PG[2 * np + 1][1] = PG[2 * np + 1][2] = PG[2 * np + 1][3] = 0.f;
         mma16816<T>(PG[2 * np], aYT, bz);
         mma16816<T>(PG[2 * np + 1], aYT, bz + 2);
       }
-      put_part<false>(PA + warp * C * PLD, PG, g, t);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float S2h[2][4][4];
+        tmem_ld32(tS2 + 32 * half, &S2h[0][0][0]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int nh = 0; nh < 4; ++nh) {
+          const int nf = 4 * half + nh, mm = nh >> 1, hh = 2 * (nh & 1);
+#pragma unroll
+          for (int ks = 0; ks < 2; ++ks) {
+            const uint32_t a[4] = {dHp[2 * ks][0], dHp[2 * ks][1], dHp[2 * ks + 1][0], dHp[2 * ks + 1][1]};
+            const uint32_t b[2] = {H::pack(S2h[mm][2 * ks][hh], S2h[mm][2 * ks][hh + 1]),
+                                   H::pack(S2h[mm][2 * ks + 1][hh], S2h[mm][2 * ks + 1][hh + 1])};
+            mma16816<T>(PG[nf], a, b);
+          }
+        }
+      }
+      put_part<true>(PA + warp * C * PLD, PG, g, t);
     }
     // dW2^T += dZ2bar^T X2bar + G2^T dH
     {
@@ -673,7 +700,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
     // ---------------- R2: dG2 -> backward of G2 = ln_fused_l2_bwd(Z2, XV - XK); d_eta, dP1
     float DTr[4];
     {
-      float dG[4], xv[4], xk[4];
+      float dG[4], xv[4], xk[4], xh[4], gh[4], Gr[4], rstd;
+      g2_rows(xh, gh, Gr, rstd);
       sum_part(PA, tk, q, dG);
       const float e = (float)E[(C - 1) * C + tk];
       const float4 db = *reinterpret_cast<const float4*>(DB2 + 4 * q);
