@@ -57,7 +57,7 @@ NCU_TRAFFIC = {
     ("linear_fwd_c2", "linear_fwd"): (557.3e6, 32 * 8 * 4096, "profiles/linear_fwd_tc_config2.md"),
     ("linear_fwdbwd_c2", "linear_bwd"): (1252.9e6, 32 * 8 * 4096, "profiles/linear_bwd_tc_config2.md"),
     # captured at batch 4 (64 streams); traffic per stream is size-independent, scaled by tokens
-    ("mlp_fwdbwd_c3", "mlp_bwd"): (1849.8e6, 4 * 16 * 8192, "profiles/mlp_bwd_tc_config3.md"),
+    ("mlp_fwdbwd_c3", "mlp_bwd"): (1851.7e6, 4 * 16 * 8192, "profiles/mlp_bwd_tc_config3.md"),
 }
 METRIC = "TTT tokens/s (B*H*L) fwd & fwd+bwd at 1/2/4/8 B200; % of HBM roofline"
 
