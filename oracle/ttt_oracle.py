@@ -260,6 +260,68 @@ def memo_mix(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, me
     return torch.cat(out_segs, dim=2)
 
 
+def process_input(hidden, wq, bq, wk, bk, wv, bv, wu, bu, lr_w, lr_b, ln_w, ln_b, freqs_cos, freqs_sin,
+                  mini_batch_size, base_lr):
+    """The TTT layer's input prologue (ttt_layer.py:261-330 with no text prefix, no multi-scene
+    interleave, no tensor parallelism): projections (:141-148), L2 normalisation of XQ, XK, XU
+    (:276-278), rotary embedding of XQ, XK and XU (:284-295, utils.py:97-123), the LayerNorm
+    reconstruction target XV <- LN(XV - XK) + XK with the unbiased std and eps 1e-8 added to it
+    (:227-244), the kernel layout [B, NH, NC, CS, F] (:246-259) and the learning rate
+    eta = 1/CS * base_lr * sigmoid(X w_h + b_h) / F repeated over rows (:150-163, :309).
+
+    hidden [B, L, W]; w* [W, W], b* [W] (nn.Linear); lr_w [NH, 1, W], lr_b [NH, 1];
+    ln_w, ln_b [NH, F]; freqs_cos / freqs_sin [L, F/2] (the real and imaginary parts of the
+    layer's freqs_cis rows 0..L-1). Returns XQ, XK, XV, XU, eta.
+    """
+    B, L, W = hidden.shape
+    NH = ln_w.shape[0]
+    F = W // NH
+    CS = int(mini_batch_size)
+    NC = L // CS
+
+    def heads(x):
+        return x.reshape(B, L, NH, F)
+
+    def rope(x):
+        a, b = x[..., 0::2], x[..., 1::2]
+        c = freqs_cos[:L].reshape(1, L, 1, F // 2)
+        sn = freqs_sin[:L].reshape(1, L, 1, F // 2)
+        return torch.stack((a * c - b * sn, a * sn + b * c), dim=-1).flatten(-2)
+
+    XQ = heads(hidden @ wq.T + bq)
+    XK = heads(hidden @ wk.T + bk)
+    XV = heads(hidden @ wv.T + bv)
+    XU = heads(hidden @ wu.T + bu)
+    XQ = rope(Fn.normalize(XQ, p=2, dim=-1))
+    XK = rope(Fn.normalize(XK, p=2, dim=-1))
+    XU = rope(Fn.normalize(XU, p=2, dim=-1))
+    Y = XV - XK
+    Y = (Y - Y.mean(dim=-1, keepdim=True)) / (Y.std(dim=-1, keepdim=True) + 1e-8)
+    XV = ln_w.reshape(1, 1, NH, F) * Y + ln_b.reshape(1, 1, NH, F) + XK
+
+    def layout(x):
+        return x.transpose(1, 2).reshape(B, NH, NC, CS, F)
+
+    Xmb = hidden.reshape(B, NC, CS, W)
+    lr = torch.einsum("bnkc,hdc->bhnkd", Xmb, lr_w) + lr_b.reshape(1, -1, 1, 1, 1)
+    lr = torch.sigmoid(lr).permute(0, 1, 2, 4, 3)  # [B, NH, NC, 1, CS]
+    eta = (1.0 / CS) * (base_lr * lr / F).repeat(1, 1, 1, CS, 1)
+    return {"XQ": layout(XQ), "XK": layout(XK), "XV": layout(XV), "XU": layout(XU), "eta": eta}
+
+
+PROLOGUE_PARAM_NAMES = ("hidden", "wq", "bq", "wk", "bk", "wv", "bv", "wu", "bu", "lr_w", "lr_b", "ln_w", "ln_b")
+
+
+def process_input_grads(inp, douts, mini_batch_size, base_lr):
+    """Autograd gradients of sum_k <out_k, douts[k]> w.r.t. every prologue input."""
+    leaves = {k: inp[k].detach().clone().requires_grad_(True) for k in PROLOGUE_PARAM_NAMES}
+    out = process_input(*(leaves[k] for k in PROLOGUE_PARAM_NAMES), inp["freqs_cos"], inp["freqs_sin"],
+                        mini_batch_size, base_lr)
+    loss = sum((out[k] * douts[k]).sum() for k in ("XQ", "XK", "XV", "XU", "eta"))
+    loss.backward()
+    return {k: leaves[k].grad for k in PROLOGUE_PARAM_NAMES}, {k: v.detach() for k, v in out.items()}
+
+
 MEMO_MIX_GRAD_NAMES = ("XQW", "XU", "XK")
 
 

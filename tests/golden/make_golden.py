@@ -11,7 +11,8 @@ cycle), runs it in float64 on seeded float32-representable inputs, and takes gra
 with torch autograd exactly as the reference's training path does. The cached-readout
 golden runs the reference's Triton kernel (kernels/mlp_cached_readout.py:7-109) under
 the Triton CPU interpreter at B = NH = 1, the only slice its offsets address correctly; the
-memo-mixing golden runs the reference's own mixing loop of TTTMLP.ttt with that kernel.
+memo-mixing golden runs the reference's own mixing loop of TTTMLP.ttt with that kernel, and
+the prologue golden the layer's own process_input.
 
 Outputs ``tests/golden/*.npz`` (float32 storage). The GPU box never runs this script.
 """
@@ -191,6 +192,48 @@ def memo_mix_case(ref_root, NC, F, FF, M, seed):
     return {k: _np(v) for k, v in res.items()}
 
 
+def prologue_case(ref_root, B, L, W, NH, CS, seed):
+    """The reference layer's own input prologue: TTTMLP.process_input (ttt_layer.py:261-330)
+    of a TTTWrapper built from a ModelConfig, eager (TorchDynamo disabled), float64, with
+    autograd gradients of every input. freqs_cis is the wrapper's own buffer."""
+    sys.path.insert(0, ref_root)
+    import forecast
+    import ttt_layer
+
+    torch.manual_seed(seed)
+    cfg = forecast.ModelConfig(seq_len=L, model_dim=W, num_heads=NH, mini_batch_size=CS, ssm_layer="ttt_mlp",
+                               use_kernel=False, ttt_base_lr=0.1)
+    wrapper = ttt_layer.TTTWrapper(cfg).double()
+    layer = wrapper.ttt
+    with torch.no_grad():  # non-trivial gate and LN parameters
+        layer.learnable_ttt_lr_bias.normal_(0, 0.5)
+        layer.ttt_norm_weight.add_(0.1 * torch.randn_like(layer.ttt_norm_weight))
+        layer.ttt_norm_bias.add_(0.1 * torch.randn_like(layer.ttt_norm_bias))
+    hidden = torch.randn(B, L, W, dtype=torch.float64, requires_grad=True)
+    out = layer.process_input(hidden, wrapper.freqs_cis, forecast.SequenceMetadata())
+    g = torch.Generator().manual_seed(seed + 1)
+    douts = {k: torch.randn(out[k].shape, generator=g, dtype=torch.float64) for k in ("XQ", "XK", "XV", "XU", "eta")}
+    loss = sum((out[k] * douts[k]).sum() for k in douts)
+    loss.backward()
+    fc = wrapper.freqs_cis[:L]
+    res = {
+        "in_hidden": hidden.detach(), "in_wq": layer.wq.weight, "in_bq": layer.wq.bias, "in_wk": layer.wk.weight,
+        "in_bk": layer.wk.bias, "in_wv": layer.wv.weight, "in_bv": layer.wv.bias, "in_wu": layer.wu.weight,
+        "in_bu": layer.wu.bias, "in_lr_w": layer.learnable_ttt_lr_weight, "in_lr_b": layer.learnable_ttt_lr_bias,
+        "in_ln_w": layer.ttt_norm_weight, "in_ln_b": layer.ttt_norm_bias,
+        "in_freqs_cos": fc.real, "in_freqs_sin": fc.imag, "CS": torch.tensor(CS), "base_lr": torch.tensor(0.1),
+    }
+    res.update({"out_" + k: v for k, v in out.items()})
+    res.update({"d_" + k: v for k, v in douts.items()})
+    grads = {"hidden": hidden.grad, "wq": layer.wq.weight.grad, "bq": layer.wq.bias.grad,
+             "wk": layer.wk.weight.grad, "bk": layer.wk.bias.grad, "wv": layer.wv.weight.grad,
+             "bv": layer.wv.bias.grad, "wu": layer.wu.weight.grad, "bu": layer.wu.bias.grad,
+             "lr_w": layer.learnable_ttt_lr_weight.grad, "lr_b": layer.learnable_ttt_lr_bias.grad,
+             "ln_w": layer.ttt_norm_weight.grad, "ln_b": layer.ttt_norm_bias.grad}
+    res.update({"grad_" + k: v for k, v in grads.items()})
+    return {k: _np(v) for k, v in res.items()}
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     sys.path.insert(0, ref_root)
@@ -205,6 +248,7 @@ def main():
         "mlp_fxf_equal_eta": mlp_case(ref_ops, B=1, NH=2, NC=3, F=32, FF=32, ckpt=16, eta_mode="equal", seed=21),
         "cached_readout": cached_readout_case(ref_root, NCs=3, F=32, FF=128, seed=30),
         "memo_mix": memo_mix_case(ref_root, NC=7, F=32, FF=128, M=2, seed=40),
+        "prologue": prologue_case(ref_root, B=2, L=64, W=128, NH=2, CS=16, seed=50),
     }
     for name, res in cases.items():
         path = os.path.join(HERE, name + ".npz")

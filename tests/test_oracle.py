@@ -66,6 +66,19 @@ def test_memo_mix_oracle_matches_reference_loop():
         assert O.rel_l2(grads[k], g["grad_" + k].double()) < 1e-6, k
 
 
+def test_prologue_oracle_matches_reference_process_input():
+    """The input-prologue restatement (projections, L2 norm, rotary embedding, LN target,
+    eta) against the reference layer's own process_input, outputs and every gradient."""
+    inp, g = load_golden("prologue")
+    inp = {k: v.double() for k, v in inp.items()}
+    douts = {k[2:]: v.double() for k, v in g.items() if k.startswith("d_")}
+    grads, out = O.process_input_grads(inp, douts, int(g["CS"]), float(g["base_lr"]))
+    for k, v in out.items():
+        assert O.rel_l2(v, g["out_" + k].double()) < 1e-6, k
+    for k in O.PROLOGUE_PARAM_NAMES:
+        assert O.rel_l2(grads[k], g["grad_" + k].double()) < 1e-6, k
+
+
 @pytest.mark.parametrize("eta_mode", ["causal", "equal"])
 @pytest.mark.parametrize("ckpt", [1, 3, 16])
 def test_linear_hand_backward_matches_autograd(eta_mode, ckpt):
