@@ -14,6 +14,9 @@ ttt-triton_b200/synthetic.py):
 * ``mlp_fwdbwd_c3``: TTT-MLP forward+backward, bf16, B64 NH16 L8192 F64 FF256, memo 16 (config 3).
 * ``memo_mix_c3``: the layer's memo-state mixing (cached read-outs of every earlier memo
   state, ttt_layer.py:503-559), forward+backward, at the config-3 shape (32 memo segments).
+* ``prologue_c4``: one TTT layer's input prologue (process_input, ttt_layer.py:261-330:
+  projections, L2 norm, rotary embedding, LN target, eta), forward+backward, bf16, at the
+  config-4 forecaster shape (global batch 256, lookback 336, d_model 256, 4 heads).
 
 A step is one pass of the hot path over one batch. Multi-GPU runs are weak scaling:
 every rank processes its own full batch (the (b, h) streams are independent, so there
@@ -45,8 +48,13 @@ WORKLOADS = {
     "linear_fwdbwd_c2": dict(kind="linear", B=32, NH=8, L=4096, F=64, FF=None, dtype="bf16", bwd=True, ckpt=16, memo=None),
     "mlp_fwdbwd_c3": dict(kind="mlp", B=64, NH=16, L=8192, F=64, FF=256, dtype="bf16", bwd=True, ckpt=16, memo=16),
     "memo_mix_c3": dict(kind="memo", B=64, NH=16, L=8192, F=64, FF=256, dtype="bf16", bwd=True, ckpt=16, memo=16),
+    "prologue_c4": dict(kind="prologue", B=256, NH=4, L=336, F=64, FF=None, dtype="bf16", bwd=True, ckpt=None,
+                        memo=None),
 }
 MEMO = ("XQW", "XQ", "XK", "XU", "W1_memo", "b1_memo", "W2_memo", "b2_memo", "ln_w", "ln_b")
+PRO = ("hidden", "wq", "bq", "wk", "bk", "wv", "bv", "wu", "bu", "lr_w", "lr_b", "ln_w", "ln_b")
+PRO_OUTS = ("XQ", "XK", "XV", "XU", "eta")
+BASE_LR = 0.1  # forecast.ModelConfig.ttt_base_lr
 CS = 16
 DT = {"f32": torch.float32, "bf16": torch.bfloat16}
 # DRAM bytes (read + write) of one launch of the dominant kernel from an ncu capture of
@@ -83,6 +91,15 @@ def algorithmic(w):
     """
     F, FF = w["F"], w["FF"]
     eb = 4 if w["dtype"] == "f32" else 2
+    if w["kind"] == "prologue":
+        # Per (token, head): the element-wise forward reads the head's projection segment
+        # (q, k, v, u and the gate: 4F + 1) and writes XQ, XK, XV, XU and its eta column (CS
+        # rows); the backward reads that segment, dXQ, dXK, dXV, dXU and the d_eta column and
+        # writes d proj. FLOPs are the projection GEMMs: 2 * W * (4F + 1) forward, twice that
+        # backward (d hidden and d weights), W = NH * F.
+        Wd = w["NH"] * F
+        return {"fwd": (eb * (8 * F + 1 + CS), 2 * Wd * (4 * F + 1)),
+                "bwd": (eb * (12 * F + 2 + CS), 4 * Wd * (4 * F + 1))}
     if w["kind"] == "memo":
         # forward reads XQW, XQ, XK, XU and writes the output; backward re-reads XQW, XQ, XK,
         # XU, reads dOut and writes dXQW, dXU, dXK. Each token of segment i reads out the i
@@ -109,6 +126,13 @@ def make_inputs(w, device, seed):
 
     NC = w["L"] // CS
     dt = DT[w["dtype"]]
+    if w["kind"] == "prologue":
+        d = S.make_prologue_inputs(w["B"], w["L"], w["NH"] * w["F"], w["NH"], device=device, seed=seed)
+        d = {k: (v if k in ("ln_w", "ln_b", "freqs_cos", "freqs_sin") else v.to(dt)) for k, v in d.items()}
+        shp = (w["B"], w["NH"], NC, CS, w["F"])
+        dO = {k: S.make_upstream(shp if k != "eta" else shp[:-1] + (CS,), device=device, seed=seed + 1 + i, dtype=dt)
+              for i, k in enumerate(PRO_OUTS)}
+        return d, dO
     if w["kind"] == "memo":
         return S.make_memo_inputs(w["B"], w["NH"], NC, CS, w["F"], w["FF"], w["memo"], dtype=dt, device=device,
                                   seed=seed), S.make_upstream((w["B"], w["NH"], NC, CS, w["F"]), device=device,
@@ -130,6 +154,9 @@ def kernel_step(w, d, dO):
     Returns the number of kernel launches it made."""
     import _core
 
+    if w["kind"] == "prologue":
+        prologue_step(w, d, dO)
+        return 2
     if w["kind"] == "memo":
         _core.memo_mix_forward(*(d[k] for k in MEMO), w["memo"])
         if w["bwd"]:
@@ -151,6 +178,36 @@ def kernel_step(w, d, dO):
     return 1
 
 
+def prologue_step(w, d, dO, time_bwd_kernel=False):
+    """Forward and backward of the prologue through the functional core: the projection GEMM
+    (library), the element-wise forward kernel, the element-wise backward kernel and the two
+    projection-gradient GEMMs (library). With time_bwd_kernel, returns the backward kernel's
+    CUDA-event time in ms."""
+    import _core
+    from prologue import concat_projections
+
+    B, L, NH, F = w["B"], w["L"], w["NH"], w["F"]
+    Wcat, bcat, _, _ = concat_projections(*(d[k] for k in PRO[1:11]))
+    h2 = d["hidden"].reshape(B * L, -1)
+    P = torch.addmm(bcat, h2, Wcat.t())
+    scale = BASE_LR / (F * CS)
+    _core.prologue_forward(P, B, L, NH, F, CS, d["ln_w"], d["ln_b"], d["freqs_cos"], d["freqs_sin"], scale)
+    if time_bwd_kernel:
+        stream = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+    dP, _, _, _ = _core.prologue_backward(P, B, L, NH, F, CS, d["ln_w"], d["ln_b"], d["freqs_cos"],
+                                          d["freqs_sin"], scale, *(dO[k] for k in PRO_OUTS))
+    if time_bwd_kernel:
+        e1.record(stream)
+    torch.mm(dP, Wcat)
+    torch.mm(dP.t(), h2)
+    if time_bwd_kernel:
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+    return None
+
+
 def api_step(w, host, dev_bufs, out_host):
     """End-to-end step through the public API with host buffers: H2D copies of every
     input, the reference-facing call (TritonLinear / TritonMLP .apply, plus backward),
@@ -163,6 +220,18 @@ def api_step(w, host, dev_bufs, out_host):
         dev_bufs[k].copy_(t, non_blocking=True)
         h2d += t.numel() * t.element_size()
     d = dev_bufs
+    if w["kind"] == "prologue":
+        from prologue import ttt_prologue
+
+        leaves = [d[k].requires_grad_(True) for k in PRO]
+        out = ttt_prologue(*leaves, (d["freqs_cos"], d["freqs_sin"]), CS, BASE_LR)
+        torch.autograd.backward([out[k] for k in PRO_OUTS], [d["d_" + k] for k in PRO_OUTS])
+        res = d["hidden"].grad
+        for t in leaves:
+            t.grad = None
+            t.requires_grad_(False)
+        out_host.copy_(res.detach(), non_blocking=True)
+        return h2d, out_host.numel() * out_host.element_size()
     if w["kind"] == "memo":
         from kernels.mlp_memo_mix import mlp_memo_mix
 
@@ -264,6 +333,21 @@ def cpu_reference(w, budget_s=12.0):
     torch.set_num_threads(threads)
     NC = w["L"] // CS
     B, NH = 1, min(w["NH"], 4)
+    if w["kind"] == "prologue":
+        B = 32
+        d = S.make_prologue_inputs(B, w["L"], w["NH"] * w["F"], w["NH"], seed=0)
+        shp = (B, w["NH"], NC, CS, w["F"])
+        dO = {k: S.make_upstream(shp if k != "eta" else shp[:-1] + (CS,), seed=1 + i) for i, k in enumerate(PRO_OUTS)}
+        best, reps = None, 0
+        t_end = time.perf_counter() + budget_s
+        while reps < 1 or (time.perf_counter() < t_end and reps < 20):
+            t0 = time.perf_counter()
+            O.process_input_grads(d, dO, CS, BASE_LR)
+            dt = time.perf_counter() - t0
+            best = dt if best is None else min(best, dt)
+            reps += 1
+        sample = f"B={B} L={w['L']} W={w['NH'] * w['F']} NH={w['NH']} (batch slice), fp32, fwd+bwd, best of {reps}"
+        return B * w["NH"] * w["L"] / best, threads, sample
     if w["kind"] == "memo":
         B, NH = 1, 1
         d = S.make_memo_inputs(B, NH, NC, CS, w["F"], w["FF"], w["memo"], seed=0)
@@ -425,6 +509,8 @@ def kernel_durations(w, d, dO, steps):
     stream = torch.cuda.current_stream()
     tot = 0.0
     n = max(1, min(steps, 5))
+    if w["kind"] == "prologue":
+        return sum(prologue_step(w, d, dO, time_bwd_kernel=True) for _ in range(n)) / n
     for _ in range(n):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if w["kind"] == "memo":
@@ -456,10 +542,13 @@ def kernel_durations(w, d, dO, steps):
 
 def e2e_time(w, d, dO, dev, args):
     host = {k: v.detach().cpu().pin_memory() for k, v in d.items()}
-    if dO is not None:
+    if isinstance(dO, dict):
+        host.update({"d_" + k: v.cpu().pin_memory() for k, v in dO.items()})
+    elif dO is not None:
         host["dO"] = dO.cpu().pin_memory()
     dev_bufs = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
-    out_host = torch.empty(d["XQ"].shape, dtype=d["XQ"].dtype).pin_memory()
+    res = d["hidden"] if w["kind"] == "prologue" else d["XQ"]
+    out_host = torch.empty(res.shape, dtype=res.dtype).pin_memory()
     for _ in range(max(1, min(args.warmup, 2))):
         api_step(w, host, dev_bufs, out_host)
     torch.cuda.synchronize()

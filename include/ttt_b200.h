@@ -180,6 +180,39 @@ int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, int memo_segm
                      void* scratch, size_t scratch_bytes, void* stream);
 
 /*
+ * Input prologue of the TTT layer, forward: everything TTTBase.process_input
+ * (ttt_layer.py:261-330; no text prefix, no multi-scene interleave, no tensor parallelism)
+ * does after its projections (get_qkvu_projections :141-148 and the learning-rate gate of
+ * get_eta :150-163, which the caller runs as one GEMM). proj is [B * L][ld_proj] (ld_proj a
+ * multiple of 8, at least 4 * NH * F + NH) holding, per token, the projections
+ * q | k | v | u (NH * F columns each, head-major) and the NH gate logits, biases included.
+ * Writes XQ, XK, XU = rope(l2_normalize(.)) (:276-295, utils.py:97-123), the LayerNorm
+ * reconstruction target XV (:227-244: unbiased std, eps 1e-8 added to it, ln_w/ln_b
+ * [NH][F]) in [B, NH, NC, CS, F] and eta = eta_scale * sigmoid(gate) repeated over the rows
+ * of each mini-batch in [B, NH, NC, CS, CS] (:309), eta_scale = ttt_base_lr / (F * CS).
+ * rope_cos / rope_sin are [L][F / 2] (real and imaginary parts of freqs_cis rows 0..L-1).
+ * F is 16, 32, 64 or 128; L a multiple of CS, CS at most 256. proj, the outputs and eta
+ * share dtype dt; every pointer is 16-byte aligned.
+ */
+int ttt_prologue_fwd(int B, int L, int NH, int F, int CS, const void* proj, int dt, long long ld_proj,
+                     const float* ln_w, const float* ln_b, const float* rope_cos, const float* rope_sin,
+                     float eta_scale, void* XQ, void* XK, void* XV, void* XU, void* eta, void* stream);
+
+/*
+ * Input prologue, backward: from the gradients of XQ, XK, XV, XU, eta (each may be NULL,
+ * meaning zero) and the same proj, writes d proj ([B * L][ld_proj], dtype dt; the padding
+ * columns past 4 * NH * F + NH are written as zeros) and ADDS the LayerNorm parameter
+ * gradients into dln_w / dln_b ([NH][F] fp32) and, when dbias is not NULL, the column sums
+ * of d proj (the projection bias gradients) into dbias ([4 * NH * F + NH] fp32). The caller
+ * finishes with library GEMMs: d hidden = d proj W_cat, d W_cat = d proj^T hidden.
+ * Pointers are 16-byte aligned (d_eta: element aligned); CS is at most 256.
+ */
+int ttt_prologue_bwd(int B, int L, int NH, int F, int CS, const void* proj, int dt, long long ld_proj,
+                     const float* ln_w, const float* ln_b, const float* rope_cos, const float* rope_sin,
+                     float eta_scale, const void* dXQ, const void* dXK, const void* dXV, const void* dXU,
+                     const void* deta, void* dproj, float* dln_w, float* dln_b, float* dbias, void* stream);
+
+/*
  * Reads and clears this library's device error word for the current device, synchronising
  * with it. Non-zero bits mean a kernel gave up waiting for its own asynchronous copies
  * (bit 0: a TMA stage did not land within 2 s) and voided the affected streams' results.

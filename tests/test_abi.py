@@ -122,3 +122,23 @@ def test_memo_mix_host_checks():
     assert fwd(8, 2, nbytes=16) == -5
     # W1/W2 16-bit copies (2 * F * FF * 2 bytes) plus summary and its gradient (2 * F * 4) per memo state
     assert _lib.lib.ttt_memo_mix_scratch_bytes(2, 3, 9, 4) == 2 * 3 * 3 * (2 * 64 * 256 * 2 + 2 * 64 * 4)
+
+
+def test_prologue_host_checks():
+    """ttt_prologue_fwd / _bwd reject bad sizes, strides, dtypes and alignment on the host."""
+    A = ctypes.c_void_p(0x1000)
+
+    def fwd(B=2, L=32, NH=4, F=64, CS=16, P=A, dt=1, ld=4 * 4 * 64 + 8, out=A):
+        return _lib.lib.ttt_prologue_fwd(B, L, NH, F, CS, P, dt, ld, A, A, A, A, 0.1, out, out, out, out, out, None)
+
+    assert fwd(P=None) == -1
+    assert fwd(out=None) == -1
+    assert fwd(F=48) == -2 and "head_dim" in _lib.lib.ttt_last_error().decode()
+    assert fwd(L=40) == -2 and "multiple" in _lib.lib.ttt_last_error().decode()
+    assert fwd(dt=9) == -3
+    assert fwd(ld=4 * 4 * 64) == -2  # no room for the gate columns
+    assert fwd(ld=4 * 4 * 64 + 6) == -2  # not a multiple of 8
+    assert fwd(P=ctypes.c_void_p(0x1002)) == -7
+    rc = _lib.lib.ttt_prologue_bwd(1, 16, 4, 64, 16, A, 1, 4 * 4 * 64 + 8, A, A, A, A, 0.1, None, None, None, None,
+                                   None, None, A, A, None, None)
+    assert rc == -1  # dproj is required; the incoming gradients may all be NULL

@@ -349,3 +349,66 @@ def memo_mix_backward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w,
     )
     check(rc, "ttt_memo_mix_bwd")
     return dXQW, dXU, dXK
+
+
+# --------------------------------------------------------------------------- input prologue
+def prologue_ld(NH, F):
+    """Row stride of the projection matrix: q | k | v | u (NH * F each) | NH gates, padded to 8."""
+    n = 4 * NH * F + NH
+    return (n + 7) // 8 * 8
+
+
+def _prologue_args(P, B, L, NH, F, CS, ln_w, ln_b, rope_cos, rope_sin):
+    require_cuda(P, ln_w, ln_b, rope_cos, rope_sin)
+    ld = prologue_ld(NH, F)
+    if P.dim() != 2 or tuple(P.shape) != (B * L, ld) or not P.is_contiguous():
+        raise ValueError(f"projections must be a contiguous [B * L, {ld}] matrix, got {tuple(P.shape)}")
+    if L % CS:
+        raise ValueError(f"sequence length {L} must be a multiple of mini_batch_size {CS}")
+    ln_w, ln_b = _check_ln(ln_w.to(torch.float32), ln_b.to(torch.float32), NH, F)
+    for name, t in (("rope_cos", rope_cos), ("rope_sin", rope_sin)):
+        if tuple(t.shape) != (L, F // 2) or t.dtype != torch.float32:
+            raise ValueError(f"{name} must be float32 [{L}, {F // 2}], got {t.dtype} {tuple(t.shape)}")
+    return ld, ln_w, ln_b, _c(rope_cos), _c(rope_sin)
+
+
+def prologue_forward(P, B, L, NH, F, CS, ln_w, ln_b, rope_cos, rope_sin, eta_scale):
+    """Element-wise prologue over the projection matrix P ([B * L, prologue_ld], biases
+    included). Returns XQ, XK, XV, XU [B, NH, NC, CS, F] and eta [B, NH, NC, CS, CS] in P's dtype."""
+    ld, ln_w, ln_b, rope_cos, rope_sin = _prologue_args(P, B, L, NH, F, CS, ln_w, ln_b, rope_cos, rope_sin)
+    NC = L // CS
+    outs = [torch.empty(B, NH, NC, CS, F, device=P.device, dtype=P.dtype) for _ in range(4)]
+    eta = torch.empty(B, NH, NC, CS, CS, device=P.device, dtype=P.dtype)
+    rc = lib.ttt_prologue_fwd(
+        B, L, NH, F, CS, ptr(P), dtype_code(P), ld, ptr(ln_w), ptr(ln_b), ptr(rope_cos), ptr(rope_sin),
+        float(eta_scale), *(ptr(o) for o in outs), ptr(eta), stream_of(P),
+    )
+    check(rc, "ttt_prologue_fwd")
+    return (*outs, eta)
+
+
+def prologue_backward(P, B, L, NH, F, CS, ln_w, ln_b, rope_cos, rope_sin, eta_scale, dXQ, dXK, dXV, dXU, deta):
+    """Gradient of the element-wise prologue: returns dP ([B * L, prologue_ld], P's dtype;
+    padding columns zero), d ln_w, d ln_b ([NH, F] fp32) and the column sums of dP (the
+    projection bias gradient, [prologue_ld] fp32). Gradients may be None."""
+    ld, ln_w, ln_b, rope_cos, rope_sin = _prologue_args(P, B, L, NH, F, CS, ln_w, ln_b, rope_cos, rope_sin)
+    NC = L // CS
+    grads = []
+    for name, g, shape in (("dXQ", dXQ, (B, NH, NC, CS, F)), ("dXK", dXK, (B, NH, NC, CS, F)),
+                           ("dXV", dXV, (B, NH, NC, CS, F)), ("dXU", dXU, (B, NH, NC, CS, F)),
+                           ("d_eta", deta, (B, NH, NC, CS, CS))):
+        if g is not None:
+            if tuple(g.shape) != shape:
+                raise ValueError(f"{name} must be {shape}, got {tuple(g.shape)}")
+            g = _c(g.to(P.dtype))
+        grads.append(g)
+    dP = torch.empty_like(P)
+    dln_w = torch.zeros(NH, F, device=P.device, dtype=torch.float32)
+    dln_b = torch.zeros(NH, F, device=P.device, dtype=torch.float32)
+    dbias = torch.zeros(ld, device=P.device, dtype=torch.float32)
+    rc = lib.ttt_prologue_bwd(
+        B, L, NH, F, CS, ptr(P), dtype_code(P), ld, ptr(ln_w), ptr(ln_b), ptr(rope_cos), ptr(rope_sin),
+        float(eta_scale), *(ptr(g) for g in grads), ptr(dP), ptr(dln_w), ptr(dln_b), ptr(dbias), stream_of(P),
+    )
+    check(rc, "ttt_prologue_bwd")
+    return dP, dln_w, dln_b, dbias

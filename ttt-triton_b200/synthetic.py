@@ -99,6 +99,35 @@ def make_memo_inputs(B, NH, NC, CS=16, F=64, FF=256, memo_segment_size=16, dtype
     return d
 
 
+def rope_cos_sin(L, F, theta=10000.0, device="cpu"):
+    """fp32 [L, F/2] cosine and sine tables of the standard 1-D rotary frequencies
+    theta^(-2i/F) at positions 0..L-1 (the kernels take any table; the reference layer builds
+    its freqs_cis with a 3-D variant, utils.py)."""
+    inv = theta ** (-torch.arange(0, F, 2, dtype=torch.float64, device=device) / F)
+    ang = torch.arange(L, dtype=torch.float64, device=device)[:, None] * inv[None, :]
+    return torch.cos(ang).float(), torch.sin(ang).float()
+
+
+def make_prologue_inputs(B, L, W, NH, device="cpu", seed=0):
+    """A TTT layer's input prologue at the given shapes (fp32): hidden ~ N(0, 1) [B, L, W];
+    projection weights ~ N(0, 0.02^2) and gate weight ~ N(0, 0.02^2) as init_weights
+    (ttt_layer.py:81-89), biases ~ N(0, 0.02^2), gate bias ~ N(0, 0.5^2) and LayerNorm
+    gamma ~ 1 + N(0, 0.1^2), beta ~ N(0, 0.1^2) so every gradient is exercised; rotary
+    tables from rope_cos_sin."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    F = W // NH
+    d = {"hidden": _randn((B, L, W), g, device)}
+    for k in ("q", "k", "v", "u"):
+        d["w" + k] = _randn((W, W), g, device) * 0.02
+        d["b" + k] = _randn((W,), g, device) * 0.02
+    d["lr_w"] = _randn((NH, 1, W), g, device) * 0.02
+    d["lr_b"] = _randn((NH, 1), g, device) * 0.5
+    d["ln_w"] = 1.0 + 0.1 * _randn((NH, F), g, device)
+    d["ln_b"] = 0.1 * _randn((NH, F), g, device)
+    d["freqs_cos"], d["freqs_sin"] = rope_cos_sin(L, F, device=device)
+    return d
+
+
 def make_upstream(shape, device="cpu", seed=1, dtype=torch.float32):
     """dZ ~ N(0, 1) with the output's shape."""
     g = torch.Generator(device=device).manual_seed(seed)
