@@ -17,6 +17,8 @@ ttt-triton_b200/synthetic.py):
 * ``prologue_c4``: one TTT layer's input prologue (process_input, ttt_layer.py:261-330:
   projections, L2 norm, rotary embedding, LN target, eta), forward+backward, bf16, at the
   config-4 forecaster shape (global batch 256, lookback 336, d_model 256, 4 heads).
+* ``epilogue_c4``: the layer's output epilogue (scan output -> post_norm -> wo,
+  ttt_layer.py:349-350, 563-564), forward+backward, bf16, at the same shape.
 
 A step is one pass of the hot path over one batch. Multi-GPU runs are weak scaling:
 every rank processes its own full batch (the (b, h) streams are independent, so there
@@ -50,11 +52,16 @@ WORKLOADS = {
     "memo_mix_c3": dict(kind="memo", B=64, NH=16, L=8192, F=64, FF=256, dtype="bf16", bwd=True, ckpt=16, memo=16),
     "prologue_c4": dict(kind="prologue", B=256, NH=4, L=336, F=64, FF=None, dtype="bf16", bwd=True, ckpt=None,
                         memo=None),
+    "epilogue_c4": dict(kind="epilogue", B=256, NH=4, L=336, F=64, FF=None, dtype="bf16", bwd=True, ckpt=None,
+                        memo=None),
 }
 MEMO = ("XQW", "XQ", "XK", "XU", "W1_memo", "b1_memo", "W2_memo", "b2_memo", "ln_w", "ln_b")
 PRO = ("hidden", "wq", "bq", "wk", "bk", "wv", "bv", "wu", "bu", "lr_w", "lr_b", "ln_w", "ln_b")
 PRO_OUTS = ("XQ", "XK", "XV", "XU", "eta")
 BASE_LR = 0.1  # forecast.ModelConfig.ttt_base_lr
+EPI = ("XQW", "pn_w", "pn_b", "wo_w", "wo_b")
+POST_NORM_EPS = 1e-6  # ttt_layer.py:77
+RESULT_KEY = {"prologue": "hidden", "epilogue": "XQW"}  # the input whose gradient e2e reads back
 CS = 16
 DT = {"f32": torch.float32, "bf16": torch.bfloat16}
 # DRAM bytes (read + write) of one launch of the dominant kernel from an ncu capture of
@@ -100,6 +107,13 @@ def algorithmic(w):
         Wd = w["NH"] * F
         return {"fwd": (eb * (8 * F + 1 + CS), 2 * Wd * (4 * F + 1)),
                 "bwd": (eb * (12 * F + 2 + CS), 4 * Wd * (4 * F + 1))}
+    if w["kind"] == "epilogue":
+        # Per (token, head): the forward kernel reads the head's F scan outputs and writes F
+        # normalised values; the backward reads them again with F of d(normalised) and F of
+        # d out (for the wo bias gradient) and writes F of d XQW. FLOPs are the wo GEMMs:
+        # 2 * W * F forward, twice that backward.
+        Wd = w["NH"] * F
+        return {"fwd": (eb * 2 * F, 2 * Wd * F), "bwd": (eb * 4 * F, 4 * Wd * F)}
     if w["kind"] == "memo":
         # forward reads XQW, XQ, XK, XU and writes the output; backward re-reads XQW, XQ, XK,
         # XU, reads dOut and writes dXQW, dXU, dXK. Each token of segment i reads out the i
@@ -133,6 +147,15 @@ def make_inputs(w, device, seed):
         dO = {k: S.make_upstream(shp if k != "eta" else shp[:-1] + (CS,), device=device, seed=seed + 1 + i, dtype=dt)
               for i, k in enumerate(PRO_OUTS)}
         return d, dO
+    if w["kind"] == "epilogue":
+        g = torch.Generator(device=device).manual_seed(seed)
+        W = w["NH"] * w["F"]
+        d = {"XQW": (torch.randn(w["B"], w["NH"], NC, CS, w["F"], generator=g, device=device) * 0.5).to(dt),
+             "pn_w": 1 + 0.1 * torch.randn(W, generator=g, device=device),
+             "pn_b": 0.1 * torch.randn(W, generator=g, device=device),
+             "wo_w": (0.02 * torch.randn(W, W, generator=g, device=device)).to(dt),
+             "wo_b": (0.02 * torch.randn(W, generator=g, device=device)).to(dt)}
+        return d, S.make_upstream((w["B"], w["L"], W), device=device, seed=seed + 1, dtype=dt)
     if w["kind"] == "memo":
         return S.make_memo_inputs(w["B"], w["NH"], NC, CS, w["F"], w["FF"], w["memo"], dtype=dt, device=device,
                                   seed=seed), S.make_upstream((w["B"], w["NH"], NC, CS, w["F"]), device=device,
@@ -156,6 +179,9 @@ def kernel_step(w, d, dO):
 
     if w["kind"] == "prologue":
         prologue_step(w, d, dO)
+        return 2
+    if w["kind"] == "epilogue":
+        epilogue_step(w, d, dO)
         return 2
     if w["kind"] == "memo":
         _core.memo_mix_forward(*(d[k] for k in MEMO), w["memo"])
@@ -208,6 +234,29 @@ def prologue_step(w, d, dO, time_bwd_kernel=False):
     return None
 
 
+def epilogue_step(w, d, dO, time_bwd_kernel=False):
+    """Forward and backward of the output epilogue through the functional core: post_norm
+    kernel, wo GEMM (library), the two wo-gradient GEMMs and bias sum (library) and the
+    post_norm backward kernel. With time_bwd_kernel, returns that kernel's CUDA-event ms."""
+    import _core
+
+    Y = _core.post_norm_forward(d["XQW"], d["pn_w"], d["pn_b"], POST_NORM_EPS)
+    torch.addmm(d["wo_b"], Y, d["wo_w"].t())
+    d2 = dO.reshape(Y.shape)
+    dY = torch.mm(d2, d["wo_w"])
+    torch.mm(d2.t(), Y)
+    if time_bwd_kernel:
+        stream = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+    _core.post_norm_backward(d["XQW"], d["pn_w"], d["pn_b"], POST_NORM_EPS, dY, d2)
+    if time_bwd_kernel:
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+    return None
+
+
 def api_step(w, host, dev_bufs, out_host):
     """End-to-end step through the public API with host buffers: H2D copies of every
     input, the reference-facing call (TritonLinear / TritonMLP .apply, plus backward),
@@ -227,6 +276,18 @@ def api_step(w, host, dev_bufs, out_host):
         out = ttt_prologue(*leaves, (d["freqs_cos"], d["freqs_sin"]), CS, BASE_LR)
         torch.autograd.backward([out[k] for k in PRO_OUTS], [d["d_" + k] for k in PRO_OUTS])
         res = d["hidden"].grad
+        for t in leaves:
+            t.grad = None
+            t.requires_grad_(False)
+        out_host.copy_(res.detach(), non_blocking=True)
+        return h2d, out_host.numel() * out_host.element_size()
+    if w["kind"] == "epilogue":
+        from epilogue import post_norm_wo
+
+        leaves = [d[k].requires_grad_(True) for k in EPI]
+        out = post_norm_wo(*leaves, POST_NORM_EPS)
+        out.backward(d["dO"])
+        res = d["XQW"].grad
         for t in leaves:
             t.grad = None
             t.requires_grad_(False)
@@ -347,6 +408,23 @@ def cpu_reference(w, budget_s=12.0):
             best = dt if best is None else min(best, dt)
             reps += 1
         sample = f"B={B} L={w['L']} W={w['NH'] * w['F']} NH={w['NH']} (batch slice), fp32, fwd+bwd, best of {reps}"
+        return B * w["NH"] * w["L"] / best, threads, sample
+    if w["kind"] == "epilogue":
+        B = 32
+        g = torch.Generator().manual_seed(0)
+        W = w["NH"] * w["F"]
+        d = {"XQW": torch.randn(B, w["NH"], NC, CS, w["F"], generator=g) * 0.5, "pn_w": torch.ones(W),
+             "pn_b": torch.zeros(W), "wo_w": 0.02 * torch.randn(W, W, generator=g), "wo_b": torch.zeros(W)}
+        dout = torch.randn(B, w["L"], W, generator=g)
+        best, reps = None, 0
+        t_end = time.perf_counter() + budget_s
+        while reps < 1 or (time.perf_counter() < t_end and reps < 20):
+            t0 = time.perf_counter()
+            O.post_norm_wo_grads(d, dout)
+            dt = time.perf_counter() - t0
+            best = dt if best is None else min(best, dt)
+            reps += 1
+        sample = f"B={B} L={w['L']} W={W} NH={w['NH']} (batch slice), fp32, fwd+bwd, best of {reps}"
         return B * w["NH"] * w["L"] / best, threads, sample
     if w["kind"] == "memo":
         B, NH = 1, 1
@@ -511,6 +589,8 @@ def kernel_durations(w, d, dO, steps):
     n = max(1, min(steps, 5))
     if w["kind"] == "prologue":
         return sum(prologue_step(w, d, dO, time_bwd_kernel=True) for _ in range(n)) / n
+    if w["kind"] == "epilogue":
+        return sum(epilogue_step(w, d, dO, time_bwd_kernel=True) for _ in range(n)) / n
     for _ in range(n):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if w["kind"] == "memo":
@@ -547,7 +627,7 @@ def e2e_time(w, d, dO, dev, args):
     elif dO is not None:
         host["dO"] = dO.cpu().pin_memory()
     dev_bufs = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
-    res = d["hidden"] if w["kind"] == "prologue" else d["XQ"]
+    res = d[RESULT_KEY.get(w["kind"], "XQ")]
     out_host = torch.empty(res.shape, dtype=res.dtype).pin_memory()
     for _ in range(max(1, min(args.warmup, 2))):
         api_step(w, host, dev_bufs, out_host)

@@ -213,6 +213,28 @@ int ttt_prologue_bwd(int B, int L, int NH, int F, int CS, const void* proj, int 
                      const void* deta, void* dproj, float* dln_w, float* dln_b, float* dbias, void* stream);
 
 /*
+ * Output epilogue, forward: the layer's post_norm (nn.LayerNorm over the width W = NH * F,
+ * biased variance, eps inside the square root; ttt_layer.py:77,349) applied to the scan
+ * output XQW in its kernel layout [B, NH, NC, CS, F] (L = NC * CS), writing the normalised
+ * rows Y [B * L, W] in token order, which is the permute + reshape of TTTMLP.ttt
+ * (:563-564) folded into the read. ln_w / ln_b are [W] fp32; XQW and Y share dtype dt;
+ * F is a multiple of 16 bytes' worth of elements, W at most 1024 (512 in fp32); pointers
+ * 16-byte aligned. The caller applies wo (:350) with a library GEMM.
+ */
+int ttt_post_norm_fwd(int B, int NH, int L, int F, const void* XQW, int dt, const float* ln_w, const float* ln_b,
+                      float eps, void* Y, void* stream);
+
+/*
+ * Output epilogue, backward: from dY [B * L, W] (d out @ wo, a library GEMM) writes d XQW
+ * in the kernel layout and ADDS the post_norm weight / bias gradients into dln_w / dln_b
+ * ([W] fp32). With dOut (the gradient of the wo output, [B * L, W], dtype dt) it also ADDS
+ * dOut's column sums, the wo bias gradient, into dbias ([W] fp32); both or neither.
+ */
+int ttt_post_norm_bwd(int B, int NH, int L, int F, const void* XQW, int dt, const float* ln_w, const float* ln_b,
+                      float eps, const void* dY, void* dXQW, float* dln_w, float* dln_b, const void* dOut,
+                      float* dbias, void* stream);
+
+/*
  * Reads and clears this library's device error word for the current device, synchronising
  * with it. Non-zero bits mean a kernel gave up waiting for its own asynchronous copies
  * (bit 0: a TMA stage did not land within 2 s) and voided the affected streams' results.

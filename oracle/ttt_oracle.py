@@ -322,6 +322,27 @@ def process_input_grads(inp, douts, mini_batch_size, base_lr):
     return {k: leaves[k].grad for k in PROLOGUE_PARAM_NAMES}, {k: v.detach() for k, v in out.items()}
 
 
+def post_norm_wo(XQW, pn_w, pn_b, wo_w, wo_b, eps=1e-6):
+    """The layer's output epilogue: the scan output [B, NH, NC, CS, F] permuted to token order
+    [B, L, NH * F] (ttt_layer.py:563-564), post_norm = LayerNorm over the width with eps 1e-6
+    (:77, :349) and the wo projection (:350)."""
+    B, NH, NC, CS, F = XQW.shape
+    h = XQW.permute(0, 2, 3, 1, 4).reshape(B, NC * CS, NH * F)
+    h = Fn.layer_norm(h, (NH * F,), pn_w, pn_b, eps)
+    return h @ wo_w.T + wo_b
+
+
+EPILOGUE_PARAM_NAMES = ("XQW", "pn_w", "pn_b", "wo_w", "wo_b")
+
+
+def post_norm_wo_grads(inp, dout, eps=1e-6):
+    """Autograd gradients of <post_norm_wo(...), dout> w.r.t. every epilogue input."""
+    leaves = {k: inp[k].detach().clone().requires_grad_(True) for k in EPILOGUE_PARAM_NAMES}
+    out = post_norm_wo(*(leaves[k] for k in EPILOGUE_PARAM_NAMES), eps)
+    (out * dout).sum().backward()
+    return {k: leaves[k].grad for k in EPILOGUE_PARAM_NAMES}, out.detach()
+
+
 MEMO_MIX_GRAD_NAMES = ("XQW", "XU", "XK")
 
 

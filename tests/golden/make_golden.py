@@ -11,8 +11,8 @@ cycle), runs it in float64 on seeded float32-representable inputs, and takes gra
 with torch autograd exactly as the reference's training path does. The cached-readout
 golden runs the reference's Triton kernel (kernels/mlp_cached_readout.py:7-109) under
 the Triton CPU interpreter at B = NH = 1, the only slice its offsets address correctly; the
-memo-mixing golden runs the reference's own mixing loop of TTTMLP.ttt with that kernel, and
-the prologue golden the layer's own process_input.
+memo-mixing golden runs the reference's own mixing loop of TTTMLP.ttt with that kernel, the
+prologue golden the layer's own process_input and the epilogue golden its forward tail.
 
 Outputs ``tests/golden/*.npz`` (float32 storage). The GPU box never runs this script.
 """
@@ -234,6 +234,37 @@ def prologue_case(ref_root, B, L, W, NH, CS, seed):
     return {k: _np(v) for k, v in res.items()}
 
 
+def epilogue_case(ref_root, B, L, W, NH, CS, seed):
+    """The reference layer's own output epilogue: TTTBase.forward (ttt_layer.py:337-357) of a
+    TTTWrapper built from a ModelConfig, float64, with its ttt() replaced by a stub that
+    returns a given scan output XQW [B, NH, NC, CS, F] through TTTMLP.ttt's own tail
+    (permute(0, 2, 3, 1, 4) + reshape, :563-564); post_norm and wo are the layer's modules."""
+    sys.path.insert(0, ref_root)
+    import forecast
+    import ttt_layer
+
+    torch.manual_seed(seed)
+    cfg = forecast.ModelConfig(seq_len=L, model_dim=W, num_heads=NH, mini_batch_size=CS, ssm_layer="ttt_mlp",
+                               use_kernel=False)
+    wrapper = ttt_layer.TTTWrapper(cfg).double()
+    layer = wrapper.ttt
+    with torch.no_grad():
+        layer.post_norm.weight.add_(0.1 * torch.randn_like(layer.post_norm.weight))
+        layer.post_norm.bias.add_(0.1 * torch.randn_like(layer.post_norm.bias))
+    F, NC = W // NH, L // CS
+    XQW = torch.randn(B, NH, NC, CS, F, dtype=torch.float64, requires_grad=True)
+    layer.ttt = lambda inputs: XQW.permute(0, 2, 3, 1, 4).reshape(B, L, W)
+    hidden = torch.randn(B, L, W, dtype=torch.float64)
+    out = layer(hidden, wrapper.freqs_cis, forecast.SequenceMetadata())
+    dout = torch.randn(out.shape, generator=torch.Generator().manual_seed(seed + 1), dtype=torch.float64)
+    (out * dout).sum().backward()
+    res = {"in_XQW": XQW.detach(), "in_pn_w": layer.post_norm.weight, "in_pn_b": layer.post_norm.bias,
+           "in_wo_w": layer.wo.weight, "in_wo_b": layer.wo.bias, "out": out.detach(), "dout": dout,
+           "eps": torch.tensor(layer.post_norm.eps), "grad_XQW": XQW.grad, "grad_pn_w": layer.post_norm.weight.grad,
+           "grad_pn_b": layer.post_norm.bias.grad, "grad_wo_w": layer.wo.weight.grad, "grad_wo_b": layer.wo.bias.grad}
+    return {k: _np(v) for k, v in res.items()}
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     sys.path.insert(0, ref_root)
@@ -249,6 +280,7 @@ def main():
         "cached_readout": cached_readout_case(ref_root, NCs=3, F=32, FF=128, seed=30),
         "memo_mix": memo_mix_case(ref_root, NC=7, F=32, FF=128, M=2, seed=40),
         "prologue": prologue_case(ref_root, B=2, L=64, W=128, NH=2, CS=16, seed=50),
+        "epilogue": epilogue_case(ref_root, B=2, L=32, W=128, NH=4, CS=16, seed=60),
     }
     for name, res in cases.items():
         path = os.path.join(HERE, name + ".npz")

@@ -142,3 +142,21 @@ def test_prologue_host_checks():
     rc = _lib.lib.ttt_prologue_bwd(1, 16, 4, 64, 16, A, 1, 4 * 4 * 64 + 8, A, A, A, A, 0.1, None, None, None, None,
                                    None, None, A, A, None, None)
     assert rc == -1  # dproj is required; the incoming gradients may all be NULL
+
+
+def test_post_norm_host_checks():
+    A = ctypes.c_void_p(0x1000)
+
+    def fwd(B=2, NH=4, L=32, F=64, X=A, dt=1, eps=1e-6, Y=A):
+        return _lib.lib.ttt_post_norm_fwd(B, NH, L, F, X, dt, A, A, eps, Y, None)
+
+    assert fwd(X=None) == -1
+    assert fwd(Y=None) == -1
+    assert fwd(F=60) == -2 and "multiple" in _lib.lib.ttt_last_error().decode()
+    assert fwd(NH=32) == -2 and "width" in _lib.lib.ttt_last_error().decode()
+    assert fwd(dt=0, NH=16) == -2  # 1024 fp32 columns exceed the fp32 limit
+    assert fwd(dt=4) == -3
+    assert fwd(eps=-1.0) == -2
+    assert fwd(X=ctypes.c_void_p(0x1008)) == -7
+    assert _lib.lib.ttt_post_norm_bwd(2, 4, 32, 64, A, 1, A, A, 1e-6, None, A, A, A, None, None, None) == -1
+    assert _lib.lib.ttt_post_norm_bwd(2, 4, 32, 64, A, 1, A, A, 1e-6, A, A, A, A, A, None, None) == -1

@@ -79,6 +79,17 @@ def test_prologue_oracle_matches_reference_process_input():
         assert O.rel_l2(grads[k], g["grad_" + k].double()) < 1e-6, k
 
 
+def test_epilogue_oracle_matches_reference_forward_tail():
+    """The output-epilogue restatement (permute, post_norm, wo) against the reference layer's
+    own forward tail, output and every gradient."""
+    inp, g = load_golden("epilogue")
+    inp = {k: v.double() for k, v in inp.items()}
+    grads, out = O.post_norm_wo_grads(inp, g["dout"].double(), float(g["eps"]))
+    assert O.rel_l2(out, g["out"].double()) < 1e-6
+    for k in O.EPILOGUE_PARAM_NAMES:
+        assert O.rel_l2(grads[k], g["grad_" + k].double()) < 1e-6, k
+
+
 @pytest.mark.parametrize("eta_mode", ["causal", "equal"])
 @pytest.mark.parametrize("ckpt", [1, 3, 16])
 def test_linear_hand_backward_matches_autograd(eta_mode, ckpt):

@@ -412,3 +412,46 @@ def prologue_backward(P, B, L, NH, F, CS, ln_w, ln_b, rope_cos, rope_sin, eta_sc
     )
     check(rc, "ttt_prologue_bwd")
     return dP, dln_w, dln_b, dbias
+
+
+# --------------------------------------------------------------------------- output epilogue
+def _post_norm_args(XQW, ln_w, ln_b):
+    require_cuda(XQW, ln_w, ln_b)
+    if XQW.dim() != 5:
+        raise ValueError(f"XQW must be [B, NH, NC, CS, F], got shape {tuple(XQW.shape)}")
+    B, NH, NC, CS, F = XQW.shape
+    W = NH * F
+    if ln_w.numel() != W or ln_b.numel() != W:
+        raise ValueError(f"post_norm weight and bias must have NH * F = {W} elements")
+    return B, NH, NC * CS, F, _c(XQW), _c(ln_w.to(torch.float32)), _c(ln_b.to(torch.float32))
+
+
+def post_norm_forward(XQW, ln_w, ln_b, eps):
+    """LayerNorm over the width of the scan output, read in its kernel layout: returns the
+    normalised rows [B * L, NH * F] in XQW's dtype (token order)."""
+    B, NH, L, F, XQW, ln_w, ln_b = _post_norm_args(XQW, ln_w, ln_b)
+    Y = torch.empty(B * L, NH * F, device=XQW.device, dtype=XQW.dtype)
+    rc = lib.ttt_post_norm_fwd(B, NH, L, F, ptr(XQW), dtype_code(XQW), ptr(ln_w), ptr(ln_b), float(eps), ptr(Y),
+                               stream_of(XQW))
+    check(rc, "ttt_post_norm_fwd")
+    return Y
+
+
+def post_norm_backward(XQW, ln_w, ln_b, eps, dY, dOut=None):
+    """Gradient of post_norm_forward: returns d XQW (kernel layout, XQW's dtype), the
+    LayerNorm weight / bias gradients ([NH * F] fp32) and, when dOut (the gradient of the wo
+    output, [B * L, NH * F]) is given, its column sums (the wo bias gradient, fp32) else None."""
+    B, NH, L, F, XQW, ln_w, ln_b = _post_norm_args(XQW, ln_w, ln_b)
+    for name, t in (("dY", dY), ("dOut", dOut)):
+        if t is not None and tuple(t.shape) != (B * L, NH * F):
+            raise ValueError(f"{name} must be [{B * L}, {NH * F}], got {tuple(t.shape)}")
+    dY = _c(dY.to(XQW.dtype))
+    dOut = _c(dOut.to(XQW.dtype)) if dOut is not None else None
+    dX = torch.empty_like(XQW)
+    dln_w = torch.zeros(NH * F, device=XQW.device, dtype=torch.float32)
+    dln_b = torch.zeros(NH * F, device=XQW.device, dtype=torch.float32)
+    dbias = torch.zeros(NH * F, device=XQW.device, dtype=torch.float32) if dOut is not None else None
+    rc = lib.ttt_post_norm_bwd(B, NH, L, F, ptr(XQW), dtype_code(XQW), ptr(ln_w), ptr(ln_b), float(eps), ptr(dY),
+                               ptr(dX), ptr(dln_w), ptr(dln_b), ptr(dOut), ptr(dbias), stream_of(XQW))
+    check(rc, "ttt_post_norm_bwd")
+    return dX, dln_w, dln_b, dbias

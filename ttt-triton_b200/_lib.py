@@ -63,6 +63,8 @@ _SIGNATURES = {
     "ttt_memo_mix_bwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P] * 4 + [_P, _Z, _P], _I),
     "ttt_prologue_fwd": ([_I] * 5 + [_P, _I, _L] + [_P] * 4 + [ctypes.c_float] + [_P] * 6, _I),
     "ttt_prologue_bwd": ([_I] * 5 + [_P, _I, _L] + [_P] * 4 + [ctypes.c_float] + [_P] * 10, _I),
+    "ttt_post_norm_fwd": ([_I] * 4 + [_P, _I, _P, _P, ctypes.c_float, _P, _P], _I),
+    "ttt_post_norm_bwd": ([_I] * 4 + [_P, _I, _P, _P, ctypes.c_float] + [_P] * 7, _I),
     "ttt_mlp_cached_readout": (
         [_I] * 6 + [_P, _I] + [_P, _L, _L] * 4 + [_P, _P, _I, _P, _P],
         _I,

@@ -156,15 +156,16 @@ __global__ void __launch_bounds__(kWarps * 32, 3) prologue_fwd_kernel(Params p) 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int grp = lane / G, r = lane % G;
   const int h = blockIdx.y, W = p.NH * F, NC = p.L / p.CS, CS = p.CS;
-  const long long n_mb = (long long)p.B * NC;
+  const int n_mb = p.B * NC;
   const T* P = static_cast<const T*>(p.P);
   __shared__ float gate_sh[kWarps][kMaxCS];
 
-  const float* gam = p.ln_w + h * F + r * V;  // LayerNorm weight and bias, read where used (L1)
-  const float* bet = p.ln_b + h * F + r * V;
+  float gam[V], bet[V];  // this lane's LayerNorm weight and bias columns
+  VecIO<float, V>::load(p.ln_w + h * F + r * V, gam);
+  VecIO<float, V>::load(p.ln_b + h * F + r * V, bet);
 
-  for (long long m = (long long)blockIdx.x * kWarps + warp; m < n_mb; m += (long long)gridDim.x * kWarps) {
-    const int b = (int)(m / NC), n = (int)(m % NC);
+  for (int m = blockIdx.x * kWarps + warp; m < n_mb; m += gridDim.x * kWarps) {
+    const int b = m / NC, n = m - b * NC;
     for (int t0 = 0; t0 < CS; t0 += TPP) {
       const int t = t0 + grp;
       const bool on = t < CS;
@@ -207,7 +208,7 @@ __global__ void __launch_bounds__(kWarps * 32, 3) prologue_fwd_kernel(Params p) 
       }
       const float rs = 1.f / (sqrtf(group_sum<G>(nsq) * (1.f / (F - 1))) + kLnEps);
 #pragma unroll
-      for (int i = 0; i < V; ++i) v[i] = fmaf(__ldg(gam + i), v[i] * rs, __ldg(bet + i)) + k[i];
+      for (int i = 0; i < V; ++i) v[i] = fmaf(gam[i], v[i] * rs, bet[i]) + k[i];
 
       if (on) {
         const long long o = (((long long)b * p.NH + h) * p.L + l) * F + r * V;
@@ -248,7 +249,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) prologue_bwd_kernel(Params p) 
   const int grp = lane / G, r = lane % G;
   const int h = blockIdx.y, W = p.NH * F, NC = p.L / p.CS, CS = p.CS;
   const int ncols = 4 * W + p.NH;
-  const long long n_mb = (long long)p.B * NC;
+  const int n_mb = p.B * NC;
   const T* P = static_cast<const T*>(p.P);
   T* dP = static_cast<T*>(p.dP);
   __shared__ float de_sh[kWarps][kMaxCS];
@@ -277,10 +278,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2) prologue_bwd_kernel(Params p) 
       SIO::store(&bacc[warp][c][ch][lane][0], cur);
     }
   };
-  const float* gam = p.ln_w + h * F + r * V;  // LayerNorm weight, read where used (L1)
+  float gam[V];  // this lane's LayerNorm weight columns
+  VecIO<float, V>::load(p.ln_w + h * F + r * V, gam);
 
-  for (long long m = (long long)blockIdx.x * kWarps + warp; m < n_mb; m += (long long)gridDim.x * kWarps) {
-    const int b = (int)(m / NC), n = (int)(m % NC);
+  for (int m = blockIdx.x * kWarps + warp; m < n_mb; m += gridDim.x * kWarps) {
+    const int b = m / NC, n = m - b * NC;
     // Column sums of this mini-batch's d_eta block: eta column j is one gate in every row.
     if (p.deta) {
       const T* deta = static_cast<const T*>(p.deta) + (((long long)b * p.NH + h) * NC + n) * CS * CS;
@@ -346,7 +348,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) prologue_bwd_kernel(Params p) 
       for (int i = 0; i < V; ++i) {
         a_g[i] = fmaf(dv[i], v[i] * rs, a_g[i]);
         a_b[i] += dv[i];
-        const float dyh = __ldg(gam + i) * dv[i];
+        const float dyh = gam[i] * dv[i];
         dyh_sum += dyh;
         dyh_n = fmaf(dyh, v[i], dyh_n);
       }
@@ -356,7 +358,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) prologue_bwd_kernel(Params p) 
       const float cn = sigma > 0.f ? dyh_n * rs * rs / ((F - 1) * sigma) : 0.f;
 #pragma unroll
       for (int i = 0; i < V; ++i) {
-        const float dy = (__ldg(gam + i) * dv[i] - dyh_sum * (1.f / F)) * rs - v[i] * cn;
+        const float dy = (gam[i] * dv[i] - dyh_sum * (1.f / F)) * rs - v[i] * cn;
         dk[i] += dv[i] - dy;
         dv[i] = dy;  // d P_v
       }
@@ -445,11 +447,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2) prologue_bwd_kernel(Params p) 
 }
 
 // ------------------------------------------------------------------------------ host
-// CTAs along x per head: enough for `per_sm` resident CTAs on every SM in total, at most
+// CTAs along x per head: one wave of resident CTAs over all heads (occupancy API), at most
 // one mini-batch per warp.
-static int grid_x(long long n_mb, int NH, int per_sm) {
-  int dev = 0, sms = 148;
+template <typename K>
+static int grid_x(K kernel, long long n_mb, int NH) {
+  int dev = 0, sms = 148, per_sm = 1;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kWarps * 32, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
   long long want = ((long long)sms * per_sm + NH - 1) / NH;
   long long most = (n_mb + kWarps - 1) / kWarps;
   long long x = want < most ? want : most;
@@ -462,9 +467,9 @@ template <bool BWD, int F, typename T>
 static void launch_t(const Params& p, cudaStream_t st) {
   const long long n_mb = (long long)p.B * (p.L / p.CS);
   if (BWD)
-    prologue_bwd_kernel<F, T><<<dim3(grid_x(n_mb, p.NH, 2), p.NH), kWarps * 32, 0, st>>>(p);
+    prologue_bwd_kernel<F, T><<<dim3(grid_x(prologue_bwd_kernel<F, T>, n_mb, p.NH), p.NH), kWarps * 32, 0, st>>>(p);
   else
-    prologue_fwd_kernel<F, T><<<dim3(grid_x(n_mb, p.NH, 3), p.NH), kWarps * 32, 0, st>>>(p);
+    prologue_fwd_kernel<F, T><<<dim3(grid_x(prologue_fwd_kernel<F, T>, n_mb, p.NH), p.NH), kWarps * 32, 0, st>>>(p);
 }
 
 template <bool BWD, int F>
@@ -494,6 +499,8 @@ static int check_common(const char* who, int B, int L, int NH, int F, int CS, co
   TTT_REQUIRE(P && ln_w && ln_b && cosv && sinv, TTT_ERR_NULL, "%s: NULL pointer argument", who);
   TTT_REQUIRE(B >= 1 && L >= 1 && NH >= 1 && NH <= 65535, TTT_ERR_SHAPE, "%s: bad sizes B=%d L=%d NH=%d", who, B, L,
               NH);
+  TTT_REQUIRE((long long)B * L < (1LL << 31), TTT_ERR_SHAPE, "%s: B * L = %lld tokens is too many", who,
+              (long long)B * L);
   TTT_REQUIRE(F == 16 || F == 32 || F == 64 || F == 128, TTT_ERR_SHAPE,
               "%s: head_dim F=%d not supported (16, 32, 64 or 128)", who, F);
   TTT_REQUIRE(CS >= 1 && L % CS == 0, TTT_ERR_SHAPE, "%s: seq len %d is not a multiple of mini_batch_size %d", who, L,
@@ -505,6 +512,8 @@ static int check_common(const char* who, int B, int L, int NH, int F, int CS, co
               "%s: projection row stride %lld must be a multiple of 8 and at least 4 * NH * F + NH = %lld", who, ld,
               4 * W + NH);
   TTT_REQUIRE(aligned(P, 16), TTT_ERR_ALIGN, "%s: projection rows must be 16-byte aligned", who);
+  TTT_REQUIRE(aligned(ln_w, 16) && aligned(ln_b, 16), TTT_ERR_ALIGN,
+              "%s: LayerNorm parameters must be 16-byte aligned", who);
   return TTT_OK;
 }
 
