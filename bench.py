@@ -19,6 +19,11 @@ ttt-triton_b200/synthetic.py):
   config-4 forecaster shape (global batch 256, lookback 336, d_model 256, 4 heads).
 * ``epilogue_c4``: the layer's output epilogue (scan output -> post_norm -> wo,
   ttt_layer.py:349-350, 563-564), forward+backward, bf16, at the same shape.
+* ``forecaster_c4``: one training step of the config-4 forecaster (4 TTT-MLP layers,
+  d_model 256, 4 heads, mini-batch 16, F x F inner MLP, memo segments of 2 mini-batches;
+  lookback 336, horizon 96, 7 channels, global batch 256, MSE, AdamW, clipping), every TTT
+  stage on this library, bf16 activations. Strong scaling: the global batch is split over
+  the ranks and DistributedDataParallel averages the gradients with NCCL.
 
 A step is one pass of the hot path over one batch. Multi-GPU runs are weak scaling:
 every rank processes its own full batch (the (b, h) streams are independent, so there
@@ -54,6 +59,8 @@ WORKLOADS = {
                         memo=None),
     "epilogue_c4": dict(kind="epilogue", B=256, NH=4, L=336, F=64, FF=None, dtype="bf16", bwd=True, ckpt=None,
                         memo=None),
+    "forecaster_c4": dict(kind="forecaster", B=256, NH=4, L=336, F=64, FF=64, dtype="bf16", bwd=True, ckpt=16,
+                          memo=2, layers=4, horizon=96, channels=7),
 }
 MEMO = ("XQW", "XQ", "XK", "XU", "W1_memo", "b1_memo", "W2_memo", "b2_memo", "ln_w", "ln_b")
 PRO = ("hidden", "wq", "bq", "wk", "bk", "wv", "bv", "wu", "bu", "lr_w", "lr_b", "ln_w", "ln_b")
@@ -461,14 +468,174 @@ def cpu_reference(w, budget_s=12.0):
     return tokens / best, threads, sample
 
 
+def forecaster_cpu_reference(w, budget_s=12.0):
+    """The forecaster's training-step forward+backward restated on the host cores
+    (oracle/ttt_oracle.py forecaster_grads: the reference's ops/ scan and layer code), fp32,
+    on a bounded sample: a few windows of the full lookback through all layers."""
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import synthetic as S
+    import ttt_oracle as O
+    from forecaster import TTTForecaster
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    B = 2
+    model = TTTForecaster(w["channels"], w["channels"], w["horizon"], w["L"], model_dim=w["NH"] * w["F"],
+                          num_heads=w["NH"], num_layers=w["layers"], mini_batch_size=CS,
+                          scan_checkpoint_group_size=w["ckpt"], mem_cache_segment_n_mini_batches=w["memo"])
+    P = {k: v.detach() for k, v in model.named_parameters()}
+    series = S.make_forecast_series(seed=0)
+    x, y = S.forecast_windows(series, w["L"], w["horizon"], B, torch.Generator().manual_seed(0))
+    lay = model.layers[0]
+    prefixes = [f"layers.{i}." for i in range(w["layers"])]
+    best, reps = None, 0
+    t_end = time.perf_counter() + budget_s
+    while reps < 1 or (time.perf_counter() < t_end and reps < 5):
+        t0 = time.perf_counter()
+        O.forecaster_grads(P, x, y, prefixes, lay.rope_cos, lay.rope_sin, w["horizon"], CS, BASE_LR, w["ckpt"],
+                           w["memo"])
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+        reps += 1
+    tokens = B * w["NH"] * w["L"] * w["layers"]
+    return tokens / best, threads, f"{B} windows x {w['layers']} layers, full lookback {w['L']}, fp32, fwd+bwd, best of {reps}"
+
+
+def run_forecaster(args, w, rank, world, local_rank):
+    """Training steps of the config-4 forecaster (strong scaling: global batch split over
+    the ranks, DDP gradient all-reduce over NCCL)."""
+    import _lib
+    import synthetic as S
+    from forecaster import TTTForecaster, make_optimizer, train_step
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if w["B"] % world:
+        raise SystemExit(f"global batch {w['B']} does not split over {world} ranks")
+    b_rank = w["B"] // world
+    torch.manual_seed(0)  # identical initial parameters on every rank
+    model = TTTForecaster(w["channels"], w["channels"], w["horizon"], w["L"], model_dim=w["NH"] * w["F"],
+                          num_heads=w["NH"], num_layers=w["layers"], mini_batch_size=CS,
+                          scan_checkpoint_group_size=w["ckpt"], mem_cache_segment_n_mini_batches=w["memo"]).to(dev)
+    net = model
+    if world > 1:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local_rank])
+    opt = make_optimizer(model)
+    series = S.make_forecast_series(seed=0)
+    gen = torch.Generator().manual_seed(1000 + rank)
+    pool = [S.forecast_windows(series, w["L"], w["horizon"], b_rank, gen) for _ in range(4)]
+    dev_pool = [(x.to(dev), y.to(dev)) for x, y in pool]
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    for i in range(args.warmup):
+        train_step(net, opt, *dev_pool[i % 4])
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local_rank)
+    sampler.start()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    n0 = _lib.launch_count()
+    ev0.record(stream)
+    for i in range(args.steps):
+        train_step(net, opt, *dev_pool[i % 4])
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    launches = _lib.launch_count() - n0
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    # dominant kernel: the scan backward of one layer at the layer's per-rank shape
+    kern_ms, scan_flops = forecaster_scan_bwd_ms(w, b_rank, dev)
+    # end to end: each step's windows copied from pinned host memory, loss read back
+    host = [(x.pin_memory(), y.pin_memory()) for x, y in pool]
+    xb, yb = torch.empty_like(dev_pool[0][0]), torch.empty_like(dev_pool[0][1])
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        hx, hy = host[i % 4]
+        xb.copy_(hx, non_blocking=True)
+        yb.copy_(hy, non_blocking=True)
+        loss_host.copy_(train_step(net, opt, xb, yb), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], world, dev)
+    if rank != 0:
+        return
+    ms_step = ms / args.steps
+    tokens = w["B"] * w["NH"] * w["L"] * w["layers"]  # global, every layer's scan tokens
+    hbm, bf16, bf16_sus, src = peaks()
+    achieved = scan_flops / (kern_ms / 1e3) / 1e12
+    line = {
+        "metric": METRIC, "value": tokens / (ms_step / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
+        "config": {"workload": args.workload, "global_batch": w["B"], "batch_per_rank": b_rank, "layers": w["layers"],
+                   "d_model": w["NH"] * w["F"], "NH": w["NH"], "L": w["L"], "horizon": w["horizon"],
+                   "channels": w["channels"], "CS": CS, "inner": "F x F (64)", "memo_segment_size": w["memo"],
+                   "checkpoint_group_size": w["ckpt"], "parallelism": f"dp{world} (DDP, NCCL all-reduce)",
+                   "tokens": "B * NH * L per TTT layer, summed over layers",
+                   "samples_per_s": w["B"] / (ms_step / 1e3),
+                   "l2": "activations larger than L2 (no flush)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
+                     "frac": achieved / bf16, "traffic": None, "peak_source": src, "kernel": "mlp_bwd (one layer)",
+                     "kernel_ms": kern_ms, "kernel_flops": scan_flops},
+        "e2e": {"value": tokens / (e2e_ms / args.steps / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": (xb.numel() * xb.element_size() + yb.numel() * yb.element_size()),
+                "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms / args.steps},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = forecaster_cpu_reference(w)
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    print(json.dumps(line), flush=True)
+
+
+def forecaster_scan_bwd_ms(w, b_rank, dev):
+    """CUDA-event time of one layer's scan backward (the F x F inner MLP) at the per-rank
+    shape, and its useful FLOPs (the dual-form backward count of algorithmic())."""
+    import _core
+    import synthetic as S
+
+    NC = w["L"] // CS
+    d = S.make_mlp_inputs(b_rank, w["NH"], NC, CS, w["F"], w["FF"], dtype=torch.bfloat16, device=dev, seed=5,
+                          eta_mode="equal")
+    dO = S.make_upstream((b_rank, w["NH"], NC, CS, w["F"]), device=dev, seed=6, dtype=torch.bfloat16)
+    _, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"])
+    stream = torch.cuda.current_stream(dev)
+    tot = 0.0
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
+                           saved=zs, W1_last=last[0], W2_last=last[2])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+    F, FF = w["F"], w["FF"]
+    flops = (38 * F * FF + 12 * CS * FF + 12 * CS * F) * b_rank * w["NH"] * w["L"]
+    return tot / 3, flops
+
+
 def run_reference(args, w, rank, world):
     if rank != 0:
         return
-    value, cores, sample = cpu_reference(w)
+    value, cores, sample = forecaster_cpu_reference(w) if w["kind"] == "forecaster" else cpu_reference(w)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "strong" if w["kind"] == "forecaster" else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
         "config": {"workload": args.workload, **{k: v for k, v in w.items() if k in ("B", "NH", "L", "F", "FF")}},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -676,7 +843,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, w, rank, world, local_rank)
+        if w["kind"] == "forecaster":
+            run_forecaster(args, w, rank, world, local_rank)
+        else:
+            run_ours(args, w, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -343,6 +343,57 @@ def post_norm_wo_grads(inp, dout, eps=1e-6):
     return {k: leaves[k].grad for k in EPILOGUE_PARAM_NAMES}, out.detach()
 
 
+def ttt_mlp_layer(P, pre, h, rope_cos, rope_sin, mini_batch_size, base_lr, checkpoint_group_size,
+                  memo_segment_size):
+    """One TTT-MLP layer's forward (TTTBase.forward, ttt_layer.py:337-357, with TTTMLP.ttt's
+    kernel branch, :453-565): process_input, the scan, memo mixing and post_norm + wo.
+    P holds the layer's parameters under the prefix `pre` (reference module names)."""
+    def q(n):
+        return P[pre + n]
+
+    inp = process_input(h, q("wq.weight"), q("wq.bias"), q("wk.weight"), q("wk.bias"), q("wv.weight"),
+                        q("wv.bias"), q("wu.weight"), q("wu.bias"), q("learnable_ttt_lr_weight"),
+                        q("learnable_ttt_lr_bias"), q("ttt_norm_weight"), q("ttt_norm_bias"), rope_cos, rope_sin,
+                        mini_batch_size, base_lr)
+    B = h.shape[0]
+    NC = inp["XV"].shape[2]
+    ckpt = min(max(int(checkpoint_group_size), 1), NC)
+
+    def tile(t):
+        return t.unsqueeze(0).expand(B, *t.shape)
+
+    r = mlp_scan(q("ttt_norm_weight"), q("ttt_norm_bias"), tile(q("W1")), tile(q("b1")), tile(q("W2")), tile(q("b2")),
+                 inp["XQ"], inp["XV"], inp["XK"], inp["eta"], ckpt, memo_segment_size)
+    XQW = memo_mix(r["XQW"], inp["XQ"], inp["XK"], inp["XU"], r["W1_memo"].detach(), r["b1_memo"].detach(),
+                   r["W2_memo"].detach(), r["b2_memo"].detach(), q("ttt_norm_weight"), q("ttt_norm_bias"),
+                   memo_segment_size)
+    return post_norm_wo(XQW, q("post_norm.weight"), q("post_norm.bias"), q("wo.weight"), q("wo.bias"))
+
+
+def forecaster(P, x, layer_prefixes, rope_cos, rope_sin, pred_len, mini_batch_size, base_lr, checkpoint_group_size,
+               memo_segment_size):
+    """TTTForecaster.forward (forecast.py:94-99) with the TTT layers stacked: in_proj, each
+    layer of `layer_prefixes` in turn, head on the last position."""
+    h = x @ P["in_proj.weight"].T + P["in_proj.bias"]
+    for pre in layer_prefixes:
+        h = ttt_mlp_layer(P, pre, h, rope_cos, rope_sin, mini_batch_size, base_lr, checkpoint_group_size,
+                          memo_segment_size)
+    out = h[:, -1] @ P["head.weight"].T + P["head.bias"]
+    return out.view(x.shape[0], pred_len, -1)
+
+
+def forecaster_grads(P, x, y, layer_prefixes, rope_cos, rope_sin, pred_len, mini_batch_size, base_lr,
+                     checkpoint_group_size, memo_segment_size):
+    """MSE loss (main.py:89) of the forecaster and its gradients w.r.t. every parameter."""
+    leaves = {k: v.detach().clone().requires_grad_(True) for k, v in P.items()}
+    out = forecaster(leaves, x, layer_prefixes, rope_cos, rope_sin, pred_len, mini_batch_size, base_lr,
+                     checkpoint_group_size, memo_segment_size)
+    loss = Fn.mse_loss(out, y)
+    loss.backward()
+    grads = {k: (v.grad if v.grad is not None else torch.zeros_like(v)) for k, v in leaves.items()}
+    return grads, out.detach(), loss.detach()
+
+
 MEMO_MIX_GRAD_NAMES = ("XQW", "XU", "XK")
 
 

@@ -12,7 +12,8 @@ with torch autograd exactly as the reference's training path does. The cached-re
 golden runs the reference's Triton kernel (kernels/mlp_cached_readout.py:7-109) under
 the Triton CPU interpreter at B = NH = 1, the only slice its offsets address correctly; the
 memo-mixing golden runs the reference's own mixing loop of TTTMLP.ttt with that kernel, the
-prologue golden the layer's own process_input and the epilogue golden its forward tail.
+prologue golden the layer's own process_input, the epilogue golden its forward tail and the
+forecaster golden the reference's TTTForecaster with its scan launch on the ops path.
 
 Outputs ``tests/golden/*.npz`` (float32 storage). The GPU box never runs this script.
 """
@@ -265,6 +266,56 @@ def epilogue_case(ref_root, B, L, W, NH, CS, seed):
     return {k: _np(v) for k, v in res.items()}
 
 
+def forecaster_case(ref_root, B, L, W, NH, CS, pred_len, d_in, seed):
+    """The reference's own TTTForecaster (forecast.py:79-99, one TTT-MLP layer, use_kernel
+    path) in float64 with MSE loss, gradients of every parameter. Its TritonMLP launch is
+    replaced by the reference's ops.ttt_mlp, returned in the kernel layout [B, NH, NC, CS, F]
+    the Triton kernel writes (ops returns [B, NC, CS, NH, F]); one memo segment covers the
+    sequence, so the mixing loop passes the scan output through (no cached read-outs)."""
+    sys.path.insert(0, ref_root)
+    import forecast
+    import ops as ref_ops
+    import ttt_layer
+
+    class ScanStub:
+        @staticmethod
+        def apply(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, ckpt, memo):
+            out = ref_ops.ttt_mlp(XK, XQ, XV, eta, ln_w, ln_b, W1, b1, W2, b2, ckpt)
+            return out.permute(0, 3, 1, 2, 4), None, None, None, None
+
+    torch.manual_seed(seed)
+    NC = L // CS
+    cfg = forecast.ModelConfig(seq_len=L, model_dim=W, num_heads=NH, mini_batch_size=CS, ssm_layer="ttt_mlp",
+                               use_kernel=True, ttt_base_lr=0.1, scan_checkpoint_group_size=2,
+                               mem_cache_segment_n_mini_batches=NC)
+    saved = ttt_layer.TritonMLP
+    ttt_layer.TritonMLP = ScanStub
+    try:
+        model = forecast.TTTForecaster(cfg, d_in=d_in, d_out=d_in, pred_len=pred_len).double()
+        with torch.no_grad():  # non-trivial gate, LayerNorm and inner-bias parameters
+            layer = model.ttt.ttt
+            layer.learnable_ttt_lr_bias.normal_(0, 0.5)
+            for t in (layer.ttt_norm_weight, layer.post_norm.weight):
+                t.add_(0.1 * torch.randn_like(t))
+            for t in (layer.ttt_norm_bias, layer.post_norm.bias, layer.b1, layer.b2):
+                t.normal_(0, 0.05)
+        x = torch.randn(B, L, d_in, dtype=torch.float64)
+        y = torch.randn(B, pred_len, d_in, dtype=torch.float64)
+        out = model(x)
+        loss = torch.nn.functional.mse_loss(out, y)
+        loss.backward()
+    finally:
+        ttt_layer.TritonMLP = saved
+    res = {"in_x": x, "in_y": y, "out": out.detach(), "loss": loss.detach(), "CS": torch.tensor(CS),
+           "pred_len": torch.tensor(pred_len), "NH": torch.tensor(NH), "ckpt": torch.tensor(2),
+           "memo": torch.tensor(NC), "base_lr": torch.tensor(0.1)}
+    for k, v in model.state_dict().items():
+        res["p_" + k] = v
+    for k, v in model.named_parameters():  # wu gets no gradient with one memo segment: zeros
+        res["g_" + k] = v.grad if v.grad is not None else torch.zeros_like(v)
+    return {k: _np(v) for k, v in res.items()}
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     sys.path.insert(0, ref_root)
@@ -281,6 +332,7 @@ def main():
         "memo_mix": memo_mix_case(ref_root, NC=7, F=32, FF=128, M=2, seed=40),
         "prologue": prologue_case(ref_root, B=2, L=64, W=128, NH=2, CS=16, seed=50),
         "epilogue": epilogue_case(ref_root, B=2, L=32, W=128, NH=4, CS=16, seed=60),
+        "forecaster": forecaster_case(ref_root, B=2, L=64, W=128, NH=2, CS=16, pred_len=8, d_in=7, seed=70),
     }
     for name, res in cases.items():
         path = os.path.join(HERE, name + ".npz")

@@ -90,6 +90,36 @@ def test_epilogue_oracle_matches_reference_forward_tail():
         assert O.rel_l2(grads[k], g["grad_" + k].double()) < 1e-6, k
 
 
+def test_forecaster_oracle_matches_reference_model():
+    """The forecaster composition (in_proj, process_input, scan, memo mixing, post_norm + wo,
+    head) against the reference's own TTTForecaster: output, loss and every gradient."""
+    import ttt_oracle as Or
+    from forecaster import rope_table_3d
+
+    inp, g = load_golden("forecaster")
+    P = {k[2:]: v.double() for k, v in g.items() if k.startswith("p_")}
+    L = inp["x"].shape[1]
+    F = P["ttt.ttt.W1"].shape[-1]
+    cos, sin = rope_table_3d(F, 1, 1, L)
+    grads, out, loss = Or.forecaster_grads(P, inp["x"].double(), inp["y"].double(), ["ttt.ttt."], cos.double(),
+                                           sin.double(), int(g["pred_len"]), int(g["CS"]), float(g["base_lr"]),
+                                           int(g["ckpt"]), int(g["memo"]))
+    assert O.rel_l2(out, g["out"].double()) < 1e-6
+    assert abs(float(loss) - float(g["loss"])) < 1e-6 * abs(float(g["loss"]))
+    for k, v in grads.items():
+        assert O.rel_l2(v, g["g_" + k].double()) < 1e-6, k
+
+
+def test_rope_table_matches_reference_precompute():
+    """rope_table_3d restates utils.precompute_freqs_cis_3d: the golden prologue was made with
+    the reference's own table at head_dim 64, 1 x 1 latent, 64 frames."""
+    from forecaster import rope_table_3d
+
+    inp, _ = load_golden("prologue")
+    cos, sin = rope_table_3d(64, 1, 1, 64)
+    assert torch.allclose(cos, inp["freqs_cos"], atol=1e-6) and torch.allclose(sin, inp["freqs_sin"], atol=1e-6)
+
+
 @pytest.mark.parametrize("eta_mode", ["causal", "equal"])
 @pytest.mark.parametrize("ckpt", [1, 3, 16])
 def test_linear_hand_backward_matches_autograd(eta_mode, ckpt):

@@ -94,10 +94,22 @@ def exported_symbols():
     return list(_SIGNATURES)
 
 
+# Kernels one successful call enqueues (1 unless listed); ttt_device_status launches none.
+_KERNELS_PER_CALL = {"ttt_memo_mix_fwd": 2, "ttt_memo_mix_bwd": 3, "ttt_device_status": 0}
+_launches = 0
+
+
+def launch_count():
+    """Kernels this process has enqueued through the library (for benchmarks)."""
+    return _launches
+
+
 def check(rc, name):
+    global _launches
     if rc != 0:
         msg = lib.ttt_last_error().decode(errors="replace")
         raise RuntimeError(f"{name} failed (status {rc}): {msg}")
+    _launches += _KERNELS_PER_CALL.get(name, 1)
 
 
 def device_status():

@@ -128,6 +128,38 @@ def make_prologue_inputs(B, L, W, NH, device="cpu", seed=0):
     return d
 
 
+def make_forecast_series(n_steps=17420, channels=7, seed=0):
+    """The config-4 stand-in for an hourly multichannel series (ETTh1's length): channel k is
+    a_k sin(2 pi t / 24 + phi_k) + b_k sin(2 pi t / 168 + psi_k) + 0.001 c_k t + AR(1) noise
+    (rho 0.9, innovation sigma 0.3), a, b ~ U(0.5, 2), c ~ U(-1, 1), phases ~ U(0, 2 pi),
+    z-normalised per channel. Returns fp32 [n_steps, channels] on the CPU."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    t = np.arange(n_steps, dtype=np.float64)[:, None]
+    a, b = rng.uniform(0.5, 2.0, channels), rng.uniform(0.5, 2.0, channels)
+    c = rng.uniform(-1.0, 1.0, channels)
+    phi, psi = rng.uniform(0, 2 * np.pi, channels), rng.uniform(0, 2 * np.pi, channels)
+    z = rng.standard_normal((n_steps, channels)) * 0.3
+    noise = np.empty_like(z)
+    noise[0] = z[0]
+    for i in range(1, n_steps):
+        noise[i] = 0.9 * noise[i - 1] + z[i]
+    x = a * np.sin(2 * np.pi * t / 24 + phi) + b * np.sin(2 * np.pi * t / 168 + psi) + 0.001 * c * t + noise
+    x = (x - x.mean(0)) / x.std(0)
+    return torch.from_numpy(x.astype(np.float32))
+
+
+def forecast_windows(series, lookback, horizon, batch, gen):
+    """`batch` random windows of a [T, C] series: inputs [batch, lookback, C] and targets the
+    following `horizon` steps [batch, horizon, C] (a torch.Generator picks the starts)."""
+    T = series.shape[0]
+    starts = torch.randint(0, T - lookback - horizon + 1, (batch,), generator=gen)
+    idx = starts[:, None] + torch.arange(lookback + horizon)[None, :]
+    w = series[idx]
+    return w[:, :lookback].contiguous(), w[:, lookback:].contiguous()
+
+
 def make_upstream(shape, device="cpu", seed=1, dtype=torch.float32):
     """dZ ~ N(0, 1) with the output's shape."""
     g = torch.Generator(device=device).manual_seed(seed)
