@@ -13,8 +13,8 @@ DEV = "cuda"
 SCAN = ("ln_w", "ln_b", "W1", "b1", "W2", "b2", "XQ", "XV", "XK", "eta")
 
 
-def make(B, NH, NC, M, dtype, seed):
-    d = S.perturb_params(S.make_mlp_inputs(B, NH, NC, 16, 64, 256, seed=seed), seed=seed + 1)
+def make(B, NH, NC, M, dtype, seed, FF=256):
+    d = S.perturb_params(S.make_mlp_inputs(B, NH, NC, 16, 64, FF, seed=seed), seed=seed + 1)
     d = {k: (v.to(dtype) if k in ("XQ", "XV", "XK", "eta") else v) for k, v in d.items()}
     od = oracle_inputs(d)
     r = O.mlp_scan(*(od[k] for k in SCAN), 1, M)
@@ -29,15 +29,19 @@ def make(B, NH, NC, M, dtype, seed):
 ORDER = ("XQW", "XQ", "XK", "XU", "W1_memo", "b1_memo", "W2_memo", "b2_memo", "ln_w", "ln_b")
 
 
+@pytest.mark.parametrize("FF", [256, 64])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("shape", [(1, 2, 7, 2), (1, 1, 40, 16), (2, 1, 9, 3)])
-def test_memo_mix_matches_oracle(dtype, shape):
-    """Forward and gradients (XQW, XU, XK), including segments of 256 tokens (two 128-token
-    tiles) and a ragged last segment."""
+@pytest.mark.parametrize("shape", [(1, 2, 7, 2), (1, 1, 40, 16), (2, 1, 9, 3), (2, 2, 21, 2)])
+def test_memo_mix_matches_oracle(dtype, shape, FF):
+    """Forward and gradients (XQW, XU, XK) of the fused kernels for the 256-wide and the F x F
+    inner MLP, including segments of 256 tokens (two 128-token tiles), a ragged last segment
+    and the config-4 layer's 11 segments of 2 mini-batches."""
     B, NH, NC, M = shape
-    inp = make(B, NH, NC, M, dtype, seed=NC + M)
+    inp = make(B, NH, NC, M, dtype, seed=NC + M, FF=FF)
     dO = S.make_upstream((B, NH, NC, 16, 64), seed=3).to(dtype)
-    from kernels.mlp_memo_mix import mlp_memo_mix
+    from kernels.mlp_memo_mix import fused_envelope, mlp_memo_mix
+
+    assert fused_envelope(inp["XQW"], inp["W1_memo"], M)
 
     leaves = {k: (v.to(DEV).requires_grad_(k in ("XQW", "XU", "XK")) if v.is_floating_point() else v.to(DEV))
               for k, v in inp.items()}

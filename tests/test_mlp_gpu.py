@@ -32,7 +32,8 @@ def run_autograd(d, ckpt, memo, dO):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("shape", [(2, 2, 5, 16, 16, 64, 2, 2), (1, 2, 4, 16, 64, 256, 16, 3),
-                                   (2, 1, 6, 16, 32, 32, 4, 1), (1, 1, 3, 8, 32, 128, 1, 2)])
+                                   (2, 1, 6, 16, 32, 32, 4, 1), (1, 1, 3, 8, 32, 128, 1, 2),
+                                   (2, 3, 5, 16, 64, 64, 2, 2)])
 def test_mlp_fwd_bwd_matches_oracle(dtype, shape):
     B, NH, NC, CS, F, FF, ckpt, memo = shape
     d, dO = make(B, NH, NC, CS, F, FF, dtype, seed=NC + F)
@@ -113,12 +114,14 @@ def test_long_sequence_config3_streams_fwd_bwd():
         assert_close("d" + k, grads[k], ref_grads[k], 2e-2)
 
 
+@pytest.mark.parametrize("FF", [256, 64])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("eta_mode", ["causal", "equal"])
-def test_backward_paths_agree(dtype, eta_mode):
-    """The single reverse walk over the stored pre-activations (tensor-core path) and the
-    checkpoint-group recompute (general path) both match the oracle on the same inputs."""
-    B, NH, NC, CS, F, FF, ckpt = 2, 2, 7, 16, 64, 256, 3
+def test_backward_paths_agree(dtype, eta_mode, FF):
+    """The single reverse walk over the stored pre-activations (tensor-core path, 8 warps for
+    the 256-wide inner MLP, 2 for the F x F one) and the checkpoint-group recompute (general
+    path) both match the oracle on the same inputs."""
+    B, NH, NC, CS, F, ckpt = 2, 2, 7, 16, 64, 3
     d, dO = make(B, NH, NC, CS, F, FF, dtype, seed=31, eta_mode=eta_mode)
     ref_grads, _ = O.mlp_grads(oracle_inputs(d), dO.double().cpu())
     _, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in NAMES), ckpt, None)
@@ -133,9 +136,10 @@ def test_backward_paths_agree(dtype, eta_mode):
             assert_close("d" + k, got[k], ref_grads[k].reshape(got[k].shape), 2e-2)
 
 
-def test_saved_preactivations_match_oracle():
+@pytest.mark.parametrize("FF", [256, 64])
+def test_saved_preactivations_match_oracle(FF):
     """The forward's stored Z1, Z2, Z1bar, Z2bar equal the oracle's per-mini-batch values."""
-    B, NH, NC, CS, F, FF = 1, 2, 5, 16, 64, 256
+    B, NH, NC, CS, F = 1, 2, 5, 16, 64
     d, _ = make(B, NH, NC, CS, F, FF, torch.bfloat16, seed=41)
     _, _, _, _, zs = _core.mlp_forward(*(d[k] for k in NAMES), 2, None)
     od = oracle_inputs(d)
@@ -163,11 +167,13 @@ def test_saved_preactivations_match_oracle():
         assert_close(name, zs[i], torch.stack(ref[i], 2), 2e-2)
 
 
-@pytest.mark.parametrize("B,NH", [(1, 2), (2, 150), (4, 64)])
-def test_forward_sampled_streams_few_and_many(B, NH):
-    """Grids below and above the number of SMs (one and several waves): final states,
-    checkpoints, memo states and outputs of sampled streams match the oracle."""
-    NC, CS, F, FF = 3, 16, 64, 256
+@pytest.mark.parametrize("FF", [256, 64])
+@pytest.mark.parametrize("B,NH", [(1, 2), (2, 150), (4, 64), (8, 160)])
+def test_forward_sampled_streams_few_and_many(B, NH, FF):
+    """Grids below and above the number of SMs (one and several waves; with FF = 64 several
+    2-warp CTAs share an SM's tensor memory): final states, checkpoints, memo states and
+    outputs of sampled streams match the oracle."""
+    NC, CS, F = 3, 16, 64
     d, _ = make(B, NH, NC, CS, F, FF, torch.bfloat16, seed=B + NH)
     out, last, ck, memo, zs = _core.mlp_forward(*(d[k] for k in NAMES), 2, 1)
     od = oracle_inputs(d)

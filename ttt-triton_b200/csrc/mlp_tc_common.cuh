@@ -1,4 +1,5 @@
-// Pieces shared by the tensor-core TTT-MLP kernels (F = 64, FF = 256, CS = 16): the
+// Pieces shared by the tensor-core TTT-MLP kernels (F = 64, CS = 16, inner width FF = 256
+// or the F x F layer's 64): the
 // accumulator-fragment layout of a warp's state slices and their TMEM / global copies.
 //
 // A warp owns 16 M consecutive hidden units (M = 2: 32 units, M = 1: 16). Its slice of W1
@@ -16,26 +17,27 @@ namespace mlp_tc {
 
 constexpr int F = 64, FF = 256, C = 16;
 
-// State slices <-> global [F][FF] (W1) and [FF][F] (W2) layouts. A warp owning 16 * M
-// hidden units from fb holds W1^T as M x 8 accumulator tiles and W2^T as 4 x 2M tiles.
-template <int M = 2>
+// State slices <-> global [F][FFS] (W1) and [FFS][F] (W2) layouts (FFS: the inner width,
+// 256 by default, 64 for the F x F inner MLP). A warp owning 16 * M hidden units from fb
+// holds W1^T as M x 8 accumulator tiles and W2^T as 4 x 2M tiles.
+template <int M = 2, int FFS = FF>
 __device__ __forceinline__ void w1_io(float (*S1)[8][4], float* W1, int fb, int g, int t, bool store) {
 #pragma unroll
   for (int m = 0; m < M; ++m)
 #pragma unroll
     for (int nf = 0; nf < 8; ++nf) {
       const int f = 8 * nf + 2 * t, ff = fb + 16 * m + g;
-      float* p0 = W1 + f * FF + ff;
+      float* p0 = W1 + f * FFS + ff;
       if (store) {
         p0[0] = S1[m][nf][0];
-        p0[FF] = S1[m][nf][1];
+        p0[FFS] = S1[m][nf][1];
         p0[8] = S1[m][nf][2];
-        p0[FF + 8] = S1[m][nf][3];
+        p0[FFS + 8] = S1[m][nf][3];
       } else {
         S1[m][nf][0] = p0[0];
-        S1[m][nf][1] = p0[FF];
+        S1[m][nf][1] = p0[FFS];
         S1[m][nf][2] = p0[8];
-        S1[m][nf][3] = p0[FF + 8];
+        S1[m][nf][3] = p0[FFS + 8];
       }
     }
 }

@@ -12,11 +12,12 @@
 //   memo_prep   one CTA per (stream, memo state j): 16-bit K-major copies of W1_j^T [FF][F]
 //               and W2_j^T [F][FF] (the tensor-core B operands) and summary_j.
 //   memo_mix    one CTA (8 warps) per (stream, segment, 128-token tile), heavy segments
-//               first. Per earlier state j:
-//                 Z1 = XQ W1_j      128 x 256 x 64 tcgen05.mma into tensor memory
-//                 X2 = gelu(Z1+b1)  all warps (more columns to warps 4-7): 32-column TMEM
-//                                   loads, 16-bit K-major swizzled tiles in shared memory
-//                 Z2 = X2 W2_j      128 x 64 x 256 tcgen05.mma
+//               first. Per earlier state j (inner width FF = 256, or 64 for the layer's
+//               F x F inner MLP):
+//                 Z1 = XQ W1_j      128 x FF x 64 tcgen05.mma into tensor memory
+//                 X2 = gelu(Z1+b1)  all warps (more columns to warps 4-7 when FF = 256):
+//                                   32-column TMEM loads, 16-bit K-major swizzled tiles
+//                 Z2 = X2 W2_j      128 x 64 x FF tcgen05.mma
 //                 R_j              warps 0-3, one token per thread: LayerNorm in registers
 //               forward: accumulate g_j R_j; backward: dg_j = <dOut_t, R_j(t)>.
 //               W1_j / W2_j arrive by TMA (128-byte swizzle) as soon as the previous
@@ -40,34 +41,48 @@
 namespace ttt {
 namespace memo {
 
-constexpr int F = 64, FF = 256, C = 16, ROWS = 128, NW = 8, NTHREADS = 32 * NW, NS_MAX = 64;
+constexpr int F = 64, FF_MAX = 256, C = 16, ROWS = 128, NW = 8, NTHREADS = 32 * NW, NS_MAX = 64;
 constexpr float kReadoutEps = 1e-6f;  // kernels/mlp_cached_readout.py:99
-// shared memory (1024-byte aligned base)
-constexpr int OFF_XQ = 0;                          // [128][64] 16-bit, K-major 128-byte swizzle
-constexpr int OFF_W1 = OFF_XQ + ROWS * F * 2;      // [256][64]: W1_j^T
-constexpr int OFF_W2 = OFF_W1 + FF * F * 2;        // 4 x [64][64]: W2_j^T, K chunks of 64
-constexpr int OFF_X2 = OFF_W2 + F * FF * 2;        // 4 x [128][64]: gelu(Z1 + b1), K chunks of 64
-constexpr int GLD = NS_MAX + 1;                    // row stride of the per-token tables (conflict-free)
-constexpr int OFF_G = OFF_X2 + ROWS * FF * 2;      // fp32 [128][GLD]: mixing weights g_j(t)
-constexpr int OFF_DG = OFF_G + ROWS * GLD * 4;     // fp32 [128][GLD]: dg_j(t) (backward)
-constexpr int OFF_LN = OFF_DG + ROWS * GLD * 4;    // fp32 [2][64]: LayerNorm weight, bias
-constexpr int OFF_B1 = OFF_LN + 2 * F * 4;         // fp32 [3][256]: b1_j ring (state j in slot j % 3)
-constexpr int OFF_B2 = OFF_B1 + 3 * FF * 4;        // fp32 [3][64]: b2_j ring
-constexpr int SMEM = OFF_B2 + 3 * F * 4 + 1024;    // + slack to align the base
-constexpr uint32_t TMEM_COLS = 512;                // Z1: columns 0-255, Z2: 256-319
-constexpr uint32_t XQ_BYTES = ROWS * F * 2, W1_BYTES = FF * F * 2, W2_BYTES = F * FF * 2;
-static_assert(OFF_W1 % 1024 == 0 && OFF_W2 % 1024 == 0 && OFF_X2 % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+constexpr int OFF_XQ = 0;             // [128][64] 16-bit, K-major 128-byte swizzle
+constexpr int GLD = NS_MAX + 1;       // row stride of the per-token tables (conflict-free)
+constexpr uint32_t XQ_BYTES = ROWS * F * 2;
+
+// Shared memory (1024-byte aligned base) and tensor memory of a CTA for inner width FF.
+template <int FF>
+struct Mix {
+  static constexpr int OFF_W1 = OFF_XQ + ROWS * F * 2;   // [FF][64]: W1_j^T
+  static constexpr int OFF_W2 = OFF_W1 + FF * F * 2;     // FF/64 x [64][64]: W2_j^T, K chunks of 64
+  // FF/64 x [128][64]: gelu(Z1 + b1), K chunks of 64; the backward's d-summary scratch
+  // ([128][64] fp32) reuses it, so it is at least 32 KB
+  static constexpr int X2_BYTES = ROWS * FF * 2 > ROWS * F * 4 ? ROWS * FF * 2 : ROWS * F * 4;
+  static constexpr int OFF_X2 = OFF_W2 + F * FF * 2;
+  static constexpr int OFF_G = OFF_X2 + X2_BYTES;        // fp32 [128][GLD]: mixing weights g_j(t)
+  static constexpr int OFF_DG = OFF_G + ROWS * GLD * 4;  // fp32 [128][GLD]: dg_j(t) (backward)
+  static constexpr int OFF_LN = OFF_DG + ROWS * GLD * 4; // fp32 [2][64]: LayerNorm weight, bias
+  static constexpr int OFF_B1 = OFF_LN + 2 * F * 4;      // fp32 [3][FF]: b1_j ring (state j in slot j % 3)
+  static constexpr int OFF_B2 = OFF_B1 + 3 * FF * 4;     // fp32 [3][64]: b2_j ring
+  static constexpr int SMEM = OFF_B2 + 3 * F * 4 + 1024; // + slack to align the base
+  static constexpr int Z2_COL = FF == 256 ? 256 : FF;    // Z1: columns [0, FF), Z2: [Z2_COL, +64)
+  static constexpr uint32_t TMEM_COLS = FF == 256 ? 512 : 128;
+  static constexpr uint32_t W1_BYTES = FF * F * 2, W2_BYTES = F * FF * 2;
+  // GELU epilogue: 32-column chunks [0, SPLIT) on warps 0-3 (which also run the read-out
+  // LayerNorm), [SPLIT, FF / 32) on warps 4-7
+  static constexpr int CHUNKS = FF / 32, SPLIT = FF == 256 ? 3 : 1;
+  static_assert(OFF_W1 % 1024 == 0 && OFF_W2 % 1024 == 0 && OFF_X2 % 1024 == 0,
+                "swizzled tiles need 1024-byte alignment");
+  static_assert(Z2_COL + F <= (int)TMEM_COLS, "tensor memory budget");
+};
 
 struct Maps {
   CUtensorMap xq;  // XQ rows, 128-row boxes
-  CUtensorMap w1;  // W1^T copies [B*NH*NS*256][64], 256-row boxes
-  CUtensorMap w2;  // W2^T copies [B*NH*NS*64][256], 64 x 64 boxes
+  CUtensorMap w1;  // W1^T copies [B*NH*NS*FF][64], FF-row boxes
+  CUtensorMap w2;  // W2^T copies [B*NH*NS*64][FF], 64 x 64 boxes
 };
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------------- prep
-template <typename T>
+template <typename T, int FF>
 __global__ void __launch_bounds__(256) memo_prep_kernel(MemoMixParams p) {
   using H = Half2<T>;
   const long long sj = blockIdx.x;  // (stream, memo state)
@@ -122,9 +137,13 @@ __device__ __forceinline__ void decode_block(const MemoMixParams& p, long long& 
   tile = (int)(r % p.TILES);
 }
 
-template <typename T, bool BWD>
+template <typename T, bool BWD, int FF>
 __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, const __grid_constant__ Maps maps) {
   using H = Half2<T>;
+  using L = Mix<FF>;
+  constexpr int OFF_W1 = L::OFF_W1, OFF_W2 = L::OFF_W2, OFF_X2 = L::OFF_X2, OFF_G = L::OFF_G, OFF_DG = L::OFF_DG;
+  constexpr int OFF_LN = L::OFF_LN, OFF_B1 = L::OFF_B1, OFF_B2 = L::OFF_B2;
+  constexpr uint32_t TMEM_COLS = L::TMEM_COLS, W1_BYTES = L::W1_BYTES, W2_BYTES = L::W2_BYTES;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   __shared__ uint32_t tmem_base_sh;
@@ -178,7 +197,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   tmem_fence_before();
   __syncthreads();
   tmem_fence_after();
-  const uint32_t tZ1 = tmem_base_sh, tZ2 = tmem_base_sh + 256;
+  const uint32_t tZ1 = tmem_base_sh, tZ2 = tmem_base_sh + L::Z2_COL;
 
   auto load_w1 = [&](int j) {
     mbar_expect_tx(b_w1, W1_BYTES);
@@ -187,14 +206,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   auto load_w2 = [&](int j) {
     mbar_expect_tx(b_w2, W2_BYTES);
 #pragma unroll
-    for (int a = 0; a < 4; ++a) tma_load_2d(sW2 + a * (F * 64 * 2), &maps.w2, 64 * a, (int)((s * p.NS + j) * F), b_w2);
+    for (int a = 0; a < FF / 64; ++a)
+      tma_load_2d(sW2 + a * (F * 64 * 2), &maps.w2, 64 * a, (int)((s * p.NS + j) * F), b_w2);
   };
   // Biases of state j into ring slot j % 3 (plain loads; the next CTA barrier publishes them).
   // A slot is rewritten two states after its last reader, which is past a barrier by then.
   auto load_bias = [&](int j) {
     float* b1s = reinterpret_cast<float*>(smem + OFF_B1) + (j % 3) * FF;
     float* b2s = reinterpret_cast<float*>(smem + OFF_B2) + (j % 3) * F;
-    b1s[tid] = __ldg(p.b1_memo + (s * p.NS + j) * FF + tid);
+    for (int i = tid; i < FF; i += NTHREADS) b1s[i] = __ldg(p.b1_memo + (s * p.NS + j) * FF + i);
     if (tid < F) b2s[tid] = __ldg(p.b2_memo + (s * p.NS + j) * F + tid);
   };
   auto product1 = [&]() {  // Z1 = XQ W1_j  (K = 64)
@@ -204,10 +224,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     for (int k = 0; k < F / 16; ++k) umma_ss(tZ1, da + 2 * k, db + 2 * k, idesc1, k > 0);
     umma_commit(b_p1);
   };
-  auto product2 = [&]() {  // Z2 = X2 W2_j  (K = 256 in four 64-wide chunks)
+  auto product2 = [&]() {  // Z2 = X2 W2_j  (K = FF in 64-wide chunks)
     tmem_fence_after();
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
+    for (int a = 0; a < FF / 64; ++a) {
       const uint64_t da = umma_desc_k_sw128(sX2 + a * (ROWS * 64 * 2)), db = umma_desc_k_sw128(sW2 + a * (F * 64 * 2));
 #pragma unroll
       for (int k = 0; k < 4; ++k) umma_ss(tZ2, da + 2 * k, db + 2 * k, idesc2, (a | k) != 0);
@@ -295,10 +315,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     tmem_fence_after();
     if (tid == 0 && j + 1 < nstate && !abort_sh) load_w1(j + 1);  // product 1 of j no longer reads W1
     {
-      // the eight 32-column chunks of a row: 3 for warps 0-3 (they also run the read-out
-      // LayerNorm below), 5 for warps 4-7
+      // the 32-column chunks of a row: [0, SPLIT) for warps 0-3 (they also run the read-out
+      // LayerNorm below), the rest for warps 4-7
       const int q = warp & 3, row = 32 * q + lane;
-      const int c_begin = warp < 4 ? 0 : 3, c_end = warp < 4 ? 3 : 8;
+      const int c_begin = warp < 4 ? 0 : L::SPLIT, c_end = warp < 4 ? L::SPLIT : L::CHUNKS;
       const float* b1 = reinterpret_cast<const float*>(smem + OFF_B1) + (j % 3) * FF;
 #pragma unroll 1
       for (int c4 = c_begin; c4 < c_end; ++c4) {
@@ -469,13 +489,15 @@ using namespace memo;
 
 static bool aligned16(const void* q) { return ((uintptr_t)q & 15) == 0; }
 
-// Scratch layout: W1^T and W2^T 16-bit copies, then summary (and d summary) fp32.
-static size_t prep_bytes(long long B, long long NH, long long NS) { return (size_t)(B * NH * NS) * 2 * F * FF * 2; }
+// Scratch layout: W1^T and W2^T 16-bit copies (sized for the widest inner MLP), then
+// summary (and d summary) fp32.
+static size_t prep_bytes(long long B, long long NH, long long NS) { return (size_t)(B * NH * NS) * 2 * F * FF_MAX * 2; }
 
-template <typename T>
+template <typename T, int FF>
 static int run(MemoMixParams p, bool bwd, cudaStream_t stream, const char* who) {
   const long long streams = (long long)p.B * p.NH;
-  memo_prep_kernel<T><<<(unsigned)(streams * p.NS), 256, 0, stream>>>(p);
+  constexpr int SMEM = Mix<FF>::SMEM;
+  memo_prep_kernel<T, FF><<<(unsigned)(streams * p.NS), 256, 0, stream>>>(p);
   int rc = check_launch(who);
   if (rc) return rc;
   Maps maps;
@@ -492,13 +514,13 @@ static int run(MemoMixParams p, bool bwd, cudaStream_t stream, const char* who) 
   }
   const unsigned grid = (unsigned)(streams * p.NS * p.TILES);
   if (!bwd) {
-    rc = prepare_smem(memo_mix_kernel<T, false>, SMEM, who);
+    rc = prepare_smem(memo_mix_kernel<T, false, FF>, SMEM, who);
     if (rc) return rc;
-    memo_mix_kernel<T, false><<<grid, NTHREADS, SMEM, stream>>>(p, maps);
+    memo_mix_kernel<T, false, FF><<<grid, NTHREADS, SMEM, stream>>>(p, maps);
   } else {
-    rc = prepare_smem(memo_mix_kernel<T, true>, SMEM, who);
+    rc = prepare_smem(memo_mix_kernel<T, true, FF>, SMEM, who);
     if (rc) return rc;
-    memo_mix_kernel<T, true><<<grid, NTHREADS, SMEM, stream>>>(p, maps);
+    memo_mix_kernel<T, true, FF><<<grid, NTHREADS, SMEM, stream>>>(p, maps);
     rc = check_launch(who);
     if (rc) return rc;
     memo_dxk_kernel<T><<<148 * 8, 256, 0, stream>>>(p);
@@ -509,8 +531,8 @@ static int run(MemoMixParams p, bool bwd, cudaStream_t stream, const char* who) 
 static int check_mix(int B, int NH, int NC, int CS, int F_, int FF_, int M, int dt, int dt_ln, const char* who) {
   TTT_REQUIRE(B > 0 && NH > 0 && NC > 0 && M > 0, TTT_ERR_SHAPE, "%s: B, NH, NC, memo_segment_size must be positive",
               who);
-  TTT_REQUIRE(CS == C && F_ == F && FF_ == FF, TTT_ERR_UNSUPPORTED,
-              "%s: implemented for CS = 16, F = 64, FF = 256 (got %d, %d, %d)", who, CS, F_, FF_);
+  TTT_REQUIRE(CS == C && F_ == F && (FF_ == 256 || FF_ == 64), TTT_ERR_UNSUPPORTED,
+              "%s: implemented for CS = 16, F = 64, FF = 256 or 64 (got %d, %d, %d)", who, CS, F_, FF_);
   TTT_REQUIRE((NC + M - 1) / M <= NS_MAX, TTT_ERR_UNSUPPORTED, "%s: at most %d memo segments (got %d)", who, NS_MAX,
               (NC + M - 1) / M);
   TTT_REQUIRE(dt == DT_BF16 || dt == DT_F16, TTT_ERR_DTYPE, "%s: activations must be bf16 or f16", who);
@@ -563,8 +585,11 @@ extern "C" int ttt_memo_mix_fwd(int B, int NH, int NC, int CS, int F, int FF, in
   p.W2T = sc + half;
   p.summary = reinterpret_cast<float*>(sc + 2 * half);
   p.dsum = p.summary + (size_t)B * NH * p.NS * memo::F;
-  return dt == DT_BF16 ? run<__nv_bfloat16>(p, false, (cudaStream_t)stream, who)
-                       : run<__half>(p, false, (cudaStream_t)stream, who);
+  if (FF == 64)
+    return dt == DT_BF16 ? run<__nv_bfloat16, 64>(p, false, (cudaStream_t)stream, who)
+                         : run<__half, 64>(p, false, (cudaStream_t)stream, who);
+  return dt == DT_BF16 ? run<__nv_bfloat16, 256>(p, false, (cudaStream_t)stream, who)
+                       : run<__half, 256>(p, false, (cudaStream_t)stream, who);
 }
 
 extern "C" int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, int memo_segment_size, const void* XQW,
@@ -593,6 +618,9 @@ extern "C" int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, in
   p.W2T = sc + half;
   p.summary = reinterpret_cast<float*>(sc + 2 * half);
   p.dsum = p.summary + (size_t)B * NH * p.NS * memo::F;
-  return dt == DT_BF16 ? run<__nv_bfloat16>(p, true, (cudaStream_t)stream, who)
-                       : run<__half>(p, true, (cudaStream_t)stream, who);
+  if (FF == 64)
+    return dt == DT_BF16 ? run<__nv_bfloat16, 64>(p, true, (cudaStream_t)stream, who)
+                         : run<__half, 64>(p, true, (cudaStream_t)stream, who);
+  return dt == DT_BF16 ? run<__nv_bfloat16, 256>(p, true, (cudaStream_t)stream, who)
+                       : run<__half, 256>(p, true, (cudaStream_t)stream, who);
 }

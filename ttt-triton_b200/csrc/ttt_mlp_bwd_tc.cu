@@ -1,5 +1,7 @@
-// TTT-MLP backward on the tensor cores (mma.sync bf16/fp16, fp32 accumulate) for the
-// benchmark shape: F = 64, FF = 256, CS = 16, 16-bit activations.
+// TTT-MLP backward on the tensor cores (mma.sync bf16/fp16, fp32 accumulate) for F = 64,
+// CS = 16, 16-bit activations and an inner width FF = 32 * NW: the benchmark MLP (FF = 256,
+// NW = 8 warps, one CTA per SM) and the layer's F x F inner MLP (FF = 64, NW = 2, two CTAs
+// per SM).
 //
 // Uses the per-mini-batch fp32 pre-activations the forward stored (Z1 = XK W1 + b1,
 // Z2 = X2 W2 + b2, Z1bar and Z2bar before their nonlinearities) and walks the sequence
@@ -11,10 +13,10 @@
 // reversed. The per-step gradient is autograd through ops/ttt_mlp.py:9-67 (full CS x CS
 // d_eta), derived by hand.
 //
-// One CTA of 8 warps per (batch, head) stream, one CTA per SM; warp w owns hidden units
-// [32w, 32w + 32). Its slices of W1, W2 and of the carried gradients dW1, dW2 (fp32, 256
-// values per thread in accumulator-fragment layout) live in tensor memory: the CTA holds
-// all 512 columns. Products that contract over the hidden units ([16 x 64] results, and
+// One CTA of NW warps per (batch, head) stream; warp w owns hidden units [32w, 32w + 32).
+// Its slices of W1, W2 and of the carried gradients dW1, dW2 (fp32, 256 values per thread
+// in accumulator-fragment layout) live in tensor memory: 256 columns of the warp's lane
+// quadrant (the 8-warp CTA holds all 512 columns). Products that contract over the hidden units ([16 x 64] results, and
 // the 16 x 16 A2 / dP1) are per-warp partial sums reduced through shared memory; A2
 // enters every formula linearly, so only its partials are formed. Per mini-batch:
 //   R1 (rows)  G2 = ln_fused_l2_bwd(Z2, XV - XK); dZ2bar = read-out LayerNorm backward
@@ -38,67 +40,82 @@ namespace ttt {
 namespace mlp_tc {
 namespace bwd {
 
-constexpr int NW = 8, NTHREADS = 32 * NW, NSTAGE = 2;
+constexpr int NSTAGE = 2;
 constexpr int TILE = C * F * 2;   // one 16 x 64 16-bit tile
 constexpr int ETA = C * C * 2;    // one 16 x 16 16-bit tile
-constexpr int ZLD = FF + 8;       // fp32 row stride of the staged Z1 / Z1bar (conflict-free float2)
+constexpr int PLD = F + 8;        // fp32 row stride of the partial tiles
 constexpr int OFF_XQ = 0, OFF_XK = TILE, OFF_XV = 2 * TILE, OFF_DO = 3 * TILE, OFF_ETA = 4 * TILE;
 constexpr int OFF_Z2 = OFF_ETA + ETA;           // fp32 [C][F]
 constexpr int OFF_Z2B = OFF_Z2 + C * F * 4;     // fp32 [C][F]
 constexpr int OFF_Z1 = OFF_Z2B + C * F * 4;     // fp32 [C][ZLD]
-constexpr int OFF_Z1B = OFF_Z1 + C * ZLD * 4;   // fp32 [C][ZLD]
-constexpr int STAGE = OFF_Z1B + C * ZLD * 4;    // 50688 bytes
-constexpr int PLD = F + 8;                      // fp32 row stride of the partial tiles
-constexpr int PART = NW * C * PLD * 4;          // one [NW][C][PLD] set of partial tiles
-constexpr int OFF_PA = NSTAGE * STAGE;          // partial dG2 (M1 -> R2), then partial dXQ (M2 -> R3)
-constexpr int OFF_PB = OFF_PA + PART;           // partial dXK (M1, M2 -> R3)
-constexpr int OFF_G = OFF_PB + PART;            // 16-bit swizzled [C][F]: G2
-constexpr int OFF_EG = OFF_G + TILE;            //   e * G2
-constexpr int OFF_DZB = OFF_EG + TILE;          //   dZ2bar
-constexpr int OFF_DZ2 = OFF_DZB + TILE;         //   dZ2
-constexpr int OFF_DETAP = OFF_DZ2 + TILE;       // fp32 [NW][C*C] partial d_eta
-constexpr int OFF_DP1P = OFF_DETAP + NW * C * C * 4;  // fp32 [NW][C*C] partial dP1
-constexpr int OFF_DP1 = OFF_DP1P + NW * C * C * 4;    // fp32 [C*C] dP1
-constexpr int OFF_DE = OFF_DP1 + C * C * 4;           // fp32 [NW][C] partial d e
-constexpr int OFF_DE2 = OFF_DE + NW * C * 4;          // fp32 [C] -G2 . db2
-constexpr int OFF_DB2 = OFF_DE2 + C * 4;              // fp32 [F] carried db2
-constexpr int SMEM = OFF_DB2 + F * 4;
-constexpr uint32_t TMEM_COLS = 512;  // per warp: W1^T, W2^T, dW1^T, dW2^T slices, 64 columns each
 
-static_assert(SMEM <= 227 * 1024, "shared memory budget");
-static_assert(OFF_PA % 128 == 0 && OFF_G % 128 == 0 && STAGE % 128 == 0, "tile alignment");
+// Layout of a CTA of NW warps (inner width FFW = 32 * NW).
+template <int NW_>
+struct Bwd {
+  static constexpr int NW = NW_, NTHREADS = 32 * NW, FFW = 32 * NW;
+  static constexpr int ZLD = FFW + 8;                        // fp32 row stride of the staged Z1 / Z1bar
+  static constexpr int OFF_Z1B = OFF_Z1 + C * ZLD * 4;       // fp32 [C][ZLD]
+  static constexpr int STAGE = OFF_Z1B + C * ZLD * 4;        // 50688 bytes for FF = 256
+  static constexpr int PART = NW * C * PLD * 4;              // one [NW][C][PLD] set of partial tiles
+  static constexpr int OFF_PA = NSTAGE * STAGE;              // partial dG2 (M1 -> R2), then partial dXQ (M2 -> R3)
+  static constexpr int OFF_PB = OFF_PA + PART;               // partial dXK (M1, M2 -> R3)
+  static constexpr int OFF_G = OFF_PB + PART;                // 16-bit swizzled [C][F]: G2
+  static constexpr int OFF_EG = OFF_G + TILE;                //   e * G2
+  static constexpr int OFF_DZB = OFF_EG + TILE;              //   dZ2bar
+  static constexpr int OFF_DZ2 = OFF_DZB + TILE;             //   dZ2
+  static constexpr int OFF_DETAP = OFF_DZ2 + TILE;           // fp32 [NW][C*C] partial d_eta
+  static constexpr int OFF_DP1P = OFF_DETAP + NW * C * C * 4;  // fp32 [NW][C*C] partial dP1
+  static constexpr int OFF_DP1 = OFF_DP1P + NW * C * C * 4;    // fp32 [C*C] dP1
+  static constexpr int OFF_DE = OFF_DP1 + C * C * 4;           // fp32 [NW][C] partial d e
+  static constexpr int OFF_DE2 = OFF_DE + NW * C * 4;          // fp32 [C] -G2 . db2
+  static constexpr int OFF_DB2 = OFF_DE2 + C * 4;              // fp32 [F] carried db2
+  static constexpr int SMEM = OFF_DB2 + F * 4;
+  // per warp: W1^T, W2^T, dW1^T, dW2^T slices, 64 columns each, in its lane quadrant
+  static constexpr uint32_t TMEM_COLS = NW > 4 ? 512 : 256;
+  static constexpr int CTAS_PER_SM = NW > 4 ? 1 : 2;
+  static_assert(SMEM * CTAS_PER_SM <= 227 * 1024, "shared memory budget");
+  static_assert(OFF_PA % 128 == 0 && OFF_G % 128 == 0 && STAGE % 128 == 0, "tile alignment");
+};
 
+template <int NW>
 __device__ __forceinline__ void load_stage(uint8_t* st, const MlpBwdParams& p, long long s, int n) {
+  using L = Bwd<NW>;
+  constexpr int NT = L::NTHREADS, FFW = L::FFW, ZLD = L::ZLD;
   const int tid = threadIdx.x;
   const long long mb = s * p.NC + n;  // mini-batch index
+  const uint32_t sb = smem_u32(st);
   {
     const long long tb = mb * (long long)(C * F) * 2;
-    const int row = (tid & 127) >> 3, ch = tid & 7;
-    const uint32_t dst = smem_u32(st) + swz128(row, ch);
-    const long long src = tb + row * 128 + ch * 16;
-    if (tid < 128) {
-      cp_async16(dst + OFF_XQ, (const uint8_t*)p.XQ + src);
-      cp_async16(dst + OFF_XK, (const uint8_t*)p.XK + src);
-      if (tid < 32) cp_async16(smem_u32(st) + OFF_ETA + tid * 16, (const uint8_t*)p.eta + mb * (C * C) * 2 + tid * 16);
-    } else {
-      cp_async16(dst + OFF_XV, (const uint8_t*)p.XV + src);
-      cp_async16(dst + OFF_DO, (const uint8_t*)p.dout + src);
+    for (int c = tid; c < 256; c += NT) {  // XQ, XK (chunks 0..127) and XV, dO (128..255)
+      const int row = (c & 127) >> 3, ch = c & 7;
+      const uint32_t dst = sb + swz128(row, ch);
+      const long long src = tb + row * 128 + ch * 16;
+      if (c < 128) {
+        cp_async16(dst + OFF_XQ, (const uint8_t*)p.XQ + src);
+        cp_async16(dst + OFF_XK, (const uint8_t*)p.XK + src);
+      } else {
+        cp_async16(dst + OFF_XV, (const uint8_t*)p.XV + src);
+        cp_async16(dst + OFF_DO, (const uint8_t*)p.dout + src);
+      }
     }
+    if (tid < 32) cp_async16(sb + OFF_ETA + tid * 16, (const uint8_t*)p.eta + mb * (C * C) * 2 + tid * 16);
   }
-  // Z2, Z2bar: 4 KB each, one 16-byte chunk per thread
-  cp_async16(smem_u32(st) + OFF_Z2 + tid * 16, p.Z2_saved + mb * (C * F) + tid * 4);
-  cp_async16(smem_u32(st) + OFF_Z2B + tid * 16, p.Z2b_saved + mb * (C * F) + tid * 4);
-  // Z1, Z1bar: 16 rows of 64 chunks each, into padded rows
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c = tid + NTHREADS * i, row = c >> 6, col = c & 63;
-    const long long src = mb * (C * FF) + row * FF + col * 4;
-    cp_async16(smem_u32(st) + OFF_Z1 + (row * ZLD + col * 4) * 4, p.Z1_saved + src);
-    cp_async16(smem_u32(st) + OFF_Z1B + (row * ZLD + col * 4) * 4, p.Z1b_saved + src);
+  // Z2, Z2bar: 4 KB each, 256 chunks of 16 bytes
+  for (int c = tid; c < 256; c += NT) {
+    cp_async16(sb + OFF_Z2 + c * 16, p.Z2_saved + mb * (C * F) + c * 4);
+    cp_async16(sb + OFF_Z2B + c * 16, p.Z2b_saved + mb * (C * F) + c * 4);
+  }
+  // Z1, Z1bar: 16 rows of FFW / 4 chunks each, into padded rows
+  for (int c = tid; c < C * FFW / 4; c += NT) {
+    const int row = c / (FFW / 4), col = c % (FFW / 4);
+    const long long src = mb * (C * FFW) + row * FFW + col * 4;
+    cp_async16(sb + OFF_Z1 + (row * ZLD + col * 4) * 4, p.Z1_saved + src);
+    cp_async16(sb + L::OFF_Z1B + (row * ZLD + col * 4) * 4, p.Z1b_saved + src);
   }
 }
 
-// Sum of the 8 warps' partial tiles for token tk, features 4q..4q+3.
+// Sum of the NW warps' partial tiles for token tk, features 4q..4q+3.
+template <int NW>
 __device__ __forceinline__ void sum_part(const float* part, int tk, int q, float* z) {
   float4 acc = *reinterpret_cast<const float4*>(part + tk * PLD + 4 * q);
 #pragma unroll
@@ -134,16 +151,23 @@ __device__ __forceinline__ void put_part(float* pw, const float (*X)[4], int g, 
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p) {
+template <typename T, int NW>
+__global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kernel(MlpBwdParams p) {
   using H = Half2<T>;
+  using L = Bwd<NW>;
+  constexpr int NTHREADS = L::NTHREADS, FFW = L::FFW, ZLD = L::ZLD, STAGE = L::STAGE;
+  constexpr int OFF_Z1B = L::OFF_Z1B, OFF_PA = L::OFF_PA, OFF_PB = L::OFF_PB, OFF_G = L::OFF_G, OFF_EG = L::OFF_EG;
+  constexpr int OFF_DZB = L::OFF_DZB, OFF_DZ2 = L::OFF_DZ2, OFF_DETAP = L::OFF_DETAP, OFF_DP1P = L::OFF_DP1P;
+  constexpr int OFF_DP1 = L::OFF_DP1, OFF_DE = L::OFF_DE, OFF_DE2 = L::OFF_DE2, OFF_DB2 = L::OFF_DB2;
+  constexpr uint32_t TMEM_COLS = L::TMEM_COLS;
+  constexpr int TPP = NTHREADS / 16, NPASS = C / TPP;  // row phases: tokens per pass, passes
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t tmem_base_sh;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int mi = lane >> 3, r8 = lane & 7;
   const long long s = blockIdx.x;
   const int h = (int)(s % p.NH);
-  const int tk = tid >> 4, q = tid & 15;
+  const int tk0 = tid >> 4, q = tid & 15;
   const int fb = 32 * warp;
   float* PA = reinterpret_cast<float*>(smem + OFF_PA);
   float* PB = reinterpret_cast<float*>(smem + OFF_PB);
@@ -167,8 +191,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
   const uint32_t tS2 = tS1 + 64, tD1 = tS1 + 128, tD2 = tS1 + 192;
   {
     float S1[2][8][4], S2[4][4][4];
-    w1_io(S1, const_cast<float*>(p.W1_last + s * F * FF), fb, g, t, false);
-    w2_io(S2, const_cast<float*>(p.W2_last + s * FF * F), fb, g, t, false);
+    w1_io<2, FFW>(S1, const_cast<float*>(p.W1_last + s * F * FFW), fb, g, t, false);
+    w2_io(S2, const_cast<float*>(p.W2_last + s * FFW * F), fb, g, t, false);
     slice_st(tS1, &S1[0][0][0]);
     slice_st(tS2, &S2[0][0][0]);
     float zero[64];
@@ -191,25 +215,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
   const uint32_t a_ones[4] = {ones, ones, ones, ones};
   const float one_w0 = warp == 0 ? 1.f : 0.f;  // the "+1" of P2 = eta * (A2 + 1) goes to warp 0's partial
 
-  load_stage(smem, p, s, p.NC - 1);
+  load_stage<NW>(smem, p, s, p.NC - 1);
   cp_async_commit();
 
   for (int it = 0; it < p.NC; ++it) {
     const int n = p.NC - 1 - it;
     cp_async_wait<0>();
     __syncthreads();  // stage of mini-batch n landed; every warp is done with mini-batch n+1
-    if (it + 1 < p.NC) load_stage(smem + ((it + 1) % NSTAGE) * STAGE, p, s, n - 1);
+    if (it + 1 < p.NC) load_stage<NW>(smem + ((it + 1) % NSTAGE) * STAGE, p, s, n - 1);
     cp_async_commit();
     const uint8_t* st = smem + (it % NSTAGE) * STAGE;
     const uint32_t sb = smem_u32(st);
     const T* E = reinterpret_cast<const T*>(st + OFF_ETA);
     const long long xb = (s * p.NC + n) * (long long)(C * F);
-    const uint32_t xo = swz128(tk, q >> 1) + (q & 1) * 8;
+    auto xo_of = [&](int tk) { return swz128(tk, q >> 1) + (q & 1) * 8; };
 
     // G2 = ln_fused_l2_bwd(Z2, XV - XK) for token tk, features 4q.., with its normalised input
     // xh, the scaled residual gh and 1/std (rows; formed in R1 and again in R2 rather than
     // kept in registers across M1)
-    auto g2_rows = [&](float* xh, float* gh, float* Gr, float& rstd) {
+    auto g2_rows = [&](int tk, float* xh, float* gh, float* Gr, float& rstd) {
+      const uint32_t xo = xo_of(tk);
       const float4 z4 = *reinterpret_cast<const float4*>(st + OFF_Z2 + (tk * F + 4 * q) * 4);
       float z[4] = {z4.x, z4.y, z4.z, z4.w}, xv[4], xk[4];
       unpack4<T>(st + OFF_XV + xo, xv);
@@ -238,9 +263,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
     };
 
     // ---------------- R1: G2 from the stored Z2; read-out LayerNorm backward from Z2bar
-    {
+#pragma unroll
+    for (int tk = tk0; tk < C; tk += TPP) {
+      const uint32_t xo = xo_of(tk);
       float xh[4], gh[4], Gr[4], rstd;
-      g2_rows(xh, gh, Gr, rstd);
+      g2_rows(tk, xh, gh, Gr, rstd);
       const float e = (float)E[(C - 1) * C + tk];
       *reinterpret_cast<uint2*>(smem + OFF_G + xo) = make_uint2(H::pack(Gr[0], Gr[1]), H::pack(Gr[2], Gr[3]));
       *reinterpret_cast<uint2*>(smem + OFF_EG + xo) =
@@ -249,7 +276,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
       const float dot = red16(Gr[0] * db.x + Gr[1] * db.y + Gr[2] * db.z + Gr[3] * db.w);
       if (q == 0) DE2[tk] = -dot;
     }
-    {
+#pragma unroll
+    for (int tk = tk0; tk < C; tk += TPP) {
+      const uint32_t xo = xo_of(tk);
       const float4 z4 = *reinterpret_cast<const float4*>(st + OFF_Z2B + (tk * F + 4 * q) * 4);
       float z[4] = {z4.x, z4.y, z4.z, z4.w}, dO4[4];
       unpack4<T>(st + OFF_DO + xo, dO4);
@@ -698,11 +727,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
     __syncthreads();
 
     // ---------------- R2: dG2 -> backward of G2 = ln_fused_l2_bwd(Z2, XV - XK); d_eta, dP1
-    float DTr[4];
-    {
+    float DTr[NPASS][4];
+#pragma unroll
+    for (int ps = 0; ps < NPASS; ++ps) {
+      const int tk = tk0 + ps * TPP;
+      const uint32_t xo = xo_of(tk);
       float dG[4], xv[4], xk[4], xh[4], gh[4], Gr[4], rstd;
-      g2_rows(xh, gh, Gr, rstd);
-      sum_part(PA, tk, q, dG);
+      g2_rows(tk, xh, gh, Gr, rstd);
+      sum_part<NW>(PA, tk, q, dG);
       const float e = (float)E[(C - 1) * C + tk];
       const float4 db = *reinterpret_cast<const float4*>(DB2 + 4 * q);
       dG[0] -= e * db.x;
@@ -730,7 +762,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
       for (int j = 0; j < 4; ++j) {
         const float dgh = (F * dG[j] - sdG - xh[j] * sdGx) * inv;
         dxh[j] = -(dG[j] * sgx + gh[j] * sdGx) * inv + dgh * gm[j] * gm[j];
-        DTr[j] = -dgh * gm[j];
+        DTr[ps][j] = -dgh * gm[j];
         const float go = gm[j] * xh[j] + bt[j] - (xv[j] - xk[j]);
         dgam[j] += dgh * (go + gm[j] * xh[j]);
         dbet[j] += dgh * gm[j];
@@ -744,29 +776,31 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
       for (int j = 0; j < 4; ++j) dz[j] = (F * dxh[j] - sx - xh[j] * sxx) * inv + dstd * xh[j] * (1.f / F);
       *reinterpret_cast<uint2*>(smem + OFF_DZ2 + xo) = make_uint2(H::pack(dz[0], dz[1]), H::pack(dz[2], dz[3]));
       *reinterpret_cast<uint2*>((uint8_t*)p.dXV + (xb + tk * F + 4 * q) * 2) =
-          make_uint2(H::pack(DTr[0], DTr[1]), H::pack(DTr[2], DTr[3]));
+          make_uint2(H::pack(DTr[ps][0], DTr[ps][1]), H::pack(DTr[ps][2], DTr[ps][3]));
     }
-    {
+#pragma unroll
+    for (int el = tid; el < C * C; el += NTHREADS) {  // element (el / C, el % C) of d_eta and dP1
       float v = 0.f, u = 0.f;
 #pragma unroll
       for (int w = 0; w < NW; ++w) {
-        v += DETAP[w * C * C + tid];
-        u += DP1P[w * C * C + tid];
+        v += DETAP[w * C * C + el];
+        u += DP1P[w * C * C + el];
       }
-      if ((tid >> 4) == C - 1) {
-        const int j = tid & 15;
+      if ((el >> 4) == C - 1) {
+        const int j = el & 15;
         float de = DE2[j];
 #pragma unroll
         for (int w = 0; w < NW; ++w) de += DE[w * C + j];
         v += de;
       }
-      reinterpret_cast<T*>(p.deta)[(s * p.NC + n) * (long long)(C * C) + tid] = H::from_float(v);
-      DP1[tid] = u;
+      reinterpret_cast<T*>(p.deta)[(s * p.NC + n) * (long long)(C * C) + el] = H::from_float(v);
+      DP1[el] = u;
     }
     __syncthreads();
 
     // ---------------- M2
-    // dX2 += dZ2 W2_n^T ; dW2^T += dZ2^T X2 ; db2 += 1^T (dZ2bar + dZ2) (warp w: features 8w..8w+7)
+    // dX2 += dZ2 W2_n^T ; dW2^T += dZ2^T X2 ; db2 += 1^T (dZ2bar + dZ2) (warp w: features
+    // 8fw..8fw+7 for fw = w, w + NW, ..)
     {
       float S2[4][4][4];
       slice_ld(tS2, &S2[0][0][0]);
@@ -797,17 +831,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
       }
       slice_st(tD2, &D2[0][0][0]);
     }
-    {
+#pragma unroll
+    for (int fw = warp; fw < F / 8; fw += NW) {
       uint32_t b1[2], b2[2];
-      const uint32_t off = swz128((lane & 8) + r8, warp);
+      const uint32_t off = swz128((lane & 8) + r8, fw);
       ldsm_x2_t(b1, sDZB + off);
       ldsm_x2_t(b2, sDZ2 + off);
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       mma16816<T>(acc, a_ones, b1);
       mma16816<T>(acc, a_ones, b2);
       if (g == 0) {
-        DB2[8 * warp + 2 * t] += acc[0];
-        DB2[8 * warp + 2 * t + 1] += acc[1];
+        DB2[8 * fw + 2 * t] += acc[0];
+        DB2[8 * fw + 2 * t + 1] += acc[1];
       }
     }
     // dZ1 += dX2 * gelu'(Z1)
@@ -835,7 +870,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
       aA1T[3] = H::pack(da(2 * t + 8, g + 8), da(2 * t + 9, g + 8));
     }
     // partial dXQ = dZ1bar W1_n^T (+ dA1 XK), partial dXK += dZ1 W1_n^T (+ dA1^T XQ); the dA1
-    // terms go to warp w's columns 8w..8w+7 only, the reduction adds them once
+    // terms go to warp w's columns 8fw..8fw+7 (fw = w, w + NW, ..) only, the reduction adds
+    // them once
     {
       float QX[8][4], KX[8][4];
 #pragma unroll
@@ -856,20 +892,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
           mma16816<T>(KX[nf], a1, b);
         }
       }
-      uint32_t bxk[2], bxq[2];
-      const uint32_t off = swz128((lane & 8) + r8, warp);
-      ldsm_x2_t(bxk, sb + OFF_XK + off);
-      ldsm_x2_t(bxq, sb + OFF_XQ + off);
-      float cq[4] = {0.f, 0.f, 0.f, 0.f}, ck[4] = {0.f, 0.f, 0.f, 0.f};
-      mma16816<T>(cq, aA1, bxk);
-      mma16816<T>(ck, aA1T, bxq);
 #pragma unroll
-      for (int nf = 0; nf < 8; ++nf)
-        if (nf == warp) {
+      for (int fw = 0; fw < F / 8; ++fw)
+        if (fw % NW == warp) {
+          uint32_t bxk[2], bxq[2];
+          const uint32_t off = swz128((lane & 8) + r8, fw);
+          ldsm_x2_t(bxk, sb + OFF_XK + off);
+          ldsm_x2_t(bxq, sb + OFF_XQ + off);
+          float cq[4] = {0.f, 0.f, 0.f, 0.f}, ck[4] = {0.f, 0.f, 0.f, 0.f};
+          mma16816<T>(cq, aA1, bxk);
+          mma16816<T>(ck, aA1T, bxq);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            QX[nf][c] += cq[c];
-            KX[nf][c] += ck[c];
+            QX[fw][c] += cq[c];
+            KX[fw][c] += ck[c];
           }
         }
       put_part<false>(PA + warp * C * PLD, QX, g, t);
@@ -916,15 +952,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
     __syncthreads();
 
     // ---------------- R3: dXQ = dO + sum of partials, dXK = sum of partials - dXV
-    {
+#pragma unroll
+    for (int ps = 0; ps < NPASS; ++ps) {
+      const int tk = tk0 + ps * TPP;
+      const uint32_t xo = xo_of(tk);
       float dq[4], dk[4], dO4[4];
-      sum_part(PA, tk, q, dq);
-      sum_part(PB, tk, q, dk);
+      sum_part<NW>(PA, tk, q, dq);
+      sum_part<NW>(PB, tk, q, dk);
       unpack4<T>(st + OFF_DO + xo, dO4);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         dq[j] += dO4[j];
-        dk[j] -= DTr[j];
+        dk[j] -= DTr[ps][j];
       }
       const long long o = (xb + tk * F + 4 * q) * 2;
       *reinterpret_cast<uint2*>((uint8_t*)p.dXQ + o) = make_uint2(H::pack(dq[0], dq[1]), H::pack(dq[2], dq[3]));
@@ -938,16 +977,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
   {
     float D1[2][8][4];
     slice_ld(tD1, &D1[0][0][0]);
-    w1_io(D1, p.dW1 + s * F * FF, fb, g, t, true);
+    w1_io<2, FFW>(D1, p.dW1 + s * F * FFW, fb, g, t, true);
     float D2[4][4][4];
     slice_ld(tD2, &D2[0][0][0]);
-    w2_io(D2, p.dW2 + s * FF * F, fb, g, t, true);
+    w2_io(D2, p.dW2 + s * FFW * F, fb, g, t, true);
   }
   if (g == 0) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      p.db1[s * FF + fb + 8 * j + 2 * t] = DB1[j][0];
-      p.db1[s * FF + fb + 8 * j + 2 * t + 1] = DB1[j][1];
+      p.db1[s * FFW + fb + 8 * j + 2 * t] = DB1[j][0];
+      p.db1[s * FFW + fb + 8 * j + 2 * t + 1] = DB1[j][1];
     }
   }
   if (tid < F) p.db2[s * F + tid] = DB2[tid];
@@ -967,8 +1006,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
   tmem_fence_before();
   __syncthreads();
   tmem_fence_after();
-  if (tid < 2 * F) {
-    const int which = tid / F, f = tid % F;
+  for (int e = tid; e < 2 * F; e += NTHREADS) {
+    const int which = e / F, f = e % F;
     float acc = 0.f;
 #pragma unroll
     for (int w = 0; w < NW; ++w) acc += RED[(w * 2 + which) * F + f];
@@ -983,12 +1022,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) mlp_bwd_tc_kernel(MlpBwdParams p)
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+template <typename T, int NW>
+static int launch_bwd(const MlpBwdParams& p, cudaStream_t stream) {
+  using namespace mlp_tc::bwd;
+  int rc = prepare_smem(mlp_bwd_tc_kernel<T, NW>, Bwd<NW>::SMEM, "ttt_mlp_bwd");
+  if (rc) return rc;
+  mlp_bwd_tc_kernel<T, NW><<<p.B * p.NH, Bwd<NW>::NTHREADS, Bwd<NW>::SMEM, stream>>>(p);
+  return check_launch("ttt_mlp_bwd");
+}
+
 int mlp_bwd_fast(const MlpBwdParams& p, cudaStream_t stream) {
   using namespace mlp_tc;
   using namespace mlp_tc::bwd;
   if (!p.Z1_saved || !p.Z2_saved || !p.Z1b_saved || !p.Z2b_saved || !p.W1_last || !p.W2_last)
     return TTT_NOT_APPLICABLE;
-  if (p.CS != C || p.F != F || p.FF != FF) return TTT_NOT_APPLICABLE;
+  if (p.CS != C || p.F != F || (p.FF != 256 && p.FF != 64)) return TTT_NOT_APPLICABLE;
   const int dt = p.dt_xq;
   if (dt != DT_BF16 && dt != DT_F16) return TTT_NOT_APPLICABLE;
   if (p.dt_xk != dt || p.dt_xv != dt || p.dt_eta != dt || p.dt_dout != dt || p.dt_grad != dt) return TTT_NOT_APPLICABLE;
@@ -996,17 +1044,9 @@ int mlp_bwd_fast(const MlpBwdParams& p, cudaStream_t stream) {
       !aligned16(p.Z1_saved) || !aligned16(p.Z2_saved) || !aligned16(p.Z1b_saved) || !aligned16(p.Z2b_saved) ||
       !aligned16(p.dXQ) || !aligned16(p.dXK) || !aligned16(p.dXV))
     return TTT_NOT_APPLICABLE;
-  int rc;
-  if (dt == DT_BF16) {
-    rc = prepare_smem(mlp_bwd_tc_kernel<__nv_bfloat16>, SMEM, "ttt_mlp_bwd");
-    if (rc) return rc;
-    mlp_bwd_tc_kernel<__nv_bfloat16><<<p.B * p.NH, NTHREADS, SMEM, stream>>>(p);
-  } else {
-    rc = prepare_smem(mlp_bwd_tc_kernel<__half>, SMEM, "ttt_mlp_bwd");
-    if (rc) return rc;
-    mlp_bwd_tc_kernel<__half><<<p.B * p.NH, NTHREADS, SMEM, stream>>>(p);
-  }
-  return check_launch("ttt_mlp_bwd");
+  if (p.FF == 256)
+    return dt == DT_BF16 ? launch_bwd<__nv_bfloat16, 8>(p, stream) : launch_bwd<__half, 8>(p, stream);
+  return dt == DT_BF16 ? launch_bwd<__nv_bfloat16, 2>(p, stream) : launch_bwd<__half, 2>(p, stream);
 }
 
 }  // namespace ttt

@@ -1,14 +1,16 @@
-// TTT-MLP forward on the tensor cores (mma.sync bf16/fp16, fp32 accumulate) for the
-// benchmark shape: F = 64, FF = 256, CS = 16, 16-bit activations.
+// TTT-MLP forward on the tensor cores (mma.sync bf16/fp16, fp32 accumulate) for F = 64,
+// CS = 16, 16-bit activations and an inner width FF = 32 * NW: the benchmark MLP
+// (FF = 256, NW = 8 warps) and the layer's F x F inner MLP (FF = 64, NW = 2).
 //
-// One CTA of 8 warps per (batch, head) stream; warp w owns hidden units
+// One CTA of NW warps per (batch, head) stream; warp w owns hidden units
 // [32w, 32w + 32). Its slices of the fp32 state, W1^T (32 x 64) and W2^T (64 x 32), stay in
 // mma accumulator fragments for the whole sequence (the accumulator layout of W1^T is the
 // B-operand layout of W1, and of W2^T the B layout of W2); the biases live in shared
 // memory. Per mini-batch (ops/ttt_mlp.py:9-67):
 //   A (MMA)  Z1 = XK W1 + b1, Z1q = XQ W1 + b1, X2 = gelu(Z1), partial Z2_w = X2_w W2_w;
 //            warps 0-1 form -P1 = -eta * (XQ XK^T + 1)
-//   C (rows) Z2 = sum_w Z2_w + b2, G2 = ln_fused_l2_bwd(Z2, XV - XK) (16 lanes per token)
+//   C (rows) Z2 = sum_w Z2_w + b2, G2 = ln_fused_l2_bwd(Z2, XV - XK) (16 lanes per token,
+//            32 * NW / 16 tokens per pass)
 //   D (MMA)  H = G2 W2^T, G1 = H * gelu_bwd(Z1); W1 += XK^T (-e G1), b1 += 1^T (-e G1);
 //            Z1bar = Z1q - P1 G1, X2bar = gelu(Z1bar), A2_w = X2bar_w X2_w^T,
 //            partial Z2bar_w = X2bar_w W2_w - (eta * A2_w) G2  (- eta G2 once);
@@ -31,7 +33,7 @@
 namespace ttt {
 namespace mlp_tc {
 
-constexpr int NW = 8, NTHREADS = 32 * NW, NSTAGE = 3;
+constexpr int NSTAGE = 3;
 constexpr int TILE = C * F * 2;
 constexpr int ETA = C * C * 2;
 // Stage of one mini-batch, filled by TMA: XQ, XK, XV tiles (1024-byte aligned for the
@@ -39,16 +41,27 @@ constexpr int ETA = C * C * 2;
 constexpr int OFF_XQ = 0, OFF_XK = 1024 * ((TILE + 1023) / 1024), OFF_XV = 2 * OFF_XK, OFF_ETA = 3 * OFF_XK;
 constexpr int STAGE = 1024 * ((OFF_ETA + ETA + 1023) / 1024);
 constexpr uint32_t STAGE_BYTES = 3 * TILE + ETA;  // bytes the copies of one stage deliver
-constexpr int kCopyThread = NTHREADS - 32;          // lane 0 of the last warp issues and awaits the copies
-constexpr int PLD = F + 8;                              // fp32 row stride of the partial tiles
-constexpr int OFF_PART = NSTAGE * STAGE;                // fp32 [NW][C][PLD] per-warp partial sums
-constexpr int OFF_G = OFF_PART + NW * C * PLD * 4;      // 16-bit [C][F] swizzled: G2
-constexpr int OFF_EG = OFF_G + TILE;                    // 16-bit [C][F] swizzled: -e * G2
-constexpr int OFF_P = OFF_EG + TILE;                    // 16-bit [C][C]: -P1
-constexpr int OFF_B1 = OFF_P + ETA;                     // fp32 [FF]
-constexpr int OFF_B2 = OFF_B1 + FF * 4;                 // fp32 [2][F] (ping-pong)
-constexpr int SMEM = OFF_B2 + 2 * F * 4 + 1024;  // + slack to align the base to 1024 bytes
-constexpr uint32_t TMEM_COLS = 256;  // W1^T and W2^T slices of 8 warps: 2 x 128 columns
+constexpr int PLD = F + 8;                          // fp32 row stride of the partial tiles
+constexpr int OFF_PART = NSTAGE * STAGE;            // fp32 [NW][C][PLD] per-warp partial sums
+
+// Layout of a CTA of NW warps (inner width 32 * NW).
+template <int NW_>
+struct Fwd {
+  static constexpr int NW = NW_, NTHREADS = 32 * NW, FFW = 32 * NW;
+  static constexpr int kCopyThread = NTHREADS - 32;      // lane 0 of the last warp issues and awaits the copies
+  static constexpr int OFF_G = OFF_PART + NW * C * PLD * 4;  // 16-bit [C][F] swizzled: G2
+  static constexpr int OFF_EG = OFF_G + TILE;                // 16-bit [C][F] swizzled: -e * G2
+  static constexpr int OFF_P = OFF_EG + TILE;                // 16-bit [C][C]: -P1
+  static constexpr int OFF_B1 = OFF_P + ETA;                 // fp32 [FFW]
+  static constexpr int OFF_B2 = OFF_B1 + FFW * 4;            // fp32 [2][F] (ping-pong)
+  static constexpr int SMEM = OFF_B2 + 2 * F * 4 + 1024;     // + slack to align the base to 1024 bytes
+  // W1^T and W2^T slices: 128 columns per warp in its lane quadrant, two column blocks for 8 warps
+  static constexpr uint32_t TMEM_COLS = NW > 4 ? 256 : 128;
+  // CTAs per SM: two of 8 warps (registers), four of 2 warps (TMEM: 4 x 128 columns). The
+  // launch asks for enough shared memory that no more CTAs become resident than TMEM holds.
+  static constexpr int CTAS_PER_SM = NW > 4 ? 2 : 4;
+  static constexpr int SMEM_LAUNCH = NW > 4 ? SMEM : (SMEM > 56 * 1024 ? SMEM : 56 * 1024);
+};
 
 // One thread: TMA copies of mini-batch n's XQ, XK, XV tiles and eta tile into stage `st`,
 // completing on mbarrier `bar`.
@@ -62,7 +75,8 @@ __device__ __forceinline__ void issue_stage(uint32_t st, uint32_t bar, const Mlp
   bulk_load(st + OFF_ETA, (const uint8_t*)p.eta + (s * p.NC + n) * (long long)ETA, ETA, bar);
 }
 
-// Sum of the 8 warps' partial tiles for token tk, features 4q..4q+3.
+// Sum of the NW warps' partial tiles for token tk, features 4q..4q+3.
+template <int NW>
 __device__ __forceinline__ void sum_partials(const float* part, int tk, int q, float* z) {
   float4 acc = *reinterpret_cast<const float4*>(part + tk * PLD + 4 * q);
 #pragma unroll
@@ -79,11 +93,16 @@ __device__ __forceinline__ void sum_partials(const float* part, int tk, int q, f
   z[3] = acc.w;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(NTHREADS, 2)
+template <typename T, int NW>
+__global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
     mlp_fwd_tc_kernel(MlpFwdParams p, const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v) {
   using H = Half2<T>;
+  using L = Fwd<NW>;
+  constexpr int NTHREADS = L::NTHREADS, FFW = L::FFW, kCopyThread = L::kCopyThread;
+  constexpr int OFF_G = L::OFF_G, OFF_EG = L::OFF_EG, OFF_P = L::OFF_P, OFF_B1 = L::OFF_B1, OFF_B2 = L::OFF_B2;
+  constexpr uint32_t TMEM_COLS = L::TMEM_COLS;
+  constexpr int TPP = NTHREADS / 16;  // tokens per pass of the row phases
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   __shared__ uint32_t tmem_base_sh;
@@ -93,7 +112,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   const int mi = lane >> 3, r8 = lane & 7;
   const long long s = blockIdx.x;
   const int h = (int)(s % p.NH);
-  const int tk = tid >> 4, q = tid & 15;
+  const int tk0 = tid >> 4, q = tid & 15;
   const int fb = 32 * warp;
   float* part = reinterpret_cast<float*>(smem + OFF_PART);
   float* pw = part + warp * C * PLD;
@@ -124,12 +143,12 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   const uint32_t tS2 = tS1 + 64;
   {
     float S1[2][8][4], S2[4][4][4];
-    w1_io(S1, const_cast<float*>(p.W1_init + s * F * FF), fb, g, t, false);
-    w2_io(S2, const_cast<float*>(p.W2_init + s * FF * F), fb, g, t, false);
+    w1_io<2, FFW>(S1, const_cast<float*>(p.W1_init + s * F * FFW), fb, g, t, false);
+    w2_io(S2, const_cast<float*>(p.W2_init + s * FFW * F), fb, g, t, false);
     slice_st(tS1, &S1[0][0][0]);
     slice_st(tS2, &S2[0][0][0]);
   }
-  for (int i = tid; i < FF; i += NTHREADS) b1s[i] = p.b1_init[s * FF + i];
+  for (int i = tid; i < FFW; i += NTHREADS) b1s[i] = p.b1_init[s * FFW + i];
   for (int i = tid; i < F; i += NTHREADS) b2s[i] = p.b2_init[s * F + i];
   float gm[4], bt[4];
 #pragma unroll
@@ -165,10 +184,10 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       const long long k = s * p.K + n / p.ckpt;
       float S1[2][8][4], S2[4][4][4];
       slice_ld(tS1, &S1[0][0][0]);
-      w1_io(S1, p.W1_ckpt + k * F * FF, fb, g, t, true);
+      w1_io<2, FFW>(S1, p.W1_ckpt + k * F * FFW, fb, g, t, true);
       slice_ld(tS2, &S2[0][0][0]);
-      w2_io(S2, p.W2_ckpt + k * FF * F, fb, g, t, true);
-      for (int i = tid; i < FF; i += NTHREADS) p.b1_ckpt[k * FF + i] = b1s[i];
+      w2_io(S2, p.W2_ckpt + k * FFW * F, fb, g, t, true);
+      for (int i = tid; i < FFW; i += NTHREADS) p.b1_ckpt[k * FFW + i] = b1s[i];
       for (int i = tid; i < F; i += NTHREADS) p.b2_ckpt[k * F + i] = b2_old[i];
       ck_left = p.ckpt;
     }
@@ -226,9 +245,9 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         Zq[j][2] += bb.x;
         Zq[j][3] += bb.y;
         if (p.Z1_out) {
-          float* zo = p.Z1_out + (s * p.NC + n) * (long long)(C * FF) + fb + 8 * j + 2 * t;
-          *reinterpret_cast<float2*>(zo + g * FF) = z01;
-          *reinterpret_cast<float2*>(zo + (g + 8) * FF) = z23;
+          float* zo = p.Z1_out + (s * p.NC + n) * (long long)(C * FFW) + fb + 8 * j + 2 * t;
+          *reinterpret_cast<float2*>(zo + g * FFW) = z01;
+          *reinterpret_cast<float2*>(zo + (g + 8) * FFW) = z23;
         }
         float2 g01, g23, d01, d23;
         gelu2_and_bwd(z01, g01, d01);
@@ -261,9 +280,10 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     __syncthreads();
 
     // ---------------- C: Z2 = sum + b2, G2 = ln_fused_l2_bwd(Z2, XV - XK)
-    {
+#pragma unroll
+    for (int tk = tk0; tk < C; tk += TPP) {
       float z[4], xv[4], xk[4];
-      sum_partials(part, tk, q, z);
+      sum_partials<NW>(part, tk, q, z);
       const float4 bb = *reinterpret_cast<const float4*>(b2_old + 4 * q);
       z[0] += bb.x;
       z[1] += bb.y;
@@ -377,9 +397,9 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         const uint32_t b[2] = {ub[0][j], ub[1][j]};
         mma16816<T>(Zq[j], ap, b);
         if (p.Z1b_out) {
-          float* zo = p.Z1b_out + (s * p.NC + n) * (long long)(C * FF) + fb + 8 * j + 2 * t;
-          *reinterpret_cast<float2*>(zo + g * FF) = make_float2(Zq[j][0], Zq[j][1]);
-          *reinterpret_cast<float2*>(zo + (g + 8) * FF) = make_float2(Zq[j][2], Zq[j][3]);
+          float* zo = p.Z1b_out + (s * p.NC + n) * (long long)(C * FFW) + fb + 8 * j + 2 * t;
+          *reinterpret_cast<float2*>(zo + g * FFW) = make_float2(Zq[j][0], Zq[j][1]);
+          *reinterpret_cast<float2*>(zo + (g + 8) * FFW) = make_float2(Zq[j][2], Zq[j][3]);
         }
         const float2 g01 = gelu2(make_float2(Zq[j][0], Zq[j][1])), g23 = gelu2(make_float2(Zq[j][2], Zq[j][3]));
         XBp[j][0] = H::pack(g01.x, g01.y);
@@ -457,13 +477,14 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       }
       slice_st(tS2, &S2[0][0][0]);
     }
-    {  // b2_new = b2_old + 1^T (-e G2) (warp w: features 8w..8w+7)
+#pragma unroll
+    for (int fw = warp; fw < F / 8; fw += NW) {  // b2_new = b2_old + 1^T (-e G2), features 8fw..8fw+7
       uint32_t bg2[2];
-      ldsm_x2_t(bg2, egb + swz128((lane & 8) + r8, warp));
+      ldsm_x2_t(bg2, egb + swz128((lane & 8) + r8, fw));
       float db[4] = {0.f, 0.f, 0.f, 0.f};
       mma16816<T>(db, a_ones, bg2);
       if (g == 0) {
-        const int f = 8 * warp + 2 * t;
+        const int f = 8 * fw + 2 * t;
         b2_new[f] = b2_old[f] + db[0];
         b2_new[f + 1] = b2_old[f + 1] + db[1];
       }
@@ -471,9 +492,10 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     __syncthreads();
 
     // ---------------- E: XQW = XQ + LN(sum_w Z2bar_w + b2_old)
-    {
+#pragma unroll
+    for (int tk = tk0; tk < C; tk += TPP) {
       float z[4], xq[4];
-      sum_partials(part, tk, q, z);
+      sum_partials<NW>(part, tk, q, z);
       const float4 bb = *reinterpret_cast<const float4*>(b2_old + 4 * q);
       z[0] += bb.x;
       z[1] += bb.y;
@@ -502,10 +524,10 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       const long long m = s * p.NS + n / p.memo;
       float S1[2][8][4], S2[4][4][4];
       slice_ld(tS1, &S1[0][0][0]);
-      w1_io(S1, p.W1_memo + m * F * FF, fb, g, t, true);
+      w1_io<2, FFW>(S1, p.W1_memo + m * F * FFW, fb, g, t, true);
       slice_ld(tS2, &S2[0][0][0]);
-      w2_io(S2, p.W2_memo + m * FF * F, fb, g, t, true);
-      for (int i = tid; i < FF; i += NTHREADS) p.b1_memo[m * FF + i] = b1s[i];
+      w2_io(S2, p.W2_memo + m * FFW * F, fb, g, t, true);
+      for (int i = tid; i < FFW; i += NTHREADS) p.b1_memo[m * FFW + i] = b1s[i];
       for (int i = tid; i < F; i += NTHREADS) p.b2_memo[m * F + i] = b2_new[i];
       memo_left = p.memo;
     }
@@ -515,9 +537,9 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   {
     float S1[2][8][4], S2[4][4][4];
     slice_ld(tS1, &S1[0][0][0]);
-    w1_io(S1, p.W1_last + s * F * FF, fb, g, t, true);
+    w1_io<2, FFW>(S1, p.W1_last + s * F * FFW, fb, g, t, true);
     slice_ld(tS2, &S2[0][0][0]);
-    w2_io(S2, p.W2_last + s * FF * F, fb, g, t, true);
+    w2_io(S2, p.W2_last + s * FFW * F, fb, g, t, true);
   }
   // after a timeout, copies issued but never awaited may still be in flight: drain them
   // (bounded) before the CTA's shared memory goes away
@@ -525,7 +547,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     for (int m = last_issued - NSTAGE + 1; m <= last_issued; ++m)
       if (m >= 0) mbar_wait(smem_u32(&full_bar[m % NSTAGE]), (uint32_t)((m / NSTAGE) & 1), nullptr);
   const float* b2_fin = b2s + (p.NC & 1) * F;
-  for (int i = tid; i < FF; i += NTHREADS) p.b1_last[s * FF + i] = b1s[i];
+  for (int i = tid; i < FFW; i += NTHREADS) p.b1_last[s * FFW + i] = b1s[i];
   for (int i = tid; i < F; i += NTHREADS) p.b2_last[s * F + i] = b2_fin[i];
   // every warp's TMEM accesses are complete (slice_ld / slice_st wait); free the columns
   tmem_fence_before();
@@ -538,9 +560,19 @@ __global__ void __launch_bounds__(NTHREADS, 2)
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+template <typename T, int NW>
+static int launch_fwd(const MlpFwdParams& q, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                      cudaStream_t stream) {
+  using namespace mlp_tc;
+  int rc = prepare_smem(mlp_fwd_tc_kernel<T, NW>, Fwd<NW>::SMEM_LAUNCH, "ttt_mlp_fwd");
+  if (rc) return rc;
+  mlp_fwd_tc_kernel<T, NW><<<q.B * q.NH, Fwd<NW>::NTHREADS, Fwd<NW>::SMEM_LAUNCH, stream>>>(q, tq, tk, tv);
+  return check_launch("ttt_mlp_fwd");
+}
+
 int mlp_fwd_fast(const MlpFwdParams& p, cudaStream_t stream) {
   using namespace mlp_tc;
-  if (p.CS != C || p.F != F || p.FF != FF) return TTT_NOT_APPLICABLE;
+  if (p.CS != C || p.F != F || (p.FF != 256 && p.FF != 64)) return TTT_NOT_APPLICABLE;
   const int dt = p.dt_xq;
   if (dt != DT_BF16 && dt != DT_F16) return TTT_NOT_APPLICABLE;
   if (p.dt_xk != dt || p.dt_xv != dt || p.dt_eta != dt || p.dt_out != dt) return TTT_NOT_APPLICABLE;
@@ -555,16 +587,11 @@ int mlp_fwd_fast(const MlpFwdParams& p, cudaStream_t stream) {
   MlpFwdParams q = p;
   rc = device_error_word(&q.err, "ttt_mlp_fwd");
   if (rc) return rc;
-  if (dt == DT_BF16) {
-    rc = prepare_smem(mlp_fwd_tc_kernel<__nv_bfloat16>, SMEM, "ttt_mlp_fwd");
-    if (rc) return rc;
-    mlp_fwd_tc_kernel<__nv_bfloat16><<<p.B * p.NH, NTHREADS, SMEM, stream>>>(q, tq, tk, tv);
-  } else {
-    rc = prepare_smem(mlp_fwd_tc_kernel<__half>, SMEM, "ttt_mlp_fwd");
-    if (rc) return rc;
-    mlp_fwd_tc_kernel<__half><<<p.B * p.NH, NTHREADS, SMEM, stream>>>(q, tq, tk, tv);
-  }
-  return check_launch("ttt_mlp_fwd");
+  if (p.FF == 256)
+    return dt == DT_BF16 ? launch_fwd<__nv_bfloat16, 8>(q, tq, tk, tv, stream)
+                         : launch_fwd<__half, 8>(q, tq, tk, tv, stream);
+  return dt == DT_BF16 ? launch_fwd<__nv_bfloat16, 2>(q, tq, tk, tv, stream)
+                       : launch_fwd<__half, 2>(q, tq, tk, tv, stream);
 }
 
 }  // namespace ttt

@@ -41,11 +41,12 @@ class MemoMix(torch.autograd.Function):
 
 
 def fused_envelope(XQW_batch, W1_memo, memo_segment_size):
-    """True when the fused mixing kernels take these shapes: CS = 16, F = 64, FF = 256,
-    16-bit activations, at most 64 memo segments (ttt_memo_mix.cu)."""
+    """True when the fused mixing kernels take these shapes: CS = 16, F = 64, an inner width
+    of 256 or 64 (the layer's F x F MLP), 16-bit activations, at most 64 memo segments
+    (ttt_memo_mix.cu)."""
     B, NH, NC, CS, F = XQW_batch.shape
     NS = -(-NC // int(memo_segment_size))
-    return (CS == 16 and F == 64 and W1_memo.shape[-1] == 256 and NS <= 64
+    return (CS == 16 and F == 64 and W1_memo.shape[-1] in (256, 64) and NS <= 64
             and XQW_batch.dtype in (torch.bfloat16, torch.float16))
 
 
