@@ -551,12 +551,15 @@ def run_forecaster(args, w, rank, world, local_rank):
     launches = _lib.launch_count() - n0
     clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1)
-    # dominant kernel: the scan backward of one layer at the layer's per-rank shape
-    kern_ms, scan_flops = forecaster_scan_bwd_ms(w, b_rank, dev)
+    # dominant kernel (largest share of the step's launch list): one layer's memo-mixing
+    # backward at the per-rank shape
+    kern_ms, kern_flops = forecaster_memo_bwd_ms(w, b_rank, dev)
     # end to end: each step's windows copied from pinned host memory, loss read back
     host = [(x.pin_memory(), y.pin_memory()) for x, y in pool]
     xb, yb = torch.empty_like(dev_pool[0][0]), torch.empty_like(dev_pool[0][1])
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize()
+    barrier()  # every rank starts the end-to-end region together (the first all-reduce waits otherwise)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -574,7 +577,7 @@ def run_forecaster(args, w, rank, world, local_rank):
     ms_step = ms / args.steps
     tokens = w["B"] * w["NH"] * w["L"] * w["layers"]  # global, every layer's scan tokens
     hbm, bf16, bf16_sus, src = peaks()
-    achieved = scan_flops / (kern_ms / 1e3) / 1e12
+    achieved = kern_flops / (kern_ms / 1e3) / 1e12
     line = {
         "metric": METRIC, "value": tokens / (ms_step / 1e3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -587,8 +590,8 @@ def run_forecaster(args, w, rank, world, local_rank):
                    "samples_per_s": w["B"] / (ms_step / 1e3),
                    "l2": "activations larger than L2 (no flush)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
-                     "frac": achieved / bf16, "traffic": None, "peak_source": src, "kernel": "mlp_bwd (one layer)",
-                     "kernel_ms": kern_ms, "kernel_flops": scan_flops},
+                     "frac": achieved / bf16, "traffic": None, "peak_source": src,
+                     "kernel": "memo_mix backward (one layer)", "kernel_ms": kern_ms, "kernel_flops": kern_flops},
         "e2e": {"value": tokens / (e2e_ms / args.steps / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": (xb.numel() * xb.element_size() + yb.numel() * yb.element_size()),
                 "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms / args.steps},
@@ -601,29 +604,30 @@ def run_forecaster(args, w, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
-def forecaster_scan_bwd_ms(w, b_rank, dev):
-    """CUDA-event time of one layer's scan backward (the F x F inner MLP) at the per-rank
-    shape, and its useful FLOPs (the dual-form backward count of algorithmic())."""
+def forecaster_memo_bwd_ms(w, b_rank, dev):
+    """CUDA-event time of one layer's memo-mixing backward (F x F inner MLP, the layer's memo
+    segments) at the per-rank shape, and its useful FLOPs: every token of segment i reads out
+    the i earlier memo states, 2 * 2 * F * FF FLOPs each (algorithmic() of memo_mix_c3)."""
     import _core
     import synthetic as S
 
     NC = w["L"] // CS
-    d = S.make_mlp_inputs(b_rank, w["NH"], NC, CS, w["F"], w["FF"], dtype=torch.bfloat16, device=dev, seed=5,
-                          eta_mode="equal")
+    d = S.make_memo_inputs(b_rank, w["NH"], NC, CS, w["F"], w["FF"], w["memo"], dtype=torch.bfloat16, device=dev,
+                           seed=5)
     dO = S.make_upstream((b_rank, w["NH"], NC, CS, w["F"]), device=dev, seed=6, dtype=torch.bfloat16)
-    _, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"])
     stream = torch.cuda.current_stream(dev)
     tot = 0.0
     for _ in range(3):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
-                           saved=zs, W1_last=last[0], W2_last=last[2])
+        _core.memo_mix_backward(*(d[k] for k in MEMO), w["memo"], dO)
         e1.record(stream)
         torch.cuda.synchronize()
         tot += e0.elapsed_time(e1)
-    F, FF = w["F"], w["FF"]
-    flops = (38 * F * FF + 12 * CS * FF + 12 * CS * F) * b_rank * w["NH"] * w["L"]
+    M = w["memo"]
+    NS = -(-NC // M)
+    mean_i = sum(i * (min((i + 1) * M, NC) - i * M) for i in range(NS)) / NC
+    flops = mean_i * 4 * w["F"] * w["FF"] * b_rank * w["NH"] * w["L"]
     return tot / 3, flops
 
 
