@@ -132,6 +132,7 @@ struct MlpBwdParams {
 // Memo-state mixing (ttt_layer.py:503-559); activations [B,NH,NC,16,64] in one 16-bit type.
 struct MemoMixParams {
   int B, NH, NC, M, NS, TILES;  // M = memo_segment_size, NS = ceil(NC / M), TILES = 128-token tiles per segment
+  int P, NG;  // segments packed per tile (P > 1 when a segment has at most 64 tokens), tile groups per stream
   int dt_ln;
   const void* XQW;
   const void* XQ;

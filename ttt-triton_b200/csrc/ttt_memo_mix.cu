@@ -12,7 +12,10 @@
 //   memo_prep   one CTA per (stream, memo state j): 16-bit K-major copies of W1_j^T [FF][F]
 //               and W2_j^T [F][FF] (the tensor-core B operands) and summary_j.
 //   memo_mix    one CTA (8 warps) per (stream, segment, 128-token tile), heavy segments
-//               first. Per earlier state j (inner width FF = 256, or 64 for the layer's
+//               first; segments of at most 64 tokens are packed P = 128 / tokens to a
+//               tile (consecutive segments of one stream are consecutive tokens), which
+//               reads the union of their earlier states and masks each row to its own
+//               segment's. Per earlier state j (inner width FF = 256, or 64 for the layer's
 //               F x F inner MLP):
 //                 Z1 = XQ W1_j      128 x FF x 64 tcgen05.mma into tensor memory
 //                 X2 = gelu(Z1+b1)  all warps (more columns to warps 4-7 when FF = 256):
@@ -127,14 +130,26 @@ __global__ void __launch_bounds__(256) memo_prep_kernel(MemoMixParams p) {
 }
 
 // ---------------------------------------------------------------------------------- mix
-// blockIdx.x -> (stream, segment, tile) with the heaviest segments first.
-__device__ __forceinline__ void decode_block(const MemoMixParams& p, long long& s, int& seg, int& tile) {
-  const long long per_seg = (long long)p.B * p.NH * p.TILES;
+// blockIdx.x -> (stream, first and last segment of the tile, tile within the segment) with
+// the heaviest tiles first. Unpacked (P = 1): one segment, TILES tiles of it. Packed: group
+// 0 is segment 0 (passes through), group g >= 1 holds segments 1 + (g-1) P .. g P.
+__device__ __forceinline__ void decode_block(const MemoMixParams& p, long long& s, int& seg_first, int& seg_last,
+                                             int& tile) {
   const long long b = blockIdx.x;
-  seg = p.NS - 1 - (int)(b / per_seg);
-  const long long r = b % per_seg;
-  s = r / p.TILES;
-  tile = (int)(r % p.TILES);
+  if (p.P == 1) {
+    const long long per_seg = (long long)p.B * p.NH * p.TILES;
+    seg_first = seg_last = p.NS - 1 - (int)(b / per_seg);
+    const long long r = b % per_seg;
+    s = r / p.TILES;
+    tile = (int)(r % p.TILES);
+  } else {
+    const long long per_grp = (long long)p.B * p.NH;
+    const int g = p.NG - 1 - (int)(b / per_grp);
+    s = b % per_grp;
+    tile = 0;
+    seg_first = g == 0 ? 0 : 1 + (g - 1) * p.P;
+    seg_last = g == 0 ? 0 : min(g * p.P, p.NS - 1);
+  }
 }
 
 template <typename T, bool BWD, int FF>
@@ -151,18 +166,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   __shared__ int abort_sh;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   long long s;
-  int seg, tile;
-  decode_block(p, s, seg, tile);
-  const int n0 = seg * p.M, n1 = min((seg + 1) * p.M, p.NC);
-  const int seg_rows = (n1 - n0) * C;
-  const int row0 = tile * ROWS;  // first token of the tile within the segment
-  if (row0 >= seg_rows) return;  // empty tail tile (uniform over the CTA)
+  int seg_first, seg_last, tile;
+  decode_block(p, s, seg_first, seg_last, tile);
+  const int n0 = seg_first * p.M, n1 = min((seg_last + 1) * p.M, p.NC);
+  const int seg_rows = (n1 - n0) * C;  // tokens of the tile's segments
+  const int row0 = tile * ROWS;        // first token of the tile within them
+  if (row0 >= seg_rows) return;        // empty tail tile (uniform over the CTA)
   const long long tok0 = (s * p.NC + n0) * C + row0;  // global token index of row 0
   const int nrows = min(ROWS, seg_rows - row0);
+  const int seg_tok = p.M * C;         // tokens of every segment but a ragged last one
+  const int seg = seg_last;            // the tile reads memo states 0 .. seg_last - 1
   const T* XQW = reinterpret_cast<const T*>(p.XQW);
   const T* XU = reinterpret_cast<const T*>(p.XU);
 
-  if (seg == 0) {  // passes through (forward: out = XQW; backward: dXQW = dOut, dXU = 0)
+  if (seg_last == 0) {  // segment 0 passes through (forward: out = XQW; backward: dXQW = dOut, dXU = 0)
     const T* src = reinterpret_cast<const T*>(BWD ? p.dOut : p.XQW);
     T* dst = reinterpret_cast<T*>(BWD ? p.dXQW : p.out);
     for (int i = tid; i < nrows * F; i += NTHREADS) dst[tok0 * F + i] = src[tok0 * F + i];
@@ -245,8 +262,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     load_w1(0);
     load_w2(0);
   }
-  // mixing weights g_j(t), j = 0..seg (threads 0-127, one token each)
+  // mixing weights g_j(t), j = 0..seg_r (threads 0-127, one token each; seg_r is the row's
+  // own segment)
   const int r = tid;  // row of threads 0-127
+  const int seg_r = seg_first + (row0 + min(r, nrows - 1)) / seg_tok;
   if (tid < ROWS && r < nrows) {
     float xu[F];
 #pragma unroll
@@ -256,7 +275,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
       xu[c + 1] = v.y;
     }
     float mx = -INFINITY;
-    for (int j = 0; j <= seg; ++j) {
+    for (int j = 0; j <= seg_r; ++j) {
       const float* sm = p.summary + (s * p.NS + j) * F;
       float d = 0.f;
 #pragma unroll
@@ -265,13 +284,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
       mx = fmaxf(mx, d);
     }
     float tot = 0.f;
-    for (int j = 0; j <= seg; ++j) {
+    for (int j = 0; j <= seg_r; ++j) {
       const float e = __expf(G[r * GLD + j] - mx);
       G[r * GLD + j] = e;
       tot += e;
     }
     const float inv = 1.f / tot;
-    for (int j = 0; j <= seg; ++j) G[r * GLD + j] *= inv;
+    for (int j = 0; j <= seg_r; ++j) G[r * GLD + j] *= inv;
   }
   if (nstate > 0) load_bias(0);
   if (tid == 0) {
@@ -379,7 +398,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
       }
       const float rstd = 1.f / sqrtf(var * (1.f / F) + kReadoutEps);
       if (!BWD) {
-        const float gj = r < nrows ? G[r * GLD + j] : 0.f;
+        const float gj = r < nrows && j < seg_r ? G[r * GLD + j] : 0.f;  // states of the row's own segment only
 #pragma unroll
         for (int c = 0; c < F; ++c) acc[c] += gj * (xq[c] + LN[c] * z[c] * rstd + LN[F + c]);
       } else {
@@ -395,7 +414,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   // ---- tail (threads 0-127, one token each)
   if (tid < ROWS && r < nrows) {
     const long long o = (tok0 + r) * F;
-    const float gi = G[r * GLD + seg];
+    const float gi = G[r * GLD + seg_r];
     if (!BWD) {
       T* out = reinterpret_cast<T*>(p.out);
 #pragma unroll
@@ -410,13 +429,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
         const float2 w = H::unpack(*reinterpret_cast<const uint32_t*>(XQW + o + c));
         dgi += acc[c] * w.x + acc[c + 1] * w.y;
       }
-      DG[r * GLD + seg] = dgi;
+      DG[r * GLD + seg_r] = dgi;
       float sg = 0.f;
-      for (int k = 0; k <= seg; ++k) sg += G[r * GLD + k] * DG[r * GLD + k];
+      for (int k = 0; k <= seg_r; ++k) sg += G[r * GLD + k] * DG[r * GLD + k];
       float dxu[F];
 #pragma unroll
       for (int c = 0; c < F; ++c) dxu[c] = 0.f;
-      for (int k = 0; k <= seg; ++k) {
+      for (int k = 0; k <= seg_r; ++k) {
         const float ds = G[r * GLD + k] * (DG[r * GLD + k] - sg);
         DG[r * GLD + k] = ds;
         const float* sm = p.summary + (s * p.NS + k) * F;
@@ -433,11 +452,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     }
   }
   if (BWD) {
-    // d summary_seg += sum over this tile's tokens of ds_seg(t) XU_t  (X2 region as scratch)
+    // d summary_i += sum over the tile's tokens of segment i of ds_i(t) XU_t  (X2 region as
+    // scratch)
     __syncthreads();
     float* red = reinterpret_cast<float*>(smem + OFF_X2);  // [128][64]
     if (tid < ROWS) {
-      const float ds = r < nrows ? DG[r * GLD + seg] : 0.f;
+      const float ds = r < nrows ? DG[r * GLD + seg_r] : 0.f;
 #pragma unroll
       for (int c = 0; c < F; c += 2) {
         float2 v = make_float2(0.f, 0.f);
@@ -447,10 +467,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
       }
     }
     __syncthreads();
-    if (tid < F) {
+    // one (segment, feature) per thread: rows [lo, hi) of the tile belong to segment
+    // seg_first + sg
+    for (int e = tid; e < (seg_last - seg_first + 1) * F; e += NTHREADS) {
+      const int sg = e / F, f = e % F;
+      const int lo = max(0, sg * seg_tok - row0), hi = min(nrows, (sg + 1) * seg_tok - row0);
       float a = 0.f;
-      for (int i = 0; i < ROWS; ++i) a += red[i * F + tid];
-      atomicAdd(p.dsum + (s * p.NS + seg) * F + tid, a);
+      for (int i = lo; i < hi; ++i) a += red[i * F + f];
+      atomicAdd(p.dsum + (s * p.NS + seg_first + sg) * F + f, a);
     }
   }
   // a timed-out wait may leave products in flight: drain (bounded) before freeing memory
@@ -512,7 +536,7 @@ static int run(MemoMixParams p, bool bwd, cudaStream_t stream, const char* who) 
     cudaError_t e = cudaMemsetAsync(p.dsum, 0, (size_t)streams * p.NS * F * sizeof(float), stream);
     if (e != cudaSuccess) return fail(TTT_ERR_CUDA, "%s: %s", who, cudaGetErrorString(e));
   }
-  const unsigned grid = (unsigned)(streams * p.NS * p.TILES);
+  const unsigned grid = (unsigned)(p.P == 1 ? streams * p.NS * p.TILES : streams * p.NG);
   if (!bwd) {
     rc = prepare_smem(memo_mix_kernel<T, false, FF>, SMEM, who);
     if (rc) return rc;
@@ -547,6 +571,10 @@ static void fill_common(MemoMixParams& p, int B, int NH, int NC, int M) {
   p.M = M;
   p.NS = (NC + M - 1) / M;
   p.TILES = (M * C + ROWS - 1) / ROWS;
+  // segments of at most 64 tokens share 128-row tiles: group 0 is segment 0, the others
+  // hold P consecutive segments each
+  p.P = M * C <= ROWS / 2 ? ROWS / (M * C) : 1;
+  p.NG = p.P == 1 ? p.NS : 1 + (p.NS - 1 + p.P - 1) / p.P;
 }
 
 }  // namespace ttt
