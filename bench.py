@@ -264,74 +264,50 @@ def epilogue_step(w, d, dO, time_bwd_kernel=False):
     return None
 
 
-def api_step(w, host, dev_bufs, out_host):
-    """End-to-end step through the public API with host buffers: H2D copies of every
-    input, the reference-facing call (TritonLinear / TritonMLP .apply, plus backward),
-    D2H of the result. Returns (h2d_bytes, d2h_bytes)."""
+def api_compute(w, d):
+    """One step through the public API on device buffers d (the reference-facing call:
+    TritonLinear / TritonMLP .apply, mlp_memo_mix, ttt_prologue or post_norm_wo, plus the
+    backward for training workloads). Returns the device tensor the step reads back: the
+    output, or the gradient of RESULT_KEY / XQ for training workloads."""
     from linear_triton import TritonLinear
     from mlp_triton import TritonMLP
 
-    h2d = 0
-    for k, t in host.items():
-        dev_bufs[k].copy_(t, non_blocking=True)
-        h2d += t.numel() * t.element_size()
-    d = dev_bufs
+    def grad_of(leaves, key):
+        res = d[key].grad
+        for t in leaves:
+            t.grad = None
+            t.requires_grad_(False)
+        return res
+
     if w["kind"] == "prologue":
         from prologue import ttt_prologue
 
         leaves = [d[k].requires_grad_(True) for k in PRO]
         out = ttt_prologue(*leaves, (d["freqs_cos"], d["freqs_sin"]), CS, BASE_LR)
         torch.autograd.backward([out[k] for k in PRO_OUTS], [d["d_" + k] for k in PRO_OUTS])
-        res = d["hidden"].grad
-        for t in leaves:
-            t.grad = None
-            t.requires_grad_(False)
-        out_host.copy_(res.detach(), non_blocking=True)
-        return h2d, out_host.numel() * out_host.element_size()
+        return grad_of(leaves, "hidden")
     if w["kind"] == "epilogue":
         from epilogue import post_norm_wo
 
         leaves = [d[k].requires_grad_(True) for k in EPI]
-        out = post_norm_wo(*leaves, POST_NORM_EPS)
-        out.backward(d["dO"])
-        res = d["XQW"].grad
-        for t in leaves:
-            t.grad = None
-            t.requires_grad_(False)
-        out_host.copy_(res.detach(), non_blocking=True)
-        return h2d, out_host.numel() * out_host.element_size()
+        post_norm_wo(*leaves, POST_NORM_EPS).backward(d["dO"])
+        return grad_of(leaves, "XQW")
     if w["kind"] == "memo":
         from kernels.mlp_memo_mix import mlp_memo_mix
 
         leaves = [d[k].requires_grad_(k in ("XQW", "XU", "XK")) for k in MEMO]
-        out = mlp_memo_mix(*leaves, w["memo"])
-        out.backward(d["dO"])
-        res = d["XU"].grad
-        for t in leaves:
-            t.grad = None
-            t.requires_grad_(False)
-        out_host.copy_(res.detach(), non_blocking=True)
-        return h2d, out_host.numel() * out_host.element_size()
+        mlp_memo_mix(*leaves, w["memo"]).backward(d["dO"])
+        return grad_of(leaves, "XU")
     if w["kind"] == "linear":
-        leaves = [d[k] for k in LIN]
-        if w["bwd"]:
-            leaves = [t.requires_grad_(True) for t in leaves]
+        leaves = [d[k].requires_grad_(w["bwd"]) for k in LIN]
         out = TritonLinear.apply(*leaves, w["ckpt"])
     else:
-        leaves = [d[k] for k in MLP]
-        if w["bwd"]:
-            leaves = [t.requires_grad_(True) for t in leaves]
+        leaves = [d[k].requires_grad_(w["bwd"]) for k in MLP]
         out = TritonMLP.apply(*leaves, w["ckpt"], w["memo"] or w["ckpt"])[0]
     if w["bwd"]:
         out.backward(d["dO"])
-        res = d["XQ"].grad
-        for t in leaves:
-            t.grad = None
-            t.requires_grad_(False)
-    else:
-        res = out
-    out_host.copy_(res.detach(), non_blocking=True)
-    return h2d, out_host.numel() * out_host.element_size()
+        return grad_of(leaves, "XQ")
+    return out.detach()
 
 
 # --------------------------------------------------------------------------- clocks
@@ -792,24 +768,55 @@ def kernel_durations(w, d, dO, steps):
 
 
 def e2e_time(w, d, dO, dev, args):
+    """End-to-end steps through the public API with host buffers. Every step copies all of
+    its inputs from pinned host memory to the device, runs api_compute and reads its result
+    back to pinned host memory, all inside the timed region. Steps are pipelined as a data
+    loader would feed them: uploads on one stream, readbacks on another, two device buffer
+    sets, so step k+1's upload and step k-1's readback overlap step k's compute (a buffer
+    set is refilled only after the compute two steps back has finished with it). Returns
+    (ms for args.steps steps, H2D bytes per step, D2H bytes per step)."""
     host = {k: v.detach().cpu().pin_memory() for k, v in d.items()}
     if isinstance(dO, dict):
         host.update({"d_" + k: v.cpu().pin_memory() for k, v in dO.items()})
     elif dO is not None:
         host["dO"] = dO.cpu().pin_memory()
-    dev_bufs = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
-    res = d[RESULT_KEY.get(w["kind"], "XQ")]
-    out_host = torch.empty(res.shape, dtype=res.dtype).pin_memory()
-    for _ in range(max(1, min(args.warmup, 2))):
-        api_step(w, host, dev_bufs, out_host)
+    bufs = [{k: torch.empty_like(v, device=dev) for k, v in host.items()} for _ in range(2)]
+    res_like = d[RESULT_KEY.get(w["kind"], "XQ")]
+    out_host = [torch.empty(res_like.shape, dtype=res_like.dtype).pin_memory() for _ in range(2)]
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host[0].numel() * out_host[0].element_size()
+    comp = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def run(n):
+        loaded = [torch.cuda.Event(), torch.cuda.Event()]
+        done = [torch.cuda.Event(), torch.cuda.Event()]
+        up.wait_stream(comp)
+        down.wait_stream(comp)
+        for i in range(n):
+            b = i % 2
+            with torch.cuda.stream(up):
+                if i >= 2:
+                    up.wait_event(done[b])  # compute of step i - 2 is done with buffer set b
+                for k, t in host.items():
+                    bufs[b][k].copy_(t, non_blocking=True)
+                loaded[b].record(up)
+            comp.wait_event(loaded[b])
+            res = api_compute(w, bufs[b])
+            done[b].record(comp)
+            with torch.cuda.stream(down):
+                down.wait_event(done[b])
+                res.record_stream(down)  # keep the result allocated until its readback ran
+                out_host[b].copy_(res, non_blocking=True)
+        comp.wait_stream(up)
+        comp.wait_stream(down)
+
+    run(max(2, min(args.warmup, 2)))
     torch.cuda.synchronize()
-    stream = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    h2d = d2h = 0
-    for _ in range(args.steps):
-        h2d, d2h = api_step(w, host, dev_bufs, out_host)
-    e1.record(stream)
+    e0.record(comp)
+    run(args.steps)
+    e1.record(comp)
     torch.cuda.synchronize()
     return e0.elapsed_time(e1), h2d, d2h
 
