@@ -162,11 +162,13 @@ int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_gro
  * reference) as one launch sequence. XQW, XQ, XK, XU, out / dOut, dXQW, dXU, dXK are
  * [B, NH, NC, CS, F] contiguous in one 16-bit type (dt); memo states [B, NH, NS, ...] fp32 as
  * ttt_mlp_fwd writes them, NS = ceil(NC / memo_segment_size). Tensor-core path: CS = 16,
- * F = 64, FF = 256, NS <= 64. The backward gives dXQW, dXU and the summary part of dXK (the
- * cached read-outs and earlier summaries carry no gradient, as in the reference). Scratch:
- * ttt_memo_mix_scratch_bytes() bytes, 16-byte aligned.
+ * F = 64, FF = 256 or 64, NS <= 64. The backward gives dXQW, dXU and the summary part of dXK
+ * (the cached read-outs and earlier summaries carry no gradient, as in the reference).
+ * Scratch: ttt_memo_mix_scratch_bytes() bytes, 16-byte aligned; the forward leaves the
+ * memo states' 16-bit operand copies and the segment summaries in it, and a backward given
+ * that same scratch with scratch_prepped = 1 reuses them instead of preparing them again.
  */
-size_t ttt_memo_mix_scratch_bytes(int B, int NH, int NC, int memo_segment_size);
+size_t ttt_memo_mix_scratch_bytes(int B, int NH, int NC, int memo_segment_size, int FF);
 int ttt_memo_mix_fwd(int B, int NH, int NC, int CS, int F, int FF, int memo_segment_size,
                      const void* XQW, const void* XQ, const void* XK, const void* XU, int dt,
                      const float* W1_memo, const float* b1_memo, const float* W2_memo, const float* b2_memo,
@@ -177,7 +179,7 @@ int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, int memo_segm
                      const float* W1_memo, const float* b1_memo, const float* W2_memo, const float* b2_memo,
                      const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln,
                      const void* dOut, void* dXQW, void* dXU, void* dXK,
-                     void* scratch, size_t scratch_bytes, void* stream);
+                     void* scratch, size_t scratch_bytes, int scratch_prepped, void* stream);
 
 /*
  * Input prologue of the TTT layer, forward: everything TTTBase.process_input

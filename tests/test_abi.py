@@ -121,7 +121,8 @@ def test_memo_mix_host_checks():
     assert fwd(8, 2, scratch=None) == -1
     assert fwd(8, 2, nbytes=16) == -5
     # W1/W2 16-bit copies (2 * F * FF * 2 bytes) plus summary and its gradient (2 * F * 4) per memo state
-    assert _lib.lib.ttt_memo_mix_scratch_bytes(2, 3, 9, 4) == 2 * 3 * 3 * (2 * 64 * 256 * 2 + 2 * 64 * 4)
+    assert _lib.lib.ttt_memo_mix_scratch_bytes(2, 3, 9, 4, 256) == 2 * 3 * 3 * (2 * 64 * 256 * 2 + 2 * 64 * 4)
+    assert _lib.lib.ttt_memo_mix_scratch_bytes(2, 3, 9, 4, 64) == 2 * 3 * 3 * (2 * 64 * 64 * 2 + 2 * 64 * 4)
 
 
 def test_prologue_host_checks():

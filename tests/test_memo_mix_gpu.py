@@ -66,3 +66,18 @@ def test_memo_mix_rejects_unsupported_shapes_and_no_wait_gave_up():
     _lib.device_status()
     _core.memo_mix_forward(*(dev[k] for k in ORDER), 2)
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("FF", [256, 64])
+def test_backward_reuses_the_forward_scratch(FF):
+    """A backward given the forward's scratch (prepared operands and summaries) gives the
+    same gradients as one that prepares them itself."""
+    inp = make(2, 1, 9, 2, torch.bfloat16, seed=11, FF=FF)
+    dev = {k: v.to(DEV) for k, v in inp.items()}
+    dO = S.make_upstream((2, 1, 9, 16, 64), seed=12).to(DEV, torch.bfloat16)
+    out, scratch = _core.memo_mix_forward(*(dev[k] for k in ORDER), 2, return_scratch=True)
+    assert torch.equal(out, _core.memo_mix_forward(*(dev[k] for k in ORDER), 2))
+    fresh = _core.memo_mix_backward(*(dev[k] for k in ORDER), 2, dO)
+    reused = _core.memo_mix_backward(*(dev[k] for k in ORDER), 2, dO, scratch=scratch)
+    assert torch.equal(fresh[0], reused[0]) and torch.equal(fresh[1], reused[1])
+    assert torch.allclose(fresh[2].float(), reused[2].float(), rtol=1e-2, atol=1e-6)  # d summary atomics

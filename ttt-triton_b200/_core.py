@@ -310,15 +310,18 @@ def _memo_args(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, 
     return (B, NH, NC, CS, F, FF, M), (_c(XQW), _c(XQ), _c(XK), _c(XU)), mem, ln_w, ln_b
 
 
-def memo_mix_forward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, memo_segment_size):
+def memo_mix_forward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, memo_segment_size,
+                     return_scratch=False):
     """Memo-state mixing of the TTT-MLP output (ttt_layer.py:503-559) as one launch sequence.
-    Returns the mixed output in XQW's dtype and layout [B, NH, NC, CS, F]."""
+    Returns the mixed output in XQW's dtype and layout [B, NH, NC, CS, F]; with
+    return_scratch, also the scratch holding the prepared memo operands and summaries, which
+    memo_mix_backward reuses."""
     dims, acts, mem, ln_w, ln_b = _memo_args(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b,
                                              memo_segment_size)
     B, NH, NC, CS, F, FF, M = dims
     XQW, XQ, XK, XU = acts
     out = torch.empty_like(XQW)
-    nbytes = lib.ttt_memo_mix_scratch_bytes(B, NH, NC, M)
+    nbytes = lib.ttt_memo_mix_scratch_bytes(B, NH, NC, M, FF)
     scratch = torch.empty(max(nbytes, 1), device=XQW.device, dtype=torch.uint8)
     rc = lib.ttt_memo_mix_fwd(
         B, NH, NC, CS, F, FF, M, ptr(XQW), ptr(XQ), ptr(XK), ptr(XU), dtype_code(XQW),
@@ -326,12 +329,14 @@ def memo_mix_forward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, 
         ptr(out), ptr(scratch), nbytes, stream_of(XQW),
     )
     check(rc, "ttt_memo_mix_fwd")
-    return out
+    return (out, scratch) if return_scratch else out
 
 
-def memo_mix_backward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, memo_segment_size, dOut):
+def memo_mix_backward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, memo_segment_size, dOut,
+                      scratch=None):
     """Gradients of the memo mixing: (dXQW, dXU, dXK), dXK being the part through the
-    segment summaries (the cached read-outs carry none, ttt_layer.py:542)."""
+    segment summaries (the cached read-outs carry none, ttt_layer.py:542). `scratch` may be
+    the one memo_mix_forward returned for the same inputs (its prepared operands are reused)."""
     dims, acts, mem, ln_w, ln_b = _memo_args(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b,
                                              memo_segment_size)
     B, NH, NC, CS, F, FF, M = dims
@@ -340,12 +345,17 @@ def memo_mix_backward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w,
         raise ValueError(f"upstream gradient must have XQW's shape {tuple(XQW.shape)}, got {tuple(dOut.shape)}")
     dOut = _c(dOut.to(XQW.dtype))
     dXQW, dXU, dXK = torch.empty_like(XQW), torch.empty_like(XQW), torch.empty_like(XQW)
-    nbytes = lib.ttt_memo_mix_scratch_bytes(B, NH, NC, M)
-    scratch = torch.empty(max(nbytes, 1), device=XQW.device, dtype=torch.uint8)
+    nbytes = lib.ttt_memo_mix_scratch_bytes(B, NH, NC, M, FF)
+    prepped = scratch is not None
+    if prepped:
+        if scratch.numel() < nbytes or scratch.device != XQW.device:
+            raise ValueError("the forward's scratch does not match these inputs")
+    else:
+        scratch = torch.empty(max(nbytes, 1), device=XQW.device, dtype=torch.uint8)
     rc = lib.ttt_memo_mix_bwd(
         B, NH, NC, CS, F, FF, M, ptr(XQW), ptr(XQ), ptr(XK), ptr(XU), dtype_code(XQW),
         *[ptr(t) for t in mem], ptr(ln_w), ptr(ln_b), dtype_code(ln_w),
-        ptr(dOut), ptr(dXQW), ptr(dXU), ptr(dXK), ptr(scratch), nbytes, stream_of(XQW),
+        ptr(dOut), ptr(dXQW), ptr(dXU), ptr(dXK), ptr(scratch), nbytes, int(prepped), stream_of(XQW),
     )
     check(rc, "ttt_memo_mix_bwd")
     return dXQW, dXU, dXK

@@ -58,9 +58,9 @@ _SIGNATURES = {
         _I,
     ),
     "ttt_device_status": ([_P], _I),
-    "ttt_memo_mix_scratch_bytes": ([_I] * 4, _Z),
+    "ttt_memo_mix_scratch_bytes": ([_I] * 5, _Z),
     "ttt_memo_mix_fwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P, _P, _Z, _P], _I),
-    "ttt_memo_mix_bwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P] * 4 + [_P, _Z, _P], _I),
+    "ttt_memo_mix_bwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P] * 4 + [_P, _Z, _I, _P], _I),
     "ttt_prologue_fwd": ([_I] * 5 + [_P, _I, _L] + [_P] * 4 + [ctypes.c_float] + [_P] * 6, _I),
     "ttt_prologue_bwd": ([_I] * 5 + [_P, _I, _L] + [_P] * 4 + [ctypes.c_float] + [_P] * 10, _I),
     "ttt_post_norm_fwd": ([_I] * 4 + [_P, _I, _P, _P, ctypes.c_float, _P, _P], _I),

@@ -58,6 +58,13 @@ int make_map_2d(CUtensorMap* map, const void* base, int dtype_code, unsigned lon
                 const char* who) {
   EncodeTiledFn fn = encode_tiled(who);
   if (!fn) return TTT_ERR_CUDA;
+  // A driver-API call uses the calling thread's current context, which a thread that has
+  // made no runtime call yet (autograd's backward worker, say) does not have: bind the
+  // current device's primary context first (no synchronisation).
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return fail(TTT_ERR_CUDA, "%s: binding the device context: %s", who, cudaGetErrorString(e));
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {row_stride_bytes};
   const cuuint32_t box[2] = {box_cols, box_rows};

@@ -489,21 +489,31 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
 }
 
 // dXK of every token: d summary_i / (tokens of segment i) for i >= 1, zero in segment 0.
+// One thread writes 8 features of one token (a 16-byte store); mini-batch rows are indexed
+// as (stream, mini-batch) pairs so the only runtime divisions are 32-bit.
 template <typename T>
 __global__ void memo_dxk_kernel(MemoMixParams p) {
-  const long long total = (long long)p.B * p.NH * p.NC * C * F;
+  const int mbs = p.B * p.NH * p.NC;  // (stream, mini-batch) pairs
+  const long long total = (long long)mbs * C * (F / 8);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const long long tok = i / F;
-    const int f = (int)(i % F);
-    const long long s = tok / ((long long)p.NC * C);
-    const int n = (int)((tok / C) % p.NC);
+    const int mb = (int)(i / (C * (F / 8)));         // constant divisor
+    const int f0 = 8 * (int)(i % (F / 8));
+    const int s = mb / p.NC, n = mb - s * p.NC;
     const int seg = n / p.M;
-    float v = 0.f;
+    float v[8];
     if (seg > 0) {
-      const int cnt = (min((seg + 1) * p.M, p.NC) - seg * p.M) * C;
-      v = p.dsum[(s * p.NS + seg) * F + f] / (float)cnt;
+      const float inv = 1.f / (float)((min((seg + 1) * p.M, p.NC) - seg * p.M) * C);
+      const float4 a = *reinterpret_cast<const float4*>(p.dsum + ((long long)s * p.NS + seg) * F + f0);
+      const float4 b = *reinterpret_cast<const float4*>(p.dsum + ((long long)s * p.NS + seg) * F + f0 + 4);
+      v[0] = a.x * inv, v[1] = a.y * inv, v[2] = a.z * inv, v[3] = a.w * inv;
+      v[4] = b.x * inv, v[5] = b.y * inv, v[6] = b.z * inv, v[7] = b.w * inv;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.f;
     }
-    reinterpret_cast<T*>(p.dXK)[i] = Half2<T>::from_float(v);
+    using H = Half2<T>;
+    *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.dXK) + i * 8) =
+        make_uint4(H::pack(v[0], v[1]), H::pack(v[2], v[3]), H::pack(v[4], v[5]), H::pack(v[6], v[7]));
   }
 }
 
@@ -513,17 +523,23 @@ using namespace memo;
 
 static bool aligned16(const void* q) { return ((uintptr_t)q & 15) == 0; }
 
-// Scratch layout: W1^T and W2^T 16-bit copies (sized for the widest inner MLP), then
-// summary (and d summary) fp32.
-static size_t prep_bytes(long long B, long long NH, long long NS) { return (size_t)(B * NH * NS) * 2 * F * FF_MAX * 2; }
+// Scratch layout: W1^T and W2^T 16-bit copies, then summary (and d summary) fp32.
+static size_t prep_bytes(long long B, long long NH, long long NS, long long FF) {
+  return (size_t)(B * NH * NS) * 2 * F * FF * 2;
+}
 
+// prepped: the scratch already holds this call's W1^T / W2^T copies and summaries (the
+// forward wrote them), so the prep kernel is skipped.
 template <typename T, int FF>
-static int run(MemoMixParams p, bool bwd, cudaStream_t stream, const char* who) {
+static int run(MemoMixParams p, bool bwd, bool prepped, cudaStream_t stream, const char* who) {
   const long long streams = (long long)p.B * p.NH;
   constexpr int SMEM = Mix<FF>::SMEM;
-  memo_prep_kernel<T, FF><<<(unsigned)(streams * p.NS), 256, 0, stream>>>(p);
-  int rc = check_launch(who);
-  if (rc) return rc;
+  int rc = TTT_OK;
+  if (!prepped) {
+    memo_prep_kernel<T, FF><<<(unsigned)(streams * p.NS), 256, 0, stream>>>(p);
+    rc = check_launch(who);
+    if (rc) return rc;
+  }
   Maps maps;
   const int dt = std::is_same<T, __nv_bfloat16>::value ? DT_BF16 : DT_F16;
   rc = make_tile_map(&maps.xq, p.XQ, dt, (unsigned long long)streams * p.NC * C, who, ROWS);
@@ -581,10 +597,10 @@ static void fill_common(MemoMixParams& p, int B, int NH, int NC, int M) {
 
 using namespace ttt;
 
-extern "C" size_t ttt_memo_mix_scratch_bytes(int B, int NH, int NC, int memo_segment_size) {
-  if (B <= 0 || NH <= 0 || NC <= 0 || memo_segment_size <= 0) return 0;
+extern "C" size_t ttt_memo_mix_scratch_bytes(int B, int NH, int NC, int memo_segment_size, int FF) {
+  if (B <= 0 || NH <= 0 || NC <= 0 || memo_segment_size <= 0 || FF <= 0) return 0;
   const long long NS = (NC + memo_segment_size - 1) / memo_segment_size;
-  return prep_bytes(B, NH, NS) + (size_t)B * NH * NS * memo::F * sizeof(float) * 2;
+  return prep_bytes(B, NH, NS, FF) + (size_t)B * NH * NS * memo::F * sizeof(float) * 2;
 }
 
 extern "C" int ttt_memo_mix_fwd(int B, int NH, int NC, int CS, int F, int FF, int memo_segment_size, const void* XQW,
@@ -599,7 +615,7 @@ extern "C" int ttt_memo_mix_fwd(int B, int NH, int NC, int CS, int F, int FF, in
                   out && scratch,
               TTT_ERR_NULL, "%s: NULL pointer argument", who);
   TTT_REQUIRE(aligned16(XQ) && aligned16(scratch), TTT_ERR_ALIGN, "%s: XQ and scratch must be 16-byte aligned", who);
-  const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size);
+  const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size, FF);
   TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "%s: scratch has %zu bytes, needs %zu", who, scratch_bytes, need);
   MemoMixParams p = {};
   fill_common(p, B, NH, NC, memo_segment_size);
@@ -608,23 +624,24 @@ extern "C" int ttt_memo_mix_fwd(int B, int NH, int NC, int CS, int F, int FF, in
   p.ln_w = ttt_norm_weight; p.ln_b = ttt_norm_bias; p.dt_ln = dt_ln;
   p.out = out;
   uint8_t* sc = static_cast<uint8_t*>(scratch);
-  const size_t half = prep_bytes(B, NH, p.NS) / 2;
+  const size_t half = prep_bytes(B, NH, p.NS, FF) / 2;
   p.W1T = sc;
   p.W2T = sc + half;
   p.summary = reinterpret_cast<float*>(sc + 2 * half);
   p.dsum = p.summary + (size_t)B * NH * p.NS * memo::F;
   if (FF == 64)
-    return dt == DT_BF16 ? run<__nv_bfloat16, 64>(p, false, (cudaStream_t)stream, who)
-                         : run<__half, 64>(p, false, (cudaStream_t)stream, who);
-  return dt == DT_BF16 ? run<__nv_bfloat16, 256>(p, false, (cudaStream_t)stream, who)
-                       : run<__half, 256>(p, false, (cudaStream_t)stream, who);
+    return dt == DT_BF16 ? run<__nv_bfloat16, 64>(p, false, false, (cudaStream_t)stream, who)
+                         : run<__half, 64>(p, false, false, (cudaStream_t)stream, who);
+  return dt == DT_BF16 ? run<__nv_bfloat16, 256>(p, false, false, (cudaStream_t)stream, who)
+                       : run<__half, 256>(p, false, false, (cudaStream_t)stream, who);
 }
 
 extern "C" int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, int memo_segment_size, const void* XQW,
                                 const void* XQ, const void* XK, const void* XU, int dt, const float* W1_memo,
                                 const float* b1_memo, const float* W2_memo, const float* b2_memo,
                                 const void* ttt_norm_weight, const void* ttt_norm_bias, int dt_ln, const void* dOut,
-                                void* dXQW, void* dXU, void* dXK, void* scratch, size_t scratch_bytes, void* stream) {
+                                void* dXQW, void* dXU, void* dXK, void* scratch, size_t scratch_bytes,
+                                int scratch_prepped, void* stream) {
   const char* who = "ttt_memo_mix_bwd";
   int rc = check_mix(B, NH, NC, CS, F, FF, memo_segment_size, dt, dt_ln, who);
   if (rc) return rc;
@@ -632,7 +649,7 @@ extern "C" int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, in
                   dOut && dXQW && dXU && dXK && scratch,
               TTT_ERR_NULL, "%s: NULL pointer argument", who);
   TTT_REQUIRE(aligned16(XQ) && aligned16(scratch), TTT_ERR_ALIGN, "%s: XQ and scratch must be 16-byte aligned", who);
-  const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size);
+  const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size, FF);
   TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "%s: scratch has %zu bytes, needs %zu", who, scratch_bytes, need);
   MemoMixParams p = {};
   fill_common(p, B, NH, NC, memo_segment_size);
@@ -641,14 +658,15 @@ extern "C" int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, in
   p.ln_w = ttt_norm_weight; p.ln_b = ttt_norm_bias; p.dt_ln = dt_ln;
   p.dOut = dOut; p.dXQW = dXQW; p.dXU = dXU; p.dXK = dXK;
   uint8_t* sc = static_cast<uint8_t*>(scratch);
-  const size_t half = prep_bytes(B, NH, p.NS) / 2;
+  const size_t half = prep_bytes(B, NH, p.NS, FF) / 2;
   p.W1T = sc;
   p.W2T = sc + half;
   p.summary = reinterpret_cast<float*>(sc + 2 * half);
   p.dsum = p.summary + (size_t)B * NH * p.NS * memo::F;
+  const bool prepped = scratch_prepped != 0;
   if (FF == 64)
-    return dt == DT_BF16 ? run<__nv_bfloat16, 64>(p, true, (cudaStream_t)stream, who)
-                         : run<__half, 64>(p, true, (cudaStream_t)stream, who);
-  return dt == DT_BF16 ? run<__nv_bfloat16, 256>(p, true, (cudaStream_t)stream, who)
-                       : run<__half, 256>(p, true, (cudaStream_t)stream, who);
+    return dt == DT_BF16 ? run<__nv_bfloat16, 64>(p, true, prepped, (cudaStream_t)stream, who)
+                         : run<__half, 64>(p, true, prepped, (cudaStream_t)stream, who);
+  return dt == DT_BF16 ? run<__nv_bfloat16, 256>(p, true, prepped, (cudaStream_t)stream, who)
+                       : run<__half, 256>(p, true, prepped, (cudaStream_t)stream, who);
 }

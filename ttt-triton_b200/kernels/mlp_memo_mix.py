@@ -26,9 +26,10 @@ import _core
 class MemoMix(torch.autograd.Function):
     @staticmethod
     def forward(ctx, XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, memo_segment_size):
-        out = _core.memo_mix_forward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b,
-                                     memo_segment_size)
+        out, scratch = _core.memo_mix_forward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b,
+                                              memo_segment_size, return_scratch=True)
         ctx.memo_segment_size = int(memo_segment_size)
+        ctx.scratch = scratch  # prepared memo operands and summaries, reused by the backward
         ctx.save_for_backward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b)
         return out
 
@@ -36,7 +37,8 @@ class MemoMix(torch.autograd.Function):
     def backward(ctx, dOut):
         XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b = ctx.saved_tensors
         dXQW, dXU, dXK = _core.memo_mix_backward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b,
-                                                 ctx.memo_segment_size, dOut)
+                                                 ctx.memo_segment_size, dOut, scratch=ctx.scratch)
+        ctx.scratch = None
         return dXQW, None, dXK, dXU, None, None, None, None, None, None, None
 
 
