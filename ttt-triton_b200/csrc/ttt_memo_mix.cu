@@ -69,8 +69,9 @@ struct Mix {
   static constexpr uint32_t TMEM_COLS = FF == 256 ? 512 : 128;
   static constexpr uint32_t W1_BYTES = FF * F * 2, W2_BYTES = F * FF * 2;
   // GELU epilogue: 32-column chunks [0, SPLIT) on warps 0-3 (which also run the read-out
-  // LayerNorm), [SPLIT, FF / 32) on warps 4-7
-  static constexpr int CHUNKS = FF / 32, SPLIT = FF == 256 ? 3 : 1;
+  // LayerNorm), [SPLIT, FF / 32) on warps 4-7; with FF = 64 warps 4-7 take both chunks, so
+  // the GELU of state j + 1 runs beside the LayerNorm of state j
+  static constexpr int CHUNKS = FF / 32, SPLIT = FF == 256 ? 3 : 0;
   static_assert(OFF_W1 % 1024 == 0 && OFF_W2 % 1024 == 0 && OFF_X2 % 1024 == 0,
                 "swizzled tiles need 1024-byte alignment");
   static_assert(Z2_COL + F <= (int)TMEM_COLS, "tensor memory budget");
