@@ -53,12 +53,15 @@ constexpr uint32_t XQ_BYTES = ROWS * F * 2;
 // Shared memory (1024-byte aligned base) and tensor memory of a CTA for inner width FF.
 template <int FF>
 struct Mix {
-  static constexpr int OFF_W1 = OFF_XQ + ROWS * F * 2;   // [FF][64]: W1_j^T
-  static constexpr int OFF_W2 = OFF_W1 + FF * F * 2;     // FF/64 x [64][64]: W2_j^T, K chunks of 64
+  // memo-state weight buffers: two per operand for FF = 64 (fetched two states ahead), one for
+  // FF = 256 (whose 32 KB tiles do not fit twice)
+  static constexpr int NB = FF == 64 ? 2 : 1;
+  static constexpr int OFF_W1 = OFF_XQ + ROWS * F * 2;   // NB x [FF][64]: W1_j^T
+  static constexpr int OFF_W2 = OFF_W1 + NB * FF * F * 2;  // NB x FF/64 x [64][64]: W2_j^T, K chunks of 64
   // FF/64 x [128][64]: gelu(Z1 + b1), K chunks of 64; the backward's d-summary scratch
   // ([128][64] fp32) reuses it, so it is at least 32 KB
   static constexpr int X2_BYTES = ROWS * FF * 2 > ROWS * F * 4 ? ROWS * FF * 2 : ROWS * F * 4;
-  static constexpr int OFF_X2 = OFF_W2 + F * FF * 2;
+  static constexpr int OFF_X2 = OFF_W2 + NB * F * FF * 2;
   static constexpr int OFF_G = OFF_X2 + X2_BYTES;        // fp32 [128][GLD]: mixing weights g_j(t)
   static constexpr int OFF_DG = OFF_G + ROWS * GLD * 4;  // fp32 [128][GLD]: dg_j(t) (backward)
   static constexpr int OFF_LN = OFF_DG + ROWS * GLD * 4; // fp32 [2][64]: LayerNorm weight, bias
@@ -160,10 +163,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   constexpr int OFF_W1 = L::OFF_W1, OFF_W2 = L::OFF_W2, OFF_X2 = L::OFF_X2, OFF_G = L::OFF_G, OFF_DG = L::OFF_DG;
   constexpr int OFF_LN = L::OFF_LN, OFF_B1 = L::OFF_B1, OFF_B2 = L::OFF_B2;
   constexpr uint32_t TMEM_COLS = L::TMEM_COLS, W1_BYTES = L::W1_BYTES, W2_BYTES = L::W2_BYTES;
+  constexpr int NB = L::NB;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   __shared__ uint32_t tmem_base_sh;
-  __shared__ __align__(8) uint64_t bars[5];  // XQ, W1, W2 landed; product 1, product 2 complete
+  // XQ landed; product 1, product 2 complete; W1 buffer b, W2 buffer b landed
+  __shared__ __align__(8) uint64_t bars[3 + 2 * NB];
   __shared__ int abort_sh;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   long long s;
@@ -195,8 +200,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   float* DG = reinterpret_cast<float*>(smem + OFF_DG);
   float* LN = reinterpret_cast<float*>(smem + OFF_LN);
 
-  const uint32_t b_xq = smem_u32(&bars[0]), b_w1 = smem_u32(&bars[1]), b_w2 = smem_u32(&bars[2]);
-  const uint32_t b_p1 = smem_u32(&bars[3]), b_p2 = smem_u32(&bars[4]);
+  const uint32_t b_xq = smem_u32(&bars[0]), b_p1 = smem_u32(&bars[1]), b_p2 = smem_u32(&bars[2]);
+  auto b_w1 = [&](int j) { return smem_u32(&bars[3 + j % NB]); };       // barrier of state j's W1 buffer
+  auto b_w2 = [&](int j) { return smem_u32(&bars[3 + NB + j % NB]); };  // and of its W2 buffer
+  int last_w1[NB], last_w2[NB];  // (thread 0) last state loaded into each buffer, for draining
+#pragma unroll
+  for (int b = 0; b < NB; ++b) last_w1[b] = last_w2[b] = -1;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const uint32_t idesc1 = umma_idesc_f32(kBf16, ROWS, FF), idesc2 = umma_idesc_f32(kBf16, ROWS, F);
   const int h = (int)(s % p.NH);
@@ -207,7 +216,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     tmem_relinquish();
   }
   if (tid == 32) {
-    for (int i = 0; i < 5; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    for (int i = 0; i < 3 + 2 * NB; ++i) mbar_init(smem_u32(&bars[i]), 1);
     abort_sh = 0;
     fence_mbar_init();
   }
@@ -217,15 +226,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   tmem_fence_after();
   const uint32_t tZ1 = tmem_base_sh, tZ2 = tmem_base_sh + L::Z2_COL;
 
+  // state j's weights go to buffer j % NB
   auto load_w1 = [&](int j) {
-    mbar_expect_tx(b_w1, W1_BYTES);
-    tma_load_2d(sW1, &maps.w1, 0, (int)((s * p.NS + j) * FF), b_w1);
+    mbar_expect_tx(b_w1(j), W1_BYTES);
+    tma_load_2d(sW1 + (j % NB) * W1_BYTES, &maps.w1, 0, (int)((s * p.NS + j) * FF), b_w1(j));
+    last_w1[j % NB] = j;
   };
   auto load_w2 = [&](int j) {
-    mbar_expect_tx(b_w2, W2_BYTES);
+    const uint32_t dst = sW2 + (j % NB) * W2_BYTES;
+    mbar_expect_tx(b_w2(j), W2_BYTES);
 #pragma unroll
     for (int a = 0; a < FF / 64; ++a)
-      tma_load_2d(sW2 + a * (F * 64 * 2), &maps.w2, 64 * a, (int)((s * p.NS + j) * F), b_w2);
+      tma_load_2d(dst + a * (F * 64 * 2), &maps.w2, 64 * a, (int)((s * p.NS + j) * F), b_w2(j));
+    last_w2[j % NB] = j;
   };
   // Biases of state j into ring slot j % 3 (plain loads; the next CTA barrier publishes them).
   // A slot is rewritten two states after its last reader, which is past a barrier by then.
@@ -235,18 +248,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     for (int i = tid; i < FF; i += NTHREADS) b1s[i] = __ldg(p.b1_memo + (s * p.NS + j) * FF + i);
     if (tid < F) b2s[tid] = __ldg(p.b2_memo + (s * p.NS + j) * F + tid);
   };
-  auto product1 = [&]() {  // Z1 = XQ W1_j  (K = 64)
+  auto product1 = [&](int j) {  // Z1 = XQ W1_j  (K = 64)
     tmem_fence_after();
-    const uint64_t da = umma_desc_k_sw128(sXQ), db = umma_desc_k_sw128(sW1);
+    const uint64_t da = umma_desc_k_sw128(sXQ), db = umma_desc_k_sw128(sW1 + (j % NB) * W1_BYTES);
 #pragma unroll
     for (int k = 0; k < F / 16; ++k) umma_ss(tZ1, da + 2 * k, db + 2 * k, idesc1, k > 0);
     umma_commit(b_p1);
   };
-  auto product2 = [&]() {  // Z2 = X2 W2_j  (K = FF in 64-wide chunks)
+  auto product2 = [&](int j) {  // Z2 = X2 W2_j  (K = FF in 64-wide chunks)
     tmem_fence_after();
+    const uint32_t w2b = sW2 + (j % NB) * W2_BYTES;
 #pragma unroll
     for (int a = 0; a < FF / 64; ++a) {
-      const uint64_t da = umma_desc_k_sw128(sX2 + a * (ROWS * 64 * 2)), db = umma_desc_k_sw128(sW2 + a * (F * 64 * 2));
+      const uint64_t da = umma_desc_k_sw128(sX2 + a * (ROWS * 64 * 2)), db = umma_desc_k_sw128(w2b + a * (F * 64 * 2));
 #pragma unroll
       for (int k = 0; k < 4; ++k) umma_ss(tZ2, da + 2 * k, db + 2 * k, idesc2, (a | k) != 0);
     }
@@ -260,8 +274,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   if (tid == 0) {
     mbar_expect_tx(b_xq, XQ_BYTES);
     tma_load_2d(sXQ, &maps.xq, 0, (int)tok0, b_xq);
-    load_w1(0);
-    load_w2(0);
+    for (int j = 0; j < NB && j < nstate; ++j) {
+      load_w1(j);
+      load_w2(j);
+    }
   }
   // mixing weights g_j(t), j = 0..seg_r (threads 0-127, one token each; seg_r is the row's
   // own segment)
@@ -296,8 +312,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   if (nstate > 0) load_bias(0);
   if (tid == 0) {
     wait(b_xq, 0);
-    wait(b_w1, 0);
-    if (!abort_sh) product1();
+    wait(b_w1(0), 0);
+    if (!abort_sh) product1(0);
   }
   __syncthreads();  // mixing weights and state 0's biases written; the XQ tile is in shared memory
 
@@ -333,7 +349,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     if (lane == 0) wait(b_p1, j);
     __syncwarp();
     tmem_fence_after();
-    if (tid == 0 && j + 1 < nstate && !abort_sh) load_w1(j + 1);  // product 1 of j no longer reads W1
+    // product 1 of j no longer reads its W1 buffer: fetch state j + NB into it
+    if (tid == 0 && j + NB < nstate && !abort_sh) load_w1(j + NB);
     {
       // the 32-column chunks of a row: [0, SPLIT) for warps 0-3 (they also run the read-out
       // LayerNorm below), the rest for warps 4-7
@@ -366,11 +383,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     tmem_fence_before();
     __syncthreads();
     if (tid == 0 && !abort_sh) {
-      wait(b_w2, j);
-      if (!abort_sh) product2();
+      wait(b_w2(j), j / NB);
+      if (!abort_sh) product2(j);
       if (j + 1 < nstate) {
-        wait(b_w1, j + 1);
-        if (!abort_sh) product1();  // Z1 of j has been read by every warp
+        wait(b_w1(j + 1), (j + 1) / NB);
+        if (!abort_sh) product1(j + 1);  // Z1 of j has been read by every warp
       }
     }
     // ---- R_j = XQ + LN(Z2 + b2_j) (warps 0-3, one token per thread)
@@ -382,7 +399,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
       tmem_ld32(tmem_lane_addr(tZ2, warp, 0), z);
       tmem_ld32(tmem_lane_addr(tZ2, warp, 32), z + 32);
       tmem_wait_ld();
-      if (tid == 0 && j + 1 < nstate && !abort_sh) load_w2(j + 1);  // product 2 of j no longer reads W2
+      // product 2 of j no longer reads its W2 buffer: fetch state j + NB into it
+      if (tid == 0 && j + NB < nstate && !abort_sh) load_w2(j + NB);
       const float* b2 = reinterpret_cast<const float*>(smem + OFF_B2) + (j % 3) * F;
       float mu = 0.f;
 #pragma unroll
@@ -480,8 +498,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   }
   // a timed-out wait may leave products in flight: drain (bounded) before freeing memory
   if (tid == 0 && abort_sh) {
+    mbar_wait(b_xq, 0, nullptr);
     mbar_wait(b_p1, (uint32_t)((nstate - 1) & 1), nullptr);
     mbar_wait(b_p2, (uint32_t)((nstate - 1) & 1), nullptr);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {  // weight loads issued and never awaited
+      if (last_w1[b] >= 0) mbar_wait(b_w1(last_w1[b]), (uint32_t)((last_w1[b] / NB) & 1), nullptr);
+      if (last_w2[b] >= 0) mbar_wait(b_w2(last_w2[b]), (uint32_t)((last_w2[b] / NB) & 1), nullptr);
+    }
   }
   tmem_fence_before();
   __syncthreads();
