@@ -67,7 +67,12 @@ struct Mix {
   static constexpr int OFF_LN = OFF_DG + ROWS * GLD * 4; // fp32 [2][64]: LayerNorm weight, bias
   static constexpr int OFF_B1 = OFF_LN + 2 * F * 4;      // fp32 [3][FF]: b1_j ring (state j in slot j % 3)
   static constexpr int OFF_B2 = OFF_B1 + 3 * FF * 4;     // fp32 [3][64]: b2_j ring
-  static constexpr int SMEM = OFF_B2 + 3 * F * 4 + 1024; // + slack to align the base
+  // fp32 [NS_MAX][64]: the stream's segment summaries, staged once per CTA; for FF = 256 in
+  // the upper half of the X2 region (free before the first read-out and, reloaded, in the
+  // backward tail), for FF = 64 in a region of its own
+  static constexpr bool SUM_IN_X2 = FF == 256;
+  static constexpr int OFF_SUM = SUM_IN_X2 ? OFF_X2 + 32768 : OFF_B2 + 3 * F * 4;
+  static constexpr int SMEM = (SUM_IN_X2 ? OFF_B2 + 3 * F * 4 : OFF_SUM + NS_MAX * F * 4) + 1024;  // + alignment slack
   static constexpr int Z2_COL = FF == 256 ? 256 : FF;    // Z1: columns [0, FF), Z2: [Z2_COL, +64)
   static constexpr uint32_t TMEM_COLS = FF == 256 ? 512 : 128;
   static constexpr uint32_t W1_BYTES = FF * F * 2, W2_BYTES = F * FF * 2;
@@ -78,6 +83,8 @@ struct Mix {
   static_assert(OFF_W1 % 1024 == 0 && OFF_W2 % 1024 == 0 && OFF_X2 % 1024 == 0,
                 "swizzled tiles need 1024-byte alignment");
   static_assert(Z2_COL + F <= (int)TMEM_COLS, "tensor memory budget");
+  static_assert(!SUM_IN_X2 || X2_BYTES >= 32768 + NS_MAX * F * 4, "summaries share the X2 region");
+  static_assert(OFF_SUM % 16 == 0, "16-byte aligned summary rows");
 };
 
 struct Maps {
@@ -161,7 +168,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   using H = Half2<T>;
   using L = Mix<FF>;
   constexpr int OFF_W1 = L::OFF_W1, OFF_W2 = L::OFF_W2, OFF_X2 = L::OFF_X2, OFF_G = L::OFF_G, OFF_DG = L::OFF_DG;
-  constexpr int OFF_LN = L::OFF_LN, OFF_B1 = L::OFF_B1, OFF_B2 = L::OFF_B2;
+  constexpr int OFF_LN = L::OFF_LN, OFF_B1 = L::OFF_B1, OFF_B2 = L::OFF_B2, OFF_SUM = L::OFF_SUM;
   constexpr uint32_t TMEM_COLS = L::TMEM_COLS, W1_BYTES = L::W1_BYTES, W2_BYTES = L::W2_BYTES;
   constexpr int NB = L::NB;
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -242,11 +249,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   };
   // Biases of state j into ring slot j % 3 (plain loads; the next CTA barrier publishes them).
   // A slot is rewritten two states after its last reader, which is past a barrier by then.
-  auto load_bias = [&](int j) {
+  auto load_bias = [&](int j) {  // all threads, blocking (setup)
     float* b1s = reinterpret_cast<float*>(smem + OFF_B1) + (j % 3) * FF;
     float* b2s = reinterpret_cast<float*>(smem + OFF_B2) + (j % 3) * F;
     for (int i = tid; i < FF; i += NTHREADS) b1s[i] = __ldg(p.b1_memo + (s * p.NS + j) * FF + i);
     if (tid < F) b2s[tid] = __ldg(p.b2_memo + (s * p.NS + j) * F + tid);
+  };
+  // Warps 4-7 fetch state j's biases into registers (bias_fetch) and write them to ring slot
+  // j % 3 later (bias_put), so the global-load latency stays off the critical path. The slot
+  // of state j + 2 is written after the barrier of state j, when every reader of its previous
+  // occupant (state j - 1) is done; the barrier of state j + 1 publishes it.
+  float pb[3];  // b1[i], b1[i + 128], b2[i] of the fetched state, i = tid - 128
+  auto bias_fetch = [&](int j) {
+    const int i = tid - 128;
+    pb[0] = i < FF ? __ldg(p.b1_memo + (s * p.NS + j) * FF + i) : 0.f;
+    pb[1] = i + 128 < FF ? __ldg(p.b1_memo + (s * p.NS + j) * FF + i + 128) : 0.f;
+    pb[2] = i < F ? __ldg(p.b2_memo + (s * p.NS + j) * F + i) : 0.f;
+  };
+  auto bias_put = [&](int j) {
+    const int i = tid - 128;
+    float* b1s = reinterpret_cast<float*>(smem + OFF_B1) + (j % 3) * FF;
+    float* b2s = reinterpret_cast<float*>(smem + OFF_B2) + (j % 3) * F;
+    if (i < FF) b1s[i] = pb[0];
+    if (i + 128 < FF) b1s[i + 128] = pb[1];
+    if (i < F) b2s[i] = pb[2];
+  };
+  float* SUM = reinterpret_cast<float*>(smem + OFF_SUM);
+  // the stream's summaries 0..seg_last into shared memory (all threads, 16-byte copies)
+  auto stage_summaries = [&]() {
+    const float4* src = reinterpret_cast<const float4*>(p.summary + s * p.NS * F);
+    float4* dst = reinterpret_cast<float4*>(SUM);
+    for (int i = tid; i < (seg_last + 1) * (F / 4); i += NTHREADS) dst[i] = src[i];
   };
   auto product1 = [&](int j) {  // Z1 = XQ W1_j  (K = 64)
     tmem_fence_after();
@@ -279,6 +312,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
       load_w2(j);
     }
   }
+  // 16-bit row c..c+7 of a [.][F] tensor <-> 8 floats (16-byte accesses)
+  auto ld_row8 = [&](const T* src, float* x) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src);
+    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 v = H::unpack(w4[k]);
+      x[2 * k] = v.x;
+      x[2 * k + 1] = v.y;
+    }
+  };
+  auto st_row8 = [&](T* dst, const float* x) {
+    *reinterpret_cast<uint4*>(dst) =
+        make_uint4(H::pack(x[0], x[1]), H::pack(x[2], x[3]), H::pack(x[4], x[5]), H::pack(x[6], x[7]));
+  };
+  stage_summaries();
+  if (nstate > 0) load_bias(0);
+  if (nstate > 1) load_bias(1);
+  __syncthreads();  // summaries and the first two states' biases in shared memory
+
   // mixing weights g_j(t), j = 0..seg_r (threads 0-127, one token each; seg_r is the row's
   // own segment)
   const int r = tid;  // row of threads 0-127
@@ -286,17 +339,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   if (tid < ROWS && r < nrows) {
     float xu[F];
 #pragma unroll
-    for (int c = 0; c < F; c += 2) {
-      const float2 v = H::unpack(*reinterpret_cast<const uint32_t*>(XU + (tok0 + r) * F + c));
-      xu[c] = v.x;
-      xu[c + 1] = v.y;
-    }
+    for (int c = 0; c < F; c += 8) ld_row8(XU + (tok0 + r) * F + c, xu + c);
     float mx = -INFINITY;
     for (int j = 0; j <= seg_r; ++j) {
-      const float* sm = p.summary + (s * p.NS + j) * F;
+      const float4* sm = reinterpret_cast<const float4*>(SUM + j * F);
       float d = 0.f;
 #pragma unroll
-      for (int c = 0; c < F; ++c) d += xu[c] * __ldg(sm + c);
+      for (int c = 0; c < F / 4; ++c) {
+        const float4 v = sm[c];  // same address in every thread: a broadcast
+        d += xu[4 * c] * v.x + xu[4 * c + 1] * v.y + xu[4 * c + 2] * v.z + xu[4 * c + 3] * v.w;
+      }
       G[r * GLD + j] = d;
       mx = fmaxf(mx, d);
     }
@@ -309,13 +361,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     const float inv = 1.f / tot;
     for (int j = 0; j <= seg_r; ++j) G[r * GLD + j] *= inv;
   }
-  if (nstate > 0) load_bias(0);
   if (tid == 0) {
     wait(b_xq, 0);
     wait(b_w1(0), 0);
     if (!abort_sh) product1(0);
   }
-  __syncthreads();  // mixing weights and state 0's biases written; the XQ tile is in shared memory
+  __syncthreads();  // mixing weights written; the XQ tile is in shared memory
 
   float acc[F];   // forward: sum_j g_j R_j;  backward: dOut row
   float xq[F];    // XQ row
@@ -333,13 +384,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     }
     const T* dO = reinterpret_cast<const T*>(p.dOut);
 #pragma unroll
-    for (int c = 0; c < F; c += 2) {
+    for (int c = 0; c < F; c += 8) {
       if (BWD && r < nrows) {
-        const float2 v = H::unpack(*reinterpret_cast<const uint32_t*>(dO + (tok0 + r) * F + c));
-        acc[c] = v.x;
-        acc[c + 1] = v.y;
+        ld_row8(dO + (tok0 + r) * F + c, acc + c);
       } else {
-        acc[c] = acc[c + 1] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[c + e] = 0.f;
       }
     }
   }
@@ -351,6 +401,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     tmem_fence_after();
     // product 1 of j no longer reads its W1 buffer: fetch state j + NB into it
     if (tid == 0 && j + NB < nstate && !abort_sh) load_w1(j + NB);
+    if (warp >= 4 && j + 2 < nstate) bias_fetch(j + 2);
     {
       // the 32-column chunks of a row: [0, SPLIT) for warps 0-3 (they also run the read-out
       // LayerNorm below), the rest for warps 4-7
@@ -378,10 +429,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
               make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
       }
     }
-    if (j + 1 < nstate) load_bias(j + 1);
     fence_proxy_async();  // X2 stores -> visible to the tensor cores
     tmem_fence_before();
     __syncthreads();
+    if (warp >= 4 && j + 2 < nstate) bias_put(j + 2);
     if (tid == 0 && !abort_sh) {
       wait(b_w2(j), j / NB);
       if (!abort_sh) product2(j);
@@ -431,22 +482,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   }
 
   // ---- tail (threads 0-127, one token each)
+  if constexpr (BWD && L::SUM_IN_X2) {
+    // the read-outs overwrote the summaries' copy in the X2 region; every product is done
+    // (warps 0-3 waited for the last one before this barrier): stage them again
+    __syncthreads();
+    stage_summaries();
+    __syncthreads();
+  }
   if (tid < ROWS && r < nrows) {
     const long long o = (tok0 + r) * F;
     const float gi = G[r * GLD + seg_r];
     if (!BWD) {
       T* out = reinterpret_cast<T*>(p.out);
 #pragma unroll
-      for (int c = 0; c < F; c += 2) {
-        const float2 w = H::unpack(*reinterpret_cast<const uint32_t*>(XQW + o + c));
-        *reinterpret_cast<uint32_t*>(out + o + c) = H::pack(acc[c] + gi * w.x, acc[c + 1] + gi * w.y);
+      for (int c = 0; c < F; c += 8) {
+        float w[8], y[8];
+        ld_row8(XQW + o + c, w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = acc[c + e] + gi * w[e];
+        st_row8(out + o + c, y);
       }
     } else {
       float dgi = 0.f;
 #pragma unroll
-      for (int c = 0; c < F; c += 2) {
-        const float2 w = H::unpack(*reinterpret_cast<const uint32_t*>(XQW + o + c));
-        dgi += acc[c] * w.x + acc[c + 1] * w.y;
+      for (int c = 0; c < F; c += 8) {
+        float w[8];
+        ld_row8(XQW + o + c, w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dgi += acc[c + e] * w[e];
       }
       DG[r * GLD + seg_r] = dgi;
       float sg = 0.f;
@@ -457,16 +520,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
       for (int k = 0; k <= seg_r; ++k) {
         const float ds = G[r * GLD + k] * (DG[r * GLD + k] - sg);
         DG[r * GLD + k] = ds;
-        const float* sm = p.summary + (s * p.NS + k) * F;
+        const float4* sm = reinterpret_cast<const float4*>(SUM + k * F);
 #pragma unroll
-        for (int c = 0; c < F; ++c) dxu[c] += ds * __ldg(sm + c);
+        for (int c = 0; c < F / 4; ++c) {
+          const float4 v = sm[c];  // broadcast
+          dxu[4 * c] += ds * v.x;
+          dxu[4 * c + 1] += ds * v.y;
+          dxu[4 * c + 2] += ds * v.z;
+          dxu[4 * c + 3] += ds * v.w;
+        }
       }
       T* dXU = reinterpret_cast<T*>(p.dXU);
       T* dXQW = reinterpret_cast<T*>(p.dXQW);
 #pragma unroll
-      for (int c = 0; c < F; c += 2) {
-        *reinterpret_cast<uint32_t*>(dXU + o + c) = H::pack(dxu[c], dxu[c + 1]);
-        *reinterpret_cast<uint32_t*>(dXQW + o + c) = H::pack(gi * acc[c], gi * acc[c + 1]);
+      for (int c = 0; c < F; c += 8) {
+        float q8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q8[e] = gi * acc[c + e];
+        st_row8(dXU + o + c, dxu + c);
+        st_row8(dXQW + o + c, q8);
       }
     }
   }
@@ -639,9 +711,11 @@ extern "C" int ttt_memo_mix_fwd(int B, int NH, int NC, int CS, int F, int FF, in
   TTT_REQUIRE(XQW && XQ && XK && XU && W1_memo && b1_memo && W2_memo && b2_memo && ttt_norm_weight && ttt_norm_bias &&
                   out && scratch,
               TTT_ERR_NULL, "%s: NULL pointer argument", who);
-  TTT_REQUIRE(aligned16(XQ) && aligned16(scratch), TTT_ERR_ALIGN, "%s: XQ and scratch must be 16-byte aligned", who);
+  TTT_REQUIRE(aligned16(XQW) && aligned16(XQ) && aligned16(XK) && aligned16(XU) && aligned16(scratch), TTT_ERR_ALIGN,
+              "%s: activations and scratch must be 16-byte aligned", who);
   const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size, FF);
   TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "%s: scratch has %zu bytes, needs %zu", who, scratch_bytes, need);
+  TTT_REQUIRE(aligned16(out), TTT_ERR_ALIGN, "%s: out must be 16-byte aligned", who);
   MemoMixParams p = {};
   fill_common(p, B, NH, NC, memo_segment_size);
   p.XQW = XQW; p.XQ = XQ; p.XK = XK; p.XU = XU;
@@ -673,7 +747,8 @@ extern "C" int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, in
   TTT_REQUIRE(XQW && XQ && XK && XU && W1_memo && b1_memo && W2_memo && b2_memo && ttt_norm_weight && ttt_norm_bias &&
                   dOut && dXQW && dXU && dXK && scratch,
               TTT_ERR_NULL, "%s: NULL pointer argument", who);
-  TTT_REQUIRE(aligned16(XQ) && aligned16(scratch), TTT_ERR_ALIGN, "%s: XQ and scratch must be 16-byte aligned", who);
+  TTT_REQUIRE(aligned16(XQW) && aligned16(XQ) && aligned16(XK) && aligned16(XU) && aligned16(scratch), TTT_ERR_ALIGN,
+              "%s: activations and scratch must be 16-byte aligned", who);
   const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size, FF);
   TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "%s: scratch has %zu bytes, needs %zu", who, scratch_bytes, need);
   MemoMixParams p = {};
@@ -681,6 +756,8 @@ extern "C" int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, in
   p.XQW = XQW; p.XQ = XQ; p.XK = XK; p.XU = XU;
   p.W1_memo = W1_memo; p.b1_memo = b1_memo; p.W2_memo = W2_memo; p.b2_memo = b2_memo;
   p.ln_w = ttt_norm_weight; p.ln_b = ttt_norm_bias; p.dt_ln = dt_ln;
+  TTT_REQUIRE(aligned16(dOut) && aligned16(dXQW) && aligned16(dXU) && aligned16(dXK), TTT_ERR_ALIGN,
+              "%s: gradients must be 16-byte aligned", who);
   p.dOut = dOut; p.dXQW = dXQW; p.dXU = dXU; p.dXK = dXK;
   uint8_t* sc = static_cast<uint8_t*>(scratch);
   const size_t half = prep_bytes(B, NH, p.NS, FF) / 2;
