@@ -44,7 +44,7 @@
 namespace ttt {
 namespace memo {
 
-constexpr int F = 64, FF_MAX = 256, C = 16, ROWS = 128, NW = 8, NTHREADS = 32 * NW, NS_MAX = 64;
+constexpr int F = 64, C = 16, ROWS = 128, NS_MAX = 64;
 constexpr float kReadoutEps = 1e-6f;  // kernels/mlp_cached_readout.py:99
 constexpr int OFF_XQ = 0;             // [128][64] 16-bit, K-major 128-byte swizzle
 constexpr int GLD = NS_MAX + 1;       // row stride of the per-token tables (conflict-free)
@@ -53,15 +53,24 @@ constexpr uint32_t XQ_BYTES = ROWS * F * 2;
 // Shared memory (1024-byte aligned base) and tensor memory of a CTA for inner width FF.
 template <int FF>
 struct Mix {
-  // memo-state weight buffers: two per operand for FF = 64 (fetched two states ahead), one for
-  // FF = 256 (whose 32 KB tiles do not fit twice)
-  static constexpr int NB = FF == 64 ? 2 : 1;
-  static constexpr int OFF_W1 = OFF_XQ + ROWS * F * 2;   // NB x [FF][64]: W1_j^T
-  static constexpr int OFF_W2 = OFF_W1 + NB * FF * F * 2;  // NB x FF/64 x [64][64]: W2_j^T, K chunks of 64
-  // FF/64 x [128][64]: gelu(Z1 + b1), K chunks of 64; the backward's d-summary scratch
-  // ([128][64] fp32) reuses it, so it is at least 32 KB
-  static constexpr int X2_BYTES = ROWS * FF * 2 > ROWS * F * 4 ? ROWS * FF * 2 : ROWS * F * 4;
-  static constexpr int OFF_X2 = OFF_W2 + NB * F * FF * 2;
+  // FF = 64 runs warp-specialised (SPEC): warps 0-3 compute the GELU, warps 4-7 own one token
+  // each (mixing weights, read-out LayerNorm, tail) and warp 8 issues the products and the
+  // weight copies; the groups meet only through mbarriers. Z1, Z2 and X2 are double-buffered
+  // so product 1 runs two states ahead and product 2 of state j under the GELU of j + 1.
+  // FF = 256 keeps one schedule for 8 warps with a CTA barrier per state (its tiles do not
+  // fit twice): the GELU columns split [0, SPLIT) on warps 0-3, the rest on warps 4-7.
+  static constexpr bool SPEC = FF == 64;
+  static constexpr int NT = SPEC ? 288 : 256;         // threads
+  static constexpr int NX = SPEC ? 2 : 1;             // Z1 / Z2 / X2 buffers (state j in j % NX)
+  static constexpr int NB1 = SPEC ? 4 : 1, NB2 = SPEC ? 3 : 1;  // W1 / W2 buffers (fetch lead)
+  static constexpr int OFF_W1 = OFF_XQ + ROWS * F * 2;     // NB1 x [FF][64]: W1_j^T
+  static constexpr int OFF_W2 = OFF_W1 + NB1 * FF * F * 2; // NB2 x FF/64 x [64][64]: W2_j^T, K chunks of 64
+  // NX x FF/64 x [128][64]: gelu(Z1 + b1), K chunks of 64; the backward's d-summary scratch
+  // (fp32 [128][RED_LD], padded rows for conflict-free row-per-thread stores) reuses it
+  static constexpr int RED_LD = F + 1;
+  static constexpr int X2_BUF = ROWS * FF * 2;
+  static constexpr int X2_BYTES = NX * X2_BUF > ROWS * RED_LD * 4 ? NX * X2_BUF : ROWS * RED_LD * 4;
+  static constexpr int OFF_X2 = OFF_W2 + NB2 * F * FF * 2;
   static constexpr int OFF_G = OFF_X2 + X2_BYTES;        // fp32 [128][GLD]: mixing weights g_j(t)
   static constexpr int OFF_DG = OFF_G + ROWS * GLD * 4;  // fp32 [128][GLD]: dg_j(t) (backward)
   static constexpr int OFF_LN = OFF_DG + ROWS * GLD * 4; // fp32 [2][64]: LayerNorm weight, bias
@@ -71,19 +80,20 @@ struct Mix {
   // the upper half of the X2 region (free before the first read-out and, reloaded, in the
   // backward tail), for FF = 64 in a region of its own
   static constexpr bool SUM_IN_X2 = FF == 256;
-  static constexpr int OFF_SUM = SUM_IN_X2 ? OFF_X2 + 32768 : OFF_B2 + 3 * F * 4;
+  static constexpr int OFF_SUM = SUM_IN_X2 ? OFF_X2 + 36864 : OFF_B2 + 3 * F * 4;
   static constexpr int SMEM = (SUM_IN_X2 ? OFF_B2 + 3 * F * 4 : OFF_SUM + NS_MAX * F * 4) + 1024;  // + alignment slack
-  static constexpr int Z2_COL = FF == 256 ? 256 : FF;    // Z1: columns [0, FF), Z2: [Z2_COL, +64)
-  static constexpr uint32_t TMEM_COLS = FF == 256 ? 512 : 128;
+  // tensor memory: Z1 buffers at columns [0, NX * FF), Z2 buffers at [Z2_COL, + NX * 64)
+  static constexpr int Z2_COL = FF == 256 ? 256 : NX * FF;
+  static constexpr uint32_t TMEM_COLS = FF == 256 ? 512 : 256;
   static constexpr uint32_t W1_BYTES = FF * F * 2, W2_BYTES = F * FF * 2;
-  // GELU epilogue: 32-column chunks [0, SPLIT) on warps 0-3 (which also run the read-out
-  // LayerNorm), [SPLIT, FF / 32) on warps 4-7; with FF = 64 warps 4-7 take both chunks, so
-  // the GELU of state j + 1 runs beside the LayerNorm of state j
   static constexpr int CHUNKS = FF / 32, SPLIT = FF == 256 ? 3 : 0;
   static_assert(OFF_W1 % 1024 == 0 && OFF_W2 % 1024 == 0 && OFF_X2 % 1024 == 0,
                 "swizzled tiles need 1024-byte alignment");
-  static_assert(Z2_COL + F <= (int)TMEM_COLS, "tensor memory budget");
-  static_assert(!SUM_IN_X2 || X2_BYTES >= 32768 + NS_MAX * F * 4, "summaries share the X2 region");
+  static_assert(Z2_COL + NX * F <= (int)TMEM_COLS, "tensor memory budget");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(!SPEC || FF == 64, "the warp-specialised GELU covers 64 columns");
+  static_assert(!SUM_IN_X2 || X2_BYTES >= 36864 + NS_MAX * F * 4, "summaries share the X2 region");
+  static_assert(ROWS * RED_LD * 4 <= (SUM_IN_X2 ? 36864 : X2_BYTES), "d-summary scratch below the summaries");
   static_assert(OFF_SUM % 16 == 0, "16-byte aligned summary rows");
 };
 
@@ -143,7 +153,9 @@ __global__ void __launch_bounds__(256) memo_prep_kernel(MemoMixParams p) {
 // ---------------------------------------------------------------------------------- mix
 // blockIdx.x -> (stream, first and last segment of the tile, tile within the segment) with
 // the heaviest tiles first. Unpacked (P = 1): one segment, TILES tiles of it. Packed: group
-// 0 is segment 0 (passes through), group g >= 1 holds segments 1 + (g-1) P .. g P.
+// k holds segments NS-1 - kP - (P-1) .. NS-1 - kP, counted from the last segment, so the one
+// group that is not full (it ends at segment 0, which only passes through) is the one that
+// reads the fewest memo states.
 __device__ __forceinline__ void decode_block(const MemoMixParams& p, long long& s, int& seg_first, int& seg_last,
                                              int& tile) {
   const long long b = blockIdx.x;
@@ -155,27 +167,34 @@ __device__ __forceinline__ void decode_block(const MemoMixParams& p, long long& 
     tile = (int)(r % p.TILES);
   } else {
     const long long per_grp = (long long)p.B * p.NH;
-    const int g = p.NG - 1 - (int)(b / per_grp);
+    const int k = (int)(b / per_grp);
     s = b % per_grp;
     tile = 0;
-    seg_first = g == 0 ? 0 : 1 + (g - 1) * p.P;
-    seg_last = g == 0 ? 0 : min(g * p.P, p.NS - 1);
+    seg_last = p.NS - 1 - k * p.P;
+    seg_first = max(0, seg_last - p.P + 1);
   }
 }
 
 template <typename T, bool BWD, int FF>
-__global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, const __grid_constant__ Maps maps) {
+__global__ void __launch_bounds__(Mix<FF>::NT, 1) memo_mix_kernel(MemoMixParams p, const __grid_constant__ Maps maps) {
   using H = Half2<T>;
   using L = Mix<FF>;
   constexpr int OFF_W1 = L::OFF_W1, OFF_W2 = L::OFF_W2, OFF_X2 = L::OFF_X2, OFF_G = L::OFF_G, OFF_DG = L::OFF_DG;
   constexpr int OFF_LN = L::OFF_LN, OFF_B1 = L::OFF_B1, OFF_B2 = L::OFF_B2, OFF_SUM = L::OFF_SUM;
   constexpr uint32_t TMEM_COLS = L::TMEM_COLS, W1_BYTES = L::W1_BYTES, W2_BYTES = L::W2_BYTES;
-  constexpr int NB = L::NB;
+  constexpr int NB1 = L::NB1, NB2 = L::NB2, NX = L::NX, NT = L::NT;
+  constexpr bool kSpecialised = L::SPEC;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   __shared__ uint32_t tmem_base_sh;
-  // XQ landed; product 1, product 2 complete; W1 buffer b, W2 buffer b landed
-  __shared__ __align__(8) uint64_t bars[3 + 2 * NB];
+  // mbarriers: XQ landed; product 1 / product 2 into buffer b complete; W1 / W2 buffer b
+  // landed; (warp-specialised) Z2 buffer b read out by the four row warps, X2 buffer b written
+  // and Z1 buffer b read by the four GELU warps
+  constexpr int BAR_XQ = 0, BAR_P1 = 1, BAR_P2 = BAR_P1 + NX, BAR_W1 = BAR_P2 + NX, BAR_W2 = BAR_W1 + NB1;
+  constexpr int BAR_ZF = BAR_W2 + NB2, BAR_GD = BAR_ZF + NX, NBARS = BAR_GD + NX;
+  __shared__ __align__(8) uint64_t bars[NBARS];
+  __shared__ int last_w1_sh[NB1], last_w2_sh[NB2];  // last state loaded into each buffer (draining)
+  __shared__ int commits_sh[2][NX];                 // product 1 / 2 commits per buffer (draining)
   __shared__ int abort_sh;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   long long s;
@@ -195,9 +214,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   if (seg_last == 0) {  // segment 0 passes through (forward: out = XQW; backward: dXQW = dOut, dXU = 0)
     const T* src = reinterpret_cast<const T*>(BWD ? p.dOut : p.XQW);
     T* dst = reinterpret_cast<T*>(BWD ? p.dXQW : p.out);
-    for (int i = tid; i < nrows * F; i += NTHREADS) dst[tok0 * F + i] = src[tok0 * F + i];
+    for (int i = tid; i < nrows * F; i += NT) dst[tok0 * F + i] = src[tok0 * F + i];
     if (BWD)
-      for (int i = tid; i < nrows * F; i += NTHREADS) reinterpret_cast<T*>(p.dXU)[tok0 * F + i] = H::from_float(0.f);
+      for (int i = tid; i < nrows * F; i += NT) reinterpret_cast<T*>(p.dXU)[tok0 * F + i] = H::from_float(0.f);
     return;
   }
 
@@ -207,12 +226,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   float* DG = reinterpret_cast<float*>(smem + OFF_DG);
   float* LN = reinterpret_cast<float*>(smem + OFF_LN);
 
-  const uint32_t b_xq = smem_u32(&bars[0]), b_p1 = smem_u32(&bars[1]), b_p2 = smem_u32(&bars[2]);
-  auto b_w1 = [&](int j) { return smem_u32(&bars[3 + j % NB]); };       // barrier of state j's W1 buffer
-  auto b_w2 = [&](int j) { return smem_u32(&bars[3 + NB + j % NB]); };  // and of its W2 buffer
-  int last_w1[NB], last_w2[NB];  // (thread 0) last state loaded into each buffer, for draining
-#pragma unroll
-  for (int b = 0; b < NB; ++b) last_w1[b] = last_w2[b] = -1;
+  // barrier of state j's buffer (the phase of state j is j / NX, j / NB1, j / NB2)
+  const uint32_t b_xq = smem_u32(&bars[BAR_XQ]);
+  auto b_p1 = [&](int j) { return smem_u32(&bars[BAR_P1 + j % NX]); };
+  auto b_p2 = [&](int j) { return smem_u32(&bars[BAR_P2 + j % NX]); };
+  auto b_w1 = [&](int j) { return smem_u32(&bars[BAR_W1 + j % NB1]); };
+  auto b_w2 = [&](int j) { return smem_u32(&bars[BAR_W2 + j % NB2]); };
+  auto b_zf = [&](int j) { return smem_u32(&bars[BAR_ZF + j % NX]); };
+  auto b_gd = [&](int j) { return smem_u32(&bars[BAR_GD + j % NX]); };
+  // Thread groups. Row threads own one token each (mixing weights, read-out, tail). In the
+  // warp-specialised schedule the GELU group takes warps 0-3, which the warp schedulers favour:
+  // the GELU is on the chain of dependent products, the read-out is not. The b1 ring is filled
+  // by the 128 threads from GELU_T0.
+  constexpr int ROW_T0 = kSpecialised ? 128 : 0, GELU_T0 = 128 - ROW_T0;
+  constexpr int kIssuer = kSpecialised ? 256 : 0;  // thread that issues the products
+  const bool row_thread = (unsigned)(tid - ROW_T0) < (unsigned)ROWS;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const uint32_t idesc1 = umma_idesc_f32(kBf16, ROWS, FF), idesc2 = umma_idesc_f32(kBf16, ROWS, F);
   const int h = (int)(s % p.NH);
@@ -223,7 +251,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     tmem_relinquish();
   }
   if (tid == 32) {
-    for (int i = 0; i < 3 + 2 * NB; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    for (int i = 0; i < NBARS; ++i) mbar_init(smem_u32(&bars[i]), i >= BAR_ZF ? 4 : 1);  // ZF, GD: one arrival per warp
+    for (int b = 0; b < NB1; ++b) last_w1_sh[b] = -1;
+    for (int b = 0; b < NB2; ++b) last_w2_sh[b] = -1;
+    for (int b = 0; b < NX; ++b) commits_sh[0][b] = commits_sh[1][b] = 0;
     abort_sh = 0;
     fence_mbar_init();
   }
@@ -233,71 +264,76 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   tmem_fence_after();
   const uint32_t tZ1 = tmem_base_sh, tZ2 = tmem_base_sh + L::Z2_COL;
 
-  // state j's weights go to buffer j % NB
+  // state j's weights go to buffers j % NB1 and j % NB2
   auto load_w1 = [&](int j) {
     mbar_expect_tx(b_w1(j), W1_BYTES);
-    tma_load_2d(sW1 + (j % NB) * W1_BYTES, &maps.w1, 0, (int)((s * p.NS + j) * FF), b_w1(j));
-    last_w1[j % NB] = j;
+    tma_load_2d(sW1 + (j % NB1) * W1_BYTES, &maps.w1, 0, (int)((s * p.NS + j) * FF), b_w1(j));
+    last_w1_sh[j % NB1] = j;
   };
   auto load_w2 = [&](int j) {
-    const uint32_t dst = sW2 + (j % NB) * W2_BYTES;
+    const uint32_t dst = sW2 + (j % NB2) * W2_BYTES;
     mbar_expect_tx(b_w2(j), W2_BYTES);
 #pragma unroll
     for (int a = 0; a < FF / 64; ++a)
       tma_load_2d(dst + a * (F * 64 * 2), &maps.w2, 64 * a, (int)((s * p.NS + j) * F), b_w2(j));
-    last_w2[j % NB] = j;
+    last_w2_sh[j % NB2] = j;
   };
-  // Biases of state j into ring slot j % 3 (plain loads; the next CTA barrier publishes them).
-  // A slot is rewritten two states after its last reader, which is past a barrier by then.
+  // Biases of state j into ring slot j % 3 (plain loads; a barrier publishes them).
   auto load_bias = [&](int j) {  // all threads, blocking (setup)
     float* b1s = reinterpret_cast<float*>(smem + OFF_B1) + (j % 3) * FF;
     float* b2s = reinterpret_cast<float*>(smem + OFF_B2) + (j % 3) * F;
-    for (int i = tid; i < FF; i += NTHREADS) b1s[i] = __ldg(p.b1_memo + (s * p.NS + j) * FF + i);
+    for (int i = tid; i < FF; i += NT) b1s[i] = __ldg(p.b1_memo + (s * p.NS + j) * FF + i);
     if (tid < F) b2s[tid] = __ldg(p.b2_memo + (s * p.NS + j) * F + tid);
   };
-  // Warps 4-7 fetch state j's biases into registers (bias_fetch) and write them to ring slot
-  // j % 3 later (bias_put), so the global-load latency stays off the critical path. The slot
-  // of state j + 2 is written after the barrier of state j, when every reader of its previous
-  // occupant (state j - 1) is done; the barrier of state j + 1 publishes it.
-  float pb[3];  // b1[i], b1[i + 128], b2[i] of the fetched state, i = tid - 128
-  auto bias_fetch = [&](int j) {
-    const int i = tid - 128;
+  // From state 2 on the biases are fetched into registers two states ahead (*_fetch) and
+  // written to their ring slot later (*_put), so the global-load latency stays off the
+  // critical path. Slot (j + 2) % 3 is written after the barrier that ends state j, when
+  // every reader of its previous occupant (state j - 1) is done; the barrier of state j + 1
+  // publishes it. b1 is read by the GELU warps only; b2 by the read-out warps (which own its
+  // ring in the warp-specialised schedule). i = this thread's index within its warp group.
+  float pb[3];  // b1[i], b1[i + 128], b2[i] of the fetched state
+  auto b1_fetch = [&](int j, int i) {
     pb[0] = i < FF ? __ldg(p.b1_memo + (s * p.NS + j) * FF + i) : 0.f;
     pb[1] = i + 128 < FF ? __ldg(p.b1_memo + (s * p.NS + j) * FF + i + 128) : 0.f;
-    pb[2] = i < F ? __ldg(p.b2_memo + (s * p.NS + j) * F + i) : 0.f;
   };
-  auto bias_put = [&](int j) {
-    const int i = tid - 128;
+  auto b1_put = [&](int j, int i) {
     float* b1s = reinterpret_cast<float*>(smem + OFF_B1) + (j % 3) * FF;
-    float* b2s = reinterpret_cast<float*>(smem + OFF_B2) + (j % 3) * F;
     if (i < FF) b1s[i] = pb[0];
     if (i + 128 < FF) b1s[i + 128] = pb[1];
-    if (i < F) b2s[i] = pb[2];
+  };
+  auto b2_fetch = [&](int j, int i) { pb[2] = i < F ? __ldg(p.b2_memo + (s * p.NS + j) * F + i) : 0.f; };
+  auto b2_put = [&](int j, int i) {
+    if (i < F) reinterpret_cast<float*>(smem + OFF_B2)[(j % 3) * F + i] = pb[2];
   };
   float* SUM = reinterpret_cast<float*>(smem + OFF_SUM);
   // the stream's summaries 0..seg_last into shared memory (all threads, 16-byte copies)
   auto stage_summaries = [&]() {
     const float4* src = reinterpret_cast<const float4*>(p.summary + s * p.NS * F);
     float4* dst = reinterpret_cast<float4*>(SUM);
-    for (int i = tid; i < (seg_last + 1) * (F / 4); i += NTHREADS) dst[i] = src[i];
+    for (int i = tid; i < (seg_last + 1) * (F / 4); i += NT) dst[i] = src[i];
   };
+  // products of state j (issuer thread): into tensor-memory buffer j % NX, committed to that
+  // buffer's barrier
   auto product1 = [&](int j) {  // Z1 = XQ W1_j  (K = 64)
     tmem_fence_after();
-    const uint64_t da = umma_desc_k_sw128(sXQ), db = umma_desc_k_sw128(sW1 + (j % NB) * W1_BYTES);
+    const uint32_t d = tZ1 + (j % NX) * FF;
+    const uint64_t da = umma_desc_k_sw128(sXQ), db = umma_desc_k_sw128(sW1 + (j % NB1) * W1_BYTES);
 #pragma unroll
-    for (int k = 0; k < F / 16; ++k) umma_ss(tZ1, da + 2 * k, db + 2 * k, idesc1, k > 0);
-    umma_commit(b_p1);
+    for (int k = 0; k < F / 16; ++k) umma_ss(d, da + 2 * k, db + 2 * k, idesc1, k > 0);
+    umma_commit(b_p1(j));
+    ++commits_sh[0][j % NX];
   };
   auto product2 = [&](int j) {  // Z2 = X2 W2_j  (K = FF in 64-wide chunks)
     tmem_fence_after();
-    const uint32_t w2b = sW2 + (j % NB) * W2_BYTES;
+    const uint32_t d = tZ2 + (j % NX) * F, x2b = sX2 + (j % NX) * L::X2_BUF, w2b = sW2 + (j % NB2) * W2_BYTES;
 #pragma unroll
     for (int a = 0; a < FF / 64; ++a) {
-      const uint64_t da = umma_desc_k_sw128(sX2 + a * (ROWS * 64 * 2)), db = umma_desc_k_sw128(w2b + a * (F * 64 * 2));
+      const uint64_t da = umma_desc_k_sw128(x2b + a * (ROWS * 64 * 2)), db = umma_desc_k_sw128(w2b + a * (F * 64 * 2));
 #pragma unroll
-      for (int k = 0; k < 4; ++k) umma_ss(tZ2, da + 2 * k, db + 2 * k, idesc2, (a | k) != 0);
+      for (int k = 0; k < 4; ++k) umma_ss(d, da + 2 * k, db + 2 * k, idesc2, (a | k) != 0);
     }
-    umma_commit(b_p2);
+    umma_commit(b_p2(j));
+    ++commits_sh[1][j % NX];
   };
   auto wait = [&](uint32_t bar, int phase) {
     if (!abort_sh && !mbar_wait(bar, (uint32_t)(phase & 1), p.err)) abort_sh = 1;
@@ -307,10 +343,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
   if (tid == 0) {
     mbar_expect_tx(b_xq, XQ_BYTES);
     tma_load_2d(sXQ, &maps.xq, 0, (int)tok0, b_xq);
-    for (int j = 0; j < NB && j < nstate; ++j) {
-      load_w1(j);
-      load_w2(j);
-    }
+    for (int j = 0; j < NB1 && j < nstate; ++j) load_w1(j);
+    for (int j = 0; j < NB2 && j < nstate; ++j) load_w2(j);
   }
   // 16-bit row c..c+7 of a [.][F] tensor <-> 8 floats (16-byte accesses)
   auto ld_row8 = [&](const T* src, float* x) {
@@ -327,19 +361,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     *reinterpret_cast<uint4*>(dst) =
         make_uint4(H::pack(x[0], x[1]), H::pack(x[2], x[3]), H::pack(x[4], x[5]), H::pack(x[6], x[7]));
   };
+  const int r = tid - ROW_T0;  // row of a row thread
+  const int seg_r = seg_first + (row0 + min(r, nrows - 1)) / seg_tok;
+  float xu[F];  // the row's XU, loaded before the summaries are staged so the latencies overlap
+  if (row_thread && r < nrows) {
+#pragma unroll
+    for (int c = 0; c < F; c += 8) ld_row8(XU + (tok0 + r) * F + c, xu + c);
+  }
   stage_summaries();
   if (nstate > 0) load_bias(0);
   if (nstate > 1) load_bias(1);
   __syncthreads();  // summaries and the first two states' biases in shared memory
 
-  // mixing weights g_j(t), j = 0..seg_r (threads 0-127, one token each; seg_r is the row's
-  // own segment)
-  const int r = tid;  // row of threads 0-127
-  const int seg_r = seg_first + (row0 + min(r, nrows - 1)) / seg_tok;
-  if (tid < ROWS && r < nrows) {
-    float xu[F];
-#pragma unroll
-    for (int c = 0; c < F; c += 8) ld_row8(XU + (tok0 + r) * F + c, xu + c);
+  // mixing weights g_j(t), j = 0..seg_r (row threads, one token each; seg_r is the row's own
+  // segment)
+  if (row_thread && r < nrows) {
     float mx = -INFINITY;
     for (int j = 0; j <= seg_r; ++j) {
       const float4* sm = reinterpret_cast<const float4*>(SUM + j * F);
@@ -361,155 +397,267 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     const float inv = 1.f / tot;
     for (int j = 0; j <= seg_r; ++j) G[r * GLD + j] *= inv;
   }
-  if (tid == 0) {
+  if (tid == kIssuer) {  // product 1 of the first NX states
     wait(b_xq, 0);
-    wait(b_w1(0), 0);
-    if (!abort_sh) product1(0);
+    for (int j = 0; j < NX && j < nstate; ++j) {
+      wait(b_w1(j), j / NB1);
+      if (!abort_sh) product1(j);
+    }
   }
   __syncthreads();  // mixing weights written; the XQ tile is in shared memory
 
-  float acc[F];   // forward: sum_j g_j R_j;  backward: dOut row
-  float xq[F];    // XQ row
-  if (tid < ROWS) {
+  // The read-out of state j is R_j = XQ + ln_w * (y_j - mu_j) rstd_j + ln_b with y_j = Z2_j +
+  // b2_j. Its terms that do not change with j are taken out of the loop:
+  //   forward  out = sum_j g_j R_j + g_i XQW
+  //                = ln_w * sum_j g_j rstd_j (y_j - mu_j) + (XQ + ln_b) sum_j g_j + g_i XQW
+  //   backward dg_j = <dOut, R_j> = <dOut, XQ + ln_b> + rstd_j <dOut * ln_w, y_j - mu_j>
+  float acc[F];      // forward: sum_j g_j rstd_j (y_j - mu_j);  backward: dOut * ln_w
+  float gsum = 0.f;  // forward: sum_j g_j over the states read out
+  float k0 = 0.f;    // backward: <dOut, XQ + ln_b>
+  // 8 values of the XQ row from the swizzled tile
+  auto xq_row8 = [&](int ch, float* x) {
+    const uint4 u = *reinterpret_cast<const uint4*>(smem + OFF_XQ + swz128(r, ch));
+    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 v = H::unpack(w4[k]);
+      x[2 * k] = v.x;
+      x[2 * k + 1] = v.y;
+    }
+  };
+  const T* dO = reinterpret_cast<const T*>(p.dOut);
+  if (row_thread) {
+#pragma unroll
+    for (int ch = 0; ch < F / 8; ++ch) {
+      if (BWD && r < nrows) {
+        float x[8];
+        xq_row8(ch, x);
+        ld_row8(dO + (tok0 + r) * F + 8 * ch, acc + 8 * ch);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int c = 8 * ch + e;
+          k0 += acc[c] * (x[e] + LN[F + c]);
+          acc[c] *= LN[c];
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[8 * ch + e] = 0.f;
+      }
+    }
+  }
+
+  // X2 = gelu(Z1 + b1_j) for 32-column chunks [c_begin, c_end) of the rows of lane quadrant
+  // warp % 4, into the K-major swizzled X2 tiles
+  auto gelu_chunks = [&](int j, int c_begin, int c_end) {
+    const int row = 32 * (warp & 3) + lane;
+    const float* b1 = reinterpret_cast<const float*>(smem + OFF_B1) + (j % 3) * FF;
+#pragma unroll 1
+    for (int c4 = c_begin; c4 < c_end; ++c4) {
+      const int col = 32 * c4;
+      float z[32];
+      tmem_ld32(tmem_lane_addr(tZ1 + (j % NX) * FF, warp, col), z);
+      tmem_wait_ld();
+      uint32_t pk[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const float2 bb = *reinterpret_cast<const float2*>(b1 + col + 2 * u);
+        const float2 g = gelu2(make_float2(z[2 * u] + bb.x, z[2 * u + 1] + bb.y));
+        pk[u] = H::pack(g.x, g.y);
+      }
+      const int atom = col / 64, ch0 = (col % 64) / 8;
+      uint8_t* base = smem + OFF_X2 + (j % NX) * L::X2_BUF + atom * (ROWS * 64 * 2);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(base + swz128(row, ch0 + u)) =
+            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+    }
+  };
+  // The same for FF = 64 in one pass: both 32-column loads issued before the wait
+  auto gelu64 = [&](int j) {
+    const int row = 32 * (warp & 3) + lane;
+    const float* b1 = reinterpret_cast<const float*>(smem + OFF_B1) + (j % 3) * FF;
+    float z[64];
+    tmem_ld32(tmem_lane_addr(tZ1 + (j % NX) * FF, warp, 0), z);
+    tmem_ld32(tmem_lane_addr(tZ1 + (j % NX) * FF, warp, 32), z + 32);
+    tmem_wait_ld();
+    uint8_t* base = smem + OFF_X2 + (j % NX) * L::X2_BUF;
 #pragma unroll
     for (int ch = 0; ch < 8; ++ch) {
-      const uint4 u = *reinterpret_cast<const uint4*>(smem + OFF_XQ + swz128(r, ch));
-      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+      uint32_t pk[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 v = H::unpack(w4[k]);
-        xq[8 * ch + 2 * k] = v.x;
-        xq[8 * ch + 2 * k + 1] = v.y;
+      for (int u = 0; u < 4; ++u) {
+        const int c = 8 * ch + 2 * u;
+        const float2 bb = *reinterpret_cast<const float2*>(b1 + c);
+        const float2 g = gelu2(__fadd2_rn(make_float2(z[c], z[c + 1]), bb));
+        pk[u] = H::pack(g.x, g.y);
       }
+      *reinterpret_cast<uint4*>(base + swz128(row, ch)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
-    const T* dO = reinterpret_cast<const T*>(p.dOut);
-#pragma unroll
-    for (int c = 0; c < F; c += 8) {
-      if (BWD && r < nrows) {
-        ld_row8(dO + (tok0 + r) * F + c, acc + c);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[c + e] = 0.f;
-      }
-    }
-  }
-
-  for (int j = 0; j < nstate; ++j) {
-    // ---- X2 = gelu(Z1 + b1_j): warp w reads lanes of quadrant w % 4, columns 128 (w / 4) ..
-    if (lane == 0) wait(b_p1, j);
+  };
+  // R_j = XQ + LN(Z2 + b2_j) (row threads, one token each): accumulate the forward's sum or
+  // record dg_j = <dOut, R_j> (backward). With signal_free each warp arrives on the Z2-free
+  // mbarrier as soon as its rows are out of tensor memory.
+  auto readout = [&](int j, bool signal_free) {
+    if (lane == 0) wait(b_p2(j), j / NX);
     __syncwarp();
     tmem_fence_after();
-    // product 1 of j no longer reads its W1 buffer: fetch state j + NB into it
-    if (tid == 0 && j + NB < nstate && !abort_sh) load_w1(j + NB);
-    if (warp >= 4 && j + 2 < nstate) bias_fetch(j + 2);
-    {
-      // the 32-column chunks of a row: [0, SPLIT) for warps 0-3 (they also run the read-out
-      // LayerNorm below), the rest for warps 4-7
-      const int q = warp & 3, row = 32 * q + lane;
-      const int c_begin = warp < 4 ? 0 : L::SPLIT, c_end = warp < 4 ? L::SPLIT : L::CHUNKS;
-      const float* b1 = reinterpret_cast<const float*>(smem + OFF_B1) + (j % 3) * FF;
-#pragma unroll 1
-      for (int c4 = c_begin; c4 < c_end; ++c4) {
-        const int col = 32 * c4;
-        float z[32];
-        tmem_ld32(tmem_lane_addr(tZ1, warp, col), z);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          const float2 bb = *reinterpret_cast<const float2*>(b1 + col + 2 * u);
-          const float2 g = gelu2(make_float2(z[2 * u] + bb.x, z[2 * u + 1] + bb.y));
-          pk[u] = H::pack(g.x, g.y);
-        }
-        const int atom = col / 64, ch0 = (col % 64) / 8;
-        uint8_t* base = smem + OFF_X2 + atom * (ROWS * 64 * 2);
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          *reinterpret_cast<uint4*>(base + swz128(row, ch0 + u)) =
-              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-      }
+    float z[F];
+    tmem_ld32(tmem_lane_addr(tZ2 + (j % NX) * F, warp, 0), z);
+    tmem_ld32(tmem_lane_addr(tZ2 + (j % NX) * F, warp, 32), z + 32);
+    tmem_wait_ld();
+    if (signal_free) {
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b_zf(j));
     }
-    fence_proxy_async();  // X2 stores -> visible to the tensor cores
-    tmem_fence_before();
-    __syncthreads();
-    if (warp >= 4 && j + 2 < nstate) bias_put(j + 2);
-    if (tid == 0 && !abort_sh) {
-      wait(b_w2(j), j / NB);
-      if (!abort_sh) product2(j);
-      if (j + 1 < nstate) {
-        wait(b_w1(j + 1), (j + 1) / NB);
-        if (!abort_sh) product1(j + 1);  // Z1 of j has been read by every warp
-      }
+    // product 2 of j no longer reads its W2 buffer: fetch state j + NB2 into it
+    if (tid == ROW_T0 && j + NB2 < nstate && !abort_sh) load_w2(j + NB2);
+    const float* b2 = reinterpret_cast<const float*>(smem + OFF_B2) + (j % 3) * F;
+    float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < F; c += 2) {
+      const float2 y = __fadd2_rn(make_float2(z[c], z[c + 1]), *reinterpret_cast<const float2*>(b2 + c));
+      z[c] = y.x;
+      z[c + 1] = y.y;
+      s2 = __fadd2_rn(s2, y);
     }
-    // ---- R_j = XQ + LN(Z2 + b2_j) (warps 0-3, one token per thread)
-    if (warp < 4) {
-      if (lane == 0) wait(b_p2, j);
+    const float2 nmu = f2(-(s2.x + s2.y) * (1.f / F));
+    float2 v2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < F; c += 2) {
+      const float2 d = __fadd2_rn(make_float2(z[c], z[c + 1]), nmu);
+      z[c] = d.x;
+      z[c + 1] = d.y;
+      v2 = __ffma2_rn(d, d, v2);
+    }
+    const float rstd = 1.f / sqrtf((v2.x + v2.y) * (1.f / F) + kReadoutEps);
+    if (!BWD) {
+      const float gj = r < nrows && j < seg_r ? G[r * GLD + j] : 0.f;  // states of the row's own segment only
+      gsum += gj;
+      const float2 sj = f2(gj * rstd);
+#pragma unroll
+      for (int c = 0; c < F; c += 2) {
+        const float2 a2 = __ffma2_rn(sj, make_float2(z[c], z[c + 1]), make_float2(acc[c], acc[c + 1]));
+        acc[c] = a2.x;
+        acc[c + 1] = a2.y;
+      }
+    } else {
+      float2 d2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < F; c += 2) d2 = __ffma2_rn(make_float2(acc[c], acc[c + 1]), make_float2(z[c], z[c + 1]), d2);
+      if (r < nrows) DG[r * GLD + j] = k0 + rstd * (d2.x + d2.y);
+    }
+  };
+
+  if constexpr (!kSpecialised) {
+    // FF = 256: every warp takes part in the GELU; a CTA barrier per state separates it from
+    // the products and the read-out
+    for (int j = 0; j < nstate; ++j) {
+      if (lane == 0) wait(b_p1(j), j / NX);
       __syncwarp();
       tmem_fence_after();
-      float z[F];
-      tmem_ld32(tmem_lane_addr(tZ2, warp, 0), z);
-      tmem_ld32(tmem_lane_addr(tZ2, warp, 32), z + 32);
-      tmem_wait_ld();
-      // product 2 of j no longer reads its W2 buffer: fetch state j + NB into it
-      if (tid == 0 && j + NB < nstate && !abort_sh) load_w2(j + NB);
-      const float* b2 = reinterpret_cast<const float*>(smem + OFF_B2) + (j % 3) * F;
-      float mu = 0.f;
-#pragma unroll
-      for (int c = 0; c < F; ++c) {
-        z[c] += b2[c];
-        mu += z[c];
+      // product 1 of j no longer reads its W1 buffer: fetch state j + NB1 into it
+      if (tid == 0 && j + NB1 < nstate && !abort_sh) load_w1(j + NB1);
+      if (warp >= 4 && j + 2 < nstate) {
+        b1_fetch(j + 2, tid - GELU_T0);
+        b2_fetch(j + 2, tid - GELU_T0);
       }
-      mu *= 1.f / F;
-      float var = 0.f;
-#pragma unroll
-      for (int c = 0; c < F; ++c) {
-        z[c] -= mu;
-        var += z[c] * z[c];
+      gelu_chunks(j, warp < 4 ? 0 : L::SPLIT, warp < 4 ? L::SPLIT : L::CHUNKS);
+      fence_proxy_async();  // X2 stores -> visible to the tensor cores
+      tmem_fence_before();
+      __syncthreads();
+      if (warp >= 4 && j + 2 < nstate) {
+        b1_put(j + 2, tid - GELU_T0);
+        b2_put(j + 2, tid - GELU_T0);
       }
-      const float rstd = 1.f / sqrtf(var * (1.f / F) + kReadoutEps);
-      if (!BWD) {
-        const float gj = r < nrows && j < seg_r ? G[r * GLD + j] : 0.f;  // states of the row's own segment only
-#pragma unroll
-        for (int c = 0; c < F; ++c) acc[c] += gj * (xq[c] + LN[c] * z[c] * rstd + LN[F + c]);
-      } else {
-        float d = 0.f;
-#pragma unroll
-        for (int c = 0; c < F; ++c) d += acc[c] * (xq[c] + LN[c] * z[c] * rstd + LN[F + c]);
-        if (r < nrows) DG[r * GLD + j] = d;
+      if (tid == 0 && !abort_sh) {
+        wait(b_w2(j), j / NB2);
+        if (!abort_sh) product2(j);
+        if (j + 1 < nstate) {
+          wait(b_w1(j + 1), (j + 1) / NB1);
+          if (!abort_sh) product1(j + 1);  // Z1 of j has been read by every warp
+        }
+      }
+      if (row_thread) readout(j, false);
+      tmem_fence_before();
+    }
+  } else if (warp < 4) {
+    // GELU group: X2_j = gelu(Z1_j + b1_j) into buffer j % 2, then one arrival per warp on
+    // the GELU-done barrier of that buffer. Product 1 of j was committed after product 2 of
+    // j - 2 by the same thread, so its completion also means X2 buffer j % 2 is free.
+    for (int j = 0; j < nstate; ++j) {
+      if (lane == 0) wait(b_p1(j), j / NX);
+      __syncwarp();
+      tmem_fence_after();
+      if (j + 2 < nstate) b1_fetch(j + 2, tid - GELU_T0);
+      gelu64(j);
+      fence_proxy_async();  // X2 stores -> visible to the tensor cores
+      tmem_fence_before();  // Z1 loads complete before the arrival
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b_gd(j));
+      named_bar_sync(1, 128);  // every GELU warp is past state j: b1 slot (j + 2) % 3 is free
+      if (j + 2 < nstate) b1_put(j + 2, tid - GELU_T0);
+    }
+  } else if (warp < 8) {
+    // row group: the read-outs, following the product-2 commits; it owns the b2 ring
+    for (int j = 0; j < nstate; ++j) {
+      if (j + 2 < nstate) b2_fetch(j + 2, r);
+      readout(j, true);
+      if (j + 2 < nstate) b2_put(j + 2, r);
+      named_bar_sync(2, 128);  // slot (j + 2) % 3 written; slot j % 3 read
+    }
+  } else if (tid == kIssuer) {
+    // issuer: once the GELU of j is done, product 2 of j (into Z2 buffer j % 2, free once the
+    // read-out of j - 2 has taken it out) and product 1 of j + 2 (into the Z1 buffer the GELU
+    // of j has just read); W1 buffer j % NB1 is free (product 1 of j has completed)
+    for (int j = 0; j < nstate; ++j) {
+      wait(b_gd(j), j / NX);
+      if (j + NB1 < nstate && !abort_sh) load_w1(j + NB1);
+      wait(b_w2(j), j / NB2);
+      if (j >= NX) wait(b_zf(j - NX), (j - NX) / NX);
+      if (!abort_sh) product2(j);
+      if (j + NX < nstate) {
+        wait(b_w1(j + NX), (j + NX) / NB1);
+        if (!abort_sh) product1(j + NX);
       }
     }
-    tmem_fence_before();
   }
+  tmem_fence_before();
 
-  // ---- tail (threads 0-127, one token each)
+  // ---- tail (row threads, one token each)
   if constexpr (BWD && L::SUM_IN_X2) {
     // the read-outs overwrote the summaries' copy in the X2 region; every product is done
-    // (warps 0-3 waited for the last one before this barrier): stage them again
+    // (the row threads waited for the last one before this barrier): stage them again
     __syncthreads();
     stage_summaries();
     __syncthreads();
   }
-  if (tid < ROWS && r < nrows) {
+  if (row_thread && r < nrows) {
     const long long o = (tok0 + r) * F;
     const float gi = G[r * GLD + seg_r];
     if (!BWD) {
       T* out = reinterpret_cast<T*>(p.out);
 #pragma unroll
-      for (int c = 0; c < F; c += 8) {
-        float w[8], y[8];
-        ld_row8(XQW + o + c, w);
+      for (int ch = 0; ch < F / 8; ++ch) {
+        float w[8], x[8], y[8];
+        ld_row8(XQW + o + 8 * ch, w);
+        xq_row8(ch, x);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) y[e] = acc[c + e] + gi * w[e];
-        st_row8(out + o + c, y);
+        for (int e = 0; e < 8; ++e) {
+          const int c = 8 * ch + e;
+          y[e] = LN[c] * acc[c] + (x[e] + LN[F + c]) * gsum + gi * w[e];
+        }
+        st_row8(out + o + 8 * ch, y);
       }
     } else {
       float dgi = 0.f;
 #pragma unroll
       for (int c = 0; c < F; c += 8) {
-        float w[8];
+        float w[8], d8[8];
         ld_row8(XQW + o + c, w);
+        ld_row8(dO + o + c, d8);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) dgi += acc[c + e] * w[e];
+        for (int e = 0; e < 8; ++e) dgi += d8[e] * w[e];
       }
       DG[r * GLD + seg_r] = dgi;
       float sg = 0.f;
@@ -535,8 +683,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
 #pragma unroll
       for (int c = 0; c < F; c += 8) {
         float q8[8];
+        ld_row8(dO + o + c, q8);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) q8[e] = gi * acc[c + e];
+        for (int e = 0; e < 8; ++e) q8[e] *= gi;
         st_row8(dXU + o + c, dxu + c);
         st_row8(dXQW + o + c, q8);
       }
@@ -546,38 +695,39 @@ __global__ void __launch_bounds__(NTHREADS, 1) memo_mix_kernel(MemoMixParams p, 
     // d summary_i += sum over the tile's tokens of segment i of ds_i(t) XU_t  (X2 region as
     // scratch)
     __syncthreads();
-    float* red = reinterpret_cast<float*>(smem + OFF_X2);  // [128][64]
-    if (tid < ROWS) {
+    float* red = reinterpret_cast<float*>(smem + OFF_X2);  // [128][RED_LD]
+    if (row_thread) {
       const float ds = r < nrows ? DG[r * GLD + seg_r] : 0.f;
 #pragma unroll
       for (int c = 0; c < F; c += 2) {
         float2 v = make_float2(0.f, 0.f);
         if (r < nrows) v = H::unpack(*reinterpret_cast<const uint32_t*>(XU + (tok0 + r) * F + c));
-        red[r * F + c] = ds * v.x;
-        red[r * F + c + 1] = ds * v.y;
+        red[r * L::RED_LD + c] = ds * v.x;
+        red[r * L::RED_LD + c + 1] = ds * v.y;
       }
     }
     __syncthreads();
     // one (segment, feature) per thread: rows [lo, hi) of the tile belong to segment
     // seg_first + sg
-    for (int e = tid; e < (seg_last - seg_first + 1) * F; e += NTHREADS) {
+    for (int e = tid; e < (seg_last - seg_first + 1) * F; e += NT) {
       const int sg = e / F, f = e % F;
       const int lo = max(0, sg * seg_tok - row0), hi = min(nrows, (sg + 1) * seg_tok - row0);
       float a = 0.f;
-      for (int i = lo; i < hi; ++i) a += red[i * F + f];
+      for (int i = lo; i < hi; ++i) a += red[i * L::RED_LD + f];
       atomicAdd(p.dsum + (s * p.NS + seg_first + sg) * F + f, a);
     }
   }
   // a timed-out wait may leave products in flight: drain (bounded) before freeing memory
   if (tid == 0 && abort_sh) {
     mbar_wait(b_xq, 0, nullptr);
-    mbar_wait(b_p1, (uint32_t)((nstate - 1) & 1), nullptr);
-    mbar_wait(b_p2, (uint32_t)((nstate - 1) & 1), nullptr);
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {  // weight loads issued and never awaited
-      if (last_w1[b] >= 0) mbar_wait(b_w1(last_w1[b]), (uint32_t)((last_w1[b] / NB) & 1), nullptr);
-      if (last_w2[b] >= 0) mbar_wait(b_w2(last_w2[b]), (uint32_t)((last_w2[b] / NB) & 1), nullptr);
+    for (int b = 0; b < NX; ++b) {  // the last commit of each product barrier
+      if (commits_sh[0][b] > 0) mbar_wait(smem_u32(&bars[BAR_P1 + b]), (uint32_t)((commits_sh[0][b] - 1) & 1), nullptr);
+      if (commits_sh[1][b] > 0) mbar_wait(smem_u32(&bars[BAR_P2 + b]), (uint32_t)((commits_sh[1][b] - 1) & 1), nullptr);
     }
+    for (int b = 0; b < NB1; ++b)  // weight loads issued and never awaited
+      if (last_w1_sh[b] >= 0) mbar_wait(b_w1(last_w1_sh[b]), (uint32_t)((last_w1_sh[b] / NB1) & 1), nullptr);
+    for (int b = 0; b < NB2; ++b)
+      if (last_w2_sh[b] >= 0) mbar_wait(b_w2(last_w2_sh[b]), (uint32_t)((last_w2_sh[b] / NB2) & 1), nullptr);
   }
   tmem_fence_before();
   __syncthreads();
@@ -653,11 +803,11 @@ static int run(MemoMixParams p, bool bwd, bool prepped, cudaStream_t stream, con
   if (!bwd) {
     rc = prepare_smem(memo_mix_kernel<T, false, FF>, SMEM, who);
     if (rc) return rc;
-    memo_mix_kernel<T, false, FF><<<grid, NTHREADS, SMEM, stream>>>(p, maps);
+    memo_mix_kernel<T, false, FF><<<grid, Mix<FF>::NT, SMEM, stream>>>(p, maps);
   } else {
     rc = prepare_smem(memo_mix_kernel<T, true, FF>, SMEM, who);
     if (rc) return rc;
-    memo_mix_kernel<T, true, FF><<<grid, NTHREADS, SMEM, stream>>>(p, maps);
+    memo_mix_kernel<T, true, FF><<<grid, Mix<FF>::NT, SMEM, stream>>>(p, maps);
     rc = check_launch(who);
     if (rc) return rc;
     memo_dxk_kernel<T><<<148 * 8, 256, 0, stream>>>(p);
@@ -684,10 +834,9 @@ static void fill_common(MemoMixParams& p, int B, int NH, int NC, int M) {
   p.M = M;
   p.NS = (NC + M - 1) / M;
   p.TILES = (M * C + ROWS - 1) / ROWS;
-  // segments of at most 64 tokens share 128-row tiles: group 0 is segment 0, the others
-  // hold P consecutive segments each
+  // segments of at most 64 tokens share 128-row tiles, P consecutive segments each
   p.P = M * C <= ROWS / 2 ? ROWS / (M * C) : 1;
-  p.NG = p.P == 1 ? p.NS : 1 + (p.NS - 1 + p.P - 1) / p.P;
+  p.NG = p.P == 1 ? p.NS : (p.NS + p.P - 1) / p.P;
 }
 
 }  // namespace ttt
