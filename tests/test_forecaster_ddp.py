@@ -66,3 +66,19 @@ def test_series_has_the_config4_statistics():
     assert torch.allclose(s.std(0, unbiased=False), torch.ones(7), atol=1e-3)
     x, y = S.forecast_windows(s, 336, 96, 4, torch.Generator().manual_seed(0))
     assert x.shape == (4, 336, 7) and y.shape == (4, 96, 7)
+
+
+def test_batch_copies_match_tile_forward_and_backward():
+    """BatchCopies (the layer's per-sequence inner-state copies) is torch.tile with the
+    batch sum of its backward done as a matrix-vector product."""
+    from forecaster import BatchCopies
+
+    torch.manual_seed(1)
+    p = torch.randn(4, 8, 16, dtype=torch.float64, requires_grad=True)
+    g = torch.randn(5, 4, 8, 16, dtype=torch.float64)
+    out = BatchCopies.apply(p, 5)
+    ref = torch.tile(p.unsqueeze(0), (5, 1, 1, 1))
+    assert out.is_contiguous() and torch.equal(out, ref)
+    (gp,) = torch.autograd.grad(out, p, g)
+    (gr,) = torch.autograd.grad(ref, p, g)
+    assert torch.allclose(gp, gr, rtol=1e-12, atol=1e-12)

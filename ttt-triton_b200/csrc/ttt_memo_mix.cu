@@ -111,43 +111,74 @@ __global__ void __launch_bounds__(256) memo_prep_kernel(MemoMixParams p) {
   using H = Half2<T>;
   const long long sj = blockIdx.x;  // (stream, memo state)
   const long long s = sj / p.NS;
-  const int j = (int)(sj % p.NS);
+  const int j = (int)(sj - s * p.NS);
+  const int tid = threadIdx.x;
   const float* W1 = p.W1_memo + sj * F * FF;  // [F][FF]
   const float* W2 = p.W2_memo + sj * FF * F;  // [FF][F]
   T* W1T = reinterpret_cast<T*>(p.W1T) + sj * FF * F;  // [FF][F]
   T* W2T = reinterpret_cast<T*>(p.W2T) + sj * F * FF;  // [F][FF]
-  __shared__ float tile[64][65];
-  // W1^T: four 64 x 64 blocks (ff block), transposed through shared memory
+  __shared__ float tile[2][64][65];
+  // 64 x 64 blocks of W1 (rows: features, columns: hidden units blk*64..) and of W2 (rows:
+  // hidden units blk*64.., columns: features), transposed together through shared memory;
+  // 16-byte global loads and stores
   for (int blk = 0; blk < FF / 64; ++blk) {
-    for (int i = threadIdx.x; i < 64 * 64; i += 256) tile[i / 64][i % 64] = W1[(i / 64) * FF + blk * 64 + i % 64];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = tid + 256 * k, r = i >> 4, c = 4 * (i & 15);
+      const float4 a = *reinterpret_cast<const float4*>(W1 + r * FF + blk * 64 + c);
+      const float4 b = *reinterpret_cast<const float4*>(W2 + (blk * 64 + r) * F + c);
+      tile[0][r][c] = a.x;
+      tile[0][r][c + 1] = a.y;
+      tile[0][r][c + 2] = a.z;
+      tile[0][r][c + 3] = a.w;
+      tile[1][r][c] = b.x;
+      tile[1][r][c + 1] = b.y;
+      tile[1][r][c + 2] = b.z;
+      tile[1][r][c + 3] = b.w;
+    }
     __syncthreads();
-    for (int i = threadIdx.x; i < 32 * 64; i += 256) {
-      const int r = i / 32, c = 2 * (i % 32);  // W1T row blk*64 + r, features c, c+1
-      *reinterpret_cast<uint32_t*>(W1T + (blk * 64 + r) * F + c) = H::pack(tile[c][r], tile[c + 1][r]);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = tid + 256 * k, r = i >> 3, c = 8 * (i & 7);  // output row r, columns c..c+7
+      uint32_t u1[4], u2[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        u1[e] = H::pack(tile[0][c + 2 * e][r], tile[0][c + 2 * e + 1][r]);
+        u2[e] = H::pack(tile[1][c + 2 * e][r], tile[1][c + 2 * e + 1][r]);
+      }
+      *reinterpret_cast<uint4*>(W1T + (blk * 64 + r) * F + c) = make_uint4(u1[0], u1[1], u1[2], u1[3]);
+      *reinterpret_cast<uint4*>(W2T + r * FF + blk * 64 + c) = make_uint4(u2[0], u2[1], u2[2], u2[3]);
     }
     __syncthreads();
   }
-  for (int blk = 0; blk < FF / 64; ++blk) {
-    for (int i = threadIdx.x; i < 64 * 64; i += 256) tile[i / 64][i % 64] = W2[(blk * 64 + i / 64) * F + i % 64];
-    __syncthreads();
-    for (int i = threadIdx.x; i < 32 * 64; i += 256) {
-      const int r = i / 32, c = 2 * (i % 32);  // W2T row r (feature), hidden blk*64 + c, c+1
-      *reinterpret_cast<uint32_t*>(W2T + r * FF + blk * 64 + c) = H::pack(tile[c][r], tile[c + 1][r]);
-    }
-    __syncthreads();
-  }
-  // summary_j = mean of segment j's XK rows
+  // summary_j = mean of segment j's XK rows: thread (part, chunk) adds rows part, part + 32, ..
+  // of 8 features (16-byte loads), then 64 threads add the 32 parts
   const int n0 = j * p.M, n1 = min((j + 1) * p.M, p.NC);
-  const long long r0 = (s * p.NC + n0) * C, nrows = (long long)(n1 - n0) * C;
+  const long long r0 = (s * p.NC + n0) * C;
+  const int nrows = (n1 - n0) * C;
   const T* XK = reinterpret_cast<const T*>(p.XK);
-  float* red = &tile[0][0];
-  const int f = threadIdx.x & 63, part = threadIdx.x >> 6;
-  float acc = 0.f;
-  for (long long r = part; r < nrows; r += 4) acc += (float)XK[(r0 + r) * F + f];
-  red[part * 64 + f] = acc;
+  float* red = &tile[0][0][0];  // [32][64]
+  const int part = tid >> 3, ch = tid & 7;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int r = part; r < nrows; r += 32) {
+    const uint4 u = *reinterpret_cast<const uint4*>(XK + (r0 + r) * F + 8 * ch);
+    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 v = H::unpack(w4[e]);
+      acc[2 * e] += v.x;
+      acc[2 * e + 1] += v.y;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) red[part * 64 + 8 * ch + e] = acc[e];
   __syncthreads();
-  if (threadIdx.x < 64)
-    p.summary[sj * F + f] = (red[f] + red[64 + f] + red[128 + f] + red[192 + f]) / (float)nrows;
+  if (tid < 64) {
+    float v = 0.f;
+#pragma unroll 8
+    for (int q = 0; q < 32; ++q) v += red[q * 64 + tid];
+    p.summary[sj * F + tid] = v / (float)nrows;
+  }
 }
 
 // ---------------------------------------------------------------------------------- mix
@@ -862,6 +893,7 @@ extern "C" int ttt_memo_mix_fwd(int B, int NH, int NC, int CS, int F, int FF, in
               TTT_ERR_NULL, "%s: NULL pointer argument", who);
   TTT_REQUIRE(aligned16(XQW) && aligned16(XQ) && aligned16(XK) && aligned16(XU) && aligned16(scratch), TTT_ERR_ALIGN,
               "%s: activations and scratch must be 16-byte aligned", who);
+  TTT_REQUIRE(aligned16(W1_memo) && aligned16(W2_memo), TTT_ERR_ALIGN, "%s: memo states must be 16-byte aligned", who);
   const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size, FF);
   TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "%s: scratch has %zu bytes, needs %zu", who, scratch_bytes, need);
   TTT_REQUIRE(aligned16(out), TTT_ERR_ALIGN, "%s: out must be 16-byte aligned", who);
@@ -898,6 +930,7 @@ extern "C" int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, in
               TTT_ERR_NULL, "%s: NULL pointer argument", who);
   TTT_REQUIRE(aligned16(XQW) && aligned16(XQ) && aligned16(XK) && aligned16(XU) && aligned16(scratch), TTT_ERR_ALIGN,
               "%s: activations and scratch must be 16-byte aligned", who);
+  TTT_REQUIRE(aligned16(W1_memo) && aligned16(W2_memo), TTT_ERR_ALIGN, "%s: memo states must be 16-byte aligned", who);
   const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size, FF);
   TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "%s: scratch has %zu bytes, needs %zu", who, scratch_bytes, need);
   MemoMixParams p = {};

@@ -53,6 +53,34 @@ def rope_table_3d(head_dim, height, width, frames, theta=10000.0):
     return torch.cos(ang), torch.sin(ang)
 
 
+_ONES = {}
+
+
+def _ones(n, like):
+    key = (n, like.device, like.dtype)
+    if key not in _ONES:
+        _ONES[key] = torch.ones(n, device=like.device, dtype=like.dtype)
+    return _ONES[key]
+
+
+class BatchCopies(torch.autograd.Function):
+    """p -> B contiguous copies [B, *p.shape], the per-sequence initial inner states of
+    ttt_layer.py:462-465 (``torch.tile(p.unsqueeze(0), (B, 1, ...))``). The backward sums
+    the B gradient copies with one matrix-vector product (a strided reduction over the
+    leading dimension is several times slower for these shapes)."""
+
+    @staticmethod
+    def forward(ctx, p, B):
+        ctx.B = B
+        return p.unsqueeze(0).expand(B, *p.shape).contiguous()
+
+    @staticmethod
+    def backward(ctx, g):
+        B = ctx.B
+        g2 = g.reshape(B, -1)
+        return torch.mv(g2.t(), _ones(B, g2)).reshape(g.shape[1:]), None
+
+
 class TTTMLPLayer(nn.Module):
     """ttt_layer.TTTMLP with use_kernel=True on this library (no tensor parallelism)."""
 
@@ -96,15 +124,26 @@ class TTTMLPLayer(nn.Module):
         NC = inputs["XV"].shape[2]
         ckpt = min(max(self.scan_checkpoint_group_size, 1), NC)
         memo = self.mem_cache_segment_n_mini_batches
-        tile = (B, 1, 1, 1)
         XQW, W1_memo, b1_memo, W2_memo, b2_memo = TritonMLP.apply(
-            self.ttt_norm_weight, self.ttt_norm_bias, torch.tile(self.W1.unsqueeze(0), tile),
-            torch.tile(self.b1.unsqueeze(0), tile), torch.tile(self.W2.unsqueeze(0), tile),
-            torch.tile(self.b2.unsqueeze(0), tile), inputs["XQ"], inputs["XV"], inputs["XK"], inputs["eta"], ckpt,
-            memo)
+            self.ttt_norm_weight, self.ttt_norm_bias, BatchCopies.apply(self.W1, B), BatchCopies.apply(self.b1, B),
+            BatchCopies.apply(self.W2, B), BatchCopies.apply(self.b2, B), inputs["XQ"], inputs["XV"], inputs["XK"],
+            inputs["eta"], ckpt, memo)
         XQW = mlp_memo_mix(XQW, inputs["XQ"], inputs["XK"], inputs["XU"], W1_memo, b1_memo, W2_memo, b2_memo,
                            self.ttt_norm_weight, self.ttt_norm_bias, memo)
         return epilogue.output_epilogue(self, XQW)
+
+
+def linear_act(x, weight, bias, dt):
+    """nn.Linear in the activation dtype dt (what the reference's autocast runs), with the
+    input width zero-padded to a multiple of 8 so that the library GEMMs take their aligned
+    tensor-core paths (the 7-channel input projection and its weight gradient otherwise fall
+    back to unaligned fp32 kernels)."""
+    k = x.shape[-1]
+    pad = -k % 8
+    if pad:
+        x = Fn.pad(x, (0, pad))
+        weight = Fn.pad(weight, (0, pad))
+    return Fn.linear(x.to(dt), weight.to(dt), bias.to(dt))
 
 
 class TTTForecaster(nn.Module):
@@ -116,6 +155,7 @@ class TTTForecaster(nn.Module):
                  mem_cache_segment_n_mini_batches=2, act_dtype=torch.bfloat16):
         super().__init__()
         self.pred_len, self.d_out = pred_len, d_out
+        self.act_dtype = act_dtype
         self.in_proj = nn.Linear(d_in, model_dim)
         self.layers = nn.ModuleList(
             TTTMLPLayer(model_dim, num_heads, mini_batch_size, seq_len, ttt_base_lr, scan_checkpoint_group_size,
@@ -123,7 +163,7 @@ class TTTForecaster(nn.Module):
         self.head = nn.Linear(model_dim, pred_len * d_out)
 
     def forward(self, seq_x):
-        h = self.in_proj(seq_x)
+        h = linear_act(seq_x, self.in_proj.weight, self.in_proj.bias, self.act_dtype)
         for layer in self.layers:
             h = layer(h)
         out = self.head(h[:, -1].to(self.head.weight.dtype))
@@ -172,5 +212,5 @@ def tokens_per_step(batch, seq_len, num_heads, num_layers):
     return batch * num_heads * seq_len * num_layers
 
 
-__all__ = ["TTTMLPLayer", "TTTForecaster", "rope_table_3d", "load_reference_state_dict", "make_optimizer",
+__all__ = ["BatchCopies", "linear_act", "TTTMLPLayer", "TTTForecaster", "rope_table_3d", "load_reference_state_dict", "make_optimizer",
            "train_step", "tokens_per_step"]

@@ -9,8 +9,10 @@ libttt_b200.so (no Triton):
                              checkpoint_group_size)
 
 XQW is [B,NH,NC,CS,F] in XQ's dtype (computed in fp32). Backward returns the ten
-gradients of linear_triton.py:254-265 in XQ's dtype: the LN parameter gradients summed
-over the batch, dW1, db1, dXQ, dXV, dXK, the full dual-form d_eta, None, None.
+gradients of linear_triton.py:254-265: the LN parameter gradients summed over the batch,
+dW1, db1 (each in its parameter's dtype; the reference casts them to XQ's dtype, which
+autograd casts back, a rounding this path skips for fp32 parameters), dXQ, dXV, dXK, the
+full dual-form d_eta (in XQ's dtype), None, None.
 ``TritonLinear.sharded_mode`` selects the head-sharded DTensor entry, as in the reference.
 """
 
@@ -29,6 +31,7 @@ def _forward_core(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, XQ, XV,
         ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, XQ, XV, XK, eta, ckpt, for_backward=train
     )
     ctx.ckpt = ckpt
+    ctx.param_dtypes = (ttt_norm_weight.dtype, ttt_norm_bias.dtype, W1_init.dtype, b1_init.dtype)
     if train:
         ctx.save_for_backward(XQ, XV, XK, eta, ttt_norm_weight, ttt_norm_bias, W_ckpt, b_ckpt, Z, W_last, b_last)
     return XQW
@@ -36,15 +39,15 @@ def _forward_core(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, XQ, XV,
 
 def _backward_core(ctx, grad_XQW):
     XQ, XV, XK, eta, ln_w, ln_b, W_ckpt, b_ckpt, Z, W_last, b_last = ctx.saved_tensors
-    mp = XQ.dtype
     d_ln_w, d_ln_b, dW1, db1, dXQ, dXV, dXK, deta = _core.linear_backward(
         ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, grad_XQW, ctx.ckpt, Z=Z, W_last=W_last, b_last=b_last
     )
+    dt = ctx.param_dtypes
     return (
-        d_ln_w.sum(0).reshape(ln_w.shape).to(mp),
-        d_ln_b.sum(0).reshape(ln_b.shape).to(mp),
-        dW1.to(mp),
-        db1.to(mp),
+        d_ln_w.sum(0).reshape(ln_w.shape).to(dt[0]),
+        d_ln_b.sum(0).reshape(ln_b.shape).to(dt[1]),
+        dW1.to(dt[2]),
+        db1.to(dt[3]),
         dXQ,
         dXV,
         dXK,

@@ -9,8 +9,13 @@
 XQW is [B,NH,NC,CS,F] in XQ's dtype. The memo states are fp32 [B,NH,NS,...] with
 NS = ceil(NC / memo_segment_size), holding the inner state AFTER mini-batch i for each
 i % memo_segment_size == 0 (kernels/mlp_forward.py:193-226); they are
-non-differentiable (mlp_triton.py:196). Backward returns the twelve gradients of
-mlp_triton.py:338-351 in XQ's dtype (LN gradients summed over the batch, full d_eta).
+non-differentiable (mlp_triton.py:196), and backward receives None for them (no zero
+tensors are materialised). Backward returns the twelve gradients of mlp_triton.py:338-351
+(LN gradients summed over the batch, full d_eta): the activations' in XQ's dtype, the
+parameters' (ttt_norm_weight/bias, W1/b1/W2/b2_init) in each parameter's own dtype. The
+reference casts the parameter gradients to XQ's dtype as well, which autograd then casts
+back to the parameter's dtype; for fp32 parameters under 16-bit activations that is a
+rounding of the gradient (and two copies) which this path skips.
 """
 
 from __future__ import annotations
@@ -29,23 +34,28 @@ def _forward_core(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init
         for_backward=any(ctx.needs_input_grad),
     )
     ctx.ckpt = ckpt
+    ctx.param_dtypes = (ttt_norm_weight.dtype, ttt_norm_bias.dtype, W1_init.dtype, b1_init.dtype, W2_init.dtype,
+                        b2_init.dtype)
     if ck is not None:
         ctx.save_for_backward(XQ, XV, XK, eta, ttt_norm_weight, ttt_norm_bias, *ck, *zs, last[0], last[2])
     ctx.mark_non_differentiable(*memo)
+    ctx.set_materialize_grads(False)
     return (XQW, *memo)
 
 
 def _backward_core(ctx, grad_XQW):
     XQ, XV, XK, eta, ln_w, ln_b, W1c, b1c, W2c, b2c, Z1, Z2, Z1b, Z2b, W1l, W2l = ctx.saved_tensors
-    mp = XQ.dtype
+    if grad_XQW is None:  # only the (non-differentiable) memo states were used
+        grad_XQW = torch.zeros(XQ.shape, device=XQ.device, dtype=XQ.dtype)
     d_ln_w, d_ln_b, dW1, db1, dW2, db2, dXQ, dXV, dXK, deta = _core.mlp_backward(
         ln_w, ln_b, (W1c, b1c, W2c, b2c), XQ, XV, XK, eta, grad_XQW, ctx.ckpt,
         saved=(Z1, Z2, Z1b, Z2b), W1_last=W1l, W2_last=W2l,
     )
+    dt = ctx.param_dtypes
     return (
-        d_ln_w.sum(0).reshape(ln_w.shape).to(mp),
-        d_ln_b.sum(0).reshape(ln_b.shape).to(mp),
-        dW1.to(mp), db1.to(mp), dW2.to(mp), db2.to(mp),
+        d_ln_w.sum(0).reshape(ln_w.shape).to(dt[0]),
+        d_ln_b.sum(0).reshape(ln_b.shape).to(dt[1]),
+        dW1.to(dt[2]), db1.to(dt[3]), dW2.to(dt[4]), db2.to(dt[5]),
         dXQ, dXV, dXK, deta,
         None, None,
     )

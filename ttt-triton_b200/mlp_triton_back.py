@@ -7,7 +7,9 @@ The F x F TTT-MLP (W1, W2 both [B,NH,F,F]) without memo outputs:
 
 The reference module launches its kernels with an argument list that no longer matches
 them, so it cannot run as shipped; this one runs the sm_100a MLP kernels with FF = F.
-Backward returns the twelve gradients of mlp_triton_back.py:301-314.
+Backward returns the twelve gradients of mlp_triton_back.py:301-314, the parameters' in
+each parameter's own dtype (the reference casts them to XQ's dtype first), the
+activations' in XQ's dtype.
 """
 
 from __future__ import annotations
@@ -30,6 +32,8 @@ def _forward_core(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init
         for_backward=any(ctx.needs_input_grad),
     )
     ctx.ckpt = ckpt
+    ctx.param_dtypes = (ttt_norm_weight.dtype, ttt_norm_bias.dtype, W1_init.dtype, b1_init.dtype, W2_init.dtype,
+                        b2_init.dtype)
     if ck is not None:
         ctx.save_for_backward(XQ, XV, XK, eta, ttt_norm_weight, ttt_norm_bias, *ck, *zs, last[0], last[2])
     return XQW
@@ -37,15 +41,15 @@ def _forward_core(ctx, ttt_norm_weight, ttt_norm_bias, W1_init, b1_init, W2_init
 
 def _backward_core(ctx, grad_XQW):
     XQ, XV, XK, eta, ln_w, ln_b, W1c, b1c, W2c, b2c, Z1, Z2, Z1b, Z2b, W1l, W2l = ctx.saved_tensors
-    mp = XQ.dtype
     d_ln_w, d_ln_b, dW1, db1, dW2, db2, dXQ, dXV, dXK, deta = _core.mlp_backward(
         ln_w, ln_b, (W1c, b1c, W2c, b2c), XQ, XV, XK, eta, grad_XQW, ctx.ckpt,
         saved=(Z1, Z2, Z1b, Z2b), W1_last=W1l, W2_last=W2l,
     )
+    dt = ctx.param_dtypes
     return (
-        d_ln_w.sum(0).reshape(ln_w.shape).to(mp),
-        d_ln_b.sum(0).reshape(ln_b.shape).to(mp),
-        dW1.to(mp), db1.to(mp), dW2.to(mp), db2.to(mp),
+        d_ln_w.sum(0).reshape(ln_w.shape).to(dt[0]),
+        d_ln_b.sum(0).reshape(ln_b.shape).to(dt[1]),
+        dW1.to(dt[2]), db1.to(dt[3]), dW2.to(dt[4]), db2.to(dt[5]),
         dXQ, dXV, dXK, deta,
         None,
     )

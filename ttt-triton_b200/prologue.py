@@ -36,6 +36,17 @@ def rope_tables(freqs_cis, L, F):
     return cos[:L].to(torch.float32).contiguous(), sin[:L].to(torch.float32).contiguous()
 
 
+_ZERO_ROWS = {}
+
+
+def _zero_rows(shape, like):
+    """A cached all-zero padding block (never written: torch.cat only reads it)."""
+    key = (tuple(shape), like.dtype, like.device)
+    if key not in _ZERO_ROWS:
+        _ZERO_ROWS[key] = torch.zeros(shape, dtype=like.dtype, device=like.device)
+    return _ZERO_ROWS[key]
+
+
 def concat_projections(wq, bq, wk, bk, wv, bv, wu, bu, lr_w, lr_b):
     """The five projections as one [prologue_ld, W] weight and bias (zero padding rows)."""
     NH = lr_w.shape[0]
@@ -48,8 +59,8 @@ def concat_projections(wq, bq, wk, bk, wv, bv, wu, bu, lr_w, lr_b):
     ws = [wq, wk, wv, wu, lr_w.reshape(NH, Win)]
     bs = [bq, bk, bv, bu, lr_b.reshape(NH)]
     if pad:
-        ws.append(wq.new_zeros(pad, Win))
-        bs.append(bq.new_zeros(pad))
+        ws.append(_zero_rows((pad, Win), wq))
+        bs.append(_zero_rows((pad,), bq))
     return torch.cat(ws, 0), torch.cat(bs, 0), NH, F
 
 
