@@ -52,7 +52,10 @@ constexpr int OFF_Z1 = OFF_Z2B + C * F * 4;     // fp32 [C][ZLD]
 // Layout of a CTA of NW warps (inner width FFW = 32 * NW).
 template <int NW_>
 struct Bwd {
-  static constexpr int NW = NW_, NTHREADS = 32 * NW, FFW = 32 * NW;
+  // NW warps own 32 hidden units each (the MMA phases); the row phases (16 threads per token)
+  // run on NR >= NW warps: at FF = 64 two more warps join them, which halves the passes over
+  // the mini-batch's tokens (registers allow 4 warps per CTA at 2 CTAs per SM)
+  static constexpr int NW = NW_, NR = NW_ > 4 ? NW_ : 4, NTHREADS = 32 * NR, FFW = 32 * NW;
   static constexpr int ZLD = FFW + 8;                        // fp32 row stride of the staged Z1 / Z1bar
   static constexpr int OFF_Z1B = OFF_Z1 + C * ZLD * 4;       // fp32 [C][ZLD]
   static constexpr int STAGE = OFF_Z1B + C * ZLD * 4;        // 50688 bytes for FF = 256
@@ -74,6 +77,7 @@ struct Bwd {
   static constexpr uint32_t TMEM_COLS = NW > 4 ? 512 : 256;
   static constexpr int CTAS_PER_SM = NW > 4 ? 1 : 2;
   static_assert(SMEM * CTAS_PER_SM <= 227 * 1024, "shared memory budget");
+  static_assert(PART >= NR * 2 * F * 4, "the gamma / beta reduction reuses one partial set");
   static_assert(OFF_PA % 128 == 0 && OFF_G % 128 == 0 && STAGE % 128 == 0, "tile alignment");
 };
 
@@ -152,10 +156,10 @@ __device__ __forceinline__ void put_part(float* pw, const float (*X)[4], int g, 
 }
 
 template <typename T, int NW>
-__global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kernel(MlpBwdParams p) {
+__global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kernel(MlpBwdParams p) {
   using H = Half2<T>;
   using L = Bwd<NW>;
-  constexpr int NTHREADS = L::NTHREADS, FFW = L::FFW, ZLD = L::ZLD, STAGE = L::STAGE;
+  constexpr int NTHREADS = L::NTHREADS, NR = L::NR, FFW = L::FFW, ZLD = L::ZLD, STAGE = L::STAGE;
   constexpr int OFF_Z1B = L::OFF_Z1B, OFF_PA = L::OFF_PA, OFF_PB = L::OFF_PB, OFF_G = L::OFF_G, OFF_EG = L::OFF_EG;
   constexpr int OFF_DZB = L::OFF_DZB, OFF_DZ2 = L::OFF_DZ2, OFF_DETAP = L::OFF_DETAP, OFF_DP1P = L::OFF_DP1P;
   constexpr int OFF_DP1 = L::OFF_DP1, OFF_DE = L::OFF_DE, OFF_DE2 = L::OFF_DE2, OFF_DB2 = L::OFF_DB2;
@@ -189,7 +193,7 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
   tmem_fence_after();
   const uint32_t tS1 = tmem_lane_addr(tmem_base_sh, warp, 256 * (warp >> 2));
   const uint32_t tS2 = tS1 + 64, tD1 = tS1 + 128, tD2 = tS1 + 192;
-  {
+  if (warp < NW) {  // the MMA warps' state slices (hidden units fb..fb+31)
     float S1[2][8][4], S2[4][4][4];
     w1_io<2, FFW>(S1, const_cast<float*>(p.W1_last + s * F * FFW), fb, g, t, false);
     w2_io(S2, const_cast<float*>(p.W2_last + s * FFW * F), fb, g, t, false);
@@ -309,7 +313,11 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
     }
     __syncthreads();
 
-    // ---------------- M1
+    // ---------------- M1 (the NW MMA warps)
+    // carried from M1 into M2 in the MMA warps' registers
+    uint32_t X2t[2][4], Zbp[4][2], Zbt[2][4];
+    float GP[4][4], dX2[4][4], dZ1[4][4];
+    if (warp < NW) {
     const float* Z1s = reinterpret_cast<const float*>(st + OFF_Z1);
     const float* Z1bs = reinterpret_cast<const float*>(st + OFF_Z1B);
     const float eg0 = (float)E[(C - 1) * C + g], eg1 = (float)E[(C - 1) * C + g + 8];
@@ -326,8 +334,7 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
     // X2 = gelu(Z1), GP = gelu'(Z1) = gelu_bwd(Z1) on the warp's hidden units. GP is
     // rounded to 16 bits as the forward rounded it, so G1 (and with it the W1 reversal)
     // reproduces the forward's values.
-    uint32_t X2p[4][2], X2t[2][4];
-    float GP[4][4];
+    uint32_t X2p[4][2];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 z01 = *reinterpret_cast<const float2*>(Z1s + g * ZLD + fb + 8 * j + 2 * t);
@@ -447,8 +454,8 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
       }
     }
     // X2bar = gelu(Z1bar); dZ1bar = dX2bar * gelu'(Z1bar); A2_w = X2bar X2^T; dX2 = dA2^T X2bar
-    uint32_t XBt[2][4], Zbp[4][2], Zbt[2][4];
-    float A2[2][4], dX2[4][4];
+    uint32_t XBt[2][4];
+    float A2[2][4];
     {
       uint32_t XBp[4][2];
 #pragma unroll
@@ -596,7 +603,6 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
       put_part<false>(PB + warp * C * PLD, KD, g, t);
     }
     // dG1 += -P1^T dZ1bar; dH = dG1 * gelu_bwd(Z1); dZ1 = dG1 * H * gelu_bwd'(Z1)
-    float dZ1[4][4];
     uint32_t dHp[4][2];
     {
       uint32_t aPT[4];
@@ -724,6 +730,7 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
         DE[warp * C + g + 8] = de1;
       }
     }
+    }  // M1
     __syncthreads();
 
     // ---------------- R2: dG2 -> backward of G2 = ln_fused_l2_bwd(Z2, XV - XK); d_eta, dP1
@@ -798,7 +805,8 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
     }
     __syncthreads();
 
-    // ---------------- M2
+    // ---------------- M2 (the NW MMA warps)
+    if (warp < NW) {
     // dX2 += dZ2 W2_n^T ; dW2^T += dZ2^T X2 ; db2 += 1^T (dZ2bar + dZ2) (warp w: features
     // 8fw..8fw+7 for fw = w, w + NW, ..)
     {
@@ -949,6 +957,7 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
         DB1[j][1] += acc[1];
       }
     }
+    }  // M2
     __syncthreads();
 
     // ---------------- R3: dXQ = dO + sum of partials, dXK = sum of partials - dXV
@@ -974,7 +983,7 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
   __syncthreads();
 
   // ---- outputs of the whole walk: dW1, dW2, db1, db2 (fp32), per-stream gamma / beta partials
-  {
+  if (warp < NW) {
     float D1[2][8][4];
     slice_ld(tD1, &D1[0][0][0]);
     w1_io<2, FFW>(D1, p.dW1 + s * F * FFW, fb, g, t, true);
@@ -982,7 +991,7 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
     slice_ld(tD2, &D2[0][0][0]);
     w2_io(D2, p.dW2 + s * FFW * F, fb, g, t, true);
   }
-  if (g == 0) {
+  if (warp < NW && g == 0) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       p.db1[s * FFW + fb + 8 * j + 2 * t] = DB1[j][0];
@@ -995,7 +1004,7 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
     dgam[j] += __shfl_xor_sync(0xffffffffu, dgam[j], 16);
     dbet[j] += __shfl_xor_sync(0xffffffffu, dbet[j], 16);
   }
-  float* RED = PA;  // [NW][2][F]
+  float* RED = PA;  // [NR][2][F]
   if ((lane & 16) == 0) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -1010,7 +1019,7 @@ __global__ void __launch_bounds__(32 * NW, Bwd<NW>::CTAS_PER_SM) mlp_bwd_tc_kern
     const int which = e / F, f = e % F;
     float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) acc += RED[(w * 2 + which) * F + f];
+    for (int w = 0; w < NR; ++w) acc += RED[(w * 2 + which) * F + f];
     (which == 0 ? p.d_ln_w : p.d_ln_b)[s * F + f] = acc;
   }
   // every warp's TMEM accesses are complete (the loads / stores above waited); free the columns
