@@ -82,3 +82,21 @@ def test_batch_copies_match_tile_forward_and_backward():
     (gp,) = torch.autograd.grad(out, p, g)
     (gr,) = torch.autograd.grad(ref, p, g)
     assert torch.allclose(gp, gr, rtol=1e-12, atol=1e-12)
+
+
+def test_linear_act_matches_linear():
+    """linear_act (the input projection with K padded to 8, the bias carried by the first
+    padding column) equals nn.Linear: output, weight and bias gradients."""
+    from forecaster import linear_act
+
+    torch.manual_seed(2)
+    for k in (7, 5, 8):
+        x = torch.randn(3, 11, k, dtype=torch.float64)
+        lin = torch.nn.Linear(k, 16).double()
+        y, ref = linear_act(x, lin.weight, lin.bias, torch.float64), lin(x)
+        g = torch.randn_like(ref)
+        got = torch.autograd.grad(y, (lin.weight, lin.bias), g)
+        want = torch.autograd.grad(ref, (lin.weight, lin.bias), g)
+        assert torch.allclose(y, ref, rtol=1e-12, atol=1e-12)
+        for a, b in zip(got, want):
+            assert torch.allclose(a, b, rtol=1e-12, atol=1e-12)

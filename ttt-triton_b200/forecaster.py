@@ -135,15 +135,21 @@ class TTTMLPLayer(nn.Module):
 
 def linear_act(x, weight, bias, dt):
     """nn.Linear in the activation dtype dt (what the reference's autocast runs), with the
-    input width zero-padded to a multiple of 8 so that the library GEMMs take their aligned
+    input width padded to a multiple of 8 so that the library GEMMs take their aligned
     tensor-core paths (the 7-channel input projection and its weight gradient otherwise fall
-    back to unaligned fp32 kernels)."""
+    back to unaligned fp32 kernels). The first padding column carries the bias: the input
+    gets a column of ones and the weight the bias as that column, so the bias gradient comes
+    out of the weight-gradient GEMM instead of a separate reduction over all B * L rows."""
     k = x.shape[-1]
     pad = -k % 8
-    if pad:
-        x = Fn.pad(x, (0, pad))
-        weight = Fn.pad(weight, (0, pad))
-    return Fn.linear(x.to(dt), weight.to(dt), bias.to(dt))
+    if not pad:
+        return Fn.linear(x.to(dt), weight.to(dt), bias.to(dt))
+    x = Fn.pad(x, (0, 1), value=1.0)
+    cols = [weight, bias[:, None]]
+    if pad > 1:
+        x = Fn.pad(x, (0, pad - 1))
+        cols.append(weight.new_zeros(weight.shape[0], pad - 1))
+    return Fn.linear(x.to(dt), torch.cat(cols, 1).to(dt))
 
 
 class TTTForecaster(nn.Module):
