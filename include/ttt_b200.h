@@ -164,7 +164,7 @@ int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_gro
  * ttt_mlp_fwd writes them, NS = ceil(NC / memo_segment_size). Tensor-core path: CS = 16,
  * F = 64, FF = 256 or 64, NS <= 64. The backward gives dXQW, dXU and the summary part of dXK
  * (the cached read-outs and earlier summaries carry no gradient, as in the reference).
- * Activations, gradients, W1_memo and W2_memo must be 16-byte aligned (TTT_ERR_ALIGN).
+ * Activations, gradients and the memo states must be 16-byte aligned (TTT_ERR_ALIGN).
  * Scratch: ttt_memo_mix_scratch_bytes() bytes, 16-byte aligned; the forward leaves the
  * memo states' 16-bit operand copies and the segment summaries in it, and a backward given
  * that same scratch with scratch_prepped = 1 reuses them instead of preparing them again.

@@ -74,14 +74,17 @@ struct Mix {
   static constexpr int OFF_G = OFF_X2 + X2_BYTES;        // fp32 [128][GLD]: mixing weights g_j(t)
   static constexpr int OFF_DG = OFF_G + ROWS * GLD * 4;  // fp32 [128][GLD]: dg_j(t) (backward)
   static constexpr int OFF_LN = OFF_DG + ROWS * GLD * 4; // fp32 [2][64]: LayerNorm weight, bias
-  static constexpr int OFF_B1 = OFF_LN + 2 * F * 4;      // fp32 [3][FF]: b1_j ring (state j in slot j % 3)
-  static constexpr int OFF_B2 = OFF_B1 + 3 * FF * 4;     // fp32 [3][64]: b2_j ring
+  // memo-state biases: FF = 64 stages every state's b1, b2 once per CTA (state j in slot j);
+  // FF = 256 keeps a 3-slot ring (state j in slot j % 3) refilled two states ahead
+  static constexpr int NBIAS = SPEC ? NS_MAX : 3;
+  static constexpr int OFF_B1 = OFF_LN + 2 * F * 4;          // fp32 [NBIAS][FF]: b1_j
+  static constexpr int OFF_B2 = OFF_B1 + NBIAS * FF * 4;     // fp32 [NBIAS][64]: b2_j
   // fp32 [NS_MAX][64]: the stream's segment summaries, staged once per CTA; for FF = 256 in
   // the upper half of the X2 region (free before the first read-out and, reloaded, in the
   // backward tail), for FF = 64 in a region of its own
   static constexpr bool SUM_IN_X2 = FF == 256;
-  static constexpr int OFF_SUM = SUM_IN_X2 ? OFF_X2 + 36864 : OFF_B2 + 3 * F * 4;
-  static constexpr int SMEM = (SUM_IN_X2 ? OFF_B2 + 3 * F * 4 : OFF_SUM + NS_MAX * F * 4) + 1024;  // + alignment slack
+  static constexpr int OFF_SUM = SUM_IN_X2 ? OFF_X2 + 36864 : OFF_B2 + NBIAS * F * 4;
+  static constexpr int SMEM = (SUM_IN_X2 ? OFF_B2 + NBIAS * F * 4 : OFF_SUM + NS_MAX * F * 4) + 1024;  // + alignment slack
   // tensor memory: Z1 buffers at columns [0, NX * FF), Z2 buffers at [Z2_COL, + NX * 64)
   static constexpr int Z2_COL = FF == 256 ? 256 : NX * FF;
   static constexpr uint32_t TMEM_COLS = FF == 256 ? 512 : 256;
@@ -94,7 +97,7 @@ struct Mix {
   static_assert(!SPEC || FF == 64, "the warp-specialised GELU covers 64 columns");
   static_assert(!SUM_IN_X2 || X2_BYTES >= 36864 + NS_MAX * F * 4, "summaries share the X2 region");
   static_assert(ROWS * RED_LD * 4 <= (SUM_IN_X2 ? 36864 : X2_BYTES), "d-summary scratch below the summaries");
-  static_assert(OFF_SUM % 16 == 0, "16-byte aligned summary rows");
+  static_assert(OFF_SUM % 16 == 0 && OFF_B1 % 16 == 0 && OFF_B2 % 16 == 0, "16-byte aligned staged rows");
 };
 
 struct Maps {
@@ -267,8 +270,8 @@ __global__ void __launch_bounds__(Mix<FF>::NT, 1) memo_mix_kernel(MemoMixParams 
   auto b_gd = [&](int j) { return smem_u32(&bars[BAR_GD + j % NX]); };
   // Thread groups. Row threads own one token each (mixing weights, read-out, tail). In the
   // warp-specialised schedule the GELU group takes warps 0-3, which the warp schedulers favour:
-  // the GELU is on the chain of dependent products, the read-out is not. The b1 ring is filled
-  // by the 128 threads from GELU_T0.
+  // the GELU is on the chain of dependent products, the read-out is not. At FF = 256 the bias
+  // ring is refilled by the 128 threads from GELU_T0 (warps 4-7).
   constexpr int ROW_T0 = kSpecialised ? 128 : 0, GELU_T0 = 128 - ROW_T0;
   constexpr int kIssuer = kSpecialised ? 256 : 0;  // thread that issues the products
   const bool row_thread = (unsigned)(tid - ROW_T0) < (unsigned)ROWS;
@@ -309,19 +312,28 @@ __global__ void __launch_bounds__(Mix<FF>::NT, 1) memo_mix_kernel(MemoMixParams 
       tma_load_2d(dst + a * (F * 64 * 2), &maps.w2, 64 * a, (int)((s * p.NS + j) * F), b_w2(j));
     last_w2_sh[j % NB2] = j;
   };
-  // Biases of state j into ring slot j % 3 (plain loads; a barrier publishes them).
+  auto bslot = [&](int j) { return kSpecialised ? j : j % 3; };  // bias slot of state j
+  // Biases of state j into slot bslot(j) (plain loads; a barrier publishes them).
   auto load_bias = [&](int j) {  // all threads, blocking (setup)
-    float* b1s = reinterpret_cast<float*>(smem + OFF_B1) + (j % 3) * FF;
-    float* b2s = reinterpret_cast<float*>(smem + OFF_B2) + (j % 3) * F;
+    float* b1s = reinterpret_cast<float*>(smem + OFF_B1) + bslot(j) * FF;
+    float* b2s = reinterpret_cast<float*>(smem + OFF_B2) + bslot(j) * F;
     for (int i = tid; i < FF; i += NT) b1s[i] = __ldg(p.b1_memo + (s * p.NS + j) * FF + i);
     if (tid < F) b2s[tid] = __ldg(p.b2_memo + (s * p.NS + j) * F + tid);
   };
-  // From state 2 on the biases are fetched into registers two states ahead (*_fetch) and
-  // written to their ring slot later (*_put), so the global-load latency stays off the
-  // critical path. Slot (j + 2) % 3 is written after the barrier that ends state j, when
+  // Every state's biases of the stream at once (warp-specialised schedule; 16-byte copies)
+  auto stage_biases = [&]() {
+    const float4* s1 = reinterpret_cast<const float4*>(p.b1_memo + s * p.NS * FF);
+    const float4* s2 = reinterpret_cast<const float4*>(p.b2_memo + s * p.NS * F);
+    float4* d1 = reinterpret_cast<float4*>(smem + OFF_B1);
+    float4* d2 = reinterpret_cast<float4*>(smem + OFF_B2);
+    for (int i = tid; i < nstate * (FF / 4); i += NT) d1[i] = s1[i];
+    for (int i = tid; i < nstate * (F / 4); i += NT) d2[i] = s2[i];
+  };
+  // FF = 256 ring: from state 2 on the biases are fetched into registers two states ahead
+  // (*_fetch) and written to their slot later (*_put), so the global-load latency stays off
+  // the critical path. Slot (j + 2) % 3 is written after the barrier that ends state j, when
   // every reader of its previous occupant (state j - 1) is done; the barrier of state j + 1
-  // publishes it. b1 is read by the GELU warps only; b2 by the read-out warps (which own its
-  // ring in the warp-specialised schedule). i = this thread's index within its warp group.
+  // publishes it. i = this thread's index within warps 4-7.
   float pb[3];  // b1[i], b1[i + 128], b2[i] of the fetched state
   auto b1_fetch = [&](int j, int i) {
     pb[0] = i < FF ? __ldg(p.b1_memo + (s * p.NS + j) * FF + i) : 0.f;
@@ -400,8 +412,12 @@ __global__ void __launch_bounds__(Mix<FF>::NT, 1) memo_mix_kernel(MemoMixParams 
     for (int c = 0; c < F; c += 8) ld_row8(XU + (tok0 + r) * F + c, xu + c);
   }
   stage_summaries();
-  if (nstate > 0) load_bias(0);
-  if (nstate > 1) load_bias(1);
+  if constexpr (kSpecialised) {
+    stage_biases();
+  } else {
+    if (nstate > 0) load_bias(0);
+    if (nstate > 1) load_bias(1);
+  }
   __syncthreads();  // summaries and the first two states' biases in shared memory
 
   // mixing weights g_j(t), j = 0..seg_r (row threads, one token each; seg_r is the row's own
@@ -481,7 +497,7 @@ __global__ void __launch_bounds__(Mix<FF>::NT, 1) memo_mix_kernel(MemoMixParams 
   // warp % 4, into the K-major swizzled X2 tiles
   auto gelu_chunks = [&](int j, int c_begin, int c_end) {
     const int row = 32 * (warp & 3) + lane;
-    const float* b1 = reinterpret_cast<const float*>(smem + OFF_B1) + (j % 3) * FF;
+    const float* b1 = reinterpret_cast<const float*>(smem + OFF_B1) + bslot(j) * FF;
 #pragma unroll 1
     for (int c4 = c_begin; c4 < c_end; ++c4) {
       const int col = 32 * c4;
@@ -506,7 +522,7 @@ __global__ void __launch_bounds__(Mix<FF>::NT, 1) memo_mix_kernel(MemoMixParams 
   // The same for FF = 64 in one pass: both 32-column loads issued before the wait
   auto gelu64 = [&](int j) {
     const int row = 32 * (warp & 3) + lane;
-    const float* b1 = reinterpret_cast<const float*>(smem + OFF_B1) + (j % 3) * FF;
+    const float* b1 = reinterpret_cast<const float*>(smem + OFF_B1) + bslot(j) * FF;
     float z[64];
     tmem_ld32(tmem_lane_addr(tZ1 + (j % NX) * FF, warp, 0), z);
     tmem_ld32(tmem_lane_addr(tZ1 + (j % NX) * FF, warp, 32), z + 32);
@@ -543,7 +559,7 @@ __global__ void __launch_bounds__(Mix<FF>::NT, 1) memo_mix_kernel(MemoMixParams 
     }
     // product 2 of j no longer reads its W2 buffer: fetch state j + NB2 into it
     if (tid == ROW_T0 && j + NB2 < nstate && !abort_sh) load_w2(j + NB2);
-    const float* b2 = reinterpret_cast<const float*>(smem + OFF_B2) + (j % 3) * F;
+    const float* b2 = reinterpret_cast<const float*>(smem + OFF_B2) + bslot(j) * F;
     float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < F; c += 2) {
@@ -620,23 +636,15 @@ __global__ void __launch_bounds__(Mix<FF>::NT, 1) memo_mix_kernel(MemoMixParams 
       if (lane == 0) wait(b_p1(j), j / NX);
       __syncwarp();
       tmem_fence_after();
-      if (j + 2 < nstate) b1_fetch(j + 2, tid - GELU_T0);
       gelu64(j);
       fence_proxy_async();  // X2 stores -> visible to the tensor cores
       tmem_fence_before();  // Z1 loads complete before the arrival
       __syncwarp();
       if (lane == 0) mbar_arrive(b_gd(j));
-      named_bar_sync(1, 128);  // every GELU warp is past state j: b1 slot (j + 2) % 3 is free
-      if (j + 2 < nstate) b1_put(j + 2, tid - GELU_T0);
     }
   } else if (warp < 8) {
-    // row group: the read-outs, following the product-2 commits; it owns the b2 ring
-    for (int j = 0; j < nstate; ++j) {
-      if (j + 2 < nstate) b2_fetch(j + 2, r);
-      readout(j, true);
-      if (j + 2 < nstate) b2_put(j + 2, r);
-      named_bar_sync(2, 128);  // slot (j + 2) % 3 written; slot j % 3 read
-    }
+    // row group: the read-outs, following the product-2 commits
+    for (int j = 0; j < nstate; ++j) readout(j, true);
   } else if (tid == kIssuer) {
     // issuer: once the GELU of j is done, product 2 of j (into Z2 buffer j % 2, free once the
     // read-out of j - 2 has taken it out) and product 1 of j + 2 (into the Z1 buffer the GELU
@@ -893,7 +901,8 @@ extern "C" int ttt_memo_mix_fwd(int B, int NH, int NC, int CS, int F, int FF, in
               TTT_ERR_NULL, "%s: NULL pointer argument", who);
   TTT_REQUIRE(aligned16(XQW) && aligned16(XQ) && aligned16(XK) && aligned16(XU) && aligned16(scratch), TTT_ERR_ALIGN,
               "%s: activations and scratch must be 16-byte aligned", who);
-  TTT_REQUIRE(aligned16(W1_memo) && aligned16(W2_memo), TTT_ERR_ALIGN, "%s: memo states must be 16-byte aligned", who);
+  TTT_REQUIRE(aligned16(W1_memo) && aligned16(W2_memo) && aligned16(b1_memo) && aligned16(b2_memo), TTT_ERR_ALIGN,
+              "%s: memo states must be 16-byte aligned", who);
   const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size, FF);
   TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "%s: scratch has %zu bytes, needs %zu", who, scratch_bytes, need);
   TTT_REQUIRE(aligned16(out), TTT_ERR_ALIGN, "%s: out must be 16-byte aligned", who);
@@ -930,7 +939,8 @@ extern "C" int ttt_memo_mix_bwd(int B, int NH, int NC, int CS, int F, int FF, in
               TTT_ERR_NULL, "%s: NULL pointer argument", who);
   TTT_REQUIRE(aligned16(XQW) && aligned16(XQ) && aligned16(XK) && aligned16(XU) && aligned16(scratch), TTT_ERR_ALIGN,
               "%s: activations and scratch must be 16-byte aligned", who);
-  TTT_REQUIRE(aligned16(W1_memo) && aligned16(W2_memo), TTT_ERR_ALIGN, "%s: memo states must be 16-byte aligned", who);
+  TTT_REQUIRE(aligned16(W1_memo) && aligned16(W2_memo) && aligned16(b1_memo) && aligned16(b2_memo), TTT_ERR_ALIGN,
+              "%s: memo states must be 16-byte aligned", who);
   const size_t need = ttt_memo_mix_scratch_bytes(B, NH, NC, memo_segment_size, FF);
   TTT_REQUIRE(scratch_bytes >= need, TTT_ERR_SCRATCH, "%s: scratch has %zu bytes, needs %zu", who, scratch_bytes, need);
   MemoMixParams p = {};
