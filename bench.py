@@ -527,9 +527,12 @@ def run_forecaster(args, w, rank, world, local_rank):
     launches = _lib.launch_count() - n0
     clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1)
-    # dominant kernel (largest share of the step's launch list): one layer's memo-mixing
-    # backward at the per-rank shape
-    kern_ms, kern_flops = forecaster_memo_bwd_ms(w, b_rank, dev)
+    # dominant kernel (largest share of the step's launch list, profiles/
+    # launches_forecaster_config4.md): one layer's F x F scan backward at the per-rank shape
+    kern_ms, kern_flops = forecaster_mlp_bwd_ms(w, b_rank, dev)
+    # its DRAM traffic from the ncu capture at batch 128 (profiles/mlp_bwd_tc_fxf_config4.md),
+    # scaled by the streams (traffic grows in proportion to them)
+    kern_traffic = FXF_BWD_TRAFFIC_B128 * b_rank / 128
     # end to end: each step's windows copied from pinned host memory, loss read back
     host = [(x.pin_memory(), y.pin_memory()) for x, y in pool]
     xb, yb = torch.empty_like(dev_pool[0][0]), torch.empty_like(dev_pool[0][1])
@@ -566,8 +569,10 @@ def run_forecaster(args, w, rank, world, local_rank):
                    "samples_per_s": w["B"] / (ms_step / 1e3),
                    "l2": "activations larger than L2 (no flush)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
-                     "frac": achieved / bf16, "traffic": None, "peak_source": src,
-                     "kernel": "memo_mix backward (one layer)", "kernel_ms": kern_ms, "kernel_flops": kern_flops},
+                     "frac": achieved / bf16, "traffic": kern_traffic,
+                     "traffic_source": "profiles/mlp_bwd_tc_fxf_config4.md (batch 128, scaled)",
+                     "peak_source": src, "kernel": "mlp_bwd F x F scan backward (one layer)",
+                     "kernel_ms": kern_ms, "kernel_flops": kern_flops},
         "e2e": {"value": tokens / (e2e_ms / args.steps / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": (xb.numel() * xb.element_size() + yb.numel() * yb.element_size()),
                 "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms / args.steps},
@@ -580,30 +585,40 @@ def run_forecaster(args, w, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
-def forecaster_memo_bwd_ms(w, b_rank, dev):
-    """CUDA-event time of one layer's memo-mixing backward (F x F inner MLP, the layer's memo
-    segments) at the per-rank shape, and its useful FLOPs: every token of segment i reads out
-    the i earlier memo states, 2 * 2 * F * FF FLOPs each (algorithmic() of memo_mix_c3)."""
+# DRAM bytes (read + write) of one F x F scan-backward launch at batch 128 (ncu capture in
+# profiles/mlp_bwd_tc_fxf_config4.md)
+FXF_BWD_TRAFFIC_B128 = 286.894336e6 + 70.784e6
+
+
+def forecaster_mlp_bwd_ms(w, b_rank, dev):
+    """CUDA-event time of one layer's F x F scan backward (the stored-pre-activation
+    tensor-core path the forecaster's TritonMLP takes) at the per-rank shape, and its useful
+    FLOPs: 38 F FF + 12 CS FF + 12 CS F per token (algorithmic())."""
     import _core
     import synthetic as S
 
-    NC = w["L"] // CS
-    d = S.make_memo_inputs(b_rank, w["NH"], NC, CS, w["F"], w["FF"], w["memo"], dtype=torch.bfloat16, device=dev,
-                           seed=5)
-    dO = S.make_upstream((b_rank, w["NH"], NC, CS, w["F"]), device=dev, seed=6, dtype=torch.bfloat16)
+    NC, F, FF = w["L"] // CS, w["F"], w["FF"]
+    d = S.make_mlp_inputs(b_rank, w["NH"], NC, CS, F, FF, dtype=torch.bfloat16, device=dev, seed=5)
+    dO = S.make_upstream((b_rank, w["NH"], NC, CS, F), device=dev, seed=6, dtype=torch.bfloat16)
+    _, last, ck, _, zs = _core.mlp_forward(d["ln_w"], d["ln_b"], d["W1"], d["b1"], d["W2"], d["b2"], d["XQ"], d["XV"],
+                                           d["XK"], d["eta"], w["ckpt"], w["memo"], for_backward=True)
     stream = torch.cuda.current_stream(dev)
+
+    def bwd():
+        _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"], saved=zs,
+                           W1_last=last[0], W2_last=last[2])
+
+    bwd()
+    torch.cuda.synchronize()
     tot = 0.0
     for _ in range(3):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        _core.memo_mix_backward(*(d[k] for k in MEMO), w["memo"], dO)
+        bwd()
         e1.record(stream)
         torch.cuda.synchronize()
         tot += e0.elapsed_time(e1)
-    M = w["memo"]
-    NS = -(-NC // M)
-    mean_i = sum(i * (min((i + 1) * M, NC) - i * M) for i in range(NS)) / NC
-    flops = mean_i * 4 * w["F"] * w["FF"] * b_rank * w["NH"] * w["L"]
+    flops = (38 * F * FF + 12 * CS * FF + 12 * CS * F) * b_rank * w["NH"] * w["L"]
     return tot / 3, flops
 
 
