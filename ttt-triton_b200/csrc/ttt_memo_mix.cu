@@ -774,6 +774,483 @@ __global__ void __launch_bounds__(Mix<FF>::NT, 1) memo_mix_kernel(MemoMixParams 
   if (warp == 0) tmem_dealloc(tmem_base_sh, TMEM_COLS);
 }
 
+// ------------------------------------------------------------- mix, two CTAs per SM (FF = 64)
+// The F x F layer with at most NSC memo states per stream (the forecaster's layers) runs two
+// 8-warp CTAs per SM, so one CTA's dependency chain (GELU -> product 2 -> read-out) overlaps
+// the other's. Warps 0-3 compute the GELU into X2 buffer j % 2 and arrive on a GELU-done
+// barrier; warps 4-7 own one token each (mixing weights, read-out, tail) and keep their
+// read-out accumulators in tensor memory, which keeps them within the 128 registers that two
+// CTAs per SM allow; lane 0 of warp 4 issues the products: product 2 of j once the GELU of j
+// is done (Z2 is single-buffered: after the read-out of j - 1 took it out) and product 1 of
+// j + 1 (W1 has had a state to land). Product 1 of j + 1 is committed after product 2 of j by
+// the same thread, so its completion also frees X2 buffer (j + 1) % 2.
+struct Mix2 {
+  static constexpr int FF = 64, NT = 256, NSC = 16, GLD2 = NSC + 1;
+  static constexpr int OFF_W1 = OFF_XQ + ROWS * F * 2;  // 2 x [64][64]: W1_j^T (state j in j % 2)
+  static constexpr int OFF_W2 = OFF_W1 + 2 * FF * F * 2;  // 2 x [64][64]: W2_j^T
+  static constexpr int X2_BUF = ROWS * FF * 2;
+  // 2 x [128][64] X2; the backward tail's d-summary scratch (fp32 [128][64], columns swizzled
+  // by the row) reuses it
+  static constexpr int OFF_X2 = OFF_W2 + 2 * F * FF * 2;
+  static constexpr int OFF_G = OFF_X2 + 2 * X2_BUF;       // fp32 [128][GLD2]: g_j(t)
+  static constexpr int OFF_DG = OFF_G + ROWS * GLD2 * 4;  // fp32 [128][GLD2]: dg_j(t)
+  static constexpr int OFF_LN = OFF_DG + ROWS * GLD2 * 4; // fp32 [2][64]
+  static constexpr int OFF_B1 = OFF_LN + 2 * F * 4;       // fp32 [NSC][64]: every state's b1
+  static constexpr int OFF_B2 = OFF_B1 + NSC * FF * 4;    // fp32 [NSC][64]: every state's b2
+  static constexpr int OFF_SUM = OFF_B2 + NSC * F * 4;    // fp32 [NSC][64]: segment summaries
+  static constexpr int SMEM = OFF_SUM + NSC * F * 4 + 1024;  // + alignment slack
+  // tensor memory: Z1 buffers [0, 128), Z2 [128, 192), the row threads' accumulators [192, 256)
+  static constexpr uint32_t TMEM_COLS = 256, W_BYTES = FF * F * 2;
+  static_assert(OFF_W1 % 1024 == 0 && OFF_W2 % 1024 == 0 && OFF_X2 % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+  static_assert(OFF_G % 16 == 0 && OFF_B1 % 16 == 0 && OFF_B2 % 16 == 0 && OFF_SUM % 16 == 0, "16-byte aligned rows");
+  static_assert(ROWS * F * 4 <= 2 * X2_BUF, "d-summary scratch fits the X2 buffers");
+  static_assert(2 * (SMEM + 2048) <= 228 * 1024, "two CTAs per SM");
+};
+
+template <typename T, bool BWD>
+__global__ void __launch_bounds__(Mix2::NT, 2) memo_mix2_kernel(MemoMixParams p, const __grid_constant__ Maps maps) {
+  using H = Half2<T>;
+  using L = Mix2;
+  constexpr int FF = L::FF, NT = L::NT, GLD2 = L::GLD2;
+  constexpr uint32_t W_BYTES = L::W_BYTES;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  __shared__ uint32_t tmem_base_sh;
+  // mbarriers: XQ landed; product 1 into Z1 buffer b complete; product 2 complete; W1 / W2
+  // buffer b landed; Z2 read out by the four row warps; X2 buffer b written (and Z1 buffer b
+  // read) by the four GELU warps
+  constexpr int BAR_XQ = 0, BAR_P1 = 1, BAR_P2 = 3, BAR_W1 = 4, BAR_W2 = 6, BAR_ZF = 8, BAR_GD = 9, NBARS = 11;
+  __shared__ __align__(8) uint64_t bars[NBARS];
+  __shared__ int last_w_sh[4];   // last state loaded into W1 buffers 0, 1 and W2 buffers 0, 1 (draining)
+  __shared__ int commits_sh[3];  // product-1 commits per Z1 buffer, product-2 commits (draining)
+  __shared__ int abort_sh;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  long long s;
+  int seg_first, seg_last, tile;
+  decode_block(p, s, seg_first, seg_last, tile);
+  const int n0 = seg_first * p.M, n1 = min((seg_last + 1) * p.M, p.NC);
+  const int seg_rows = (n1 - n0) * C;
+  const int row0 = tile * ROWS;
+  if (row0 >= seg_rows) return;  // empty tail tile (uniform over the CTA)
+  const long long tok0 = (s * p.NC + n0) * C + row0;
+  const int nrows = min(ROWS, seg_rows - row0);
+  const int seg_tok = p.M * C;
+  const T* XQW = reinterpret_cast<const T*>(p.XQW);
+  const T* XU = reinterpret_cast<const T*>(p.XU);
+
+  if (seg_last == 0) {  // segment 0 passes through (forward: out = XQW; backward: dXQW = dOut, dXU = 0)
+    const T* src = reinterpret_cast<const T*>(BWD ? p.dOut : p.XQW);
+    T* dst = reinterpret_cast<T*>(BWD ? p.dXQW : p.out);
+    for (int i = tid; i < nrows * F; i += NT) dst[tok0 * F + i] = src[tok0 * F + i];
+    if (BWD)
+      for (int i = tid; i < nrows * F; i += NT) reinterpret_cast<T*>(p.dXU)[tok0 * F + i] = H::from_float(0.f);
+    return;
+  }
+
+  const uint32_t sXQ = smem_u32(smem + OFF_XQ), sW1 = smem_u32(smem + L::OFF_W1), sW2 = smem_u32(smem + L::OFF_W2);
+  const uint32_t sX2 = smem_u32(smem + L::OFF_X2);
+  float* G = reinterpret_cast<float*>(smem + L::OFF_G);
+  float* DG = reinterpret_cast<float*>(smem + L::OFF_DG);
+  float* LN = reinterpret_cast<float*>(smem + L::OFF_LN);
+  float* SUM = reinterpret_cast<float*>(smem + L::OFF_SUM);
+  // barrier of state j (its phase there: j / 2 for the double buffers, j for P2 and ZF)
+  const uint32_t b_xq = smem_u32(&bars[BAR_XQ]), b_p2 = smem_u32(&bars[BAR_P2]), b_zf = smem_u32(&bars[BAR_ZF]);
+  auto b_p1 = [&](int j) { return smem_u32(&bars[BAR_P1 + (j & 1)]); };
+  auto b_w1 = [&](int j) { return smem_u32(&bars[BAR_W1 + (j & 1)]); };
+  auto b_w2 = [&](int j) { return smem_u32(&bars[BAR_W2 + (j & 1)]); };
+  auto b_gd = [&](int j) { return smem_u32(&bars[BAR_GD + (j & 1)]); };
+  constexpr int ROW_T0 = 128, kIssuer = 128;  // row threads 128..255; lane 0 of warp 4 issues
+  const bool row_thread = tid >= ROW_T0;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  const uint32_t idesc1 = umma_idesc_f32(kBf16, ROWS, FF), idesc2 = umma_idesc_f32(kBf16, ROWS, F);
+  const int h = (int)(s % p.NH);
+  const int nstate = seg_last;  // memo states 0 .. seg_last - 1 are read out
+
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_sh, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (tid == 32) {
+    for (int i = 0; i < NBARS; ++i) mbar_init(smem_u32(&bars[i]), i >= BAR_ZF ? 4 : 1);  // ZF, GD: one arrival per warp
+    for (int b = 0; b < 4; ++b) last_w_sh[b] = -1;
+    for (int b = 0; b < 3; ++b) commits_sh[b] = 0;
+    abort_sh = 0;
+    fence_mbar_init();
+  }
+  if (tid < 2 * F) LN[tid] = ld_elem(tid < F ? p.ln_w : p.ln_b, (long long)h * F + (tid % F), p.dt_ln);
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tZ1 = tmem_base_sh, tZ2 = tmem_base_sh + 128, tACC = tmem_base_sh + 192;
+
+  auto load_w1 = [&](int j) {
+    mbar_expect_tx(b_w1(j), W_BYTES);
+    tma_load_2d(sW1 + (j & 1) * W_BYTES, &maps.w1, 0, (int)((s * p.NS + j) * FF), b_w1(j));
+    last_w_sh[j & 1] = j;
+  };
+  auto load_w2 = [&](int j) {
+    mbar_expect_tx(b_w2(j), W_BYTES);
+    tma_load_2d(sW2 + (j & 1) * W_BYTES, &maps.w2, 0, (int)((s * p.NS + j) * F), b_w2(j));
+    last_w_sh[2 + (j & 1)] = j;
+  };
+  auto product1 = [&](int j) {  // Z1 buffer j % 2 = XQ W1_j  (K = 64)
+    tmem_fence_after();
+    const uint32_t d = tZ1 + (j & 1) * FF;
+    const uint64_t da = umma_desc_k_sw128(sXQ), db = umma_desc_k_sw128(sW1 + (j & 1) * W_BYTES);
+#pragma unroll
+    for (int k = 0; k < F / 16; ++k) umma_ss(d, da + 2 * k, db + 2 * k, idesc1, k > 0);
+    umma_commit(b_p1(j));
+    ++commits_sh[j & 1];
+  };
+  auto product2 = [&](int j) {  // Z2 = X2 (buffer j % 2) W2_j  (K = 64)
+    tmem_fence_after();
+    const uint64_t da = umma_desc_k_sw128(sX2 + (j & 1) * L::X2_BUF), db = umma_desc_k_sw128(sW2 + (j & 1) * W_BYTES);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) umma_ss(tZ2, da + 2 * k, db + 2 * k, idesc2, k > 0);
+    umma_commit(b_p2);
+    ++commits_sh[2];
+  };
+  auto wait = [&](uint32_t bar, int phase) {
+    if (!abort_sh && !mbar_wait(bar, (uint32_t)(phase & 1), p.err)) abort_sh = 1;
+  };
+
+  if (tid == 0) {  // XQ tile and the first two states' weights
+    mbar_expect_tx(b_xq, XQ_BYTES);
+    tma_load_2d(sXQ, &maps.xq, 0, (int)tok0, b_xq);
+    for (int j = 0; j < 2 && j < nstate; ++j) {
+      load_w1(j);
+      load_w2(j);
+    }
+  }
+  auto ld_row8 = [&](const T* src, float* x) {  // 16-bit row c..c+7 -> 8 floats
+    const uint4 u = *reinterpret_cast<const uint4*>(src);
+    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 v = H::unpack(w4[k]);
+      x[2 * k] = v.x;
+      x[2 * k + 1] = v.y;
+    }
+  };
+  auto st_row8 = [&](T* dst, const float* x) {
+    *reinterpret_cast<uint4*>(dst) =
+        make_uint4(H::pack(x[0], x[1]), H::pack(x[2], x[3]), H::pack(x[4], x[5]), H::pack(x[6], x[7]));
+  };
+  const int r = tid - ROW_T0;  // row of a row thread
+  const int seg_r = seg_first + (row0 + min(max(r, 0), nrows - 1)) / seg_tok;
+  float xu[F];
+  if (row_thread && r < nrows) {
+#pragma unroll
+    for (int c = 0; c < F; c += 8) ld_row8(XU + (tok0 + r) * F + c, xu + c);
+  }
+  {  // the stream's summaries 0..seg_last and every state's biases (16-byte copies)
+    const float4* ss = reinterpret_cast<const float4*>(p.summary + s * p.NS * F);
+    const float4* s1 = reinterpret_cast<const float4*>(p.b1_memo + s * p.NS * FF);
+    const float4* s2 = reinterpret_cast<const float4*>(p.b2_memo + s * p.NS * F);
+    for (int i = tid; i < (seg_last + 1) * (F / 4); i += NT) reinterpret_cast<float4*>(SUM)[i] = ss[i];
+    for (int i = tid; i < nstate * (FF / 4); i += NT) reinterpret_cast<float4*>(smem + L::OFF_B1)[i] = s1[i];
+    for (int i = tid; i < nstate * (F / 4); i += NT) reinterpret_cast<float4*>(smem + L::OFF_B2)[i] = s2[i];
+  }
+  __syncthreads();
+
+  // mixing weights g_j(t), j = 0..seg_r (row threads)
+  if (row_thread && r < nrows) {
+    float mx = -INFINITY;
+    for (int j = 0; j <= seg_r; ++j) {
+      const float4* sm = reinterpret_cast<const float4*>(SUM + j * F);
+      float d = 0.f;
+#pragma unroll
+      for (int c = 0; c < F / 4; ++c) {
+        const float4 v = sm[c];  // broadcast
+        d += xu[4 * c] * v.x + xu[4 * c + 1] * v.y + xu[4 * c + 2] * v.z + xu[4 * c + 3] * v.w;
+      }
+      G[r * GLD2 + j] = d;
+      mx = fmaxf(mx, d);
+    }
+    float tot = 0.f;
+    for (int j = 0; j <= seg_r; ++j) {
+      const float e = __expf(G[r * GLD2 + j] - mx);
+      G[r * GLD2 + j] = e;
+      tot += e;
+    }
+    const float inv = 1.f / tot;
+    for (int j = 0; j <= seg_r; ++j) G[r * GLD2 + j] *= inv;
+  }
+  if (tid == kIssuer) {  // product 1 of state 0
+    wait(b_xq, 0);
+    wait(b_w1(0), 0);
+    if (!abort_sh) product1(0);
+  }
+  __syncthreads();  // mixing weights written; the XQ tile is in shared memory
+
+  // The read-out of state j is R_j = XQ + ln_w * (y_j - mu_j) rstd_j + ln_b, y_j = Z2_j + b2_j:
+  //   forward  out = ln_w * sum_j g_j rstd_j (y_j - mu_j) + (XQ + ln_b) sum_j g_j + g_i XQW
+  //   backward dg_j = <dOut, XQ + ln_b> + rstd_j <dOut * ln_w, y_j - mu_j>
+  // The per-row vector (forward: the running sum; backward: dOut * ln_w) lives in tensor-memory
+  // columns tACC of the row's lane.
+  float gsum = 0.f;  // forward: sum_j g_j over the states read out
+  float k0 = 0.f;    // backward: <dOut, XQ + ln_b>
+  auto xq_row8 = [&](int ch, float* x) {  // 8 values of the XQ row from the swizzled tile
+    const uint4 u = *reinterpret_cast<const uint4*>(smem + OFF_XQ + swz128(r, ch));
+    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 v = H::unpack(w4[k]);
+      x[2 * k] = v.x;
+      x[2 * k + 1] = v.y;
+    }
+  };
+  const T* dO = reinterpret_cast<const T*>(p.dOut);
+  if (row_thread) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      float a[32];
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        if (BWD && r < nrows) {
+          float x[8];
+          xq_row8(4 * hh + ch, x);
+          ld_row8(dO + (tok0 + r) * F + 32 * hh + 8 * ch, a + 8 * ch);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int c = 32 * hh + 8 * ch + e;
+            k0 += a[8 * ch + e] * (x[e] + LN[F + c]);
+            a[8 * ch + e] *= LN[c];
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a[8 * ch + e] = 0.f;
+        }
+      }
+      tmem_st32(tmem_lane_addr(tACC, warp, 32 * hh), a);
+    }
+    tmem_wait_st();
+  }
+
+  if (warp < 4) {
+    // GELU group: X2_j = gelu(Z1_j + b1_j) into buffer j % 2
+    const int row = 32 * warp + lane;
+    for (int j = 0; j < nstate; ++j) {
+      if (lane == 0) wait(b_p1(j), j >> 1);
+      __syncwarp();
+      tmem_fence_after();
+      const float* b1 = reinterpret_cast<const float*>(smem + L::OFF_B1) + j * FF;
+      float z[64];
+      tmem_ld32(tmem_lane_addr(tZ1 + (j & 1) * FF, warp, 0), z);
+      tmem_ld32(tmem_lane_addr(tZ1 + (j & 1) * FF, warp, 32), z + 32);
+      tmem_wait_ld();
+      uint8_t* base = smem + L::OFF_X2 + (j & 1) * L::X2_BUF;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = 8 * ch + 2 * u;
+          const float2 bb = *reinterpret_cast<const float2*>(b1 + c);
+          const float2 g = gelu2(__fadd2_rn(make_float2(z[c], z[c + 1]), bb));
+          pk[u] = H::pack(g.x, g.y);
+        }
+        *reinterpret_cast<uint4*>(base + swz128(row, ch)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      fence_proxy_async();  // X2 stores -> visible to the tensor cores
+      tmem_fence_before();  // Z1 loads complete before the arrival
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b_gd(j));
+    }
+  } else {
+    // row group: (lane 0 of warp 4) the products of state j, then the read-out of state j
+    for (int j = 0; j < nstate; ++j) {
+      if (tid == kIssuer) {
+        wait(b_gd(j), j >> 1);
+        // W1 buffer j % 2 is free (product 1 of j completed before the GELU of j began)
+        if (j + 2 < nstate && !abort_sh) load_w1(j + 2);
+        wait(b_w2(j), j >> 1);
+        if (j >= 1) wait(b_zf, (j - 1) & 1);  // Z2 taken out for state j - 1
+        if (!abort_sh) product2(j);
+        if (j + 1 < nstate) {
+          wait(b_w1(j + 1), (j + 1) >> 1);
+          if (!abort_sh) product1(j + 1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) wait(b_p2, j);
+      __syncwarp();
+      tmem_fence_after();
+      float z[F];
+      tmem_ld32(tmem_lane_addr(tZ2, warp, 0), z);
+      tmem_ld32(tmem_lane_addr(tZ2, warp, 32), z + 32);
+      tmem_wait_ld();
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b_zf);
+      // product 2 of j no longer reads W2 buffer j % 2: fetch state j + 2 into it
+      if (tid == kIssuer && j + 2 < nstate && !abort_sh) load_w2(j + 2);
+      const float* b2 = reinterpret_cast<const float*>(smem + L::OFF_B2) + j * F;
+      float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < F; c += 2) {
+        const float2 y = __fadd2_rn(make_float2(z[c], z[c + 1]), *reinterpret_cast<const float2*>(b2 + c));
+        z[c] = y.x;
+        z[c + 1] = y.y;
+        s2 = __fadd2_rn(s2, y);
+      }
+      const float2 nmu = f2(-(s2.x + s2.y) * (1.f / F));
+      float2 v2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < F; c += 2) {
+        const float2 d = __fadd2_rn(make_float2(z[c], z[c + 1]), nmu);
+        z[c] = d.x;
+        z[c + 1] = d.y;
+        v2 = __ffma2_rn(d, d, v2);
+      }
+      const float rstd = 1.f / sqrtf((v2.x + v2.y) * (1.f / F) + kReadoutEps);
+      if (!BWD) {
+        const float gj = r < nrows && j < seg_r ? G[r * GLD2 + j] : 0.f;  // states of the row's own segment only
+        gsum += gj;
+        const float2 sj = f2(gj * rstd);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float a[32];
+          tmem_ld32(tmem_lane_addr(tACC, warp, 32 * hh), a);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const float2 a2 = __ffma2_rn(sj, make_float2(z[32 * hh + c], z[32 * hh + c + 1]), make_float2(a[c], a[c + 1]));
+            a[c] = a2.x;
+            a[c + 1] = a2.y;
+          }
+          tmem_st32(tmem_lane_addr(tACC, warp, 32 * hh), a);
+        }
+        tmem_wait_st();
+      } else {
+        float2 d2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float a[32];
+          tmem_ld32(tmem_lane_addr(tACC, warp, 32 * hh), a);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; c += 2)
+            d2 = __ffma2_rn(make_float2(a[c], a[c + 1]), make_float2(z[32 * hh + c], z[32 * hh + c + 1]), d2);
+        }
+        if (r < nrows) DG[r * GLD2 + j] = k0 + rstd * (d2.x + d2.y);
+      }
+    }
+  }
+  tmem_fence_before();
+
+  // ---- tail (row threads, one token each). The tensor-memory loads are warp-collective, so
+  // they run for every row thread, before the branch on the tile's ragged row count.
+  if (!BWD && row_thread) {
+    float a[F];
+    tmem_ld32(tmem_lane_addr(tACC, warp, 0), a);
+    tmem_ld32(tmem_lane_addr(tACC, warp, 32), a + 32);
+    tmem_wait_ld();
+    if (r < nrows) {
+      const long long o = (tok0 + r) * F;
+      const float gi = G[r * GLD2 + seg_r];
+      T* out = reinterpret_cast<T*>(p.out);
+#pragma unroll
+      for (int ch = 0; ch < F / 8; ++ch) {
+        float w[8], x[8], y[8];
+        ld_row8(XQW + o + 8 * ch, w);
+        xq_row8(ch, x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int c = 8 * ch + e;
+          y[e] = LN[c] * a[c] + (x[e] + LN[F + c]) * gsum + gi * w[e];
+        }
+        st_row8(out + o + 8 * ch, y);
+      }
+    }
+  }
+  if (BWD && row_thread && r < nrows) {
+    const long long o = (tok0 + r) * F;
+    const float gi = G[r * GLD2 + seg_r];
+    {
+      float dgi = 0.f;
+#pragma unroll
+      for (int c = 0; c < F; c += 8) {
+        float w[8], d8[8];
+        ld_row8(XQW + o + c, w);
+        ld_row8(dO + o + c, d8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dgi += d8[e] * w[e];
+      }
+      DG[r * GLD2 + seg_r] = dgi;
+      float sg = 0.f;
+      for (int k = 0; k <= seg_r; ++k) sg += G[r * GLD2 + k] * DG[r * GLD2 + k];
+      float dxu[F];
+#pragma unroll
+      for (int c = 0; c < F; ++c) dxu[c] = 0.f;
+      for (int k = 0; k <= seg_r; ++k) {
+        const float ds = G[r * GLD2 + k] * (DG[r * GLD2 + k] - sg);
+        DG[r * GLD2 + k] = ds;
+        const float4* sm = reinterpret_cast<const float4*>(SUM + k * F);
+#pragma unroll
+        for (int c = 0; c < F / 4; ++c) {
+          const float4 v = sm[c];  // broadcast
+          dxu[4 * c] += ds * v.x;
+          dxu[4 * c + 1] += ds * v.y;
+          dxu[4 * c + 2] += ds * v.z;
+          dxu[4 * c + 3] += ds * v.w;
+        }
+      }
+      T* dXU = reinterpret_cast<T*>(p.dXU);
+      T* dXQW = reinterpret_cast<T*>(p.dXQW);
+#pragma unroll
+      for (int c = 0; c < F; c += 8) {
+        float q8[8];
+        ld_row8(dO + o + c, q8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q8[e] *= gi;
+        st_row8(dXU + o + c, dxu + c);
+        st_row8(dXQW + o + c, q8);
+      }
+    }
+  }
+  if (BWD) {
+    // d summary_i += sum over the tile's tokens of segment i of ds_i(t) XU_t, through the X2
+    // buffers as fp32 [128][64] scratch (column c of row i at c ^ (i % 32): conflict-free row
+    // writes and column reads)
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(smem + L::OFF_X2);
+    if (row_thread) {
+      const float ds = r < nrows ? DG[r * GLD2 + seg_r] : 0.f;
+#pragma unroll
+      for (int c = 0; c < F; c += 2) {
+        float2 v = make_float2(0.f, 0.f);
+        if (r < nrows) v = H::unpack(*reinterpret_cast<const uint32_t*>(XU + (tok0 + r) * F + c));
+        red[r * F + (c ^ (r & 31))] = ds * v.x;
+        red[r * F + ((c + 1) ^ (r & 31))] = ds * v.y;
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < (seg_last - seg_first + 1) * F; e += NT) {
+      const int sg = e / F, f = e % F;
+      const int lo = max(0, sg * seg_tok - row0), hi = min(nrows, (sg + 1) * seg_tok - row0);
+      float a = 0.f;
+      for (int i = lo; i < hi; ++i) a += red[i * F + (f ^ (i & 31))];
+      atomicAdd(p.dsum + (s * p.NS + seg_first + sg) * F + f, a);
+    }
+  }
+  // a timed-out wait may leave products in flight: drain (bounded) before freeing memory
+  if (tid == 0 && abort_sh) {
+    mbar_wait(b_xq, 0, nullptr);
+    for (int b = 0; b < 2; ++b)
+      if (commits_sh[b] > 0) mbar_wait(smem_u32(&bars[BAR_P1 + b]), (uint32_t)((commits_sh[b] - 1) & 1), nullptr);
+    if (commits_sh[2] > 0) mbar_wait(b_p2, (uint32_t)((commits_sh[2] - 1) & 1), nullptr);
+    for (int b = 0; b < 2; ++b) {  // weight loads issued and never awaited
+      if (last_w_sh[b] >= 0) mbar_wait(b_w1(last_w_sh[b]), (uint32_t)((last_w_sh[b] >> 1) & 1), nullptr);
+      if (last_w_sh[2 + b] >= 0) mbar_wait(b_w2(last_w_sh[2 + b]), (uint32_t)((last_w_sh[2 + b] >> 1) & 1), nullptr);
+    }
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  if (warp == 0) tmem_dealloc(tmem_base_sh, L::TMEM_COLS);
+}
+
 // dXK of every token: d summary_i / (tokens of segment i) for i >= 1, zero in segment 0.
 // One thread writes 8 features of one token (a 16-byte store); mini-batch rows are indexed
 // as (stream, mini-batch) pairs so the only runtime divisions are 32-bit.
@@ -839,6 +1316,19 @@ static int run(MemoMixParams p, bool bwd, bool prepped, cudaStream_t stream, con
     if (e != cudaSuccess) return fail(TTT_ERR_CUDA, "%s: %s", who, cudaGetErrorString(e));
   }
   const unsigned grid = (unsigned)(p.P == 1 ? streams * p.NS * p.TILES : streams * p.NG);
+  if (FF == 64 && p.NS <= Mix2::NSC) {  // two CTAs per SM
+    auto kern = bwd ? memo_mix2_kernel<T, true> : memo_mix2_kernel<T, false>;
+    rc = prepare_smem(kern, Mix2::SMEM, who);
+    if (rc) return rc;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return fail(TTT_ERR_CUDA, "%s: cudaFuncSetAttribute: %s", who, cudaGetErrorString(e));
+    kern<<<grid, Mix2::NT, Mix2::SMEM, stream>>>(p, maps);
+    if (!bwd) return check_launch(who);
+    rc = check_launch(who);
+    if (rc) return rc;
+    memo_dxk_kernel<T><<<148 * 8, 256, 0, stream>>>(p);
+    return check_launch(who);
+  }
   if (!bwd) {
     rc = prepare_smem(memo_mix_kernel<T, false, FF>, SMEM, who);
     if (rc) return rc;
