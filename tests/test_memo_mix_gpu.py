@@ -31,11 +31,12 @@ ORDER = ("XQW", "XQ", "XK", "XU", "W1_memo", "b1_memo", "W2_memo", "b2_memo", "l
 
 @pytest.mark.parametrize("FF", [256, 64])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("shape", [(1, 2, 7, 2), (1, 1, 40, 16), (2, 1, 9, 3), (2, 2, 21, 2)])
+@pytest.mark.parametrize("shape", [(1, 2, 7, 2), (1, 1, 40, 16), (2, 1, 9, 3), (2, 2, 21, 2), (1, 1, 40, 2)])
 def test_memo_mix_matches_oracle(dtype, shape, FF):
     """Forward and gradients (XQW, XU, XK) of the fused kernels for the 256-wide and the F x F
-    inner MLP, including segments of 256 tokens (two 128-token tiles), a ragged last segment
-    and the config-4 layer's 11 segments of 2 mini-batches."""
+    inner MLP, including segments of 256 tokens (two 128-token tiles), a ragged last segment,
+    the config-4 layer's 11 segments of 2 mini-batches (F x F: two CTAs per SM) and 20
+    segments (F x F: more memo states than the two-CTA kernel holds, the one-CTA kernel)."""
     B, NH, NC, M = shape
     inp = make(B, NH, NC, M, dtype, seed=NC + M, FF=FF)
     dO = S.make_upstream((B, NH, NC, 16, 64), seed=3).to(dtype)
