@@ -62,10 +62,13 @@ struct Bwd {
   static constexpr int PART = NW * C * PLD * 4;              // one [NW][C][PLD] set of partial tiles
   static constexpr int OFF_PA = NSTAGE * STAGE;              // partial dG2 (M1 -> R2), then partial dXQ (M2 -> R3)
   static constexpr int OFF_PB = OFF_PA + PART;               // partial dXK (M1, M2 -> R3)
-  static constexpr int OFF_G = OFF_PB + PART;                // 16-bit swizzled [C][F]: G2
-  static constexpr int OFF_EG = OFF_G + TILE;                //   e * G2
-  static constexpr int OFF_DZB = OFF_EG + TILE;              //   dZ2bar
-  static constexpr int OFF_DZ2 = OFF_DZB + TILE;             //   dZ2
+  // R1's outputs; with row-only warps (NR > NW) they compute R1 of the next mini-batch while
+  // the MMA warps work on this one, so those tiles are double-buffered (mini-batch n in n % 2)
+  static constexpr int NRB = NR > NW ? 2 : 1;
+  static constexpr int OFF_G = OFF_PB + PART;                // NRB x 16-bit swizzled [C][F]: G2
+  static constexpr int OFF_EG = OFF_G + NRB * TILE;          //   e * G2
+  static constexpr int OFF_DZB = OFF_EG + NRB * TILE;        //   dZ2bar
+  static constexpr int OFF_DZ2 = OFF_DZB + NRB * TILE;       //   dZ2
   static constexpr int OFF_DETAP = OFF_DZ2 + TILE;           // fp32 [NW][C*C] partial d_eta
   static constexpr int OFF_DP1P = OFF_DETAP + NW * C * C * 4;  // fp32 [NW][C*C] partial dP1
   static constexpr int OFF_DP1 = OFF_DP1P + NW * C * C * 4;    // fp32 [C*C] dP1
@@ -81,11 +84,12 @@ struct Bwd {
   static_assert(OFF_PA % 128 == 0 && OFF_G % 128 == 0 && STAGE % 128 == 0, "tile alignment");
 };
 
-template <int NW>
-__device__ __forceinline__ void load_stage(uint8_t* st, const MlpBwdParams& p, long long s, int n) {
+// Copies of mini-batch n's stage, issued by the NT threads t0 .. t0 + NT - 1.
+template <int NW, int NT>
+__device__ __forceinline__ void load_stage(uint8_t* st, const MlpBwdParams& p, long long s, int n, int t0) {
   using L = Bwd<NW>;
-  constexpr int NT = L::NTHREADS, FFW = L::FFW, ZLD = L::ZLD;
-  const int tid = threadIdx.x;
+  constexpr int FFW = L::FFW, ZLD = L::ZLD;
+  const int tid = threadIdx.x - t0;
   const long long mb = s * p.NC + n;  // mini-batch index
   const uint32_t sb = smem_u32(st);
   {
@@ -181,8 +185,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
   float* DE = reinterpret_cast<float*>(smem + OFF_DE);
   float* DE2 = reinterpret_cast<float*>(smem + OFF_DE2);
   float* DB2 = reinterpret_cast<float*>(smem + OFF_DB2);
-  const uint32_t sG = smem_u32(smem + OFF_G), sEG = smem_u32(smem + OFF_EG);
-  const uint32_t sDZB = smem_u32(smem + OFF_DZB), sDZ2 = smem_u32(smem + OFF_DZ2);
+  const uint32_t sDZ2 = smem_u32(smem + OFF_DZ2);
 
   if (warp == 0) {
     tmem_alloc(&tmem_base_sh, TMEM_COLS);
@@ -219,73 +222,71 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
   const uint32_t a_ones[4] = {ones, ones, ones, ones};
   const float one_w0 = warp == 0 ? 1.f : 0.f;  // the "+1" of P2 = eta * (A2 + 1) goes to warp 0's partial
 
-  load_stage<NW>(smem, p, s, p.NC - 1);
-  cp_async_commit();
-
-  for (int it = 0; it < p.NC; ++it) {
-    const int n = p.NC - 1 - it;
-    cp_async_wait<0>();
-    __syncthreads();  // stage of mini-batch n landed; every warp is done with mini-batch n+1
-    if (it + 1 < p.NC) load_stage<NW>(smem + ((it + 1) % NSTAGE) * STAGE, p, s, n - 1);
-    cp_async_commit();
-    const uint8_t* st = smem + (it % NSTAGE) * STAGE;
-    const uint32_t sb = smem_u32(st);
-    const T* E = reinterpret_cast<const T*>(st + OFF_ETA);
-    const long long xb = (s * p.NC + n) * (long long)(C * F);
-    auto xo_of = [&](int tk) { return swz128(tk, q >> 1) + (q & 1) * 8; };
-
-    // G2 = ln_fused_l2_bwd(Z2, XV - XK) for token tk, features 4q.., with its normalised input
-    // xh, the scaled residual gh and 1/std (rows; formed in R1 and again in R2 rather than
-    // kept in registers across M1)
-    auto g2_rows = [&](int tk, float* xh, float* gh, float* Gr, float& rstd) {
-      const uint32_t xo = xo_of(tk);
-      const float4 z4 = *reinterpret_cast<const float4*>(st + OFF_Z2 + (tk * F + 4 * q) * 4);
-      float z[4] = {z4.x, z4.y, z4.z, z4.w}, xv[4], xk[4];
-      unpack4<T>(st + OFF_XV + xo, xv);
-      unpack4<T>(st + OFF_XK + xo, xk);
-      const float mu = red16(z[0] + z[1] + z[2] + z[3]) * (1.f / F);
-      float d[4], m2 = 0.f;
+  // Row-only warps (NR > NW, FF = 64): while the MMA warps run M1 and M2 of mini-batch n, warps
+  // NW.. copy mini-batch n - 1's stage (waiting on their own copies) and compute its R1, whose
+  // inputs are the staged tiles only; R1's db2 term moves to R2, where db2 is current.
+  constexpr bool kAhead = NR > NW;
+  constexpr int NRT = 32 * (NR - NW);  // row-only threads
+  auto xo_of = [&](int tk) { return swz128(tk, q >> 1) + (q & 1) * 8; };
+  // G2 = ln_fused_l2_bwd(Z2, XV - XK) for token tk of the stage at sx, features 4q.., with its
+  // normalised input xh, the scaled residual gh and 1/std
+  auto g2_rows_at = [&](const uint8_t* sx, int tk, float* xh, float* gh, float* Gr, float& rstd) {
+    const uint32_t xo = xo_of(tk);
+    const float4 z4 = *reinterpret_cast<const float4*>(sx + OFF_Z2 + (tk * F + 4 * q) * 4);
+    float z[4] = {z4.x, z4.y, z4.z, z4.w}, xv[4], xk[4];
+    unpack4<T>(sx + OFF_XV + xo, xv);
+    unpack4<T>(sx + OFF_XK + xo, xk);
+    const float mu = red16(z[0] + z[1] + z[2] + z[3]) * (1.f / F);
+    float d[4], m2 = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        d[j] = z[j] - mu;
-        m2 += d[j] * d[j];
-      }
-      rstd = 1.f / sqrtf(red16(m2) * (1.f / F) + kLnEps);
-      float s1 = 0.f, s2 = 0.f;
+    for (int j = 0; j < 4; ++j) {
+      d[j] = z[j] - mu;
+      m2 += d[j] * d[j];
+    }
+    rstd = 1.f / sqrtf(red16(m2) * (1.f / F) + kLnEps);
+    float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        xh[j] = d[j] * rstd;
-        gh[j] = (gm[j] * xh[j] + bt[j] - (xv[j] - xk[j])) * gm[j];
-        s1 += gh[j];
-        s2 += gh[j] * xh[j];
-      }
-      s1 = red16(s1);
-      s2 = red16(s2);
-      const float inv = rstd * (1.f / F);
+    for (int j = 0; j < 4; ++j) {
+      xh[j] = d[j] * rstd;
+      gh[j] = (gm[j] * xh[j] + bt[j] - (xv[j] - xk[j])) * gm[j];
+      s1 += gh[j];
+      s2 += gh[j] * xh[j];
+    }
+    s1 = red16(s1);
+    s2 = red16(s2);
+    const float inv = rstd * (1.f / F);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) Gr[j] = (F * gh[j] - s1 - xh[j] * s2) * inv;
-    };
-
-    // ---------------- R1: G2 from the stored Z2; read-out LayerNorm backward from Z2bar
-#pragma unroll
-    for (int tk = tk0; tk < C; tk += TPP) {
+    for (int j = 0; j < 4; ++j) Gr[j] = (F * gh[j] - s1 - xh[j] * s2) * inv;
+  };
+  // R1, part 1: G2 and e * G2 tiles (buffer ob) of the stage at sx, tokens tkb, tkb + tps, ..;
+  // with_de2: also -G2 . db2 per token
+  auto r1_g = [&](const uint8_t* sx, int ob, int tkb, int tps, bool with_de2) {
+    const T* Ex = reinterpret_cast<const T*>(sx + OFF_ETA);
+#pragma unroll 4
+    for (int tk = tkb; tk < C; tk += tps) {
       const uint32_t xo = xo_of(tk);
       float xh[4], gh[4], Gr[4], rstd;
-      g2_rows(tk, xh, gh, Gr, rstd);
-      const float e = (float)E[(C - 1) * C + tk];
-      *reinterpret_cast<uint2*>(smem + OFF_G + xo) = make_uint2(H::pack(Gr[0], Gr[1]), H::pack(Gr[2], Gr[3]));
-      *reinterpret_cast<uint2*>(smem + OFF_EG + xo) =
+      g2_rows_at(sx, tk, xh, gh, Gr, rstd);
+      const float e = (float)Ex[(C - 1) * C + tk];
+      *reinterpret_cast<uint2*>(smem + OFF_G + ob * TILE + xo) = make_uint2(H::pack(Gr[0], Gr[1]), H::pack(Gr[2], Gr[3]));
+      *reinterpret_cast<uint2*>(smem + OFF_EG + ob * TILE + xo) =
           make_uint2(H::pack(e * Gr[0], e * Gr[1]), H::pack(e * Gr[2], e * Gr[3]));
-      const float4 db = *reinterpret_cast<const float4*>(DB2 + 4 * q);
-      const float dot = red16(Gr[0] * db.x + Gr[1] * db.y + Gr[2] * db.z + Gr[3] * db.w);
-      if (q == 0) DE2[tk] = -dot;
+      if (with_de2) {
+        const float4 db = *reinterpret_cast<const float4*>(DB2 + 4 * q);
+        const float dot = red16(Gr[0] * db.x + Gr[1] * db.y + Gr[2] * db.z + Gr[3] * db.w);
+        if (q == 0) DE2[tk] = -dot;
+      }
     }
-#pragma unroll
-    for (int tk = tk0; tk < C; tk += TPP) {
+  };
+  // R1, part 2: read-out LayerNorm backward dZ2bar (buffer ob) from the stored Z2bar and dO,
+  // and this thread's share of the TTT LayerNorm gradients
+  auto r1_dzb = [&](const uint8_t* sx, int ob, int tkb, int tps) {
+#pragma unroll 4
+    for (int tk = tkb; tk < C; tk += tps) {
       const uint32_t xo = xo_of(tk);
-      const float4 z4 = *reinterpret_cast<const float4*>(st + OFF_Z2B + (tk * F + 4 * q) * 4);
+      const float4 z4 = *reinterpret_cast<const float4*>(sx + OFF_Z2B + (tk * F + 4 * q) * 4);
       float z[4] = {z4.x, z4.y, z4.z, z4.w}, dO4[4];
-      unpack4<T>(st + OFF_DO + xo, dO4);
+      unpack4<T>(sx + OFF_DO + xo, dO4);
       const float mu = red16(z[0] + z[1] + z[2] + z[3]) * (1.f / F);
       float d[4], m2 = 0.f;
 #pragma unroll
@@ -309,9 +310,83 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
       float dz[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) dz[j] = (F * gg[j] - s1 - xbn[j] * s2) * (rb * (1.f / F));
-      *reinterpret_cast<uint2*>(smem + OFF_DZB + xo) = make_uint2(H::pack(dz[0], dz[1]), H::pack(dz[2], dz[3]));
+      *reinterpret_cast<uint2*>(smem + OFF_DZB + ob * TILE + xo) = make_uint2(H::pack(dz[0], dz[1]), H::pack(dz[2], dz[3]));
     }
+  };
+  load_stage<NW, NTHREADS>(smem, p, s, p.NC - 1, 0);
+  cp_async_commit();
+  if constexpr (kAhead) {  // R1 of the first mini-batch (all threads)
+    cp_async_wait<0>();
     __syncthreads();
+    r1_g(smem, (p.NC - 1) & 1, tk0, TPP, false);
+    r1_dzb(smem, (p.NC - 1) & 1, tk0, TPP);
+  }
+
+  for (int it = 0; it < p.NC; ++it) {
+    const int n = p.NC - 1 - it;
+    cp_async_wait<0>();
+    __syncthreads();  // stage of mini-batch n landed; every warp is done with mini-batch n+1
+    if (!kAhead && it + 1 < p.NC) load_stage<NW, NTHREADS>(smem + ((it + 1) % NSTAGE) * STAGE, p, s, n - 1, 0);
+    cp_async_commit();
+    const uint8_t* st = smem + (it % NSTAGE) * STAGE;
+    const uint32_t sb = smem_u32(st);
+    const T* E = reinterpret_cast<const T*>(st + OFF_ETA);
+    const long long xb = (s * p.NC + n) * (long long)(C * F);
+    // G2 rows of this mini-batch (formed in R1 and again in R2 rather than kept in registers
+    // across M1)
+    auto g2_rows = [&](int tk, float* xh, float* gh, float* Gr, float& rstd) { g2_rows_at(st, tk, xh, gh, Gr, rstd); };
+    const int ob = kAhead ? (n & 1) : 0;  // R1 output buffer of this mini-batch
+    const uint32_t sG = smem_u32(smem + OFF_G + ob * TILE), sEG = smem_u32(smem + OFF_EG + ob * TILE);
+    const uint32_t sDZB = smem_u32(smem + OFF_DZB + ob * TILE);
+
+    if constexpr (!kAhead) {
+      // ---------------- R1: G2 from the stored Z2; read-out LayerNorm backward from Z2bar
+  #pragma unroll
+      for (int tk = tk0; tk < C; tk += TPP) {
+        const uint32_t xo = xo_of(tk);
+        float xh[4], gh[4], Gr[4], rstd;
+        g2_rows(tk, xh, gh, Gr, rstd);
+        const float e = (float)E[(C - 1) * C + tk];
+        *reinterpret_cast<uint2*>(smem + OFF_G + xo) = make_uint2(H::pack(Gr[0], Gr[1]), H::pack(Gr[2], Gr[3]));
+        *reinterpret_cast<uint2*>(smem + OFF_EG + xo) =
+            make_uint2(H::pack(e * Gr[0], e * Gr[1]), H::pack(e * Gr[2], e * Gr[3]));
+        const float4 db = *reinterpret_cast<const float4*>(DB2 + 4 * q);
+        const float dot = red16(Gr[0] * db.x + Gr[1] * db.y + Gr[2] * db.z + Gr[3] * db.w);
+        if (q == 0) DE2[tk] = -dot;
+      }
+  #pragma unroll
+      for (int tk = tk0; tk < C; tk += TPP) {
+        const uint32_t xo = xo_of(tk);
+        const float4 z4 = *reinterpret_cast<const float4*>(st + OFF_Z2B + (tk * F + 4 * q) * 4);
+        float z[4] = {z4.x, z4.y, z4.z, z4.w}, dO4[4];
+        unpack4<T>(st + OFF_DO + xo, dO4);
+        const float mu = red16(z[0] + z[1] + z[2] + z[3]) * (1.f / F);
+        float d[4], m2 = 0.f;
+  #pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          d[j] = z[j] - mu;
+          m2 += d[j] * d[j];
+        }
+        const float rb = 1.f / sqrtf(red16(m2) * (1.f / F) + kLnEps);
+        float xbn[4], gg[4], s1 = 0.f, s2 = 0.f;
+  #pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          xbn[j] = d[j] * rb;
+          gg[j] = dO4[j] * gm[j];
+          s1 += gg[j];
+          s2 += gg[j] * xbn[j];
+          dgam[j] += dO4[j] * xbn[j];
+          dbet[j] += dO4[j];
+        }
+        s1 = red16(s1);
+        s2 = red16(s2);
+        float dz[4];
+  #pragma unroll
+        for (int j = 0; j < 4; ++j) dz[j] = (F * gg[j] - s1 - xbn[j] * s2) * (rb * (1.f / F));
+        *reinterpret_cast<uint2*>(smem + OFF_DZB + xo) = make_uint2(H::pack(dz[0], dz[1]), H::pack(dz[2], dz[3]));
+      }
+      __syncthreads();
+    }
 
     // ---------------- M1 (the NW MMA warps)
     // carried from M1 into M2 in the MMA warps' registers
@@ -731,6 +806,16 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
       }
     }
     }  // M1
+    if constexpr (kAhead) {
+      if (warp >= NW && it + 1 < p.NC) {  // row-only warps: stage and R1 part 1 of mini-batch n - 1
+        uint8_t* nx = smem + ((it + 1) % NSTAGE) * STAGE;
+        load_stage<NW, NRT>(nx, p, s, n - 1, 32 * NW);
+        cp_async_commit();
+        cp_async_wait<0>();
+        asm volatile("bar.sync 1, %0;" ::"r"(NRT) : "memory");  // the row-only warps' copies landed
+        r1_g(nx, (n - 1) & 1, (tid - 32 * NW) >> 4, NRT / 16, false);
+      }
+    }
     __syncthreads();
 
     // ---------------- R2: dG2 -> backward of G2 = ln_fused_l2_bwd(Z2, XV - XK); d_eta, dP1
@@ -744,6 +829,10 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
       sum_part<NW>(PA, tk, q, dG);
       const float e = (float)E[(C - 1) * C + tk];
       const float4 db = *reinterpret_cast<const float4*>(DB2 + 4 * q);
+      if constexpr (kAhead) {  // R1's db2 term, here where db2 is current
+        const float dot = red16(Gr[0] * db.x + Gr[1] * db.y + Gr[2] * db.z + Gr[3] * db.w);
+        if (q == 0) DE2[tk] = -dot;
+      }
       dG[0] -= e * db.x;
       dG[1] -= e * db.y;
       dG[2] -= e * db.z;
@@ -785,6 +874,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
       *reinterpret_cast<uint2*>((uint8_t*)p.dXV + (xb + tk * F + 4 * q) * 2) =
           make_uint2(H::pack(DTr[ps][0], DTr[ps][1]), H::pack(DTr[ps][2], DTr[ps][3]));
     }
+    if constexpr (kAhead) __syncthreads();  // DE2 of every token written
 #pragma unroll
     for (int el = tid; el < C * C; el += NTHREADS) {  // element (el / C, el % C) of d_eta and dP1
       float v = 0.f, u = 0.f;
@@ -958,6 +1048,10 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
       }
     }
     }  // M2
+    if constexpr (kAhead) {
+      if (warp >= NW && it + 1 < p.NC)  // row-only warps: R1 part 2 of mini-batch n - 1
+        r1_dzb(smem + ((it + 1) % NSTAGE) * STAGE, (n - 1) & 1, (tid - 32 * NW) >> 4, NRT / 16);
+    }
     __syncthreads();
 
     // ---------------- R3: dXQ = dO + sum of partials, dXK = sum of partials - dXV
