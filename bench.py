@@ -587,7 +587,7 @@ def run_forecaster(args, w, rank, world, local_rank):
 
 # DRAM bytes (read + write) of one F x F scan-backward launch at batch 128 (ncu capture in
 # profiles/mlp_bwd_tc_fxf_config4.md)
-FXF_BWD_TRAFFIC_B128 = 286.894336e6 + 70.784e6
+FXF_BWD_TRAFFIC_B128 = 286.697984e6 + 73.438464e6
 
 
 def forecaster_mlp_bwd_ms(w, b_rank, dev):
