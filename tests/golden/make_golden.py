@@ -317,7 +317,9 @@ def forecaster_case(ref_root, B, L, W, NH, CS, pred_len, d_in, seed):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py /path/to/ttt-triton")
+    ref_root = sys.argv[1]
     sys.path.insert(0, ref_root)
     import forecast  # noqa: F401  (must precede ttt_layer / ops imports in the reference)
     import ops as ref_ops
