@@ -120,6 +120,13 @@ def test_memo_mix_host_checks():
     assert fwd(8, 2, dt=0) == -3
     assert fwd(8, 2, scratch=None) == -1
     assert fwd(8, 2, nbytes=16) == -5
+    # fp32 memo states are read with 16-byte accesses: each of the four must be 16-byte aligned
+    odd = ctypes.c_void_p(0x1004)
+    for i in range(4):
+        memo = [FAKE] * 4
+        memo[i] = odd
+        rc = _lib.lib.ttt_memo_mix_fwd(1, 1, 8, 16, 64, 64, 2, *P, 1, *memo, FAKE, FAKE, 1, FAKE, FAKE, 1 << 40, None)
+        assert rc == -7 and "memo states" in _lib.lib.ttt_last_error().decode()
     # W1/W2 16-bit copies (2 * F * FF * 2 bytes) plus summary and its gradient (2 * F * 4) per memo state
     assert _lib.lib.ttt_memo_mix_scratch_bytes(2, 3, 9, 4, 256) == 2 * 3 * 3 * (2 * 64 * 256 * 2 + 2 * 64 * 4)
     assert _lib.lib.ttt_memo_mix_scratch_bytes(2, 3, 9, 4, 64) == 2 * 3 * 3 * (2 * 64 * 64 * 2 + 2 * 64 * 4)
