@@ -25,11 +25,19 @@ ttt-triton_b200/synthetic.py):
   stage on this library, bf16 activations. Strong scaling: the global batch is split over
   the ranks and DistributedDataParallel averages the gradients with NCCL.
 
-A step is one pass of the hot path over one batch. Multi-GPU runs are weak scaling:
-every rank processes its own full batch (the (b, h) streams are independent, so there
-is no data-path collective); timing is the max over ranks of the device-timed region.
-The reference arm (``--impl reference``) times the CPU port of the reference's ops/
-path (oracle/ttt_oracle.py) on the host cores over a bounded sample of the workload.
+A step is one pass of the hot path over one batch. Multi-GPU runs of a workload are weak
+scaling: every rank processes its own full batch (the (b, h) streams are independent, so
+there is no data-path collective); timing is the max over ranks of the device-timed region.
+
+The default line (``mlp_fwd_c1``) also carries a ``fwdbwd`` record: config 3 (TTT-MLP
+forward+backward, B64 NH16 L8192) as ONE global batch whose (batch, head) streams are split
+over the ranks by batch (sharding.py), strong scaling: at N GPUs each rank runs B/N
+batches, the step time is the max over ranks and the value is the global tokens over it.
+It has its own roofline (the backward kernel), end-to-end leg and CPU baseline.
+
+The reference arm (``--impl reference``) times the CPU port of the reference's ops/ path
+(oracle/ttt_oracle.py) on the host cores at the workload's full shape (chunked over
+streams); the training workloads and the forecaster run a bounded batch slice there.
 """
 
 from __future__ import annotations
@@ -203,12 +211,19 @@ def kernel_step(w, d, dO):
                                   Z=Z, W_last=Wl, b_last=bl)
             return 2
         return 1
-    XQW, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"], for_backward=w["bwd"])
+    XQW, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], memo_of(w), for_backward=w["bwd"])
     if w["bwd"]:
         _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
                            saved=zs, W1_last=last[0], W2_last=last[2])
         return 2
     return 1
+
+
+def memo_of(w):
+    """Memo-segment size of an MLP workload: TritonMLP.apply always writes memo states
+    (mlp_triton.py:15-62), so both the device-timed and the end-to-end legs write them, at
+    the workload's memo size or, when it names none, every checkpoint group."""
+    return w["memo"] or w["ckpt"]
 
 
 def prologue_step(w, d, dO, time_bwd_kernel=False):
@@ -303,7 +318,7 @@ def api_compute(w, d):
         out = TritonLinear.apply(*leaves, w["ckpt"])
     else:
         leaves = [d[k].requires_grad_(w["bwd"]) for k in MLP]
-        out = TritonMLP.apply(*leaves, w["ckpt"], w["memo"] or w["ckpt"])[0]
+        out = TritonMLP.apply(*leaves, w["ckpt"], memo_of(w))[0]
     if w["bwd"]:
         out.backward(d["dO"])
         return grad_of(leaves, "XQ")
@@ -363,6 +378,16 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def smi_index(dev):
+    """nvidia-smi's index of a torch CUDA device (CUDA_VISIBLE_DEVICES renumbers devices)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if dev.index < len(ids) and ids[dev.index].isdigit():
+            return int(ids[dev.index])
+    return dev.index
 
 
 # --------------------------------------------------------------------------- arms
@@ -511,7 +536,7 @@ def run_forecaster(args, w, rank, world, local_rank):
     for i in range(args.warmup):
         train_step(net, opt, *dev_pool[i % 4])
     torch.cuda.synchronize()
-    sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local_rank)
+    sampler = ClockSampler(smi_index(dev))
     sampler.start()
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -622,39 +647,100 @@ def forecaster_mlp_bwd_ms(w, b_rank, dev):
     return tot / 3, flops
 
 
+def cpu_full_shape(w, steps, warmup):
+    """The reference's ops/ path restated on the host cores (oracle/ttt_oracle.py, fp32) at
+    the workload's FULL shape: every step runs all B * NH streams over the whole sequence,
+    in chunks of 4 streams (batched matmuls over all streams at once run several times
+    slower on the host, cache-bound). Warm-up steps run one chunk each. Returns (tokens/s
+    over the timed steps, threads, sample description)."""
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import synthetic as S
+    import ttt_oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    NC = w["L"] // CS
+    mk = S.make_linear_inputs if w["kind"] == "linear" else S.make_mlp_inputs
+    kw = {} if w["kind"] == "linear" else {"FF": w["FF"]}
+    d = mk(w["B"], w["NH"], NC, CS, w["F"], seed=0, **kw)
+    names = LIN if w["kind"] == "linear" else MLP
+    scan = O.linear_scan if w["kind"] == "linear" else O.mlp_scan
+    chunks = []
+    for b in range(w["B"]):
+        for h0 in range(0, w["NH"], 4):
+            h1 = min(h0 + 4, w["NH"])
+            chunks.append({k: (v[h0:h1] if k in ("ln_w", "ln_b") else v[b:b + 1, h0:h1]) for k, v in d.items()})
+    extra = () if w["kind"] == "linear" else (w["ckpt"], memo_of(w))
+
+    def one(c):
+        with torch.no_grad():
+            scan(*(c[k] for k in names), *extra)
+
+    for _ in range(warmup):
+        one(chunks[0])
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for c in chunks:
+            one(c)
+    dt = time.perf_counter() - t0
+    tokens = w["B"] * w["NH"] * w["L"] * steps
+    sample = (f"full shape B={w['B']} NH={w['NH']} L={w['L']}, {steps} step(s), all streams in chunks of 4, "
+              f"fp32, forward")
+    return tokens / dt, threads, sample
+
+
 def run_reference(args, w, rank, world):
+    """The reference arm: rank 0 alone times the CPU port of the reference's ops/ path on the
+    host cores, on this arm's workload and config; other ranks exit without work."""
     if rank != 0:
         return
-    value, cores, sample = forecaster_cpu_reference(w) if w["kind"] == "forecaster" else cpu_reference(w)
+    config = {"workload": args.workload, **{k: v for k, v in w.items() if k in ("B", "NH", "L", "F", "FF")}}
+    if w["kind"] in ("linear", "mlp") and not w["bwd"]:
+        value, cores, sample = cpu_full_shape(w, args.steps, args.warmup)
+        config = ours_config(args, w, 1)
+    elif w["kind"] == "forecaster":
+        value, cores, sample = forecaster_cpu_reference(w)
+    else:
+        value, cores, sample = cpu_reference(w)
+        config["shape_run"] = sample
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "scaling": "strong" if w["kind"] == "forecaster" else "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic",
-        "config": {"workload": args.workload, **{k: v for k, v in w.items() if k in ("B", "NH", "L", "F", "FF")}},
+        "data": "synthetic", "config": config,
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args, w, rank, world, local_rank):
-    import torch.distributed as dist
+def ours_config(args, w, world, sharded=False):
+    """The `config` object of a line (the reference arm reports the same one)."""
+    par = (f"batch split over {world} GPU(s) (strong scaling), no collective" if sharded
+           else f"streams sharded over {world} GPU(s), no collective")
+    return {"workload": args.workload if not sharded else "mlp_fwdbwd_c3", "B_per_rank": w["B"], "NH": w["NH"],
+            "L": w["L"], "F": w["F"], "FF": w["FF"], "CS": CS, "checkpoint_group_size": w["ckpt"],
+            "memo_segment_size": memo_of(w) if w["kind"] == "mlp" else w["memo"],
+            "global_batch": w["B"] * (1 if sharded else world), "parallelism": par,
+            "l2": "inputs larger than L2 (no flush)"}
 
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    d, dO = make_inputs(w, dev, seed=rank)
-    NC = w["L"] // CS
-    tokens_rank = w["B"] * w["NH"] * w["L"]
+
+def measure(args, w, d, dO, dev, rank, world, global_tokens, with_cpu):
+    """Device-timed steps of workload w on this rank's inputs (barrier + synchronize around
+    the region, max over ranks), the dominant kernel's back-to-back launch time and the
+    end-to-end leg. Returns the record on rank 0 (None elsewhere): step time, tokens/s of the
+    whole job (global_tokens per step), roofline, e2e, launches, clocks, CPU baseline."""
+    import torch.distributed as dist
 
     def barrier():
         if world > 1:
             dist.barrier()
 
+    tokens_rank = w["B"] * w["NH"] * w["L"]
     for _ in range(args.warmup):
         kernel_step(w, d, dO)
     torch.cuda.synchronize()
-    sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local_rank)
+    sampler = ClockSampler(smi_index(dev))
     sampler.start()
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -669,34 +755,30 @@ def run_ours(args, w, rank, world, local_rank):
     barrier()
     clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1)
-    # per-kernel durations of the dominant kernel (backward for fwd+bwd workloads)
-    kern_ms = kernel_durations(w, d, dO, args.steps)
-    # end-to-end through the public API with host buffers
+    kern_ms, kname = kernel_durations(w, d, dO, args.steps)
     e2e_ms, h2d, d2h = e2e_time(w, d, dO, dev, args)
-    ms, e2e_ms = max_over_ranks([ms, e2e_ms], world, dev)
+    ms, e2e_ms, kern_ms = max_over_ranks([ms, e2e_ms, kern_ms], world, dev)
     if rank != 0:
-        return
+        return None
     ms_step = ms / args.steps
-    value = weak_scaling_value(world, tokens_rank, ms_step)
     hbm, bf16, bf16_sus, src = peaks()
     alg = algorithmic(w)
     dom = "bwd" if w["bwd"] else "fwd"  # dominant kernel: the backward when there is one
     dom_bytes, dom_flops = alg[dom]
-    dom_ms = kern_ms
     if w["kind"] in ("mlp", "memo"):
-        achieved = dom_flops * tokens_rank / (dom_ms / 1e3) / 1e12
+        achieved = dom_flops * tokens_rank / (kern_ms / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16}
     else:
-        achieved = dom_bytes * tokens_rank / (dom_ms / 1e3) / 1e9
+        achieved = dom_bytes * tokens_rank / (kern_ms / 1e3) / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm}
-    kname = w["kind"] + "_" + dom
-    traffic = NCU_TRAFFIC.get((args.workload, kname))
+    traffic = NCU_TRAFFIC.get((w.get("name", args.workload), kname))
     roof.update({
         "traffic": traffic[0] * (tokens_rank / traffic[1]) if traffic else None,
         "traffic_source": traffic[2] if traffic else None,
         "peak_source": src,
         "kernel": kname,
-        "kernel_ms": dom_ms,
+        "kernel_ms": kern_ms,
+        "kernel_timing": "back-to-back launches between CUDA events, average (max over ranks)",
         "algorithmic_bytes_per_token": dom_bytes,
         "algorithmic_flops_per_token": dom_flops,
     })
@@ -706,23 +788,72 @@ def run_ours(args, w, rank, world, local_rank):
     roof["hbm_frac_of_step"] = (tokens_rank / (ms_step / 1e3)) / roof["hbm_roofline_tokens_per_s"]
     roof["tensor_roofline_tokens_per_s"] = bf16 * 1e12 / step_flops
     roof["tensor_frac_of_step"] = (tokens_rank / (ms_step / 1e3)) / roof["tensor_roofline_tokens_per_s"]
-    line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
-        "config": {"workload": args.workload, "B_per_rank": w["B"], "NH": w["NH"], "L": w["L"], "F": w["F"],
-                   "FF": w["FF"], "CS": CS, "checkpoint_group_size": w["ckpt"], "memo_segment_size": w["memo"],
-                   "global_batch": w["B"] * world, "parallelism": f"streams sharded over {world} GPU(s), no collective",
-                   "l2": "inputs larger than L2 (no flush)"},
+    rec = {
+        "value": global_tokens / (ms_step / 1e3), "unit": "tokens/s", "ms_per_step": ms_step,
         "roofline": roof,
-        "e2e": {"value": world * tokens_rank / (e2e_ms / args.steps / 1e3), "unit": "tokens/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps},
+        "e2e": {"value": global_tokens / (e2e_ms / args.steps / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                "ms_per_step": e2e_ms / args.steps},
         "gpu_launches": launches,
         "clocks": clocks,
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if with_cpu:
         v, cores, sample = cpu_reference(w)
-        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+        rec["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    return rec
+
+
+def run_fwdbwd_sharded(args, rank, world, dev):
+    """Config 3 (TTT-MLP forward+backward, B64 NH16 L8192) as one global batch split over the
+    ranks by batch (sharding.shard), strong scaling. Every rank builds the same seeded global
+    inputs on its device, keeps its slice and frees the rest."""
+    import sharding
+
+    w = dict(WORKLOADS["mlp_fwdbwd_c3"], name="mlp_fwdbwd_c3")
+    Bg = w["B"]
+    if Bg % world:
+        raise SystemExit(f"config-3 batch {Bg} does not split over {world} ranks")
+    g, gO = make_inputs(w, dev, seed=0)
+    d = sharding.shard(g, rank, world)
+    b0, b1 = sharding.batch_range(Bg, rank, world)
+    dO = gO[b0:b1].contiguous()
+    del g, gO
+    torch.cuda.empty_cache()
+    wr = dict(w, B=b1 - b0)
+    rec = measure(args, wr, d, dO, dev, rank, world, Bg * w["NH"] * w["L"], with_cpu=(world == 1))
+    del d, dO
+    torch.cuda.empty_cache()
+    if rec is None:
+        return None
+    rec["config"] = ours_config(args, dict(w, B=Bg // world), world, sharded=True)
+    rec["config"]["global_batch"] = Bg
+    rec["scaling"] = "strong"
+    rec["metric"] = "TTT-MLP fwd+bwd tokens/s (B*H*L), config 3 global batch split over the GPUs"
+    return rec
+
+
+def run_ours(args, w, rank, world, local_rank):
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    d, dO = make_inputs(w, dev, seed=rank)
+    tokens_rank = w["B"] * w["NH"] * w["L"]
+    rec = measure(args, w, d, dO, dev, rank, world, world * tokens_rank, with_cpu=(world == 1 and not args.no_cpu_baseline))
+    del d, dO
+    torch.cuda.empty_cache()
+    fwdbwd = None
+    if args.workload == "mlp_fwd_c1" and not args.no_fwdbwd:
+        fwdbwd = run_fwdbwd_sharded(args, rank, world, dev)
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": rec["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": rec["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
+        "config": ours_config(args, w, world),
+    }
+    line.update({k: v for k, v in rec.items() if k not in ("value", "unit", "ms_per_step")})
+    if fwdbwd is not None:
+        line["fwdbwd"] = fwdbwd
     print(json.dumps(line), flush=True)
 
 
@@ -742,44 +873,61 @@ def weak_scaling_value(world, tokens_per_rank, ms_per_step):
     return world * tokens_per_rank / (ms_per_step / 1e3)
 
 
-def kernel_durations(w, d, dO, steps):
-    """Average device time of the dominant kernel's launch (CUDA events on its stream)."""
+def dominant_launch(w, d, dO):
+    """A closure that enqueues one call of the dominant kernel's entry point (the backward
+    when the workload has one), with every input it reads prepared beforehand (the forward
+    it follows has run), and that kernel's name."""
     import _core
 
-    stream = torch.cuda.current_stream()
-    tot = 0.0
-    n = max(1, min(steps, 5))
     if w["kind"] == "prologue":
-        return sum(prologue_step(w, d, dO, time_bwd_kernel=True) for _ in range(n)) / n
+        from prologue import concat_projections
+
+        B, L, NH, F = w["B"], w["L"], w["NH"], w["F"]
+        Wcat, bcat, _, _ = concat_projections(*(d[k] for k in PRO[1:11]))
+        P = torch.addmm(bcat, d["hidden"].reshape(B * L, -1), Wcat.t())
+        scale = BASE_LR / (F * CS)
+        return (lambda: _core.prologue_backward(P, B, L, NH, F, CS, d["ln_w"], d["ln_b"], d["freqs_cos"],
+                                                d["freqs_sin"], scale, *(dO[k] for k in PRO_OUTS))), "prologue_bwd"
     if w["kind"] == "epilogue":
-        return sum(epilogue_step(w, d, dO, time_bwd_kernel=True) for _ in range(n)) / n
+        Y = _core.post_norm_forward(d["XQW"], d["pn_w"], d["pn_b"], POST_NORM_EPS)
+        d2 = dO.reshape(Y.shape)
+        dY = torch.mm(d2, d["wo_w"])
+        return (lambda: _core.post_norm_backward(d["XQW"], d["pn_w"], d["pn_b"], POST_NORM_EPS, dY, d2)), \
+            "post_norm_bwd"
+    if w["kind"] == "memo":
+        _, scratch = _core.memo_mix_forward(*(d[k] for k in MEMO), w["memo"], return_scratch=True)
+        return (lambda: _core.memo_mix_backward(*(d[k] for k in MEMO), w["memo"], dO, scratch=scratch)), \
+            "memo_bwd (mix + dXK launches)"
+    if w["kind"] == "linear":
+        if w["bwd"]:
+            _, Wl, bl, Wc, bc, Z = _core.linear_forward(*(d[k] for k in LIN), w["ckpt"])
+            return (lambda: _core.linear_backward(d["ln_w"], d["ln_b"], Wc, bc, d["XQ"], d["XV"], d["XK"], d["eta"],
+                                                  dO, w["ckpt"], Z=Z, W_last=Wl, b_last=bl)), "linear_bwd"
+        return (lambda: _core.linear_forward(*(d[k] for k in LIN), w["ckpt"], for_backward=False)), "linear_fwd"
+    if w["bwd"]:
+        _, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], memo_of(w))
+        return (lambda: _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO,
+                                           w["ckpt"], saved=zs, W1_last=last[0], W2_last=last[2])), "mlp_bwd"
+    return (lambda: _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], memo_of(w), for_backward=False)), "mlp_fwd"
+
+
+def kernel_durations(w, d, dO, steps):
+    """Average device time of one launch of the dominant kernel: n calls enqueued back to
+    back between two CUDA events on their stream, so the host work of each call (output
+    allocation, tensor-map encoding) overlaps the previous launch and the GPU never idles
+    between them. Returns (ms per launch, kernel name)."""
+    launch, name = dominant_launch(w, d, dO)
+    stream = torch.cuda.current_stream()
+    n = max(3, min(steps, 10))
+    launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
     for _ in range(n):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        if w["kind"] == "memo":
-            e0.record(stream)
-            _core.memo_mix_backward(*(d[k] for k in MEMO), w["memo"], dO)
-        elif w["kind"] == "linear":
-            if w["bwd"]:
-                _, Wl, bl, Wc, bc, Z = _core.linear_forward(*(d[k] for k in LIN), w["ckpt"])
-                e0.record(stream)
-                _core.linear_backward(d["ln_w"], d["ln_b"], Wc, bc, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
-                                      Z=Z, W_last=Wl, b_last=bl)
-            else:
-                e0.record(stream)
-                _core.linear_forward(*(d[k] for k in LIN), w["ckpt"], for_backward=False)
-        else:
-            if w["bwd"]:
-                _, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"])
-                e0.record(stream)
-                _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
-                                   saved=zs, W1_last=last[0], W2_last=last[2])
-            else:
-                e0.record(stream)
-                _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], w["memo"], for_backward=False)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        tot += e0.elapsed_time(e1)
-    return tot / n
+        launch()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n, name
 
 
 def e2e_time(w, d, dO, dev, args):
@@ -844,6 +992,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mlp_fwd_c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-fwdbwd", action="store_true",
+                    help="skip the config-3 forward+backward record of the default workload")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's per-rank batch (smaller cases for profiling)")
     args = ap.parse_args()

@@ -245,6 +245,19 @@ int ttt_post_norm_bwd(int B, int NH, int L, int F, const void* XQW, int dt, cons
  */
 int ttt_device_status(unsigned int* status);
 
+/*
+ * Test switch for the bounded waits (no counterpart in the reference). While enabled
+ * (enable != 0), every launch of the tensor-core TTT-MLP forward leaves the copies of each
+ * stream's first mini-batch un-issued, so the wait for them can only end by its time limit,
+ * which this call sets to wait_limit_ns (0: the library's 2 s; larger values are refused
+ * with TTT_ERR_SHAPE). The kernel then sets bit 0 of the device error word
+ * (ttt_device_status), waits (bounded) for the copies it did issue, frees its tensor memory
+ * and returns; that call's outputs are void. Nothing faults and nothing is left in flight.
+ * Disabling restores the 2 s limit. The setting is process-wide and only affects launches
+ * enqueued after the call. For tests of failure reporting; off by default.
+ */
+int ttt_test_hold_first_stage(int enable, unsigned long long wait_limit_ns);
+
 /* Bytes of scratch ttt_mlp_bwd needs for these sizes. */
 size_t ttt_mlp_bwd_scratch_bytes(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_group_size);
 

@@ -316,6 +316,95 @@ def forecaster_case(ref_root, B, L, W, NH, CS, pred_len, d_in, seed):
     return {k: _np(v) for k, v in res.items()}
 
 
+def forecaster_main_case(ref_root, B, W, NH, memo, seed):
+    """The reference's TTTForecaster built from main.py's own ModelConfig (main.py:54-65: seq_len
+    384, mini_batch_size 64, ttt_base_lr 0.05, checkpoint group 16, ttt_mlp with its F x F
+    inner MLP, d_in = d_out = 1 for the univariate "S" features, pred_len 96) in float64 with
+    MSE loss and the gradient of every parameter.
+
+    The layer's TritonMLP launch runs the reference's own dual-form step
+    (ops/ttt_mlp.py:compute_mini_batch) mini-batch by mini-batch, and its memo states are the
+    states after mini-batch i for i % memo == 0 (the definition of kernels/mlp_forward.py:
+    193-226), non-differentiable as mlp_triton.py:196 marks them. With memo < NC the layer's
+    mixing loop runs the reference's cached read-out kernel under the CPU interpreter, which
+    addresses only (b, h) = (0, 0) correctly (kernels/mlp_cached_readout.py:66-70), so that case
+    uses B = NH = 1 (model_dim 32 keeps main.py's head_dim 32)."""
+    sys.path.insert(0, ref_root)
+    import forecast
+    import ttt_layer
+    from kernels.mlp_cached_readout import mlp_cached_readout_kernel
+    from ops.ttt_mlp import compute_mini_batch
+
+    L, CS, pred_len, d_in = 384, 64, 96, 1
+    NC = L // CS
+    memo = NC if memo is None else memo
+    if memo < NC and B * NH != 1:
+        raise ValueError("the reference's cached read-out kernel is correct only for B = NH = 1")
+
+    class ScanStep:
+        @staticmethod
+        def apply(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, ckpt, memo_seg):
+            params = {"W1_states": W1, "b1_states": b1, "W2_states": W2, "b2_states": b2,
+                      "ttt_norm_weight": ln_w, "ttt_norm_bias": ln_b}
+            outs, mem = [], {k: [] for k in ("W1_states", "b1_states", "W2_states", "b2_states")}
+            for n in range(XQ.shape[2]):
+                x = {"XQ": XQ[:, :, n], "XV": XV[:, :, n], "XK": XK[:, :, n], "eta": eta[:, :, n]}
+                params, o = compute_mini_batch(params, x)
+                outs.append(o)
+                if n % memo_seg == 0:
+                    for k in mem:
+                        mem[k].append(params[k].detach())
+            memo_t = [torch.stack(mem[k], dim=2) for k in ("W1_states", "b1_states", "W2_states", "b2_states")]
+            # handed over non-contiguous, as in memo_mix_case: with B = NH = 1 a contiguous
+            # output makes the mixing loop's segment copies aliases it writes in place
+            xqw = torch.stack(outs, dim=2).transpose(-1, -2).contiguous().transpose(-1, -2)
+            return (xqw, *memo_t)
+
+    def readout(XQ_seg, W1, b1, W2, b2, ln_w, ln_b):
+        Bq, NHq, NCs, CSq, F = XQ_seg.shape
+        FF = W1.shape[-1]
+        XQ_seg, W1, b1, W2, b2 = (x.detach().contiguous() for x in (XQ_seg, W1, b1, W2, b2))
+        out = torch.empty_like(XQ_seg)
+        mlp_cached_readout_kernel[(1, 1, NCs)](
+            XQ_seg, W1, b1, W2, b2, ln_w.detach(), ln_b.detach(), out,
+            CS_F_stride=CSq * F, F_FF_stride=F * FF, FF_F_stride=FF * F, F_stride=F, FF_stride=FF,
+            NH=1, CS=CSq, F=F, FF=FF, num_warps=4,
+        )
+        return XQ_seg + out
+
+    torch.manual_seed(seed)
+    cfg = forecast.ModelConfig(seq_len=L, model_dim=W, num_heads=NH, num_layers=1, ssm_layer="ttt_mlp",
+                               mini_batch_size=CS, ttt_base_lr=0.05, scan_checkpoint_group_size=16,
+                               latent_height=1, latent_width=1, compressed_num_frames=None,
+                               mem_cache_segment_n_mini_batches=memo)
+    saved = ttt_layer.TritonMLP, ttt_layer.mlp_cached_readout_triton
+    ttt_layer.TritonMLP, ttt_layer.mlp_cached_readout_triton = ScanStep, readout
+    try:
+        model = forecast.TTTForecaster(cfg, d_in=d_in, d_out=d_in, pred_len=pred_len).double()
+        with torch.no_grad():  # non-trivial gate, LayerNorm and inner-bias parameters
+            layer = model.ttt.ttt
+            layer.learnable_ttt_lr_bias.normal_(0, 0.5)
+            for t in (layer.ttt_norm_weight, layer.post_norm.weight):
+                t.add_(0.1 * torch.randn_like(t))
+            for t in (layer.ttt_norm_bias, layer.post_norm.bias, layer.b1, layer.b2):
+                t.normal_(0, 0.05)
+        x = torch.randn(B, L, d_in, dtype=torch.float64)
+        y = torch.randn(B, pred_len, d_in, dtype=torch.float64)
+        out = model(x)
+        loss = torch.nn.functional.mse_loss(out, y)
+        loss.backward()
+    finally:
+        ttt_layer.TritonMLP, ttt_layer.mlp_cached_readout_triton = saved
+    res = {"in_x": x, "in_y": y, "out": out.detach(), "loss": loss.detach(), "CS": torch.tensor(CS),
+           "pred_len": torch.tensor(pred_len), "NH": torch.tensor(NH), "ckpt": torch.tensor(16),
+           "memo": torch.tensor(memo), "base_lr": torch.tensor(0.05)}
+    for k, v in model.state_dict().items():
+        res["p_" + k] = v
+    for k, v in model.named_parameters():  # wu gets no gradient with one memo segment: zeros
+        res["g_" + k] = v.grad if v.grad is not None else torch.zeros_like(v)
+    return {k: _np(v) for k, v in res.items()}
+
+
 def main():
     if len(sys.argv) < 2:
         raise SystemExit("usage: python tests/golden/make_golden.py /path/to/ttt-triton")
@@ -325,18 +414,25 @@ def main():
     import ops as ref_ops
 
     cases = {
-        "linear_small": linear_case(ref_ops, B=2, NH=2, NC=4, F=32, ckpt=2, eta_mode="causal", seed=10),
-        "linear_equal_eta": linear_case(ref_ops, B=1, NH=2, NC=3, F=64, ckpt=16, eta_mode="equal", seed=11),
-        "linear_config0_fwd": linear_case(ref_ops, B=2, NH=4, NC=16, F=64, ckpt=16, eta_mode="causal", seed=0, with_grads=False, perturb=False),
-        "mlp_small": mlp_case(ref_ops, B=2, NH=2, NC=3, F=16, FF=64, ckpt=2, eta_mode="causal", seed=20),
-        "mlp_fxf_equal_eta": mlp_case(ref_ops, B=1, NH=2, NC=3, F=32, FF=32, ckpt=16, eta_mode="equal", seed=21),
-        "cached_readout": cached_readout_case(ref_root, NCs=3, F=32, FF=128, seed=30),
-        "memo_mix": memo_mix_case(ref_root, NC=7, F=32, FF=128, M=2, seed=40),
-        "prologue": prologue_case(ref_root, B=2, L=64, W=128, NH=2, CS=16, seed=50),
-        "epilogue": epilogue_case(ref_root, B=2, L=32, W=128, NH=4, CS=16, seed=60),
-        "forecaster": forecaster_case(ref_root, B=2, L=64, W=128, NH=2, CS=16, pred_len=8, d_in=7, seed=70),
+        "linear_small": lambda: linear_case(ref_ops, B=2, NH=2, NC=4, F=32, ckpt=2, eta_mode="causal", seed=10),
+        "linear_equal_eta": lambda: linear_case(ref_ops, B=1, NH=2, NC=3, F=64, ckpt=16, eta_mode="equal", seed=11),
+        "linear_config0_fwd": lambda: linear_case(ref_ops, B=2, NH=4, NC=16, F=64, ckpt=16, eta_mode="causal", seed=0, with_grads=False, perturb=False),
+        "mlp_small": lambda: mlp_case(ref_ops, B=2, NH=2, NC=3, F=16, FF=64, ckpt=2, eta_mode="causal", seed=20),
+        "mlp_fxf_equal_eta": lambda: mlp_case(ref_ops, B=1, NH=2, NC=3, F=32, FF=32, ckpt=16, eta_mode="equal", seed=21),
+        "cached_readout": lambda: cached_readout_case(ref_root, NCs=3, F=32, FF=128, seed=30),
+        "memo_mix": lambda: memo_mix_case(ref_root, NC=7, F=32, FF=128, M=2, seed=40),
+        "prologue": lambda: prologue_case(ref_root, B=2, L=64, W=128, NH=2, CS=16, seed=50),
+        "epilogue": lambda: epilogue_case(ref_root, B=2, L=32, W=128, NH=4, CS=16, seed=60),
+        "forecaster": lambda: forecaster_case(ref_root, B=2, L=64, W=128, NH=2, CS=16, pred_len=8, d_in=7, seed=70),
+        # main.py's own model configuration (CS 64, head_dim 32, F x F inner MLP)
+        "forecaster_main": lambda: forecaster_main_case(ref_root, B=2, W=128, NH=4, memo=None, seed=80),
+        "forecaster_main_memo": lambda: forecaster_main_case(ref_root, B=1, W=32, NH=1, memo=2, seed=81),
     }
-    for name, res in cases.items():
+    only = sys.argv[2:]  # optional case names: regenerate just those
+    if only:
+        cases = {k: v for k, v in cases.items() if k in only}
+    for name, make in cases.items():
+        res = make()
         path = os.path.join(HERE, name + ".npz")
         np.savez_compressed(path, **res)
         print(f"wrote {path} ({os.path.getsize(path) / 1024:.0f} KiB)")

@@ -168,3 +168,20 @@ def test_post_norm_host_checks():
     assert fwd(X=ctypes.c_void_p(0x1008)) == -7
     assert _lib.lib.ttt_post_norm_bwd(2, 4, 32, 64, A, 1, A, A, 1e-6, None, A, A, A, None, None, None) == -1
     assert _lib.lib.ttt_post_norm_bwd(2, 4, 32, 64, A, 1, A, A, 1e-6, A, A, A, A, A, None, None) == -1
+
+
+def test_noalloc_backward_rejects_requests_beyond_its_fixed_scratch():
+    """ttt_linear_bwd_noalloc checks the scratch its sizes need against the library's fixed
+    16 MiB array before any CUDA call: a request twice the array (batch 64, 8 heads, group 16) is refused with
+    TTT_ERR_SCRATCH and a message naming both sizes."""
+    def call(B, NH, NC, ckpt):
+        return _lib.lib.ttt_linear_bwd_noalloc(
+            B, NH, NC, 16, 64, ckpt, FAKE, FAKE, 0, FAKE, FAKE, FAKE, 1, FAKE, 1, FAKE, 1, FAKE, 1, FAKE, 1,
+            FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, None)
+
+    need = _lib.lib.ttt_linear_bwd_scratch_bytes(64, 8, 256, 16, 64, 16)
+    assert need > 16 << 20
+    assert call(64, 8, 256, 16) == -5
+    msg = _lib.lib.ttt_last_error().decode()
+    assert str(need) in msg and str(16 << 20) in msg
+    assert call(0, 8, 256, 16) == -2  # the shape checks run first

@@ -189,6 +189,29 @@ def test_forward_sampled_streams_few_and_many(B, NH, FF):
             assert_close(f"{name}_memo[{b},{hh}]", memo[i][b:b + 1, hh:hh + 1], r[name + "_memo"], 2e-2)
 
 
+def test_a_wait_that_runs_out_is_reported_and_the_device_stays_usable():
+    """With the first stage's copies held back (ttt_test_hold_first_stage) the forward's
+    wait for them runs out after 1 ms: the launch completes, the device error word reports
+    bit 0, and the next normal launch gives the oracle's results with the word clear."""
+    import _lib
+
+    _lib.device_status()
+    d, _ = make(2, 3, 4, 16, 64, 256, torch.bfloat16, seed=52)
+    _lib.hold_first_stage(True, 1_000_000)
+    try:
+        _core.mlp_forward(*(d[k] for k in NAMES), 2, None, for_backward=False)
+        torch.cuda.synchronize()
+    finally:
+        _lib.hold_first_stage(False)
+    assert _lib.device_status() & 1
+    out, _, _, _, _ = _core.mlp_forward(*(d[k] for k in NAMES), 2, None, for_backward=False)
+    r = O.mlp_scan(*(oracle_inputs(d)[k] for k in NAMES))
+    assert_close("XQW", out, r["XQW"], 2e-2)
+    assert _lib.device_status() == 0
+    with pytest.raises(RuntimeError, match="wait limit"):
+        _lib.hold_first_stage(True, 3_000_000_000)
+
+
 def test_no_bounded_wait_gave_up():
     """The TMA-staged kernels report a stage that never landed in the device error word;
     after a run it must be clear."""
@@ -198,3 +221,24 @@ def test_no_bounded_wait_gave_up():
     d, _ = make(2, 3, 5, 16, 64, 256, torch.bfloat16, seed=51)
     _core.mlp_forward(*(d[k] for k in NAMES), 2, None, for_backward=False)
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_ops_ttt_mlp_gradients_match_oracle(dtype):
+    """ops.ttt_mlp (signature and [B, NC, CS, NH, F] output of ops/ttt_mlp.py:70-99) is
+    differentiable in every tensor argument: its gradients match the oracle's and come back
+    in each argument's own dtype (fp32 parameters get fp32 gradients, as TritonMLP's do)."""
+    import ops
+
+    d, dO = make(2, 2, 5, 16, 64, 256, dtype, seed=61)
+    leaves = {k: d[k].detach().clone().requires_grad_(True) for k in NAMES}
+    out = ops.ttt_mlp(leaves["XK"], leaves["XQ"], leaves["XV"], leaves["eta"], leaves["ln_w"], leaves["ln_b"],
+                      leaves["W1"], leaves["b1"], leaves["W2"], leaves["b2"], 2)
+    assert out.shape == (2, 5, 16, 2, 64) and out.dtype == dtype
+    out.backward(dO.permute(0, 2, 3, 1, 4))
+    ref_grads, ref = O.mlp_grads(oracle_inputs(d), dO.double().cpu())
+    tol = TOL[dtype]
+    assert_close("XQW", out.permute(0, 3, 1, 2, 4), ref["XQW"], tol)
+    for k in NAMES:
+        assert leaves[k].grad.dtype == d[k].dtype, k
+        assert_close("d" + k, leaves[k].grad, ref_grads[k], tol)

@@ -90,13 +90,17 @@ def test_epilogue_oracle_matches_reference_forward_tail():
         assert O.rel_l2(grads[k], g["grad_" + k].double()) < 1e-6, k
 
 
-def test_forecaster_oracle_matches_reference_model():
+@pytest.mark.parametrize("name", ["forecaster", "forecaster_main", "forecaster_main_memo"])
+def test_forecaster_oracle_matches_reference_model(name):
     """The forecaster composition (in_proj, process_input, scan, memo mixing, post_norm + wo,
-    head) against the reference's own TTTForecaster: output, loss and every gradient."""
+    head) against the reference's own TTTForecaster: output, loss and every gradient. The
+    `forecaster_main*` goldens are main.py's model configuration (CS 64, head_dim 32, base
+    learning rate 0.05, one input channel), the `_memo` one with three memo segments mixed
+    through the reference's cached read-out kernel."""
     import ttt_oracle as Or
     from forecaster import rope_table_3d
 
-    inp, g = load_golden("forecaster")
+    inp, g = load_golden(name)
     P = {k[2:]: v.double() for k, v in g.items() if k.startswith("p_")}
     L = inp["x"].shape[1]
     F = P["ttt.ttt.W1"].shape[-1]

@@ -8,6 +8,7 @@ synchronises the device.
 
 from __future__ import annotations
 
+import functools
 import math
 
 import torch
@@ -17,6 +18,24 @@ from _lib import check, dtype_code, lib, ptr, require_cuda, stream_of
 
 def _c(t):
     return t.contiguous()
+
+
+def _on_tensor_device(fn):
+    """Run an entry point with its first tensor argument's device current: the library
+    launches on the current device and resolves the per-device error word, scratch address
+    and tensor maps there, while the stream comes from the tensors' device."""
+
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        for a in args:
+            if isinstance(a, torch.Tensor):
+                if a.is_cuda and a.device.index != torch.cuda.current_device():
+                    with torch.cuda.device(a.device):
+                        return fn(*args, **kwargs)
+                break
+        return fn(*args, **kwargs)
+
+    return wrapper
 
 
 def _check_acts(XQ, XV, XK, eta):
@@ -47,6 +66,7 @@ def _state(t, shape, name):
 
 
 # --------------------------------------------------------------------------- Linear
+@_on_tensor_device
 def linear_forward(ln_w, ln_b, W1, b1, XQ, XV, XK, eta, checkpoint_group_size, for_backward=True):
     """TTT-Linear scan forward. Returns (XQW in XQ's dtype, W_last, b_last, W_ckpt, b_ckpt, Z).
 
@@ -86,6 +106,7 @@ def linear_forward(ln_w, ln_b, W1, b1, XQ, XV, XK, eta, checkpoint_group_size, f
     return XQW, W_last, b_last, W_ckpt, b_ckpt, Z
 
 
+@_on_tensor_device
 def linear_backward(ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, dXQW, checkpoint_group_size, grad_dtype=None,
                     Z=None, W_last=None, b_last=None):
     """TTT-Linear scan backward. Returns (d_ln_w [B,NH,F] per-(b,h) partials, d_ln_b,
@@ -133,6 +154,7 @@ def linear_backward(ln_w, ln_b, W_ckpt, b_ckpt, XQ, XV, XK, eta, dXQW, checkpoin
 
 
 # --------------------------------------------------------------------------- MLP
+@_on_tensor_device
 def mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, checkpoint_group_size, memo_segment_size=None,
                 for_backward=True):
     """TTT-MLP scan forward. Returns (XQW, (W1,b1,W2,b2)_last, (…)_ckpt or None, (…)_memo or None,
@@ -192,6 +214,7 @@ def mlp_forward(ln_w, ln_b, W1, b1, W2, b2, XQ, XV, XK, eta, checkpoint_group_si
     return XQW, last, ck, memo, zs
 
 
+@_on_tensor_device
 def mlp_backward(ln_w, ln_b, ckpts, XQ, XV, XK, eta, dXQW, checkpoint_group_size, grad_dtype=None,
                  saved=None, W1_last=None, W2_last=None):
     """TTT-MLP scan backward. ckpts = (W1, b1, W2, b2) checkpoints from mlp_forward.
@@ -261,6 +284,7 @@ def _lead_strides(t, inner_numel, name):
     return t, t.stride(0), t.stride(1)
 
 
+@_on_tensor_device
 def mlp_cached_readout(XQ_seg, W1, b1, W2, b2, ln_w, ln_b):
     """XQ_seg + LN(gelu(XQ_seg W1 + b1) W2 + b2) in fp32 (LN eps 1e-6)."""
     require_cuda(XQ_seg, W1, b1, W2, b2, ln_w, ln_b)
@@ -310,6 +334,7 @@ def _memo_args(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, 
     return (B, NH, NC, CS, F, FF, M), (_c(XQW), _c(XQ), _c(XK), _c(XU)), mem, ln_w, ln_b
 
 
+@_on_tensor_device
 def memo_mix_forward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, memo_segment_size,
                      return_scratch=False):
     """Memo-state mixing of the TTT-MLP output (ttt_layer.py:503-559) as one launch sequence.
@@ -332,6 +357,7 @@ def memo_mix_forward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, 
     return (out, scratch) if return_scratch else out
 
 
+@_on_tensor_device
 def memo_mix_backward(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, memo_segment_size, dOut,
                       scratch=None):
     """Gradients of the memo mixing: (dXQW, dXU, dXK), dXK being the part through the
@@ -382,6 +408,7 @@ def _prologue_args(P, B, L, NH, F, CS, ln_w, ln_b, rope_cos, rope_sin):
     return ld, ln_w, ln_b, _c(rope_cos), _c(rope_sin)
 
 
+@_on_tensor_device
 def prologue_forward(P, B, L, NH, F, CS, ln_w, ln_b, rope_cos, rope_sin, eta_scale):
     """Element-wise prologue over the projection matrix P ([B * L, prologue_ld], biases
     included). Returns XQ, XK, XV, XU [B, NH, NC, CS, F] and eta [B, NH, NC, CS, CS] in P's dtype."""
@@ -397,6 +424,7 @@ def prologue_forward(P, B, L, NH, F, CS, ln_w, ln_b, rope_cos, rope_sin, eta_sca
     return (*outs, eta)
 
 
+@_on_tensor_device
 def prologue_backward(P, B, L, NH, F, CS, ln_w, ln_b, rope_cos, rope_sin, eta_scale, dXQ, dXK, dXV, dXU, deta):
     """Gradient of the element-wise prologue: returns dP ([B * L, prologue_ld], P's dtype;
     padding columns zero), d ln_w, d ln_b ([NH, F] fp32) and the column sums of dP (the
@@ -436,6 +464,7 @@ def _post_norm_args(XQW, ln_w, ln_b):
     return B, NH, NC * CS, F, _c(XQW), _c(ln_w.to(torch.float32)), _c(ln_b.to(torch.float32))
 
 
+@_on_tensor_device
 def post_norm_forward(XQW, ln_w, ln_b, eps):
     """LayerNorm over the width of the scan output, read in its kernel layout: returns the
     normalised rows [B * L, NH * F] in XQW's dtype (token order)."""
@@ -447,6 +476,7 @@ def post_norm_forward(XQW, ln_w, ln_b, eps):
     return Y
 
 
+@_on_tensor_device
 def post_norm_backward(XQW, ln_w, ln_b, eps, dY, dOut=None):
     """Gradient of post_norm_forward: returns d XQW (kernel layout, XQW's dtype), the
     LayerNorm weight / bias gradients ([NH * F] fp32) and, when dOut (the gradient of the wo

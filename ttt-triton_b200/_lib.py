@@ -58,6 +58,7 @@ _SIGNATURES = {
         _I,
     ),
     "ttt_device_status": ([_P], _I),
+    "ttt_test_hold_first_stage": ([_I, ctypes.c_ulonglong], _I),
     "ttt_memo_mix_scratch_bytes": ([_I] * 5, _Z),
     "ttt_memo_mix_fwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P, _P, _Z, _P], _I),
     "ttt_memo_mix_bwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P] * 4 + [_P, _Z, _I, _P], _I),
@@ -94,8 +95,9 @@ def exported_symbols():
     return list(_SIGNATURES)
 
 
-# Kernels one successful call enqueues (1 unless listed); ttt_device_status launches none.
-_KERNELS_PER_CALL = {"ttt_memo_mix_fwd": 2, "ttt_memo_mix_bwd": 3, "ttt_device_status": 0}
+# Kernels one successful call enqueues (1 unless listed); the status calls launch none.
+_KERNELS_PER_CALL = {"ttt_memo_mix_fwd": 2, "ttt_memo_mix_bwd": 3, "ttt_device_status": 0,
+                     "ttt_test_hold_first_stage": 0}
 _launches = 0
 
 
@@ -117,6 +119,11 @@ def device_status():
     v = ctypes.c_uint(0)
     check(lib.ttt_device_status(ctypes.byref(v)), "ttt_device_status")
     return v.value
+
+
+def hold_first_stage(enable, wait_limit_ns=0):
+    """Test switch of the bounded waits (ttt_test_hold_first_stage in include/ttt_b200.h)."""
+    check(lib.ttt_test_hold_first_stage(int(bool(enable)), int(wait_limit_ns)), "ttt_test_hold_first_stage")
 
 
 def dtype_code(t):

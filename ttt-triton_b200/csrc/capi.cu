@@ -1,5 +1,6 @@
 // ABI-wide entry points: version, the per-thread last-error message and the device error
 // word; host helpers shared by the kernels' entry points (TMA tensor maps).
+#include <atomic>
 #include <mutex>
 
 #include "capi_common.cuh"
@@ -83,7 +84,22 @@ int make_tile_map(CUtensorMap* map, const void* base, int dtype_code, unsigned l
   return make_map_2d(map, base, dtype_code, 64, rows, 128, 64, box_rows, true, who);
 }
 
+static std::atomic<int> g_test_hold{0};
+static std::atomic<unsigned long long> g_test_wait_ns{kWaitLimitNs};
+
+bool test_hold_first_stage() { return g_test_hold.load(std::memory_order_relaxed) != 0; }
+unsigned long long test_wait_limit_ns() { return g_test_wait_ns.load(std::memory_order_relaxed); }
+
 }  // namespace ttt
+
+extern "C" int ttt_test_hold_first_stage(int enable, unsigned long long wait_limit_ns) {
+  TTT_REQUIRE(wait_limit_ns <= ttt::kWaitLimitNs, TTT_ERR_SHAPE,
+              "ttt_test_hold_first_stage: wait limit %llu ns is above the library's %llu ns", wait_limit_ns,
+              ttt::kWaitLimitNs);
+  ttt::g_test_wait_ns.store(wait_limit_ns ? wait_limit_ns : ttt::kWaitLimitNs);
+  ttt::g_test_hold.store(enable ? 1 : 0);
+  return ttt::ok();
+}
 
 // Reads and clears the device error word of the current device (synchronises with it).
 extern "C" int ttt_device_status(unsigned int* status) {

@@ -89,6 +89,8 @@ struct MlpFwdParams {
   float* Z1b_out;
   float* Z2b_out;
   unsigned int* err;  // device error word (set by the entry point for kernels with bounded waits)
+  unsigned long long wait_ns;  // limit of each bounded wait (tensor-core path)
+  int hold_stage0;             // wait-expiry test: the first stage's copies are never issued
 };
 
 struct MlpBwdParams {

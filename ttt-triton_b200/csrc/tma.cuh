@@ -66,13 +66,14 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Wait for phase `parity` of the mbarrier, at most kWaitLimitNs. On timeout ORs
-// kDevErrTmaTimeout into *err (when given) and returns false.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned int* err) {
+// Wait for phase `parity` of the mbarrier, at most limit_ns (kWaitLimitNs by default). On
+// timeout ORs kDevErrTmaTimeout into *err (when given) and returns false.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned int* err,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   while (!mbar_test(bar, parity)) {
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       if (err) atomicOr(err, kDevErrTmaTimeout);
       return false;
     }
@@ -96,5 +97,10 @@ int make_map_2d(CUtensorMap* map, const void* base, int dtype_code, unsigned lon
 
 // Device address of the library's device error word on the current device.
 int device_error_word(unsigned int** out, const char* who);
+
+// Wait-expiry test switch (ttt_test_hold_first_stage): whether the tensor-core MLP forward
+// holds back its first stage's copies, and the wait limit its launches use (ns).
+bool test_hold_first_stage();
+unsigned long long test_wait_limit_ns();
 
 }  // namespace ttt

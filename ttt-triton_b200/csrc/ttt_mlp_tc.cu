@@ -136,7 +136,9 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
   int last_issued = -1;  // (copy thread) last mini-batch whose stage copies were issued
   if (tid == kCopyThread)
     for (int i = 0; i < NSTAGE - 1 && i < p.NC; ++i) {
-      issue_stage(smem_u32(smem + i * STAGE), smem_u32(&full_bar[i]), p, &tm_q, &tm_k, &tm_v, s, i);
+      // (wait-expiry test) stage 0 never issued: nothing is in flight for its barrier
+      if (!(p.hold_stage0 && i == 0))
+        issue_stage(smem_u32(smem + i * STAGE), smem_u32(&full_bar[i]), p, &tm_q, &tm_k, &tm_v, s, i);
       last_issued = i;
     }
   const uint32_t tS1 = tmem_lane_addr(tmem_base_sh, warp, 128 * (warp >> 2));
@@ -164,7 +166,7 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
     // The copy thread waits for stage n; the CTA barrier then publishes it to every warp and
     // tells the copy thread that mini-batch n-1 is done, so its stage may be refilled.
     if (tid == kCopyThread && !abort_sh &&
-        !mbar_wait(smem_u32(&full_bar[n % NSTAGE]), (uint32_t)((n / NSTAGE) & 1), p.err))
+        !mbar_wait(smem_u32(&full_bar[n % NSTAGE]), (uint32_t)((n / NSTAGE) & 1), p.err, p.wait_ns))
       abort_sh = 1;  // results of this stream are void; the error word reports it
     __syncthreads();
     {
@@ -545,7 +547,8 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
   // (bounded) before the CTA's shared memory goes away
   if (tid == kCopyThread && abort_sh)
     for (int m = last_issued - NSTAGE + 1; m <= last_issued; ++m)
-      if (m >= 0) mbar_wait(smem_u32(&full_bar[m % NSTAGE]), (uint32_t)((m / NSTAGE) & 1), nullptr);
+      if (m >= 0 && !(p.hold_stage0 && m == 0))  // full 2 s limit: these copies were issued
+        mbar_wait(smem_u32(&full_bar[m % NSTAGE]), (uint32_t)((m / NSTAGE) & 1), nullptr);
   const float* b2_fin = b2s + (p.NC & 1) * F;
   for (int i = tid; i < FFW; i += NTHREADS) p.b1_last[s * FFW + i] = b1s[i];
   for (int i = tid; i < F; i += NTHREADS) p.b2_last[s * F + i] = b2_fin[i];
@@ -587,6 +590,8 @@ int mlp_fwd_fast(const MlpFwdParams& p, cudaStream_t stream) {
   MlpFwdParams q = p;
   rc = device_error_word(&q.err, "ttt_mlp_fwd");
   if (rc) return rc;
+  q.wait_ns = test_wait_limit_ns();
+  q.hold_stage0 = test_hold_first_stage() ? 1 : 0;
   if (p.FF == 256)
     return dt == DT_BF16 ? launch_fwd<__nv_bfloat16, 8>(q, tq, tk, tv, stream)
                          : launch_fwd<__half, 8>(q, tq, tk, tv, stream);
