@@ -85,6 +85,39 @@ def gelu_tanh(x):
     return Fn.gelu(x, approximate="tanh")
 
 
+class _Round(torch.autograd.Function):
+    """Rounds a tensor to a 16-bit type in the forward and the gradient reaching it to the
+    same type in the backward, keeping the working dtype (float64 in the tests)."""
+
+    @staticmethod
+    def forward(ctx, x, dt):
+        ctx.dt = dt
+        return x.to(dt).to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        return g.to(ctx.dt).to(g.dtype), None
+
+
+def rounding(dt):
+    """The tensor-boundary rounding of a 16-bit activation path: a function that rounds a
+    tensor (and, under autograd, its gradient) to dt; the identity for dt None or float32.
+
+    Passed as `rnd` to the layer and forecaster restatements below, it reproduces the
+    precision a 16-bit implementation of them has at the boundaries where it stores 16-bit
+    tensors (projection outputs, the prologue's XQ/XK/XV/XU/eta, the scan and mixing
+    outputs, the post_norm rows, the wo output; the gradients of each), with exact
+    arithmetic in between. The reference's own 16-bit training (autocast, main.py:87)
+    rounds at the same kind of boundaries."""
+    if dt is None or dt == torch.float32:
+        return lambda x: x
+    return lambda x: _Round.apply(x, dt)
+
+
+def _ident(x):
+    return x
+
+
 # --------------------------------------------------------------------------- one step
 def linear_step(W, b, ln_w, ln_b, XQ, XK, XV, eta):
     """One mini-batch of TTT-Linear in dual form (ops/ttt_linear.py:8-54).
@@ -261,7 +294,7 @@ def memo_mix(XQW, XQ, XK, XU, W1_memo, b1_memo, W2_memo, b2_memo, ln_w, ln_b, me
 
 
 def process_input(hidden, wq, bq, wk, bk, wv, bv, wu, bu, lr_w, lr_b, ln_w, ln_b, freqs_cos, freqs_sin,
-                  mini_batch_size, base_lr):
+                  mini_batch_size, base_lr, rnd=_ident):
     """The TTT layer's input prologue (ttt_layer.py:261-330 with no text prefix, no multi-scene
     interleave, no tensor parallelism): projections (:141-148), L2 normalisation of XQ, XK, XU
     (:276-278), rotary embedding of XQ, XK and XU (:284-295, utils.py:97-123), the LayerNorm
@@ -271,7 +304,8 @@ def process_input(hidden, wq, bq, wk, bk, wv, bv, wu, bu, lr_w, lr_b, ln_w, ln_b
 
     hidden [B, L, W]; w* [W, W], b* [W] (nn.Linear); lr_w [NH, 1, W], lr_b [NH, 1];
     ln_w, ln_b [NH, F]; freqs_cos / freqs_sin [L, F/2] (the real and imaginary parts of the
-    layer's freqs_cis rows 0..L-1). Returns XQ, XK, XV, XU, eta.
+    layer's freqs_cis rows 0..L-1). Returns XQ, XK, XV, XU, eta. `rnd` (see rounding())
+    rounds the projection weights and outputs and the five results.
     """
     B, L, W = hidden.shape
     NH = ln_w.shape[0]
@@ -288,10 +322,12 @@ def process_input(hidden, wq, bq, wk, bk, wv, bv, wu, bu, lr_w, lr_b, ln_w, ln_b
         sn = freqs_sin[:L].reshape(1, L, 1, F // 2)
         return torch.stack((a * c - b * sn, a * sn + b * c), dim=-1).flatten(-2)
 
-    XQ = heads(hidden @ wq.T + bq)
-    XK = heads(hidden @ wk.T + bk)
-    XV = heads(hidden @ wv.T + bv)
-    XU = heads(hidden @ wu.T + bu)
+    hidden = rnd(hidden)
+
+    def proj(w, b):
+        return heads(rnd(hidden @ rnd(w).T + rnd(b)))
+
+    XQ, XK, XV, XU = proj(wq, bq), proj(wk, bk), proj(wv, bv), proj(wu, bu)
     XQ = rope(Fn.normalize(XQ, p=2, dim=-1))
     XK = rope(Fn.normalize(XK, p=2, dim=-1))
     XU = rope(Fn.normalize(XU, p=2, dim=-1))
@@ -303,10 +339,11 @@ def process_input(hidden, wq, bq, wk, bk, wv, bv, wu, bu, lr_w, lr_b, ln_w, ln_b
         return x.transpose(1, 2).reshape(B, NH, NC, CS, F)
 
     Xmb = hidden.reshape(B, NC, CS, W)
-    lr = torch.einsum("bnkc,hdc->bhnkd", Xmb, lr_w) + lr_b.reshape(1, -1, 1, 1, 1)
+    lr = rnd(torch.einsum("bnkc,hdc->bhnkd", Xmb, rnd(lr_w)) + rnd(lr_b).reshape(1, -1, 1, 1, 1))
     lr = torch.sigmoid(lr).permute(0, 1, 2, 4, 3)  # [B, NH, NC, 1, CS]
     eta = (1.0 / CS) * (base_lr * lr / F).repeat(1, 1, 1, CS, 1)
-    return {"XQ": layout(XQ), "XK": layout(XK), "XV": layout(XV), "XU": layout(XU), "eta": eta}
+    return {"XQ": rnd(layout(XQ)), "XK": rnd(layout(XK)), "XV": rnd(layout(XV)), "XU": rnd(layout(XU)),
+            "eta": rnd(eta)}
 
 
 PROLOGUE_PARAM_NAMES = ("hidden", "wq", "bq", "wk", "bk", "wv", "bv", "wu", "bu", "lr_w", "lr_b", "ln_w", "ln_b")
@@ -322,14 +359,14 @@ def process_input_grads(inp, douts, mini_batch_size, base_lr):
     return {k: leaves[k].grad for k in PROLOGUE_PARAM_NAMES}, {k: v.detach() for k, v in out.items()}
 
 
-def post_norm_wo(XQW, pn_w, pn_b, wo_w, wo_b, eps=1e-6):
+def post_norm_wo(XQW, pn_w, pn_b, wo_w, wo_b, eps=1e-6, rnd=_ident):
     """The layer's output epilogue: the scan output [B, NH, NC, CS, F] permuted to token order
     [B, L, NH * F] (ttt_layer.py:563-564), post_norm = LayerNorm over the width with eps 1e-6
     (:77, :349) and the wo projection (:350)."""
     B, NH, NC, CS, F = XQW.shape
     h = XQW.permute(0, 2, 3, 1, 4).reshape(B, NC * CS, NH * F)
-    h = Fn.layer_norm(h, (NH * F,), pn_w, pn_b, eps)
-    return h @ wo_w.T + wo_b
+    h = rnd(Fn.layer_norm(h, (NH * F,), pn_w, pn_b, eps))
+    return rnd(h @ rnd(wo_w).T + rnd(wo_b))
 
 
 EPILOGUE_PARAM_NAMES = ("XQW", "pn_w", "pn_b", "wo_w", "wo_b")
@@ -344,17 +381,18 @@ def post_norm_wo_grads(inp, dout, eps=1e-6):
 
 
 def ttt_mlp_layer(P, pre, h, rope_cos, rope_sin, mini_batch_size, base_lr, checkpoint_group_size,
-                  memo_segment_size):
+                  memo_segment_size, rnd=_ident):
     """One TTT-MLP layer's forward (TTTBase.forward, ttt_layer.py:337-357, with TTTMLP.ttt's
     kernel branch, :453-565): process_input, the scan, memo mixing and post_norm + wo.
-    P holds the layer's parameters under the prefix `pre` (reference module names)."""
+    P holds the layer's parameters under the prefix `pre` (reference module names); `rnd`
+    rounds the stage boundaries (rounding())."""
     def q(n):
         return P[pre + n]
 
     inp = process_input(h, q("wq.weight"), q("wq.bias"), q("wk.weight"), q("wk.bias"), q("wv.weight"),
                         q("wv.bias"), q("wu.weight"), q("wu.bias"), q("learnable_ttt_lr_weight"),
                         q("learnable_ttt_lr_bias"), q("ttt_norm_weight"), q("ttt_norm_bias"), rope_cos, rope_sin,
-                        mini_batch_size, base_lr)
+                        mini_batch_size, base_lr, rnd)
     B = h.shape[0]
     NC = inp["XV"].shape[2]
     ckpt = min(max(int(checkpoint_group_size), 1), NC)
@@ -364,30 +402,31 @@ def ttt_mlp_layer(P, pre, h, rope_cos, rope_sin, mini_batch_size, base_lr, check
 
     r = mlp_scan(q("ttt_norm_weight"), q("ttt_norm_bias"), tile(q("W1")), tile(q("b1")), tile(q("W2")), tile(q("b2")),
                  inp["XQ"], inp["XV"], inp["XK"], inp["eta"], ckpt, memo_segment_size)
-    XQW = memo_mix(r["XQW"], inp["XQ"], inp["XK"], inp["XU"], r["W1_memo"].detach(), r["b1_memo"].detach(),
-                   r["W2_memo"].detach(), r["b2_memo"].detach(), q("ttt_norm_weight"), q("ttt_norm_bias"),
-                   memo_segment_size)
-    return post_norm_wo(XQW, q("post_norm.weight"), q("post_norm.bias"), q("wo.weight"), q("wo.bias"))
+    XQW = rnd(memo_mix(rnd(r["XQW"]), inp["XQ"], inp["XK"], inp["XU"], r["W1_memo"].detach(), r["b1_memo"].detach(),
+                       r["W2_memo"].detach(), r["b2_memo"].detach(), q("ttt_norm_weight"), q("ttt_norm_bias"),
+                       memo_segment_size))
+    return post_norm_wo(XQW, q("post_norm.weight"), q("post_norm.bias"), q("wo.weight"), q("wo.bias"), rnd=rnd)
 
 
 def forecaster(P, x, layer_prefixes, rope_cos, rope_sin, pred_len, mini_batch_size, base_lr, checkpoint_group_size,
-               memo_segment_size):
+               memo_segment_size, rnd=_ident):
     """TTTForecaster.forward (forecast.py:94-99) with the TTT layers stacked: in_proj, each
-    layer of `layer_prefixes` in turn, head on the last position."""
-    h = x @ P["in_proj.weight"].T + P["in_proj.bias"]
+    layer of `layer_prefixes` in turn, head on the last position. `rnd` rounds the input
+    projection and every layer's stage boundaries (rounding()); the head runs unrounded."""
+    h = rnd(rnd(x) @ rnd(P["in_proj.weight"]).T + rnd(P["in_proj.bias"]))
     for pre in layer_prefixes:
         h = ttt_mlp_layer(P, pre, h, rope_cos, rope_sin, mini_batch_size, base_lr, checkpoint_group_size,
-                          memo_segment_size)
+                          memo_segment_size, rnd)
     out = h[:, -1] @ P["head.weight"].T + P["head.bias"]
     return out.view(x.shape[0], pred_len, -1)
 
 
 def forecaster_grads(P, x, y, layer_prefixes, rope_cos, rope_sin, pred_len, mini_batch_size, base_lr,
-                     checkpoint_group_size, memo_segment_size):
+                     checkpoint_group_size, memo_segment_size, rnd=_ident):
     """MSE loss (main.py:89) of the forecaster and its gradients w.r.t. every parameter."""
     leaves = {k: v.detach().clone().requires_grad_(True) for k, v in P.items()}
     out = forecaster(leaves, x, layer_prefixes, rope_cos, rope_sin, pred_len, mini_batch_size, base_lr,
-                     checkpoint_group_size, memo_segment_size)
+                     checkpoint_group_size, memo_segment_size, rnd)
     loss = Fn.mse_loss(out, y)
     loss.backward()
     grads = {k: (v.grad if v.grad is not None else torch.zeros_like(v)) for k, v in leaves.items()}

@@ -123,3 +123,25 @@ def test_training_steps_of_the_main_py_model():
     losses = [float(train_step(model, opt, x.to(DEV), y.to(DEV))) for _ in range(6)]
     assert all(math.isfinite(v) for v in losses)
     assert losses[-1] < losses[0]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_triton_linear_at_main_config(dtype):
+    """TritonLinear.apply (the ModelConfig default ssm_layer, ttt_linear) at main.py's shape:
+    XQW and all ten gradients against the oracle."""
+    from linear_triton import TritonLinear
+
+    names = ("ln_w", "ln_b", "W1", "b1", "XQ", "XV", "XK", "eta")
+    d = S.perturb_params(S.make_linear_inputs(B, NH, NC, CS, F, seed=97, eta_mode="equal"), seed=98)
+    d = to_dev(d, DEV, dtype)
+    # upstream gradient at the scale of a training loss: N(0, 1) per element with CS = 64 drives
+    # d_eta past the fp16 range (65504) in fp64 too
+    dO = (S.make_upstream((B, NH, NC, CS, F), seed=99) * 0.01).to(DEV, dtype)
+    leaves = {k: d[k].detach().clone().requires_grad_(True) for k in names}
+    out = TritonLinear.apply(*(leaves[k] for k in names), min(CKPT, NC))
+    out.backward(dO)
+    ref_grads, ref = O.linear_grads(oracle_inputs(d), dO.double().cpu())
+    tol = TOL[dtype]
+    assert_close("XQW", out, ref["XQW"], tol)
+    for k in names:
+        assert_close("d" + k, leaves[k].grad, ref_grads[k], tol)

@@ -202,3 +202,18 @@ def test_equal_eta_dual_equals_primal():
         b = b - (e * G).sum(-2, keepdim=True)
         outs.append(XQ + O.ln_fwd(XQ @ W + b, lw, lb))
     assert O.rel_l2(res["XQW"], torch.stack(outs, 2)) < 1e-12
+
+
+def test_precision_matched_rounding_rounds_values_and_gradients():
+    """ttt_oracle.rounding: the identity for None / float32; for bf16 it rounds the value in
+    the forward and the gradient reaching it in the backward, in the working dtype."""
+    import ttt_oracle as Or
+
+    x = torch.tensor([1.0 + 2.0 ** -10, -3.0 + 2.0 ** -12], dtype=torch.float64, requires_grad=True)
+    assert Or.rounding(None)(x) is x and Or.rounding(torch.float32)(x) is x
+    r = Or.rounding(torch.bfloat16)
+    y = r(x)
+    assert y.dtype == torch.float64 and torch.equal(y.detach(), x.detach().to(torch.bfloat16).double())
+    g = torch.tensor([1.0 + 2.0 ** -11, 0.5], dtype=torch.float64)
+    y.backward(g)
+    assert torch.equal(x.grad, g.to(torch.bfloat16).double())

@@ -13,7 +13,9 @@ import os
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libttt_b200.so")
+# TTT_B200_LIB names another build of the same ABI in this directory (the timeline build,
+# libttt_b200_stamps.so, of build.py --phase-stamps)
+LIB_PATH = os.path.join(_HERE, os.environ.get("TTT_B200_LIB", "libttt_b200.so"))
 
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 

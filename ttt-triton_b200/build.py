@@ -1,9 +1,11 @@
 """Build libttt_b200.so in-tree with nvcc for sm_100a.
 
-    python ttt-triton_b200/build.py [--force]
+    python ttt-triton_b200/build.py [--force] [--phase-stamps]
 
 The library is a plain C-ABI shared object (include/ttt_b200.h); nothing here links
-against torch. The build is incremental on source modification times.
+against torch. The build is incremental on source modification times. ``--phase-stamps``
+builds a second library, libttt_b200_stamps.so, whose TTT-MLP tensor-core forward records a
+per-phase %globaltimer timeline (phase_timeline.py reads it); the product library has none.
 """
 
 from __future__ import annotations
@@ -37,28 +39,34 @@ def sources():
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
 
 
-def _stale():
-    if not os.path.exists(LIB):
+STAMPS_LIB = os.path.join(HERE, "libttt_b200_stamps.so")
+
+
+def _stale(lib=LIB):
+    if not os.path.exists(lib):
         return True
-    t = os.path.getmtime(LIB)
+    t = os.path.getmtime(lib)
     deps = sources() + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(REPO, "include", "*.h"))
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force=False, verbose=False):
-    """Compile every .cu under csrc/ into libttt_b200.so (sm_100a). Returns the path."""
-    if not force and not _stale():
-        return LIB
-    tmp = LIB + ".tmp"
-    cmd = [_nvcc(), *NVCC_FLAGS, "-I", os.path.join(REPO, "include"), "-o", tmp, *sources()]
+def build(force=False, verbose=False, phase_stamps=False):
+    """Compile every .cu under csrc/ into libttt_b200.so (sm_100a), or with phase_stamps into
+    libttt_b200_stamps.so with the forward's timeline stamps compiled in. Returns the path."""
+    lib = STAMPS_LIB if phase_stamps else LIB
+    if not force and not _stale(lib):
+        return lib
+    tmp = lib + ".tmp"
+    extra = ["-DTTT_PHASE_STAMPS"] if phase_stamps else []
+    cmd = [_nvcc(), *NVCC_FLAGS, *extra, "-I", os.path.join(REPO, "include"), "-o", tmp, *sources()]
     if verbose:
         print(" ".join(cmd))
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True))
+    print(build(force="--force" in sys.argv, verbose=True, phase_stamps="--phase-stamps" in sys.argv))

@@ -129,6 +129,7 @@ struct MlpBwdParams {
   const float* Z2b_saved;
   const float* W1_last;
   const float* W2_last;
+  long long spill;  // general kernel: floats per stream of tiles placed in global scratch
 };
 
 // Memo-state mixing (ttt_layer.py:503-559); activations [B,NH,NC,16,64] in one 16-bit type.

@@ -144,6 +144,59 @@ __global__ void __launch_bounds__(256) mlp_fwd_kernel(MlpFwdParams p) {
   copy_f32(p.b2_last + s * F, b2, F);
 }
 
+// Shared-memory budget of the general backward's fp32 tiles (the opt-in maximum per CTA).
+constexpr long long kMlpBwdSmemFloats = 232448 / 4;
+
+// The general backward's fp32 tiles, carved in a fixed order: into shared memory while they
+// fit in `cap` floats, then (from the first that does not, all the rest) into the stream's
+// spill region of the global scratch, which stays L2-resident. Every shape then runs; the
+// mini-batch-16 shapes keep every tile on chip. With null bases this only counts: returns
+// the shared-memory floats used and stores the spill floats.
+struct BwdTiles {
+  float *b1, *db1, *tmp1, *b2, *db2, *tmp2, *gam, *bet, *dgam, *dbet;
+  float *XQ, *XK, *XV, *dO, *Z2, *G2, *Z2b, *dZ2b, *dG2, *dXQ, *dXK, *XdW2, *dZ2, *dT, *T1, *T2;
+  float *Z1, *X2, *H, *G1, *Z1b, *X2b, *DX2B, *DX2, *DG1;
+  float *E, *A1, *P1, *A2, *P2, *dP, *dEta, *dA, *mu2, *sd2, *de;
+};
+
+struct Carver {
+  float* sm;
+  float* gl;
+  long long cap, off = 0, goff = 0;
+  bool out = false;
+  __host__ __device__ float* take(long long n) {
+    if (!out && off + n <= cap) {
+      float* r = sm ? sm + off : nullptr;
+      off += n;
+      return r;
+    }
+    out = true;
+    float* r = gl ? gl + goff : nullptr;
+    goff += n;
+    return r;
+  }
+};
+
+__host__ __device__ inline long long carve_bwd(BwdTiles& t, int C, int F, int FF, long long cap, float* sm,
+                                               float* gl, long long* spill) {
+  const long long CF = (long long)C * F, CFF = (long long)C * FF, CC = (long long)C * C;
+  Carver c{sm, gl, cap};
+  t.b1 = c.take(FF); t.db1 = c.take(FF); t.tmp1 = c.take(FF);
+  t.b2 = c.take(F); t.db2 = c.take(F); t.tmp2 = c.take(F);
+  t.gam = c.take(F); t.bet = c.take(F); t.dgam = c.take(F); t.dbet = c.take(F);
+  t.XQ = c.take(CF); t.XK = c.take(CF); t.XV = c.take(CF); t.dO = c.take(CF);
+  t.Z2 = c.take(CF); t.G2 = c.take(CF); t.Z2b = c.take(CF); t.dZ2b = c.take(CF);
+  t.dG2 = c.take(CF); t.dXQ = c.take(CF); t.dXK = c.take(CF); t.XdW2 = c.take(CF);
+  t.dZ2 = c.take(CF); t.dT = c.take(CF); t.T1 = c.take(CF); t.T2 = c.take(CF);
+  t.Z1 = c.take(CFF); t.X2 = c.take(CFF); t.H = c.take(CFF); t.G1 = c.take(CFF); t.Z1b = c.take(CFF);
+  t.X2b = c.take(CFF); t.DX2B = c.take(CFF); t.DX2 = c.take(CFF); t.DG1 = c.take(CFF);
+  t.E = c.take(CC); t.A1 = c.take(CC); t.P1 = c.take(CC); t.A2 = c.take(CC);
+  t.P2 = c.take(CC); t.dP = c.take(CC); t.dEta = c.take(CC); t.dA = c.take(CC);
+  t.mu2 = c.take(C); t.sd2 = c.take(C); t.de = c.take(C);
+  *spill = c.goff;
+  return c.off;
+}
+
 __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
   extern __shared__ float sm[];
   const int C = p.CS, F = p.F, FF = p.FF;
@@ -152,54 +205,26 @@ __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
   const int h = (int)(s % p.NH);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
 
-  float* b1 = sm;
-  float* db1 = b1 + FF;
-  float* tmp1 = db1 + FF;
-  float* b2 = tmp1 + FF;
-  float* db2 = b2 + F;
-  float* tmp2 = db2 + F;
-  float* gam = tmp2 + F;
-  float* bet = gam + F;
-  float* dgam = bet + F;
-  float* dbet = dgam + F;
-  float* XQ = dbet + F;
-  float* XK = XQ + CF;
-  float* XV = XK + CF;
-  float* dO = XV + CF;
-  float* Z2 = dO + CF;
-  float* G2 = Z2 + CF;
-  float* Z2b = G2 + CF;
-  float* dZ2b = Z2b + CF;
-  float* dG2 = dZ2b + CF;
-  float* dXQ = dG2 + CF;
-  float* dXK = dXQ + CF;
-  float* XdW2 = dXK + CF;
-  float* dZ2 = XdW2 + CF;
-  float* dT = dZ2 + CF;
-  float* T1 = dT + CF;  // e*XK, then d x_hat
-  float* T2 = T1 + CF;  // d g_hat
-  float* Z1 = T2 + CF;
-  float* X2 = Z1 + CFF;
-  float* H = X2 + CFF;    // G2 W2^T, later dZ1
-  float* G1 = H + CFF;
-  float* Z1b = G1 + CFF;  // Z1_bar, later XK dW1_next
-  float* X2b = Z1b + CFF;
-  float* DX2B = X2b + CFF;  // dX2_bar, then dZ1_bar
-  float* DX2 = DX2B + CFF;  // e*X2, then dX2
-  float* DG1 = DX2 + CFF;   // dG1, then dH
-  float* E = DG1 + CFF;
-  float* A1 = E + CC;
-  float* P1 = A1 + CC;
-  float* A2 = P1 + CC;
-  float* P2 = A2 + CC;
-  float* dP = P2 + CC;
-  float* dEta = dP + CC;
-  float* dA = dEta + CC;
-  float* mu2 = dA + CC;
-  float* sd2 = mu2 + C;
-  float* de = sd2 + C;
+  const long long per_stream = (long long)F * FF * 2 + (long long)p.ckpt * (CFF + CF) + p.spill;
+  BwdTiles tl;
+  long long spill = 0;
+  carve_bwd(tl, C, F, FF, kMlpBwdSmemFloats, sm, p.scratch + s * per_stream + (per_stream - p.spill), &spill);
+  float *b1 = tl.b1, *db1 = tl.db1, *tmp1 = tl.tmp1, *b2 = tl.b2, *db2 = tl.db2, *tmp2 = tl.tmp2;
+  float *gam = tl.gam, *bet = tl.bet, *dgam = tl.dgam, *dbet = tl.dbet;
+  float *XQ = tl.XQ, *XK = tl.XK, *XV = tl.XV, *dO = tl.dO, *Z2 = tl.Z2, *G2 = tl.G2, *Z2b = tl.Z2b;
+  float *dZ2b = tl.dZ2b, *dG2 = tl.dG2, *dXQ = tl.dXQ, *dXK = tl.dXK, *XdW2 = tl.XdW2, *dZ2 = tl.dZ2;
+  float *dT = tl.dT, *T1 = tl.T1, *T2 = tl.T2;  // T1: e*XK, then d x_hat; T2: d g_hat
+  float *Z1 = tl.Z1, *X2 = tl.X2;
+  float* H = tl.H;      // G2 W2^T, later dZ1
+  float* G1 = tl.G1;
+  float* Z1b = tl.Z1b;  // Z1_bar, later XK dW1_next
+  float* X2b = tl.X2b;
+  float* DX2B = tl.DX2B;  // dX2_bar, then dZ1_bar
+  float* DX2 = tl.DX2;    // e*X2, then dX2
+  float* DG1 = tl.DG1;    // dG1, then dH
+  float *E = tl.E, *A1 = tl.A1, *P1 = tl.P1, *A2 = tl.A2, *P2 = tl.P2, *dP = tl.dP, *dEta = tl.dEta, *dA = tl.dA;
+  float *mu2 = tl.mu2, *sd2 = tl.sd2, *de = tl.de;
 
-  const long long per_stream = (long long)F * FF * 2 + (long long)p.ckpt * (CFF + CF);
   float* W1 = p.scratch + s * per_stream;
   float* W2 = W1 + (long long)F * FF;
   float* zs = W2 + (long long)FF * F;
@@ -475,9 +500,11 @@ static size_t mlp_fwd_smem(int C, int F, int FF) {
   return sizeof(float) * (2 * (size_t)FF + 4 * (size_t)F + 7 * (size_t)C * F + 5 * (size_t)C * FF + 3 * (size_t)C * C);
 }
 
-static size_t mlp_bwd_smem(int C, int F, int FF) {
-  return sizeof(float) * (3 * (size_t)FF + 7 * (size_t)F + 16 * (size_t)C * F + 9 * (size_t)C * FF +
-                          8 * (size_t)C * C + 3 * (size_t)C);
+// Shared memory of the general backward and the floats per stream of its tiles that go to
+// the global scratch instead (carve_bwd).
+static size_t mlp_bwd_smem(int C, int F, int FF, long long* spill) {
+  BwdTiles t;
+  return sizeof(float) * (size_t)carve_bwd(t, C, F, FF, kMlpBwdSmemFloats, nullptr, nullptr, spill);
 }
 
 static int check_mlp(int B, int NH, int NC, int CS, int F, int FF, int ckpt) {
@@ -544,7 +571,9 @@ extern "C" int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int che
 extern "C" size_t ttt_mlp_bwd_scratch_bytes(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_group_size) {
   if (B <= 0 || NH <= 0 || NC <= 0 || CS <= 0 || F <= 0 || FF <= 0 || checkpoint_group_size <= 0) return 0;
   const size_t g = (size_t)(checkpoint_group_size < NC ? checkpoint_group_size : NC);
-  const size_t per_stream = 2 * (size_t)F * FF + g * (size_t)CS * (FF + F);
+  long long spill = 0;
+  mlp_bwd_smem(CS, F, FF, &spill);
+  const size_t per_stream = 2 * (size_t)F * FF + g * (size_t)CS * (FF + F) + (size_t)spill;
   return sizeof(float) * (size_t)B * NH * per_stream;
 }
 
@@ -582,12 +611,13 @@ extern "C" int ttt_mlp_bwd(int B, int NH, int NC, int CS, int F, int FF, int che
   p.scratch = (float*)scratch;
   p.Z1_saved = Z1_saved; p.Z2_saved = Z2_saved; p.Z1b_saved = Z1b_saved; p.Z2b_saved = Z2b_saved;
   p.W1_last = W1_last; p.W2_last = W2_last;
+  p.spill = 0;
   rc = mlp_bwd_fast(p, (cudaStream_t)stream);
   if (rc != TTT_NOT_APPLICABLE) return rc;
   const size_t need = ttt_mlp_bwd_scratch_bytes(B, NH, NC, CS, F, FF, checkpoint_group_size);
   TTT_REQUIRE(scratch && scratch_bytes >= need, TTT_ERR_SCRATCH, "ttt_mlp_bwd: scratch has %zu bytes, needs %zu",
               scratch ? scratch_bytes : (size_t)0, need);
-  const size_t smem = mlp_bwd_smem(CS, F, FF);
+  const size_t smem = mlp_bwd_smem(CS, F, FF, &p.spill);
   rc = prepare_smem(mlp_bwd_kernel, smem, "ttt_mlp_bwd");
   if (rc) return rc;
   mlp_bwd_kernel<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);

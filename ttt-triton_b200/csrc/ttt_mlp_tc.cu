@@ -33,6 +33,31 @@
 namespace ttt {
 namespace mlp_tc {
 
+// Per-phase timeline (built only with -DTTT_PHASE_STAMPS, see build.py --phase-stamps): for
+// mini-batch kStampN, thread 0 of each CTA records %globaltimer at the phase boundaries
+// (before / after each CTA barrier) and its SM id; ttt_phase_stamps_read copies them out.
+#ifdef TTT_PHASE_STAMPS
+constexpr int kStampN = 64, kStampCTAs = 4096, kStamps = 10;
+__device__ unsigned long long g_phase_stamps[kStampCTAs][kStamps];
+#define TTT_STAMP(k)                                                                                  \
+  do {                                                                                                \
+    if (tid == 0 && n == kStampN && blockIdx.x < kStampCTAs) g_phase_stamps[blockIdx.x][k] = global_ns(); \
+  } while (0)
+#define TTT_STAMP_SM()                                                                                \
+  do {                                                                                                \
+    unsigned sm_;                                                                                     \
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm_));                                                \
+    if (tid == 0 && n == kStampN && blockIdx.x < kStampCTAs) g_phase_stamps[blockIdx.x][9] = sm_;      \
+  } while (0)
+#else
+#define TTT_STAMP(k) \
+  do {               \
+  } while (0)
+#define TTT_STAMP_SM() \
+  do {                 \
+  } while (0)
+#endif
+
 constexpr int NSTAGE = 3;
 constexpr int TILE = C * F * 2;
 constexpr int ETA = C * C * 2;
@@ -168,7 +193,9 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
     if (tid == kCopyThread && !abort_sh &&
         !mbar_wait(smem_u32(&full_bar[n % NSTAGE]), (uint32_t)((n / NSTAGE) & 1), p.err, p.wait_ns))
       abort_sh = 1;  // results of this stream are void; the error word reports it
+    TTT_STAMP(0);
     __syncthreads();
+    TTT_STAMP(1);
     {
       const int nn = n + NSTAGE - 1;
       if (tid == kCopyThread && nn < p.NC && !abort_sh) {
@@ -279,7 +306,9 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
         *reinterpret_cast<float2*>(pw + (g + 8) * PLD + 8 * nf + 2 * t) = make_float2(acc[2], acc[3]);
       }
     }
+    TTT_STAMP(2);
     __syncthreads();
+    TTT_STAMP(3);
 
     // ---------------- C: Z2 = sum + b2, G2 = ln_fused_l2_bwd(Z2, XV - XK)
 #pragma unroll
@@ -324,7 +353,9 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
       *reinterpret_cast<uint2*>(smem + OFF_EG + xo) =
           make_uint2(H::pack(-e * G[0], -e * G[1]), H::pack(-e * G[2], -e * G[3]));
     }
+    TTT_STAMP(4);
     __syncthreads();
+    TTT_STAMP(5);
 
     // ---------------- D
     const uint32_t gb = smem_u32(smem + OFF_G), egb = smem_u32(smem + OFF_EG);
@@ -491,7 +522,9 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
         b2_new[f + 1] = b2_old[f + 1] + db[1];
       }
     }
+    TTT_STAMP(6);
     __syncthreads();
+    TTT_STAMP(7);
 
     // ---------------- E: XQW = XQ + LN(sum_w Z2bar_w + b2_old)
 #pragma unroll
@@ -522,6 +555,8 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
       *reinterpret_cast<uint2*>(dst) = make_uint2(H::pack(y[0], y[1]), H::pack(y[2], y[3]));
     }
 
+    TTT_STAMP(8);
+    TTT_STAMP_SM();
     if (p.W1_memo && memo_left == 0) {  // state after this mini-batch
       const long long m = s * p.NS + n / p.memo;
       float S1[2][8][4], S2[4][4][4];
@@ -600,3 +635,14 @@ int mlp_fwd_fast(const MlpFwdParams& p, cudaStream_t stream) {
 }
 
 }  // namespace ttt
+
+#ifdef TTT_PHASE_STAMPS
+// Copies the timeline of the last forward launch: rows x 10 values (9 stamps in ns, SM id).
+extern "C" int ttt_phase_stamps_read(unsigned long long* out, int rows) {
+  if (rows < 0 || rows > ttt::mlp_tc::kStampCTAs) return TTT_ERR_SHAPE;
+  return cudaMemcpyFromSymbol(out, ttt::mlp_tc::g_phase_stamps, sizeof(unsigned long long) * ttt::mlp_tc::kStamps * rows) ==
+                 cudaSuccess
+             ? TTT_OK
+             : TTT_ERR_CUDA;
+}
+#endif

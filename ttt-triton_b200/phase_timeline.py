@@ -1,0 +1,72 @@
+"""Per-phase timeline of the TTT-MLP tensor-core forward (one mini-batch, every CTA).
+
+    python ttt-triton_b200/build.py --phase-stamps
+    python ttt-triton_b200/phase_timeline.py [--batch B]
+
+Runs the config-1 forward (B x 12 heads, L 2048, F 64, FF 256, bf16, memo states every 16
+mini-batches) on libttt_b200_stamps.so, whose kernel records %globaltimer on thread 0 of
+every CTA before and after each CTA barrier of mini-batch 64, and prints the median time of
+each phase, separately for CTAs alone on their SM and CTAs sharing it. Phases: A = the first
+MMA phase (Z1, XQ W1, GELU, partial Z2), C = the LayerNorm-gradient row phase, D = the
+second MMA phase (G1, the updates, the dual-form read-out products), E = the read-out
+LayerNorm row phase; "sync" = the wait at the barrier that ends a phase.
+"""
+
+from __future__ import annotations
+
+import argparse
+import collections
+import ctypes
+import os
+import statistics
+import sys
+
+os.environ["TTT_B200_LIB"] = "libttt_b200_stamps.so"
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+import torch  # noqa: E402
+
+import _core  # noqa: E402
+import _lib  # noqa: E402
+import synthetic as S  # noqa: E402
+
+PHASES = ("top barrier", "A", "A sync", "C", "C sync", "D", "D sync", "E")
+NAMES = ("ln_w", "ln_b", "W1", "b1", "W2", "b2", "XQ", "XV", "XK", "eta")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=16)
+    args = ap.parse_args()
+    read = _lib.lib.ttt_phase_stamps_read
+    read.argtypes, read.restype = [ctypes.c_void_p, ctypes.c_int], ctypes.c_int
+    B, NH = args.batch, 12
+    d = S.make_mlp_inputs(B, NH, 128, 16, 64, 256, dtype=torch.bfloat16, device="cuda", seed=0)
+    for _ in range(3):
+        _core.mlp_forward(*(d[k] for k in NAMES), 16, 16, for_backward=False)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        _core.mlp_forward(*(d[k] for k in NAMES), 16, 16, for_backward=False)
+    e1.record()
+    torch.cuda.synchronize()
+    n = B * NH
+    buf = (ctypes.c_ulonglong * (10 * n))()
+    if read(buf, n) != 0:
+        raise RuntimeError("reading the timeline failed (is this the --phase-stamps build?)")
+    rows = [[buf[i * 10 + k] for k in range(10)] for i in range(n)]
+    per_sm = collections.Counter(r[9] for r in rows)
+    print(f"B={B}: {n} streams, {e0.elapsed_time(e1) / 5:.4f} ms per launch")
+    for label, sel in (("alone on its SM", [r for r in rows if per_sm[r[9]] == 1]),
+                       ("sharing its SM", [r for r in rows if per_sm[r[9]] > 1])):
+        if not sel:
+            continue
+        total = statistics.median(r[8] - r[0] for r in sel)
+        print(f"{label}: {len(sel)} CTAs, mini-batch {total:.0f} ns (median)")
+        for k, name in enumerate(PHASES):
+            print(f"  {name:12s} {statistics.median(r[k + 1] - r[k] for r in sel):7.0f} ns")
+
+
+if __name__ == "__main__":
+    main()
