@@ -83,7 +83,9 @@ DT = {"f32": torch.float32, "bf16": torch.bfloat16}
 # the same workload: (bytes, tokens in that launch, summary file). Scaled to the
 # launch measured here by tokens processed.
 NCU_TRAFFIC = {
-    ("mlp_fwd_c1", "mlp_fwd"): (232.0e6, 16 * 12 * 2048, "profiles/mlp_fwd_tc_config1.md"),
+    # captured with a memo state every 16 mini-batches (201 MB more writes than the one memo
+    # state per stream the workload now asks for): an upper bound, re-captured when possible
+    ("mlp_fwd_c1", "mlp_fwd"): (422.88e6, 16 * 12 * 2048, "profiles/mlp_fwd_tc_config1.md"),
     ("linear_fwd_c2", "linear_fwd"): (557.3e6, 32 * 8 * 4096, "profiles/linear_fwd_tc_config2.md"),
     ("linear_fwdbwd_c2", "linear_bwd"): (1252.9e6, 32 * 8 * 4096, "profiles/linear_bwd_tc_config2.md"),
     # captured at batch 4 (64 streams); traffic per stream is size-independent, scaled by tokens
@@ -220,10 +222,11 @@ def kernel_step(w, d, dO):
 
 
 def memo_of(w):
-    """Memo-segment size of an MLP workload: TritonMLP.apply always writes memo states
-    (mlp_triton.py:15-62), so both the device-timed and the end-to-end legs write them, at
-    the workload's memo size or, when it names none, every checkpoint group."""
-    return w["memo"] or w["ckpt"]
+    """Memo-segment size of an MLP workload. TritonMLP.apply always writes memo states
+    (mlp_triton.py:15-62), so the device-timed and the end-to-end legs both ask for them: at
+    the workload's memo size, or, for a workload that names none (config 1), one segment
+    covering the sequence, the API's minimum (one memo state per stream)."""
+    return w["memo"] or w["L"] // CS
 
 
 def prologue_step(w, d, dO, time_bwd_kernel=False):
