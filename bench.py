@@ -83,9 +83,7 @@ DT = {"f32": torch.float32, "bf16": torch.bfloat16}
 # the same workload: (bytes, tokens in that launch, summary file). Scaled to the
 # launch measured here by tokens processed.
 NCU_TRAFFIC = {
-    # captured with a memo state every 16 mini-batches (201 MB more writes than the one memo
-    # state per stream the workload now asks for): an upper bound, re-captured when possible
-    ("mlp_fwd_c1", "mlp_fwd"): (422.88e6, 16 * 12 * 2048, "profiles/mlp_fwd_tc_config1.md"),
+    ("mlp_fwd_c1", "mlp_fwd"): (255.97e6, 16 * 12 * 2048, "profiles/mlp_fwd_tc_config1.md"),
     ("linear_fwd_c2", "linear_fwd"): (557.3e6, 32 * 8 * 4096, "profiles/linear_fwd_tc_config2.md"),
     ("linear_fwdbwd_c2", "linear_bwd"): (1252.9e6, 32 * 8 * 4096, "profiles/linear_bwd_tc_config2.md"),
     # captured at batch 4 (64 streams); traffic per stream is size-independent, scaled by tokens
