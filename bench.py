@@ -24,6 +24,9 @@ ttt-triton_b200/synthetic.py):
   lookback 336, horizon 96, 7 channels, global batch 256, MSE, AdamW, clipping), every TTT
   stage on this library, bf16 activations. Strong scaling: the global batch is split over
   the ranks and DistributedDataParallel averages the gradients with NCCL.
+* ``forecaster_main``: one training step of the reference's own main.py model (one TTT-MLP
+  layer, d_model 128, 4 heads of 32, mini-batch 64, base learning rate 0.05, lookback 384,
+  horizon 96, one channel, batch 32, fp16 activations), on the general kernels.
 
 A step is one pass of the hot path over one batch. Multi-GPU runs of a workload are weak
 scaling: every rank processes its own full batch (the (b, h) streams are independent, so
@@ -69,6 +72,10 @@ WORKLOADS = {
                         memo=None),
     "forecaster_c4": dict(kind="forecaster", B=256, NH=4, L=336, F=64, FF=64, dtype="bf16", bwd=True, ckpt=16,
                           memo=2, layers=4, horizon=96, channels=7),
+    # the reference's own main.py model: ModelConfig(seq_len=384, model_dim=128, num_heads=4,
+    # mini_batch_size=64, ttt_base_lr=0.05, ...), batch 32, univariate series, fp16 autocast
+    "forecaster_main": dict(kind="forecaster", B=32, NH=4, L=384, F=32, FF=32, dtype="f16", bwd=True, ckpt=16,
+                            memo=2, layers=1, horizon=96, channels=1, cs=64, base_lr=0.05),
 }
 MEMO = ("XQW", "XQ", "XK", "XU", "W1_memo", "b1_memo", "W2_memo", "b2_memo", "ln_w", "ln_b")
 PRO = ("hidden", "wq", "bq", "wk", "bk", "wv", "bv", "wu", "bu", "lr_w", "lr_b", "ln_w", "ln_b")
@@ -78,7 +85,7 @@ EPI = ("XQW", "pn_w", "pn_b", "wo_w", "wo_b")
 POST_NORM_EPS = 1e-6  # ttt_layer.py:77
 RESULT_KEY = {"prologue": "hidden", "epilogue": "XQW"}  # the input whose gradient e2e reads back
 CS = 16
-DT = {"f32": torch.float32, "bf16": torch.bfloat16}
+DT = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
 # DRAM bytes (read + write) of one launch of the dominant kernel from an ncu capture of
 # the same workload: (bytes, tokens in that launch, summary file). Scaled to the
 # launch measured here by tokens processed.
@@ -482,11 +489,12 @@ def forecaster_cpu_reference(w, budget_s=12.0):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     B = 2
+    cs, lr = w.get("cs", CS), w.get("base_lr", BASE_LR)
     model = TTTForecaster(w["channels"], w["channels"], w["horizon"], w["L"], model_dim=w["NH"] * w["F"],
-                          num_heads=w["NH"], num_layers=w["layers"], mini_batch_size=CS,
+                          num_heads=w["NH"], num_layers=w["layers"], mini_batch_size=cs, ttt_base_lr=lr,
                           scan_checkpoint_group_size=w["ckpt"], mem_cache_segment_n_mini_batches=w["memo"])
     P = {k: v.detach() for k, v in model.named_parameters()}
-    series = S.make_forecast_series(seed=0)
+    series = S.make_forecast_series(channels=w["channels"], seed=0)
     x, y = S.forecast_windows(series, w["L"], w["horizon"], B, torch.Generator().manual_seed(0))
     lay = model.layers[0]
     prefixes = [f"layers.{i}." for i in range(w["layers"])]
@@ -494,7 +502,7 @@ def forecaster_cpu_reference(w, budget_s=12.0):
     t_end = time.perf_counter() + budget_s
     while reps < 1 or (time.perf_counter() < t_end and reps < 5):
         t0 = time.perf_counter()
-        O.forecaster_grads(P, x, y, prefixes, lay.rope_cos, lay.rope_sin, w["horizon"], CS, BASE_LR, w["ckpt"],
+        O.forecaster_grads(P, x, y, prefixes, lay.rope_cos, lay.rope_sin, w["horizon"], cs, lr, w["ckpt"],
                            w["memo"])
         dt = time.perf_counter() - t0
         best = dt if best is None else min(best, dt)
@@ -517,13 +525,14 @@ def run_forecaster(args, w, rank, world, local_rank):
     b_rank = w["B"] // world
     torch.manual_seed(0)  # identical initial parameters on every rank
     model = TTTForecaster(w["channels"], w["channels"], w["horizon"], w["L"], model_dim=w["NH"] * w["F"],
-                          num_heads=w["NH"], num_layers=w["layers"], mini_batch_size=CS,
-                          scan_checkpoint_group_size=w["ckpt"], mem_cache_segment_n_mini_batches=w["memo"]).to(dev)
+                          num_heads=w["NH"], num_layers=w["layers"], mini_batch_size=w.get("cs", CS),
+                          ttt_base_lr=w.get("base_lr", BASE_LR), scan_checkpoint_group_size=w["ckpt"],
+                          mem_cache_segment_n_mini_batches=w["memo"], act_dtype=DT[w["dtype"]]).to(dev)
     net = model
     if world > 1:
         net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local_rank])
     opt = make_optimizer(model)
-    series = S.make_forecast_series(seed=0)
+    series = S.make_forecast_series(channels=w["channels"], seed=0)
     gen = torch.Generator().manual_seed(1000 + rank)
     pool = [S.forecast_windows(series, w["L"], w["horizon"], b_rank, gen) for _ in range(4)]
     dev_pool = [(x.to(dev), y.to(dev)) for x, y in pool]
@@ -558,7 +567,7 @@ def run_forecaster(args, w, rank, world, local_rank):
     kern_ms, kern_flops = forecaster_mlp_bwd_ms(w, b_rank, dev)
     # its DRAM traffic from the ncu capture at batch 128 (profiles/mlp_bwd_tc_fxf_config4.md),
     # scaled by the streams (traffic grows in proportion to them)
-    kern_traffic = FXF_BWD_TRAFFIC_B128 * b_rank / 128
+    kern_traffic = FXF_BWD_TRAFFIC_B128 * b_rank / 128 if w.get("cs", CS) == CS else None
     # end to end: each step's windows copied from pinned host memory, loss read back
     host = [(x.pin_memory(), y.pin_memory()) for x, y in pool]
     xb, yb = torch.empty_like(dev_pool[0][0]), torch.empty_like(dev_pool[0][1])
@@ -589,14 +598,16 @@ def run_forecaster(args, w, rank, world, local_rank):
         "scaling": "strong", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
         "config": {"workload": args.workload, "global_batch": w["B"], "batch_per_rank": b_rank, "layers": w["layers"],
                    "d_model": w["NH"] * w["F"], "NH": w["NH"], "L": w["L"], "horizon": w["horizon"],
-                   "channels": w["channels"], "CS": CS, "inner": "F x F (64)", "memo_segment_size": w["memo"],
+                   "channels": w["channels"], "CS": w.get("cs", CS), "inner": f"F x F ({w['F']})",
+                   "base_lr": w.get("base_lr", BASE_LR), "memo_segment_size": w["memo"],
                    "checkpoint_group_size": w["ckpt"], "parallelism": f"dp{world} (DDP, NCCL all-reduce)",
                    "tokens": "B * NH * L per TTT layer, summed over layers",
                    "samples_per_s": w["B"] / (ms_step / 1e3),
                    "l2": "activations larger than L2 (no flush)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
                      "frac": achieved / bf16, "traffic": kern_traffic,
-                     "traffic_source": "profiles/mlp_bwd_tc_fxf_config4.md (batch 128, scaled)",
+                     "traffic_source": ("profiles/mlp_bwd_tc_fxf_config4.md (batch 128, scaled)"
+                                        if kern_traffic is not None else None),
                      "peak_source": src, "kernel": "mlp_bwd F x F scan backward (one layer)",
                      "kernel_ms": kern_ms, "kernel_flops": kern_flops},
         "e2e": {"value": tokens / (e2e_ms / args.steps / 1e3), "unit": "tokens/s",
@@ -617,35 +628,36 @@ FXF_BWD_TRAFFIC_B128 = 286.697984e6 + 73.438464e6
 
 
 def forecaster_mlp_bwd_ms(w, b_rank, dev):
-    """CUDA-event time of one layer's F x F scan backward (the stored-pre-activation
-    tensor-core path the forecaster's TritonMLP takes) at the per-rank shape, and its useful
-    FLOPs: 38 F FF + 12 CS FF + 12 CS F per token (algorithmic())."""
+    """Device time of one layer's scan backward at the per-rank shape, averaged over
+    back-to-back launches (the stored-pre-activation tensor-core path the config-4 layer
+    takes; the general kernel for main.py's CS 64, head_dim 32), and its useful FLOPs:
+    38 F FF + 12 CS FF + 12 CS F per token (algorithmic())."""
     import _core
     import synthetic as S
 
-    NC, F, FF = w["L"] // CS, w["F"], w["FF"]
-    d = S.make_mlp_inputs(b_rank, w["NH"], NC, CS, F, FF, dtype=torch.bfloat16, device=dev, seed=5)
-    dO = S.make_upstream((b_rank, w["NH"], NC, CS, F), device=dev, seed=6, dtype=torch.bfloat16)
+    cs = w.get("cs", CS)
+    NC, F, FF = w["L"] // cs, w["F"], w["FF"]
+    dt = DT[w["dtype"]]
+    d = S.make_mlp_inputs(b_rank, w["NH"], NC, cs, F, FF, dtype=dt, device=dev, seed=5)
+    dO = S.make_upstream((b_rank, w["NH"], NC, cs, F), device=dev, seed=6, dtype=dt)
     _, last, ck, _, zs = _core.mlp_forward(d["ln_w"], d["ln_b"], d["W1"], d["b1"], d["W2"], d["b2"], d["XQ"], d["XV"],
-                                           d["XK"], d["eta"], w["ckpt"], w["memo"], for_backward=True)
+                                           d["XK"], d["eta"], min(w["ckpt"], NC), w["memo"], for_backward=True)
     stream = torch.cuda.current_stream(dev)
 
     def bwd():
-        _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"], saved=zs,
-                           W1_last=last[0], W2_last=last[2])
+        _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, min(w["ckpt"], NC),
+                           saved=zs, W1_last=last[0], W2_last=last[2])
 
     bwd()
     torch.cuda.synchronize()
-    tot = 0.0
-    for _ in range(3):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(5):
         bwd()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        tot += e0.elapsed_time(e1)
-    flops = (38 * F * FF + 12 * CS * FF + 12 * CS * F) * b_rank * w["NH"] * w["L"]
-    return tot / 3, flops
+    e1.record(stream)
+    torch.cuda.synchronize()
+    flops = (38 * F * FF + 12 * cs * FF + 12 * cs * F) * b_rank * w["NH"] * w["L"]
+    return e0.elapsed_time(e1) / 5, flops
 
 
 def cpu_full_shape(w, steps, warmup):

@@ -54,38 +54,86 @@ __device__ __forceinline__ void copy_f32(float* dst, const float* src, int n) {
 // participates; callers synchronise before (inputs ready) and after (outputs ready).
 // Every output element is owned by one thread, and the owner depends only on (M, N),
 // so two calls with the same (M, N) may update the same C without a barrier between.
+// Shared-memory banks: with a transposed B the lanes of a warp read B[n*ldb + k] at one k
+// and n two apart, so for ldb a multiple of 16 floats they all fall in one bank. Each thread
+// then runs its k loop from its own offset (lane mod K) and wraps around, spreading the lanes
+// over the banks (the order of the sum changes, not its terms). Pairs that sit next to each
+// other in memory (A(m, k), A(m+1, k) of a transposed A; B(k, n), B(k, n+1) of a plain B)
+// are read as one 8-byte load when their addresses allow it.
+template <bool TA, bool TB, bool VA, bool VB>
+__device__ __forceinline__ void block_mm_tile(float* C, int ldc, const float* A, int lda, const float* B, int ldb,
+                                              int m, int n, int K, int rot, float alpha, float beta) {
+  float c00 = 0.f, c01 = 0.f, c10 = 0.f, c11 = 0.f;
+#pragma unroll 4
+  for (int kk = 0; kk < K; ++kk) {
+    int k = kk + rot;
+    if (k >= K) k -= K;
+    float a0, a1, b0, b1;
+    if (TA) {
+      if (VA) {
+        const float2 a = *reinterpret_cast<const float2*>(A + (long long)k * lda + m);
+        a0 = a.x;
+        a1 = a.y;
+      } else {
+        a0 = A[(long long)k * lda + m];
+        a1 = A[(long long)k * lda + m + 1];
+      }
+    } else {
+      a0 = A[(long long)m * lda + k];
+      a1 = A[(long long)(m + 1) * lda + k];
+    }
+    if (TB) {
+      b0 = B[(long long)n * ldb + k];
+      b1 = B[(long long)(n + 1) * ldb + k];
+    } else if (VB) {
+      const float2 b = *reinterpret_cast<const float2*>(B + (long long)k * ldb + n);
+      b0 = b.x;
+      b1 = b.y;
+    } else {
+      b0 = B[(long long)k * ldb + n];
+      b1 = B[(long long)k * ldb + n + 1];
+    }
+    c00 = fmaf(a0, b0, c00);
+    c01 = fmaf(a0, b1, c01);
+    c10 = fmaf(a1, b0, c10);
+    c11 = fmaf(a1, b1, c11);
+  }
+  float* c0 = C + (long long)m * ldc + n;
+  float* c1 = c0 + ldc;
+  if (beta == 0.f) {
+    c0[0] = alpha * c00;
+    c0[1] = alpha * c01;
+    c1[0] = alpha * c10;
+    c1[1] = alpha * c11;
+  } else {
+    c0[0] = fmaf(alpha, c00, beta * c0[0]);
+    c0[1] = fmaf(alpha, c01, beta * c0[1]);
+    c1[0] = fmaf(alpha, c10, beta * c1[0]);
+    c1[1] = fmaf(alpha, c11, beta * c1[1]);
+  }
+}
+
 template <bool TA, bool TB>
 __device__ __forceinline__ void block_mm(float* C, int ldc, const float* A, int lda, const float* B, int ldb,
                                          int M, int N, int K, float alpha, float beta) {
   const int tn = N >> 1;
   const int tiles = (M >> 1) * tn;
+  const int rot = TB ? (threadIdx.x & 31) % K : 0;
+  // 8-byte loads need an even leading dimension and an 8-byte aligned base (m and n are even)
+  const bool va = TA && (lda & 1) == 0 && (reinterpret_cast<uintptr_t>(A) & 7) == 0;
+  const bool vb = !TB && (ldb & 1) == 0 && (reinterpret_cast<uintptr_t>(B) & 7) == 0;
   for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
     const int m = (t / tn) << 1;
     const int n = (t % tn) << 1;
-    float c00 = 0.f, c01 = 0.f, c10 = 0.f, c11 = 0.f;
-#pragma unroll 4
-    for (int k = 0; k < K; ++k) {
-      const float a0 = TA ? A[(long long)k * lda + m] : A[(long long)m * lda + k];
-      const float a1 = TA ? A[(long long)k * lda + m + 1] : A[(long long)(m + 1) * lda + k];
-      const float b0 = TB ? B[(long long)n * ldb + k] : B[(long long)k * ldb + n];
-      const float b1 = TB ? B[(long long)(n + 1) * ldb + k] : B[(long long)k * ldb + n + 1];
-      c00 = fmaf(a0, b0, c00);
-      c01 = fmaf(a0, b1, c01);
-      c10 = fmaf(a1, b0, c10);
-      c11 = fmaf(a1, b1, c11);
-    }
-    float* c0 = C + (long long)m * ldc + n;
-    float* c1 = c0 + ldc;
-    if (beta == 0.f) {
-      c0[0] = alpha * c00;
-      c0[1] = alpha * c01;
-      c1[0] = alpha * c10;
-      c1[1] = alpha * c11;
+    if (va) {
+      if (vb)
+        block_mm_tile<TA, TB, true, true>(C, ldc, A, lda, B, ldb, m, n, K, rot, alpha, beta);
+      else
+        block_mm_tile<TA, TB, true, false>(C, ldc, A, lda, B, ldb, m, n, K, rot, alpha, beta);
+    } else if (vb) {
+      block_mm_tile<TA, TB, false, true>(C, ldc, A, lda, B, ldb, m, n, K, rot, alpha, beta);
     } else {
-      c0[0] = fmaf(alpha, c00, beta * c0[0]);
-      c0[1] = fmaf(alpha, c01, beta * c0[1]);
-      c1[0] = fmaf(alpha, c10, beta * c1[0]);
-      c1[1] = fmaf(alpha, c11, beta * c1[1]);
+      block_mm_tile<TA, TB, false, false>(C, ldc, A, lda, B, ldb, m, n, K, rot, alpha, beta);
     }
   }
 }

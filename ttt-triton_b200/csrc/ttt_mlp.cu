@@ -144,8 +144,12 @@ __global__ void __launch_bounds__(256) mlp_fwd_kernel(MlpFwdParams p) {
   copy_f32(p.b2_last + s * F, b2, F);
 }
 
-// Shared-memory budget of the general backward's fp32 tiles (the opt-in maximum per CTA).
-constexpr long long kMlpBwdSmemFloats = 232448 / 4;
+// Shared-memory budget of the general backward's fp32 tiles (bytes; default the opt-in
+// maximum per CTA).
+#ifndef TTT_BWD_SMEM_CAP
+#define TTT_BWD_SMEM_CAP 232448
+#endif
+constexpr long long kMlpBwdSmemFloats = TTT_BWD_SMEM_CAP / 4;
 
 // The general backward's fp32 tiles, carved in a fixed order: into shared memory while they
 // fit in `cap` floats, then (from the first that does not, all the rest) into the stream's
