@@ -516,7 +516,7 @@ def run_forecaster(args, w, rank, world, local_rank):
     the ranks, DDP gradient all-reduce over NCCL)."""
     import _lib
     import synthetic as S
-    from forecaster import TTTForecaster, make_optimizer, train_step
+    from forecaster import GraphedTrainStep, TTTForecaster, make_optimizer, train_step
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -531,7 +531,8 @@ def run_forecaster(args, w, rank, world, local_rank):
     net = model
     if world > 1:
         net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local_rank])
-    opt = make_optimizer(model)
+    graphed = world == 1 and not args.no_graph  # one CUDA-graph replay per step on one GPU
+    opt = make_optimizer(model, capturable=graphed)
     series = S.make_forecast_series(channels=w["channels"], seed=0)
     gen = torch.Generator().manual_seed(1000 + rank)
     pool = [S.forecast_windows(series, w["L"], w["horizon"], b_rank, gen) for _ in range(4)]
@@ -543,8 +544,17 @@ def run_forecaster(args, w, rank, world, local_rank):
 
             dist.barrier()
 
-    for i in range(args.warmup):
-        train_step(net, opt, *dev_pool[i % 4])
+    step_fn = lambda x, y: train_step(net, opt, x, y)  # noqa: E731
+    per_step_launches = None
+    if graphed:
+        n0 = _lib.launch_count()
+        step_fn = GraphedTrainStep(net, opt, *dev_pool[0], warmup=args.warmup)
+        # library kernels in the captured step (the warm-up steps' launches counted first)
+        per_step_launches = _lib.launch_count() - n0
+        per_step_launches //= args.warmup + 1
+    else:
+        for i in range(args.warmup):
+            step_fn(*dev_pool[i % 4])
     torch.cuda.synchronize()
     sampler = ClockSampler(smi_index(dev))
     sampler.start()
@@ -555,11 +565,11 @@ def run_forecaster(args, w, rank, world, local_rank):
     n0 = _lib.launch_count()
     ev0.record(stream)
     for i in range(args.steps):
-        train_step(net, opt, *dev_pool[i % 4])
+        step_fn(*dev_pool[i % 4])
     ev1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    launches = _lib.launch_count() - n0
+    launches = _lib.launch_count() - n0 if per_step_launches is None else per_step_launches * args.steps
     clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1)
     # dominant kernel (largest share of the step's launch list, profiles/
@@ -579,9 +589,12 @@ def run_forecaster(args, w, rank, world, local_rank):
     e0.record(stream)
     for i in range(args.steps):
         hx, hy = host[i % 4]
+        if graphed:  # straight into the captured step's input buffers
+            loss_host.copy_(step_fn(hx, hy), non_blocking=True)
+            continue
         xb.copy_(hx, non_blocking=True)
         yb.copy_(hy, non_blocking=True)
-        loss_host.copy_(train_step(net, opt, xb, yb), non_blocking=True)
+        loss_host.copy_(step_fn(xb, yb), non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -603,6 +616,7 @@ def run_forecaster(args, w, rank, world, local_rank):
                    "checkpoint_group_size": w["ckpt"], "parallelism": f"dp{world} (DDP, NCCL all-reduce)",
                    "tokens": "B * NH * L per TTT layer, summed over layers",
                    "samples_per_s": w["B"] / (ms_step / 1e3),
+                   "cuda_graph": graphed,
                    "l2": "activations larger than L2 (no flush)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
                      "frac": achieved / bf16, "traffic": kern_traffic,
@@ -1005,6 +1019,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mlp_fwd_c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="forecaster workloads on one GPU: eager steps instead of one CUDA-graph replay per step")
     ap.add_argument("--no-fwdbwd", action="store_true",
                     help="skip the config-3 forward+backward record of the default workload")
     ap.add_argument("--batch", type=int, default=None,

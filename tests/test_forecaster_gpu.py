@@ -114,3 +114,42 @@ def test_training_step_on_the_synthetic_series():
     assert all(l == l and l < 1e3 for l in losses)
     assert not torch.equal(before, model.head.weight.detach())
     assert losses[-1] < losses[0]
+
+
+@pytest.mark.parametrize("cfg", ["config4_like", "main_py"])
+def test_cuda_graph_training_step_matches_eager(cfg):
+    """GraphedTrainStep (the step captured once in a CUDA graph, then replayed) trains exactly
+    as eager train_step: the same losses and parameters after three warm-up steps and three
+    replays on different batches (fp32 atomics in the memo-mixing backward may reorder
+    additions: compared at 1e-3)."""
+    from forecaster import GraphedTrainStep
+
+    if cfg == "main_py":
+        kw = dict(model_dim=128, num_heads=4, num_layers=1, mini_batch_size=64, ttt_base_lr=0.05,
+                  act_dtype=torch.float16)
+        C, L, H = 1, 384, 96
+    else:
+        kw = dict(model_dim=128, num_heads=2, num_layers=2)
+        C, L, H = 7, 96, 24
+    series = S.make_forecast_series(3000, C, seed=5)
+    gen = torch.Generator().manual_seed(6)
+    batches = [tuple(t.to(DEV) for t in S.forecast_windows(series, L, H, 8, gen)) for _ in range(4)]
+    models, losses = [], []
+    for graphed in (False, True):
+        torch.manual_seed(7)
+        model = TTTForecaster(C, C, H, L, **kw).to(DEV)
+        opt = make_optimizer(model, capturable=graphed)
+        if graphed:
+            step = GraphedTrainStep(model, opt, *batches[0], warmup=3)
+            got = [float(step(*b)) for b in batches[1:]]
+        else:
+            for _ in range(3):
+                train_step(model, opt, *batches[0])
+            got = [float(train_step(model, opt, *b)) for b in batches[1:]]
+        models.append(model)
+        losses.append(got)
+    torch.cuda.synchronize()
+    for a, b in zip(*losses):
+        assert abs(a - b) <= 1e-3 * abs(b)
+    for (name, pa), (_, pb) in zip(models[0].named_parameters(), models[1].named_parameters()):
+        assert_close(name, pb, pa.detach(), 1e-3)

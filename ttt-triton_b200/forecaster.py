@@ -193,10 +193,12 @@ def load_reference_state_dict(model, state_dict):
         raise KeyError(f"state dict mismatch: missing {missing}, unexpected {unexpected}")
 
 
-def make_optimizer(model, lr=1e-3, weight_decay=1e-2):
-    """AdamW as main.py:68 (the fused multi-tensor update on CUDA)."""
+def make_optimizer(model, lr=1e-3, weight_decay=1e-2, capturable=False):
+    """AdamW as main.py:68 (the fused multi-tensor update on CUDA). capturable keeps the step
+    counts on the device, as a CUDA-graph-captured step (GraphedTrainStep) needs."""
     fused = all(p.is_cuda for p in model.parameters())
-    return torch.optim.AdamW(model.parameters(), lr=lr, weight_decay=weight_decay, fused=fused)
+    return torch.optim.AdamW(model.parameters(), lr=lr, weight_decay=weight_decay, fused=fused,
+                             capturable=capturable and fused)
 
 
 def train_step(model, optimizer, x, y, clip=1.0):
@@ -213,10 +215,44 @@ def train_step(model, optimizer, x, y, clip=1.0):
     return loss.detach()
 
 
+class GraphedTrainStep:
+    """train_step captured once in a CUDA graph and replayed: one graph launch per step
+    instead of the step's ~80-400 kernel launches from Python, for a single-GPU model whose
+    step is launch-bound (small batches, short sequences). The optimizer must be made with
+    make_optimizer(..., capturable=True). Construction runs `warmup` ordinary training steps
+    on (x, y) on a side stream (the model trains on them) and then captures one step;
+    calling the object copies a batch into the captured input buffers, replays the graph and
+    returns the loss tensor of that step (not synchronised). The batch shape is fixed at
+    construction. Not for DistributedDataParallel models (their all-reduce is not captured
+    here)."""
+
+    def __init__(self, model, optimizer, x, y, clip=1.0, warmup=3):
+        if isinstance(model, nn.parallel.DistributedDataParallel):
+            raise ValueError("GraphedTrainStep captures single-GPU steps; use train_step with DDP")
+        self.x = x.detach().clone()
+        self.y = y.detach().clone()
+        side = torch.cuda.Stream(device=self.x.device)
+        side.wait_stream(torch.cuda.current_stream(self.x.device))
+        with torch.cuda.stream(side):  # allocator pools, optimizer state, one-time set-up
+            for _ in range(warmup):
+                train_step(model, optimizer, self.x, self.y, clip)
+        torch.cuda.current_stream(self.x.device).wait_stream(side)
+        optimizer.zero_grad(set_to_none=True)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.loss = train_step(model, optimizer, self.x, self.y, clip)
+
+    def __call__(self, x, y):
+        self.x.copy_(x, non_blocking=True)
+        self.y.copy_(y, non_blocking=True)
+        self.graph.replay()
+        return self.loss
+
+
 def tokens_per_step(batch, seq_len, num_heads, num_layers):
     """TTT tokens (b, h, t) one step runs through the scan: every layer's B * NH * L."""
     return batch * num_heads * seq_len * num_layers
 
 
 __all__ = ["BatchCopies", "linear_act", "TTTMLPLayer", "TTTForecaster", "rope_table_3d", "load_reference_state_dict", "make_optimizer",
-           "train_step", "tokens_per_step"]
+           "train_step", "GraphedTrainStep", "tokens_per_step"]
