@@ -79,7 +79,8 @@ struct Fwd {
   static constexpr int OFF_P = OFF_EG + TILE;                // 16-bit [C][C]: -P1
   static constexpr int OFF_B1 = OFF_P + ETA;                 // fp32 [FFW]
   static constexpr int OFF_B2 = OFF_B1 + FFW * 4;            // fp32 [2][F] (ping-pong)
-  static constexpr int SMEM = OFF_B2 + 2 * F * 4 + 1024;     // + slack to align the base to 1024 bytes
+  static constexpr int OFF_LN = OFF_B2 + 2 * F * 4;          // fp32 [2][F]: this head's LayerNorm gamma, beta
+  static constexpr int SMEM = OFF_LN + 2 * F * 4 + 1024;     // + slack to align the base to 1024 bytes
   // W1^T and W2^T slices: 128 columns per warp in its lane quadrant, two column blocks for 8 warps
   static constexpr uint32_t TMEM_COLS = NW > 4 ? 256 : 128;
   // CTAs per SM: two of 8 warps (registers), four of 2 warps (TMEM: 4 x 128 columns). The
@@ -100,22 +101,91 @@ __device__ __forceinline__ void issue_stage(uint32_t st, uint32_t bar, const Mlp
   bulk_load(st + OFF_ETA, (const uint8_t*)p.eta + (s * p.NC + n) * (long long)ETA, ETA, bar);
 }
 
-// Sum of the NW warps' partial tiles for token tk, features 4q..4q+3.
-template <int NW>
-__device__ __forceinline__ void sum_partials(const float* part, int tk, int q, float* z) {
-  float4 acc = *reinterpret_cast<const float4*>(part + tk * PLD + 4 * q);
+// Row phases: LPT lanes per token, lane rq holding features FPL*rq .. FPL*rq + FPL-1
+// (FPL = 64 / LPT). The 8-warp CTA uses 16 lanes per token (one pass over the 16 tokens, short
+// per-thread load chains); the 2-warp CTA uses 8 (two passes instead of four).
+template <int LPT>
+__device__ __forceinline__ float red_lanes(float v) {
 #pragma unroll
-  for (int w = 1; w < NW; ++w) {
-    const float4 v = *reinterpret_cast<const float4*>(part + (w * C + tk) * PLD + 4 * q);
-    acc.x += v.x;
-    acc.y += v.y;
-    acc.z += v.z;
-    acc.w += v.w;
+  for (int o = 1; o < LPT; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Sum of the NW warps' partial tiles for token tk, features FPL*rq.. (FPL = 4 or 8).
+template <int NW, int FPL>
+__device__ __forceinline__ void sum_partials_rows(const float* part, int tk, int rq, float* z) {
+  const float* p0 = part + tk * PLD + FPL * rq;
+#pragma unroll
+  for (int c = 0; c < FPL / 4; ++c) {
+    float4 a = *reinterpret_cast<const float4*>(p0 + 4 * c);
+#pragma unroll
+    for (int w = 1; w < NW; ++w) {
+      const float4 u = *reinterpret_cast<const float4*>(p0 + w * C * PLD + 4 * c);
+      a.x += u.x;
+      a.y += u.y;
+      a.z += u.z;
+      a.w += u.w;
+    }
+    z[4 * c] = a.x;
+    z[4 * c + 1] = a.y;
+    z[4 * c + 2] = a.z;
+    z[4 * c + 3] = a.w;
   }
-  z[0] = acc.x;
-  z[1] = acc.y;
-  z[2] = acc.z;
-  z[3] = acc.w;
+}
+
+// Adds FPL consecutive fp32 values of a shared / global row (16-byte aligned) to z.
+template <int FPL>
+__device__ __forceinline__ void add_row(float* z, const float* src) {
+#pragma unroll
+  for (int c = 0; c < FPL / 4; ++c) {
+    const float4 b = *reinterpret_cast<const float4*>(src + 4 * c);
+    z[4 * c] += b.x;
+    z[4 * c + 1] += b.y;
+    z[4 * c + 2] += b.z;
+    z[4 * c + 3] += b.w;
+  }
+}
+
+template <int FPL>
+__device__ __forceinline__ void store_row(float* dst, const float* z) {
+#pragma unroll
+  for (int c = 0; c < FPL / 4; ++c)
+    *reinterpret_cast<float4*>(dst + 4 * c) = make_float4(z[4 * c], z[4 * c + 1], z[4 * c + 2], z[4 * c + 3]);
+}
+
+// Byte offset of features FPL*rq.. of row tk in a 128-byte-swizzled 16-bit [16][64] tile.
+template <int FPL>
+__device__ __forceinline__ uint32_t row_off(int tk, int rq) {
+  return swz128(tk, (rq * FPL) >> 3) + ((rq * FPL) & 7) * 2;
+}
+
+// FPL consecutive 16-bit values -> fp32 (an 8- or 16-byte load).
+template <typename T, int FPL>
+__device__ __forceinline__ void unpack_row(const uint8_t* src, float* v) {
+  if constexpr (FPL == 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = Half2<T>::unpack(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    unpack4<T>(src, v);
+  }
+}
+
+// FPL fp32 values -> FPL consecutive 16-bit values (an 8- or 16-byte store).
+template <typename T, int FPL>
+__device__ __forceinline__ void pack_row(uint8_t* dst, const float* v, float scale) {
+  using H = Half2<T>;
+  if constexpr (FPL == 8) {
+    *reinterpret_cast<uint4*>(dst) = make_uint4(H::pack(scale * v[0], scale * v[1]), H::pack(scale * v[2], scale * v[3]),
+                                                H::pack(scale * v[4], scale * v[5]), H::pack(scale * v[6], scale * v[7]));
+  } else {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(H::pack(scale * v[0], scale * v[1]), H::pack(scale * v[2], scale * v[3]));
+  }
 }
 
 template <typename T, int NW>
@@ -127,7 +197,8 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
   constexpr int NTHREADS = L::NTHREADS, FFW = L::FFW, kCopyThread = L::kCopyThread;
   constexpr int OFF_G = L::OFF_G, OFF_EG = L::OFF_EG, OFF_P = L::OFF_P, OFF_B1 = L::OFF_B1, OFF_B2 = L::OFF_B2;
   constexpr uint32_t TMEM_COLS = L::TMEM_COLS;
-  constexpr int TPP = NTHREADS / 16;  // tokens per pass of the row phases
+  constexpr int LPT = NW > 4 ? 16 : 8, FPL = F / LPT;  // row phases: lanes per token, features per lane
+  constexpr int RTPP = NTHREADS / LPT;                // tokens per pass of the row phases
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   __shared__ uint32_t tmem_base_sh;
@@ -137,7 +208,7 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
   const int mi = lane >> 3, r8 = lane & 7;
   const long long s = blockIdx.x;
   const int h = (int)(s % p.NH);
-  const int tk0 = tid >> 4, q = tid & 15;
+  const int rtk0 = tid / LPT, rq = tid % LPT;  // row phases: token, feature group
   const int fb = 32 * warp;
   float* part = reinterpret_cast<float*>(smem + OFF_PART);
   float* pw = part + warp * C * PLD;
@@ -177,11 +248,11 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
   }
   for (int i = tid; i < FFW; i += NTHREADS) b1s[i] = p.b1_init[s * FFW + i];
   for (int i = tid; i < F; i += NTHREADS) b2s[i] = p.b2_init[s * F + i];
-  float gm[4], bt[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    gm[j] = ld_elem(p.ln_w, (long long)h * F + 4 * q + j, p.dt_ln);
-    bt[j] = ld_elem(p.ln_b, (long long)h * F + 4 * q + j, p.dt_ln);
+  // the head's LayerNorm parameters, read by the row phases from shared memory (8 per lane)
+  float* lns = reinterpret_cast<float*>(smem + L::OFF_LN);
+  for (int i = tid; i < F; i += NTHREADS) {
+    lns[i] = ld_elem(p.ln_w, (long long)h * F + i, p.dt_ln);
+    lns[F + i] = ld_elem(p.ln_b, (long long)h * F + i, p.dt_ln);
   }
   const uint32_t ones = H::pack(1.f, 1.f);
   const uint32_t a_ones[4] = {ones, ones, ones, ones};
@@ -312,46 +383,43 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
 
     // ---------------- C: Z2 = sum + b2, G2 = ln_fused_l2_bwd(Z2, XV - XK)
 #pragma unroll
-    for (int tk = tk0; tk < C; tk += TPP) {
-      float z[4], xv[4], xk[4];
-      sum_partials<NW>(part, tk, q, z);
-      const float4 bb = *reinterpret_cast<const float4*>(b2_old + 4 * q);
-      z[0] += bb.x;
-      z[1] += bb.y;
-      z[2] += bb.z;
-      z[3] += bb.w;
-      if (p.Z2_out)
-        *reinterpret_cast<float4*>(p.Z2_out + (s * p.NC + n) * (long long)(C * F) + tk * F + 4 * q) =
-            make_float4(z[0], z[1], z[2], z[3]);
-      const uint32_t xo = swz128(tk, q >> 1) + (q & 1) * 8;
-      unpack4<T>(st + OFF_XV + xo, xv);
-      unpack4<T>(st + OFF_XK + xo, xk);
-      const float mu = red16(z[0] + z[1] + z[2] + z[3]) * (1.f / F);
-      float d[4], m2 = 0.f;
+    for (int tk = rtk0; tk < C; tk += RTPP) {  // every lane of a warp takes the same passes
+      float z[FPL], xv[FPL], xk[FPL];
+      sum_partials_rows<NW, FPL>(part, tk, rq, z);
+      add_row<FPL>(z, b2_old + FPL * rq);
+      if (p.Z2_out) store_row<FPL>(p.Z2_out + (s * p.NC + n) * (long long)(C * F) + tk * F + FPL * rq, z);
+      const uint32_t xo = row_off<FPL>(tk, rq);
+      unpack_row<T, FPL>(st + OFF_XV + xo, xv);
+      unpack_row<T, FPL>(st + OFF_XK + xo, xk);
+      float sz = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < FPL; ++j) sz += z[j];
+      const float mu = red_lanes<LPT>(sz) * (1.f / F);
+      float d[FPL], m2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < FPL; ++j) {
         d[j] = z[j] - mu;
         m2 += d[j] * d[j];
       }
-      const float rstd = 1.f / sqrtf(red16(m2) * (1.f / F) + kLnEps);
-      float xh[4], gh[4], s1 = 0.f, s2 = 0.f;
+      const float rstd = 1.f / sqrtf(red_lanes<LPT>(m2) * (1.f / F) + kLnEps);
+      float xh[FPL], gh[FPL], s1 = 0.f, s2 = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < FPL; ++j) {
+        const float gm = lns[FPL * rq + j], bt = lns[F + FPL * rq + j];
         xh[j] = d[j] * rstd;
-        gh[j] = (gm[j] * xh[j] + bt[j] - (xv[j] - xk[j])) * gm[j];
+        gh[j] = (gm * xh[j] + bt - (xv[j] - xk[j])) * gm;
         s1 += gh[j];
         s2 += gh[j] * xh[j];
       }
-      s1 = red16(s1);
-      s2 = red16(s2);
+      s1 = red_lanes<LPT>(s1);
+      s2 = red_lanes<LPT>(s2);
       const float inv = rstd * (1.f / F);
-      float G[4];
+      float G[FPL];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) G[j] = (F * gh[j] - s1 - xh[j] * s2) * inv;
+      for (int j = 0; j < FPL; ++j) G[j] = (F * gh[j] - s1 - xh[j] * s2) * inv;
       const float e = (float)reinterpret_cast<const T*>(st + OFF_ETA)[(C - 1) * C + tk];
-      *reinterpret_cast<uint2*>(smem + OFF_G + xo) = make_uint2(H::pack(G[0], G[1]), H::pack(G[2], G[3]));
-      *reinterpret_cast<uint2*>(smem + OFF_EG + xo) =
-          make_uint2(H::pack(-e * G[0], -e * G[1]), H::pack(-e * G[2], -e * G[3]));
+      pack_row<T, FPL>(smem + OFF_G + xo, G, 1.f);
+      pack_row<T, FPL>(smem + OFF_EG + xo, G, -e);
     }
     TTT_STAMP(4);
     __syncthreads();
@@ -528,31 +596,27 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
 
     // ---------------- E: XQW = XQ + LN(sum_w Z2bar_w + b2_old)
 #pragma unroll
-    for (int tk = tk0; tk < C; tk += TPP) {
-      float z[4], xq[4];
-      sum_partials<NW>(part, tk, q, z);
-      const float4 bb = *reinterpret_cast<const float4*>(b2_old + 4 * q);
-      z[0] += bb.x;
-      z[1] += bb.y;
-      z[2] += bb.z;
-      z[3] += bb.w;
-      if (p.Z2b_out)
-        *reinterpret_cast<float4*>(p.Z2b_out + (s * p.NC + n) * (long long)(C * F) + tk * F + 4 * q) =
-            make_float4(z[0], z[1], z[2], z[3]);
-      unpack4<T>(st + OFF_XQ + swz128(tk, q >> 1) + (q & 1) * 8, xq);
-      const float mu = red16(z[0] + z[1] + z[2] + z[3]) * (1.f / F);
-      float d[4], m2 = 0.f;
+    for (int tk = rtk0; tk < C; tk += RTPP) {
+      float z[FPL], xq[FPL];
+      sum_partials_rows<NW, FPL>(part, tk, rq, z);
+      add_row<FPL>(z, b2_old + FPL * rq);
+      if (p.Z2b_out) store_row<FPL>(p.Z2b_out + (s * p.NC + n) * (long long)(C * F) + tk * F + FPL * rq, z);
+      unpack_row<T, FPL>(st + OFF_XQ + row_off<FPL>(tk, rq), xq);
+      float sz = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < FPL; ++j) sz += z[j];
+      const float mu = red_lanes<LPT>(sz) * (1.f / F);
+      float d[FPL], m2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < FPL; ++j) {
         d[j] = z[j] - mu;
         m2 += d[j] * d[j];
       }
-      const float rstd = 1.f / sqrtf(red16(m2) * (1.f / F) + kLnEps);
-      float y[4];
+      const float rstd = 1.f / sqrtf(red_lanes<LPT>(m2) * (1.f / F) + kLnEps);
+      float y[FPL];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) y[j] = xq[j] + gm[j] * d[j] * rstd + bt[j];
-      uint8_t* dst = (uint8_t*)p.out + ((s * p.NC + n) * (long long)(C * F) + tk * F + 4 * q) * 2;
-      *reinterpret_cast<uint2*>(dst) = make_uint2(H::pack(y[0], y[1]), H::pack(y[2], y[3]));
+      for (int j = 0; j < FPL; ++j) y[j] = xq[j] + lns[FPL * rq + j] * d[j] * rstd + lns[F + FPL * rq + j];
+      pack_row<T, FPL>((uint8_t*)p.out + ((s * p.NC + n) * (long long)(C * F) + tk * F + FPL * rq) * 2, y, 1.f);
     }
 
     TTT_STAMP(8);
