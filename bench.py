@@ -234,11 +234,10 @@ def memo_of(w):
     return w["memo"] or w["L"] // CS
 
 
-def prologue_step(w, d, dO, time_bwd_kernel=False):
+def prologue_step(w, d, dO):
     """Forward and backward of the prologue through the functional core: the projection GEMM
     (library), the element-wise forward kernel, the element-wise backward kernel and the two
-    projection-gradient GEMMs (library). With time_bwd_kernel, returns the backward kernel's
-    CUDA-event time in ms."""
+    projection-gradient GEMMs (library)."""
     import _core
     from prologue import concat_projections
 
@@ -248,26 +247,16 @@ def prologue_step(w, d, dO, time_bwd_kernel=False):
     P = torch.addmm(bcat, h2, Wcat.t())
     scale = BASE_LR / (F * CS)
     _core.prologue_forward(P, B, L, NH, F, CS, d["ln_w"], d["ln_b"], d["freqs_cos"], d["freqs_sin"], scale)
-    if time_bwd_kernel:
-        stream = torch.cuda.current_stream()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
     dP, _, _, _ = _core.prologue_backward(P, B, L, NH, F, CS, d["ln_w"], d["ln_b"], d["freqs_cos"],
                                           d["freqs_sin"], scale, *(dO[k] for k in PRO_OUTS))
-    if time_bwd_kernel:
-        e1.record(stream)
     torch.mm(dP, Wcat)
     torch.mm(dP.t(), h2)
-    if time_bwd_kernel:
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1)
-    return None
 
 
-def epilogue_step(w, d, dO, time_bwd_kernel=False):
+def epilogue_step(w, d, dO):
     """Forward and backward of the output epilogue through the functional core: post_norm
     kernel, wo GEMM (library), the two wo-gradient GEMMs and bias sum (library) and the
-    post_norm backward kernel. With time_bwd_kernel, returns that kernel's CUDA-event ms."""
+    post_norm backward kernel."""
     import _core
 
     Y = _core.post_norm_forward(d["XQW"], d["pn_w"], d["pn_b"], POST_NORM_EPS)
@@ -275,16 +264,7 @@ def epilogue_step(w, d, dO, time_bwd_kernel=False):
     d2 = dO.reshape(Y.shape)
     dY = torch.mm(d2, d["wo_w"])
     torch.mm(d2.t(), Y)
-    if time_bwd_kernel:
-        stream = torch.cuda.current_stream()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
     _core.post_norm_backward(d["XQW"], d["pn_w"], d["pn_b"], POST_NORM_EPS, dY, d2)
-    if time_bwd_kernel:
-        e1.record(stream)
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1)
-    return None
 
 
 def api_compute(w, d):

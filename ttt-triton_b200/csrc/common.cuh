@@ -52,8 +52,9 @@ __device__ __forceinline__ void copy_f32(float* dst, const float* src, int n) {
 // A(m,k) = TA ? A[k*lda + m] : A[m*lda + k];  B(k,n) = TB ? B[n*ldb + k] : B[k*ldb + n]
 // Pointers are generic (shared or global). M and N must be even. The whole block
 // participates; callers synchronise before (inputs ready) and after (outputs ready).
-// Every output element is owned by one thread, and the owner depends only on (M, N),
-// so two calls with the same (M, N) may update the same C without a barrier between.
+// Every output element is owned by one thread, and the owner depends only on (M, N) (and
+// the block size), so two calls with the same (M, N) may update the same C without a
+// barrier between.
 // Shared-memory banks: with a transposed B the lanes of a warp read B[n*ldb + k] at one k
 // and n two apart, so for ldb a multiple of 16 floats they all fall in one bank. Each thread
 // then runs its k loop from its own offset (lane mod K) and wraps around, spreading the lanes
@@ -113,12 +114,52 @@ __device__ __forceinline__ void block_mm_tile(float* C, int ldc, const float* A,
   }
 }
 
+// 4 x 4 output tile per thread (two loads per four FMAs instead of one per FMA): used when M
+// and N are multiples of 4 and there are at least as many such tiles as threads.
+template <bool TA, bool TB>
+__device__ __forceinline__ void block_mm_tile4(float* C, int ldc, const float* A, int lda, const float* B, int ldb,
+                                               int m, int n, int K, int rot, float alpha, float beta) {
+  float c[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) c[i][j] = 0.f;
+#pragma unroll 2
+  for (int kk = 0; kk < K; ++kk) {
+    int k = kk + rot;
+    if (k >= K) k -= K;
+    float a[4], b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      a[i] = TA ? A[(long long)k * lda + m + i] : A[(long long)(m + i) * lda + k];
+      b[i] = TB ? B[(long long)(n + i) * ldb + k] : B[(long long)k * ldb + n + i];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) c[i][j] = fmaf(a[i], b[j], c[i][j]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float* ci = C + (long long)(m + i) * ldc + n;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ci[j] = beta == 0.f ? alpha * c[i][j] : fmaf(alpha, c[i][j], beta * ci[j]);
+  }
+}
+
 template <bool TA, bool TB>
 __device__ __forceinline__ void block_mm(float* C, int ldc, const float* A, int lda, const float* B, int ldb,
                                          int M, int N, int K, float alpha, float beta) {
+  const int rot = TB ? (threadIdx.x & 31) % K : 0;
+  if ((M & 3) == 0 && (N & 3) == 0 && (M >> 2) * (N >> 2) >= (int)blockDim.x) {
+    const int tn = N >> 2;
+    const int tiles = (M >> 2) * tn;
+    for (int t = threadIdx.x; t < tiles; t += blockDim.x)
+      block_mm_tile4<TA, TB>(C, ldc, A, lda, B, ldb, (t / tn) << 2, (t % tn) << 2, K, rot, alpha, beta);
+    return;
+  }
   const int tn = N >> 1;
   const int tiles = (M >> 1) * tn;
-  const int rot = TB ? (threadIdx.x & 31) % K : 0;
   // 8-byte loads need an even leading dimension and an 8-byte aligned base (m and n are even)
   const bool va = TA && (lda & 1) == 0 && (reinterpret_cast<uintptr_t>(A) & 7) == 0;
   const bool vb = !TB && (ldb & 1) == 0 && (reinterpret_cast<uintptr_t>(B) & 7) == 0;
