@@ -32,11 +32,12 @@ A step is one pass of the hot path over one batch. Multi-GPU runs of a workload 
 scaling: every rank processes its own full batch (the (b, h) streams are independent, so
 there is no data-path collective); timing is the max over ranks of the device-timed region.
 
-The default line (``mlp_fwd_c1``) also carries a ``fwdbwd`` record: config 3 (TTT-MLP
-forward+backward, B64 NH16 L8192) as ONE global batch whose (batch, head) streams are split
-over the ranks by batch (sharding.py), strong scaling: at N GPUs each rank runs B/N
+The default line (``mlp_fwd_c1``) also carries two training records, ``fwdbwd`` (config 3:
+TTT-MLP forward+backward, B64 NH16 L8192) and ``fwdbwd_linear`` (config 2: TTT-Linear
+forward+backward, B32 NH8 L4096), each as ONE global batch whose (batch, head) streams are
+split over the ranks by batch (sharding.py), strong scaling: at N GPUs each rank runs B/N
 batches, the step time is the max over ranks and the value is the global tokens over it.
-It has its own roofline (the backward kernel), end-to-end leg and CPU baseline.
+Each has its own roofline (the backward kernel), end-to-end leg and CPU baseline.
 
 The reference arm (``--impl reference``) times the CPU port of the reference's ops/ path
 (oracle/ttt_oracle.py) on the host cores at the workload's full shape (chunked over
@@ -725,7 +726,7 @@ def ours_config(args, w, world, sharded=False):
     """The `config` object of a line (the reference arm reports the same one)."""
     par = (f"batch split over {world} GPU(s) (strong scaling), no collective" if sharded
            else f"streams sharded over {world} GPU(s), no collective")
-    return {"workload": args.workload if not sharded else "mlp_fwdbwd_c3", "B_per_rank": w["B"], "NH": w["NH"],
+    return {"workload": args.workload, "B_per_rank": w["B"], "NH": w["NH"],
             "L": w["L"], "F": w["F"], "FF": w["FF"], "CS": CS, "checkpoint_group_size": w["ckpt"],
             "memo_segment_size": memo_of(w) if w["kind"] == "mlp" else w["memo"],
             "global_batch": w["B"] * (1 if sharded else world), "parallelism": par,
@@ -810,16 +811,24 @@ def measure(args, w, d, dO, dev, rank, world, global_tokens, with_cpu):
     return rec
 
 
-def run_fwdbwd_sharded(args, rank, world, dev):
-    """Config 3 (TTT-MLP forward+backward, B64 NH16 L8192) as one global batch split over the
-    ranks by batch (sharding.shard), strong scaling. Every rank builds the same seeded global
-    inputs on its device, keeps its slice and frees the rest."""
+FWDBWD_RECORDS = (
+    ("mlp_fwdbwd_c3", "fwdbwd", "TTT-MLP fwd+bwd tokens/s (B*H*L), config 3 global batch split over the GPUs"),
+    ("linear_fwdbwd_c2", "fwdbwd_linear",
+     "TTT-Linear fwd+bwd tokens/s (B*H*L), config 2 global batch split over the GPUs"),
+)
+
+
+def run_fwdbwd_sharded(args, rank, world, dev, workload, metric):
+    """A training config (config 3: TTT-MLP, B64 NH16 L8192; config 2: TTT-Linear, B32 NH8
+    L4096; forward+backward) as one global batch split over the ranks by batch
+    (sharding.shard), strong scaling. Every rank builds the same seeded global inputs on its
+    device, keeps its slice and frees the rest."""
     import sharding
 
-    w = dict(WORKLOADS["mlp_fwdbwd_c3"], name="mlp_fwdbwd_c3")
+    w = dict(WORKLOADS[workload], name=workload)
     Bg = w["B"]
     if Bg % world:
-        raise SystemExit(f"config-3 batch {Bg} does not split over {world} ranks")
+        raise SystemExit(f"{workload} batch {Bg} does not split over {world} ranks")
     g, gO = make_inputs(w, dev, seed=0)
     d = sharding.shard(g, rank, world)
     b0, b1 = sharding.batch_range(Bg, rank, world)
@@ -827,15 +836,17 @@ def run_fwdbwd_sharded(args, rank, world, dev):
     del g, gO
     torch.cuda.empty_cache()
     wr = dict(w, B=b1 - b0)
-    rec = measure(args, wr, d, dO, dev, rank, world, Bg * w["NH"] * w["L"], with_cpu=(world == 1))
+    rec = measure(args, wr, d, dO, dev, rank, world, Bg * w["NH"] * w["L"],
+                  with_cpu=(world == 1 and not args.no_cpu_baseline))
     del d, dO
     torch.cuda.empty_cache()
     if rec is None:
         return None
     rec["config"] = ours_config(args, dict(w, B=Bg // world), world, sharded=True)
+    rec["config"]["workload"] = workload
     rec["config"]["global_batch"] = Bg
     rec["scaling"] = "strong"
-    rec["metric"] = "TTT-MLP fwd+bwd tokens/s (B*H*L), config 3 global batch split over the GPUs"
+    rec["metric"] = metric
     return rec
 
 
@@ -847,9 +858,10 @@ def run_ours(args, w, rank, world, local_rank):
     rec = measure(args, w, d, dO, dev, rank, world, world * tokens_rank, with_cpu=(world == 1 and not args.no_cpu_baseline))
     del d, dO
     torch.cuda.empty_cache()
-    fwdbwd = None
+    records = {}
     if args.workload == "mlp_fwd_c1" and not args.no_fwdbwd:
-        fwdbwd = run_fwdbwd_sharded(args, rank, world, dev)
+        for workload, key, metric in FWDBWD_RECORDS:
+            records[key] = run_fwdbwd_sharded(args, rank, world, dev, workload, metric)
     if rank != 0:
         return
     line = {
@@ -859,8 +871,7 @@ def run_ours(args, w, rank, world, local_rank):
         "config": ours_config(args, w, world),
     }
     line.update({k: v for k, v in rec.items() if k not in ("value", "unit", "ms_per_step")})
-    if fwdbwd is not None:
-        line["fwdbwd"] = fwdbwd
+    line.update(records)
     print(json.dumps(line), flush=True)
 
 
