@@ -197,34 +197,30 @@ MLP = ("ln_w", "ln_b", "W1", "b1", "W2", "b2", "XQ", "XV", "XK", "eta")
 
 def kernel_step(w, d, dO):
     """One pass of the hot path through the functional core (inputs resident in HBM).
-    Returns the number of kernel launches it made."""
+    Returns the number of the library's kernels it launched (its own launch counter)."""
     import _core
+    import _lib
 
+    n0 = _lib.launch_count()
     if w["kind"] == "prologue":
         prologue_step(w, d, dO)
-        return 2
-    if w["kind"] == "epilogue":
+    elif w["kind"] == "epilogue":
         epilogue_step(w, d, dO)
-        return 2
-    if w["kind"] == "memo":
+    elif w["kind"] == "memo":
         _core.memo_mix_forward(*(d[k] for k in MEMO), w["memo"])
         if w["bwd"]:
             _core.memo_mix_backward(*(d[k] for k in MEMO), w["memo"], dO)
-            return 5  # prep + mix (forward), prep + mix + dXK (backward)
-        return 2
-    if w["kind"] == "linear":
+    elif w["kind"] == "linear":
         XQW, Wl, bl, Wc, bc, Z = _core.linear_forward(*(d[k] for k in LIN), w["ckpt"], for_backward=w["bwd"])
         if w["bwd"]:
             _core.linear_backward(d["ln_w"], d["ln_b"], Wc, bc, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
                                   Z=Z, W_last=Wl, b_last=bl)
-            return 2
-        return 1
-    XQW, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], memo_of(w), for_backward=w["bwd"])
-    if w["bwd"]:
-        _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
-                           saved=zs, W1_last=last[0], W2_last=last[2])
-        return 2
-    return 1
+    else:
+        XQW, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in MLP), w["ckpt"], memo_of(w), for_backward=w["bwd"])
+        if w["bwd"]:
+            _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, w["ckpt"],
+                               saved=zs, W1_last=last[0], W2_last=last[2])
+    return _lib.launch_count() - n0
 
 
 def memo_of(w):

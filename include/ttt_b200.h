@@ -258,6 +258,25 @@ int ttt_device_status(unsigned int* status);
  */
 int ttt_test_hold_first_stage(int enable, unsigned long long wait_limit_ns);
 
+/*
+ * Kernels this library has enqueued in this process so far (every successful launch of any
+ * entry point). No counterpart in the reference; for benchmarks that count launches.
+ */
+unsigned long long ttt_kernel_launches(void);
+
+/*
+ * Schedule of the tensor-core MLP forward (ttt_mlp_fwd at F = 64, CS = 16, FF = 256, 16-bit
+ * activations) when B * NH streams number between the device's SM count M and 4M/3: with
+ * `balanced` set (the default) it runs as two launches of one two-stream CTA per SM that
+ * swap which streams share an SM halfway, splitting the sequence by `paired_ratio_milli`,
+ * the time of a mini-batch on an SM shared by two streams over one alone, x1000 (0: the
+ * library's measured 1500; values outside [1000, 4000] are refused with TTT_ERR_SHAPE);
+ * with it clear, one CTA per stream runs the whole sequence. Outputs are bit-identical
+ * either way; only the time differs. Process-wide; affects launches enqueued after the
+ * call. No counterpart in the reference (its grid is one program per stream).
+ */
+int ttt_set_forward_schedule(int balanced, int paired_ratio_milli);
+
 /* Bytes of scratch ttt_mlp_bwd needs for these sizes. */
 size_t ttt_mlp_bwd_scratch_bytes(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_group_size);
 

@@ -15,7 +15,8 @@ HDR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), 
 
 def header_functions():
     text = open(HDR).read()
-    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(ttt_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?(?:unsigned\s+)?(?:long\s+)*\w+\*?\s+\*?(ttt_\w+)\s*\(", text,
+                                 flags=re.M)))
 
 
 def test_header_declares_the_abi():

@@ -242,3 +242,58 @@ def test_ops_ttt_mlp_gradients_match_oracle(dtype):
     for k in NAMES:
         assert leaves[k].grad.dtype == d[k].dtype, k
         assert_close("d" + k, leaves[k].grad, ref_grads[k], tol)
+
+
+def _forward_all(d, ckpt, memo):
+    import _lib
+
+    n0 = _lib.launch_count()
+    res = _core.mlp_forward(*(d[k] for k in NAMES), ckpt, memo)
+    torch.cuda.synchronize()
+    return res, _lib.launch_count() - n0
+
+
+@pytest.mark.parametrize("extra,NC,dtype", [(2, 13, torch.bfloat16), ("third", 9, torch.float16),
+                                            (44, 128, torch.bfloat16)])
+def test_balanced_schedule_is_bit_identical(extra, NC, dtype):
+    """Between M and 4M/3 streams (M = SM count) the FF = 256 forward runs its balanced
+    two-launch schedule (two-stream CTAs, pairing swapped between the launches, the state
+    handed over in fp32 through W*_last / b*_last). Every output -- XQW, final states,
+    checkpoints and memo states split mid-group, stored pre-activations -- equals the
+    one-CTA-per-stream launch bit for bit, and sampled streams match the oracle."""
+    import _lib
+
+    M = torch.cuda.get_device_properties(0).multi_processor_count
+    S_ = M + (M // 3 if extra == "third" else extra)
+    B, NH = (2, S_ // 2) if S_ % 2 == 0 else (1, S_)
+    CS, F, FF, ckpt, memo = 16, 64, 256, 4, 3
+    d, _ = make(B, NH, NC, CS, F, FF, dtype, seed=S_ + NC)
+    try:
+        _lib.set_forward_schedule(False)
+        plain, n_plain = _forward_all(d, ckpt, memo)
+    finally:
+        _lib.set_forward_schedule(True)
+    bal, n_bal = _forward_all(d, ckpt, memo)
+    assert (n_plain, n_bal) == (1, 2)
+    out_p, *groups_p = plain
+    out_b, *groups_b = bal
+    assert torch.equal(out_p, out_b)
+    for gp, gb in zip(groups_p, groups_b):
+        for i, (a, b) in enumerate(zip(gp, gb)):
+            assert torch.equal(a, b), i
+    od = oracle_inputs(d)
+    for b, hh in ((0, 0), (B - 1, NH - 1)):
+        sub = {k: (v[b:b + 1, hh:hh + 1] if k not in ("ln_w", "ln_b") else v[hh:hh + 1]) for k, v in od.items()}
+        r = O.mlp_scan(*(sub[k] for k in NAMES), ckpt, memo)
+        assert_close(f"XQW[{b},{hh}]", out_b[b:b + 1, hh:hh + 1], r["XQW"], 2e-2)
+        init = sub["W1"]
+        assert_close(f"W1_last[{b},{hh}]", bal[1][0][b:b + 1, hh:hh + 1].double().cpu() - init,
+                     r["W1_last"] - init, 2e-2)
+
+
+def test_forward_schedule_switch_rejects_bad_ratio():
+    import _lib
+
+    with pytest.raises(RuntimeError, match="ratio"):
+        _lib.set_forward_schedule(True, 500)
+    _lib.set_forward_schedule(True, 0)

@@ -61,6 +61,8 @@ _SIGNATURES = {
     ),
     "ttt_device_status": ([_P], _I),
     "ttt_test_hold_first_stage": ([_I, ctypes.c_ulonglong], _I),
+    "ttt_kernel_launches": ([], ctypes.c_ulonglong),
+    "ttt_set_forward_schedule": ([_I, _I], _I),
     "ttt_memo_mix_scratch_bytes": ([_I] * 5, _Z),
     "ttt_memo_mix_fwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P, _P, _Z, _P], _I),
     "ttt_memo_mix_bwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P] * 4 + [_P, _Z, _I, _P], _I),
@@ -97,23 +99,15 @@ def exported_symbols():
     return list(_SIGNATURES)
 
 
-# Kernels one successful call enqueues (1 unless listed); the status calls launch none.
-_KERNELS_PER_CALL = {"ttt_memo_mix_fwd": 2, "ttt_memo_mix_bwd": 3, "ttt_device_status": 0,
-                     "ttt_test_hold_first_stage": 0}
-_launches = 0
-
-
 def launch_count():
-    """Kernels this process has enqueued through the library (for benchmarks)."""
-    return _launches
+    """Kernels this process has enqueued through the library (ttt_kernel_launches)."""
+    return int(lib.ttt_kernel_launches())
 
 
 def check(rc, name):
-    global _launches
     if rc != 0:
         msg = lib.ttt_last_error().decode(errors="replace")
         raise RuntimeError(f"{name} failed (status {rc}): {msg}")
-    _launches += _KERNELS_PER_CALL.get(name, 1)
 
 
 def device_status():
@@ -126,6 +120,12 @@ def device_status():
 def hold_first_stage(enable, wait_limit_ns=0):
     """Test switch of the bounded waits (ttt_test_hold_first_stage in include/ttt_b200.h)."""
     check(lib.ttt_test_hold_first_stage(int(bool(enable)), int(wait_limit_ns)), "ttt_test_hold_first_stage")
+
+
+def set_forward_schedule(balanced, paired_ratio_milli=0):
+    """Schedule switch of the tensor-core MLP forward (ttt_set_forward_schedule in
+    include/ttt_b200.h): balanced two-launch schedule on (default) or off."""
+    check(lib.ttt_set_forward_schedule(int(bool(balanced)), int(paired_ratio_milli)), "ttt_set_forward_schedule")
 
 
 def dtype_code(t):

@@ -90,7 +90,29 @@ static std::atomic<unsigned long long> g_test_wait_ns{kWaitLimitNs};
 bool test_hold_first_stage() { return g_test_hold.load(std::memory_order_relaxed) != 0; }
 unsigned long long test_wait_limit_ns() { return g_test_wait_ns.load(std::memory_order_relaxed); }
 
+// Measured on B200 for the FF = 256 forward's two-stream CTAs: about 6.25 us per mini-batch
+// for an engine whose CTA runs two streams, 4.17 us for one running alone (best split
+// measured between 1.45 and 1.6).
+constexpr int kPairedRatioMilli = 1500;
+static std::atomic<int> g_fwd_balanced{1};
+static std::atomic<int> g_fwd_ratio{kPairedRatioMilli};
+
+bool forward_schedule_balanced() { return g_fwd_balanced.load(std::memory_order_relaxed) != 0; }
+int forward_paired_ratio_milli() { return g_fwd_ratio.load(std::memory_order_relaxed); }
+
 }  // namespace ttt
+
+extern "C" unsigned long long ttt_kernel_launches(void) {
+  return ttt::launch_counter().load(std::memory_order_relaxed);
+}
+
+extern "C" int ttt_set_forward_schedule(int balanced, int paired_ratio_milli) {
+  TTT_REQUIRE(paired_ratio_milli == 0 || (paired_ratio_milli >= 1000 && paired_ratio_milli <= 4000), TTT_ERR_SHAPE,
+              "ttt_set_forward_schedule: paired / alone ratio %d (x1000) outside [1000, 4000]", paired_ratio_milli);
+  ttt::g_fwd_ratio.store(paired_ratio_milli ? paired_ratio_milli : ttt::kPairedRatioMilli);
+  ttt::g_fwd_balanced.store(balanced ? 1 : 0);
+  return ttt::ok();
+}
 
 extern "C" int ttt_test_hold_first_stage(int enable, unsigned long long wait_limit_ns) {
   TTT_REQUIRE(wait_limit_ns <= ttt::kWaitLimitNs, TTT_ERR_SHAPE,

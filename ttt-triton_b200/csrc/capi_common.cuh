@@ -6,6 +6,8 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
+
 #include "../../include/ttt_b200.h"
 
 namespace ttt {
@@ -48,9 +50,17 @@ inline int prepare_smem(K kernel, size_t smem_bytes, const char* name) {
   return TTT_OK;
 }
 
+// Kernels the library has enqueued in this process (ttt_kernel_launches()).
+inline std::atomic<unsigned long long>& launch_counter() {
+  static std::atomic<unsigned long long> n{0};
+  return n;
+}
+
+// After each kernel launch: reports a failed launch, counts a successful one.
 inline int check_launch(const char* name) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(TTT_ERR_CUDA, "%s: launch failed: %s", name, cudaGetErrorString(e));
+  launch_counter().fetch_add(1, std::memory_order_relaxed);
   return ok();
 }
 

@@ -91,6 +91,10 @@ struct MlpFwdParams {
   unsigned int* err;  // device error word (set by the entry point for kernels with bounded waits)
   unsigned long long wait_ns;  // limit of each bounded wait (tensor-core path)
   int hold_stage0;             // wait-expiry test: the first stage's copies are never issued
+  // Balanced two-launch schedule of the tensor-core forward (mlp_fwd_fast): 0 = one CTA per
+  // stream over the whole sequence; 1 / 2 = its first / second launch, with sched_D SMs running
+  // two streams and the paired streams of launch 1 advancing sched_kp mini-batches.
+  int sched, sched_D, sched_kp;
 };
 
 struct MlpBwdParams {

@@ -103,4 +103,10 @@ int device_error_word(unsigned int** out, const char* who);
 bool test_hold_first_stage();
 unsigned long long test_wait_limit_ns();
 
+// Forward schedule switch (ttt_set_forward_schedule): whether the tensor-core MLP forward may
+// use its balanced two-launch schedule, and the paired / alone mini-batch time ratio (x1000)
+// it splits the sequence by.
+bool forward_schedule_balanced();
+int forward_paired_ratio_milli();
+
 }  // namespace ttt

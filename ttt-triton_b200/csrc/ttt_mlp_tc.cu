@@ -39,19 +39,39 @@ namespace mlp_tc {
 #ifdef TTT_PHASE_STAMPS
 constexpr int kStampN = 64, kStampCTAs = 4096, kStamps = 10;
 __device__ unsigned long long g_phase_stamps[kStampCTAs][kStamps];
+// Steady-state rate of every engine: %globaltimer at the loop top of mini-batches n0 + 4 and
+// n1 - 4, the mini-batches between them and the SM id, per launch of the balanced schedule
+// (index 0: one-engine launch or launch 1, 1: launch 2), row blockIdx.x * ENG + eng.
+__device__ unsigned long long g_rate_stamps[2][kStampCTAs][4];
+#define TTT_RATE_STAMP()                                                                              \
+  do {                                                                                                \
+    if (tid == 0 && n1 - n0 > 8 && (n == n0 + 4 || n == n1 - 4) && blockIdx.x * ENG + eng < kStampCTAs) { \
+      unsigned long long* r_ = g_rate_stamps[p.sched == 2][blockIdx.x * ENG + eng];                  \
+      r_[n == n0 + 4 ? 0 : 1] = global_ns();                                                          \
+      if (n == n0 + 4) {                                                                              \
+        unsigned sm_;                                                                                 \
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(sm_));                                            \
+        r_[2] = n1 - n0 - 8;                                                                          \
+        r_[3] = sm_;                                                                                  \
+      }                                                                                               \
+    }                                                                                                 \
+  } while (0)
 #define TTT_STAMP(k)                                                                                  \
   do {                                                                                                \
-    if (tid == 0 && n == kStampN && blockIdx.x < kStampCTAs) g_phase_stamps[blockIdx.x][k] = global_ns(); \
+    if (tid == 0 && eng == 0 && n == kStampN && blockIdx.x < kStampCTAs) g_phase_stamps[blockIdx.x][k] = global_ns(); \
   } while (0)
 #define TTT_STAMP_SM()                                                                                \
   do {                                                                                                \
     unsigned sm_;                                                                                     \
     asm volatile("mov.u32 %0, %%smid;" : "=r"(sm_));                                                \
-    if (tid == 0 && n == kStampN && blockIdx.x < kStampCTAs) g_phase_stamps[blockIdx.x][9] = sm_;      \
+    if (tid == 0 && eng == 0 && n == kStampN && blockIdx.x < kStampCTAs) g_phase_stamps[blockIdx.x][9] = sm_; \
   } while (0)
 #else
 #define TTT_STAMP(k) \
   do {               \
+  } while (0)
+#define TTT_RATE_STAMP() \
+  do {                   \
   } while (0)
 #define TTT_STAMP_SM() \
   do {                 \
@@ -80,7 +100,8 @@ struct Fwd {
   static constexpr int OFF_B1 = OFF_P + ETA;                 // fp32 [FFW]
   static constexpr int OFF_B2 = OFF_B1 + FFW * 4;            // fp32 [2][F] (ping-pong)
   static constexpr int OFF_LN = OFF_B2 + 2 * F * 4;          // fp32 [2][F]: this head's LayerNorm gamma, beta
-  static constexpr int SMEM = OFF_LN + 2 * F * 4 + 1024;     // + slack to align the base to 1024 bytes
+  static constexpr int SPAN = 1024 * ((OFF_LN + 2 * F * 4 + 1023) / 1024);  // one stream's region
+  static constexpr int SMEM = SPAN + 1024;                   // + slack to align the base to 1024 bytes
   // W1^T and W2^T slices: 128 columns per warp in its lane quadrant, two column blocks for 8 warps
   static constexpr uint32_t TMEM_COLS = NW > 4 ? 256 : 128;
   // CTAs per SM: two of 8 warps (registers), four of 2 warps (TMEM: 4 x 128 columns). The
@@ -88,6 +109,42 @@ struct Fwd {
   static constexpr int CTAS_PER_SM = NW > 4 ? 2 : 4;
   static constexpr int SMEM_LAUNCH = NW > 4 ? SMEM : (SMEM > 56 * 1024 ? SMEM : 56 * 1024);
 };
+
+// The balanced schedule (sched 1, 2) for S streams on M SMs, M < S <= 4M/3: D = S - M SMs must
+// hold two streams at any time. A two-stream CTA (two engines of NW warps, one CTA per SM)
+// makes that pairing explicit, and two launches swap it:
+//   launch 1: CTA c < D runs streams 2c, 2c+1 (set X) for mini-batches [0, kp); CTA c >= D
+//             runs stream 2D + c - D (set Y) alone for [0, NC - kp);
+//   launch 2: CTA c < D runs the first 2D streams of Y paired, [NC - kp, NC); CTAs D..3D-1
+//             finish X alone, [kp, NC); the rest finish Y alone.
+// With kp = NC / (1 + r), r the paired / alone time ratio of a mini-batch, both launches take
+// kp * r alone-mini-batch times, so no SM holds two streams for the whole sequence. The state
+// crosses the launch boundary exactly (fp32 in W*_last / b*_last). Returns false for an idle
+// engine.
+__device__ __forceinline__ bool fwd_segment(const MlpFwdParams& p, int c, int eng, long long* s, int* n0, int* n1) {
+  const int D = p.sched_D, kp = p.sched_kp, ka = p.NC - kp;
+  if (c < D) {  // two streams
+    *s = p.sched == 1 ? 2 * c + eng : 2 * D + 2 * c + eng;
+    *n0 = p.sched == 1 ? 0 : ka;
+    *n1 = p.sched == 1 ? kp : p.NC;
+    return true;
+  }
+  if (eng != 0) return false;
+  if (p.sched == 1) {
+    *s = 2 * D + (c - D);
+    *n0 = 0;
+    *n1 = ka;
+  } else if (c < 3 * D) {
+    *s = c - D;
+    *n0 = kp;
+    *n1 = p.NC;
+  } else {
+    *s = 4 * D + (c - 3 * D);
+    *n0 = ka;
+    *n1 = p.NC;
+  }
+  return true;
+}
 
 // One thread: TMA copies of mini-batch n's XQ, XK, XV tiles and eta tile into stage `st`,
 // completing on mbarrier `bar`.
@@ -188,25 +245,37 @@ __device__ __forceinline__ void pack_row(uint8_t* dst, const float* v, float sca
   }
 }
 
-template <typename T, int NW>
-__global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
-    mlp_fwd_tc_kernel(MlpFwdParams p, const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_v) {
+// CTA barrier of one engine: the whole CTA when it runs one stream, else the engine's own
+// named barrier (ids 1, 2) over its 32 * NW threads.
+template <int ENG, int NTHREADS>
+__device__ __forceinline__ void engine_sync(int eng) {
+  if constexpr (ENG == 1)
+    __syncthreads();
+  else
+    named_barrier(1 + eng, NTHREADS);
+}
+
+// One engine (NW warps) runs stream s over mini-batches [n0, n1): the state enters from
+// W*_init / b*_init (n0 == 0) or from W*_last / b*_last, where it also leaves.
+template <typename T, int NW, int ENG>
+__device__ __forceinline__ void fwd_stream(const MlpFwdParams& p, const CUtensorMap* tm_q, const CUtensorMap* tm_k,
+                                           const CUtensorMap* tm_v, uint8_t* smem, uint64_t* full_bar, int& abort_sh,
+                                           uint32_t tmem_base, int eng, int tid, long long s, int n0, int n1) {
   using H = Half2<T>;
   using L = Fwd<NW>;
   constexpr int NTHREADS = L::NTHREADS, FFW = L::FFW, kCopyThread = L::kCopyThread;
   constexpr int OFF_G = L::OFF_G, OFF_EG = L::OFF_EG, OFF_P = L::OFF_P, OFF_B1 = L::OFF_B1, OFF_B2 = L::OFF_B2;
-  constexpr uint32_t TMEM_COLS = L::TMEM_COLS;
   constexpr int LPT = NW > 4 ? 16 : 8, FPL = F / LPT;  // row phases: lanes per token, features per lane
   constexpr int RTPP = NTHREADS / LPT;                // tokens per pass of the row phases
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  __shared__ uint32_t tmem_base_sh;
-  __shared__ __align__(8) uint64_t full_bar[NSTAGE];  // stage n % NSTAGE landed
-  __shared__ int abort_sh;                            // a stage never landed: stop waiting
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  if constexpr (ENG == 1) {  // whole sequence: bounds straight from the launch parameters
+    s = blockIdx.x;
+    n0 = 0;
+    n1 = p.NC;
+  }
+  // (one engine) the warp index as a uniform value as well: without it this kernel spills
+  const int warp = ENG == 1 ? (int)__reduce_max_sync(0xffffffffu, (unsigned)tid >> 5) : tid >> 5;
+  const int lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int mi = lane >> 3, r8 = lane & 7;
-  const long long s = blockIdx.x;
   const int h = (int)(s % p.NH);
   const int rtk0 = tid / LPT, rq = tid % LPT;  // row phases: token, feature group
   const int fb = 32 * warp;
@@ -215,39 +284,32 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
   float* b1s = reinterpret_cast<float*>(smem + OFF_B1);
   float* b2s = reinterpret_cast<float*>(smem + OFF_B2);
 
-  // fp32 state slices live in TMEM: warp w uses lanes 32*(w%4).. and columns
-  // [128*(w/4), +64) for W1^T, [+64, +128) for W2^T.
-  if (warp == 0) {
-    tmem_alloc(&tmem_base_sh, TMEM_COLS);
-    tmem_relinquish();
-  }
-  if (tid == 32) {
-    for (int i = 0; i < NSTAGE; ++i) mbar_init(smem_u32(&full_bar[i]), 1);
-    abort_sh = 0;
-    fence_mbar_init();
-  }
-  tmem_fence_before();
-  __syncthreads();
-  tmem_fence_after();
-  int last_issued = -1;  // (copy thread) last mini-batch whose stage copies were issued
+  int last_issued = -1;  // (copy thread) last stage index (mini-batch - n0) whose copies were issued
   if (tid == kCopyThread)
-    for (int i = 0; i < NSTAGE - 1 && i < p.NC; ++i) {
+    for (int i = 0; i < NSTAGE - 1 && n0 + i < n1; ++i) {
       // (wait-expiry test) stage 0 never issued: nothing is in flight for its barrier
       if (!(p.hold_stage0 && i == 0))
-        issue_stage(smem_u32(smem + i * STAGE), smem_u32(&full_bar[i]), p, &tm_q, &tm_k, &tm_v, s, i);
+        issue_stage(smem_u32(smem + i * STAGE), smem_u32(&full_bar[i]), p, tm_q, tm_k, tm_v, s, n0 + i);
       last_issued = i;
     }
-  const uint32_t tS1 = tmem_lane_addr(tmem_base_sh, warp, 128 * (warp >> 2));
+  // fp32 state slices live in TMEM: warp w uses lanes 32*(w%4).. and columns
+  // [128*(w/4), +64) of its engine's 256 for W1^T, [+64, +128) for W2^T.
+  const uint32_t tS1 = tmem_lane_addr(tmem_base, warp, L::TMEM_COLS * eng + 128 * (warp >> 2));
   const uint32_t tS2 = tS1 + 64;
+  const bool first = n0 == 0;
   {
     float S1[2][8][4], S2[4][4][4];
-    w1_io<2, FFW>(S1, const_cast<float*>(p.W1_init + s * F * FFW), fb, g, t, false);
-    w2_io(S2, const_cast<float*>(p.W2_init + s * FFW * F), fb, g, t, false);
+    w1_io<2, FFW>(S1, const_cast<float*>((first ? p.W1_init : p.W1_last) + s * F * FFW), fb, g, t, false);
+    w2_io(S2, const_cast<float*>((first ? p.W2_init : p.W2_last) + s * FFW * F), fb, g, t, false);
     slice_st(tS1, &S1[0][0][0]);
     slice_st(tS2, &S2[0][0][0]);
   }
-  for (int i = tid; i < FFW; i += NTHREADS) b1s[i] = p.b1_init[s * FFW + i];
-  for (int i = tid; i < F; i += NTHREADS) b2s[i] = p.b2_init[s * F + i];
+  {
+    const float* b1i = (first ? p.b1_init : p.b1_last) + s * FFW;
+    const float* b2i = (first ? p.b2_init : p.b2_last) + s * F;
+    for (int i = tid; i < FFW; i += NTHREADS) b1s[i] = b1i[i];
+    for (int i = tid; i < F; i += NTHREADS) b2s[i] = b2i[i];
+  }
   // the head's LayerNorm parameters, read by the row phases from shared memory (8 per lane)
   float* lns = reinterpret_cast<float*>(smem + L::OFF_LN);
   for (int i = tid; i < F; i += NTHREADS) {
@@ -257,28 +319,31 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
   const uint32_t ones = H::pack(1.f, 1.f);
   const uint32_t a_ones[4] = {ones, ones, ones, ones};
 
-  int ck_left = 0, memo_left = 0;  // mini-batches until the next checkpoint / memo state
-  for (int n = 0; n < p.NC; ++n) {
-    // The copy thread waits for stage n; the CTA barrier then publishes it to every warp and
-    // tells the copy thread that mini-batch n-1 is done, so its stage may be refilled.
+  // mini-batches until the next checkpoint / memo state (both taken where n is a multiple)
+  int ck_left = n0 ? (p.ckpt - n0 % p.ckpt) % p.ckpt : 0, memo_left = n0 ? (p.memo - n0 % p.memo) % p.memo : 0;
+  for (int n = n0; n < n1; ++n) {
+    const int i = n - n0;  // stage index: stage i % NSTAGE, its barrier's (i / NSTAGE)-th phase
+    // The copy thread waits for stage i; the engine barrier then publishes it to every warp
+    // and tells the copy thread that mini-batch n-1 is done, so its stage may be refilled.
     if (tid == kCopyThread && !abort_sh &&
-        !mbar_wait(smem_u32(&full_bar[n % NSTAGE]), (uint32_t)((n / NSTAGE) & 1), p.err, p.wait_ns))
+        !mbar_wait(smem_u32(&full_bar[i % NSTAGE]), (uint32_t)((i / NSTAGE) & 1), p.err, p.wait_ns))
       abort_sh = 1;  // results of this stream are void; the error word reports it
     TTT_STAMP(0);
-    __syncthreads();
+    engine_sync<ENG, NTHREADS>(eng);
     TTT_STAMP(1);
+    TTT_RATE_STAMP();
     {
-      const int nn = n + NSTAGE - 1;
-      if (tid == kCopyThread && nn < p.NC && !abort_sh) {
-        issue_stage(smem_u32(smem + (nn % NSTAGE) * STAGE), smem_u32(&full_bar[nn % NSTAGE]), p, &tm_q, &tm_k, &tm_v, s,
-                    nn);
-        last_issued = nn;
+      const int ii = i + NSTAGE - 1;
+      if (tid == kCopyThread && n0 + ii < n1 && !abort_sh) {
+        issue_stage(smem_u32(smem + (ii % NSTAGE) * STAGE), smem_u32(&full_bar[ii % NSTAGE]), p, tm_q, tm_k, tm_v, s,
+                    n0 + ii);
+        last_issued = ii;
       }
     }
-    const uint8_t* st = smem + (n % NSTAGE) * STAGE;
+    const uint8_t* st = smem + (i % NSTAGE) * STAGE;
     const uint32_t sb = smem_u32(st);
-    const float* b2_old = b2s + (n & 1) * F;
-    float* b2_new = b2s + ((n + 1) & 1) * F;
+    const float* b2_old = b2s + (i & 1) * F;
+    float* b2_new = b2s + ((i + 1) & 1) * F;
 
     if (p.W1_ckpt && ck_left == 0) {  // state at the start of the checkpoint group
       const long long k = s * p.K + n / p.ckpt;
@@ -378,7 +443,7 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
       }
     }
     TTT_STAMP(2);
-    __syncthreads();
+    engine_sync<ENG, NTHREADS>(eng);
     TTT_STAMP(3);
 
     // ---------------- C: Z2 = sum + b2, G2 = ln_fused_l2_bwd(Z2, XV - XK)
@@ -422,7 +487,7 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
       pack_row<T, FPL>(smem + OFF_EG + xo, G, -e);
     }
     TTT_STAMP(4);
-    __syncthreads();
+    engine_sync<ENG, NTHREADS>(eng);
     TTT_STAMP(5);
 
     // ---------------- D
@@ -591,7 +656,7 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
       }
     }
     TTT_STAMP(6);
-    __syncthreads();
+    engine_sync<ENG, NTHREADS>(eng);
     TTT_STAMP(7);
 
     // ---------------- E: XQW = XQ + LN(sum_w Z2bar_w + b2_old)
@@ -634,7 +699,7 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
     }
     --memo_left;
   }
-  __syncthreads();
+  engine_sync<ENG, NTHREADS>(eng);
   {
     float S1[2][8][4], S2[4][4][4];
     slice_ld(tS1, &S1[0][0][0]);
@@ -648,14 +713,54 @@ __global__ void __launch_bounds__(32 * NW, Fwd<NW>::CTAS_PER_SM)
     for (int m = last_issued - NSTAGE + 1; m <= last_issued; ++m)
       if (m >= 0 && !(p.hold_stage0 && m == 0))  // full 2 s limit: these copies were issued
         mbar_wait(smem_u32(&full_bar[m % NSTAGE]), (uint32_t)((m / NSTAGE) & 1), nullptr);
-  const float* b2_fin = b2s + (p.NC & 1) * F;
+  const float* b2_fin = b2s + ((n1 - n0) & 1) * F;
   for (int i = tid; i < FFW; i += NTHREADS) p.b1_last[s * FFW + i] = b1s[i];
   for (int i = tid; i < F; i += NTHREADS) p.b2_last[s * F + i] = b2_fin[i];
+}
+
+// ENG engines of NW warps per CTA: ENG = 1 is one CTA per stream over the whole sequence
+// (grid B * NH); ENG = 2 is one two-stream CTA per SM for the balanced schedule (fwd_segment,
+// sched 1 or 2).
+template <typename T, int NW, int ENG>
+__global__ void __launch_bounds__(32 * NW * ENG, ENG == 1 ? Fwd<NW>::CTAS_PER_SM : 1)
+    mlp_fwd_tc_kernel(MlpFwdParams p, const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v) {
+  using L = Fwd<NW>;
+  constexpr uint32_t TMEM_COLS = L::TMEM_COLS * ENG;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ __align__(8) uint64_t full_bar[ENG][NSTAGE];  // engine e: stage i % NSTAGE landed
+  __shared__ int abort_sh[ENG];                            // a stage never landed: stop waiting
+  // the engine index through redux.sync: provably warp-uniform, so the compiler keeps it and
+  // what derives from it (shared-memory base, stream, mini-batch bounds) in uniform registers
+  const int eng = ENG == 1 ? 0 : (int)__reduce_max_sync(0xffffffffu, threadIdx.x / L::NTHREADS);
+  const int tid = ENG == 1 ? (int)threadIdx.x : (int)(threadIdx.x & (L::NTHREADS - 1));
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u) + eng * L::SPAN;
+  long long s = blockIdx.x;
+  int n0 = 0, n1 = p.NC;
+  bool active = true;
+  if constexpr (ENG == 2) active = fwd_segment(p, (int)blockIdx.x, eng, &s, &n0, &n1);
+
+  if (threadIdx.x < 32) {
+    tmem_alloc(&tmem_base_sh, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (tid == 32) {
+    for (int i = 0; i < NSTAGE; ++i) mbar_init(smem_u32(&full_bar[eng][i]), 1);
+    abort_sh[eng] = 0;
+    fence_mbar_init();
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  if (active)
+    fwd_stream<T, NW, ENG>(p, &tm_q, &tm_k, &tm_v, smem, full_bar[eng], abort_sh[eng], tmem_base_sh, eng, tid, s, n0,
+                           n1);
   // every warp's TMEM accesses are complete (slice_ld / slice_st wait); free the columns
   tmem_fence_before();
   __syncthreads();
   tmem_fence_after();
-  if (warp == 0) tmem_dealloc(tmem_base_sh, TMEM_COLS);
+  if (threadIdx.x < 32) tmem_dealloc(tmem_base_sh, TMEM_COLS);
 }
 
 }  // namespace mlp_tc
@@ -666,10 +771,55 @@ template <typename T, int NW>
 static int launch_fwd(const MlpFwdParams& q, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                       cudaStream_t stream) {
   using namespace mlp_tc;
-  int rc = prepare_smem(mlp_fwd_tc_kernel<T, NW>, Fwd<NW>::SMEM_LAUNCH, "ttt_mlp_fwd");
+  int rc = prepare_smem(mlp_fwd_tc_kernel<T, NW, 1>, Fwd<NW>::SMEM_LAUNCH, "ttt_mlp_fwd");
   if (rc) return rc;
-  mlp_fwd_tc_kernel<T, NW><<<q.B * q.NH, Fwd<NW>::NTHREADS, Fwd<NW>::SMEM_LAUNCH, stream>>>(q, tq, tk, tv);
+  mlp_fwd_tc_kernel<T, NW, 1><<<q.B * q.NH, Fwd<NW>::NTHREADS, Fwd<NW>::SMEM_LAUNCH, stream>>>(q, tq, tk, tv);
   return check_launch("ttt_mlp_fwd");
+}
+
+// The balanced schedule's two launches (fwd_segment) on M SMs.
+template <typename T>
+static int launch_fwd_balanced(const MlpFwdParams& q, const CUtensorMap& tq, const CUtensorMap& tk,
+                               const CUtensorMap& tv, int M, int D, int kp, cudaStream_t stream) {
+  using namespace mlp_tc;
+  using L = Fwd<8>;
+  constexpr int kSmem = 2 * L::SPAN + 1024;
+  int rc = prepare_smem(mlp_fwd_tc_kernel<T, 8, 2>, kSmem, "ttt_mlp_fwd");
+  if (rc) return rc;
+  MlpFwdParams a = q;
+  a.sched_D = D;
+  a.sched_kp = kp;
+  for (int phase = 1; phase <= 2; ++phase) {
+    a.sched = phase;
+    mlp_fwd_tc_kernel<T, 8, 2><<<M, 2 * L::NTHREADS, kSmem, stream>>>(a, tq, tk, tv);
+    rc = check_launch("ttt_mlp_fwd");
+    if (rc) return rc;
+  }
+  return TTT_OK;
+}
+
+// SMs of the current device (cached per device).
+static int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+// Whether the balanced schedule applies to S streams of NC mini-batches on M SMs (the FF = 256
+// forward), and its split: D two-stream SMs, kp mini-batches for the streams paired first.
+static bool balanced_split(long long S, int NC, int M, int ratio_milli, int* D, int* kp) {
+  if (M <= 0 || S <= M || 3 * (S - M) > M || NC < 4) return false;  // needs M - D >= 2D
+  *D = (int)(S - M);
+  *kp = (int)((1000LL * NC + (1000 + ratio_milli) / 2) / (1000 + ratio_milli));
+  if (*kp < 1) *kp = 1;
+  if (*kp > NC - 1) *kp = NC - 1;
+  return true;
 }
 
 int mlp_fwd_fast(const MlpFwdParams& p, cudaStream_t stream) {
@@ -691,9 +841,17 @@ int mlp_fwd_fast(const MlpFwdParams& p, cudaStream_t stream) {
   if (rc) return rc;
   q.wait_ns = test_wait_limit_ns();
   q.hold_stage0 = test_hold_first_stage() ? 1 : 0;
-  if (p.FF == 256)
+  q.sched = 0;
+  if (p.FF == 256) {
+    int D = 0, kp = 0;
+    const int M = sm_count();
+    if (forward_schedule_balanced() &&
+        balanced_split((long long)p.B * p.NH, p.NC, M, forward_paired_ratio_milli(), &D, &kp))
+      return dt == DT_BF16 ? launch_fwd_balanced<__nv_bfloat16>(q, tq, tk, tv, M, D, kp, stream)
+                           : launch_fwd_balanced<__half>(q, tq, tk, tv, M, D, kp, stream);
     return dt == DT_BF16 ? launch_fwd<__nv_bfloat16, 8>(q, tq, tk, tv, stream)
                          : launch_fwd<__half, 8>(q, tq, tk, tv, stream);
+  }
   return dt == DT_BF16 ? launch_fwd<__nv_bfloat16, 2>(q, tq, tk, tv, stream)
                        : launch_fwd<__half, 2>(q, tq, tk, tv, stream);
 }
@@ -701,6 +859,17 @@ int mlp_fwd_fast(const MlpFwdParams& p, cudaStream_t stream) {
 }  // namespace ttt
 
 #ifdef TTT_PHASE_STAMPS
+// Copies the engines' steady-state rate stamps: 2 launches x rows x 4 values (start ns, end ns,
+// mini-batches between them, SM id).
+extern "C" int ttt_rate_stamps_read(unsigned long long* out, int rows) {
+  if (rows < 0 || rows > ttt::mlp_tc::kStampCTAs) return TTT_ERR_SHAPE;
+  for (int l = 0; l < 2; ++l)
+    if (cudaMemcpyFromSymbol(out + (size_t)l * rows * 4, ttt::mlp_tc::g_rate_stamps, sizeof(unsigned long long) * 4 * rows,
+                             sizeof(unsigned long long) * 4 * ttt::mlp_tc::kStampCTAs * l) != cudaSuccess)
+      return TTT_ERR_CUDA;
+  return TTT_OK;
+}
+
 // Copies the timeline of the last forward launch: rows x 10 values (9 stamps in ns, SM id).
 extern "C" int ttt_phase_stamps_read(unsigned long long* out, int rows) {
   if (rows < 0 || rows > ttt::mlp_tc::kStampCTAs) return TTT_ERR_SHAPE;
