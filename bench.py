@@ -87,11 +87,12 @@ POST_NORM_EPS = 1e-6  # ttt_layer.py:77
 RESULT_KEY = {"prologue": "hidden", "epilogue": "XQW"}  # the input whose gradient e2e reads back
 CS = 16
 DT = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
-# DRAM bytes (read + write) of one launch of the dominant kernel from an ncu capture of
-# the same workload: (bytes, tokens in that launch, summary file). Scaled to the
-# launch measured here by tokens processed.
+# DRAM bytes (read + write) of one call of the dominant kernel's entry point from an ncu
+# capture of the same workload: (bytes, tokens in that call, summary file). Scaled to the
+# call measured here by tokens processed. The config-1 forward is two launches (the
+# balanced schedule); its bytes are their sum.
 NCU_TRAFFIC = {
-    ("mlp_fwd_c1", "mlp_fwd"): (255.97e6, 16 * 12 * 2048, "profiles/mlp_fwd_tc_config1.md"),
+    ("mlp_fwd_c1", "mlp_fwd"): (270.5e6, 16 * 12 * 2048, "profiles/mlp_fwd_tc_config1.md"),
     ("linear_fwd_c2", "linear_fwd"): (557.3e6, 32 * 8 * 4096, "profiles/linear_fwd_tc_config2.md"),
     ("linear_fwdbwd_c2", "linear_bwd"): (1252.9e6, 32 * 8 * 4096, "profiles/linear_bwd_tc_config2.md"),
     # captured at batch 4 (64 streams); traffic per stream is size-independent, scaled by tokens
