@@ -87,7 +87,10 @@ template <typename T>
 __global__ void __launch_bounds__(NTHREADS, 2) linear_bwd_tc_kernel(LinBwdParams p) {
   using H = Half2<T>;
   extern __shared__ __align__(128) uint8_t smem[];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  // the warp index through redux.sync: provably warp-uniform, so what derives from it stays in
+  // uniform registers (fewer spills at the 128-register bound)
+  const int tid = threadIdx.x, warp = (int)__reduce_max_sync(0xffffffffu, threadIdx.x >> 5), lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
   const int mi = lane >> 3, r8 = lane & 7;
   const long long s = blockIdx.x;
   const int h = (int)(s % p.NH);
