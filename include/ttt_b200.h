@@ -277,6 +277,17 @@ unsigned long long ttt_kernel_launches(void);
  */
 int ttt_set_forward_schedule(int balanced, int paired_ratio_milli);
 
+/*
+ * The plan ttt_mlp_fwd's balanced schedule would follow for `streams` = B * NH streams of NC
+ * mini-batches on `num_sms` SMs (host only, no GPU needed; paired_ratio_milli 0 = the
+ * current setting). *launches = 2 when it applies, 0 when one CTA per stream runs the whole
+ * sequence. For 2, rows[6 k .. 6 k + 5] = (launch 1 or 2, CTA, engine 0 or 1, stream, first
+ * mini-batch, end mini-batch) for every engine that has work; *n_rows = their count
+ * (TTT_ERR_SHAPE if above max_rows). For tests and tuning; no counterpart in the reference.
+ */
+int ttt_mlp_fwd_schedule_plan(int streams, int NC, int num_sms, int paired_ratio_milli, int* launches, int* rows,
+                              int max_rows, int* n_rows);
+
 /* Bytes of scratch ttt_mlp_bwd needs for these sizes. */
 size_t ttt_mlp_bwd_scratch_bytes(int B, int NH, int NC, int CS, int F, int FF, int checkpoint_group_size);
 

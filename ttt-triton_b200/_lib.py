@@ -63,6 +63,7 @@ _SIGNATURES = {
     "ttt_test_hold_first_stage": ([_I, ctypes.c_ulonglong], _I),
     "ttt_kernel_launches": ([], ctypes.c_ulonglong),
     "ttt_set_forward_schedule": ([_I, _I], _I),
+    "ttt_mlp_fwd_schedule_plan": ([_I, _I, _I, _I, _P, _P, _I, _P], _I),
     "ttt_memo_mix_scratch_bytes": ([_I] * 5, _Z),
     "ttt_memo_mix_fwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P, _P, _Z, _P], _I),
     "ttt_memo_mix_bwd": ([_I] * 7 + [_P] * 4 + [_I] + [_P] * 4 + [_P, _P, _I] + [_P] * 4 + [_P, _Z, _I, _P], _I),
@@ -126,6 +127,18 @@ def set_forward_schedule(balanced, paired_ratio_milli=0):
     """Schedule switch of the tensor-core MLP forward (ttt_set_forward_schedule in
     include/ttt_b200.h): balanced two-launch schedule on (default) or off."""
     check(lib.ttt_set_forward_schedule(int(bool(balanced)), int(paired_ratio_milli)), "ttt_set_forward_schedule")
+
+
+def forward_schedule_plan(streams, NC, num_sms, paired_ratio_milli=0):
+    """(launches, rows) of the tensor-core MLP forward's balanced schedule for these sizes
+    (ttt_mlp_fwd_schedule_plan; host only): rows are (launch, CTA, engine, stream, n0, n1)."""
+    launches, n = ctypes.c_int(0), ctypes.c_int(0)
+    cap = 4 * int(num_sms) + 8
+    buf = (ctypes.c_int * (6 * cap))()
+    check(lib.ttt_mlp_fwd_schedule_plan(int(streams), int(NC), int(num_sms), int(paired_ratio_milli),
+                                        ctypes.byref(launches), buf, cap, ctypes.byref(n)),
+          "ttt_mlp_fwd_schedule_plan")
+    return launches.value, [tuple(buf[6 * k:6 * k + 6]) for k in range(n.value)]
 
 
 def dtype_code(t):

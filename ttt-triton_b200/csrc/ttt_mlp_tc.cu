@@ -121,7 +121,8 @@ struct Fwd {
 // kp * r alone-mini-batch times, so no SM holds two streams for the whole sequence. The state
 // crosses the launch boundary exactly (fp32 in W*_last / b*_last). Returns false for an idle
 // engine.
-__device__ __forceinline__ bool fwd_segment(const MlpFwdParams& p, int c, int eng, long long* s, int* n0, int* n1) {
+__host__ __device__ __forceinline__ bool fwd_segment(const MlpFwdParams& p, int c, int eng, long long* s, int* n0,
+                                                     int* n1) {
   const int D = p.sched_D, kp = p.sched_kp, ka = p.NC - kp;
   if (c < D) {  // two streams
     *s = p.sched == 1 ? 2 * c + eng : 2 * D + 2 * c + eng;
@@ -857,6 +858,43 @@ int mlp_fwd_fast(const MlpFwdParams& p, cudaStream_t stream) {
 }
 
 }  // namespace ttt
+
+extern "C" int ttt_mlp_fwd_schedule_plan(int streams, int NC, int num_sms, int paired_ratio_milli, int* launches,
+                                         int* rows, int max_rows, int* n_rows) {
+  using namespace ttt;
+  TTT_REQUIRE(launches && n_rows && (rows || max_rows == 0), TTT_ERR_NULL,
+              "ttt_mlp_fwd_schedule_plan: NULL pointer argument");
+  TTT_REQUIRE(streams > 0 && NC > 0 && num_sms > 0 && max_rows >= 0, TTT_ERR_SHAPE,
+              "ttt_mlp_fwd_schedule_plan: sizes must be positive (got %d, %d, %d)", streams, NC, num_sms);
+  TTT_REQUIRE(paired_ratio_milli == 0 || (paired_ratio_milli >= 1000 && paired_ratio_milli <= 4000), TTT_ERR_SHAPE,
+              "ttt_mlp_fwd_schedule_plan: paired / alone ratio %d (x1000) outside [1000, 4000]", paired_ratio_milli);
+  *launches = 0;
+  *n_rows = 0;
+  MlpFwdParams p{};
+  p.NC = NC;
+  const int ratio = paired_ratio_milli ? paired_ratio_milli : forward_paired_ratio_milli();
+  if (!forward_schedule_balanced() || !balanced_split(streams, NC, num_sms, ratio, &p.sched_D, &p.sched_kp))
+    return ok();
+  *launches = 2;
+  int k = 0;
+  for (int l = 1; l <= 2; ++l) {
+    p.sched = l;
+    for (int c = 0; c < num_sms; ++c)
+      for (int e = 0; e < 2; ++e) {
+        long long st = 0;
+        int n0 = 0, n1 = 0;
+        if (!mlp_tc::fwd_segment(p, c, e, &st, &n0, &n1)) continue;
+        if (k < max_rows) {
+          int* r = rows + 6 * k;
+          r[0] = l; r[1] = c; r[2] = e; r[3] = (int)st; r[4] = n0; r[5] = n1;
+        }
+        ++k;
+      }
+  }
+  *n_rows = k;
+  TTT_REQUIRE(k <= max_rows, TTT_ERR_SHAPE, "ttt_mlp_fwd_schedule_plan: %d rows, room for %d", k, max_rows);
+  return ok();
+}
 
 #ifdef TTT_PHASE_STAMPS
 // Copies the engines' steady-state rate stamps: 2 launches x rows x 4 values (start ns, end ns,
