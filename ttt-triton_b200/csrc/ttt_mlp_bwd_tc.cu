@@ -40,6 +40,34 @@ namespace ttt {
 namespace mlp_tc {
 namespace bwd {
 
+// Per-phase timeline (built only with -DTTT_PHASE_STAMPS): for the walk's step kBStampIt,
+// thread 0 of each CTA records %globaltimer before and after each CTA barrier (11 stamps) and
+// its SM id; ttt_bwd_phase_stamps_read copies them out.
+#ifdef TTT_PHASE_STAMPS
+constexpr int kBStampIt = 64, kBStampCTAs = 4096, kBStamps = 12;
+__device__ unsigned long long g_bwd_stamps[kBStampCTAs][kBStamps];
+__device__ __forceinline__ unsigned long long bstamp_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define TTT_BSTAMP(k)                                                                              \
+  do {                                                                                             \
+    if (threadIdx.x == 0 && it == kBStampIt && blockIdx.x < kBStampCTAs) {                         \
+      g_bwd_stamps[blockIdx.x][k] = bstamp_ns();                                                   \
+      if ((k) == 0) {                                                                              \
+        unsigned sm_;                                                                              \
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(sm_));                                         \
+        g_bwd_stamps[blockIdx.x][11] = sm_;                                                        \
+      }                                                                                            \
+    }                                                                                              \
+  } while (0)
+#else
+#define TTT_BSTAMP(k) \
+  do {                \
+  } while (0)
+#endif
+
 constexpr int NSTAGE = 2;
 constexpr int TILE = C * F * 2;   // one 16 x 64 16-bit tile
 constexpr int ETA = C * C * 2;    // one 16 x 16 16-bit tile
@@ -324,8 +352,10 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
 
   for (int it = 0; it < p.NC; ++it) {
     const int n = p.NC - 1 - it;
+    TTT_BSTAMP(0);
     cp_async_wait<0>();
     __syncthreads();  // stage of mini-batch n landed; every warp is done with mini-batch n+1
+    TTT_BSTAMP(1);
     if (!kAhead && it + 1 < p.NC) load_stage<NW, NTHREADS>(smem + ((it + 1) % NSTAGE) * STAGE, p, s, n - 1, 0);
     cp_async_commit();
     const uint8_t* st = smem + (it % NSTAGE) * STAGE;
@@ -385,8 +415,10 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
         for (int j = 0; j < 4; ++j) dz[j] = (F * gg[j] - s1 - xbn[j] * s2) * (rb * (1.f / F));
         *reinterpret_cast<uint2*>(smem + OFF_DZB + xo) = make_uint2(H::pack(dz[0], dz[1]), H::pack(dz[2], dz[3]));
       }
+      TTT_BSTAMP(2);
       __syncthreads();
     }
+    TTT_BSTAMP(3);
 
     // ---------------- M1 (the NW MMA warps)
     // carried from M1 into M2 in the MMA warps' registers
@@ -816,7 +848,9 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
         r1_g(nx, (n - 1) & 1, (tid - 32 * NW) >> 4, NRT / 16, false);
       }
     }
+    TTT_BSTAMP(4);
     __syncthreads();
+    TTT_BSTAMP(5);
 
     // ---------------- R2: dG2 -> backward of G2 = ln_fused_l2_bwd(Z2, XV - XK); d_eta, dP1
     float DTr[NPASS][4];
@@ -893,7 +927,9 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
       reinterpret_cast<T*>(p.deta)[(s * p.NC + n) * (long long)(C * C) + el] = H::from_float(v);
       DP1[el] = u;
     }
+    TTT_BSTAMP(6);
     __syncthreads();
+    TTT_BSTAMP(7);
 
     // ---------------- M2 (the NW MMA warps)
     if (warp < NW) {
@@ -1052,7 +1088,9 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
       if (warp >= NW && it + 1 < p.NC)  // row-only warps: R1 part 2 of mini-batch n - 1
         r1_dzb(smem + ((it + 1) % NSTAGE) * STAGE, (n - 1) & 1, (tid - 32 * NW) >> 4, NRT / 16);
     }
+    TTT_BSTAMP(8);
     __syncthreads();
+    TTT_BSTAMP(9);
 
     // ---------------- R3: dXQ = dO + sum of partials, dXK = sum of partials - dXV
 #pragma unroll
@@ -1072,6 +1110,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
       *reinterpret_cast<uint2*>((uint8_t*)p.dXQ + o) = make_uint2(H::pack(dq[0], dq[1]), H::pack(dq[2], dq[3]));
       *reinterpret_cast<uint2*>((uint8_t*)p.dXK + o) = make_uint2(H::pack(dk[0], dk[1]), H::pack(dk[2], dk[3]));
     }
+    TTT_BSTAMP(10);
   }
   cp_async_wait<0>();
   __syncthreads();
@@ -1153,3 +1192,14 @@ int mlp_bwd_fast(const MlpBwdParams& p, cudaStream_t stream) {
 }
 
 }  // namespace ttt
+
+#ifdef TTT_PHASE_STAMPS
+// Copies the backward's timeline: rows x 12 values (11 stamps in ns, SM id).
+extern "C" int ttt_bwd_phase_stamps_read(unsigned long long* out, int rows) {
+  using namespace ttt::mlp_tc::bwd;
+  if (rows < 0 || rows > kBStampCTAs) return TTT_ERR_SHAPE;
+  return cudaMemcpyFromSymbol(out, g_bwd_stamps, sizeof(unsigned long long) * kBStamps * rows) == cudaSuccess
+             ? TTT_OK
+             : TTT_ERR_CUDA;
+}
+#endif
