@@ -3,6 +3,11 @@ steady-state time per mini-batch of every stream.
 
     python ttt-triton_b200/build.py --phase-stamps
     python ttt-triton_b200/phase_timeline.py [--batch B] [--plain]
+    python ttt-triton_b200/phase_timeline.py --backward --batch 9
+
+With --backward it times the MLP backward's reverse walk instead (config 3's heads and
+length, FF 256, bf16): the median time of each phase of walk step 64, phases R1 / M1 / R2 /
+M2 / R3 as in ttt_mlp_bwd_tc.cu.
 
 Runs the config-1 forward (B x 12 heads, L 2048, F 64, FF 256, bf16, memo states every 16
 mini-batches) on libttt_b200_stamps.so. That build records, on thread 0 of every stream's
@@ -64,11 +69,55 @@ def rates(n_rows, balanced, M, S_):
             print(f"  {launch}, {label} ({len(sel)} streams): {v:.0f} ns per mini-batch")
 
 
+BWD_PHASES = ("loop top (stage wait + barrier)", "R1", "R1 barrier", "M1", "M1 barrier", "R2", "R2 barrier",
+              "M2", "M2 barrier", "R3")
+
+
+def backward(B, NH, NC):
+    """Per-phase timeline of step 64 of the MLP backward's reverse walk (FF 256, bf16): median
+    over CTAs of each phase (ns), from the stamps of thread 0 of every CTA."""
+    d = S.make_mlp_inputs(B, NH, NC, 16, 64, 256, dtype=torch.bfloat16, device="cuda", seed=0)
+    dO = S.make_upstream((B, NH, NC, 16, 64), device="cuda", seed=1, dtype=torch.bfloat16)
+    _, last, ck, _, zs = _core.mlp_forward(*(d[k] for k in NAMES), 16, None)
+
+    def step():
+        _core.mlp_backward(d["ln_w"], d["ln_b"], ck, d["XQ"], d["XV"], d["XK"], d["eta"], dO, 16, saved=zs,
+                           W1_last=last[0], W2_last=last[2])
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    step()
+    e1.record()
+    torch.cuda.synchronize()
+    read = _lib.lib.ttt_bwd_phase_stamps_read
+    read.argtypes, read.restype = [ctypes.c_void_p, ctypes.c_int], ctypes.c_int
+    n = B * NH
+    buf = (ctypes.c_ulonglong * (12 * n))()
+    if read(buf, n) != 0:
+        raise RuntimeError("reading the timeline failed (is this the --phase-stamps build?)")
+    rows = [[buf[i * 12 + k] for k in range(12)] for i in range(n)]
+    rows = [r for r in rows if r[0] and r[10]]
+    print(f"backward B={B} NH={NH} NC={NC}: {e0.elapsed_time(e1):.3f} ms per launch, {len(rows)} CTAs stamped")
+    for k, name in enumerate(BWD_PHASES):
+        v = [r[k + 1] - r[k] for r in rows if r[k] and r[k + 1]]
+        if v:
+            print(f"  {name:32s} {statistics.median(v):7.0f} ns")
+    print(f"  {'step':32s} {statistics.median(r[10] - r[0] for r in rows):7.0f} ns")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--plain", action="store_true", help="one CTA per stream (balanced schedule off)")
+    ap.add_argument("--backward", action="store_true",
+                    help="the MLP backward instead: config-3 heads and length (NH 16, L 8192) at --batch")
     args = ap.parse_args()
+    if args.backward:
+        backward(args.batch, 16, 512)
+        return
     read = _lib.lib.ttt_phase_stamps_read
     read.argtypes, read.restype = [ctypes.c_void_p, ctypes.c_int], ctypes.c_int
     B, NH = args.batch, 12
