@@ -76,6 +76,14 @@ __device__ __forceinline__ void slice_st(uint32_t a, const float* v) {
   if (NV == 64) tmem_st32(a + 32, v + 32);
   tmem_wait_st();
 }
+// The same store without waiting for it to land: the caller issues tmem_wait_st() before its
+// next tcgen05.ld of these columns (and before the CTA's final barrier), at a point by which
+// the store has long completed, so the store latency leaves the dependency chain.
+template <int NV = 64>
+__device__ __forceinline__ void slice_st_async(uint32_t a, const float* v) {
+  tmem_st32(a, v);
+  if (NV == 64) tmem_st32(a + 32, v + 32);
+}
 
 }  // namespace mlp_tc
 }  // namespace ttt

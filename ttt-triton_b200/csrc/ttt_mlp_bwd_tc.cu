@@ -425,6 +425,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
     uint32_t X2t[2][4], Zbp[4][2], Zbt[2][4];
     float GP[4][4], dX2[4][4], dZ1[4][4];
     if (warp < NW) {
+    tmem_wait_st();  // the previous step's M2 stores of dW1, dW2 (issued without waiting) landed
     const float* Z1s = reinterpret_cast<const float*>(st + OFF_Z1);
     const float* Z1bs = reinterpret_cast<const float*>(st + OFF_Z1B);
     const float eg0 = (float)E[(C - 1) * C + g], eg1 = (float)E[(C - 1) * C + g + 8];
@@ -478,7 +479,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
           mma16816<T>(S2[m][j], a, b);
         }
       }
-      slice_st(tS2, &S2[0][0][0]);
+      slice_st_async(tS2, &S2[0][0][0]);
 #pragma unroll
       for (int kf = 0; kf < 4; ++kf) {
         uint32_t ag[4], ad[4];
@@ -520,7 +521,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
           mma16816<T>(S1[m][2 * np + 1], a, bx + 2);
         }
       }
-      slice_st(tS1, &S1[0][0][0]);
+      slice_st_async(tS1, &S1[0][0][0]);
     }
     // dP2 = -dZ2bar G2^T and A1 = XQ XK^T (whole 16 x 16 in every warp)
     float dP2[2][4], A1[2][4];
@@ -753,6 +754,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
         mma16816<T>(PG[2 * np], aYT, bz);
         mma16816<T>(PG[2 * np + 1], aYT, bz + 2);
       }
+      tmem_wait_st();  // the reversed W2 this step stored (without waiting) earlier in M1
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         float S2h[2][4][4];
@@ -796,7 +798,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
           mma16816<T>(D2[m][j], a2, b2);
         }
       }
-      slice_st(tD2, &D2[0][0][0]);
+      slice_st_async(tD2, &D2[0][0][0]);
     }
     // partial dP1 = -dZ1bar G1^T; partial d_eta = dP2 * (A2_w [+1]) + dP1_w * (A1 + 1); d e
     {
@@ -933,6 +935,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
 
     // ---------------- M2 (the NW MMA warps)
     if (warp < NW) {
+    tmem_wait_st();  // M1's stores of W1, W2, dW2 (issued without waiting) landed
     // dX2 += dZ2 W2_n^T ; dW2^T += dZ2^T X2 ; db2 += 1^T (dZ2bar + dZ2) (warp w: features
     // 8fw..8fw+7 for fw = w, w + NW, ..)
     {
@@ -963,7 +966,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
           mma16816<T>(D2[m][j], a, b);
         }
       }
-      slice_st(tD2, &D2[0][0][0]);
+      slice_st_async(tD2, &D2[0][0][0]);
     }
 #pragma unroll
     for (int fw = warp; fw < F / 8; fw += NW) {
@@ -1071,7 +1074,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
           mma16816<T>(D1[m][2 * np + 1], a2, bk + 2);
         }
       }
-      slice_st(tD1, &D1[0][0][0]);
+      slice_st_async(tD1, &D1[0][0][0]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1118,6 +1121,7 @@ __global__ void __launch_bounds__(Bwd<NW>::NTHREADS, Bwd<NW>::CTAS_PER_SM) mlp_b
   // ---- outputs of the whole walk: dW1, dW2, db1, db2 (fp32), per-stream gamma / beta partials
   if (warp < NW) {
     float D1[2][8][4];
+    tmem_wait_st();
     slice_ld(tD1, &D1[0][0][0]);
     w1_io<2, FFW>(D1, p.dW1 + s * F * FFW, fb, g, t, true);
     float D2[4][4][4];

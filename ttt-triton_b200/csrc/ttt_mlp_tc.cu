@@ -345,6 +345,7 @@ __device__ __forceinline__ void fwd_stream(const MlpFwdParams& p, const CUtensor
     const uint32_t sb = smem_u32(st);
     const float* b2_old = b2s + (i & 1) * F;
     float* b2_new = b2s + ((i + 1) & 1) * F;
+    tmem_wait_st();  // the previous mini-batch's state stores (issued without waiting) have landed
 
     if (p.W1_ckpt && ck_left == 0) {  // state at the start of the checkpoint group
       const long long k = s * p.K + n / p.ckpt;
@@ -642,7 +643,7 @@ __device__ __forceinline__ void fwd_stream(const MlpFwdParams& p, const CUtensor
 #pragma unroll
         for (int j = 0; j < 4; ++j) mma16816<T>(S2[m][j], a, bx2[j]);
       }
-      slice_st(tS2, &S2[0][0][0]);
+      slice_st_async(tS2, &S2[0][0][0]);
     }
 #pragma unroll
     for (int fw = warp; fw < F / 8; fw += NW) {  // b2_new = b2_old + 1^T (-e G2), features 8fw..8fw+7
@@ -690,6 +691,7 @@ __device__ __forceinline__ void fwd_stream(const MlpFwdParams& p, const CUtensor
     if (p.W1_memo && memo_left == 0) {  // state after this mini-batch
       const long long m = s * p.NS + n / p.memo;
       float S1[2][8][4], S2[4][4][4];
+      tmem_wait_st();
       slice_ld(tS1, &S1[0][0][0]);
       w1_io<2, FFW>(S1, p.W1_memo + m * F * FFW, fb, g, t, true);
       slice_ld(tS2, &S2[0][0][0]);
@@ -703,6 +705,7 @@ __device__ __forceinline__ void fwd_stream(const MlpFwdParams& p, const CUtensor
   engine_sync<ENG, NTHREADS>(eng);
   {
     float S1[2][8][4], S2[4][4][4];
+    tmem_wait_st();
     slice_ld(tS1, &S1[0][0][0]);
     w1_io<2, FFW>(S1, p.W1_last + s * F * FFW, fb, g, t, true);
     slice_ld(tS2, &S2[0][0][0]);
