@@ -2,11 +2,13 @@
 // CS = 16, 16-bit activations and an inner width FF = 32 * NW: the benchmark MLP
 // (FF = 256, NW = 8 warps) and the layer's F x F inner MLP (FF = 64, NW = 2).
 //
-// One CTA of NW warps per (batch, head) stream; warp w owns hidden units
-// [32w, 32w + 32). Its slices of the fp32 state, W1^T (32 x 64) and W2^T (64 x 32), stay in
-// mma accumulator fragments for the whole sequence (the accumulator layout of W1^T is the
-// B-operand layout of W1, and of W2^T the B layout of W2); the biases live in shared
-// memory. Per mini-batch (ops/ttt_mlp.py:9-67):
+// One engine of NW warps per (batch, head) stream: a CTA of its own, or (FF = 256, between
+// M and 4M/3 streams on M SMs) one of the two engines of a CTA per SM in the balanced
+// two-launch schedule (fwd_segment). Warp w owns hidden units [32w, 32w + 32). Its slices
+// of the fp32 state, W1^T (32 x 64) and W2^T (64 x 32), live in tensor memory in mma
+// accumulator-fragment order for the whole sequence and are loaded into fragments for each
+// product (the accumulator layout of W1^T is the B-operand layout of W1, and of W2^T the B
+// layout of W2); the biases live in shared memory. Per mini-batch (ops/ttt_mlp.py:9-67):
 //   A (MMA)  Z1 = XK W1 + b1, Z1q = XQ W1 + b1, X2 = gelu(Z1), partial Z2_w = X2_w W2_w;
 //            warps 0-1 form -P1 = -eta * (XQ XK^T + 1)
 //   C (rows) Z2 = sum_w Z2_w + b2, G2 = ln_fused_l2_bwd(Z2, XV - XK) (16 lanes per token,
