@@ -270,7 +270,7 @@ unsigned long long ttt_kernel_launches(void);
  * `balanced` set (the default) it runs as two launches of one two-stream CTA per SM that
  * swap which streams share an SM halfway, splitting the sequence by `paired_ratio_milli`,
  * the time of a mini-batch on an SM shared by two streams over one alone, x1000 (0: the
- * library's measured 1500; values outside [1000, 4000] are refused with TTT_ERR_SHAPE);
+ * library's measured 1550; values outside [1000, 4000] are refused with TTT_ERR_SHAPE);
  * with it clear, one CTA per stream runs the whole sequence. Outputs are bit-identical
  * either way; only the time differs. Process-wide; affects launches enqueued after the
  * call. No counterpart in the reference (its grid is one program per stream).

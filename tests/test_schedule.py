@@ -36,7 +36,7 @@ def _check_plan(S, NC, M, ratio_milli):
         assert len(paired[launch]) == 2 * D
     assert not (paired[1] & paired[2])  # no stream shares an SM in both launches
     # both launches last about kp * r alone-mini-batch times (rounding of kp aside)
-    r = (ratio_milli or 1500) / 1000
+    r = (ratio_milli or 1550) / 1000
     kp = next(n1 for l, c, e, s, n0, n1 in rows if l == 1 and c < D)
     ka = NC - kp
     assert abs(kp * r - ka) <= r + 1
