@@ -154,13 +154,16 @@ constexpr long long kMlpBwdSmemFloats = TTT_BWD_SMEM_CAP / 4;
 // The general backward's fp32 tiles, carved in a fixed order: into shared memory while they
 // fit in `cap` floats, then (from the first that does not, all the rest) into the stream's
 // spill region of the global scratch, which stays L2-resident. Every shape then runs; the
-// mini-batch-16 shapes keep every tile on chip. With null bases this only counts: returns
-// the shared-memory floats used and stores the spill floats.
+// mini-batch-16 shapes keep every tile on chip. Tiles whose lives within a walk step do not
+// overlap share a buffer (noted below); the C x C tiles come last, those read by products
+// first, so at large mini-batches (64) the ones that spill are only read element-wise. With
+// null bases this only counts: returns the shared-memory floats used and stores the spill
+// floats.
 struct BwdTiles {
-  float *b1, *db1, *tmp1, *b2, *db2, *tmp2, *gam, *bet, *dgam, *dbet;
+  float *b1, *db1, *tmp1, *b2, *db2, *tmp2, *gam, *bet, *dgam, *dbet, *mu2, *sd2, *de;
   float *XQ, *XK, *XV, *dO, *Z2, *G2, *Z2b, *dZ2b, *dG2, *dXQ, *dXK, *XdW2, *dZ2, *dT, *T1, *T2;
   float *Z1, *X2, *H, *G1, *Z1b, *X2b, *DX2B, *DX2, *DG1;
-  float *E, *A1, *P1, *A2, *P2, *dP, *dEta, *dA, *mu2, *sd2, *de;
+  float *E, *A1, *P1, *A2, *P2, *dP, *dEta, *dA;
 };
 
 struct Carver {
@@ -188,15 +191,19 @@ __host__ __device__ inline long long carve_bwd(BwdTiles& t, int C, int F, int FF
   t.b1 = c.take(FF); t.db1 = c.take(FF); t.tmp1 = c.take(FF);
   t.b2 = c.take(F); t.db2 = c.take(F); t.tmp2 = c.take(F);
   t.gam = c.take(F); t.bet = c.take(F); t.dgam = c.take(F); t.dbet = c.take(F);
+  t.mu2 = c.take(C); t.sd2 = c.take(C); t.de = c.take(C);
   t.XQ = c.take(CF); t.XK = c.take(CF); t.XV = c.take(CF); t.dO = c.take(CF);
   t.Z2 = c.take(CF); t.G2 = c.take(CF); t.Z2b = c.take(CF); t.dZ2b = c.take(CF);
-  t.dG2 = c.take(CF); t.dXQ = c.take(CF); t.dXK = c.take(CF); t.XdW2 = c.take(CF);
-  t.dZ2 = c.take(CF); t.dT = c.take(CF); t.T1 = c.take(CF); t.T2 = c.take(CF);
+  t.dG2 = c.take(CF); t.dXQ = c.take(CF); t.dXK = c.take(CF); t.XdW2 = c.take(CF); t.T1 = c.take(CF);
+  t.dZ2 = t.Z2b;   // Z2bar (then the read-out x_bar) is dead after the gamma / beta columns
+  t.T2 = t.XdW2;   // X2 dW2_next is dead after the row loop
+  t.dT = t.dZ2b;   // dZ2bar is dead after the dW2 / db2 updates
   t.Z1 = c.take(CFF); t.X2 = c.take(CFF); t.H = c.take(CFF); t.G1 = c.take(CFF); t.Z1b = c.take(CFF);
   t.X2b = c.take(CFF); t.DX2B = c.take(CFF); t.DX2 = c.take(CFF); t.DG1 = c.take(CFF);
-  t.E = c.take(CC); t.A1 = c.take(CC); t.P1 = c.take(CC); t.A2 = c.take(CC);
-  t.P2 = c.take(CC); t.dP = c.take(CC); t.dEta = c.take(CC); t.dA = c.take(CC);
-  t.mu2 = c.take(C); t.sd2 = c.take(C); t.de = c.take(C);
+  t.A2 = c.take(CC); t.P1 = c.take(CC); t.P2 = c.take(CC);  // read by products
+  t.dP = c.take(CC); t.A1 = c.take(CC); t.E = c.take(CC);   // read element-wise only
+  t.dA = t.A2;     // A2 is read, element by element, just before dA is written in its place
+  t.dEta = t.P2;   // P2 is dead after dG2 = -P2^T dZ2bar
   *spill = c.goff;
   return c.off;
 }
@@ -362,8 +369,9 @@ __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
       block_mm<false, true>(DX2, FF, G2, F, dW2, F, C, FF, F, 1.f, 0.f);    // G2 dW2_next^T
       __syncthreads();
       for (int i = threadIdx.x; i < CC; i += blockDim.x) {
+        const float a2 = A2[i];  // dA takes A2's buffer: read it first
+        dEta[i] = dP[i] * (a2 + 1.f);
         dA[i] = dP[i] * E[i];
-        dEta[i] = dP[i] * (A2[i] + 1.f);
       }
       for (int i = threadIdx.x; i < CFF; i += blockDim.x) DX2[i] *= -e[i / FF];
       __syncthreads();
