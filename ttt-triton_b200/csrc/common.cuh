@@ -179,6 +179,75 @@ __device__ __forceinline__ void block_mm(float* C, int ldc, const float* A, int 
   }
 }
 
+// ----------------------------------------------------------------- block matmul (TF32 tensor cores)
+// The same product on mma.sync m16n8k16's TF32 sibling, m16n8k8 (fp32 operands rounded to
+// TF32 -- 10 explicit mantissa bits, fp32 range -- and fp32 accumulation): for kernels whose
+// activations are 16-bit, where the operands carry no more precision than that anyway (the
+// reference's Triton tl.dot also multiplies fp32 operands in TF32). Each warp computes
+// 16 x 16 output tiles (two m16n8 accumulators) in turn; M and N multiples of 16, K of 8.
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32_16808(float* d, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+template <bool TA, bool TB>
+__device__ __forceinline__ void block_mm_tf32(float* C, int ldc, const float* A, int lda, const float* B, int ldb,
+                                              int M, int N, int K, float alpha, float beta) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int tn = N >> 4, tiles = (M >> 4) * tn;
+  // element (m, k) of op(A) and (k, n) of op(B)
+  auto a_at = [&](int m, int k) { return TA ? A[(long long)k * lda + m] : A[(long long)m * lda + k]; };
+  auto b_at = [&](int k, int n) { return TB ? B[(long long)n * ldb + k] : B[(long long)k * ldb + n]; };
+  for (int tile = warp; tile < tiles; tile += nw) {
+    const int m0 = (tile / tn) << 4, n0 = (tile % tn) << 4;
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 2
+    for (int k0 = 0; k0 < K; k0 += 8) {
+      const uint32_t a[4] = {to_tf32(a_at(m0 + g, k0 + t)), to_tf32(a_at(m0 + g + 8, k0 + t)),
+                             to_tf32(a_at(m0 + g, k0 + t + 4)), to_tf32(a_at(m0 + g + 8, k0 + t + 4))};
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t b[2] = {to_tf32(b_at(k0 + t, n0 + 8 * j + g)), to_tf32(b_at(k0 + t + 4, n0 + 8 * j + g))};
+        mma_tf32_16808(acc[j], a, b);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float* c = C + (long long)(m0 + g + 8 * h) * ldc + n0 + 8 * j + 2 * t;
+        const float v0 = acc[j][2 * h], v1 = acc[j][2 * h + 1];
+        if (beta == 0.f) {
+          c[0] = alpha * v0;
+          c[1] = alpha * v1;
+        } else {
+          c[0] = fmaf(alpha, v0, beta * c[0]);
+          c[1] = fmaf(alpha, v1, beta * c[1]);
+        }
+      }
+  }
+}
+
+// block_mm on the TF32 tensor cores when TC and the shape allows it, else on fp32 FMA.
+template <bool TC, bool TA, bool TB>
+__device__ __forceinline__ void block_mm_sel(float* C, int ldc, const float* A, int lda, const float* B, int ldb,
+                                             int M, int N, int K, float alpha, float beta) {
+  if (TC && (M & 15) == 0 && (N & 15) == 0 && (K & 7) == 0)
+    block_mm_tf32<TA, TB>(C, ldc, A, lda, B, ldb, M, N, K, alpha, beta);
+  else
+    block_mm<TA, TB>(C, ldc, A, lda, B, ldb, M, N, K, alpha, beta);
+}
+
 // ----------------------------------------------------------------- warp reductions
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
