@@ -248,6 +248,16 @@ __device__ __forceinline__ void block_mm_sel(float* C, int ldc, const float* A, 
     block_mm<TA, TB>(C, ldc, A, lda, B, ldb, M, N, K, alpha, beta);
 }
 
+// The same as a real call, for the general backward: it runs some fifty products per
+// mini-batch, and inlined they kept its 255 registers busy and spilled; as calls their
+// registers are free again between products (128 registers, no spills; the forward, with
+// fewer products, is faster inlined).
+template <bool TC, bool TA, bool TB>
+__device__ __noinline__ void block_mm_call(float* C, int ldc, const float* A, int lda, const float* B, int ldb,
+                                           int M, int N, int K, float alpha, float beta) {
+  block_mm_sel<TC, TA, TB>(C, ldc, A, lda, B, ldb, M, N, K, alpha, beta);
+}
+
 // ----------------------------------------------------------------- warp reductions
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

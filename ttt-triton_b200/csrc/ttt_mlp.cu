@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
       load_tile(E + (C - 1) * C, p.eta, eb + (C - 1) * C, C, p.dt_eta);
       __syncthreads();
       const float* e = E + (C - 1) * C;
-      block_mm_sel<TC, false, false>(Z1, FF, XK, F, W1, FF, C, FF, F, 1.f, 0.f);
+      block_mm_call<TC, false, false>(Z1, FF, XK, F, W1, FF, C, FF, F, 1.f, 0.f);
       __syncthreads();
       for (int i = threadIdx.x; i < CFF; i += blockDim.x) {
         const float z = Z1[i] + b1[i % FF];
@@ -288,17 +288,17 @@ __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
       }
       for (int i = threadIdx.x; i < CF; i += blockDim.x) T1[i] = e[i / F] * XK[i];
       __syncthreads();
-      block_mm_sel<TC, false, false>(Z2, F, X2, FF, W2, F, C, F, FF, 1.f, 0.f);
+      block_mm_call<TC, false, false>(Z2, F, X2, FF, W2, F, C, F, FF, 1.f, 0.f);
       __syncthreads();
       ln_fused_rows(Z2, G2, b2, XV, XK, gam, bet, C, F, nullptr, nullptr);
       __syncthreads();
       for (int i = threadIdx.x; i < CF; i += blockDim.x) z2s[i] = Z2[i];
-      block_mm_sel<TC, false, true>(H, FF, G2, F, W2, F, C, FF, F, 1.f, 0.f);
+      block_mm_call<TC, false, true>(H, FF, G2, F, W2, F, C, FF, F, 1.f, 0.f);
       __syncthreads();
       for (int i = threadIdx.x; i < CFF; i += blockDim.x) G1[i] = H[i] * gelu_bwd_ref(Z1[i]);
       __syncthreads();
-      block_mm_sel<TC, true, false>(W1, FF, T1, F, G1, FF, F, FF, C, -1.f, 1.f);
-      block_mm_sel<TC, true, false>(W2, F, DX2, FF, G2, F, FF, F, C, -1.f, 1.f);
+      block_mm_call<TC, true, false>(W1, FF, T1, F, G1, FF, F, FF, C, -1.f, 1.f);
+      block_mm_call<TC, true, false>(W2, F, DX2, FF, G2, F, FF, F, C, -1.f, 1.f);
       weighted_colsum(tmp1, e, G1, C, FF);
       weighted_colsum(tmp2, e, G2, C, F);
       __syncthreads();
@@ -329,24 +329,24 @@ __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
       }
       ln_fused_rows(Z2, G2, nullptr, XV, XK, gam, bet, C, F, mu2, sd2);
       for (int i = threadIdx.x; i < CF; i += blockDim.x) T1[i] = e[i / F] * XK[i];
-      block_mm_sel<TC, false, true>(A1, C, XQ, F, XK, F, C, C, F, 1.f, 0.f);
+      block_mm_call<TC, false, true>(A1, C, XQ, F, XK, F, C, C, F, 1.f, 0.f);
       __syncthreads();
-      block_mm_sel<TC, true, false>(W2, F, DX2, FF, G2, F, FF, F, C, 1.f, 1.f);  // W2 += (e*X2)^T G2
+      block_mm_call<TC, true, false>(W2, F, DX2, FF, G2, F, FF, F, C, 1.f, 1.f);  // W2 += (e*X2)^T G2
       weighted_colsum(tmp2, e, G2, C, F);
       for (int i = threadIdx.x; i < CC; i += blockDim.x) P1[i] = E[i] * (A1[i] + 1.f);
       __syncthreads();
       for (int j = threadIdx.x; j < F; j += blockDim.x) b2[j] += tmp2[j];
-      block_mm_sel<TC, false, true>(H, FF, G2, F, W2, F, C, FF, F, 1.f, 0.f);  // H = G2 W2^T
+      block_mm_call<TC, false, true>(H, FF, G2, F, W2, F, C, FF, F, 1.f, 0.f);  // H = G2 W2^T
       __syncthreads();
       for (int i = threadIdx.x; i < CFF; i += blockDim.x) G1[i] = H[i] * gelu_bwd_ref(Z1[i]);
       __syncthreads();
-      block_mm_sel<TC, true, false>(W1, FF, T1, F, G1, FF, F, FF, C, 1.f, 1.f);  // W1 += (e*XK)^T G1
+      block_mm_call<TC, true, false>(W1, FF, T1, F, G1, FF, F, FF, C, 1.f, 1.f);  // W1 += (e*XK)^T G1
       weighted_colsum(tmp1, e, G1, C, FF);
       __syncthreads();
       for (int j = threadIdx.x; j < FF; j += blockDim.x) b1[j] += tmp1[j];
       // readout recompute
-      block_mm_sel<TC, false, false>(Z1b, FF, XQ, F, W1, FF, C, FF, F, 1.f, 0.f);
-      block_mm_sel<TC, false, false>(Z1b, FF, P1, C, G1, FF, C, FF, C, -1.f, 1.f);
+      block_mm_call<TC, false, false>(Z1b, FF, XQ, F, W1, FF, C, FF, F, 1.f, 0.f);
+      block_mm_call<TC, false, false>(Z1b, FF, P1, C, G1, FF, C, FF, C, -1.f, 1.f);
       __syncthreads();
       for (int i = threadIdx.x; i < CFF; i += blockDim.x) {
         const float z = Z1b[i] + b1[i % FF];
@@ -354,22 +354,22 @@ __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
         X2b[i] = gelu_tanh(z);
       }
       __syncthreads();
-      block_mm_sel<TC, false, true>(A2, C, X2b, FF, X2, FF, C, C, FF, 1.f, 0.f);
-      block_mm_sel<TC, false, false>(Z2b, F, X2b, FF, W2, F, C, F, FF, 1.f, 0.f);
+      block_mm_call<TC, false, true>(A2, C, X2b, FF, X2, FF, C, C, FF, 1.f, 0.f);
+      block_mm_call<TC, false, false>(Z2b, F, X2b, FF, W2, F, C, F, FF, 1.f, 0.f);
       __syncthreads();
       for (int i = threadIdx.x; i < CC; i += blockDim.x) P2[i] = E[i] * (A2[i] + 1.f);
       __syncthreads();
-      block_mm_sel<TC, false, false>(Z2b, F, P2, C, G2, F, C, F, C, -1.f, 1.f);
+      block_mm_call<TC, false, false>(Z2b, F, P2, C, G2, F, C, F, C, -1.f, 1.f);
       __syncthreads();
       readout_ln_bwd_rows(Z2b, b2, dO, gam, C, F, dZ2b);  // Z2b -> x_bar
       __syncthreads();
       readout_ln_bwd_cols(dO, Z2b, C, F, dgam, dbet);
       // first-level products of the readout backward (dW*_next = incoming carries)
-      block_mm_sel<TC, false, true>(DX2B, FF, dZ2b, F, W2, F, C, FF, F, 1.f, 0.f);  // dX2b = dZ2b W2^T
-      block_mm_sel<TC, false, true>(dP, C, dZ2b, F, G2, F, C, C, F, -1.f, 0.f);     // dP2 = -dZ2b G2^T
-      block_mm_sel<TC, true, false>(dG2, F, P2, C, dZ2b, F, C, F, C, -1.f, 0.f);    // dG2 = -P2^T dZ2b
-      block_mm_sel<TC, false, false>(XdW2, F, X2, FF, dW2, F, C, F, FF, 1.f, 0.f);  // X2 dW2_next
-      block_mm_sel<TC, false, true>(DX2, FF, G2, F, dW2, F, C, FF, F, 1.f, 0.f);    // G2 dW2_next^T
+      block_mm_call<TC, false, true>(DX2B, FF, dZ2b, F, W2, F, C, FF, F, 1.f, 0.f);  // dX2b = dZ2b W2^T
+      block_mm_call<TC, false, true>(dP, C, dZ2b, F, G2, F, C, C, F, -1.f, 0.f);     // dP2 = -dZ2b G2^T
+      block_mm_call<TC, true, false>(dG2, F, P2, C, dZ2b, F, C, F, C, -1.f, 0.f);    // dG2 = -P2^T dZ2b
+      block_mm_call<TC, false, false>(XdW2, F, X2, FF, dW2, F, C, F, FF, 1.f, 0.f);  // X2 dW2_next
+      block_mm_call<TC, false, true>(DX2, FF, G2, F, dW2, F, C, FF, F, 1.f, 0.f);    // G2 dW2_next^T
       __syncthreads();
       for (int i = threadIdx.x; i < CC; i += blockDim.x) {
         const float a2 = A2[i];  // dA takes A2's buffer: read it first
@@ -378,16 +378,16 @@ __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
       }
       for (int i = threadIdx.x; i < CFF; i += blockDim.x) DX2[i] *= -e[i / FF];
       __syncthreads();
-      block_mm_sel<TC, false, false>(DX2B, FF, dA, C, X2, FF, C, FF, C, 1.f, 1.f);  // dX2b += dA2 X2
-      block_mm_sel<TC, true, false>(DX2, FF, dA, C, X2b, FF, C, FF, C, 1.f, 1.f);   // dX2 += dA2^T X2b
+      block_mm_call<TC, false, false>(DX2B, FF, dA, C, X2, FF, C, FF, C, 1.f, 1.f);  // dX2b += dA2 X2
+      block_mm_call<TC, true, false>(DX2, FF, dA, C, X2b, FF, C, FF, C, 1.f, 1.f);   // dX2 += dA2^T X2b
       __syncthreads();
       for (int i = threadIdx.x; i < CFF; i += blockDim.x) DX2B[i] *= gelu_tanh_grad(Z1b[i]);  // dZ1b
       __syncthreads();
-      block_mm_sel<TC, false, true>(dXQ, F, DX2B, FF, W1, FF, C, F, FF, 1.f, 0.f);   // dXQ = dZ1b W1^T
-      block_mm_sel<TC, false, true>(dP, C, DX2B, FF, G1, FF, C, C, FF, -1.f, 0.f);   // dP1 = -dZ1b G1^T
-      block_mm_sel<TC, true, false>(DG1, FF, P1, C, DX2B, FF, C, FF, C, -1.f, 0.f);  // dG1 = -P1^T dZ1b
-      block_mm_sel<TC, false, false>(Z1b, FF, XK, F, dW1, FF, C, FF, F, 1.f, 0.f);  // XK dW1_next
-      block_mm_sel<TC, false, true>(dXK, F, G1, FF, dW1, FF, C, F, FF, 1.f, 0.f);    // G1 dW1_next^T
+      block_mm_call<TC, false, true>(dXQ, F, DX2B, FF, W1, FF, C, F, FF, 1.f, 0.f);   // dXQ = dZ1b W1^T
+      block_mm_call<TC, false, true>(dP, C, DX2B, FF, G1, FF, C, C, FF, -1.f, 0.f);   // dP1 = -dZ1b G1^T
+      block_mm_call<TC, true, false>(DG1, FF, P1, C, DX2B, FF, C, FF, C, -1.f, 0.f);  // dG1 = -P1^T dZ1b
+      block_mm_call<TC, false, false>(Z1b, FF, XK, F, dW1, FF, C, FF, F, 1.f, 0.f);  // XK dW1_next
+      block_mm_call<TC, false, true>(dXK, F, G1, FF, dW1, FF, C, F, FF, 1.f, 0.f);    // G1 dW1_next^T
       __syncthreads();
       for (int i = threadIdx.x; i < CC; i += blockDim.x) {
         dEta[i] += dP[i] * (A1[i] + 1.f);
@@ -415,10 +415,10 @@ __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
       }
       __syncthreads();
       for (int c = threadIdx.x; c < C; c += blockDim.x) dEta[(C - 1) * C + c] += de[c];
-      block_mm_sel<TC, false, false>(dXQ, F, dA, C, XK, F, C, F, C, 1.f, 1.f);         // dXQ += dA1 XK
-      block_mm_sel<TC, true, false>(dXK, F, dA, C, XQ, F, C, F, C, 1.f, 1.f);          // dXK += dA1^T XQ
-      block_mm_sel<TC, true, false>(dW2, F, X2b, FF, dZ2b, F, FF, F, C, 1.f, 1.f);     // dW2 += X2b^T dZ2b
-      block_mm_sel<TC, true, false>(dW1, FF, XQ, F, DX2B, FF, F, FF, C, 1.f, 1.f);     // dW1 += XQ^T dZ1b
+      block_mm_call<TC, false, false>(dXQ, F, dA, C, XK, F, C, F, C, 1.f, 1.f);         // dXQ += dA1 XK
+      block_mm_call<TC, true, false>(dXK, F, dA, C, XQ, F, C, F, C, 1.f, 1.f);          // dXK += dA1^T XQ
+      block_mm_call<TC, true, false>(dW2, F, X2b, FF, dZ2b, F, FF, F, C, 1.f, 1.f);     // dW2 += X2b^T dZ2b
+      block_mm_call<TC, true, false>(dW1, FF, XQ, F, DX2B, FF, F, FF, C, 1.f, 1.f);     // dW1 += XQ^T dZ1b
       for (int j = threadIdx.x; j < F; j += blockDim.x) {
         float a = 0.f;
         for (int r = 0; r < C; ++r) a += dZ2b[r * F + j];
@@ -437,15 +437,15 @@ __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
         H[i] = t * H[i] * gelu_bwd_ref_grad(z);
       }
       __syncthreads();
-      block_mm_sel<TC, false, false>(dG2, F, DG1, FF, W2, F, C, F, FF, 1.f, 1.f);  // dG2 += dH W2
-      block_mm_sel<TC, true, false>(dW2, F, DG1, FF, G2, F, FF, F, C, 1.f, 1.f);   // dW2 += dH^T G2
+      block_mm_call<TC, false, false>(dG2, F, DG1, FF, W2, F, C, F, FF, 1.f, 1.f);  // dG2 += dH W2
+      block_mm_call<TC, true, false>(dW2, F, DG1, FF, G2, F, FF, F, C, 1.f, 1.f);   // dW2 += dH^T G2
       __syncthreads();
       ln_fused_bwd_rows(Z2, mu2, sd2, G2, dG2, XV, XK, gam, bet, C, F, T1, T2, dT, dZ2);
       __syncthreads();
       ln_fused_bwd_cols(Z2, mu2, sd2, T2, XV, XK, gam, bet, C, F, dgam, dbet);
       for (int i = threadIdx.x; i < CF; i += blockDim.x) dXK[i] -= dT[i];
-      block_mm_sel<TC, false, true>(DX2, FF, dZ2, F, W2, F, C, FF, F, 1.f, 1.f);  // dX2 += dZ2 W2^T
-      block_mm_sel<TC, true, false>(dW2, F, X2, FF, dZ2, F, FF, F, C, 1.f, 1.f);  // dW2 += X2^T dZ2
+      block_mm_call<TC, false, true>(DX2, FF, dZ2, F, W2, F, C, FF, F, 1.f, 1.f);  // dX2 += dZ2 W2^T
+      block_mm_call<TC, true, false>(dW2, F, X2, FF, dZ2, F, FF, F, C, 1.f, 1.f);  // dW2 += X2^T dZ2
       for (int j = threadIdx.x; j < F; j += blockDim.x) {
         float a = 0.f;
         for (int r = 0; r < C; ++r) a += dZ2[r * F + j];
@@ -454,8 +454,8 @@ __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
       __syncthreads();
       for (int i = threadIdx.x; i < CFF; i += blockDim.x) H[i] += DX2[i] * gelu_tanh_grad(Z1[i]);  // dZ1
       __syncthreads();
-      block_mm_sel<TC, false, true>(dXK, F, H, FF, W1, FF, C, F, FF, 1.f, 1.f);  // dXK += dZ1 W1^T
-      block_mm_sel<TC, true, false>(dW1, FF, XK, F, H, FF, F, FF, C, 1.f, 1.f);  // dW1 += XK^T dZ1
+      block_mm_call<TC, false, true>(dXK, F, H, FF, W1, FF, C, F, FF, 1.f, 1.f);  // dXK += dZ1 W1^T
+      block_mm_call<TC, true, false>(dW1, FF, XK, F, H, FF, F, FF, C, 1.f, 1.f);  // dW1 += XK^T dZ1
       for (int j = threadIdx.x; j < FF; j += blockDim.x) {
         float a = 0.f;
         for (int r = 0; r < C; ++r) a += H[r * FF + j];
