@@ -20,6 +20,7 @@
 
 namespace ttt {
 
+template <bool TC>
 __global__ void __launch_bounds__(256) linear_fwd_kernel(LinFwdParams p) {
   extern __shared__ float sm[];
   const int C = p.CS, F = p.F;
@@ -62,9 +63,9 @@ __global__ void __launch_bounds__(256) linear_fwd_kernel(LinFwdParams p) {
     load_tile(E, p.eta, eb, CC, p.dt_eta);
     __syncthreads();
 
-    block_mm<false, false>(Z, F, XK, F, W, F, C, F, F, 1.f, 0.f);   // Z  = XK W
-    block_mm<false, true>(P, C, XQ, F, XK, F, C, C, F, 1.f, 0.f);   // P  = XQ XK^T
-    block_mm<false, false>(Zb, F, XQ, F, W, F, C, F, F, 1.f, 0.f);  // Zb = XQ W
+    block_mm_sel<TC, false, false>(Z, F, XK, F, W, F, C, F, F, 1.f, 0.f);   // Z  = XK W
+    block_mm_sel<TC, false, true>(P, C, XQ, F, XK, F, C, C, F, 1.f, 0.f);   // P  = XQ XK^T
+    block_mm_sel<TC, false, false>(Zb, F, XQ, F, W, F, C, F, F, 1.f, 0.f);  // Zb = XQ W
     __syncthreads();
 
     ln_fused_rows(Z, G, bvec, XV, XK, gam, bet, C, F, nullptr, nullptr);
@@ -76,13 +77,13 @@ __global__ void __launch_bounds__(256) linear_fwd_kernel(LinFwdParams p) {
     for (int i = threadIdx.x; i < CF; i += blockDim.x) XKe[i] = E[(C - 1) * C + i / F] * XK[i];
     __syncthreads();
 
-    block_mm<false, false>(Zb, F, P, C, G, F, C, F, C, -1.f, 1.f);  // Zb -= (eta*(A+1)) G
+    block_mm_sel<TC, false, false>(Zb, F, P, C, G, F, C, F, C, -1.f, 1.f);  // Zb -= (eta*(A+1)) G
     weighted_colsum(tmpF, E + (C - 1) * C, G, C, F);
     __syncthreads();
 
     // readout: XQW = XQ + LN(Zb + b) with the old b; state update in parallel
     readout_ln_store_rows(Zb, bvec, XQ, gam, bet, C, F, kLnEps, p.out, xb, p.dt_out);
-    block_mm<true, false>(W, F, XKe, F, G, F, F, F, C, -1.f, 1.f);  // W -= (e*XK)^T G
+    block_mm_sel<TC, true, false>(W, F, XKe, F, G, F, F, F, C, -1.f, 1.f);  // W -= (e*XK)^T G
     __syncthreads();
     for (int j = threadIdx.x; j < F; j += blockDim.x) bvec[j] -= tmpF[j];
     __syncthreads();
@@ -91,6 +92,7 @@ __global__ void __launch_bounds__(256) linear_fwd_kernel(LinFwdParams p) {
   for (int i = threadIdx.x; i < F; i += blockDim.x) p.b_last[s * F + i] = bvec[i];
 }
 
+template <bool TC>
 __global__ void __launch_bounds__(256) linear_bwd_kernel(LinBwdParams p) {
   extern __shared__ float sm[];
   const int C = p.CS, F = p.F;
@@ -157,13 +159,13 @@ __global__ void __launch_bounds__(256) linear_bwd_kernel(LinBwdParams p) {
       load_tile(XV, p.XV, xb, CF, p.dt_xv);
       load_tile(E + (C - 1) * C, p.eta, eb + (C - 1) * C, C, p.dt_eta);
       __syncthreads();
-      block_mm<false, false>(Z, F, XK, F, W, F, C, F, F, 1.f, 0.f);
+      block_mm_sel<TC, false, false>(Z, F, XK, F, W, F, C, F, F, 1.f, 0.f);
       for (int i = threadIdx.x; i < CF; i += blockDim.x) T1[i] = E[(C - 1) * C + i / F] * XK[i];
       __syncthreads();
       ln_fused_rows(Z, G, bvec, XV, XK, gam, bet, C, F, nullptr, nullptr);
       __syncthreads();
       for (int i = threadIdx.x; i < CF; i += blockDim.x) zs[(long long)(n - n0) * CF + i] = Z[i];
-      block_mm<true, false>(W, F, T1, F, G, F, F, F, C, -1.f, 1.f);
+      block_mm_sel<TC, true, false>(W, F, T1, F, G, F, F, F, C, -1.f, 1.f);
       weighted_colsum(tmpF, E + (C - 1) * C, G, C, F);
       __syncthreads();
       for (int j = threadIdx.x; j < F; j += blockDim.x) bvec[j] -= tmpF[j];
@@ -181,31 +183,31 @@ __global__ void __launch_bounds__(256) linear_bwd_kernel(LinBwdParams p) {
       for (int i = threadIdx.x; i < CF; i += blockDim.x) Z[i] = zs[(long long)(n - n0) * CF + i];
       __syncthreads();
       // G from the stored Z (its bias is already included)
-      block_mm<false, true>(A, C, XQ, F, XK, F, C, C, F, 1.f, 0.f);  // A = XQ XK^T
+      block_mm_sel<TC, false, true>(A, C, XQ, F, XK, F, C, C, F, 1.f, 0.f);  // A = XQ XK^T
       for (int i = threadIdx.x; i < CF; i += blockDim.x) T1[i] = E[(C - 1) * C + i / F] * XK[i];
       __syncthreads();
       ln_fused_rows(Z, G, nullptr, XV, XK, gam, bet, C, F, mu1, sd1);
       for (int i = threadIdx.x; i < CC; i += blockDim.x) P[i] = E[i] * (A[i] + 1.f);
       __syncthreads();
       // state reversal: W_n = W_{n+1} + (e*XK)^T G ; b_n = b_{n+1} + e G
-      block_mm<true, false>(W, F, T1, F, G, F, F, F, C, 1.f, 1.f);
+      block_mm_sel<TC, true, false>(W, F, T1, F, G, F, F, F, C, 1.f, 1.f);
       weighted_colsum(tmpF, E + (C - 1) * C, G, C, F);
       __syncthreads();
       for (int j = threadIdx.x; j < F; j += blockDim.x) bvec[j] += tmpF[j];
       __syncthreads();
       // readout recompute Zb = XQ W + b - P G
-      block_mm<false, false>(Zb, F, XQ, F, W, F, C, F, F, 1.f, 0.f);
-      block_mm<false, false>(Zb, F, P, C, G, F, C, F, C, -1.f, 1.f);
+      block_mm_sel<TC, false, false>(Zb, F, XQ, F, W, F, C, F, F, 1.f, 0.f);
+      block_mm_sel<TC, false, false>(Zb, F, P, C, G, F, C, F, C, -1.f, 1.f);
       __syncthreads();
       // readout LayerNorm backward: Zb -> x_bar (in place), dZb
       readout_ln_bwd_rows(Zb, bvec, dO, gam, C, F, dZb);
       __syncthreads();
       readout_ln_bwd_cols(dO, Zb, C, F, dgam, dbet);
-      block_mm<false, true>(dXQ, F, dZb, F, W, F, C, F, F, 1.f, 0.f);  // dXQ = dZb W^T
-      block_mm<false, true>(dP, C, dZb, F, G, F, C, C, F, -1.f, 0.f);  // dP = -dZb G^T
-      block_mm<true, false>(dG, F, P, C, dZb, F, C, F, C, -1.f, 0.f);  // dG = -P^T dZb
-      block_mm<false, false>(T1, F, XK, F, dW, F, C, F, F, 1.f, 0.f);  // XK dW_next
-      block_mm<false, true>(T2, F, G, F, dW, F, C, F, F, 1.f, 0.f);    // G dW_next^T
+      block_mm_sel<TC, false, true>(dXQ, F, dZb, F, W, F, C, F, F, 1.f, 0.f);  // dXQ = dZb W^T
+      block_mm_sel<TC, false, true>(dP, C, dZb, F, G, F, C, C, F, -1.f, 0.f);  // dP = -dZb G^T
+      block_mm_sel<TC, true, false>(dG, F, P, C, dZb, F, C, F, C, -1.f, 0.f);  // dG = -P^T dZb
+      block_mm_sel<TC, false, false>(T1, F, XK, F, dW, F, C, F, F, 1.f, 0.f);  // XK dW_next
+      block_mm_sel<TC, false, true>(T2, F, G, F, dW, F, C, F, F, 1.f, 0.f);    // G dW_next^T
       __syncthreads();
       for (int i = threadIdx.x; i < CC; i += blockDim.x) {
         dA[i] = dP[i] * E[i];
@@ -226,8 +228,8 @@ __global__ void __launch_bounds__(256) linear_bwd_kernel(LinBwdParams p) {
       }
       __syncthreads();
       for (int c = threadIdx.x; c < C; c += blockDim.x) dP[(C - 1) * C + c] += de[c];
-      block_mm<false, false>(dXQ, F, dA, C, XK, F, C, F, C, 1.f, 1.f);  // dXQ += dA XK
-      block_mm<true, false>(dXK, F, dA, C, XQ, F, C, F, C, 1.f, 1.f);   // dXK += dA^T XQ
+      block_mm_sel<TC, false, false>(dXQ, F, dA, C, XK, F, C, F, C, 1.f, 1.f);  // dXQ += dA XK
+      block_mm_sel<TC, true, false>(dXK, F, dA, C, XQ, F, C, F, C, 1.f, 1.f);   // dXK += dA^T XQ
       __syncthreads();
       // backward of G = ln_fused_l2_bwd(Z, XV - XK)
       ln_fused_bwd_rows(Z, mu1, sd1, G, dG, XV, XK, gam, bet, C, F, T1, T2, dT, dZ);
@@ -235,9 +237,9 @@ __global__ void __launch_bounds__(256) linear_bwd_kernel(LinBwdParams p) {
       ln_fused_bwd_cols(Z, mu1, sd1, T2, XV, XK, gam, bet, C, F, dgam, dbet);
       for (int i = threadIdx.x; i < CF; i += blockDim.x) dXK[i] -= dT[i];
       __syncthreads();
-      block_mm<false, true>(dXK, F, dZ, F, W, F, C, F, F, 1.f, 1.f);   // dXK += dZ W^T
-      block_mm<true, false>(dW, F, XQ, F, dZb, F, F, F, C, 1.f, 1.f);  // dW += XQ^T dZb
-      block_mm<true, false>(dW, F, XK, F, dZ, F, F, F, C, 1.f, 1.f);   // dW += XK^T dZ
+      block_mm_sel<TC, false, true>(dXK, F, dZ, F, W, F, C, F, F, 1.f, 1.f);   // dXK += dZ W^T
+      block_mm_sel<TC, true, false>(dW, F, XQ, F, dZb, F, F, F, C, 1.f, 1.f);  // dW += XQ^T dZb
+      block_mm_sel<TC, true, false>(dW, F, XK, F, dZ, F, F, F, C, 1.f, 1.f);   // dW += XK^T dZ
       for (int j = threadIdx.x; j < F; j += blockDim.x) {
         float acc = 0.f;
         for (int r = 0; r < C; ++r) acc += dZb[r * F + j] + dZ[r * F + j];
@@ -257,6 +259,13 @@ __global__ void __launch_bounds__(256) linear_bwd_kernel(LinBwdParams p) {
     p.d_ln_w[s * F + i] = dgam[i];
     p.d_ln_b[s * F + i] = dbet[i];
   }
+}
+
+// The general kernels multiply on the TF32 tensor cores (block_mm_tf32) when the activations
+// are 16-bit (their operands then carry no more than TF32's precision), on fp32 FMA otherwise.
+static bool lin_tc_products(int dt_xq, int dt_xv, int dt_xk) {
+  auto half = [](int dt) { return dt == DT_BF16 || dt == DT_F16; };
+  return half(dt_xq) && half(dt_xv) && half(dt_xk);
 }
 
 static size_t linear_fwd_smem(int C, int F) {
@@ -307,9 +316,10 @@ extern "C" int ttt_linear_fwd(int B, int NH, int NC, int CS, int F, int checkpoi
   rc = linear_fwd_fast(p, (cudaStream_t)stream);
   if (rc != TTT_NOT_APPLICABLE) return rc;
   const size_t smem = linear_fwd_smem(CS, F);
-  rc = prepare_smem(linear_fwd_kernel, smem, "ttt_linear_fwd");
+  auto kern = lin_tc_products(dt_xq, dt_xv, dt_xk) ? linear_fwd_kernel<true> : linear_fwd_kernel<false>;
+  rc = prepare_smem(kern, smem, "ttt_linear_fwd");
   if (rc) return rc;
-  linear_fwd_kernel<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
+  kern<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
   return check_launch("ttt_linear_fwd");
 }
 
@@ -354,9 +364,10 @@ extern "C" int ttt_linear_bwd(int B, int NH, int NC, int CS, int F, int checkpoi
   TTT_REQUIRE(scratch && scratch_bytes >= need, TTT_ERR_SCRATCH, "ttt_linear_bwd: scratch has %zu bytes, needs %zu",
               scratch ? scratch_bytes : (size_t)0, need);
   const size_t smem = linear_bwd_smem(CS, F);
-  rc = prepare_smem(linear_bwd_kernel, smem, "ttt_linear_bwd");
+  auto kern = lin_tc_products(dt_xq, dt_xv, dt_xk) ? linear_bwd_kernel<true> : linear_bwd_kernel<false>;
+  rc = prepare_smem(kern, smem, "ttt_linear_bwd");
   if (rc) return rc;
-  linear_bwd_kernel<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
+  kern<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
   return check_launch("ttt_linear_bwd");
 }
 
@@ -430,8 +441,9 @@ extern "C" int ttt_linear_bwd_noalloc(int B, int NH, int NC, int CS, int F, int 
   p.scratch = scratch;
   p.Z_saved = nullptr; p.W_last = nullptr; p.b_last = nullptr;
   const size_t smem = linear_bwd_smem(CS, F);
-  rc = prepare_smem(linear_bwd_kernel, smem, "ttt_linear_bwd_noalloc");
+  auto kern = lin_tc_products(dt_xq, dt_xv, dt_xk) ? linear_bwd_kernel<true> : linear_bwd_kernel<false>;
+  rc = prepare_smem(kern, smem, "ttt_linear_bwd_noalloc");
   if (rc) return rc;
-  linear_bwd_kernel<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
+  kern<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
   return check_launch("ttt_linear_bwd_noalloc");
 }

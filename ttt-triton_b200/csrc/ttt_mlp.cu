@@ -476,6 +476,7 @@ __global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
 }
 
 // Memo read-out: one CTA per (b, h, mini-batch); weights read through L2.
+template <bool TC>
 __global__ void __launch_bounds__(256) mlp_readout_kernel(ReadoutParams p) {
   extern __shared__ float sm[];
   const int C = p.CS, F = p.F, FF = p.FF;
@@ -499,11 +500,11 @@ __global__ void __launch_bounds__(256) mlp_readout_kernel(ReadoutParams p) {
   load_tile(bet, p.ln_b, (long long)h * F, F, p.dt_ln);
   load_tile(XQ, p.XQ, xb, CF, p.dt_xq);
   __syncthreads();
-  block_mm<false, false>(Z1, FF, XQ, F, W1, FF, C, FF, F, 1.f, 0.f);
+  block_mm_sel<TC, false, false>(Z1, FF, XQ, F, W1, FF, C, FF, F, 1.f, 0.f);
   __syncthreads();
   for (int i = threadIdx.x; i < C * FF; i += blockDim.x) Z1[i] = gelu_tanh(Z1[i] + b1[i % FF]);
   __syncthreads();
-  block_mm<false, false>(Z2, F, Z1, FF, W2, F, C, F, FF, 1.f, 0.f);
+  block_mm_sel<TC, false, false>(Z2, F, Z1, FF, W2, F, C, F, FF, 1.f, 0.f);
   __syncthreads();
   // b2 lives in global memory: add it, then LN + residual
   for (int i = threadIdx.x; i < CF; i += blockDim.x) Z2[i] += b2[i % F];
@@ -672,8 +673,9 @@ extern "C" int ttt_mlp_cached_readout(int B, int NH, int NCseg, int CS, int F, i
   p.ln_w = ttt_norm_weight; p.ln_b = ttt_norm_bias; p.dt_ln = dt_ln;
   p.out = out;
   const size_t smem = sizeof(float) * (2 * (size_t)F + 2 * (size_t)CS * F + (size_t)CS * FF);
-  const int rc = prepare_smem(mlp_readout_kernel, smem, "ttt_mlp_cached_readout");
+  auto kern = tc_products(dt_xq, dt_xq, dt_xq) ? mlp_readout_kernel<true> : mlp_readout_kernel<false>;
+  const int rc = prepare_smem(kern, smem, "ttt_mlp_cached_readout");
   if (rc) return rc;
-  mlp_readout_kernel<<<(unsigned)((long long)B * NH * NCseg), 256, smem, (cudaStream_t)stream>>>(p);
+  kern<<<(unsigned)((long long)B * NH * NCseg), 256, smem, (cudaStream_t)stream>>>(p);
   return check_launch("ttt_mlp_cached_readout");
 }
