@@ -205,27 +205,29 @@ __device__ __forceinline__ void block_mm_tf32(float* C, int ldc, const float* A,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int tn = N >> 4, tiles = (M >> 4) * tn;
-  // element (m, k) of op(A) and (k, n) of op(B)
-  auto a_at = [&](int m, int k) { return TA ? A[(long long)k * lda + m] : A[(long long)m * lda + k]; };
-  auto b_at = [&](int k, int n) { return TB ? B[(long long)n * ldb + k] : B[(long long)k * ldb + n]; };
+  // Per k-step of 8, this lane reads op(A) at rows m0+g, m0+g+8 and columns k0+t, k0+t+4, and
+  // op(B) at rows k0+t, k0+t+4 and columns n0+g, n0+8+g: base pointers per tile, then fixed
+  // strides (sa / sb per k-step; ra, rb the row / column offsets within it).
+  const int sa = TA ? 8 * lda : 8, ra8 = TA ? 8 : 8 * lda, ra4 = TA ? 4 * lda : 4;
+  const int sb = TB ? 8 : 8 * ldb, rb8 = TB ? 8 * ldb : 8, rb4 = TB ? 4 : 4 * ldb;
   for (int tile = warp; tile < tiles; tile += nw) {
     const int m0 = (tile / tn) << 4, n0 = (tile % tn) << 4;
+    const float* pa = TA ? A + t * lda + m0 + g : A + (m0 + g) * lda + t;
+    const float* pb = TB ? B + (n0 + g) * ldb + t : B + t * ldb + n0 + g;
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll 2
-    for (int k0 = 0; k0 < K; k0 += 8) {
-      const uint32_t a[4] = {to_tf32(a_at(m0 + g, k0 + t)), to_tf32(a_at(m0 + g + 8, k0 + t)),
-                             to_tf32(a_at(m0 + g, k0 + t + 4)), to_tf32(a_at(m0 + g + 8, k0 + t + 4))};
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const uint32_t b[2] = {to_tf32(b_at(k0 + t, n0 + 8 * j + g)), to_tf32(b_at(k0 + t + 4, n0 + 8 * j + g))};
-        mma_tf32_16808(acc[j], a, b);
-      }
+    for (int k0 = 0; k0 < K; k0 += 8, pa += sa, pb += sb) {
+      const uint32_t a[4] = {to_tf32(pa[0]), to_tf32(pa[ra8]), to_tf32(pa[ra4]), to_tf32(pa[ra8 + ra4])};
+      const uint32_t b0[2] = {to_tf32(pb[0]), to_tf32(pb[rb4])};
+      const uint32_t b1[2] = {to_tf32(pb[rb8]), to_tf32(pb[rb8 + rb4])};
+      mma_tf32_16808(acc[0], a, b0);
+      mma_tf32_16808(acc[1], a, b1);
     }
 #pragma unroll
     for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        float* c = C + (long long)(m0 + g + 8 * h) * ldc + n0 + 8 * j + 2 * t;
+        float* c = C + (m0 + g + 8 * h) * ldc + n0 + 8 * j + 2 * t;
         const float v0 = acc[j][2 * h], v1 = acc[j][2 * h + 1];
         if (beta == 0.f) {
           c[0] = alpha * v0;
