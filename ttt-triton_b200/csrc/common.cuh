@@ -254,10 +254,28 @@ __device__ __forceinline__ void block_mm_sel(float* C, int ldc, const float* A, 
 // mini-batch, and inlined they kept its 255 registers busy and spilled; as calls their
 // registers are free again between products (128 registers, no spills; the forward, with
 // fewer products, is faster inlined).
+//
+// Inside the call the operand pointers are generic, so their loads would be generic loads
+// (tracked like global ones) even for the shared-memory tiles; operands found in shared
+// memory are rebased onto the dynamic shared array, which makes them shared-memory loads.
+__device__ __forceinline__ const float* as_shared(const float* p) {
+  extern __shared__ float ttt_dyn_smem[];
+  const uint32_t off = (uint32_t)__cvta_generic_to_shared(p) - (uint32_t)__cvta_generic_to_shared(ttt_dyn_smem);
+  return ttt_dyn_smem + (off >> 2);
+}
+
 template <bool TC, bool TA, bool TB>
 __device__ __noinline__ void block_mm_call(float* C, int ldc, const float* A, int lda, const float* B, int ldb,
                                            int M, int N, int K, float alpha, float beta) {
-  block_mm_sel<TC, TA, TB>(C, ldc, A, lda, B, ldb, M, N, K, alpha, beta);
+  const bool ash = __isShared(A), bsh = __isShared(B);
+  if (ash && bsh)
+    block_mm_sel<TC, TA, TB>(C, ldc, as_shared(A), lda, as_shared(B), ldb, M, N, K, alpha, beta);
+  else if (ash)
+    block_mm_sel<TC, TA, TB>(C, ldc, as_shared(A), lda, B, ldb, M, N, K, alpha, beta);
+  else if (bsh)
+    block_mm_sel<TC, TA, TB>(C, ldc, A, lda, as_shared(B), ldb, M, N, K, alpha, beta);
+  else
+    block_mm_sel<TC, TA, TB>(C, ldc, A, lda, B, ldb, M, N, K, alpha, beta);
 }
 
 // ----------------------------------------------------------------- warp reductions
