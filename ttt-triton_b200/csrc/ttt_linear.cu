@@ -21,7 +21,7 @@
 namespace ttt {
 
 template <bool TC>
-__global__ void __launch_bounds__(256) linear_fwd_kernel(LinFwdParams p) {
+__global__ void __launch_bounds__(512) linear_fwd_kernel(LinFwdParams p) {
   extern __shared__ float sm[];
   const int C = p.CS, F = p.F;
   const int CF = C * F, CC = C * C;
@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(256) linear_fwd_kernel(LinFwdParams p) {
 }
 
 template <bool TC>
-__global__ void __launch_bounds__(256) linear_bwd_kernel(LinBwdParams p) {
+__global__ void __launch_bounds__(512) linear_bwd_kernel(LinBwdParams p) {
   extern __shared__ float sm[];
   const int C = p.CS, F = p.F;
   const int CF = C * F, CC = C * C;
@@ -268,6 +268,10 @@ static bool lin_tc_products(int dt_xq, int dt_xv, int dt_xk) {
   return half(dt_xq) && half(dt_xv) && half(dt_xk);
 }
 
+// Threads of a CTA (one stream): sixteen warps for F <= 64, for latency hiding in the chains
+// of small barrier-separated products; eight above.
+static int lin_threads(int F) { return F <= 64 ? 512 : 256; }
+
 static size_t linear_fwd_smem(int C, int F) {
   return sizeof(float) * ((size_t)F * F + 4 * F + 7 * (size_t)C * F + 2 * (size_t)C * C);
 }
@@ -319,7 +323,7 @@ extern "C" int ttt_linear_fwd(int B, int NH, int NC, int CS, int F, int checkpoi
   auto kern = lin_tc_products(dt_xq, dt_xv, dt_xk) ? linear_fwd_kernel<true> : linear_fwd_kernel<false>;
   rc = prepare_smem(kern, smem, "ttt_linear_fwd");
   if (rc) return rc;
-  kern<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
+  kern<<<B * NH, lin_threads(F), smem, (cudaStream_t)stream>>>(p);
   return check_launch("ttt_linear_fwd");
 }
 
@@ -367,7 +371,7 @@ extern "C" int ttt_linear_bwd(int B, int NH, int NC, int CS, int F, int checkpoi
   auto kern = lin_tc_products(dt_xq, dt_xv, dt_xk) ? linear_bwd_kernel<true> : linear_bwd_kernel<false>;
   rc = prepare_smem(kern, smem, "ttt_linear_bwd");
   if (rc) return rc;
-  kern<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
+  kern<<<B * NH, lin_threads(F), smem, (cudaStream_t)stream>>>(p);
   return check_launch("ttt_linear_bwd");
 }
 
@@ -444,6 +448,6 @@ extern "C" int ttt_linear_bwd_noalloc(int B, int NH, int NC, int CS, int F, int 
   auto kern = lin_tc_products(dt_xq, dt_xv, dt_xk) ? linear_bwd_kernel<true> : linear_bwd_kernel<false>;
   rc = prepare_smem(kern, smem, "ttt_linear_bwd_noalloc");
   if (rc) return rc;
-  kern<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
+  kern<<<B * NH, lin_threads(F), smem, (cudaStream_t)stream>>>(p);
   return check_launch("ttt_linear_bwd_noalloc");
 }

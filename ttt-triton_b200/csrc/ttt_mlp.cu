@@ -19,13 +19,22 @@
 
 namespace ttt {
 
+// Threads of a general-kernel CTA (one stream): up to sixteen warps (the kernels fit 128
+// registers per thread). Narrow inner states (F, FF <= 64: the reference's main.py model)
+// get sixteen, for latency hiding in their chains of small barrier-separated products
+// (forward 0.34 -> 0.24 ms, backward 1.05 -> 0.83 ms there); wider ones keep eight, whose
+// products then still fill every thread with 4 x 4 FMA tiles (sixteen warps: 14.6 -> 18.3 ms
+// for an fp32 F 64, FF 256 backward).
+constexpr int kGenThreads = 512;
+static int gen_threads(int F, int FF) { return F <= 64 && FF <= 64 ? 512 : 256; }
+
 __device__ __forceinline__ void copy_state(float* dst, const float* src, long long n) {
   for (long long i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
 }
 
 // TC: the products on the TF32 tensor cores (16-bit activations), else on fp32 FMA.
 template <bool TC>
-__global__ void __launch_bounds__(256) mlp_fwd_kernel(MlpFwdParams p) {
+__global__ void __launch_bounds__(kGenThreads) mlp_fwd_kernel(MlpFwdParams p) {
   extern __shared__ float sm[];
   const int C = p.CS, F = p.F, FF = p.FF;
   const int CF = C * F, CFF = C * FF, CC = C * C;
@@ -211,7 +220,7 @@ __host__ __device__ inline long long carve_bwd(BwdTiles& t, int C, int F, int FF
 }
 
 template <bool TC>
-__global__ void __launch_bounds__(256) mlp_bwd_kernel(MlpBwdParams p) {
+__global__ void __launch_bounds__(kGenThreads) mlp_bwd_kernel(MlpBwdParams p) {
   extern __shared__ float sm[];
   const int C = p.CS, F = p.F, FF = p.FF;
   const int CF = C * F, CFF = C * FF, CC = C * C;
@@ -588,7 +597,7 @@ extern "C" int ttt_mlp_fwd(int B, int NH, int NC, int CS, int F, int FF, int che
   auto kern = tc_products(dt_xq, dt_xv, dt_xk) ? mlp_fwd_kernel<true> : mlp_fwd_kernel<false>;
   rc = prepare_smem(kern, smem, "ttt_mlp_fwd");
   if (rc) return rc;
-  kern<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
+  kern<<<B * NH, gen_threads(F, FF), smem, (cudaStream_t)stream>>>(p);
   return check_launch("ttt_mlp_fwd");
 }
 
@@ -645,7 +654,7 @@ extern "C" int ttt_mlp_bwd(int B, int NH, int NC, int CS, int F, int FF, int che
   auto kern = tc_products(dt_xq, dt_xv, dt_xk) ? mlp_bwd_kernel<true> : mlp_bwd_kernel<false>;
   rc = prepare_smem(kern, smem, "ttt_mlp_bwd");
   if (rc) return rc;
-  kern<<<B * NH, 256, smem, (cudaStream_t)stream>>>(p);
+  kern<<<B * NH, gen_threads(F, FF), smem, (cudaStream_t)stream>>>(p);
   return check_launch("ttt_mlp_bwd");
 }
 
