@@ -257,7 +257,8 @@ __device__ __forceinline__ void block_mm_sel(float* C, int ldc, const float* A, 
 //
 // Inside the call the operand pointers are generic, so their loads would be generic loads
 // (tracked like global ones) even for the shared-memory tiles; operands found in shared
-// memory are rebased onto the dynamic shared array, which makes them shared-memory loads.
+// memory are rebased onto the dynamic shared array, which makes them shared-memory loads
+// (the general kernels keep every shared tile in that array: they declare no static ones).
 __device__ __forceinline__ const float* as_shared(const float* p) {
   extern __shared__ float ttt_dyn_smem[];
   const uint32_t off = (uint32_t)__cvta_generic_to_shared(p) - (uint32_t)__cvta_generic_to_shared(ttt_dyn_smem);
