@@ -199,27 +199,36 @@ __device__ __forceinline__ void mma_tf32_16808(float* d, const uint32_t* a, cons
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-template <bool TA, bool TB>
-__device__ __forceinline__ void block_mm_tf32(float* C, int ldc, const float* A, int lda, const float* B, int ldb,
-                                              int M, int N, int K, float alpha, float beta) {
+// Within each k-step of 8 the MMA's k slots t and t + 4 (t = lane % 4) carry k0 + 2t and
+// k0 + 2t + 1 -- the same permutation of k for A and B, so the sum is unchanged -- which makes a
+// lane's two A values (row-major A) or B values (B stored transposed) adjacent: one 8-byte
+// shared-memory load instead of two scalar ones, at half the bank-conflict replays (tile rows
+// here are multiples of 32 floats apart). VA / VB: take that 8-byte load.
+template <bool TA, bool TB, bool VA, bool VB>
+__device__ __forceinline__ void block_mm_tf32_impl(float* C, int ldc, const float* A, int lda, const float* B,
+                                                   int ldb, int M, int N, int K, float alpha, float beta) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int tn = N >> 4, tiles = (M >> 4) * tn;
-  // Per k-step of 8, this lane reads op(A) at rows m0+g, m0+g+8 and columns k0+t, k0+t+4, and
-  // op(B) at rows k0+t, k0+t+4 and columns n0+g, n0+8+g: base pointers per tile, then fixed
-  // strides (sa / sb per k-step; ra, rb the row / column offsets within it).
-  const int sa = TA ? 8 * lda : 8, ra8 = TA ? 8 : 8 * lda, ra4 = TA ? 4 * lda : 4;
-  const int sb = TB ? 8 : 8 * ldb, rb8 = TB ? 8 * ldb : 8, rb4 = TB ? 4 : 4 * ldb;
+  // strides: per k-step (sa, sb), to row m + 8 of A (ra8) and column n + 8 of B (rb8), to k + 1
+  const int sa = TA ? 8 * lda : 8, ra8 = TA ? 8 : 8 * lda, ra1 = TA ? lda : 1;
+  const int sb = TB ? 8 : 8 * ldb, rb8 = TB ? 8 * ldb : 8, rb1 = TB ? 1 : ldb;
+  auto pair = [](const float* p, int step, bool vec) {
+    if (vec) return *reinterpret_cast<const float2*>(p);
+    return make_float2(p[0], p[step]);
+  };
   for (int tile = warp; tile < tiles; tile += nw) {
     const int m0 = (tile / tn) << 4, n0 = (tile % tn) << 4;
-    const float* pa = TA ? A + t * lda + m0 + g : A + (m0 + g) * lda + t;
-    const float* pb = TB ? B + (n0 + g) * ldb + t : B + t * ldb + n0 + g;
+    const float* pa = TA ? A + 2 * t * lda + m0 + g : A + (m0 + g) * lda + 2 * t;
+    const float* pb = TB ? B + (n0 + g) * ldb + 2 * t : B + 2 * t * ldb + n0 + g;
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll 2
     for (int k0 = 0; k0 < K; k0 += 8, pa += sa, pb += sb) {
-      const uint32_t a[4] = {to_tf32(pa[0]), to_tf32(pa[ra8]), to_tf32(pa[ra4]), to_tf32(pa[ra8 + ra4])};
-      const uint32_t b0[2] = {to_tf32(pb[0]), to_tf32(pb[rb4])};
-      const uint32_t b1[2] = {to_tf32(pb[rb8]), to_tf32(pb[rb8 + rb4])};
+      const float2 a_lo = pair(pa, ra1, VA), a_hi = pair(pa + ra8, ra1, VA);  // rows m, m + 8
+      const uint32_t a[4] = {to_tf32(a_lo.x), to_tf32(a_hi.x), to_tf32(a_lo.y), to_tf32(a_hi.y)};
+      const float2 b_lo = pair(pb, rb1, VB), b_hi = pair(pb + rb8, rb1, VB);  // columns n, n + 8
+      const uint32_t b0[2] = {to_tf32(b_lo.x), to_tf32(b_lo.y)};
+      const uint32_t b1[2] = {to_tf32(b_hi.x), to_tf32(b_hi.y)};
       mma_tf32_16808(acc[0], a, b0);
       mma_tf32_16808(acc[1], a, b1);
     }
@@ -237,6 +246,24 @@ __device__ __forceinline__ void block_mm_tf32(float* C, int ldc, const float* A,
           c[1] = fmaf(alpha, v1, beta * c[1]);
         }
       }
+  }
+}
+
+template <bool TA, bool TB>
+__device__ __forceinline__ void block_mm_tf32(float* C, int ldc, const float* A, int lda, const float* B, int ldb,
+                                              int M, int N, int K, float alpha, float beta) {
+  // 8-byte loads need an even leading dimension and an 8-byte aligned base
+  const bool va = !TA && (lda & 1) == 0 && (reinterpret_cast<uintptr_t>(A) & 7) == 0;
+  const bool vb = TB && (ldb & 1) == 0 && (reinterpret_cast<uintptr_t>(B) & 7) == 0;
+  if (va) {
+    if (vb)
+      block_mm_tf32_impl<TA, TB, true, true>(C, ldc, A, lda, B, ldb, M, N, K, alpha, beta);
+    else
+      block_mm_tf32_impl<TA, TB, true, false>(C, ldc, A, lda, B, ldb, M, N, K, alpha, beta);
+  } else if (vb) {
+    block_mm_tf32_impl<TA, TB, false, true>(C, ldc, A, lda, B, ldb, M, N, K, alpha, beta);
+  } else {
+    block_mm_tf32_impl<TA, TB, false, false>(C, ldc, A, lda, B, ldb, M, N, K, alpha, beta);
   }
 }
 
